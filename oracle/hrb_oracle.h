@@ -1,0 +1,122 @@
+/* Test infrastructure only: the CPU restatement ("oracle") of hotarubi's
+ * quantized GEMM hot path.  Only tests/, bench.py's CPU-baseline leg and
+ * __graft_entry__.smoke() load it, as the checker.  The product library
+ * (hotarubi_b200/lib/libhrb_gemm.so) never links or calls it.
+ *
+ * Every function cites the reference source it restates.  FP32 values travel
+ * as their IEEE bit patterns (uint32_t) so that no host FPU rounding mode or
+ * flush setting can touch them.
+ */
+#ifndef HRB_ORACLE_H_
+#define HRB_ORACLE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Weight modes of the GEMM instruction (include/hotarubi/isa.hpp:88-92), plus
+ * MXFP8, which the reference does not have. */
+enum {
+  HRBO_FP4 = 0,
+  HRBO_W8_HI = 1,
+  HRBO_W8_LO = 2,
+  HRBO_E4M3 = 4
+};
+
+/* Scale bias per weight mode: tools/iss/gemm_array.cpp:62-72 for the three
+ * reference modes; -15 for E4M3 (activation 2^-6 times E4M3 read as an
+ * integer multiple of 2^-9). */
+int32_t hrbo_scale_bias(uint32_t mode);
+
+/* FP32 add with the ISS semantics of tools/iss/fp32.hpp:46-75: round to
+ * nearest even, subnormal inputs read as zero, subnormal results and exact
+ * zeros give +0, overflow gives +-inf, exponent 255 read as an ordinary
+ * exponent. */
+uint32_t hrbo_fp32_add(uint32_t a, uint32_t b);
+
+/* sum * 2^exponent rounded once to FP32 (nearest even), flushed to +0 below
+ * 2^-126 and saturated to +-inf at 2^128.  For |sum| < 2^24 it is the exact
+ * BlockValue of tools/iss/gemm_array.cpp:136-147 with
+ * exponent = a_scale + w_scale - 254 + SBIAS. */
+uint32_t hrbo_round_scaled(int64_t sum, int32_t exponent);
+
+/* BlockValue (tools/iss/gemm_array.cpp:136-147). */
+uint32_t hrbo_block_value(int64_t sum, uint32_t a_scale, uint32_t w_scale,
+                          uint32_t mode);
+
+/* WeightValue (tools/iss/gemm_array.cpp:121-134): nibble -> small integer. */
+int32_t hrbo_weight_value(uint32_t nibble, uint32_t mode);
+
+/* E4M3 byte -> value as an integer multiple of 2^-9 (OCP E4M3; the two NaN
+ * codes read as +-480, the ISS-style "no NaN" convention). */
+int32_t hrbo_e4m3_units(uint32_t code);
+
+/* GEMM instruction fields (tools/iss/gemm_array.hpp:16-27). */
+typedef struct {
+  uint32_t a_base, a_stride, kb, m, w_base, w_stride, n8, c_base, wmode, acc;
+} hrbo_cmd;
+
+/* 0 when ExecuteGemm would run the command, else 1, 2 or 3 for the three
+ * Require checks of tools/iss/gemm_array.cpp:150-156 (m, kb, n8). */
+int hrbo_check_command(const hrbo_cmd* cmd);
+
+/* ExecuteGemm (tools/iss/gemm_array.cpp:149-186) over full memories:
+ * abuf 8192 x 132 bytes, wbuf 2048 x 144 bytes, fbuf 4096 x 32 FP32 bits.
+ * Returns hrbo_check_command's code and leaves fbuf untouched on error. */
+int hrbo_execute_gemm(const hrbo_cmd* cmd, const uint8_t* abuf,
+                      const uint8_t* wbuf, uint32_t* fbuf);
+
+/* EncodeMxint8 (tools/runtime/formats.cpp:35-56,138-162) on a rows x cols FP32
+ * matrix.  q: rows x kp int8 (kp = cols rounded up to 32, padding 0), scale:
+ * rows x kp/32 E8M0 bytes (e + 127).  Returns 1 on an Inf/NaN input (the
+ * reference's Require), else 0. */
+int hrbo_encode_mxint8(const uint32_t* x, uint32_t rows, uint32_t cols,
+                       int8_t* q, uint8_t* scale);
+
+/* The VEC 'q' pass of tools/iss/lane.cpp:384-423 on the same layout:
+ * subnormal inputs quantize to 0 and an all-zero block gets scale byte 127. */
+void hrbo_quantize_vec(const uint32_t* x, uint32_t rows, uint32_t cols,
+                       int8_t* q, uint8_t* scale);
+
+/* Weight formats of the dense entry point. */
+enum {
+  HRBO_WFMT_MXFP4 = 0, /* codes [N][kp/2] nibble pairs, low nibble = even k */
+  HRBO_WFMT_W8 = 1,    /* MXINT8 q [N][kp]; run as W8_HI then W8_LO planes */
+  HRBO_WFMT_MXFP8 = 2  /* E4M3 [N][kp] */
+};
+
+/* The dense GEMM as hotarubi's compiler chains it (LinearEmitter::Emit,
+ * tools/compiler/kernels.cpp:343-395): for each K piece in order, for each
+ * weight plane in order (W8: HI then LO, kernels.cpp:35-37), one FP32 chain
+ * of block values over the piece's blocks; then, when bias is given, one
+ * ADDP-style add of bias[n] (tools/compiler/sparsedrive_encoder.cpp:422-428).
+ * pieces: npieces block counts summing to kb (NULL: one piece).  c holds
+ * M x N FP32 bits; with accumulate != 0 its contents start each chain,
+ * otherwise chains start at +0.  Rows [row0, row1) only. */
+void hrbo_gemm_dense(uint32_t wfmt, uint32_t M, uint32_t N, uint32_t kb,
+                     const int8_t* aq, const uint8_t* ascale,
+                     const uint8_t* w, const uint8_t* wscale,
+                     const uint32_t* pieces, uint32_t npieces,
+                     const uint32_t* bias, uint32_t* c, int accumulate,
+                     uint32_t row0, uint32_t row1);
+
+/* Sum of |block value| over the chain of one output, in double: the scale
+ * the tolerance of the tensor-core path is stated against. */
+double hrbo_abs_chain(uint32_t wfmt, uint32_t N, uint32_t kb,
+                      const int8_t* aq_row, const uint8_t* ascale_row,
+                      const uint8_t* w, const uint8_t* wscale, uint32_t n);
+
+/* Element-wise array forms of hrbo_fp32_add and hrbo_round_scaled. */
+void hrbo_fp32_add_n(const uint32_t* a, const uint32_t* b, uint32_t* out,
+                     size_t n);
+void hrbo_round_scaled_n(const int64_t* sum, const int32_t* exponent,
+                         uint32_t* out, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HRB_ORACLE_H_ */

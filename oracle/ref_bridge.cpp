@@ -1,0 +1,453 @@
+// Test infrastructure only.  This file is compiled together with hotarubi's
+// own sources (left where they lie in the reference checkout) into
+// oracle/_ref/libhrb_ref.so.  It gives the Python tests a C entry point to
+// the reference's GEMM executor and its helpers so that they can check the
+// C restatement in oracle/hrb_oracle.c and generate the golden fixtures.  The
+// product never links or loads it.
+//
+// Each wrapper names the reference function it calls.
+#include <algorithm>
+#include <cstddef>
+#include <cstdint>
+#include <cstring>
+#include <atomic>
+#include <memory>
+#include <random>
+#include <thread>
+#include <span>
+#include <vector>
+
+#include "fp32.hpp"            // tools/iss/fp32.hpp
+#include "gemm_array.hpp"      // tools/iss/gemm_array.hpp
+#include "hotarubi/exact.hpp"  // include/hotarubi/exact.hpp
+#include "hotarubi/formats.hpp"
+#include "lane.hpp"       // tools/iss/lane.hpp
+#include "memories.hpp"   // tools/iss/memories.hpp
+#include "reference.hpp"  // tools/iss/reference.hpp
+#include "weights.hpp"    // tools/compiler/weights.hpp
+
+#include "tb_types.hpp"
+
+// Declarations of tb/fp32_ref.hpp and tb/gemm_ref.hpp, restated because the
+// real headers include the Verilator-dependent word headers.
+namespace hotarubi::tb {
+uint32_t Fp32Add(uint32_t a, uint32_t b);
+void ReferenceGemm(const GemmArgs& args, const std::vector<AbufWord>& abuf,
+                   const std::vector<WbufWord>& wbuf,
+                   std::vector<FbufWord>& fbuf);
+}  // namespace hotarubi::tb
+
+namespace {
+
+using hotarubi::iss::GemmCommand;
+using hotarubi::iss::Memories;
+
+GemmCommand Command(const uint32_t* f) {
+  return {.a_base = f[0],
+          .a_stride = f[1],
+          .kb = f[2],
+          .m = f[3],
+          .w_base = f[4],
+          .w_stride = f[5],
+          .n8 = f[6],
+          .c_base = f[7],
+          .wmode = f[8],
+          .acc = f[9] != 0};
+}
+
+template <size_t N>
+void StoreBits(const std::bitset<N>& bits, uint8_t* out) {
+  for (size_t i = 0; i < N; ++i) {
+    out[i] = bits.test(i) ? 1 : 0;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+// hotarubi::iss::ExecuteGemm (tools/iss/gemm_array.cpp:149-186) on a full set
+// of GEMM memories.  abuf: 8192 words of 132 bytes, wbuf: 2048 words of 144
+// bytes, fbuf: 4096 words of 32 FP32 bit patterns (updated in place).  When
+// log is not null it receives one byte per word: ABUF reads [8192], WBUF
+// reads [2048], FBUF reads [4096], FBUF writes [4096].
+void hrbref_execute_gemm(const uint32_t* fields, const uint8_t* abuf,
+                         const uint8_t* wbuf, uint32_t* fbuf, uint8_t* log) {
+  static Memories memories;
+  memories.log.Clear();
+  for (size_t i = 0; i < hotarubi::iss::kAbufDepth; ++i) {
+    std::memcpy(memories.abuf[i].data(), abuf + (i * 132), 132);
+  }
+  for (size_t i = 0; i < hotarubi::iss::kWbufDepth; ++i) {
+    std::memcpy(memories.wbuf[i].data(), wbuf + (i * 144), 144);
+  }
+  for (size_t i = 0; i < hotarubi::iss::kFbufDepth; ++i) {
+    std::memcpy(memories.fbuf[i].data(), fbuf + (i * 32), 128);
+  }
+  hotarubi::iss::ExecuteGemm(Command(fields), memories);
+  for (size_t i = 0; i < hotarubi::iss::kFbufDepth; ++i) {
+    std::memcpy(fbuf + (i * 32), memories.fbuf[i].data(), 128);
+  }
+  if (log != nullptr) {
+    StoreBits(memories.log.reads.abuf, log);
+    StoreBits(memories.log.reads.wbuf, log + 8192);
+    StoreBits(memories.log.reads.fbuf, log + 8192 + 2048);
+    StoreBits(memories.log.writes.fbuf, log + 8192 + 2048 + 4096);
+  }
+}
+
+// hotarubi::tb::ReferenceGemm (tb/gemm_ref.cpp:47-68).  Word arrays use the
+// DDR word layout of 144 bytes (tb/npu_data.cpp): ABUF bytes 0..127 int8,
+// 128..131 scales; WBUF bytes 0..127 packed nibbles (low nibble first),
+// 128..135 scales.
+void hrbref_reference_gemm(const uint32_t* fields, const uint8_t* abuf,
+                           uint32_t a_words, const uint8_t* wbuf,
+                           uint32_t w_words, uint32_t* fbuf, uint32_t f_words) {
+  std::vector<hotarubi::tb::AbufWord> a(a_words);
+  std::vector<hotarubi::tb::WbufWord> w(w_words);
+  std::vector<hotarubi::tb::FbufWord> c(f_words);
+  for (uint32_t i = 0; i < a_words; ++i) {
+    std::memcpy(a[i].q.data(), abuf + (size_t{i} * 144), 128);
+    std::memcpy(a[i].scale.data(), abuf + (size_t{i} * 144) + 128, 4);
+  }
+  for (uint32_t i = 0; i < w_words; ++i) {
+    const uint8_t* word = wbuf + (size_t{i} * 144);
+    for (uint32_t n = 0; n < 256; ++n) {
+      w[i].nibble[n] = (word[n / 2] >> (4 * (n % 2))) & 0xFU;
+    }
+    std::memcpy(w[i].scale.data(), word + 128, 8);
+  }
+  for (uint32_t i = 0; i < f_words; ++i) {
+    std::memcpy(c[i].data(), fbuf + (size_t{i} * 32), 128);
+  }
+  const hotarubi::tb::GemmArgs args{.a_base = fields[0],
+                                    .a_stride = fields[1],
+                                    .kb = fields[2],
+                                    .m = fields[3],
+                                    .w_base = fields[4],
+                                    .w_stride = fields[5],
+                                    .n8 = fields[6],
+                                    .c_base = fields[7],
+                                    .wmode = fields[8],
+                                    .acc = fields[9] != 0};
+  hotarubi::tb::ReferenceGemm(args, a, w, c);
+  for (uint32_t i = 0; i < f_words; ++i) {
+    std::memcpy(fbuf + (size_t{i} * 32), c[i].data(), 128);
+  }
+}
+
+// tools/iss/fp32.hpp:46-75
+uint32_t hrbref_fp32_add(uint32_t a, uint32_t b) {
+  return hotarubi::iss::Fp32Add(a, b);
+}
+
+// tb/fp32_ref.cpp:64-88
+uint32_t hrbref_tb_fp32_add(uint32_t a, uint32_t b) {
+  return hotarubi::tb::Fp32Add(a, b);
+}
+
+// tools/iss/reference.cpp: exact-real model of the FP32 adder.
+uint32_t hrbref_exact_add(uint32_t a, uint32_t b) {
+  return hotarubi::iss::reference::Add(a, b);
+}
+
+// reference::Round(Integer(sum) * 2^exponent): the exact model the ISS unit
+// test uses for one block product (tools/iss/gemm_array_test.cpp:91-98).
+uint32_t hrbref_exact_round(int64_t sum, int64_t exponent) {
+  return hotarubi::iss::reference::Round(
+      hotarubi::exact::Real::Integer(sum).Scaled(exponent));
+}
+
+// tools/iss/gemm_array.cpp:121-134 and :136-147
+int32_t hrbref_weight_value(uint32_t nibble, uint32_t wmode) {
+  return hotarubi::iss::WeightValue(nibble,
+                                    hotarubi::iss::DecodeWeightMode(wmode));
+}
+
+uint32_t hrbref_block_value(int32_t sum, uint32_t a_scale, uint32_t w_scale,
+                            uint32_t wmode) {
+  return hotarubi::iss::BlockValue(sum, a_scale, w_scale,
+                                   hotarubi::iss::DecodeWeightMode(wmode));
+}
+
+// hotarubi::EncodeMxint8 (tools/runtime/formats.cpp:138-162).  bits is a
+// rows x cols FP32 matrix; q receives rows x padded-cols int8 and e receives
+// rows x blocks exponents (scale byte = e + 127).
+void hrbref_encode_mxint8(const uint32_t* bits, uint32_t rows, uint32_t cols,
+                          int8_t* q, int32_t* e) {
+  hotarubi::Matrix m{.rows = rows,
+                     .cols = cols,
+                     .bits = std::vector<uint32_t>(
+                         bits, bits + (static_cast<size_t>(rows) * cols))};
+  const hotarubi::Mxint8Matrix out = hotarubi::EncodeMxint8(m);
+  std::copy(out.q.begin(), out.q.end(), q);
+  std::copy(out.e.begin(), out.e.end(), e);
+}
+
+// hotarubi::PackAbuf (tools/runtime/formats.cpp:114-136): 144-byte words.
+void hrbref_pack_abuf(const int8_t* q, const int32_t* e, uint32_t rows,
+                      uint32_t cols, uint8_t* out) {
+  const size_t blocks = cols / 32;
+  hotarubi::Mxint8Matrix m{
+      .rows = rows,
+      .cols = cols,
+      .q = std::vector<int8_t>(q, q + (static_cast<size_t>(rows) * cols)),
+      .e = std::vector<int32_t>(e, e + (rows * blocks))};
+  const std::vector<std::byte> bytes = hotarubi::PackAbuf(m);
+  std::memcpy(out, bytes.data(), bytes.size());
+}
+
+// hotarubi::iss::QuantizeBlock (tools/iss/lane.cpp:406-423): four FBUF words
+// (32 FP32 each) -> one 132-byte ABUF word, the VEC 'q' pass.
+void hrbref_quantize_block(const uint32_t* words, uint8_t* out) {
+  std::array<hotarubi::iss::FbufWord, 4> in{};
+  for (size_t i = 0; i < 4; ++i) {
+    std::memcpy(in[i].data(), words + (i * 32), 128);
+  }
+  const hotarubi::iss::AbufWord word =
+      hotarubi::iss::QuantizeBlock(std::span<const hotarubi::iss::FbufWord, 4>(in));
+  std::memcpy(out, word.data(), word.size());
+}
+
+// hotarubi::compiler::CanonicalMxfp4 (tools/compiler/weights.cpp:39-70).
+void hrbref_canonical_mxfp4(const uint8_t* code, const int32_t* e,
+                            uint32_t rows, uint32_t cols, int32_t shift,
+                            uint32_t out_rows, uint8_t* code_out,
+                            int32_t* e_out) {
+  const size_t blocks = cols / 32;
+  hotarubi::compiler::Mxfp4Matrix m{
+      .rows = rows,
+      .cols = cols,
+      .code = std::vector<uint8_t>(code, code + (static_cast<size_t>(rows) * cols)),
+      .e = std::vector<int32_t>(e, e + (rows * blocks))};
+  const hotarubi::compiler::Mxfp4Matrix out =
+      hotarubi::compiler::CanonicalMxfp4(m, shift, out_rows);
+  std::copy(out.code.begin(), out.code.end(), code_out);
+  std::copy(out.e.begin(), out.e.end(), e_out);
+}
+
+// hotarubi::compiler::SplitW8 (tools/compiler/weights.cpp:72-88).
+void hrbref_split_w8(const int8_t* q, uint32_t rows, uint32_t cols,
+                     uint8_t* hi, uint8_t* lo) {
+  hotarubi::Mxint8Matrix m{
+      .rows = rows,
+      .cols = cols,
+      .q = std::vector<int8_t>(q, q + (static_cast<size_t>(rows) * cols)),
+      .e = std::vector<int32_t>(static_cast<size_t>(rows) * (cols / 32))};
+  const hotarubi::compiler::W8Planes planes = hotarubi::compiler::SplitW8(m);
+  std::copy(planes.hi.code.begin(), planes.hi.code.end(), hi);
+  std::copy(planes.lo.code.begin(), planes.lo.code.end(), lo);
+}
+
+// hotarubi::compiler::PackWbuf (tools/compiler/tensors.cpp:66-90).
+void hrbref_pack_wbuf(const uint8_t* code, const int32_t* e, uint32_t rows,
+                      uint32_t cols, uint8_t* out) {
+  const size_t blocks = cols / 32;
+  hotarubi::compiler::Mxfp4Matrix m{
+      .rows = rows,
+      .cols = cols,
+      .code = std::vector<uint8_t>(code, code + (static_cast<size_t>(rows) * cols)),
+      .e = std::vector<int32_t>(e, e + (rows * blocks))};
+  const std::vector<std::byte> bytes = hotarubi::compiler::PackWbuf(m);
+  std::memcpy(out, bytes.data(), bytes.size());
+}
+
+// Element-wise array forms of the three adders and of the exact rounding.
+void hrbref_fp32_add_n(const uint32_t* a, const uint32_t* b, uint32_t* out,
+                       size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = hotarubi::iss::Fp32Add(a[i], b[i]);
+}
+
+void hrbref_tb_fp32_add_n(const uint32_t* a, const uint32_t* b, uint32_t* out,
+                          size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = hotarubi::tb::Fp32Add(a[i], b[i]);
+}
+
+void hrbref_exact_add_n(const uint32_t* a, const uint32_t* b, uint32_t* out,
+                        size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = hotarubi::iss::reference::Add(a[i], b[i]);
+}
+
+void hrbref_exact_round_n(const int64_t* sum, const int32_t* exponent,
+                          uint32_t* out, size_t n) {
+  for (size_t i = 0; i < n; ++i) {
+    out[i] = hotarubi::iss::reference::Round(
+        hotarubi::exact::Real::Integer(sum[i]).Scaled(exponent[i]));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Input generators of the reference's own GEMM tests, restated so that the
+// golden fixtures carry exactly the inputs those tests feed the reference.
+// They draw from std::mt19937 with the same distributions in the same order.
+
+// GemmArrayTest::Fill (tools/iss/gemm_array_test.cpp:45-70) over full
+// memories (ABUF 8192 x 132, WBUF 2048 x 144, FBUF 4096 x 32).
+void hrbref_fill_gemm_array_test(uint32_t seed, uint8_t* abuf, uint8_t* wbuf,
+                                 uint32_t* fbuf) {
+  std::mt19937 generator(seed);
+  std::uniform_int_distribution<uint32_t> byte(0, 255);
+  std::uniform_int_distribution<uint32_t> scale(118, 136);
+  for (size_t w = 0; w < hotarubi::iss::kAbufDepth; ++w) {
+    uint8_t* word = abuf + (w * 132);
+    for (size_t i = 0; i < 128; ++i) word[i] = static_cast<uint8_t>(byte(generator));
+    for (size_t t = 0; t < 4; ++t) word[128 + t] = static_cast<uint8_t>(scale(generator));
+  }
+  for (size_t w = 0; w < hotarubi::iss::kWbufDepth; ++w) {
+    uint8_t* word = wbuf + (w * 144);
+    for (size_t i = 0; i < 128; ++i) word[i] = static_cast<uint8_t>(byte(generator));
+    for (size_t c = 0; c < 8; ++c) word[128 + c] = static_cast<uint8_t>(scale(generator));
+    for (size_t i = 136; i < 144; ++i) word[i] = 0;
+  }
+  for (size_t w = 0; w < hotarubi::iss::kFbufDepth; ++w) {
+    for (size_t e = 0; e < 32; ++e) {
+      fbuf[(w * 32) + e] = 0x3F000000U + (byte(generator) << 16);
+    }
+  }
+}
+
+// RandomAbuf / RandomWbuf / RandomFbuf (tb/gemm_test.cpp:31-65) and
+// RandomFp32 (tb/npu_data.cpp:112-118) on a caller-held generator.  The words
+// use the 144-byte DDR layout.
+void* hrbref_tb_rng_new(uint32_t seed) { return new std::mt19937(seed); }
+void hrbref_tb_rng_free(void* rng) { delete static_cast<std::mt19937*>(rng); }
+
+void hrbref_tb_random_abuf(void* handle, uint32_t count, uint8_t* out) {
+  std::mt19937& rng = *static_cast<std::mt19937*>(handle);
+  for (uint32_t w = 0; w < count; ++w) {
+    uint8_t* word = out + (size_t{w} * 144);
+    std::memset(word, 0, 144);
+    for (size_t i = 0; i < 128; ++i) {
+      word[i] = static_cast<uint8_t>(static_cast<int8_t>(static_cast<int>(rng() % 256) - 128));
+    }
+    for (size_t t = 0; t < 4; ++t) word[128 + t] = static_cast<uint8_t>(118 + (rng() % 18));
+  }
+}
+
+void hrbref_tb_random_wbuf(void* handle, uint32_t count, uint8_t* out) {
+  std::mt19937& rng = *static_cast<std::mt19937*>(handle);
+  for (uint32_t w = 0; w < count; ++w) {
+    uint8_t* word = out + (size_t{w} * 144);
+    std::memset(word, 0, 144);
+    for (size_t n = 0; n < 256; ++n) {
+      const auto nibble = static_cast<uint8_t>(rng() % 16);
+      word[n / 2] = static_cast<uint8_t>(word[n / 2] | (nibble << (4 * (n % 2))));
+    }
+    for (size_t c = 0; c < 8; ++c) word[128 + c] = static_cast<uint8_t>(118 + (rng() % 18));
+  }
+}
+
+void hrbref_tb_random_fbuf(void* handle, uint32_t count, uint32_t* out) {
+  std::mt19937& rng = *static_cast<std::mt19937*>(handle);
+  for (uint32_t i = 0; i < count * 32; ++i) {
+    const auto exponent = static_cast<uint32_t>(-6 + 127 + static_cast<int>(rng() % 13));
+    const uint32_t sign = rng() & 1U;
+    out[i] = (sign << 31) | (exponent << 23) | (rng() & 0x7FFFFFU);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The CPU baseline: a dense GEMM run through the reference's ExecuteGemm,
+// tiled into legal GEMM instructions the way hotarubi's compiler tiles a
+// Linear (one weight tile loaded per plane, planes accumulating in order,
+// tools/compiler/kernels.cpp:343-395), with independent (row chunk, column
+// tile) units spread over `threads` std::threads, each owning a Memories.
+//
+// a_words: PackAbuf words (144 bytes) of the rows, [ceil(M/4)][kb].
+// planes: PackWbuf words of each plane, [N/8][kb] per plane, planes back to
+// back (1 plane: FP4, mode 0; 2 planes: W8 HI then LO, modes 1 and 2).
+// c: M x N FP32 bits, row-major.  Only rows [row0, row1) are computed;
+// row0 must be a multiple of 4.  Returns 0, or -1 when kb does not fit.
+int hrbref_dense_gemm_iss(uint32_t nplanes, uint32_t M, uint32_t N,
+                          uint32_t kb, const uint8_t* a_words,
+                          const uint8_t* planes, uint32_t* c, uint32_t threads,
+                          uint32_t row0, uint32_t row1) {
+  using hotarubi::iss::kAbufDepth;
+  using hotarubi::iss::kFbufDepth;
+  using hotarubi::iss::kWbufDepth;
+  if (kb == 0 || kb > kWbufDepth || N % 8 != 0 || row0 % 4 != 0) return -1;
+  const uint32_t groups_total = N / 8;
+  uint32_t tile_groups = std::min<uint32_t>(255, kWbufDepth / kb);
+  uint32_t chunk_quads = std::min<uint32_t>(248, kAbufDepth / kb);
+  chunk_quads -= chunk_quads % 8;
+  if (tile_groups == 0 || chunk_quads == 0) return -1;
+  while (chunk_quads * tile_groups > kFbufDepth) {
+    if (tile_groups > 8) {
+      tile_groups /= 2;
+    } else {
+      chunk_quads -= 8;
+    }
+  }
+  row1 = std::min(row1, M);
+  if (row1 <= row0) return 0;
+  const uint32_t quad0 = row0 / 4;
+  const uint32_t quads = (row1 - row0 + 3) / 4;
+  const uint32_t chunks = (quads + chunk_quads - 1) / chunk_quads;
+  const uint32_t tiles = (groups_total + tile_groups - 1) / tile_groups;
+  const size_t plane_bytes = size_t{groups_total} * kb * 144;
+  std::atomic<uint32_t> next{0};
+  auto worker = [&]() {
+    auto memories = std::make_unique<Memories>();
+    for (;;) {
+      const uint32_t unit = next.fetch_add(1);
+      if (unit >= chunks * tiles) break;
+      const uint32_t chunk = unit / tiles;
+      const uint32_t tile = unit % tiles;
+      const uint32_t q_first = quad0 + chunk * chunk_quads;
+      const uint32_t q_count = std::min(chunk_quads, quad0 + quads - q_first);
+      const uint32_t m = ((q_count * 4) + 31) / 32 * 32;
+      const uint32_t g_first = tile * tile_groups;
+      const uint32_t g_count = std::min(tile_groups, groups_total - g_first);
+      for (uint32_t q = 0; q < m / 4; ++q) {
+        for (uint32_t b = 0; b < kb; ++b) {
+          auto& word = memories->abuf[(q * kb) + b];
+          if (q < q_count) {
+            std::memcpy(word.data(), a_words + ((size_t{q_first + q} * kb) + b) * 144, 132);
+          } else {
+            std::fill(word.begin(), word.end(), 0);
+          }
+        }
+      }
+      for (uint32_t l = 0; l < nplanes; ++l) {
+        for (uint32_t g = 0; g < g_count; ++g) {
+          for (uint32_t b = 0; b < kb; ++b) {
+            std::memcpy(memories->wbuf[(g * kb) + b].data(),
+                        planes + (l * plane_bytes) + ((size_t{g_first + g} * kb) + b) * 144,
+                        144);
+          }
+        }
+        const GemmCommand command{.a_base = 0,
+                                  .a_stride = kb,
+                                  .kb = kb,
+                                  .m = m,
+                                  .w_base = 0,
+                                  .w_stride = kb,
+                                  .n8 = g_count,
+                                  .c_base = 0,
+                                  .wmode = nplanes == 1 ? 0U : l + 1,
+                                  .acc = l > 0};
+        hotarubi::iss::ExecuteGemm(command, *memories);
+      }
+      for (uint32_t q = 0; q < q_count; ++q) {
+        for (uint32_t g = 0; g < g_count; ++g) {
+          const auto& word = memories->fbuf[(q * g_count) + g];
+          for (uint32_t t = 0; t < 4; ++t) {
+            const uint32_t row = ((q_first + q) * 4) + t;
+            if (row < row0 || row >= row1) continue;
+            for (uint32_t col = 0; col < 8; ++col) {
+              c[(size_t{row} * N) + ((g_first + g) * 8) + col] = word[(t * 8) + col];
+            }
+          }
+        }
+      }
+      memories->log.Clear();
+    }
+  };
+  std::vector<std::thread> pool;
+  for (uint32_t t = 1; t < std::max<uint32_t>(threads, 1); ++t) pool.emplace_back(worker);
+  worker();
+  for (auto& thread : pool) thread.join();
+  return 0;
+}
+
+}  // extern "C"
