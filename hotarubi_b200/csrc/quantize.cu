@@ -1,0 +1,152 @@
+// FP32 -> MXINT8 on the device: the prologue of every hotarubi GEMM (the VEC
+// 'q' pass that writes ABUF on the NPU; EncodeMxint8 on the host).
+//
+//   host rule  tools/runtime/formats.cpp:35-56 (QuantizeInt8),
+//              :138-162 (EncodeMxint8)
+//   VEC rule   tools/iss/lane.cpp:384-423 (QuantizeElement, QuantizeBlock)
+//
+// Both rules: the block exponent is the FP32 exponent field of the block's
+// largest magnitude; q = x * 2^(6 - e) rounded to nearest even and clamped to
+// [-128, 127].  They differ on subnormal inputs (the VEC pass reads them as
+// zero) and on all-zero blocks' scale bytes only when those hold subnormals.
+//
+// Layout: a thread owns four consecutive elements of a row, eight lanes own a
+// 32-element block, a warp covers 128 elements (4 blocks) of one row.  The
+// block maximum is an integer max over the magnitude bits across 8 lanes.
+// Traffic is the compulsory 4 bytes in and 1 + 1/32 bytes out per element.
+#include <cstdint>
+
+#include "hrb_kernels.cuh"
+
+namespace hrb {
+namespace {
+
+__device__ __forceinline__ int32_t quantize_host_rule(uint32_t bits, int32_t e) {
+  const uint32_t f = (bits >> 23) & 0xFFu;
+  const uint32_t sig = f == 0 ? (bits & 0x7FFFFFu) : ((bits & 0x7FFFFFu) | 0x800000u);
+  // shift = (f == 0 ? -149 : f - 150) + 6 - e; inside a block it is <= -16.
+  const int32_t shift = (f == 0 ? -149 : static_cast<int32_t>(f) - 150) + 6 - e;
+  uint32_t mag;
+  if (shift >= 0) {
+    mag = shift > 8 ? 256u : (sig << shift);
+  } else {
+    const int32_t s = -shift;
+    if (s >= 32) {
+      mag = 0;
+    } else {
+      const uint32_t kept = sig >> s;
+      const uint32_t rest = sig & ((1u << s) - 1u);
+      const uint32_t half = 1u << (s - 1);
+      mag = kept + ((rest > half || (rest == half && (kept & 1u))) ? 1u : 0u);
+    }
+  }
+  const int32_t v = (bits >> 31) ? -static_cast<int32_t>(mag) : static_cast<int32_t>(mag);
+  return v < -128 ? -128 : (v > 127 ? 127 : v);
+}
+
+__device__ __forceinline__ int32_t quantize_vec_rule(uint32_t bits, uint32_t emax) {
+  const uint32_t f = (bits >> 23) & 0xFFu;
+  if (f == 0) return 0;
+  const uint32_t sig = (bits & 0x7FFFFFu) | 0x800000u;
+  const uint32_t shift = emax - f + 17u;
+  uint32_t mag = 0;
+  if (shift < 25u) {
+    const uint32_t whole = sig >> shift;
+    const uint32_t guard = (sig >> (shift - 1u)) & 1u;
+    const uint32_t sticky = (sig & ((1u << (shift - 1u)) - 1u)) != 0u;
+    mag = whole + ((guard && (sticky || (whole & 1u))) ? 1u : 0u);
+  }
+  if (bits >> 31) return mag >= 128u ? -128 : -static_cast<int32_t>(mag);
+  return mag >= 128u ? 127 : static_cast<int32_t>(mag);
+}
+
+__global__ void __launch_bounds__(256)
+k_quantize(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ QuantJob inline_job,
+           uint32_t* error_flag) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint32_t nwarps = (gridDim.x * blockDim.x) >> 5;
+  // Work item = (job, row, 128-element chunk); jobs are laid end to end and
+  // found by binary search over their prefix sums.
+  const uint64_t total = jobs != nullptr ? jobs[njobs - 1].unit_begin + jobs[njobs - 1].units
+                                         : inline_job.units;
+  for (uint64_t unit = warp; unit < total; unit += nwarps) {
+    uint32_t lo = 0, hi = njobs - 1;
+    while (jobs != nullptr && lo < hi) {
+      const uint32_t mid = (lo + hi + 1) >> 1;
+      if (jobs[mid].unit_begin <= unit) lo = mid; else hi = mid - 1;
+    }
+    const QuantJob& job = jobs != nullptr ? jobs[lo] : inline_job;
+    const uint64_t u = unit - job.unit_begin;
+    const uint32_t chunks = (job.kb + 3u) / 4u;
+    const uint32_t row = static_cast<uint32_t>(u / chunks);
+    const uint32_t chunk = static_cast<uint32_t>(u % chunks);
+    const uint32_t col0 = chunk * 128u + lane * 4u;
+    const float* src = job.x + static_cast<size_t>(row) * job.ldx;
+    uint32_t v[4];
+    if (col0 + 3u < job.cols && job.vec4) {
+      const float4 t = *reinterpret_cast<const float4*>(src + col0);
+      v[0] = __float_as_uint(t.x);
+      v[1] = __float_as_uint(t.y);
+      v[2] = __float_as_uint(t.z);
+      v[3] = __float_as_uint(t.w);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[i] = col0 + i < job.cols ? __float_as_uint(src[col0 + i]) : 0u;
+      }
+    }
+    uint32_t key = 0;  // host rule: max magnitude; VEC rule: max exponent field
+    bool bad = false;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t mag = v[i] & 0x7FFFFFFFu;
+      bad |= (mag >> 23) == 0xFFu;
+      const uint32_t k = job.vec_rule ? (mag >> 23) : mag;
+      key = k > key ? k : key;
+    }
+    key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 1));
+    key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 2));
+    key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 4));
+    if (!job.vec_rule && __any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(error_flag, 1u);
+    const uint32_t block = chunk * 4u + (lane >> 3);
+    if (block >= job.kb) continue;
+    int32_t q[4];
+    uint32_t scale;
+    if (job.vec_rule) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) q[i] = quantize_vec_rule(v[i], key);
+      scale = key == 0 ? 127u : key;
+    } else {
+      const int32_t e = key != 0 ? static_cast<int32_t>(key >> 23) - 127 : 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) q[i] = quantize_host_rule(v[i], e);
+      scale = static_cast<uint32_t>(e + 127);
+    }
+    const uint32_t packed = (static_cast<uint32_t>(q[0]) & 0xFFu) |
+                            ((static_cast<uint32_t>(q[1]) & 0xFFu) << 8) |
+                            ((static_cast<uint32_t>(q[2]) & 0xFFu) << 16) |
+                            ((static_cast<uint32_t>(q[3]) & 0xFFu) << 24);
+    const size_t kp = static_cast<size_t>(job.kb) * 32u;
+    *reinterpret_cast<uint32_t*>(job.q + static_cast<size_t>(row) * kp + col0) = packed;
+    if ((lane & 7u) == 0) job.scale[static_cast<size_t>(row) * job.kb + block] = static_cast<uint8_t>(scale);
+  }
+}
+
+}  // namespace
+
+void launch_quantize(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* inline_job,
+                     uint64_t total_units, uint32_t* error_flag, int sm_count,
+                     cudaStream_t stream) {
+  // One warp per unit, 8 warps per CTA, at most 8 resident CTAs per SM: a
+  // grid-stride loop over the rest.
+  uint64_t blocks = (total_units + 7) / 8;
+  const uint64_t cap = static_cast<uint64_t>(sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks == 0) blocks = 1;
+  QuantJob one{};
+  if (inline_job != nullptr) one = *inline_job;
+  k_quantize<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(jobs_dev, njobs, one, error_flag);
+}
+
+}  // namespace hrb

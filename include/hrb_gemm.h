@@ -1,0 +1,250 @@
+/* hrb_gemm.h — C ABI of the B200 backend for hotarubi's quantized GEMM.
+ *
+ * The hot path it replaces is the GEMM instruction of hotarubi's NPU as the
+ * instruction-set simulator executes it:
+ *
+ *   void hotarubi::iss::ExecuteGemm(const GemmCommand&, Memories&);
+ *       (tools/iss/gemm_array.hpp:33, tools/iss/gemm_array.cpp:149-186,
+ *        called from Machine::Execute, tools/iss/machine.cpp:339-343)
+ *
+ * and the dense Linear that hotarubi's compiler lowers into a chain of such
+ * instructions (LinearEmitter::Emit, tools/compiler/kernels.cpp:343-395).
+ *
+ * Conventions
+ *   - Plain C: pointers and sizes only.  No exception or C++ type crosses.
+ *   - Every entry point returns an hrb_status.  Where the reference calls
+ *     Require() (and aborts), this library returns HRB_EINVAL and keeps a
+ *     message for hrb_last_error(); the reference-facing C++ shim
+ *     (hotarubi_b200/host/iss_gemm.hpp) turns that back into the reference's
+ *     abort.
+ *   - FP32 data is IEEE binary32.  Results follow hotarubi's FP32 rules
+ *     (round to nearest even, subnormal inputs and results flushed to +0, a
+ *     zero result is +0): docs/design.md "Number formats" of the reference.
+ *   - "stream" arguments are cudaStream_t values passed as void*; NULL means
+ *     the context's own stream.
+ */
+#ifndef HRB_GEMM_H_
+#define HRB_GEMM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define HRB_API __attribute__((visibility("default")))
+#else
+#define HRB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum hrb_status {
+  HRB_OK = 0,
+  HRB_EINVAL = 1,   /* invalid argument: the reference would Require()-fail */
+  HRB_ECUDA = 2,    /* a CUDA runtime call failed (message in hrb_last_error) */
+  HRB_ENOMEM = 3,   /* device or pinned host allocation failed */
+  HRB_ENOTSUP = 4,  /* valid request this build does not serve */
+  HRB_EDATA = 5     /* non-finite activation given to the MXINT8 encoder
+                       (formats.cpp:37 Require) */
+} hrb_status;
+
+typedef struct hrb_ctx hrb_ctx;
+
+/* ---------------------------------------------------------------------
+ * Lifecycle
+ * ------------------------------------------------------------------- */
+
+/* Creates a context on CUDA device `device` with its own non-blocking
+ * stream.  Device buffers the context needs are owned by it. */
+HRB_API hrb_status hrb_create(int device, hrb_ctx** out);
+HRB_API hrb_status hrb_destroy(hrb_ctx* ctx);
+/* Waits for all work on the context's stream; returns HRB_EDATA when an
+ * MXINT8 encode since the last sync met Inf/NaN. */
+HRB_API hrb_status hrb_sync(hrb_ctx* ctx);
+/* Message of the last failed call on this context ("" if none). */
+HRB_API const char* hrb_last_error(const hrb_ctx* ctx);
+HRB_API const char* hrb_status_string(hrb_status status);
+/* The context's stream (a cudaStream_t) and a way to replace it. */
+HRB_API void* hrb_get_stream(const hrb_ctx* ctx);
+HRB_API hrb_status hrb_set_stream(hrb_ctx* ctx, void* stream);
+/* Number of this library's kernels launched on the context so far. */
+HRB_API uint64_t hrb_launch_count(const hrb_ctx* ctx);
+
+/* ---------------------------------------------------------------------
+ * 1. The ISS drop-in: one GEMM instruction over the NPU's on-chip memories
+ * ------------------------------------------------------------------- */
+
+/* GemmCommand (tools/iss/gemm_array.hpp:16-27), field for field. */
+typedef struct hrb_gemm_cmd {
+  uint32_t a_base;   /* ABUF word of token quad 0, block 0 */
+  uint32_t a_stride; /* ABUF words between token quads */
+  uint32_t kb;       /* K blocks of 32 */
+  uint32_t m;        /* tokens: a multiple of 32 from 32 to 992 */
+  uint32_t w_base;   /* WBUF word of column group 0, block 0 */
+  uint32_t w_stride; /* WBUF words between column groups of 8 */
+  uint32_t n8;       /* column groups of 8, 1..255 */
+  uint32_t c_base;   /* FBUF word of quad 0, group 0 */
+  uint32_t wmode;    /* 0 FP4, 1 W8_HI, 2 and 3 W8_LO (isa.hpp:88-92) */
+  uint32_t acc;      /* nonzero: accumulate onto FBUF */
+} hrb_gemm_cmd;
+
+/* Memory geometry of the reference (tools/iss/memories.hpp:20-27). */
+#define HRB_ABUF_WORDS 8192u
+#define HRB_ABUF_WORD_BYTES 132u
+#define HRB_WBUF_WORDS 2048u
+#define HRB_WBUF_WORD_BYTES 144u
+#define HRB_FBUF_WORDS 4096u
+#define HRB_FBUF_WORD_FLOATS 32u
+
+/* DecodeGemm (tools/iss/machine.cpp:93-104): the GEMM fields of one 128-bit
+ * instruction given as 16 little-endian bytes (isa.hpp:75-86). */
+HRB_API hrb_status hrb_gemm_decode(const uint8_t instruction[16], hrb_gemm_cmd* out);
+
+/* The checks of ExecuteGemm (gemm_array.cpp:150-156): HRB_OK or HRB_EINVAL
+ * with the reference's message in hrb_last_error (ctx may be NULL). */
+HRB_API hrb_status hrb_gemm_check(hrb_ctx* ctx, const hrb_gemm_cmd* cmd);
+
+/* ExecuteGemm (gemm_array.cpp:149-186) on host-resident memories:
+ *   abuf: HRB_ABUF_WORDS x 132 bytes, wbuf: HRB_WBUF_WORDS x 144 bytes,
+ *   fbuf: HRB_FBUF_WORDS x 32 FP32 bit patterns, updated in place.
+ * Addresses are masked to 20 bits and wrap modulo each depth as in the
+ * reference.  Bit-exact with the reference.  Synchronous: fbuf holds the
+ * result on return, as Machine::Execute requires (machine.cpp:281-298). */
+HRB_API hrb_status hrb_gemm_exec(hrb_ctx* ctx, const hrb_gemm_cmd* cmd,
+                         const uint8_t* abuf, const uint8_t* wbuf,
+                         uint32_t* fbuf);
+
+/* The same on device-resident memories (same layouts), asynchronous on
+ * `stream`.  For a simulator that keeps its memories on the GPU. */
+HRB_API hrb_status hrb_gemm_exec_device(hrb_ctx* ctx, const hrb_gemm_cmd* cmd,
+                                const void* abuf, const void* wbuf,
+                                void* fbuf, void* stream);
+
+/* The words ExecuteGemm records in Memories::log (gemm_array.cpp:164,172,
+ * 178,182): one byte per word, set to 1 when touched.  Host-only. */
+HRB_API hrb_status hrb_gemm_accesses(const hrb_gemm_cmd* cmd, uint8_t* abuf_reads,
+                             uint8_t* wbuf_reads, uint8_t* fbuf_reads,
+                             uint8_t* fbuf_writes);
+
+/* ---------------------------------------------------------------------
+ * 2. Dense GEMM: a whole Linear as hotarubi's compiler lowers it
+ * ------------------------------------------------------------------- */
+
+/* Weight formats.  kp = K rounded up to a multiple of 32, kb = kp / 32;
+ * a K tail is zero padding (formats.cpp:60, docs/design.md).  Scales are
+ * E8M0 bytes (e + 127), one per (output column, K block): [N][kb]. */
+typedef enum hrb_wfmt {
+  /* MXFP4: [N][kp/2] bytes, element 2j in the low nibble of byte j (the nibble
+   * order of a WBUF word, tensors.cpp:78-84); FP4 mode, SBIAS -7. */
+  HRB_WFMT_MXFP4 = 0,
+  /* W8: MXINT8 weights [N][kp] int8, run as a W8_HI chain then a W8_LO chain
+   * (SplitW8, weights.cpp:72-88; kernels.cpp:35-37). */
+  HRB_WFMT_W8 = 1,
+  /* MXFP8: [N][kp] OCP E4M3 bytes.  No reference counterpart: block sums are
+   * exact and rounded once to FP32 (nearest even), chained like FP4. */
+  HRB_WFMT_MXFP8 = 2
+} hrb_wfmt;
+
+typedef enum hrb_mode {
+  /* Bit-exact with the reference chain: each output's block values are
+   * added one by one in K order (W8: all HI blocks, then all LO blocks). */
+  HRB_MODE_EXACT = 0,
+  /* Tensor-core accumulation: within the stated FP32 tolerance of the exact
+   * chain (block values summed in another order). */
+  HRB_MODE_FAST = 1
+} hrb_mode;
+
+typedef enum hrb_quant {
+  HRB_QUANT_HOST = 0, /* EncodeMxint8 (formats.cpp:35-56,138-162) */
+  HRB_QUANT_VEC = 1   /* VEC 'q' pass (lane.cpp:384-423): subnormals -> 0 */
+} hrb_quant;
+
+typedef struct hrb_gemm_desc {
+  uint32_t wfmt;       /* hrb_wfmt */
+  uint32_t mode;       /* hrb_mode */
+  uint32_t M, N, K;    /* C[M][N] (+)= A[M][K] . W[N][K]^T, then + bias */
+  /* Activations: either FP32 `a` [M][lda] (encoded to MXINT8 on the device
+   * with `quant`), or pre-encoded `aq` [M][kp] int8 with `ascale` [M][kb]. */
+  const float* a;
+  uint32_t lda;
+  uint32_t quant;      /* hrb_quant, for `a` */
+  const int8_t* aq;
+  const uint8_t* ascale;
+  /* Weights in `wfmt` and their scales [N][kb]. */
+  const uint8_t* w;
+  const uint8_t* wscale;
+  const float* bias;   /* [N] or NULL: one FP32 add after the chain (ADDP,
+                          sparsedrive_encoder.cpp:422-428) */
+  float* c;            /* [M][ldc] */
+  uint32_t ldc;
+  uint32_t accumulate; /* nonzero: chains start from C's contents */
+  /* K pieces, in blocks (the LinearPiece split of kernels.hpp:70-75): the
+   * chain runs piece by piece, planes in order within each piece.  NULL or
+   * npieces 0: one piece of kb blocks.  At most 64 pieces. */
+  const uint32_t* pieces;
+  uint32_t npieces;
+} hrb_gemm_desc;
+
+/* One dense GEMM, all pointers device pointers, asynchronous on `stream`. */
+HRB_API hrb_status hrb_gemm_dense(hrb_ctx* ctx, const hrb_gemm_desc* desc, void* stream);
+
+/* The same with HOST pointers: copies the operands in, runs, copies C out,
+ * synchronizes.  The call a host-side caller (the ISS, a runtime) makes. */
+HRB_API hrb_status hrb_gemm_dense_host(hrb_ctx* ctx, const hrb_gemm_desc* desc);
+
+/* FP32 [rows][ldx] -> MXINT8 q [rows][kp] + scale bytes [rows][kb] on the
+ * device (the prologue of every GEMM; the VEC 'q' pass on the NPU). */
+HRB_API hrb_status hrb_quantize_mxint8(hrb_ctx* ctx, const float* x, uint32_t rows,
+                               uint32_t cols, uint32_t ldx, uint32_t quant,
+                               int8_t* q, uint8_t* scale, void* stream);
+
+/* ---------------------------------------------------------------------
+ * 3. Plans: a batch of independent dense GEMMs, prepared once, launched many
+ *    times without allocation or host synchronisation (capturable into a
+ *    CUDA graph).  Each GEMM keeps its own operands.
+ * ------------------------------------------------------------------- */
+
+typedef struct hrb_plan hrb_plan;
+
+HRB_API hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs,
+                           uint32_t count, hrb_plan** out);
+/* Launches the whole batch on `stream`; returns the number of kernels it
+ * launched in *launches (may be NULL). */
+HRB_API hrb_status hrb_plan_run(hrb_plan* plan, void* stream, uint32_t* launches);
+HRB_API hrb_status hrb_plan_destroy(hrb_plan* plan);
+
+/* ---------------------------------------------------------------------
+ * 4. Layout translation between hotarubi's image.bin word streams and the
+ *    dense formats (device pointers, asynchronous).
+ * ------------------------------------------------------------------- */
+
+/* A WBUF word stream of one plane as the compiler places it (PackWbuf,
+ * tensors.cpp:66-90: word (g * kb + b), 144 bytes, nibbles then 8 scales),
+ * to dense 4-bit codes [8*groups][kb*16] bytes and scales [8*groups][kb]. */
+HRB_API hrb_status hrb_wbuf_to_dense(hrb_ctx* ctx, const uint8_t* words,
+                             uint32_t groups, uint32_t kb, uint8_t* codes,
+                             uint8_t* scales, void* stream);
+
+/* Two W8 planes (HI words, LO words, same geometry) back to MXINT8 weights
+ * [8*groups][kb*32] int8 and their scales (the inverse of SplitW8). */
+HRB_API hrb_status hrb_w8_planes_to_dense(hrb_ctx* ctx, const uint8_t* hi_words,
+                                  const uint8_t* lo_words, uint32_t groups,
+                                  uint32_t kb, int8_t* q, uint8_t* scales,
+                                  void* stream);
+
+/* ABUF words (PackAbuf, formats.cpp:114-136; 144-byte DDR words in (quad,
+ * block) order) to MXINT8 activations [4*quads][kb*32] and scales. */
+HRB_API hrb_status hrb_abuf_to_dense(hrb_ctx* ctx, const uint8_t* words,
+                             uint32_t quads, uint32_t kb, int8_t* q,
+                             uint8_t* scales, void* stream);
+
+/* Row-major FP32 [rows][cols] to FBUF words (PackFbuf, formats.cpp:72-88). */
+HRB_API hrb_status hrb_dense_to_fbuf(hrb_ctx* ctx, const float* c, uint32_t rows,
+                             uint32_t cols, float* words, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HRB_GEMM_H_ */
