@@ -89,6 +89,7 @@ def load() -> ctypes.CDLL:
             "hrb_gemm_accesses": (ctypes.c_int, [ctypes.POINTER(GemmCmd), P, P, P, P]),
             "hrb_gemm_dense": (ctypes.c_int, [P, ctypes.POINTER(GemmDesc), P]),
             "hrb_gemm_dense_host": (ctypes.c_int, [P, ctypes.POINTER(GemmDesc)]),
+            "hrb_gemm_dense_noalloc": (ctypes.c_int, [ctypes.POINTER(GemmDesc), P]),
             "hrb_quantize_mxint8": (ctypes.c_int, [P, P, u32, u32, u32, u32, P, P, P]),
             "hrb_plan_create": (ctypes.c_int, [P, ctypes.POINTER(GemmDesc), u32,
                                                ctypes.POINTER(P)]),

@@ -253,6 +253,25 @@ Span circular(uint64_t base, uint64_t length, uint32_t depth) {
 
 }  // namespace
 
+namespace hrb {
+
+hrb_status check_desc_for_noalloc(const hrb_gemm_desc* desc, uint32_t* pieces,
+                                  uint32_t* npieces) {
+  return check_desc(nullptr, desc, pieces, npieces);
+}
+
+QuantJob make_quant_job_for_noalloc(const hrb_gemm_desc* d, int8_t* q, uint8_t* scale) {
+  return make_quant_job(d->a, d->M, d->K, d->lda, d->quant, q, scale);
+}
+
+DenseJob make_dense_job_for_noalloc(const hrb_gemm_desc* d, const int8_t* aq,
+                                    const uint8_t* ascale, const uint32_t* pieces,
+                                    uint32_t npieces) {
+  return make_dense_job(d, aq, ascale, pieces, npieces);
+}
+
+}  // namespace hrb
+
 extern "C" {
 
 const char* hrb_status_string(hrb_status status) {

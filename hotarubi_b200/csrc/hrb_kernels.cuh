@@ -6,6 +6,8 @@
 
 #include <cstdint>
 
+#include "../../include/hrb_gemm.h"
+
 namespace hrb {
 
 // One FP32 -> MXINT8 encode.  Units are (row, 128-column chunk) pairs;
@@ -62,6 +64,19 @@ struct ExecCmd {
 // ExecuteGemm on device-resident memories.
 int launch_exec(const ExecCmd& cmd, const uint8_t* abuf, const uint8_t* wbuf, float* fbuf,
                 cudaStream_t stream);
+
+}  // namespace hrb
+
+// The argument checks and job builders of the dense entry points, shared
+// with hrb_gemm_dense_noalloc (noalloc.cu), which has no context to hold a
+// message.
+namespace hrb {
+hrb_status check_desc_for_noalloc(const hrb_gemm_desc* desc, uint32_t* pieces,
+                                  uint32_t* npieces);
+QuantJob make_quant_job_for_noalloc(const hrb_gemm_desc* desc, int8_t* q, uint8_t* scale);
+DenseJob make_dense_job_for_noalloc(const hrb_gemm_desc* desc, const int8_t* aq,
+                                    const uint8_t* ascale, const uint32_t* pieces,
+                                    uint32_t npieces);
 
 // Layout translation kernels.
 void launch_wbuf_to_dense(const uint8_t* words, uint32_t groups, uint32_t kb, uint8_t* codes,

@@ -193,6 +193,25 @@ HRB_API hrb_status hrb_gemm_dense(hrb_ctx* ctx, const hrb_gemm_desc* desc, void*
  * synchronizes.  The call a host-side caller (the ISS, a runtime) makes. */
 HRB_API hrb_status hrb_gemm_dense_host(hrb_ctx* ctx, const hrb_gemm_desc* desc);
 
+/* hrb_gemm_dense for callers that cannot allocate device memory.  No
+ * counterpart in the reference: hotarubi's GEMM runs in the simulator's own
+ * host memory.  Some hosts of this backend may not call cudaMalloc (a
+ * simulator plugin inside a process whose device memory someone else owns,
+ * code that runs during stream capture, a real-time loop): this entry point
+ * takes the same descriptor with device pointers for all inputs and outputs,
+ * needs no context, and allocates nothing.  Its only scratch, the MXINT8
+ * encoding of FP32 activations, lives in a fixed device array of
+ * HRB_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
+ * exit; an FP32-input GEMM whose encoding (M*kp code bytes plus M*kp/32
+ * scale bytes, each rounded up to 256) does not fit returns HRB_EINVAL.
+ * All calls share that array: calls that overlap on the GPU race, so
+ * serialise them on one stream.  The first call on a device (the current
+ * device) looks the array's address up; make it before any stream capture.
+ * Runs on `stream` (NULL: the default stream).  Non-finite activations are
+ * not reported. */
+#define HRB_NOALLOC_SCRATCH_BYTES (4u << 20)
+HRB_API hrb_status hrb_gemm_dense_noalloc(const hrb_gemm_desc* desc, void* stream);
+
 /* FP32 [rows][ldx] -> MXINT8 q [rows][kp] + scale bytes [rows][kb] on the
  * device (the prologue of every GEMM; the VEC 'q' pass on the NPU). */
 HRB_API hrb_status hrb_quantize_mxint8(hrb_ctx* ctx, const float* x, uint32_t rows,

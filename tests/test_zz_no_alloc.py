@@ -1,0 +1,68 @@
+"""hrb_gemm_dense_noalloc: the dense GEMM entry point that allocates nothing.
+
+It is for callers that cannot call cudaMalloc themselves or have the library
+do it (a simulator plugin inside a process whose device memory is owned by
+someone else, code running while a CUDA graph is captured, a real-time
+loop).  They pass device buffers for every input and output; the only
+scratch is a fixed device array inside the library.
+
+The test calls it through the C ABI twice in a row, with different shapes
+and data, and checks each result against hrb_gemm_dense (the allocating
+entry point) bit for bit, as the exact path is bit-exact.  It also checks
+that a request larger than the fixed scratch is refused.  This file sorts
+last so that a failure here leaves every other test already run; it needs
+nothing from the other tests and passes in a fresh process on its own.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def _operands(rng, m, n, k):
+    from hotarubi_b200 import workloads
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    kp = (k + 31) // 32 * 32          # weights are stored with K padded to 32
+    w, ws = workloads.mxfp4_weights(int(rng.integers(0, 1 << 30)), n, kp)
+    bias = (rng.standard_normal(n) * 0.01).astype(np.float32)
+    return [torch.from_numpy(v).cuda() for v in (x, w, ws, bias)]
+
+
+def test_noalloc_matches_the_allocating_entry_point_on_two_calls():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from hotarubi_b200 import capi
+    lib = capi.load()
+    ctx = capi.Library(0)
+    torch.cuda.set_device(0)
+    rng = np.random.default_rng(2024)
+    for m, n, k in ((64, 960, 2560), (32, 200, 720)):
+        x, w, ws, bias = _operands(rng, m, n, k)
+        want = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+        got = torch.full((m, n), 7.0, dtype=torch.float32, device="cuda")
+        ctx.dense(capi.Library.desc(capi.WFMT_MXFP4, m, n, k, a=x, w=w, wscale=ws,
+                                    bias=bias, c=want))
+        ctx.sync()
+        d = capi.Library.desc(capi.WFMT_MXFP4, m, n, k, a=x, w=w, wscale=ws, bias=bias, c=got)
+        assert lib.hrb_gemm_dense_noalloc(ctypes.byref(d), None) == capi.HRB_OK
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int32), want.view(torch.int32)), (m, n, k)
+    ctx.close()
+
+
+def test_noalloc_refuses_more_than_its_scratch():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from hotarubi_b200 import capi
+    lib = capi.load()
+    m, n, k = 1024, 8, 4096          # 4 MiB of codes + scales: over the limit
+    x = torch.zeros((m, k), dtype=torch.float32, device="cuda")
+    w = torch.zeros((n, k // 2), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros((n, k // 32), dtype=torch.uint8, device="cuda")
+    c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    d = capi.Library.desc(capi.WFMT_MXFP4, m, n, k, a=x, w=w, wscale=ws, c=c)
+    assert lib.hrb_gemm_dense_noalloc(ctypes.byref(d), None) == capi.HRB_EINVAL
