@@ -64,58 +64,58 @@ def peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML every
+    millisecond while the timed region runs (reads only; nothing is set).
+    nvidia-smi's 200 ms sampling would miss a timed region of a few ms."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown",
+               0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap", 0x80: "hw_power_brake"}
 
     def __init__(self, device: int):
         self.device = device
-        self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self.stop = threading.Event()
+        self.nvml = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(self.device)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+            self.thread = threading.Thread(target=self._poll, daemon=True)
             self.thread.start()
-        except FileNotFoundError:
-            self.proc = None
+        except Exception:
+            self.nvml = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _poll(self):
+        p = self.nvml
+        while not self.stop.is_set():
+            try:
+                mhz = p.nvmlDeviceGetClockInfo(self.h, p.NVML_CLOCK_SM)
+                reasons = p.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((float(mhz), int(reasons)))
+            except Exception:
+                break
+            time.sleep(0.001)
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self.stop.set()
+        if self.nvml is not None:
+            self.thread.join(timeout=5)
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
+        sm = [s[0] for s in self.samples]
+        reasons = set()
+        for _, bits in self.samples:
+            for bit, name in self.REASONS.items():
+                if bits & bit:
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvml"}
 
 
 # ---------------------------------------------------------------------------
@@ -315,8 +315,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
 
-    e2e = time_e2e(lib, capi, sets, args.batch, max(1, min(args.steps, 3)), 1, mode)
-    if dist is not None:
+    e2e = None
+    if not args.no_e2e:
+        e2e = time_e2e(lib, capi, sets, args.batch, max(1, min(args.steps, 3)), 1, mode)
+    if dist is not None and e2e is not None:
         t = torch.tensor([e2e["ms_per_step"]], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e["ms_per_step"] = float(t.item())
@@ -372,6 +374,8 @@ def main() -> None:
     p.add_argument("--mode", choices=["exact", "fast"], default="exact")
     p.add_argument("--batch", type=int, default=128)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true", help="skip the host entry-point leg "
+                   "(profiling runs)")
     args = p.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
