@@ -38,7 +38,9 @@ struct hrb_ctx {
   // Operand staging for hrb_gemm_dense_host.
   void* staging = nullptr;
   size_t staging_bytes = 0;
-  uint32_t* d_error = nullptr;  // set by the encoder on Inf/NaN input
+  // Bit 0: the encoder met Inf/NaN; bit 1: a tensor-core kernel gave up
+  // waiting (it then leaves its outputs unwritten).
+  uint32_t* d_error = nullptr;
 };
 
 struct hrb_plan {
@@ -49,9 +51,8 @@ struct hrb_plan {
   uint64_t quant_units = 0;
   const hrb::QuantJob* d_quant = nullptr;
   struct Group {
-    uint32_t wfmt, mode, njobs, tiles;
-    const hrb::DenseJob* d_dense;
-    std::vector<hrb::DenseJob> host;  // the tensor-core path keeps jobs on the host
+    uint32_t wfmt, mode, nt, njobs, tiles;
+    const void* d_jobs;  // DenseJob (exact) or TcJob (tensor-core) array
   };
   std::vector<Group> groups;
 };
@@ -201,23 +202,49 @@ size_t act_scratch_bytes(uint32_t M, uint32_t K) {
   return align_up(size_t{M} * kb * 32u, 256) + align_up(size_t{M} * kb, 256);
 }
 
-// The GEMM itself, once activations are MXINT8 on the device.
-hrb_status run_dense(hrb_ctx* ctx, const hrb::DenseJob& job, uint32_t mode, cudaStream_t s) {
-  if (mode == HRB_MODE_FAST && hrb::tc_supported(job)) {
-    const int n = hrb::launch_tc(&job, 1, ctx->sm_count, s);
-    if (n < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
-    ctx->launches += static_cast<uint64_t>(n);
-  } else {
-    hrb::DenseJob one = job;
-    uint32_t tiles_n = 0;
-    const uint32_t tiles = hrb::dense_exact_tiles(job.M, job.N, tiles_n);
-    one.tiles_n = tiles_n;
-    one.tile_begin = 0;
-    ctx->launches += static_cast<uint64_t>(
-        hrb::launch_dense_exact(nullptr, 1, &one, tiles, job.wfmt, s));
-  }
+// The exact GEMM, once activations are MXINT8 on the device.
+hrb_status run_dense(hrb_ctx* ctx, const hrb::DenseJob& job, cudaStream_t s) {
+  hrb::DenseJob one = job;
+  uint32_t tiles_n = 0;
+  const uint32_t tiles = hrb::dense_exact_tiles(job.M, job.N, tiles_n);
+  one.tiles_n = tiles_n;
+  one.tile_begin = 0;
+  ctx->launches += static_cast<uint64_t>(
+      hrb::launch_dense_exact(nullptr, 1, &one, tiles, job.wfmt, s));
   HRB_CUDA(ctx, cudaGetLastError());
   return HRB_OK;
+}
+
+// The tensor-core path serves HRB_MODE_FAST GEMMs whose activations arrive
+// as FP32 (the encoder then writes the BF16 tiles it streams); MXINT8 input
+// runs the exact kernel, whose results are within any tolerance.
+bool use_tc(const hrb_gemm_desc* d) { return d->mode == HRB_MODE_FAST && d->a != nullptr; }
+
+// Tensor-core bytes of one GEMM: activation tiles then weight chunks.
+size_t tc_scratch_bytes(const hrb_gemm_desc* d) {
+  const uint32_t kb = blocks_of(d->K);
+  return align_up(hrb::tc_act_tile_bytes(d->M, kb), 1024) +
+         align_up(hrb::tc_weight_tile_bytes(d->wfmt, d->N, kb), 1024);
+}
+
+// Fills the encoder job and the tensor-core job of one GEMM whose prepared
+// operands live at `base` (tc_scratch_bytes of them).
+void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJob* tj) {
+  const uint32_t kb = blocks_of(d->K);
+  uint8_t* act = base;
+  uint8_t* wt = base + align_up(hrb::tc_act_tile_bytes(d->M, kb), 1024);
+  *qj = make_quant_job(d->a, d->M, d->K, d->lda, d->quant, nullptr, nullptr);
+  qj->tiles = act;
+  qj->tile_rows = hrb::tc_tokens_per_tile(d->M);
+  qj->k_steps = hrb::tc_k_steps(kb);
+  *tj = hrb::TcJob{};
+  hrb::tc_fill_job(*tj, d->wfmt, d->M, d->N, kb);
+  tj->a_tiles = act;
+  tj->w_tiles = wt;
+  tj->bias = d->bias;
+  tj->c = d->c;
+  tj->ldc = d->ldc;
+  tj->accumulate = d->accumulate != 0;
 }
 
 // ABUF/WBUF/FBUF words a command touches: the circular span from `base` of
@@ -333,6 +360,7 @@ hrb_status hrb_sync(hrb_ctx* ctx) {
   HRB_CUDA(ctx, cudaMemcpy(&flag, ctx->d_error, sizeof flag, cudaMemcpyDeviceToHost));
   if (flag != 0) {
     HRB_CUDA(ctx, cudaMemset(ctx->d_error, 0, sizeof(uint32_t)));
+    if (flag & 2u) return fail(ctx, HRB_ECUDA, "a tensor-core GEMM timed out waiting");
     return fail(ctx, HRB_EDATA, "MXINT8 input is infinite or NaN");
   }
   return HRB_OK;
@@ -515,6 +543,23 @@ hrb_status hrb_gemm_dense(hrb_ctx* ctx, const hrb_gemm_desc* d, void* stream) {
   if (st != HRB_OK) return st;
   HRB_CUDA(ctx, cudaSetDevice(ctx->device));
   cudaStream_t s = pick(ctx, stream);
+  if (use_tc(d)) {
+    st = grow(ctx, &ctx->scratch, &ctx->scratch_bytes, tc_scratch_bytes(d));
+    if (st != HRB_OK) return st;
+    hrb::QuantJob qj;
+    hrb::TcJob tj;
+    tc_jobs(d, static_cast<uint8_t*>(ctx->scratch), &qj, &tj);
+    hrb::launch_tile_weights(d->w, d->wscale, d->N, blocks_of(d->K), d->wfmt,
+                             const_cast<uint8_t*>(tj.w_tiles), s);
+    hrb::launch_quantize(nullptr, 1, &qj, qj.units, ctx->d_error, ctx->sm_count, s);
+    tj.tile_begin = 0;
+    const int n = hrb::launch_tc_jobs(nullptr, 1, &tj, qj.tile_rows, d->wfmt,
+                                      tj.m_tiles * tj.n_tiles, ctx->d_error, s);
+    if (n < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
+    ctx->launches += 2u + static_cast<uint64_t>(n);
+    HRB_CUDA(ctx, cudaGetLastError());
+    return HRB_OK;
+  }
   const int8_t* aq = d->aq;
   const uint8_t* ascale = d->ascale;
   if (d->a != nullptr) {
@@ -529,7 +574,7 @@ hrb_status hrb_gemm_dense(hrb_ctx* ctx, const hrb_gemm_desc* d, void* stream) {
     aq = q;
     ascale = sc;
   }
-  return run_dense(ctx, make_dense_job(d, aq, ascale, pieces, npieces), d->mode, s);
+  return run_dense(ctx, make_dense_job(d, aq, ascale, pieces, npieces), s);
 }
 
 hrb_status hrb_gemm_dense_host(hrb_ctx* ctx, const hrb_gemm_desc* d) {
@@ -607,7 +652,11 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
   for (uint32_t i = 0; i < count; ++i) {
     const hrb_status st = check_desc(ctx, &descs[i], pieces[i].data(), &npieces[i]);
     if (st != HRB_OK) return st;
-    if (descs[i].a != nullptr) scratch += act_scratch_bytes(descs[i].M, descs[i].K);
+    if (use_tc(&descs[i])) {
+      scratch += tc_scratch_bytes(&descs[i]);
+    } else if (descs[i].a != nullptr) {
+      scratch += align_up(act_scratch_bytes(descs[i].M, descs[i].K), 1024);
+    }
   }
   HRB_CUDA(ctx, cudaSetDevice(ctx->device));
   auto plan = new (std::nothrow) hrb_plan();
@@ -620,48 +669,66 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
       return cuda_fail(ctx, err, "plan scratch");
     }
   }
-  // Encode jobs and the activations each GEMM reads.
+  // Encoder jobs, exact-kernel jobs per format, tensor-core jobs per
+  // (tokens per tile, format).  Tensor-core weights are translated now, once.
   std::vector<hrb::QuantJob> quant;
-  std::vector<const int8_t*> aq(count);
-  std::vector<const uint8_t*> as(count);
+  std::vector<std::vector<hrb::DenseJob>> exact(3);
+  uint32_t exact_tiles[3] = {0, 0, 0};
+  struct TcKey { uint32_t nt, wfmt; };
+  std::vector<TcKey> tc_keys;
+  std::vector<std::vector<hrb::TcJob>> tc_groups;
+  std::vector<uint32_t> tc_tiles;
+  auto* sbase = static_cast<uint8_t*>(plan->d_scratch);
   size_t soff = 0;
   for (uint32_t i = 0; i < count; ++i) {
     const hrb_gemm_desc& d = descs[i];
-    if (d.a == nullptr) {
-      aq[i] = d.aq;
-      as[i] = d.ascale;
+    if (use_tc(&d)) {
+      hrb::QuantJob qj;
+      hrb::TcJob tj;
+      tc_jobs(&d, sbase + soff, &qj, &tj);
+      soff += tc_scratch_bytes(&d);
+      hrb::launch_tile_weights(d.w, d.wscale, d.N, blocks_of(d.K), d.wfmt,
+                               const_cast<uint8_t*>(tj.w_tiles), ctx->stream);
+      qj.unit_begin = plan->quant_units;
+      plan->quant_units += qj.units;
+      quant.push_back(qj);
+      size_t g = 0;
+      while (g < tc_keys.size() && !(tc_keys[g].nt == qj.tile_rows && tc_keys[g].wfmt == d.wfmt)) ++g;
+      if (g == tc_keys.size()) {
+        tc_keys.push_back({qj.tile_rows, d.wfmt});
+        tc_groups.emplace_back();
+        tc_tiles.push_back(0);
+      }
+      tj.tile_begin = tc_tiles[g];
+      tc_tiles[g] += tj.m_tiles * tj.n_tiles;
+      tc_groups[g].push_back(tj);
       continue;
     }
-    const uint32_t kb = blocks_of(d.K);
-    auto* q = static_cast<int8_t*>(plan->d_scratch) + soff;
-    auto* sc = reinterpret_cast<uint8_t*>(q) + align_up(size_t{d.M} * kb * 32u, 256);
-    soff += act_scratch_bytes(d.M, d.K);
-    hrb::QuantJob j = make_quant_job(d.a, d.M, d.K, d.lda, d.quant, q, sc);
-    j.unit_begin = plan->quant_units;
-    plan->quant_units += j.units;
-    quant.push_back(j);
-    aq[i] = q;
-    as[i] = sc;
-  }
-  // GEMM jobs grouped by (format, path).
-  std::vector<std::vector<hrb::DenseJob>> exact(3);
-  std::vector<std::vector<hrb::DenseJob>> fast(3);
-  uint32_t exact_tiles[3] = {0, 0, 0};
-  for (uint32_t i = 0; i < count; ++i) {
-    hrb::DenseJob j = make_dense_job(&descs[i], aq[i], as[i], pieces[i].data(), npieces[i]);
-    if (descs[i].mode == HRB_MODE_FAST && hrb::tc_supported(j)) {
-      fast[j.wfmt].push_back(j);
-    } else {
-      uint32_t tiles_n = 0;
-      const uint32_t tiles = hrb::dense_exact_tiles(j.M, j.N, tiles_n);
-      j.tiles_n = tiles_n;
-      j.tile_begin = exact_tiles[j.wfmt];
-      exact_tiles[j.wfmt] += tiles;
-      exact[j.wfmt].push_back(j);
+    const int8_t* aq = d.aq;
+    const uint8_t* as = d.ascale;
+    if (d.a != nullptr) {
+      const uint32_t kb = blocks_of(d.K);
+      auto* q = reinterpret_cast<int8_t*>(sbase + soff);
+      auto* sc = reinterpret_cast<uint8_t*>(q) + align_up(size_t{d.M} * kb * 32u, 256);
+      soff += align_up(act_scratch_bytes(d.M, d.K), 1024);
+      hrb::QuantJob j = make_quant_job(d.a, d.M, d.K, d.lda, d.quant, q, sc);
+      j.unit_begin = plan->quant_units;
+      plan->quant_units += j.units;
+      quant.push_back(j);
+      aq = q;
+      as = sc;
     }
+    hrb::DenseJob j = make_dense_job(&d, aq, as, pieces[i].data(), npieces[i]);
+    uint32_t tiles_n = 0;
+    const uint32_t tiles = hrb::dense_exact_tiles(j.M, j.N, tiles_n);
+    j.tiles_n = tiles_n;
+    j.tile_begin = exact_tiles[j.wfmt];
+    exact_tiles[j.wfmt] += tiles;
+    exact[j.wfmt].push_back(j);
   }
   size_t bytes = quant.size() * sizeof(hrb::QuantJob);
   for (auto& g : exact) bytes += g.size() * sizeof(hrb::DenseJob);
+  for (auto& g : tc_groups) bytes += g.size() * sizeof(hrb::TcJob);
   if (bytes > 0) {
     const cudaError_t err = cudaMalloc(&plan->d_jobs, bytes);
     if (err != cudaSuccess) {
@@ -679,18 +746,22 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
   }
   for (uint32_t f = 0; f < 3; ++f) {
     auto& g = exact[f];
-    if (!g.empty()) {
-      HRB_CUDA(ctx, cudaMemcpy(dst, g.data(), g.size() * sizeof(hrb::DenseJob),
-                               cudaMemcpyHostToDevice));
-      plan->groups.push_back({f, HRB_MODE_EXACT, static_cast<uint32_t>(g.size()),
-                              exact_tiles[f], reinterpret_cast<const hrb::DenseJob*>(dst), {}});
-      dst += g.size() * sizeof(hrb::DenseJob);
-    }
-    if (!fast[f].empty()) {
-      plan->groups.push_back({f, HRB_MODE_FAST, static_cast<uint32_t>(fast[f].size()), 0,
-                              nullptr, fast[f]});
-    }
+    if (g.empty()) continue;
+    HRB_CUDA(ctx, cudaMemcpy(dst, g.data(), g.size() * sizeof(hrb::DenseJob),
+                             cudaMemcpyHostToDevice));
+    plan->groups.push_back({f, HRB_MODE_EXACT, 0, static_cast<uint32_t>(g.size()),
+                            exact_tiles[f], dst});
+    dst += g.size() * sizeof(hrb::DenseJob);
   }
+  for (size_t g = 0; g < tc_groups.size(); ++g) {
+    HRB_CUDA(ctx, cudaMemcpy(dst, tc_groups[g].data(), tc_groups[g].size() * sizeof(hrb::TcJob),
+                             cudaMemcpyHostToDevice));
+    plan->groups.push_back({tc_keys[g].wfmt, HRB_MODE_FAST, tc_keys[g].nt,
+                            static_cast<uint32_t>(tc_groups[g].size()), tc_tiles[g], dst});
+    dst += tc_groups[g].size() * sizeof(hrb::TcJob);
+  }
+  HRB_CUDA(ctx, cudaGetLastError());
+  HRB_CUDA(ctx, cudaStreamSynchronize(ctx->stream));   // weight translation done
   *out = plan;
   return HRB_OK;
 }
@@ -708,11 +779,11 @@ hrb_status hrb_plan_run(hrb_plan* plan, void* stream, uint32_t* launches) {
   }
   for (auto& g : plan->groups) {
     if (g.mode == HRB_MODE_EXACT) {
-      n += static_cast<uint32_t>(hrb::launch_dense_exact(g.d_dense, g.njobs, nullptr, g.tiles,
-                                                         g.wfmt, s));
+      n += static_cast<uint32_t>(hrb::launch_dense_exact(
+          static_cast<const hrb::DenseJob*>(g.d_jobs), g.njobs, nullptr, g.tiles, g.wfmt, s));
     } else {
-      const int k = hrb::launch_tc(g.host.data(), static_cast<uint32_t>(g.host.size()),
-                                   ctx->sm_count, s);
+      const int k = hrb::launch_tc_jobs(static_cast<const hrb::TcJob*>(g.d_jobs), g.njobs,
+                                        nullptr, g.nt, g.wfmt, g.tiles, ctx->d_error, s);
       if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
       n += static_cast<uint32_t>(k);
     }

@@ -102,7 +102,7 @@ __device__ __forceinline__ uint32_t iss_round_pack(uint32_t sign, uint64_t mag,
          (static_cast<uint32_t>(kept) & 0x7FFFFFu);
 }
 
-__device__ __noinline__ uint32_t iss_add(uint32_t a, uint32_t b) {
+static __device__ __noinline__ uint32_t iss_add(uint32_t a, uint32_t b) {
   uint32_t ea = (a >> 23) & 0xFFu, eb = (b >> 23) & 0xFFu;
   uint32_t ma = ea ? ((a & 0x7FFFFFu) | 0x800000u) : 0u;
   uint32_t mb = eb ? ((b & 0x7FFFFFu) | 0x800000u) : 0u;

@@ -14,13 +14,18 @@ namespace hrb {
 // `unit_begin` is the prefix sum over the jobs of a launch.
 struct QuantJob {
   const float* x;
-  int8_t* q;          // [rows][kb * 32]
-  uint8_t* scale;     // [rows][kb]
+  int8_t* q;          // [rows][kb * 32], or null
+  uint8_t* scale;     // [rows][kb], or null
+  // Optional second output for the tensor-core path: the exact values
+  // q * 2^(e - 133) as BF16 tiles of tile_rows rows x 64 K, each row 128
+  // bytes in the 128-byte swizzle: [row tiles][k_steps][tile_rows][128 B].
+  uint8_t* tiles;
   uint64_t unit_begin;
   uint64_t units;     // rows * ceil(kb / 4)
   uint32_t rows, cols, ldx, kb;
   uint32_t vec_rule;  // 0: EncodeMxint8, 1: VEC 'q' pass
   uint32_t vec4;      // x rows are 16-byte aligned: load float4
+  uint32_t tile_rows, k_steps;
 };
 
 constexpr uint32_t kMaxPieces = 64;

@@ -60,6 +60,36 @@ __device__ __forceinline__ int32_t quantize_vec_rule(uint32_t bits, uint32_t ema
   return mag >= 128u ? 127 : static_cast<int32_t>(mag);
 }
 
+// BF16 bits of q * 2^(scale - 133), exact: |q| <= 128 has at most 8
+// significant bits.  Values below the normal range read as 0.
+__device__ __forceinline__ uint32_t bf16_of(int32_t q, uint32_t scale) {
+  if (q == 0) return 0u;
+  const uint32_t m = static_cast<uint32_t>(q < 0 ? -q : q);
+  const int32_t msb = 31 - __clz(m);
+  const int32_t field = msb + static_cast<int32_t>(scale) - 6;
+  if (field <= 0) return 0u;
+  if (field >= 255) return (q < 0 ? 0x8000u : 0u) | 0x7F80u;
+  const uint32_t mant = (m << (7 - msb)) & 0x7Fu;
+  return (q < 0 ? 0x8000u : 0u) | (static_cast<uint32_t>(field) << 7) | mant;
+}
+
+__device__ __forceinline__ uint32_t bf16_pair(int32_t lo, int32_t hi, uint32_t scale) {
+  return bf16_of(lo, scale) | (bf16_of(hi, scale) << 16);
+}
+
+// Four BF16 (elements col0..col0+3 of `row`) into the swizzled tile layout:
+// tile (row / tile_rows, col0 / 64), row r = row % tile_rows, 16-byte chunk c
+// of the 128-byte row stored at chunk c ^ (r % 8).
+__device__ __forceinline__ void write_tile(const QuantJob& job, uint32_t row, uint32_t col0,
+                                           uint32_t w0, uint32_t w1) {
+  const uint32_t rt = row / job.tile_rows, r = row % job.tile_rows;
+  const uint32_t step = col0 / 64u, within = col0 % 64u;
+  const uint32_t c = within / 8u, half = (within % 8u) / 4u;
+  const size_t tile = static_cast<size_t>(rt) * job.k_steps + step;
+  uint8_t* dst = job.tiles + tile * job.tile_rows * 128u + r * 128u + ((c ^ (r & 7u)) << 4) + half * 8u;
+  *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);
+}
+
 __global__ void __launch_bounds__(256)
 k_quantize(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ QuantJob inline_job,
            uint32_t* error_flag) {
@@ -110,7 +140,12 @@ k_quantize(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ QuantJo
     key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 4));
     if (!job.vec_rule && __any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(error_flag, 1u);
     const uint32_t block = chunk * 4u + (lane >> 3);
-    if (block >= job.kb) continue;
+    if (block >= job.kb) {
+      // The tensor-core tiles run K in steps of 64: when kb is odd the last
+      // step's second block is zero padding.
+      if (job.tiles != nullptr && block < 2u * job.k_steps) write_tile(job, row, col0, 0u, 0u);
+      continue;
+    }
     int32_t q[4];
     uint32_t scale;
     if (job.vec_rule) {
@@ -123,13 +158,18 @@ k_quantize(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ QuantJo
       for (int i = 0; i < 4; ++i) q[i] = quantize_host_rule(v[i], e);
       scale = static_cast<uint32_t>(e + 127);
     }
-    const uint32_t packed = (static_cast<uint32_t>(q[0]) & 0xFFu) |
-                            ((static_cast<uint32_t>(q[1]) & 0xFFu) << 8) |
-                            ((static_cast<uint32_t>(q[2]) & 0xFFu) << 16) |
-                            ((static_cast<uint32_t>(q[3]) & 0xFFu) << 24);
-    const size_t kp = static_cast<size_t>(job.kb) * 32u;
-    *reinterpret_cast<uint32_t*>(job.q + static_cast<size_t>(row) * kp + col0) = packed;
-    if ((lane & 7u) == 0) job.scale[static_cast<size_t>(row) * job.kb + block] = static_cast<uint8_t>(scale);
+    if (job.q != nullptr) {
+      const uint32_t packed = (static_cast<uint32_t>(q[0]) & 0xFFu) |
+                              ((static_cast<uint32_t>(q[1]) & 0xFFu) << 8) |
+                              ((static_cast<uint32_t>(q[2]) & 0xFFu) << 16) |
+                              ((static_cast<uint32_t>(q[3]) & 0xFFu) << 24);
+      const size_t kp = static_cast<size_t>(job.kb) * 32u;
+      *reinterpret_cast<uint32_t*>(job.q + static_cast<size_t>(row) * kp + col0) = packed;
+      if ((lane & 7u) == 0) job.scale[static_cast<size_t>(row) * job.kb + block] = static_cast<uint8_t>(scale);
+    }
+    if (job.tiles != nullptr) {
+      write_tile(job, row, col0, bf16_pair(q[0], q[1], scale), bf16_pair(q[2], q[3], scale));
+    }
   }
 }
 

@@ -1,0 +1,161 @@
+"""HRB_MODE_FAST (the tcgen05 tensor-core path) against the exact answer.
+
+Tolerance: the fast path computes the same exact products as the reference
+(BF16 holds every MXINT8 activation and every weight value exactly) but adds
+them in the tensor cores' order, in FP32.  Against the real-valued dot
+product of the dequantized operands (float64), each output may differ by at
+most (K/16 + 4) * 2^-23 * sum_k |a_k * w_k| (one FP32 rounding per 16-wide
+MMA step plus the bias/accumulate adds, doubled for safety).  The tests also
+report the max relative error and the ulp histogram against the bit-exact
+chain of the oracle.
+"""
+import numpy as np
+import pytest
+
+from oracle import cpu
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def dequant_a(x_bits):
+    q, s = cpu.encode_mxint8(x_bits)
+    sc = np.ldexp(1.0, s.astype(np.int64) - 133)
+    return q.astype(np.float64) * np.repeat(sc, 32, axis=1), q, s
+
+
+E2M1 = np.array([0, .5, 1, 1.5, 2, 3, 4, 6], np.float64)
+
+
+def dequant_w(wfmt, w, ws, n, kp):
+    sc = np.repeat(np.ldexp(1.0, ws.astype(np.int64) - 127), 32, axis=1)
+    if wfmt == 0:
+        codes = np.zeros((n, kp), np.uint8)
+        codes[:, 0::2] = w & 0xF
+        codes[:, 1::2] = w >> 4
+        v = E2M1[codes & 7] * np.where(codes & 8, -1.0, 1.0)
+        return v * sc
+    if wfmt == 1:
+        return w.view(np.int8).astype(np.float64) * sc * 2.0**-6
+    units = np.vectorize(lambda c: cpu.oracle().hrbo_e4m3_units(int(c)))(np.arange(256))
+    return units[w].astype(np.float64) * 2.0**-9 * sc
+
+
+def weights(rng, wfmt, n, kb):
+    k = kb * 32
+    if wfmt == 0:
+        code = rng.integers(0, 16, (n, k)).astype(np.uint8)
+        e = rng.integers(-10, -3, (n, kb))
+        code, e = cpu.canonical_mxfp4(code, e)
+        return cpu.pack_nibbles(code), (e + 127).astype(np.uint8)
+    if wfmt == 1:
+        return (rng.integers(-128, 128, (n, k)).astype(np.int8).view(np.uint8),
+                rng.integers(115, 125, (n, kb)).astype(np.uint8))
+    code = rng.integers(0, 254, (n, k)).astype(np.uint8)
+    code[code >= 0x7F] += 1
+    return code, rng.integers(117, 124, (n, kb)).astype(np.uint8)
+
+
+def ulp_hist(got, want):
+    g = got.view(np.int32).astype(np.int64)
+    w = want.view(np.int32).astype(np.int64)
+    g = np.where(g < 0, -(g & 0x7FFFFFFF), g)
+    w = np.where(w < 0, -(w & 0x7FFFFFFF), w)
+    d = np.abs(g - w)
+    return {"0": int((d == 0).sum()), "1": int((d == 1).sum()), "2-3": int(((d >= 2) & (d < 4)).sum()),
+            "4-15": int(((d >= 4) & (d < 16)).sum()), ">=16": int((d >= 16).sum())}
+
+
+def check_fast(hrb, wfmt, m, n, k, *, bias=False, accumulate=False, seed=0, plan=False):
+    from hotarubi_b200 import capi
+    rng = np.random.default_rng(seed)
+    kb = (k + 31) // 32
+    kp = kb * 32
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w, ws = weights(rng, wfmt, n, kb)
+    b = (rng.standard_normal(n) * 0.01).astype(np.float32) if bias else None
+    c0 = rng.standard_normal((m, n)).astype(np.float32) if accumulate else None
+    a_deq, q, s = dequant_a(x.view(np.uint32))
+    w_deq = dequant_w(wfmt, w, ws, n, kp)
+    ref = a_deq @ w_deq.T
+    absref = np.abs(a_deq) @ np.abs(w_deq).T
+    if c0 is not None:
+        ref += c0
+        absref += np.abs(c0)
+    if b is not None:
+        ref += b
+        absref += np.abs(b)
+    c = dev(c0) if c0 is not None else torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    keep = [dev(x), dev(w), dev(ws), None if b is None else dev(b)]
+    d = capi.Library.desc(wfmt, m, n, k, a=keep[0], w=keep[1], wscale=keep[2], bias=keep[3],
+                          c=c, accumulate=accumulate, mode=capi.MODE_FAST)
+    if plan:
+        p = hrb.plan([d])
+        p.run()
+        hrb.sync()
+        p.close()
+    else:
+        hrb.dense(d)
+        hrb.sync()
+    got = c.cpu().numpy()
+    tol = (k / 16 + 4) * 2.0**-23
+    err = np.abs(got.astype(np.float64) - ref)
+    bad = err > tol * absref + 1e-30
+    assert not bad.any(), (f"{bad.sum()} outputs off; worst rel "
+                           f"{(err / (absref + 1e-30)).max():.3e} tol {tol:.3e}")
+    exact = cpu.gemm_dense(wfmt, q, s, w, ws, n,
+                           bias_bits=None if b is None else b.view(np.uint32),
+                           c_init=None if c0 is None else c0.view(np.uint32))
+    ex = exact.view(np.float32).astype(np.float64)
+    rel = np.abs(got - ex) / (np.abs(ex) + 1e-30)
+    return {"max_rel_vs_exact": float(rel.max()), "ulp": ulp_hist(got, exact.view(np.float32))}
+
+
+@pytest.mark.parametrize("wfmt", [0, 1, 2])
+@pytest.mark.parametrize("shape", [(64, 960, 2560), (64, 2560, 960), (1, 8, 32),
+                                   (100, 130, 224), (300, 200, 320), (70, 72, 720)])
+def test_fast_matches_exact_dot_within_tolerance(hrb, wfmt, shape):
+    m, n, k = shape
+    check_fast(hrb, wfmt, m, n, k, seed=hash(shape) % 1000 + wfmt)
+
+
+@pytest.mark.parametrize("wfmt", [0, 1, 2])
+def test_fast_bias_and_accumulate(hrb, wfmt):
+    check_fast(hrb, wfmt, 96, 160, 736, bias=True, accumulate=True, seed=5 + wfmt)
+
+
+@pytest.mark.parametrize("wfmt", [0, 1, 2])
+def test_fast_through_a_plan(hrb, wfmt):
+    check_fast(hrb, wfmt, 64, 256, 512, bias=True, plan=True, seed=9 + wfmt)
+
+
+def test_fast_batched_plan_of_mixed_shapes(hrb):
+    from hotarubi_b200 import capi
+    rng = np.random.default_rng(41)
+    descs, keep, refs, outs = [], [], [], []
+    for i in range(9):
+        wfmt = i % 3
+        m, n, kb = int(rng.integers(1, 300)), int(rng.integers(8, 300)), int(rng.integers(1, 30))
+        x = rng.standard_normal((m, kb * 32)).astype(np.float32)
+        w, ws = weights(rng, wfmt, n, kb)
+        a_deq, _, _ = dequant_a(x.view(np.uint32))
+        w_deq = dequant_w(wfmt, w, ws, n, kb * 32)
+        refs.append((a_deq @ w_deq.T, np.abs(a_deq) @ np.abs(w_deq).T, kb * 32))
+        t = [dev(x), dev(w), dev(ws)]
+        keep += t
+        c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+        outs.append(c)
+        descs.append(capi.Library.desc(wfmt, m, n, kb * 32, a=t[0], w=t[1], wscale=t[2], c=c,
+                                       mode=capi.MODE_FAST))
+    plan = hrb.plan(descs)
+    plan.run()
+    hrb.sync()
+    for c, (ref, absref, k) in zip(outs, refs):
+        got = c.cpu().numpy().astype(np.float64)
+        assert (np.abs(got - ref) <= (k / 16 + 4) * 2.0**-23 * absref + 1e-30).all()
+    plan.close()
