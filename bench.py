@@ -208,35 +208,24 @@ def build_batch(torch, lib, capi, batch: int, mode: int, distinct: int = 4):
         inst.append(dict(
             a=torch.from_numpy(x).cuda(), w=torch.from_numpy(w).cuda(),
             ws=torch.from_numpy(ws).cuda(),
-            c=torch.zeros((M, N), dtype=torch.float32, device="cuda"),
-            aq=torch.zeros((M, K), dtype=torch.int8, device="cuda"),
-            asc=torch.zeros((M, KB), dtype=torch.uint8, device="cuda")))
+            c=torch.zeros((M, N), dtype=torch.float32, device="cuda")))
     full = [capi.Library.desc(capi.WFMT_MXFP4, M, N, K, a=d["a"], w=d["w"], wscale=d["ws"],
                               c=d["c"], mode=mode) for d in inst]
-    gemm_only = [capi.Library.desc(capi.WFMT_MXFP4, M, N, K, aq=d["aq"], ascale=d["asc"],
-                                   w=d["w"], wscale=d["ws"], c=d["c"], mode=mode)
-                 for d in inst]
-    # Pre-encode the activations for the GEMM-only plan.
-    for d in inst:
-        lib.quantize(d["a"], M, K, d["aq"], d["asc"])
-    lib.sync()
-    return inst, lib.plan(full), lib.plan(gemm_only), sets
+    torch.cuda.synchronize()
+    return inst, lib.plan(full), sets
 
 
-def time_plan(torch, lib, plan, steps: int, warmup: int, stream) -> tuple[float, int]:
-    launches = 0
-    for _ in range(warmup):
-        plan.run(stream.cuda_stream)
-    stream.synchronize()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(steps):
-        launches += plan.run(stream.cuda_stream)
-    end.record(stream)
-    end.synchronize()
-    lib.sync()
-    return start.elapsed_time(end) / steps, launches
+def traffic_from_profiles(kernel: str):
+    """DRAM bytes per launch of `kernel` on this workload, as summarised from
+    an ncu capture in profiles/dram_traffic.txt (kernel=bytes per GEMM)."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == kernel:
+            return float(parts[1])
+    return None
 
 
 def time_e2e(lib, capi, sets, batch: int, steps: int, warmup: int, mode: int) -> dict:
@@ -281,11 +270,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     mode = capi.MODE_FAST if args.mode == "fast" else capi.MODE_EXACT
     stream = torch.cuda.Stream()
     lib.set_stream(stream.cuda_stream)
-    inst, plan_full, plan_gemm, sets = build_batch(torch, lib, capi, args.batch, mode)
+    inst, plan_full, sets = build_batch(torch, lib, capi, args.batch, mode)
 
-    # Per-kernel timings (the dominant kernel's roofline): GEMM alone, and the
-    # encoder alone (full plan minus GEMM).
-    gemm_ms, _ = time_plan(torch, lib, plan_gemm, max(3, args.steps), 2, stream)
+    # Per-kernel device times (the dominant kernel's roofline): events around
+    # each launch of the plan, a few runs (not the timed region).
+    kernel_ms = plan_full.profile(reps=5, stream=stream.cuda_stream)
+    quant_ms, gemm_ms = kernel_ms[0], sum(kernel_ms[1:])
 
     if dist is not None:
         dist.barrier()
@@ -329,6 +319,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if rank == 0:
         pk = peaks()
         gemm_gbs = args.batch * ALG_BYTES_GEMM / (gemm_ms / 1e3) / 1e9
+        quant_gbs = args.batch * ALG_BYTES_QUANT / (quant_ms / 1e3) / 1e9
+        kname = "k_gemm_tc" if mode == capi.MODE_FAST else "k_dense_exact"
+        per_gemm_traffic = traffic_from_profiles(kname)
         step_gbs = args.batch * ALG_BYTES_STEP / (ms / 1e3) / 1e9
         total_gemms = world * args.batch
         line = {
@@ -345,12 +338,16 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                              "> 2 x 126 MB L2, no flush",
                        "parallelism": f"replicas x{world} (independent GEMMs)"},
             "step_hbm_gbs": step_gbs,
-            "roofline": {"bound": "hbm", "kernel": "k_dense_exact (GEMM)",
+            "roofline": {"bound": "hbm", "kernel": kname,
                          "achieved": gemm_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": gemm_gbs / pk["hbm_gbs"], "peak_source": pk["source"],
-                         "traffic": None,
+                         "traffic": (None if per_gemm_traffic is None
+                                     else per_gemm_traffic * args.batch),
                          "alg_bytes_per_launch": args.batch * ALG_BYTES_GEMM,
                          "launch_ms": gemm_ms},
+            "encoder": {"kernel": "k_quantize", "launch_ms": quant_ms, "achieved_gbs": quant_gbs,
+                        "frac": quant_gbs / pk["hbm_gbs"],
+                        "alg_bytes_per_launch": args.batch * ALG_BYTES_QUANT},
             "e2e": e2e, "gpu_launches": launches,
             "clocks": clocks.summary(),
         }
@@ -358,7 +355,6 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             line["cpu_baseline"] = {k: v for k, v in cpu_reference().items() if k != "seconds"}
         print(json.dumps(line), flush=True)
     plan_full.close()
-    plan_gemm.close()
     lib.close()
     if dist is not None:
         dist.barrier()
@@ -371,7 +367,7 @@ def main() -> None:
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--mode", choices=["exact", "fast"], default="exact")
+    p.add_argument("--mode", choices=["exact", "fast"], default="fast")
     p.add_argument("--batch", type=int, default=128)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the host entry-point leg "

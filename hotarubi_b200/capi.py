@@ -95,6 +95,8 @@ def load() -> ctypes.CDLL:
                                                ctypes.POINTER(P)]),
             "hrb_plan_run": (ctypes.c_int, [P, P, ctypes.POINTER(u32)]),
             "hrb_plan_destroy": (ctypes.c_int, [P]),
+            "hrb_plan_profile": (ctypes.c_int, [P, P, u32, ctypes.POINTER(ctypes.c_float), u32,
+                                                ctypes.POINTER(u32)]),
             "hrb_wbuf_to_dense": (ctypes.c_int, [P, P, u32, u32, P, P, P]),
             "hrb_w8_planes_to_dense": (ctypes.c_int, [P, P, P, u32, u32, P, P, P]),
             "hrb_abuf_to_dense": (ctypes.c_int, [P, P, u32, u32, P, P, P]),
@@ -273,6 +275,15 @@ class Plan:
         n = ctypes.c_uint32()
         self.owner._check(self.owner.lib.hrb_plan_run(self.h, stream or None, ctypes.byref(n)))
         return n.value
+
+    def profile(self, reps: int = 10, stream: int = 0) -> list[float]:
+        """Mean milliseconds of each kernel launch of the plan."""
+        cap = 16
+        ms = (ctypes.c_float * cap)()
+        n = ctypes.c_uint32()
+        self.owner._check(self.owner.lib.hrb_plan_profile(self.h, stream or None, reps, ms, cap,
+                                                          ctypes.byref(n)))
+        return [float(ms[i]) for i in range(n.value)]
 
     def close(self) -> None:
         if self.h:

@@ -766,18 +766,27 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
   return HRB_OK;
 }
 
-hrb_status hrb_plan_run(hrb_plan* plan, void* stream, uint32_t* launches) {
-  if (plan == nullptr) return HRB_EINVAL;
+}  // extern "C"
+
+namespace {
+
+// Launches every kernel of a plan on s; when `events` is given, records
+// events[i] before launch i and events[n] after the last.
+hrb_status plan_launch(hrb_plan* plan, cudaStream_t s, cudaEvent_t* events, uint32_t cap,
+                       uint32_t* launched) {
   hrb_ctx* ctx = plan->ctx;
-  HRB_CUDA(ctx, cudaSetDevice(ctx->device));
-  cudaStream_t s = pick(ctx, stream);
   uint32_t n = 0;
+  auto mark = [&]() {
+    if (events != nullptr && n <= cap) cudaEventRecord(events[n], s);
+  };
   if (plan->nquant > 0) {
+    mark();
     hrb::launch_quantize(plan->d_quant, plan->nquant, nullptr, plan->quant_units, ctx->d_error,
                          ctx->sm_count, s);
     ++n;
   }
   for (auto& g : plan->groups) {
+    mark();
     if (g.mode == HRB_MODE_EXACT) {
       n += static_cast<uint32_t>(hrb::launch_dense_exact(
           static_cast<const hrb::DenseJob*>(g.d_jobs), g.njobs, nullptr, g.tiles, g.wfmt, s));
@@ -788,9 +797,53 @@ hrb_status hrb_plan_run(hrb_plan* plan, void* stream, uint32_t* launches) {
       n += static_cast<uint32_t>(k);
     }
   }
+  mark();
   ctx->launches += n;
-  if (launches != nullptr) *launches = n;
+  *launched = n;
   HRB_CUDA(ctx, cudaGetLastError());
+  return HRB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+hrb_status hrb_plan_run(hrb_plan* plan, void* stream, uint32_t* launches) {
+  if (plan == nullptr) return HRB_EINVAL;
+  HRB_CUDA(plan->ctx, cudaSetDevice(plan->ctx->device));
+  uint32_t n = 0;
+  const hrb_status st = plan_launch(plan, pick(plan->ctx, stream), nullptr, 0, &n);
+  if (launches != nullptr) *launches = n;
+  return st;
+}
+
+hrb_status hrb_plan_profile(hrb_plan* plan, void* stream, uint32_t reps, float* ms, uint32_t cap,
+                            uint32_t* nkernels) {
+  if (plan == nullptr || ms == nullptr || nkernels == nullptr || reps == 0 || cap == 0) {
+    return HRB_EINVAL;
+  }
+  hrb_ctx* ctx = plan->ctx;
+  HRB_CUDA(ctx, cudaSetDevice(ctx->device));
+  cudaStream_t s = pick(ctx, stream);
+  std::vector<cudaEvent_t> ev(cap + 1);
+  for (auto& e : ev) HRB_CUDA(ctx, cudaEventCreate(&e));
+  std::vector<double> sum(cap, 0.0);
+  uint32_t n = 0;
+  hrb_status st = HRB_OK;
+  for (uint32_t r = 0; r < reps && st == HRB_OK; ++r) {
+    st = plan_launch(plan, s, ev.data(), cap, &n);
+    if (st != HRB_OK) break;
+    HRB_CUDA(ctx, cudaStreamSynchronize(s));
+    for (uint32_t i = 0; i < std::min(n, cap); ++i) {
+      float t = 0;
+      HRB_CUDA(ctx, cudaEventElapsedTime(&t, ev[i], ev[i + 1]));
+      sum[i] += t;
+    }
+  }
+  for (auto& e : ev) cudaEventDestroy(e);
+  if (st != HRB_OK) return st;
+  *nkernels = std::min(n, cap);
+  for (uint32_t i = 0; i < *nkernels; ++i) ms[i] = static_cast<float>(sum[i] / reps);
   return HRB_OK;
 }
 

@@ -20,8 +20,9 @@
 // One CTA computes C[tokens m0..m0+NT) x [columns n0..n0+128) with the weight
 // tile as the MMA's A operand (M = 128 columns) and the activation tile as B
 // (N = NT tokens): D[column][token] in TMEM, 128 lanes x NT columns.
-// Warp roles: 0 = bulk-copy producer, 1 = TMEM owner and MMA issuer,
-// 2..5 = weight decoders, then the epilogue (TMEM -> registers -> C).
+// Warp roles: 0 = weight-chunk producer, 1 = TMEM owner and MMA issuer,
+// 2 = activation-tile producer, 3..6 = weight decoders, then the epilogue
+// (TMEM -> registers -> C); warps 3..6 cover the four TMEM subpartitions.
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -51,18 +52,23 @@ __host__ __device__ constexpr uint32_t chunk_bytes(uint32_t wfmt) {
 
 template <uint32_t NT, uint32_t WF>
 struct TcCfg {
-  static constexpr uint32_t kStages = 3;                       // A + decoded W
-  static constexpr uint32_t kRaw = WF == 0 ? 8u : 4u;          // raw weight chunks
+  // Rings: activation tiles (bulk-copied), decoded BF16 weight tiles
+  // (written by the decoder warps), raw weight chunks (bulk-copied).  Sized
+  // so that NT = 64 fits two CTAs per SM.
+  static constexpr uint32_t kAStages = NT == 256 ? 3u : 4u;
+  static constexpr uint32_t kWStages = 2;
+  static constexpr uint32_t kRaw = WF == 0 ? 8u : 5u;
   static constexpr uint32_t kABytes = NT * kRowBytes;
-  static constexpr uint32_t kWBytes = kTileW * kRowBytes;      // decoded BF16
+  static constexpr uint32_t kWBytes = kTileW * kRowBytes;
   static constexpr uint32_t kChunk = chunk_bytes(WF);
+  static constexpr uint32_t kRawStride = (kChunk + 127) / 128 * 128;
   static constexpr uint32_t kTmemCols = NT < 32 ? 32 : NT;
   // Layout: [A stages][W stages][raw chunks][barriers][tmem slot]
-  static constexpr uint32_t kOffW = kStages * kABytes;
-  static constexpr uint32_t kOffRaw = kOffW + kStages * kWBytes;
-  static constexpr uint32_t kOffBar = kOffRaw + kRaw * ((kChunk + 127) / 128 * 128);
-  static constexpr uint32_t kRawStride = (kChunk + 127) / 128 * 128;
+  static constexpr uint32_t kOffW = kAStages * kABytes;
+  static constexpr uint32_t kOffRaw = kOffW + kWStages * kWBytes;
+  static constexpr uint32_t kOffBar = kOffRaw + kRaw * kRawStride;
   static constexpr uint32_t kSmem = kOffBar + 256 + 1024;  // + alignment slack
+  static constexpr uint32_t kThreads = 224;
 };
 
 struct TcParams {
@@ -186,7 +192,7 @@ __device__ __forceinline__ void decode_row(const uint8_t* raw, uint32_t r, uint8
 }
 
 template <uint32_t NT, uint32_t WF>
-__global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ TcParams p) {
+__global__ void __launch_bounds__(224, 1) k_gemm_tc(const __grid_constant__ TcParams p) {
   using Cfg = TcCfg<NT, WF>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -195,12 +201,13 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ TcPa
   uint8_t* sW = smem + Cfg::kOffW;
   uint8_t* sRaw = smem + Cfg::kOffRaw;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
-  uint64_t* a_full = bars;                          // [kStages] A tile landed
-  uint64_t* w_full = bars + Cfg::kStages;           // [kStages] decoded W ready (128 arrivals)
-  uint64_t* mma_done = bars + 2 * Cfg::kStages;     // [kStages] stage consumed by MMA
-  uint64_t* raw_full = bars + 3 * Cfg::kStages;     // [kRaw] raw chunk landed
-  uint64_t* raw_free = raw_full + Cfg::kRaw;        // [kRaw] raw chunk decoded (128 arrivals)
-  uint64_t* acc_full = raw_free + Cfg::kRaw;        // accumulator complete
+  uint64_t* a_full = bars;                            // [kAStages] tile landed
+  uint64_t* a_free = a_full + Cfg::kAStages;          // [kAStages] MMA done with it
+  uint64_t* w_full = a_free + Cfg::kAStages;          // [kWStages] decoded (128 arrivals)
+  uint64_t* w_free = w_full + Cfg::kWStages;          // [kWStages] MMA done with it
+  uint64_t* raw_full = w_free + Cfg::kWStages;        // [kRaw] chunk landed
+  uint64_t* raw_free = raw_full + Cfg::kRaw;          // [kRaw] chunk decoded (128 arrivals)
+  uint64_t* acc_full = raw_free + Cfg::kRaw;          // accumulator complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
   const TcJob& job = p.jobs != nullptr ? p.jobs[find_tc_job(p.jobs, p.njobs, blockIdx.x)]
@@ -211,10 +218,13 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ TcPa
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
 
   if (threadIdx.x == 0) {
-    for (uint32_t s = 0; s < Cfg::kStages; ++s) {
+    for (uint32_t s = 0; s < Cfg::kAStages; ++s) {
       mbar_init(&a_full[s], 1);
+      mbar_init(&a_free[s], 1);
+    }
+    for (uint32_t s = 0; s < Cfg::kWStages; ++s) {
       mbar_init(&w_full[s], 128);
-      mbar_init(&mma_done[s], 1);
+      mbar_init(&w_free[s], 1);
     }
     for (uint32_t s = 0; s < Cfg::kRaw; ++s) {
       mbar_init(&raw_full[s], 1);
@@ -234,11 +244,9 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ TcPa
   bool ok = true;
 
   if (warp == 0) {
-    // Producer: raw weight chunks run ahead of the A tiles by the raw ring.
+    // Raw weight chunks, as far ahead as the raw ring allows.
     if (lane == 0) {
-      const uint8_t* a_base = job.a_tiles + static_cast<size_t>(mt) * steps * Cfg::kABytes;
       const uint8_t* w_base = job.w_tiles + static_cast<size_t>(nt) * steps * Cfg::kChunk;
-      uint32_t a_issued = 0;
       for (uint32_t i = 0; i < steps && ok; ++i) {
         const uint32_t r = i % Cfg::kRaw;
         if (i >= Cfg::kRaw) ok = mbar_wait(&raw_free[r], ((i / Cfg::kRaw) - 1) & 1u, p.err);
@@ -246,33 +254,26 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ TcPa
         mbar_arrive_expect_tx(&raw_full[r], Cfg::kChunk);
         bulk_g2s(sRaw + r * Cfg::kRawStride, w_base + static_cast<size_t>(i) * Cfg::kChunk,
                  Cfg::kChunk, &raw_full[r]);
-        // Keep the A tiles kStages - 1 steps behind the raw chunks at most.
-        while (ok && a_issued < steps && a_issued + Cfg::kRaw <= i + Cfg::kStages) {
-          const uint32_t s = a_issued % Cfg::kStages;
-          if (a_issued >= Cfg::kStages) {
-            ok = mbar_wait(&mma_done[s], ((a_issued / Cfg::kStages) - 1) & 1u, p.err);
-          }
-          if (!ok) break;
-          mbar_arrive_expect_tx(&a_full[s], Cfg::kABytes);
-          bulk_g2s(sA + s * Cfg::kABytes, a_base + static_cast<size_t>(a_issued) * Cfg::kABytes,
-                   Cfg::kABytes, &a_full[s]);
-          ++a_issued;
-        }
       }
-      while (ok && a_issued < steps) {
-        const uint32_t s = a_issued % Cfg::kStages;
-        if (a_issued >= Cfg::kStages) {
-          ok = mbar_wait(&mma_done[s], ((a_issued / Cfg::kStages) - 1) & 1u, p.err);
-        }
-        if (!ok) break;
-        mbar_arrive_expect_tx(&a_full[s], Cfg::kABytes);
-        bulk_g2s(sA + s * Cfg::kABytes, a_base + static_cast<size_t>(a_issued) * Cfg::kABytes,
-                 Cfg::kABytes, &a_full[s]);
-        ++a_issued;
-      }
-      // Leave only after every copy this thread issued has landed.
+      // Leave only after every copy issued here has landed.
       for (uint32_t i = (steps > Cfg::kRaw ? steps - Cfg::kRaw : 0); i < steps && ok; ++i) {
         ok = mbar_wait(&raw_full[i % Cfg::kRaw], (i / Cfg::kRaw) & 1u, p.err);
+      }
+    }
+  } else if (warp == 2) {
+    // Activation tiles, as far ahead as the A ring allows.
+    if (lane == 0) {
+      const uint8_t* a_base = job.a_tiles + static_cast<size_t>(mt) * steps * Cfg::kABytes;
+      for (uint32_t i = 0; i < steps && ok; ++i) {
+        const uint32_t s = i % Cfg::kAStages;
+        if (i >= Cfg::kAStages) ok = mbar_wait(&a_free[s], ((i / Cfg::kAStages) - 1) & 1u, p.err);
+        if (!ok) break;
+        mbar_arrive_expect_tx(&a_full[s], Cfg::kABytes);
+        bulk_g2s(sA + s * Cfg::kABytes, a_base + static_cast<size_t>(i) * Cfg::kABytes,
+                 Cfg::kABytes, &a_full[s]);
+      }
+      for (uint32_t i = (steps > Cfg::kAStages ? steps - Cfg::kAStages : 0); i < steps && ok; ++i) {
+        ok = mbar_wait(&a_full[i % Cfg::kAStages], (i / Cfg::kAStages) & 1u, p.err);
       }
     }
   } else if (warp == 1) {
@@ -280,33 +281,35 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ TcPa
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16(kTileW, NT);
       for (uint32_t i = 0; i < steps && ok; ++i) {
-        const uint32_t s = i % Cfg::kStages, ph = (i / Cfg::kStages) & 1u;
-        ok = mbar_wait(&a_full[s], ph, p.err) && mbar_wait(&w_full[s], ph, p.err);
+        const uint32_t sa = i % Cfg::kAStages, sw = i % Cfg::kWStages;
+        ok = mbar_wait(&a_full[sa], (i / Cfg::kAStages) & 1u, p.err) &&
+             mbar_wait(&w_full[sw], (i / Cfg::kWStages) & 1u, p.err);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t a_addr = smem_addr(sW + s * Cfg::kWBytes);
-        const uint32_t b_addr = smem_addr(sA + s * Cfg::kABytes);
+        const uint32_t a_addr = smem_addr(sW + sw * Cfg::kWBytes);
+        const uint32_t b_addr = smem_addr(sA + sa * Cfg::kABytes);
 #pragma unroll
         for (uint32_t k = 0; k < kStepK / 16; ++k) {
           mma_bf16(tmem, desc_sw128(a_addr + k * 32u), desc_sw128(b_addr + k * 32u), idesc,
                    (i > 0 || k > 0) ? 1u : 0u);
         }
-        mma_commit(&mma_done[s]);
+        mma_commit(&a_free[sa]);
+        mma_commit(&w_free[sw]);
       }
       mma_commit(acc_full);
     }
   } else {
     // Decoders: thread d expands weight row d of every step.
-    const uint32_t d = threadIdx.x - 64u;
+    const uint32_t d = threadIdx.x - 96u;
     for (uint32_t i = 0; i < steps && ok; ++i) {
-      const uint32_t s = i % Cfg::kStages, r = i % Cfg::kRaw;
-      if (i >= Cfg::kStages) ok = mbar_wait(&mma_done[s], ((i / Cfg::kStages) - 1) & 1u, p.err);
+      const uint32_t sw = i % Cfg::kWStages, r = i % Cfg::kRaw;
+      if (i >= Cfg::kWStages) ok = mbar_wait(&w_free[sw], ((i / Cfg::kWStages) - 1) & 1u, p.err);
       ok = ok && mbar_wait(&raw_full[r], (i / Cfg::kRaw) & 1u, p.err);
       if (!ok) break;
-      decode_row<WF>(sRaw + r * Cfg::kRawStride, d, sW + s * Cfg::kWBytes);
+      decode_row<WF>(sRaw + r * Cfg::kRawStride, d, sW + sw * Cfg::kWBytes);
       fence_proxy_async_smem();
       mbar_arrive(&raw_free[r]);
-      mbar_arrive(&w_full[s]);
+      mbar_arrive(&w_full[sw]);
     }
     // Epilogue: D[column][token] -> C[token][column].
     if (ok) ok = mbar_wait(acc_full, 0, p.err);
@@ -390,7 +393,7 @@ int launch_one(const TcJob* jobs_dev, uint32_t njobs, const TcJob* inline_job, u
   p.njobs = njobs;
   p.err = err;
   if (inline_job != nullptr) p.inline_job = *inline_job;
-  k_gemm_tc<NT, WF><<<tiles, 192, Cfg::kSmem, s>>>(p);
+  k_gemm_tc<NT, WF><<<tiles, Cfg::kThreads, Cfg::kSmem, s>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? 1 : -1;
 }
 

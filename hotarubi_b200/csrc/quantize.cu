@@ -90,86 +90,147 @@ __device__ __forceinline__ void write_tile(const QuantJob& job, uint32_t row, ui
   *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);
 }
 
+// One unit of work: 128 consecutive elements (four blocks) of one row.
+struct Unit {
+  const QuantJob* job;
+  uint32_t row, chunk, col0;
+};
+
+// Loads the unit's four elements of this lane.
+__device__ __forceinline__ void load_unit(const Unit& t, uint32_t v[4]) {
+  const QuantJob& job = *t.job;
+  const float* src = job.x + static_cast<size_t>(t.row) * job.ldx;
+  if (t.col0 + 3u < job.cols && job.vec4) {
+    const float4 f = __ldcs(reinterpret_cast<const float4*>(src + t.col0));
+    v[0] = __float_as_uint(f.x);
+    v[1] = __float_as_uint(f.y);
+    v[2] = __float_as_uint(f.z);
+    v[3] = __float_as_uint(f.w);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = t.col0 + i < job.cols ? __float_as_uint(src[t.col0 + i]) : 0u;
+  }
+}
+
+// Block maximum, encoding and stores of one unit.
+__device__ __forceinline__ void finish_unit(const Unit& t, const uint32_t v[4], uint32_t lane,
+                                            uint32_t* error_flag) {
+  const QuantJob& job = *t.job;
+  uint32_t key = 0;  // host rule: max magnitude; VEC rule: max exponent field
+  bool bad = false;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t mag = v[i] & 0x7FFFFFFFu;
+    bad |= (mag >> 23) == 0xFFu;
+    const uint32_t k = job.vec_rule ? (mag >> 23) : mag;
+    key = k > key ? k : key;
+  }
+  key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 1));
+  key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 2));
+  key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 4));
+  if (!job.vec_rule && __any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(error_flag, 1u);
+  const uint32_t block = t.chunk * 4u + (lane >> 3);
+  if (block >= job.kb) {
+    // The tensor-core tiles run K in steps of 64: when kb is odd the last
+    // step's second block is zero padding.
+    if (job.tiles != nullptr && block < 2u * job.k_steps) write_tile(job, t.row, t.col0, 0u, 0u);
+    return;
+  }
+  int32_t q[4];
+  uint32_t scale;
+  if (job.vec_rule) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = quantize_vec_rule(v[i], key);
+    scale = key == 0 ? 127u : key;
+  } else {
+    const int32_t e = key != 0 ? static_cast<int32_t>(key >> 23) - 127 : 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = quantize_host_rule(v[i], e);
+    scale = static_cast<uint32_t>(e + 127);
+  }
+  if (job.q != nullptr) {
+    const uint32_t packed = (static_cast<uint32_t>(q[0]) & 0xFFu) |
+                            ((static_cast<uint32_t>(q[1]) & 0xFFu) << 8) |
+                            ((static_cast<uint32_t>(q[2]) & 0xFFu) << 16) |
+                            ((static_cast<uint32_t>(q[3]) & 0xFFu) << 24);
+    const size_t kp = static_cast<size_t>(job.kb) * 32u;
+    *reinterpret_cast<uint32_t*>(job.q + static_cast<size_t>(t.row) * kp + t.col0) = packed;
+    if ((lane & 7u) == 0) job.scale[static_cast<size_t>(t.row) * job.kb + block] = static_cast<uint8_t>(scale);
+  }
+  if (job.tiles != nullptr) {
+    write_tile(job, t.row, t.col0, bf16_pair(q[0], q[1], scale), bf16_pair(q[2], q[3], scale));
+  }
+}
+
+// Each warp walks a contiguous range of units, so the job a unit belongs to
+// is found by one binary search and then by stepping forward; the next
+// unit's load is issued before the current one is encoded.
 __global__ void __launch_bounds__(256)
 k_quantize(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ QuantJob inline_job,
            uint32_t* error_flag) {
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint32_t nwarps = (gridDim.x * blockDim.x) >> 5;
-  // Work item = (job, row, 128-element chunk); jobs are laid end to end and
-  // found by binary search over their prefix sums.
   const uint64_t total = jobs != nullptr ? jobs[njobs - 1].unit_begin + jobs[njobs - 1].units
                                          : inline_job.units;
-  for (uint64_t unit = warp; unit < total; unit += nwarps) {
+  const uint64_t per = (total + nwarps - 1) / nwarps;
+  const uint64_t begin = static_cast<uint64_t>(warp) * per;
+  const uint64_t end = begin + per < total ? begin + per : total;
+  if (begin >= end) return;
+  uint32_t j = 0;
+  if (jobs != nullptr) {
     uint32_t lo = 0, hi = njobs - 1;
-    while (jobs != nullptr && lo < hi) {
+    while (lo < hi) {
       const uint32_t mid = (lo + hi + 1) >> 1;
-      if (jobs[mid].unit_begin <= unit) lo = mid; else hi = mid - 1;
+      if (jobs[mid].unit_begin <= begin) lo = mid; else hi = mid - 1;
     }
-    const QuantJob& job = jobs != nullptr ? jobs[lo] : inline_job;
-    const uint64_t u = unit - job.unit_begin;
-    const uint32_t chunks = (job.kb + 3u) / 4u;
-    const uint32_t row = static_cast<uint32_t>(u / chunks);
-    const uint32_t chunk = static_cast<uint32_t>(u % chunks);
-    const uint32_t col0 = chunk * 128u + lane * 4u;
-    const float* src = job.x + static_cast<size_t>(row) * job.ldx;
-    uint32_t v[4];
-    if (col0 + 3u < job.cols && job.vec4) {
-      const float4 t = *reinterpret_cast<const float4*>(src + col0);
-      v[0] = __float_as_uint(t.x);
-      v[1] = __float_as_uint(t.y);
-      v[2] = __float_as_uint(t.z);
-      v[3] = __float_as_uint(t.w);
-    } else {
+    j = lo;
+  }
+  // Position of a unit inside its job: found once by division, then stepped
+  // (consecutive units are consecutive 128-element chunks of a row).
+  const QuantJob* job = jobs != nullptr ? &jobs[j] : &inline_job;
+  uint64_t job_end = job->unit_begin + job->units;
+  uint32_t chunks = (job->kb + 3u) / 4u;
+  uint32_t row, chunk;
+  {
+    const uint32_t u = static_cast<uint32_t>(begin - job->unit_begin);
+    row = u / chunks;
+    chunk = u % chunks;
+  }
+  auto locate = [&](uint64_t unit) {
+    if (unit >= job_end) {  // next job (only with a job array)
+      job = &jobs[++j];
+      job_end = job->unit_begin + job->units;
+      chunks = (job->kb + 3u) / 4u;
+      row = 0;
+      chunk = 0;
+    }
+    Unit t;
+    t.job = job;
+    t.row = row;
+    t.chunk = chunk;
+    t.col0 = chunk * 128u + lane * 4u;
+    if (++chunk == chunks) {
+      chunk = 0;
+      ++row;
+    }
+    return t;
+  };
+  Unit cur = locate(begin);
+  uint32_t v[4];
+  load_unit(cur, v);
+  for (uint64_t unit = begin; unit < end; ++unit) {
+    Unit nxt = cur;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    const bool more = unit + 1 < end;
+    if (more) {
+      nxt = locate(unit + 1);
+      load_unit(nxt, w);
+    }
+    finish_unit(cur, v, lane, error_flag);
+    cur = nxt;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        v[i] = col0 + i < job.cols ? __float_as_uint(src[col0 + i]) : 0u;
-      }
-    }
-    uint32_t key = 0;  // host rule: max magnitude; VEC rule: max exponent field
-    bool bad = false;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t mag = v[i] & 0x7FFFFFFFu;
-      bad |= (mag >> 23) == 0xFFu;
-      const uint32_t k = job.vec_rule ? (mag >> 23) : mag;
-      key = k > key ? k : key;
-    }
-    key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 1));
-    key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 2));
-    key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 4));
-    if (!job.vec_rule && __any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(error_flag, 1u);
-    const uint32_t block = chunk * 4u + (lane >> 3);
-    if (block >= job.kb) {
-      // The tensor-core tiles run K in steps of 64: when kb is odd the last
-      // step's second block is zero padding.
-      if (job.tiles != nullptr && block < 2u * job.k_steps) write_tile(job, row, col0, 0u, 0u);
-      continue;
-    }
-    int32_t q[4];
-    uint32_t scale;
-    if (job.vec_rule) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) q[i] = quantize_vec_rule(v[i], key);
-      scale = key == 0 ? 127u : key;
-    } else {
-      const int32_t e = key != 0 ? static_cast<int32_t>(key >> 23) - 127 : 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) q[i] = quantize_host_rule(v[i], e);
-      scale = static_cast<uint32_t>(e + 127);
-    }
-    if (job.q != nullptr) {
-      const uint32_t packed = (static_cast<uint32_t>(q[0]) & 0xFFu) |
-                              ((static_cast<uint32_t>(q[1]) & 0xFFu) << 8) |
-                              ((static_cast<uint32_t>(q[2]) & 0xFFu) << 16) |
-                              ((static_cast<uint32_t>(q[3]) & 0xFFu) << 24);
-      const size_t kp = static_cast<size_t>(job.kb) * 32u;
-      *reinterpret_cast<uint32_t*>(job.q + static_cast<size_t>(row) * kp + col0) = packed;
-      if ((lane & 7u) == 0) job.scale[static_cast<size_t>(row) * job.kb + block] = static_cast<uint8_t>(scale);
-    }
-    if (job.tiles != nullptr) {
-      write_tile(job, row, col0, bf16_pair(q[0], q[1], scale), bf16_pair(q[2], q[3], scale));
-    }
+    for (int i = 0; i < 4; ++i) v[i] = w[i];
   }
 }
 
@@ -178,8 +239,8 @@ k_quantize(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ QuantJo
 void launch_quantize(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* inline_job,
                      uint64_t total_units, uint32_t* error_flag, int sm_count,
                      cudaStream_t stream) {
-  // One warp per unit, 8 warps per CTA, at most 8 resident CTAs per SM: a
-  // grid-stride loop over the rest.
+  // Enough warps to keep every SM full (8 CTAs of 256 threads per SM); each
+  // walks a contiguous range of units.
   uint64_t blocks = (total_units + 7) / 8;
   const uint64_t cap = static_cast<uint64_t>(sm_count) * 8;
   if (blocks > cap) blocks = cap;

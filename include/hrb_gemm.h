@@ -232,6 +232,13 @@ HRB_API hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs,
  * launched in *launches (may be NULL). */
 HRB_API hrb_status hrb_plan_run(hrb_plan* plan, void* stream, uint32_t* launches);
 HRB_API hrb_status hrb_plan_destroy(hrb_plan* plan);
+/* Measurement aid: runs the plan `reps` times on `stream` with CUDA events
+ * around each kernel launch (synchronising after every run) and writes the
+ * mean milliseconds of launch i to ms[i] for the first min(launches, cap)
+ * launches; *nkernels receives that count.  Launch 0 is the activation
+ * encoder when the plan has FP32 inputs, then one GEMM launch per group. */
+HRB_API hrb_status hrb_plan_profile(hrb_plan* plan, void* stream, uint32_t reps, float* ms,
+                                    uint32_t cap, uint32_t* nkernels);
 
 /* ---------------------------------------------------------------------
  * 4. Layout translation between hotarubi's image.bin word streams and the
