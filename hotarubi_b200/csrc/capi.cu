@@ -51,7 +51,9 @@ struct hrb_plan {
   uint64_t quant_units = 0;
   const hrb::QuantJob* d_quant = nullptr;
   struct Group {
-    uint32_t wfmt, mode, nt, njobs, tiles;
+    uint32_t wfmt;
+    uint32_t kind;  // 0 exact kernel, 1 BF16 tensor-core kernel, 2 kind::mxf4 kernel
+    uint32_t nt, njobs, tiles;
     const void* d_jobs;  // DenseJob (exact) or TcJob (tensor-core) array
   };
   std::vector<Group> groups;
@@ -190,6 +192,7 @@ hrb::QuantJob make_quant_job(const float* x, uint32_t rows, uint32_t cols, uint3
   j.cols = cols;
   j.ldx = ldx;
   j.kb = blocks_of(cols);
+  j.cover_blocks = j.kb;
   j.units = static_cast<uint64_t>(rows) * ((j.kb + 3u) / 4u);
   j.vec_rule = quant == HRB_QUANT_VEC;
   j.vec4 = aligned(x, 16) && (ldx % 4u) == 0;
@@ -220,11 +223,21 @@ hrb_status run_dense(hrb_ctx* ctx, const hrb::DenseJob& job, cudaStream_t s) {
 // runs the exact kernel, whose results are within any tolerance.
 bool use_tc(const hrb_gemm_desc* d) { return d->mode == HRB_MODE_FAST && d->a != nullptr; }
 
-// Tensor-core bytes of one GEMM: activation tiles then weight chunks.
-size_t tc_scratch_bytes(const hrb_gemm_desc* d) {
+// MXFP4 weights in fast mode take the kind::mxf4 kernel (no decode);
+// W8 and MXFP8 take the BF16 kernel.
+bool use_mx(const hrb_gemm_desc* d) { return use_tc(d) && d->wfmt == HRB_WFMT_MXFP4; }
+
+// Tensor-core bytes of one GEMM: prepared activations then weight chunks.
+size_t tc_act_bytes(const hrb_gemm_desc* d) {
   const uint32_t kb = blocks_of(d->K);
-  return align_up(hrb::tc_act_tile_bytes(d->M, kb), 1024) +
-         align_up(hrb::tc_weight_tile_bytes(d->wfmt, d->N, kb), 1024);
+  return use_mx(d) ? hrb::mx_act_bytes(d->M, kb) : hrb::tc_act_tile_bytes(d->M, kb);
+}
+size_t tc_weight_bytes(const hrb_gemm_desc* d) {
+  const uint32_t kb = blocks_of(d->K);
+  return use_mx(d) ? hrb::mx_weight_bytes(d->N, kb) : hrb::tc_weight_tile_bytes(d->wfmt, d->N, kb);
+}
+size_t tc_scratch_bytes(const hrb_gemm_desc* d) {
+  return align_up(tc_act_bytes(d), 1024) + align_up(tc_weight_bytes(d), 1024);
 }
 
 // Fills the encoder job and the tensor-core job of one GEMM whose prepared
@@ -232,19 +245,49 @@ size_t tc_scratch_bytes(const hrb_gemm_desc* d) {
 void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJob* tj) {
   const uint32_t kb = blocks_of(d->K);
   uint8_t* act = base;
-  uint8_t* wt = base + align_up(hrb::tc_act_tile_bytes(d->M, kb), 1024);
+  uint8_t* wt = base + align_up(tc_act_bytes(d), 1024);
   *qj = make_quant_job(d->a, d->M, d->K, d->lda, d->quant, nullptr, nullptr);
   qj->tiles = act;
-  qj->tile_rows = hrb::tc_tokens_per_tile(d->M);
-  qj->k_steps = hrb::tc_k_steps(kb);
   *tj = hrb::TcJob{};
   hrb::tc_fill_job(*tj, d->wfmt, d->M, d->N, kb);
+  if (use_mx(d)) {
+    qj->tiles_kind = 2;
+    qj->tile_rows = hrb::mx_tokens_per_tile(d->M);
+    qj->k_steps = hrb::mx_k_steps(kb);
+    qj->cover_blocks = 8u * qj->k_steps;
+    tj->k_steps = qj->k_steps;
+    tj->m_tiles = (d->M + qj->tile_rows - 1) / qj->tile_rows;
+  } else {
+    qj->tiles_kind = 1;
+    qj->tile_rows = hrb::tc_tokens_per_tile(d->M);
+    qj->k_steps = hrb::tc_k_steps(kb);
+    qj->cover_blocks = 2u * qj->k_steps;
+  }
+  qj->units = static_cast<uint64_t>(qj->rows) * ((qj->cover_blocks + 3u) / 4u);
   tj->a_tiles = act;
   tj->w_tiles = wt;
   tj->bias = d->bias;
   tj->c = d->c;
   tj->ldc = d->ldc;
   tj->accumulate = d->accumulate != 0;
+}
+
+// Translates the weights of one tensor-core GEMM into the chunk layout.
+void tc_translate(const hrb_gemm_desc* d, const hrb::TcJob& tj, cudaStream_t s) {
+  const uint32_t kb = blocks_of(d->K);
+  if (use_mx(d)) {
+    hrb::launch_tile_weights_mxf4(d->w, d->wscale, d->N, kb, const_cast<uint8_t*>(tj.w_tiles), s);
+  } else {
+    hrb::launch_tile_weights(d->w, d->wscale, d->N, kb, d->wfmt, const_cast<uint8_t*>(tj.w_tiles), s);
+  }
+}
+
+// One launch of the tensor-core kernel for a group of jobs.
+int tc_launch(bool mx, const hrb::TcJob* jobs_dev, uint32_t njobs, const hrb::TcJob* inline_job,
+              uint32_t nt, uint32_t wfmt, uint32_t tiles, hrb_ctx* ctx, cudaStream_t s) {
+  if (mx) return hrb::launch_mxf4_jobs(jobs_dev, njobs, inline_job, nt, tiles, ctx->sm_count,
+                                       ctx->d_error, s);
+  return hrb::launch_tc_jobs(jobs_dev, njobs, inline_job, nt, wfmt, tiles, ctx->d_error, s);
 }
 
 // ABUF/WBUF/FBUF words a command touches: the circular span from `base` of
@@ -549,12 +592,13 @@ hrb_status hrb_gemm_dense(hrb_ctx* ctx, const hrb_gemm_desc* d, void* stream) {
     hrb::QuantJob qj;
     hrb::TcJob tj;
     tc_jobs(d, static_cast<uint8_t*>(ctx->scratch), &qj, &tj);
-    hrb::launch_tile_weights(d->w, d->wscale, d->N, blocks_of(d->K), d->wfmt,
-                             const_cast<uint8_t*>(tj.w_tiles), s);
+    // Rows of the last activation tile past M stay zero.
+    HRB_CUDA(ctx, cudaMemsetAsync(ctx->scratch, 0, align_up(tc_act_bytes(d), 1024), s));
+    tc_translate(d, tj, s);
     hrb::launch_quantize(nullptr, 1, &qj, qj.units, ctx->d_error, ctx->sm_count, s);
     tj.tile_begin = 0;
-    const int n = hrb::launch_tc_jobs(nullptr, 1, &tj, qj.tile_rows, d->wfmt,
-                                      tj.m_tiles * tj.n_tiles, ctx->d_error, s);
+    const int n = tc_launch(use_mx(d), nullptr, 1, &tj, qj.tile_rows, d->wfmt,
+                            tj.m_tiles * tj.n_tiles, ctx, s);
     if (n < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
     ctx->launches += 2u + static_cast<uint64_t>(n);
     HRB_CUDA(ctx, cudaGetLastError());
@@ -663,7 +707,9 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
   if (plan == nullptr) return HRB_ENOMEM;
   plan->ctx = ctx;
   if (scratch > 0) {
-    const cudaError_t err = cudaMalloc(&plan->d_scratch, scratch);
+    cudaError_t err = cudaMalloc(&plan->d_scratch, scratch);
+    // Zero once: padding rows of the last activation tile are never written.
+    if (err == cudaSuccess) err = cudaMemset(plan->d_scratch, 0, scratch);
     if (err != cudaSuccess) {
       hrb_plan_destroy(plan);
       return cuda_fail(ctx, err, "plan scratch");
@@ -674,7 +720,7 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
   std::vector<hrb::QuantJob> quant;
   std::vector<std::vector<hrb::DenseJob>> exact(3);
   uint32_t exact_tiles[3] = {0, 0, 0};
-  struct TcKey { uint32_t nt, wfmt; };
+  struct TcKey { uint32_t nt, wfmt, kind; };
   std::vector<TcKey> tc_keys;
   std::vector<std::vector<hrb::TcJob>> tc_groups;
   std::vector<uint32_t> tc_tiles;
@@ -687,15 +733,18 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
       hrb::TcJob tj;
       tc_jobs(&d, sbase + soff, &qj, &tj);
       soff += tc_scratch_bytes(&d);
-      hrb::launch_tile_weights(d.w, d.wscale, d.N, blocks_of(d.K), d.wfmt,
-                               const_cast<uint8_t*>(tj.w_tiles), ctx->stream);
+      tc_translate(&d, tj, ctx->stream);
       qj.unit_begin = plan->quant_units;
       plan->quant_units += qj.units;
       quant.push_back(qj);
       size_t g = 0;
-      while (g < tc_keys.size() && !(tc_keys[g].nt == qj.tile_rows && tc_keys[g].wfmt == d.wfmt)) ++g;
+      const uint32_t kind = use_mx(&d) ? 2u : 1u;
+      while (g < tc_keys.size() && !(tc_keys[g].nt == qj.tile_rows && tc_keys[g].wfmt == d.wfmt &&
+                                     tc_keys[g].kind == kind)) {
+        ++g;
+      }
       if (g == tc_keys.size()) {
-        tc_keys.push_back({qj.tile_rows, d.wfmt});
+        tc_keys.push_back({qj.tile_rows, d.wfmt, kind});
         tc_groups.emplace_back();
         tc_tiles.push_back(0);
       }
@@ -749,14 +798,13 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
     if (g.empty()) continue;
     HRB_CUDA(ctx, cudaMemcpy(dst, g.data(), g.size() * sizeof(hrb::DenseJob),
                              cudaMemcpyHostToDevice));
-    plan->groups.push_back({f, HRB_MODE_EXACT, 0, static_cast<uint32_t>(g.size()),
-                            exact_tiles[f], dst});
+    plan->groups.push_back({f, 0u, 0, static_cast<uint32_t>(g.size()), exact_tiles[f], dst});
     dst += g.size() * sizeof(hrb::DenseJob);
   }
   for (size_t g = 0; g < tc_groups.size(); ++g) {
     HRB_CUDA(ctx, cudaMemcpy(dst, tc_groups[g].data(), tc_groups[g].size() * sizeof(hrb::TcJob),
                              cudaMemcpyHostToDevice));
-    plan->groups.push_back({tc_keys[g].wfmt, HRB_MODE_FAST, tc_keys[g].nt,
+    plan->groups.push_back({tc_keys[g].wfmt, tc_keys[g].kind, tc_keys[g].nt,
                             static_cast<uint32_t>(tc_groups[g].size()), tc_tiles[g], dst});
     dst += tc_groups[g].size() * sizeof(hrb::TcJob);
   }
@@ -787,12 +835,12 @@ hrb_status plan_launch(hrb_plan* plan, cudaStream_t s, cudaEvent_t* events, uint
   }
   for (auto& g : plan->groups) {
     mark();
-    if (g.mode == HRB_MODE_EXACT) {
+    if (g.kind == 0) {
       n += static_cast<uint32_t>(hrb::launch_dense_exact(
           static_cast<const hrb::DenseJob*>(g.d_jobs), g.njobs, nullptr, g.tiles, g.wfmt, s));
     } else {
-      const int k = hrb::launch_tc_jobs(static_cast<const hrb::TcJob*>(g.d_jobs), g.njobs,
-                                        nullptr, g.nt, g.wfmt, g.tiles, ctx->d_error, s);
+      const int k = tc_launch(g.kind == 2, static_cast<const hrb::TcJob*>(g.d_jobs), g.njobs,
+                              nullptr, g.nt, g.wfmt, g.tiles, ctx, s);
       if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
       n += static_cast<uint32_t>(k);
     }

@@ -21,11 +21,16 @@ struct QuantJob {
   // bytes in the 128-byte swizzle: [row tiles][k_steps][tile_rows][128 B].
   uint8_t* tiles;
   uint64_t unit_begin;
-  uint64_t units;     // rows * ceil(kb / 4)
+  uint64_t units;     // rows * ceil(cover_blocks / 4)
   uint32_t rows, cols, ldx, kb;
   uint32_t vec_rule;  // 0: EncodeMxint8, 1: VEC 'q' pass
   uint32_t vec4;      // x rows are 16-byte aligned: load float4
   uint32_t tile_rows, k_steps;
+  // tiles_kind 1: the BF16 tiles above (64-element K steps).  tiles_kind 2:
+  // the activations as three E2M1 digit planes for kind::mxf4 (see
+  // gemm_mxf4.cu), 256-element K steps, with their E8M0 scales.
+  uint32_t tiles_kind;
+  uint32_t cover_blocks;  // K blocks written (kb plus the steps' zero padding)
 };
 
 constexpr uint32_t kMaxPieces = 64;

@@ -31,6 +31,18 @@ size_t tc_weight_tile_bytes(uint32_t wfmt, uint32_t N, uint32_t kb);
 size_t tc_act_tile_bytes(uint32_t M, uint32_t kb);
 void tc_fill_job(TcJob& t, uint32_t wfmt, uint32_t M, uint32_t N, uint32_t kb);
 
+// The kind::mxf4 path for MXFP4 weights (gemm_mxf4.cu): tokens per tile
+// (64 or 128), 256-element K steps, prepared operand sizes, the weight
+// translation and the launch.
+uint32_t mx_tokens_per_tile(uint32_t M);
+uint32_t mx_k_steps(uint32_t kb);
+size_t mx_weight_bytes(uint32_t N, uint32_t kb);
+size_t mx_act_bytes(uint32_t M, uint32_t kb);
+void launch_tile_weights_mxf4(const uint8_t* w, const uint8_t* ws, uint32_t N, uint32_t kb,
+                              uint8_t* out, cudaStream_t stream);
+int launch_mxf4_jobs(const TcJob* jobs_dev, uint32_t njobs, const TcJob* inline_job, uint32_t nt,
+                     uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t stream);
+
 // Dense weights -> the chunk layout the kernel streams.
 void launch_tile_weights(const uint8_t* w, const uint8_t* ws, uint32_t N, uint32_t kb,
                          uint32_t wfmt, uint8_t* out, cudaStream_t stream);

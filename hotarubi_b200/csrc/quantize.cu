@@ -90,6 +90,63 @@ __device__ __forceinline__ void write_tile(const QuantJob& job, uint32_t row, ui
   *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);
 }
 
+// E2M1 code of a digit in [-4, 4] (the integers E2M1 holds exactly):
+// 0 -> 0, 1 -> 0b010, 2 -> 0b100, 3 -> 0b101, 4 -> 0b110, sign in bit 3.
+__device__ __forceinline__ uint32_t e2m1_digit(int32_t d) {
+  const uint32_t m = static_cast<uint32_t>(d < 0 ? -d : d);
+  const uint32_t code = (0x65420u >> (4 * m)) & 0xFu;
+  return d < 0 ? (code | 8u) : code;
+}
+
+// The three E2M1 digit planes of four activations, as 4 nibbles per plane
+// (element 0 in the low nibble).  q = 64 d2 + 8 d1 + d0 with d0, d1 in
+// [-4, 3] (balanced base 8) and d2 in [-2, 2].
+__device__ __forceinline__ void digit_planes(const int32_t q[4], uint32_t planes[3]) {
+  planes[0] = planes[1] = planes[2] = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int32_t d0 = ((q[i] + 4) & 7) - 4;
+    const int32_t r1 = (q[i] - d0) >> 3;
+    const int32_t d1 = ((r1 + 4) & 7) - 4;
+    const int32_t d2 = (r1 - d1) >> 3;
+    planes[0] |= e2m1_digit(d0) << (4 * i);
+    planes[1] |= e2m1_digit(d1) << (4 * i);
+    planes[2] |= e2m1_digit(d2) << (4 * i);
+  }
+}
+
+// Elements col0..col0+3 of `row` into the kind::mxf4 activation blocks
+// (layout in gemm_mxf4.cu): per (row tile, 256-element step) the three digit
+// planes, each tile_rows rows of 128 bytes in the 128-byte swizzle, then the
+// planes' scale chunks; lanes that own a block's first elements also write
+// its three E8M0 scales (plane p: scale - 6 + 3p, i.e. 2^(e - 6 + 3p)).
+__device__ __forceinline__ void write_planes(const QuantJob& job, uint32_t row, uint32_t col0,
+                                             const uint32_t planes[3], uint32_t scale,
+                                             bool first_of_block) {
+  const uint32_t rt = row / job.tile_rows, r = row % job.tile_rows;
+  const uint32_t step = col0 / 256u, kk = col0 % 256u;
+  const size_t plane_bytes = static_cast<size_t>(job.tile_rows) * 128u;
+  uint8_t* blk = job.tiles + (static_cast<size_t>(rt) * job.k_steps + step) *
+                                 (3u * plane_bytes + 3u * 1024u);
+  const uint32_t byte = kk / 2u, c = byte / 16u, within = byte % 16u;
+  const uint32_t off = r * 128u + ((c ^ (r & 7u)) << 4) + within;
+#pragma unroll
+  for (int p = 0; p < 3; ++p) {
+    *reinterpret_cast<uint16_t*>(blk + p * plane_bytes + off) = static_cast<uint16_t>(planes[p]);
+  }
+  if (first_of_block) {
+    const uint32_t b = kk / 32u, g = b / 4u, s = b % 4u;
+    const uint32_t sf_off = (r % 32u) * 16u + ((r % 128u) / 32u) * 4u + s;
+    uint8_t* sf = blk + 3u * plane_bytes;
+#pragma unroll
+    for (int p = 0; p < 3; ++p) {
+      int32_t e = static_cast<int32_t>(scale) - 6 + 3 * p;
+      e = e < 0 ? 0 : (e > 254 ? 254 : e);
+      sf[(p * 2u + g) * 512u + sf_off] = static_cast<uint8_t>(e);
+    }
+  }
+}
+
 // One unit of work: 128 consecutive elements (four blocks) of one row.
 struct Unit {
   const QuantJob* job;
@@ -131,9 +188,16 @@ __device__ __forceinline__ void finish_unit(const Unit& t, const uint32_t v[4], 
   if (!job.vec_rule && __any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(error_flag, 1u);
   const uint32_t block = t.chunk * 4u + (lane >> 3);
   if (block >= job.kb) {
-    // The tensor-core tiles run K in steps of 64: when kb is odd the last
-    // step's second block is zero padding.
-    if (job.tiles != nullptr && block < 2u * job.k_steps) write_tile(job, t.row, t.col0, 0u, 0u);
+    // The tensor-core operands run K in whole steps: blocks past kb up to
+    // the step boundary are zero padding.
+    if (job.tiles != nullptr && block < job.cover_blocks) {
+      if (job.tiles_kind == 2) {
+        const uint32_t zero[3] = {0u, 0u, 0u};
+        write_planes(job, t.row, t.col0, zero, 127u, (lane & 7u) == 0);
+      } else {
+        write_tile(job, t.row, t.col0, 0u, 0u);
+      }
+    }
     return;
   }
   int32_t q[4];
@@ -158,7 +222,13 @@ __device__ __forceinline__ void finish_unit(const Unit& t, const uint32_t v[4], 
     if ((lane & 7u) == 0) job.scale[static_cast<size_t>(t.row) * job.kb + block] = static_cast<uint8_t>(scale);
   }
   if (job.tiles != nullptr) {
-    write_tile(job, t.row, t.col0, bf16_pair(q[0], q[1], scale), bf16_pair(q[2], q[3], scale));
+    if (job.tiles_kind == 2) {
+      uint32_t planes[3];
+      digit_planes(q, planes);
+      write_planes(job, t.row, t.col0, planes, scale, (lane & 7u) == 0);
+    } else {
+      write_tile(job, t.row, t.col0, bf16_pair(q[0], q[1], scale), bf16_pair(q[2], q[3], scale));
+    }
   }
 }
 
@@ -190,7 +260,7 @@ k_quantize(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ QuantJo
   // (consecutive units are consecutive 128-element chunks of a row).
   const QuantJob* job = jobs != nullptr ? &jobs[j] : &inline_job;
   uint64_t job_end = job->unit_begin + job->units;
-  uint32_t chunks = (job->kb + 3u) / 4u;
+  uint32_t chunks = (job->cover_blocks + 3u) / 4u;
   uint32_t row, chunk;
   {
     const uint32_t u = static_cast<uint32_t>(begin - job->unit_begin);
@@ -201,7 +271,7 @@ k_quantize(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ QuantJo
     if (unit >= job_end) {  // next job (only with a job array)
       job = &jobs[++j];
       job_end = job->unit_begin + job->units;
-      chunks = (job->kb + 3u) / 4u;
+      chunks = (job->cover_blocks + 3u) / 4u;
       row = 0;
       chunk = 0;
     }
