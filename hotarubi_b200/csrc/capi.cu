@@ -17,7 +17,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/hrb_gemm.h"
+#include "hrb_gemm.h"
 #include "hrb_kernels.cuh"
 #include "hrb_tc.cuh"
 

@@ -84,6 +84,36 @@ __device__ __forceinline__ const TcJob& mx_job(const MxParams& p, uint32_t tile)
   return p.jobs[lo];
 }
 
+// The fields of a tile's job the roles need, copied into registers once per
+// tile (stores to C could alias a job held in global memory, which would
+// force the compiler to reload fields after every store).
+struct TileInfo {
+  const uint8_t* w;
+  const uint8_t* a;
+  float* c;
+  const float* bias;
+  uint32_t M, N, ldc, accumulate, k_steps, mt, nt;
+};
+
+template <uint32_t NT>
+__device__ __forceinline__ TileInfo tile_info(const MxParams& p, uint32_t tile) {
+  const TcJob& job = mx_job(p, tile);
+  TileInfo t;
+  const uint32_t local = tile - job.tile_begin;
+  t.mt = local / job.n_tiles;
+  t.nt = local % job.n_tiles;
+  t.k_steps = job.k_steps;
+  t.w = job.w_tiles + static_cast<size_t>(t.nt) * t.k_steps * kWChunk;
+  t.a = job.a_tiles + static_cast<size_t>(t.mt) * t.k_steps * MxCfg<NT>::kABlock;
+  t.c = job.c;
+  t.bias = job.bias;
+  t.M = job.M;
+  t.N = job.N;
+  t.ldc = job.ldc;
+  t.accumulate = job.accumulate;
+  return t;
+}
+
 // Instruction descriptor of kind::mxf4 block-scaled (E2M1 x E2M1, E8M0
 // scales): A/B format 1 at [7,10)/[10,13), B scale id [4,6), N >> 3 at
 // [17,23), scale format E8M0 at bit 23, M >> 4 at [24,29), A scale id [29,31).
@@ -159,12 +189,10 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
     if (lane == 0) {
       uint32_t g = 0;  // global step counter across this CTA's tiles
       for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-        const TcJob& job = mx_job(p, tile);
-        const uint32_t local = tile - job.tile_begin;
-        const uint32_t mt = local / job.n_tiles, nt = local % job.n_tiles;
-        const uint8_t* wsrc = job.w_tiles + static_cast<size_t>(nt) * job.k_steps * kWChunk;
-        const uint8_t* asrc = job.a_tiles + static_cast<size_t>(mt) * job.k_steps * Cfg::kABlock;
-        for (uint32_t i = 0; i < job.k_steps && ok; ++i, ++g) {
+        const TileInfo ti = tile_info<NT>(p, tile);
+        const uint8_t* wsrc = ti.w;
+        const uint8_t* asrc = ti.a;
+        for (uint32_t i = 0; i < ti.k_steps && ok; ++i, ++g) {
           const uint32_t s = g % Cfg::kStages;
           if (g >= Cfg::kStages) ok = mbar_wait(&empty[s], ((g / Cfg::kStages) - 1) & 1u, p.err);
           if (!ok) break;
@@ -185,13 +213,13 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
       uint32_t g = 0, t = 0;
       const uint32_t sfa = tmem + Cfg::kColSfa;
       for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++t) {
-        const TcJob& job = mx_job(p, tile);
+        const uint32_t k_steps = mx_job(p, tile).k_steps;
         const uint32_t b = t % Cfg::kDBufs;
         if (t >= Cfg::kDBufs) ok = mbar_wait(&acc_empty[b], ((t / Cfg::kDBufs) - 1) & 1u, p.err);
         if (!ok) break;
         tc_fence_after();
         const uint32_t d = tmem + b * NT;
-        for (uint32_t i = 0; i < job.k_steps && ok; ++i, ++g) {
+        for (uint32_t i = 0; i < k_steps && ok; ++i, ++g) {
           const uint32_t s = g % Cfg::kStages;
           ok = mbar_wait(&full[s], (g / Cfg::kStages) & 1u, p.err);
           if (!ok) break;
@@ -229,16 +257,17 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
     const uint32_t sp = warp & 3u;
     uint32_t t = 0;
     for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++t) {
-      const TcJob& job = mx_job(p, tile);
-      const uint32_t local = tile - job.tile_begin;
-      const uint32_t mt = local / job.n_tiles, nt = local % job.n_tiles;
+      const TileInfo ti = tile_info<NT>(p, tile);
       const uint32_t b = t % Cfg::kDBufs;
       if (ok) ok = mbar_wait(&acc_full[b], (t / Cfg::kDBufs) & 1u, p.err);
       ok = __all_sync(0xFFFFFFFFu, ok);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t col = nt * kTileW + sp * 32u + lane;
-      const float bias = (job.bias != nullptr && col < job.N) ? job.bias[col] : 0.0f;
+      const uint32_t col = ti.nt * kTileW + sp * 32u + lane;
+      const bool col_ok = col < ti.N;
+      const float bias = (ti.bias != nullptr && col_ok) ? ti.bias[col] : 0.0f;
+      const uint32_t row0 = ti.mt * NT;
+      float* cbase = ti.c + static_cast<size_t>(row0) * ti.ldc + col;
 #pragma unroll 1
       for (uint32_t j0 = 0; j0 < NT; j0 += 16) {
         uint32_t v[16];
@@ -246,11 +275,10 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
         tmem_wait_ld();
 #pragma unroll
         for (uint32_t j = 0; j < 16; ++j) {
-          const uint32_t row = mt * NT + j0 + j;
-          if (row < job.M && col < job.N) {
-            float* dst = job.c + static_cast<size_t>(row) * job.ldc + col;
+          if (col_ok && row0 + j0 + j < ti.M) {
+            float* dst = cbase + static_cast<size_t>(j0 + j) * ti.ldc;
             float x = __uint_as_float(v[j]);
-            if (job.accumulate) x += *dst;
+            if (ti.accumulate) x += *dst;
             *dst = x + bias;
           }
         }

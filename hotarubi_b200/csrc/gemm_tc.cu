@@ -316,9 +316,16 @@ __global__ void __launch_bounds__(224, 1) k_gemm_tc(const __grid_constant__ TcPa
     ok = __all_sync(0xFFFFFFFFu, ok);   // tcgen05.ld needs the whole warp
     tc_fence_after();
     if (ok) {
+      // Job fields in registers: stores to C could alias the job in global
+      // memory and would force reloads after every store.
+      const uint32_t M = job.M, N = job.N, ldc = job.ldc, acc_in = job.accumulate;
+      const float* bias_p = job.bias;
       const uint32_t sp = warp & 3u;                      // TMEM subpartition of this warp
       const uint32_t col = nt * kTileW + sp * 32u + lane; // output column of this thread
-      const float bias = (job.bias != nullptr && col < job.N) ? job.bias[col] : 0.0f;
+      const bool col_ok = col < N;
+      const float bias = (bias_p != nullptr && col_ok) ? bias_p[col] : 0.0f;
+      const uint32_t row0 = mt * NT;
+      float* cbase = job.c + static_cast<size_t>(row0) * ldc + col;
 #pragma unroll 1
       for (uint32_t j0 = 0; j0 < NT; j0 += 16) {
         uint32_t v[16];
@@ -326,11 +333,10 @@ __global__ void __launch_bounds__(224, 1) k_gemm_tc(const __grid_constant__ TcPa
         tmem_wait_ld();
 #pragma unroll
         for (uint32_t j = 0; j < 16; ++j) {
-          const uint32_t row = mt * NT + j0 + j;
-          if (row < job.M && col < job.N) {
-            float* dst = job.c + static_cast<size_t>(row) * job.ldc + col;
+          if (col_ok && row0 + j0 + j < M) {
+            float* dst = cbase + static_cast<size_t>(j0 + j) * ldc;
             float x = __uint_as_float(v[j]);
-            if (job.accumulate) x += *dst;
+            if (acc_in) x += *dst;
             *dst = x + bias;
           }
         }

@@ -6,7 +6,7 @@
 
 #include <cstdint>
 
-#include "../../include/hrb_gemm.h"
+#include "hrb_gemm.h"
 
 namespace hrb {
 

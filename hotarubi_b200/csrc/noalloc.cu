@@ -32,7 +32,7 @@
 #include <cstdint>
 #include <mutex>
 
-#include "../../include/hrb_gemm.h"
+#include "hrb_gemm.h"
 #include "hrb_kernels.cuh"
 #include "hrb_tc.cuh"
 

@@ -123,10 +123,12 @@ __device__ __forceinline__ void digit_planes(const int32_t q[4], uint32_t planes
 __device__ __forceinline__ void write_planes(const QuantJob& job, uint32_t row, uint32_t col0,
                                              const uint32_t planes[3], uint32_t scale,
                                              bool first_of_block) {
-  const uint32_t rt = row / job.tile_rows, r = row % job.tile_rows;
-  const uint32_t step = col0 / 256u, kk = col0 % 256u;
-  const size_t plane_bytes = static_cast<size_t>(job.tile_rows) * 128u;
-  uint8_t* blk = job.tiles + (static_cast<size_t>(rt) * job.k_steps + step) *
+  // tile_rows is 64 or 128: shifts, not divisions.
+  const uint32_t shift = job.tile_rows == 64 ? 6u : 7u;
+  const uint32_t rt = row >> shift, r = row & (job.tile_rows - 1u);
+  const uint32_t step = col0 >> 8, kk = col0 & 255u;
+  const uint32_t plane_bytes = job.tile_rows * 128u;
+  uint8_t* blk = job.tiles + static_cast<size_t>(rt * job.k_steps + step) *
                                  (3u * plane_bytes + 3u * 1024u);
   const uint32_t byte = kk / 2u, c = byte / 16u, within = byte % 16u;
   const uint32_t off = r * 128u + ((c ^ (r & 7u)) << 4) + within;
@@ -169,23 +171,81 @@ __device__ __forceinline__ void load_unit(const Unit& t, uint32_t v[4]) {
   }
 }
 
+// q of four elements of one block.  Normal case: x * 2^(6 - e) is an exact
+// FP32 scaling (|result| < 2^7), and adding 1.5 * 2^23 rounds it to the
+// nearest integer, ties to even, exactly as QuantizeInt8 / QuantizeElement do;
+// the integer rules above handle blocks whose scale 2^(6 - e) leaves the FP32
+// range.  The VEC rule reads subnormal inputs as zero.
+__device__ __forceinline__ void quantize4(const uint32_t v[4], uint32_t key, bool vec_rule,
+                                          int32_t q[4], uint32_t& scale) {
+  int32_t e;  // block exponent, value scale 2^(e - 6)
+  if (vec_rule) {
+    e = static_cast<int32_t>(key) - 127;
+    scale = key == 0 ? 127u : key;
+  } else {
+    e = key != 0 ? static_cast<int32_t>(key >> 23) - 127 : 0;
+    scale = static_cast<uint32_t>(e + 127);
+  }
+  if (e >= -120 && e < 128) {
+    const float sc = __uint_as_float(static_cast<uint32_t>(133 - e) << 23);  // 2^(6 - e)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float y = __uint_as_float(v[i]) * sc;
+      int32_t r = __float_as_int(y + 12582912.0f) - 0x4B400000;
+      r = r < -128 ? -128 : (r > 127 ? 127 : r);
+      if (vec_rule && ((v[i] >> 23) & 0xFFu) == 0) r = 0;
+      q[i] = r;
+    }
+  } else if (vec_rule) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = quantize_vec_rule(v[i], key);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = quantize_host_rule(v[i], e);
+  }
+}
+
+// The three planes' E2M1 codes of four digits each, 4 nibbles per plane.
+// t = q + 292 = 64 (d2 + 4) + 8 (d1 + 4) + (d0 + 4): the base-8 digits of t
+// index the code table of d + 4 = 0..7 (d = -4..3).
+__device__ __forceinline__ void digit_planes_fast(const int32_t q[4], uint32_t planes[3]) {
+  constexpr uint32_t kLo = 0x0A0C0D0Eu;   // codes of d = -4, -3, -2, -1
+  constexpr uint32_t kHi = 0x05040200u;   // codes of d = 0, 1, 2, 3
+  uint32_t sel0 = 0, sel1 = 0, sel2 = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t t = static_cast<uint32_t>(q[i] + 292);
+    sel0 |= (t & 7u) << (4 * i);
+    sel1 |= ((t >> 3) & 7u) << (4 * i);
+    sel2 |= ((t >> 6) & 7u) << (4 * i);
+  }
+  const uint32_t sels[3] = {sel0, sel1, sel2};
+#pragma unroll
+  for (int p = 0; p < 3; ++p) {
+    const uint32_t c = __byte_perm(kLo, kHi, sels[p]);      // four codes, one per byte
+    const uint32_t n = (c | (c >> 4)) & 0x00FF00FFu;         // nibble pairs in bytes 0, 2
+    planes[p] = __byte_perm(n, 0u, 0x0020u) & 0xFFFFu;
+  }
+}
+
 // Block maximum, encoding and stores of one unit.
 __device__ __forceinline__ void finish_unit(const Unit& t, const uint32_t v[4], uint32_t lane,
                                             uint32_t* error_flag) {
   const QuantJob& job = *t.job;
+  const bool vec_rule = job.vec_rule != 0;
   uint32_t key = 0;  // host rule: max magnitude; VEC rule: max exponent field
   bool bad = false;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint32_t mag = v[i] & 0x7FFFFFFFu;
     bad |= (mag >> 23) == 0xFFu;
-    const uint32_t k = job.vec_rule ? (mag >> 23) : mag;
+    const uint32_t k = vec_rule ? (mag >> 23) : mag;
     key = k > key ? k : key;
   }
   key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 1));
   key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 2));
   key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 4));
-  if (!job.vec_rule && __any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(error_flag, 1u);
+  if (!vec_rule && __any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(error_flag, 1u);
   const uint32_t block = t.chunk * 4u + (lane >> 3);
   if (block >= job.kb) {
     // The tensor-core operands run K in whole steps: blocks past kb up to
@@ -202,16 +262,7 @@ __device__ __forceinline__ void finish_unit(const Unit& t, const uint32_t v[4], 
   }
   int32_t q[4];
   uint32_t scale;
-  if (job.vec_rule) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) q[i] = quantize_vec_rule(v[i], key);
-    scale = key == 0 ? 127u : key;
-  } else {
-    const int32_t e = key != 0 ? static_cast<int32_t>(key >> 23) - 127 : 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) q[i] = quantize_host_rule(v[i], e);
-    scale = static_cast<uint32_t>(e + 127);
-  }
+  quantize4(v, key, vec_rule, q, scale);
   if (job.q != nullptr) {
     const uint32_t packed = (static_cast<uint32_t>(q[0]) & 0xFFu) |
                             ((static_cast<uint32_t>(q[1]) & 0xFFu) << 8) |
@@ -224,7 +275,7 @@ __device__ __forceinline__ void finish_unit(const Unit& t, const uint32_t v[4], 
   if (job.tiles != nullptr) {
     if (job.tiles_kind == 2) {
       uint32_t planes[3];
-      digit_planes(q, planes);
+      digit_planes_fast(q, planes);
       write_planes(job, t.row, t.col0, planes, scale, (lane & 7u) == 0);
     } else {
       write_tile(job, t.row, t.col0, bf16_pair(q[0], q[1], scale), bf16_pair(q[2], q[3], scale));
