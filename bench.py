@@ -320,7 +320,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         pk = peaks()
         gemm_gbs = args.batch * ALG_BYTES_GEMM / (gemm_ms / 1e3) / 1e9
         quant_gbs = args.batch * ALG_BYTES_QUANT / (quant_ms / 1e3) / 1e9
-        kname = "k_gemm_tc" if mode == capi.MODE_FAST else "k_dense_exact"
+        kname = "k_gemm_mxf4" if mode == capi.MODE_FAST else "k_dense_exact"
         per_gemm_traffic = traffic_from_profiles(kname)
         step_gbs = args.batch * ALG_BYTES_STEP / (ms / 1e3) / 1e9
         total_gemms = world * args.batch
@@ -364,8 +364,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 def main() -> None:
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
-    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--mode", choices=["exact", "fast"], default="fast")
     p.add_argument("--batch", type=int, default=128)

@@ -2,7 +2,7 @@
 // staging, plans, and the dispatch onto the kernels.
 //
 // Error convention: where hotarubi's ExecuteGemm / EncodeMxint8 call Require()
-// (tools/iss/gemm_array.cpp:150-156, tools/runtime/formats.cpp:37) the entry
+// (tools/iss/gemm_array.cpp:113-119, tools/runtime/formats.cpp:37) the entry
 // points return HRB_EINVAL / HRB_EDATA with the same message text; nothing
 // aborts inside the library.
 #include <cuda_runtime.h>
@@ -50,11 +50,16 @@ struct hrb_plan {
   uint32_t nquant = 0;
   uint64_t quant_units = 0;
   const hrb::QuantJob* d_quant = nullptr;
+  // Activations of kind::mxf4 GEMMs: the digit-plane encoder's jobs.
+  uint32_t nplanes = 0;
+  uint64_t plane_units = 0;
+  const hrb::QuantJob* d_planes = nullptr;
   struct Group {
     uint32_t wfmt;
     uint32_t kind;  // 0 exact kernel, 1 BF16 tensor-core kernel, 2 kind::mxf4 kernel
     uint32_t nt, njobs, tiles;
     const void* d_jobs;  // DenseJob (exact) or TcJob (tensor-core) array
+    const hrb::MxTile* d_tiles;  // kind 2: the launch's output tiles
   };
   std::vector<Group> groups;
 };
@@ -263,7 +268,10 @@ void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJo
     qj->k_steps = hrb::tc_k_steps(kb);
     qj->cover_blocks = 2u * qj->k_steps;
   }
-  qj->units = static_cast<uint64_t>(qj->rows) * ((qj->cover_blocks + 3u) / 4u);
+  // Units of the encoders: (row, 256-element step) for the digit planes,
+  // (row, 128 elements) for the BF16 tiles.
+  qj->units = use_mx(d) ? static_cast<uint64_t>(qj->rows) * qj->k_steps
+                        : static_cast<uint64_t>(qj->rows) * ((qj->cover_blocks + 3u) / 4u);
   tj->a_tiles = act;
   tj->w_tiles = wt;
   tj->bias = d->bias;
@@ -283,10 +291,10 @@ void tc_translate(const hrb_gemm_desc* d, const hrb::TcJob& tj, cudaStream_t s) 
 }
 
 // One launch of the tensor-core kernel for a group of jobs.
-int tc_launch(bool mx, const hrb::TcJob* jobs_dev, uint32_t njobs, const hrb::TcJob* inline_job,
-              uint32_t nt, uint32_t wfmt, uint32_t tiles, hrb_ctx* ctx, cudaStream_t s) {
-  if (mx) return hrb::launch_mxf4_jobs(jobs_dev, njobs, inline_job, nt, tiles, ctx->sm_count,
-                                       ctx->d_error, s);
+int tc_launch(bool mx, const hrb::TcJob* jobs_dev, const hrb::MxTile* mx_tiles, uint32_t njobs,
+              const hrb::TcJob* inline_job, uint32_t nt, uint32_t wfmt, uint32_t tiles,
+              hrb_ctx* ctx, cudaStream_t s) {
+  if (mx) return hrb::launch_mxf4(mx_tiles, inline_job, nt, tiles, ctx->sm_count, ctx->d_error, s);
   return hrb::launch_tc_jobs(jobs_dev, njobs, inline_job, nt, wfmt, tiles, ctx->d_error, s);
 }
 
@@ -595,9 +603,13 @@ hrb_status hrb_gemm_dense(hrb_ctx* ctx, const hrb_gemm_desc* d, void* stream) {
     // Rows of the last activation tile past M stay zero.
     HRB_CUDA(ctx, cudaMemsetAsync(ctx->scratch, 0, align_up(tc_act_bytes(d), 1024), s));
     tc_translate(d, tj, s);
-    hrb::launch_quantize(nullptr, 1, &qj, qj.units, ctx->d_error, ctx->sm_count, s);
+    if (use_mx(d)) {
+      hrb::launch_quantize_planes(nullptr, 1, &qj, qj.units, ctx->d_error, ctx->sm_count, s);
+    } else {
+      hrb::launch_quantize(nullptr, 1, &qj, qj.units, ctx->d_error, ctx->sm_count, s);
+    }
     tj.tile_begin = 0;
-    const int n = tc_launch(use_mx(d), nullptr, 1, &tj, qj.tile_rows, d->wfmt,
+    const int n = tc_launch(use_mx(d), nullptr, nullptr, 1, &tj, qj.tile_rows, d->wfmt,
                             tj.m_tiles * tj.n_tiles, ctx, s);
     if (n < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
     ctx->launches += 2u + static_cast<uint64_t>(n);
@@ -717,7 +729,7 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
   }
   // Encoder jobs, exact-kernel jobs per format, tensor-core jobs per
   // (tokens per tile, format).  Tensor-core weights are translated now, once.
-  std::vector<hrb::QuantJob> quant;
+  std::vector<hrb::QuantJob> quant, planes;
   std::vector<std::vector<hrb::DenseJob>> exact(3);
   uint32_t exact_tiles[3] = {0, 0, 0};
   struct TcKey { uint32_t nt, wfmt, kind; };
@@ -734,9 +746,15 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
       tc_jobs(&d, sbase + soff, &qj, &tj);
       soff += tc_scratch_bytes(&d);
       tc_translate(&d, tj, ctx->stream);
-      qj.unit_begin = plan->quant_units;
-      plan->quant_units += qj.units;
-      quant.push_back(qj);
+      if (use_mx(&d)) {
+        qj.unit_begin = plan->plane_units;
+        plan->plane_units += qj.units;
+        planes.push_back(qj);
+      } else {
+        qj.unit_begin = plan->quant_units;
+        plan->quant_units += qj.units;
+        quant.push_back(qj);
+      }
       size_t g = 0;
       const uint32_t kind = use_mx(&d) ? 2u : 1u;
       while (g < tc_keys.size() && !(tc_keys[g].nt == qj.tile_rows && tc_keys[g].wfmt == d.wfmt &&
@@ -775,9 +793,19 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
     exact_tiles[j.wfmt] += tiles;
     exact[j.wfmt].push_back(j);
   }
-  size_t bytes = quant.size() * sizeof(hrb::QuantJob);
+  size_t bytes = (quant.size() + planes.size()) * sizeof(hrb::QuantJob);
   for (auto& g : exact) bytes += g.size() * sizeof(hrb::DenseJob);
   for (auto& g : tc_groups) bytes += g.size() * sizeof(hrb::TcJob);
+  // kind::mxf4 groups also get their output tiles located on the host.
+  std::vector<std::vector<hrb::MxTile>> mx_tiles(tc_groups.size());
+  for (size_t g = 0; g < tc_groups.size(); ++g) {
+    if (tc_keys[g].kind != 2) continue;
+    mx_tiles[g].resize(tc_tiles[g]);
+    for (const hrb::TcJob& tj : tc_groups[g]) {
+      hrb::mx_fill_tiles(tj, tc_keys[g].nt, mx_tiles[g].data() + tj.tile_begin);
+    }
+    bytes += 16 + mx_tiles[g].size() * sizeof(hrb::MxTile);  // 16: alignment slack
+  }
   if (bytes > 0) {
     const cudaError_t err = cudaMalloc(&plan->d_jobs, bytes);
     if (err != cudaSuccess) {
@@ -793,20 +821,37 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
     plan->nquant = static_cast<uint32_t>(quant.size());
     dst += quant.size() * sizeof(hrb::QuantJob);
   }
+  if (!planes.empty()) {
+    HRB_CUDA(ctx, cudaMemcpy(dst, planes.data(), planes.size() * sizeof(hrb::QuantJob),
+                             cudaMemcpyHostToDevice));
+    plan->d_planes = reinterpret_cast<const hrb::QuantJob*>(dst);
+    plan->nplanes = static_cast<uint32_t>(planes.size());
+    dst += planes.size() * sizeof(hrb::QuantJob);
+  }
   for (uint32_t f = 0; f < 3; ++f) {
     auto& g = exact[f];
     if (g.empty()) continue;
     HRB_CUDA(ctx, cudaMemcpy(dst, g.data(), g.size() * sizeof(hrb::DenseJob),
                              cudaMemcpyHostToDevice));
-    plan->groups.push_back({f, 0u, 0, static_cast<uint32_t>(g.size()), exact_tiles[f], dst});
+    plan->groups.push_back({f, 0u, 0, static_cast<uint32_t>(g.size()), exact_tiles[f], dst,
+                            nullptr});
     dst += g.size() * sizeof(hrb::DenseJob);
   }
   for (size_t g = 0; g < tc_groups.size(); ++g) {
     HRB_CUDA(ctx, cudaMemcpy(dst, tc_groups[g].data(), tc_groups[g].size() * sizeof(hrb::TcJob),
                              cudaMemcpyHostToDevice));
     plan->groups.push_back({tc_keys[g].wfmt, tc_keys[g].kind, tc_keys[g].nt,
-                            static_cast<uint32_t>(tc_groups[g].size()), tc_tiles[g], dst});
+                            static_cast<uint32_t>(tc_groups[g].size()), tc_tiles[g], dst,
+                            nullptr});
     dst += tc_groups[g].size() * sizeof(hrb::TcJob);
+    if (!mx_tiles[g].empty()) {
+      auto* base = static_cast<uint8_t*>(plan->d_jobs);
+      dst = base + align_up(static_cast<size_t>(dst - base), 16);
+      HRB_CUDA(ctx, cudaMemcpy(dst, mx_tiles[g].data(), mx_tiles[g].size() * sizeof(hrb::MxTile),
+                               cudaMemcpyHostToDevice));
+      plan->groups.back().d_tiles = reinterpret_cast<const hrb::MxTile*>(dst);
+      dst += mx_tiles[g].size() * sizeof(hrb::MxTile);
+    }
   }
   HRB_CUDA(ctx, cudaGetLastError());
   HRB_CUDA(ctx, cudaStreamSynchronize(ctx->stream));   // weight translation done
@@ -833,13 +878,19 @@ hrb_status plan_launch(hrb_plan* plan, cudaStream_t s, cudaEvent_t* events, uint
                          ctx->sm_count, s);
     ++n;
   }
+  if (plan->nplanes > 0) {
+    mark();
+    hrb::launch_quantize_planes(plan->d_planes, plan->nplanes, nullptr, plan->plane_units,
+                                ctx->d_error, ctx->sm_count, s);
+    ++n;
+  }
   for (auto& g : plan->groups) {
     mark();
     if (g.kind == 0) {
       n += static_cast<uint32_t>(hrb::launch_dense_exact(
           static_cast<const hrb::DenseJob*>(g.d_jobs), g.njobs, nullptr, g.tiles, g.wfmt, s));
     } else {
-      const int k = tc_launch(g.kind == 2, static_cast<const hrb::TcJob*>(g.d_jobs), g.njobs,
+      const int k = tc_launch(g.kind == 2, static_cast<const hrb::TcJob*>(g.d_jobs), g.d_tiles, g.njobs,
                               nullptr, g.nt, g.wfmt, g.tiles, ctx, s);
       if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
       n += static_cast<uint32_t>(k);
@@ -873,23 +924,29 @@ hrb_status hrb_plan_profile(hrb_plan* plan, void* stream, uint32_t reps, float* 
   hrb_ctx* ctx = plan->ctx;
   HRB_CUDA(ctx, cudaSetDevice(ctx->device));
   cudaStream_t s = pick(ctx, stream);
-  std::vector<cudaEvent_t> ev(cap + 1);
+  // reps + 1 runs enqueued back to back (the first is not counted): the
+  // host stays ahead of the GPU, so no event waits on a launch still being
+  // submitted and each pair of events brackets one kernel alone.
+  const uint32_t runs = reps + 1;
+  std::vector<cudaEvent_t> ev(static_cast<size_t>(cap + 1) * runs);
   for (auto& e : ev) HRB_CUDA(ctx, cudaEventCreate(&e));
   std::vector<double> sum(cap, 0.0);
   uint32_t n = 0;
   hrb_status st = HRB_OK;
-  for (uint32_t r = 0; r < reps && st == HRB_OK; ++r) {
-    st = plan_launch(plan, s, ev.data(), cap, &n);
-    if (st != HRB_OK) break;
-    HRB_CUDA(ctx, cudaStreamSynchronize(s));
+  for (uint32_t r = 0; r < runs && st == HRB_OK; ++r) {
+    st = plan_launch(plan, s, ev.data() + static_cast<size_t>(r) * (cap + 1), cap, &n);
+  }
+  if (st == HRB_OK && cudaStreamSynchronize(s) != cudaSuccess) st = HRB_ECUDA;
+  for (uint32_t r = 1; r < runs && st == HRB_OK; ++r) {
+    const cudaEvent_t* e = ev.data() + static_cast<size_t>(r) * (cap + 1);
     for (uint32_t i = 0; i < std::min(n, cap); ++i) {
       float t = 0;
-      HRB_CUDA(ctx, cudaEventElapsedTime(&t, ev[i], ev[i + 1]));
+      if (cudaEventElapsedTime(&t, e[i], e[i + 1]) != cudaSuccess) st = HRB_ECUDA;
       sum[i] += t;
     }
   }
   for (auto& e : ev) cudaEventDestroy(e);
-  if (st != HRB_OK) return st;
+  if (st != HRB_OK) return fail(ctx, st, "profiling run failed");
   *nkernels = std::min(n, cap);
   for (uint32_t i = 0; i < *nkernels; ++i) ms[i] = static_cast<float>(sum[i] / reps);
   return HRB_OK;

@@ -8,9 +8,12 @@
 //   * an MXINT8 activation q * 2^(e-6), |q| <= 128, is split into three
 //     E2M1 digit planes, q = 64 d2 + 8 d1 + d0 with every digit an integer in
 //     [-4, 4] (E2M1 holds 0..4 exactly); plane p carries the scale
-//     2^(e - 6 + 3p).  Three MMAs, one per plane, accumulate the exact
-//     products; only the FP32 summation order differs from the reference's
-//     chain (HRB_MODE_FAST).
+//     2^(e - 6 + 3p).  The planes are stacked as 3 NT operand rows, so one
+//     M = 128, N = 192 MMA per 64 elements of K multiplies a weight tile by
+//     all three planes of 64 tokens (each plane row with its own scales) and
+//     the epilogue adds the three FP32 partial sums.  The products are exact;
+//     only the FP32 summation order differs from the reference's chain
+//     (HRB_MODE_FAST).
 //
 // Data layout (all prepared once per plan or written by the encoder):
 //   K runs in steps of 256 elements = one 128-byte row of packed E2M1 (element
@@ -19,19 +22,20 @@
 //   memory layout the MMA descriptors describe.
 //   Weights: per (128-column tile, step) one 17 KB chunk: 128 rows x 128 B,
 //   then two 512-byte scale chunks (blocks 0-3 and 4-7 of the step).
-//   Activations: per (NT-row tile, step): the three planes (NT x 128 B each),
-//   then each plane's two scale chunks.
+//   Activations: per (NT-row tile, step) the block of mx_act_block_bytes
+//   (hrb_tc.cuh): 3 NT stacked plane rows, then their scale chunks.
 //   A scale chunk covers 128 rows x 4 blocks in the order tcgen05.cp
 //   .32x128b.warpx4 copies to TMEM: row i of 32, bytes 4j + s = scale of
-//   row i + 32 j, block s.  In TMEM the chunk occupies 4 columns, replicated
-//   in all four lane quarters; MMA k (64 elements = blocks 2k, 2k+1) reads
-//   the chunk of group k / 2 at byte 2 (k % 2) (the sf_id).
+//   row i + 32 j, block s.  In TMEM the chunk occupies 4 columns (column j
+//   holds rows 32 j .. 32 j + 31), replicated in all four lane quarters; MMA
+//   k (64 elements = blocks 2k, 2k+1) reads the chunks of group k / 2 at
+//   byte 2 (k % 2) (the sf_id).
 //
 // One persistent CTA per SM walks output tiles (128 weight columns x NT
 // tokens): warp 0 streams operand stages with bulk copies, warp 1 owns TMEM
 // and issues scale copies and MMAs, warps 3..6 drain finished accumulators
-// (two TMEM accumulator buffers, so one tile's epilogue overlaps the next
-// tile's MMAs).  Every wait is bounded.
+// (for NT = 64 two TMEM accumulator buffers, so one tile's epilogue overlaps
+// the next tile's MMAs).  Every wait is bounded.
 #include <algorithm>
 #include <cstdint>
 
@@ -53,64 +57,65 @@ constexpr uint32_t kWChunk = kTileW * kRowB + 2 * kSfChunk;  // 17408
 template <uint32_t NT>
 struct MxCfg {
   static constexpr uint32_t kPlane = NT * kRowB;
-  static constexpr uint32_t kABlock = 3 * kPlane + 3 * 2 * kSfChunk;
+  static constexpr uint32_t kParts = mx_parts(NT);               // 192-row MMAs per K slice
+  static constexpr uint32_t kABlock = mx_act_block_bytes(NT);
   static constexpr uint32_t kStageBytes = kWChunk + kABlock;    // multiple of 1024
-  static constexpr uint32_t kStages = NT == 64 ? 4u : 3u;
-  static constexpr uint32_t kDBufs = 2;
-  // TMEM columns: accumulators [0, 2 NT), weight scales 8, activation scales 3 x 8.
-  static constexpr uint32_t kColSfa = kDBufs * NT;
+  static constexpr uint32_t kStages = NT == 64 ? 5u : 3u;
+  // Accumulator buffers of 3 NT columns (one per stacked plane row); two for
+  // NT = 64 so one tile's epilogue overlaps the next tile's MMAs.
+  static constexpr uint32_t kDBufs = NT == 64 ? 2u : 1u;
+  static constexpr uint32_t kDCols = 3 * NT;
+  // TMEM columns: accumulators, weight scales (2 groups x 4), activation
+  // scales (per part, 2 groups x 8).
+  static constexpr uint32_t kColSfa = kDBufs * kDCols;
   static constexpr uint32_t kColSfb = kColSfa + 8;
-  static constexpr uint32_t kTmemCols = (kColSfb + 24) <= 256 ? 256u : 512u;
+  static constexpr uint32_t kTmemCols = 512;
+  static_assert(kColSfb + 16 * kParts <= kTmemCols, "TMEM columns");
   static constexpr uint32_t kOffBar = kStages * kStageBytes;
   static constexpr uint32_t kSmem = kOffBar + 256 + 1024;
+  static_assert(kStageBytes % 1024 == 0, "stage alignment");
+  static_assert(kSmem <= 232448, "shared memory");
   static constexpr uint32_t kThreads = 224;
 };
 
 struct MxParams {
-  const TcJob* jobs;   // device jobs, or null: use inline_job
-  uint32_t njobs;
+  const MxTile* tiles;  // device tiles, or null: the tiles of inline_job
   uint32_t total_tiles;
   uint32_t* err;
   TcJob inline_job;
 };
 
-__device__ __forceinline__ const TcJob& mx_job(const MxParams& p, uint32_t tile) {
-  if (p.jobs == nullptr) return p.inline_job;
-  uint32_t lo = 0, hi = p.njobs - 1;
-  while (lo < hi) {
-    const uint32_t mid = (lo + hi + 1) >> 1;
-    if (p.jobs[mid].tile_begin <= tile) lo = mid; else hi = mid - 1;
-  }
-  return p.jobs[lo];
+__host__ __device__ inline MxTile make_tile(const TcJob& job, uint32_t nt, uint32_t local) {
+  const uint32_t mt = local / job.n_tiles, n_tile = local % job.n_tiles;
+  const uint32_t row0 = mt * nt, col0 = n_tile * kTileW;
+  MxTile t;
+  t.w = job.w_tiles + static_cast<size_t>(n_tile) * job.k_steps * kWChunk;
+  t.a = job.a_tiles + static_cast<size_t>(mt) * job.k_steps * mx_act_block_bytes(nt);
+  t.c = job.c + static_cast<size_t>(row0) * job.ldc + col0;
+  t.bias = job.bias != nullptr ? job.bias + col0 : nullptr;
+  t.rows = job.M - row0 < nt ? job.M - row0 : nt;
+  t.cols = job.N - col0 < kTileW ? job.N - col0 : kTileW;
+  t.ldc = job.ldc;
+  t.steps_acc = job.k_steps | (job.accumulate ? 0x80000000u : 0u);
+  return t;
 }
 
-// The fields of a tile's job the roles need, copied into registers once per
-// tile (stores to C could alias a job held in global memory, which would
-// force the compiler to reload fields after every store).
-struct TileInfo {
-  const uint8_t* w;
-  const uint8_t* a;
-  float* c;
-  const float* bias;
-  uint32_t M, N, ldc, accumulate, k_steps, mt, nt;
-};
-
 template <uint32_t NT>
-__device__ __forceinline__ TileInfo tile_info(const MxParams& p, uint32_t tile) {
-  const TcJob& job = mx_job(p, tile);
-  TileInfo t;
-  const uint32_t local = tile - job.tile_begin;
-  t.mt = local / job.n_tiles;
-  t.nt = local % job.n_tiles;
-  t.k_steps = job.k_steps;
-  t.w = job.w_tiles + static_cast<size_t>(t.nt) * t.k_steps * kWChunk;
-  t.a = job.a_tiles + static_cast<size_t>(t.mt) * t.k_steps * MxCfg<NT>::kABlock;
-  t.c = job.c;
-  t.bias = job.bias;
-  t.M = job.M;
-  t.N = job.N;
-  t.ldc = job.ldc;
-  t.accumulate = job.accumulate;
+__device__ __forceinline__ MxTile tile_info(const MxParams& p, uint32_t tile) {
+  if (p.tiles == nullptr) return make_tile(p.inline_job, NT, tile);
+  // Three independent 16-byte loads; nothing consumes them until the tile
+  // is reached.
+  const uint4* src = reinterpret_cast<const uint4*>(p.tiles + tile);
+  const uint4 x = __ldg(src), y = __ldg(src + 1), z = __ldg(src + 2);
+  MxTile t;
+  t.w = reinterpret_cast<const uint8_t*>((static_cast<uint64_t>(x.y) << 32) | x.x);
+  t.a = reinterpret_cast<const uint8_t*>((static_cast<uint64_t>(x.w) << 32) | x.z);
+  t.c = reinterpret_cast<float*>((static_cast<uint64_t>(y.y) << 32) | y.x);
+  t.bias = reinterpret_cast<const float*>((static_cast<uint64_t>(y.w) << 32) | y.z);
+  t.rows = z.x;
+  t.cols = z.y;
+  t.ldc = z.z;
+  t.steps_acc = z.w;
   return t;
 }
 
@@ -188,11 +193,16 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
   if (warp == 0) {
     if (lane == 0) {
       uint32_t g = 0;  // global step counter across this CTA's tiles
+      // Each tile's job fields are loaded one tile ahead, so their global
+      // memory latency overlaps the previous tile's copies.
+      MxTile next = tile_info<NT>(p, blockIdx.x);
       for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-        const TileInfo ti = tile_info<NT>(p, tile);
+        const MxTile ti = next;
+        if (tile + gridDim.x < p.total_tiles) next = tile_info<NT>(p, tile + gridDim.x);
         const uint8_t* wsrc = ti.w;
         const uint8_t* asrc = ti.a;
-        for (uint32_t i = 0; i < ti.k_steps && ok; ++i, ++g) {
+        const uint32_t k_steps = ti.steps_acc & 0x7FFFFFFFu;
+        for (uint32_t i = 0; i < k_steps && ok; ++i, ++g) {
           const uint32_t s = g % Cfg::kStages;
           if (g >= Cfg::kStages) ok = mbar_wait(&empty[s], ((g / Cfg::kStages) - 1) & 1u, p.err);
           if (!ok) break;
@@ -212,13 +222,17 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
     if (lane == 0) {
       uint32_t g = 0, t = 0;
       const uint32_t sfa = tmem + Cfg::kColSfa;
+      uint32_t next_steps = tile_info<NT>(p, blockIdx.x).steps_acc & 0x7FFFFFFFu;
       for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++t) {
-        const uint32_t k_steps = mx_job(p, tile).k_steps;
+        const uint32_t k_steps = next_steps;
+        if (tile + gridDim.x < p.total_tiles) {
+          next_steps = tile_info<NT>(p, tile + gridDim.x).steps_acc & 0x7FFFFFFFu;
+        }
         const uint32_t b = t % Cfg::kDBufs;
         if (t >= Cfg::kDBufs) ok = mbar_wait(&acc_empty[b], ((t / Cfg::kDBufs) - 1) & 1u, p.err);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t d = tmem + b * NT;
+        const uint32_t d = tmem + b * Cfg::kDCols;
         for (uint32_t i = 0; i < k_steps && ok; ++i, ++g) {
           const uint32_t s = g % Cfg::kStages;
           ok = mbar_wait(&full[s], (g / Cfg::kStages) & 1u, p.err);
@@ -231,21 +245,21 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
           sf_copy(sfa, desc_sf_chunk(w_sf));
           sf_copy(sfa + 4, desc_sf_chunk(w_sf + kSfChunk));
 #pragma unroll
-          for (uint32_t pl = 0; pl < 3; ++pl) {
-            sf_copy(tmem + Cfg::kColSfb + 8 * pl, desc_sf_chunk(a_sf + (2 * pl) * kSfChunk));
-            sf_copy(tmem + Cfg::kColSfb + 8 * pl + 4,
-                    desc_sf_chunk(a_sf + (2 * pl + 1) * kSfChunk));
+          for (uint32_t c = 0; c < 4 * Cfg::kParts; ++c) {
+            // chunk c = (part * 2 + group) * 2 + half -> columns 8 (part * 2 + group) + 4 half
+            sf_copy(tmem + Cfg::kColSfb + 4 * c, desc_sf_chunk(a_sf + c * kSfChunk));
           }
 #pragma unroll
           for (uint32_t k = 0; k < 4; ++k) {
             const uint32_t grp = k / 2, sf_id = (k % 2) * 2;
-            const uint32_t idesc = idesc_mxf4(kTileW, NT, sf_id);
+            const uint32_t idesc = idesc_mxf4(kTileW, 192, sf_id);
             const uint32_t sfa_k = (sfa + 4 * grp) | (sf_id << 30);
 #pragma unroll
-            for (uint32_t pl = 0; pl < 3; ++pl) {
-              const uint32_t sfb_k = (tmem + Cfg::kColSfb + 8 * pl + 4 * grp) | (sf_id << 30);
-              mma_mxf4(d, desc_sw128(w_tile + 32 * k), desc_sw128(a_planes + pl * Cfg::kPlane + 32 * k),
-                       idesc, sfa_k, sfb_k, (i > 0 || k > 0 || pl > 0) ? 1u : 0u);
+            for (uint32_t part = 0; part < Cfg::kParts; ++part) {
+              const uint32_t sfb_k = (tmem + Cfg::kColSfb + 8 * (part * 2 + grp)) | (sf_id << 30);
+              mma_mxf4(d + 192 * part, desc_sw128(w_tile + 32 * k),
+                       desc_sw128(a_planes + part * 192 * kRowB + 32 * k), idesc, sfa_k, sfb_k,
+                       (i > 0 || k > 0) ? 1u : 0u);
             }
           }
           mma_commit(&empty[s]);
@@ -256,29 +270,36 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
   } else if (warp >= 3) {
     const uint32_t sp = warp & 3u;
     uint32_t t = 0;
+    MxTile next = tile_info<NT>(p, blockIdx.x);
     for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++t) {
-      const TileInfo ti = tile_info<NT>(p, tile);
+      const MxTile ti = next;
+      if (tile + gridDim.x < p.total_tiles) next = tile_info<NT>(p, tile + gridDim.x);
       const uint32_t b = t % Cfg::kDBufs;
       if (ok) ok = mbar_wait(&acc_full[b], (t / Cfg::kDBufs) & 1u, p.err);
       ok = __all_sync(0xFFFFFFFFu, ok);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t col = ti.nt * kTileW + sp * 32u + lane;
-      const bool col_ok = col < ti.N;
+      const uint32_t col = sp * 32u + lane;
+      const bool col_ok = col < ti.cols;
+      const bool acc = (ti.steps_acc >> 31) != 0;
       const float bias = (ti.bias != nullptr && col_ok) ? ti.bias[col] : 0.0f;
-      const uint32_t row0 = ti.mt * NT;
-      float* cbase = ti.c + static_cast<size_t>(row0) * ti.ldc + col;
+      float* cbase = ti.c + col;
 #pragma unroll 1
       for (uint32_t j0 = 0; j0 < NT; j0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem + ((sp * 32u) << 16) + b * NT + j0, v);
+        // The three digit-plane partial sums of tokens j0..j0+15, added
+        // smallest scale first.
+        uint32_t v0[16], v1[16], v2[16];
+        const uint32_t taddr = tmem + ((sp * 32u) << 16) + b * Cfg::kDCols + j0;
+        tmem_ld16(taddr, v0);
+        tmem_ld16(taddr + NT, v1);
+        tmem_ld16(taddr + 2 * NT, v2);
         tmem_wait_ld();
 #pragma unroll
         for (uint32_t j = 0; j < 16; ++j) {
-          if (col_ok && row0 + j0 + j < ti.M) {
+          if (col_ok && j0 + j < ti.rows) {
             float* dst = cbase + static_cast<size_t>(j0 + j) * ti.ldc;
-            float x = __uint_as_float(v[j]);
-            if (ti.accumulate) x += *dst;
+            float x = (__uint_as_float(v0[j]) + __uint_as_float(v1[j])) + __uint_as_float(v2[j]);
+            if (acc) x += *dst;
             *dst = x + bias;
           }
         }
@@ -342,16 +363,14 @@ __global__ void k_tile_weights_mxf4(const uint8_t* __restrict__ w, const uint8_t
 }
 
 template <uint32_t NT>
-int launch_mx(const TcJob* jobs_dev, uint32_t njobs, const TcJob* inline_job, uint32_t tiles,
-              int sm_count, uint32_t* err, cudaStream_t s) {
+int launch_mx(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, int sm_count,
+              uint32_t* err, cudaStream_t s) {
   using Cfg = MxCfg<NT>;
-  if (cudaFuncSetAttribute(k_gemm_mxf4<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           Cfg::kSmem) != cudaSuccess) {
+  if (!set_smem_limit_once(reinterpret_cast<const void*>(k_gemm_mxf4<NT>), Cfg::kSmem)) {
     return -1;
   }
   MxParams p{};
-  p.jobs = jobs_dev;
-  p.njobs = njobs;
+  p.tiles = tiles_dev;
   p.total_tiles = tiles;
   p.err = err;
   if (inline_job != nullptr) p.inline_job = *inline_job;
@@ -372,8 +391,7 @@ size_t mx_weight_bytes(uint32_t N, uint32_t kb) {
 
 size_t mx_act_bytes(uint32_t M, uint32_t kb) {
   const uint32_t nt = mx_tokens_per_tile(M);
-  return static_cast<size_t>((M + nt - 1) / nt) * mx_k_steps(kb) *
-         (3u * nt * kRowB + 3u * 2u * kSfChunk);
+  return static_cast<size_t>((M + nt - 1) / nt) * mx_k_steps(kb) * mx_act_block_bytes(nt);
 }
 
 void launch_tile_weights_mxf4(const uint8_t* w, const uint8_t* ws, uint32_t N, uint32_t kb,
@@ -385,11 +403,16 @@ void launch_tile_weights_mxf4(const uint8_t* w, const uint8_t* ws, uint32_t N, u
                                                                            mx_k_steps(kb), out);
 }
 
-int launch_mxf4_jobs(const TcJob* jobs_dev, uint32_t njobs, const TcJob* inline_job, uint32_t nt,
-                     uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t s) {
+void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out) {
+  for (uint32_t i = 0; i < job.m_tiles * job.n_tiles; ++i) out[i] = make_tile(job, nt, i);
+}
+
+int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t tiles,
+                int sm_count, uint32_t* err, cudaStream_t s) {
   if (tiles == 0) return 0;
-  if (nt == 64) return launch_mx<64>(jobs_dev, njobs, inline_job, tiles, sm_count, err, s);
-  if (nt == 128) return launch_mx<128>(jobs_dev, njobs, inline_job, tiles, sm_count, err, s);
+  if (tiles_dev == nullptr && inline_job == nullptr) return -1;
+  if (nt == 64) return launch_mx<64>(tiles_dev, inline_job, tiles, sm_count, err, s);
+  if (nt == 128) return launch_mx<128>(tiles_dev, inline_job, tiles, sm_count, err, s);
   return -1;
 }
 

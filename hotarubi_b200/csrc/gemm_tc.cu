@@ -27,6 +27,8 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
+#include <tuple>
 #include <vector>
 
 #include "hrb_device.cuh"
@@ -388,10 +390,7 @@ template <uint32_t NT, uint32_t WF>
 int launch_one(const TcJob* jobs_dev, uint32_t njobs, const TcJob* inline_job, uint32_t tiles,
                uint32_t* err, cudaStream_t s) {
   using Cfg = TcCfg<NT, WF>;
-  // The attribute is per device and per kernel: set it on every launch
-  // (cheap) rather than caching across devices.
-  if (cudaFuncSetAttribute(k_gemm_tc<NT, WF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           Cfg::kSmem) != cudaSuccess) {
+  if (!set_smem_limit_once(reinterpret_cast<const void*>(k_gemm_tc<NT, WF>), Cfg::kSmem)) {
     return -1;
   }
   TcParams p{};
@@ -404,6 +403,25 @@ int launch_one(const TcJob* jobs_dev, uint32_t njobs, const TcJob* inline_job, u
 }
 
 }  // namespace
+
+bool set_smem_limit_once(const void* kernel, uint32_t bytes) {
+  // The limit is a per-(kernel, device) attribute; the host call is not free
+  // (it would sit between back-to-back launches), so it is made once.
+  static std::mutex mu;
+  static std::vector<std::tuple<const void*, int, uint32_t>> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& d : done) {
+    if (std::get<0>(d) == kernel && std::get<1>(d) == dev && std::get<2>(d) >= bytes) return true;
+  }
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(bytes)) != cudaSuccess) {
+    return false;
+  }
+  done.emplace_back(kernel, dev, bytes);
+  return true;
+}
 
 uint32_t tc_tokens_per_tile(uint32_t M) { return M <= 64 ? 64u : (M <= 128 ? 128u : 256u); }
 

@@ -21,7 +21,7 @@ struct QuantJob {
   // bytes in the 128-byte swizzle: [row tiles][k_steps][tile_rows][128 B].
   uint8_t* tiles;
   uint64_t unit_begin;
-  uint64_t units;     // rows * ceil(cover_blocks / 4)
+  uint64_t units;     // rows * ceil(cover_blocks / 4); planes: rows * k_steps
   uint32_t rows, cols, ldx, kb;
   uint32_t vec_rule;  // 0: EncodeMxint8, 1: VEC 'q' pass
   uint32_t vec4;      // x rows are 16-byte aligned: load float4
@@ -59,6 +59,13 @@ struct DenseJob {
 void launch_quantize(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* inline_job,
                      uint64_t total_units, uint32_t* error_flag, int sm_count,
                      cudaStream_t stream);
+
+// The activations of kind::mxf4 GEMMs (tiles_kind 2): E2M1 digit planes and
+// their scales, no MXINT8 output.  A unit is one (row, 256-element K step):
+// units = rows * k_steps per job, unit_begin the prefix over the launch.
+void launch_quantize_planes(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* inline_job,
+                            uint64_t total_units, uint32_t* error_flag, int sm_count,
+                            cudaStream_t stream);
 
 // The exact (bit-identical) dense GEMM on CUDA cores, all GEMMs of one weight
 // format per launch.  Returns the number of kernels launched.

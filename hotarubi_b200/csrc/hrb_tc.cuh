@@ -36,12 +36,53 @@ void tc_fill_job(TcJob& t, uint32_t wfmt, uint32_t M, uint32_t N, uint32_t kb);
 // translation and the launch.
 uint32_t mx_tokens_per_tile(uint32_t M);
 uint32_t mx_k_steps(uint32_t kb);
+
+// Activation block of one (token tile of nt rows, 256-element K step) for
+// the kind::mxf4 kernel.  The three digit planes are stacked as 3 * nt
+// operand rows (plane p, token t -> stacked row p * nt + t), 128 bytes each
+// in the 128-byte swizzle; the MMAs take the stack 192 rows at a time (one
+// MMA for nt = 64, two for nt = 128).  After the rows come the E8M0 scales:
+// per 192-row part and 4-block group, two 512-byte chunks (part rows 0-127,
+// then 128-191 with 64 unused rows) in the order tcgen05.cp .32x128b.warpx4
+// reads them: row i of 32, bytes 4j + s = scale of part row i + 32 j, block s.
+__host__ __device__ constexpr uint32_t mx_parts(uint32_t nt) { return 3u * nt / 192u; }
+__host__ __device__ constexpr uint32_t mx_act_block_bytes(uint32_t nt) {
+  return 3u * nt * 128u + mx_parts(nt) * 2048u;
+}
+__host__ __device__ inline uint32_t mx_act_sf_offset(uint32_t nt, uint32_t stacked_row,
+                                                     uint32_t block_in_step) {
+  const uint32_t part = stacked_row / 192u, r = stacked_row % 192u;
+  const uint32_t chunk = (part * 2u + block_in_step / 4u) * 2u + r / 128u;
+  return 3u * nt * 128u + chunk * 512u + (r % 32u) * 16u + ((r % 128u) / 32u) * 4u +
+         block_in_step % 4u;
+}
 size_t mx_weight_bytes(uint32_t N, uint32_t kb);
 size_t mx_act_bytes(uint32_t M, uint32_t kb);
 void launch_tile_weights_mxf4(const uint8_t* w, const uint8_t* ws, uint32_t N, uint32_t kb,
                               uint8_t* out, cudaStream_t stream);
-int launch_mxf4_jobs(const TcJob* jobs_dev, uint32_t njobs, const TcJob* inline_job, uint32_t nt,
-                     uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t stream);
+// One output tile of a kind::mxf4 launch with its operands located.  Plans
+// build the array on the host once, so the kernel's roles read a tile's
+// fields with independent loads, one tile ahead, instead of searching jobs.
+struct MxTile {
+  const uint8_t* w;     // the tile's first weight chunk
+  const uint8_t* a;     // its first activation block
+  float* c;             // C at the tile's first row and column
+  const float* bias;    // bias at the tile's first column, or null
+  uint32_t rows, cols;  // valid token rows and weight columns
+  uint32_t ldc;
+  uint32_t steps_acc;   // K steps | accumulate << 31
+};
+static_assert(sizeof(MxTile) == 48, "MxTile is read as three 16-byte loads");
+// The m_tiles * n_tiles tiles of one job (tile index mt * n_tiles + nt).
+void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out);
+// One launch over `tiles` output tiles: the device array tiles_dev, or, when
+// it is null, the tiles of the single *inline_job.
+int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t tiles,
+                int sm_count, uint32_t* err, cudaStream_t stream);
+
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current
+// device, once per (kernel, device).
+bool set_smem_limit_once(const void* kernel, uint32_t bytes);
 
 // Dense weights -> the chunk layout the kernel streams.
 void launch_tile_weights(const uint8_t* w, const uint8_t* ws, uint32_t N, uint32_t kb,

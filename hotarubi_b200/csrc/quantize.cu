@@ -17,6 +17,7 @@
 #include <cstdint>
 
 #include "hrb_kernels.cuh"
+#include "hrb_tc.cuh"
 
 namespace hrb {
 namespace {
@@ -90,65 +91,6 @@ __device__ __forceinline__ void write_tile(const QuantJob& job, uint32_t row, ui
   *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);
 }
 
-// E2M1 code of a digit in [-4, 4] (the integers E2M1 holds exactly):
-// 0 -> 0, 1 -> 0b010, 2 -> 0b100, 3 -> 0b101, 4 -> 0b110, sign in bit 3.
-__device__ __forceinline__ uint32_t e2m1_digit(int32_t d) {
-  const uint32_t m = static_cast<uint32_t>(d < 0 ? -d : d);
-  const uint32_t code = (0x65420u >> (4 * m)) & 0xFu;
-  return d < 0 ? (code | 8u) : code;
-}
-
-// The three E2M1 digit planes of four activations, as 4 nibbles per plane
-// (element 0 in the low nibble).  q = 64 d2 + 8 d1 + d0 with d0, d1 in
-// [-4, 3] (balanced base 8) and d2 in [-2, 2].
-__device__ __forceinline__ void digit_planes(const int32_t q[4], uint32_t planes[3]) {
-  planes[0] = planes[1] = planes[2] = 0;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int32_t d0 = ((q[i] + 4) & 7) - 4;
-    const int32_t r1 = (q[i] - d0) >> 3;
-    const int32_t d1 = ((r1 + 4) & 7) - 4;
-    const int32_t d2 = (r1 - d1) >> 3;
-    planes[0] |= e2m1_digit(d0) << (4 * i);
-    planes[1] |= e2m1_digit(d1) << (4 * i);
-    planes[2] |= e2m1_digit(d2) << (4 * i);
-  }
-}
-
-// Elements col0..col0+3 of `row` into the kind::mxf4 activation blocks
-// (layout in gemm_mxf4.cu): per (row tile, 256-element step) the three digit
-// planes, each tile_rows rows of 128 bytes in the 128-byte swizzle, then the
-// planes' scale chunks; lanes that own a block's first elements also write
-// its three E8M0 scales (plane p: scale - 6 + 3p, i.e. 2^(e - 6 + 3p)).
-__device__ __forceinline__ void write_planes(const QuantJob& job, uint32_t row, uint32_t col0,
-                                             const uint32_t planes[3], uint32_t scale,
-                                             bool first_of_block) {
-  // tile_rows is 64 or 128: shifts, not divisions.
-  const uint32_t shift = job.tile_rows == 64 ? 6u : 7u;
-  const uint32_t rt = row >> shift, r = row & (job.tile_rows - 1u);
-  const uint32_t step = col0 >> 8, kk = col0 & 255u;
-  const uint32_t plane_bytes = job.tile_rows * 128u;
-  uint8_t* blk = job.tiles + static_cast<size_t>(rt * job.k_steps + step) *
-                                 (3u * plane_bytes + 3u * 1024u);
-  const uint32_t byte = kk / 2u, c = byte / 16u, within = byte % 16u;
-  const uint32_t off = r * 128u + ((c ^ (r & 7u)) << 4) + within;
-#pragma unroll
-  for (int p = 0; p < 3; ++p) {
-    *reinterpret_cast<uint16_t*>(blk + p * plane_bytes + off) = static_cast<uint16_t>(planes[p]);
-  }
-  if (first_of_block) {
-    const uint32_t b = kk / 32u, g = b / 4u, s = b % 4u;
-    const uint32_t sf_off = (r % 32u) * 16u + ((r % 128u) / 32u) * 4u + s;
-    uint8_t* sf = blk + 3u * plane_bytes;
-#pragma unroll
-    for (int p = 0; p < 3; ++p) {
-      int32_t e = static_cast<int32_t>(scale) - 6 + 3 * p;
-      e = e < 0 ? 0 : (e > 254 ? 254 : e);
-      sf[(p * 2u + g) * 512u + sf_off] = static_cast<uint8_t>(e);
-    }
-  }
-}
-
 // One unit of work: 128 consecutive elements (four blocks) of one row.
 struct Unit {
   const QuantJob* job;
@@ -205,29 +147,6 @@ __device__ __forceinline__ void quantize4(const uint32_t v[4], uint32_t key, boo
   }
 }
 
-// The three planes' E2M1 codes of four digits each, 4 nibbles per plane.
-// t = q + 292 = 64 (d2 + 4) + 8 (d1 + 4) + (d0 + 4): the base-8 digits of t
-// index the code table of d + 4 = 0..7 (d = -4..3).
-__device__ __forceinline__ void digit_planes_fast(const int32_t q[4], uint32_t planes[3]) {
-  constexpr uint32_t kLo = 0x0A0C0D0Eu;   // codes of d = -4, -3, -2, -1
-  constexpr uint32_t kHi = 0x05040200u;   // codes of d = 0, 1, 2, 3
-  uint32_t sel0 = 0, sel1 = 0, sel2 = 0;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t t = static_cast<uint32_t>(q[i] + 292);
-    sel0 |= (t & 7u) << (4 * i);
-    sel1 |= ((t >> 3) & 7u) << (4 * i);
-    sel2 |= ((t >> 6) & 7u) << (4 * i);
-  }
-  const uint32_t sels[3] = {sel0, sel1, sel2};
-#pragma unroll
-  for (int p = 0; p < 3; ++p) {
-    const uint32_t c = __byte_perm(kLo, kHi, sels[p]);      // four codes, one per byte
-    const uint32_t n = (c | (c >> 4)) & 0x00FF00FFu;         // nibble pairs in bytes 0, 2
-    planes[p] = __byte_perm(n, 0u, 0x0020u) & 0xFFFFu;
-  }
-}
-
 // Block maximum, encoding and stores of one unit.
 __device__ __forceinline__ void finish_unit(const Unit& t, const uint32_t v[4], uint32_t lane,
                                             uint32_t* error_flag) {
@@ -250,14 +169,7 @@ __device__ __forceinline__ void finish_unit(const Unit& t, const uint32_t v[4], 
   if (block >= job.kb) {
     // The tensor-core operands run K in whole steps: blocks past kb up to
     // the step boundary are zero padding.
-    if (job.tiles != nullptr && block < job.cover_blocks) {
-      if (job.tiles_kind == 2) {
-        const uint32_t zero[3] = {0u, 0u, 0u};
-        write_planes(job, t.row, t.col0, zero, 127u, (lane & 7u) == 0);
-      } else {
-        write_tile(job, t.row, t.col0, 0u, 0u);
-      }
-    }
+    if (job.tiles != nullptr && block < job.cover_blocks) write_tile(job, t.row, t.col0, 0u, 0u);
     return;
   }
   int32_t q[4];
@@ -273,13 +185,7 @@ __device__ __forceinline__ void finish_unit(const Unit& t, const uint32_t v[4], 
     if ((lane & 7u) == 0) job.scale[static_cast<size_t>(t.row) * job.kb + block] = static_cast<uint8_t>(scale);
   }
   if (job.tiles != nullptr) {
-    if (job.tiles_kind == 2) {
-      uint32_t planes[3];
-      digit_planes_fast(q, planes);
-      write_planes(job, t.row, t.col0, planes, scale, (lane & 7u) == 0);
-    } else {
-      write_tile(job, t.row, t.col0, bf16_pair(q[0], q[1], scale), bf16_pair(q[2], q[3], scale));
-    }
+    write_tile(job, t.row, t.col0, bf16_pair(q[0], q[1], scale), bf16_pair(q[2], q[3], scale));
   }
 }
 
@@ -355,6 +261,219 @@ k_quantize(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ QuantJo
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Activations for the kind::mxf4 kernel: MXINT8 codes as three E2M1 digit
+// planes (layout: mx_act_block_bytes / mx_act_sf_offset in hrb_tc.cuh).
+//
+// A unit is one (row, 256-element K step); lane l of the unit's warp owns
+// elements 8l .. 8l+7 (four lanes per 32-element block), so each plane's row
+// of the step is one 32-bit store per lane.  In FP32, all exact:
+//   q  = RNE(x * 2^(6 - e))           (1.5 * 2^23 added and subtracted)
+//   d2 = RNE(q / 64), r = q - 64 d2   (|r| <= 32)
+//   d1 = RNE(r / 8),  d0 = r - 8 d1   (all digits in [-4, 4])
+// and cvt.rn.satfinite.e2m1x2 packs the digits, which E2M1 holds exactly.
+// Blocks whose scale 2^(6 - e) leaves the FP32 range take the integer rules
+// of QuantizeInt8 / QuantizeElement for q.  A block whose scale byte is below
+// 6 (largest magnitude under 2^-121) has no E8M0 scale for its lowest plane
+// and is encoded as zero: its products, below 2^-121 |w|, are dropped.
+
+__device__ __forceinline__ float rint_exact(float v) {
+  return __fadd_rn(__fadd_rn(v, 12582912.0f), -12582912.0f);
+}
+
+__device__ __forceinline__ uint32_t pack_e2m1x8(const float d[8]) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(out)
+      : "f"(d[0]), "f"(d[1]), "f"(d[2]), "f"(d[3]), "f"(d[4]), "f"(d[5]), "f"(d[6]), "f"(d[7]));
+  return out;
+}
+
+// The job fields the plane encoder reads, kept in registers.
+struct PlaneJob {
+  const float* x;
+  uint8_t* tiles;
+  uint32_t cols, ldx, k_steps, tile_rows, vec4, vec_rule;
+  uint64_t unit_begin, units;
+};
+
+__device__ __forceinline__ PlaneJob plane_job(const QuantJob& j) {
+  PlaneJob p;
+  p.x = j.x;
+  p.tiles = j.tiles;
+  p.cols = j.cols;
+  p.ldx = j.ldx;
+  p.k_steps = j.k_steps;
+  p.tile_rows = j.tile_rows;
+  p.vec4 = j.vec4;
+  p.vec_rule = j.vec_rule;
+  p.unit_begin = j.unit_begin;
+  p.units = j.units;
+  return p;
+}
+
+__device__ __forceinline__ void load8(const PlaneJob& j, uint32_t row, uint32_t col0,
+                                      uint32_t v[8]) {
+  const float* src = j.x + static_cast<size_t>(row) * j.ldx;
+  if (j.vec4 && col0 + 7u < j.cols) {
+    const float4 a = __ldcs(reinterpret_cast<const float4*>(src + col0));
+    const float4 b = __ldcs(reinterpret_cast<const float4*>(src + col0 + 4));
+    v[0] = __float_as_uint(a.x); v[1] = __float_as_uint(a.y);
+    v[2] = __float_as_uint(a.z); v[3] = __float_as_uint(a.w);
+    v[4] = __float_as_uint(b.x); v[5] = __float_as_uint(b.y);
+    v[6] = __float_as_uint(b.z); v[7] = __float_as_uint(b.w);
+  } else {
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) v[i] = col0 + i < j.cols ? __float_as_uint(src[col0 + i]) : 0u;
+  }
+}
+
+template <bool kVec>
+__device__ __forceinline__ void encode_planes(const PlaneJob& j, uint32_t row, uint32_t step,
+                                              uint32_t v[8], uint32_t lane, uint32_t* error_flag) {
+  uint32_t key = 0;  // host rule: max magnitude; VEC rule: max exponent field
+  bool bad = false;
+#pragma unroll
+  for (uint32_t i = 0; i < 8; ++i) {
+    const uint32_t mag = v[i] & 0x7FFFFFFFu;
+    bad |= (mag >> 23) == 0xFFu;
+    if (kVec && (mag >> 23) == 0) v[i] = 0;  // the VEC pass reads subnormals as zero
+    const uint32_t k = kVec ? (mag >> 23) : mag;
+    key = k > key ? k : key;
+  }
+  key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 1));
+  key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 2));
+  if (!kVec && __any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(error_flag, 1u);
+  int32_t e;
+  uint32_t scale;
+  if (kVec) {
+    e = static_cast<int32_t>(key) - 127;
+    scale = key == 0 ? 127u : key;
+  } else {
+    e = key != 0 ? static_cast<int32_t>(key >> 23) - 127 : 0;
+    scale = static_cast<uint32_t>(e + 127);
+  }
+  float qf[8];
+  if (scale < 6u) {
+    // The planes' scales 2^(e - 6 + 3p) start below E8M0's 2^-127: such a
+    // block (largest magnitude under 2^-121) is encoded as zero.
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) qf[i] = 0.0f;
+  } else if (e >= -120 && e < 128) {
+    const float sc = __uint_as_float(static_cast<uint32_t>(133 - e) << 23);  // 2^(6 - e)
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) {
+      qf[i] = fminf(rint_exact(__fmul_rn(__uint_as_float(v[i]), sc)), 127.0f);
+    }
+  } else {
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) {
+      qf[i] = static_cast<float>(kVec ? quantize_vec_rule(v[i], key) : quantize_host_rule(v[i], e));
+    }
+  }
+  float d0[8], d1[8], d2[8];
+#pragma unroll
+  for (uint32_t i = 0; i < 8; ++i) {
+    d2[i] = rint_exact(__fmul_rn(qf[i], 0.015625f));
+    const float r = __fmaf_rn(d2[i], -64.0f, qf[i]);
+    d1[i] = rint_exact(__fmul_rn(r, 0.125f));
+    d0[i] = __fmaf_rn(d1[i], -8.0f, r);
+  }
+  const uint32_t shift = j.tile_rows == 64 ? 6u : 7u;
+  const uint32_t rt = row >> shift, r = row & (j.tile_rows - 1u);
+  uint8_t* blk = j.tiles + static_cast<size_t>(rt * j.k_steps + step) *
+                               mx_act_block_bytes(j.tile_rows);
+  // Lane l's four bytes sit in logical 16-byte chunk l / 4 of the row.
+  const uint32_t off = r * 128u + (((lane >> 2) ^ (r & 7u)) << 4) + (lane & 3u) * 4u;
+  const uint32_t plane_bytes = j.tile_rows * 128u;
+  *reinterpret_cast<uint32_t*>(blk + off) = pack_e2m1x8(d0);
+  *reinterpret_cast<uint32_t*>(blk + plane_bytes + off) = pack_e2m1x8(d1);
+  *reinterpret_cast<uint32_t*>(blk + 2u * plane_bytes + off) = pack_e2m1x8(d2);
+  if ((lane & 3u) == 0) {
+    const uint32_t b = lane >> 2;
+#pragma unroll
+    for (uint32_t p = 0; p < 3; ++p) {
+      int32_t se = static_cast<int32_t>(scale) - 6 + 3 * static_cast<int32_t>(p);
+      se = se < 0 ? 0 : (se > 254 ? 254 : se);
+      blk[mx_act_sf_offset(j.tile_rows, p * j.tile_rows + r, b)] = static_cast<uint8_t>(se);
+    }
+  }
+}
+
+// Each warp walks a contiguous range of units; the next unit's loads are
+// issued before the current unit is encoded.
+__global__ void __launch_bounds__(256)
+k_quantize_planes(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ QuantJob inline_job,
+                  uint32_t* error_flag) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint32_t nwarps = (gridDim.x * blockDim.x) >> 5;
+  const uint64_t total = jobs != nullptr ? jobs[njobs - 1].unit_begin + jobs[njobs - 1].units
+                                         : inline_job.units;
+  const uint64_t per = (total + nwarps - 1) / nwarps;
+  const uint64_t begin = static_cast<uint64_t>(warp) * per;
+  const uint64_t end = begin + per < total ? begin + per : total;
+  if (begin >= end) return;
+  uint32_t jx = 0;
+  if (jobs != nullptr) {
+    uint32_t lo = 0, hi = njobs - 1;
+    while (lo < hi) {
+      const uint32_t mid = (lo + hi + 1) >> 1;
+      if (jobs[mid].unit_begin <= begin) lo = mid; else hi = mid - 1;
+    }
+    jx = lo;
+  }
+  PlaneJob job = plane_job(jobs != nullptr ? jobs[jx] : inline_job);
+  uint32_t row, step;
+  {
+    const uint32_t u = static_cast<uint32_t>(begin - job.unit_begin);
+    row = u / job.k_steps;
+    step = u % job.k_steps;
+  }
+  // The unit after (row, step) of the current job, moving to the next job
+  // at the end of this one.
+  PlaneJob njob = job;
+  uint32_t nrow = row, nstep = step;
+  auto advance = [&](uint64_t next_unit) {
+    if (++nstep == njob.k_steps) {
+      nstep = 0;
+      ++nrow;
+    }
+    if (next_unit >= njob.unit_begin + njob.units && jobs != nullptr && jx + 1 < njobs) {
+      njob = plane_job(jobs[++jx]);
+      nrow = 0;
+      nstep = 0;
+    }
+  };
+  uint32_t v[8];
+  load8(job, row, step * 256u + lane * 8u, v);
+  for (uint64_t unit = begin; unit < end; ++unit) {
+    uint32_t w[8];
+    const bool more = unit + 1 < end;
+    if (more) {
+      advance(unit + 1);
+      load8(njob, nrow, nstep * 256u + lane * 8u, w);
+    }
+    if (job.vec_rule) {
+      encode_planes<true>(job, row, step, v, lane, error_flag);
+    } else {
+      encode_planes<false>(job, row, step, v, lane, error_flag);
+    }
+    if (!more) break;
+    job = njob;
+    row = nrow;
+    step = nstep;
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) v[i] = w[i];
+  }
+}
+
 }  // namespace
 
 void launch_quantize(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* inline_job,
@@ -369,6 +488,19 @@ void launch_quantize(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* i
   QuantJob one{};
   if (inline_job != nullptr) one = *inline_job;
   k_quantize<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(jobs_dev, njobs, one, error_flag);
+}
+
+void launch_quantize_planes(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* inline_job,
+                            uint64_t total_units, uint32_t* error_flag, int sm_count,
+                            cudaStream_t stream) {
+  uint64_t blocks = (total_units + 7) / 8;
+  const uint64_t cap = static_cast<uint64_t>(sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks == 0) blocks = 1;
+  QuantJob one{};
+  if (inline_job != nullptr) one = *inline_job;
+  k_quantize_planes<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(jobs_dev, njobs, one,
+                                                                      error_flag);
 }
 
 }  // namespace hrb

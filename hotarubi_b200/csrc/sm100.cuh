@@ -73,6 +73,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Asks L2 to fetch [src, src + bytes) from global memory (no shared memory,
+// no completion to wait for).  src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Generic-proxy writes to shared memory become visible to the async proxy
 // (the tensor cores read operands through it).
 __device__ __forceinline__ void fence_proxy_async_smem() {

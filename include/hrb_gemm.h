@@ -4,7 +4,7 @@
  * instruction-set simulator executes it:
  *
  *   void hotarubi::iss::ExecuteGemm(const GemmCommand&, Memories&);
- *       (tools/iss/gemm_array.hpp:33, tools/iss/gemm_array.cpp:149-186,
+ *       (tools/iss/gemm_array.hpp:33, tools/iss/gemm_array.cpp:112-149,
  *        called from Machine::Execute, tools/iss/machine.cpp:339-343)
  *
  * and the dense Linear that hotarubi's compiler lowers into a chain of such
@@ -101,11 +101,11 @@ typedef struct hrb_gemm_cmd {
  * instruction given as 16 little-endian bytes (isa.hpp:75-86). */
 HRB_API hrb_status hrb_gemm_decode(const uint8_t instruction[16], hrb_gemm_cmd* out);
 
-/* The checks of ExecuteGemm (gemm_array.cpp:150-156): HRB_OK or HRB_EINVAL
+/* The checks of ExecuteGemm (gemm_array.cpp:113-119): HRB_OK or HRB_EINVAL
  * with the reference's message in hrb_last_error (ctx may be NULL). */
 HRB_API hrb_status hrb_gemm_check(hrb_ctx* ctx, const hrb_gemm_cmd* cmd);
 
-/* ExecuteGemm (gemm_array.cpp:149-186) on host-resident memories:
+/* ExecuteGemm (gemm_array.cpp:112-149) on host-resident memories:
  *   abuf: HRB_ABUF_WORDS x 132 bytes, wbuf: HRB_WBUF_WORDS x 144 bytes,
  *   fbuf: HRB_FBUF_WORDS x 32 FP32 bit patterns, updated in place.
  * Addresses are masked to 20 bits and wrap modulo each depth as in the
@@ -121,8 +121,8 @@ HRB_API hrb_status hrb_gemm_exec_device(hrb_ctx* ctx, const hrb_gemm_cmd* cmd,
                                 const void* abuf, const void* wbuf,
                                 void* fbuf, void* stream);
 
-/* The words ExecuteGemm records in Memories::log (gemm_array.cpp:164,172,
- * 178,182): one byte per word, set to 1 when touched.  Host-only. */
+/* The words ExecuteGemm records in Memories::log (gemm_array.cpp:127,135,
+ * 141,145): one byte per word, set to 1 when touched.  Host-only. */
 HRB_API hrb_status hrb_gemm_accesses(const hrb_gemm_cmd* cmd, uint8_t* abuf_reads,
                              uint8_t* wbuf_reads, uint8_t* fbuf_reads,
                              uint8_t* fbuf_writes);
@@ -232,11 +232,12 @@ HRB_API hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs,
  * launched in *launches (may be NULL). */
 HRB_API hrb_status hrb_plan_run(hrb_plan* plan, void* stream, uint32_t* launches);
 HRB_API hrb_status hrb_plan_destroy(hrb_plan* plan);
-/* Measurement aid: runs the plan `reps` times on `stream` with CUDA events
- * around each kernel launch (synchronising after every run) and writes the
- * mean milliseconds of launch i to ms[i] for the first min(launches, cap)
- * launches; *nkernels receives that count.  Launch 0 is the activation
- * encoder when the plan has FP32 inputs, then one GEMM launch per group. */
+/* Measurement aid: enqueues the plan reps + 1 times back to back on
+ * `stream` with CUDA events around each kernel launch, waits, and writes
+ * the mean milliseconds of launch i over the last `reps` runs to ms[i] for
+ * the first min(launches, cap) launches; *nkernels receives that count.
+ * Launch 0 is the activation encoder when the plan has FP32 inputs, then one
+ * GEMM launch per group. */
 HRB_API hrb_status hrb_plan_profile(hrb_plan* plan, void* stream, uint32_t reps, float* ms,
                                     uint32_t cap, uint32_t* nkernels);
 

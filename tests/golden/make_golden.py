@@ -63,7 +63,7 @@ def iss_unit_cases(ref):
     cases.append(("other_words", 30, fields(a_base=0, a_stride=1, kb=1, m=32, w_base=0,
                                             w_stride=1, n8=1, c_base=64, wmode=0, acc=0)))
     # Address wrap: the 20-bit mask and the modulo of each memory depth
-    # (tools/iss/gemm_array.cpp:162-177), exercised on the same generator.
+    # (tools/iss/gemm_array.cpp:125-140), exercised on the same generator.
     cases.append(("wraps", 40, fields(a_base=8180, a_stride=7, kb=5, m=96, w_base=2040,
                                       w_stride=9, n8=4, c_base=4090, wmode=3, acc=1)))
     out = {}

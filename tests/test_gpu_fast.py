@@ -1,8 +1,9 @@
 """HRB_MODE_FAST (the tcgen05 tensor-core path) against the exact answer.
 
 Tolerance: the fast path computes the same exact products as the reference
-(BF16 holds every MXINT8 activation and every weight value exactly) but adds
-them in the tensor cores' order, in FP32.  Against the real-valued dot
+(BF16 holds every MXINT8 activation and every W8/MXFP8 weight value exactly;
+for MXFP4 weights the activations are split into three exact E2M1 digit
+planes) but adds them in the tensor cores' order, in FP32.  Against the real-valued dot
 product of the dequantized operands (float64), each output may differ by at
 most (K/16 + 4) * 2^-23 * sum_k |a_k * w_k| (one FP32 rounding per 16-wide
 MMA step plus the bias/accumulate adds, doubled for safety).  The tests also
@@ -159,3 +160,43 @@ def test_fast_batched_plan_of_mixed_shapes(hrb):
         got = c.cpu().numpy().astype(np.float64)
         assert (np.abs(got - ref) <= (k / 16 + 4) * 2.0**-23 * absref + 1e-30).all()
     plan.close()
+
+
+@pytest.mark.parametrize("quant", [0, 1])
+@pytest.mark.parametrize("m", [64, 70, 130])
+def test_fast_mxfp4_activation_planes_are_exact(hrb, quant, m):
+    """W = I (E2M1 code of 1.0, scale byte 127), so every output is a single
+    activation: C[r][i] = q[r][i] * 2^(e_r - 6), which the three digit-plane
+    products and their FP32 sum give exactly.  Bit-equality with the oracle's
+    MXINT8 encoding pins the plane encoder (both rounding rules, padded K
+    steps, ragged token tiles).  The one exception is the fast path's rule
+    for blocks whose scale byte is below 6 (largest magnitude under
+    2^-121): they are encoded as zero."""
+    from hotarubi_b200 import capi
+    rng = np.random.default_rng(70 + m + quant)
+    n = k = 544                      # kb = 17: the third 256-element step is mostly padding
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    x *= np.repeat(np.ldexp(1.0, rng.integers(-90, 90, (m, k // 32))), 32, axis=1).astype(np.float32)
+    x[rng.random((m, k)) < 0.02] = 0.0
+    x[:, 64:96] = 0.0                # an all-zero block
+    sub = rng.random((m, k)) < 0.01  # subnormal inputs: the VEC rule reads them as zero
+    x[sub] = np.float32(1e-40)
+    codes = np.zeros((n, k), np.uint8)
+    codes[np.arange(n), np.arange(n)] = 2
+    w = cpu.pack_nibbles(codes)
+    ws = np.full((n, k // 32), 127, np.uint8)
+    c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    keep = [dev(x), dev(w), dev(ws)]
+    d = capi.Library.desc(0, m, n, k, a=keep[0], w=keep[1], wscale=keep[2], c=c,
+                          mode=capi.MODE_FAST, quant=quant)
+    hrb.dense(d)
+    hrb.sync()
+    got = c.cpu().numpy()
+    xb = x.view(np.uint32)
+    q, s = cpu.quantize_vec(xb) if quant == 1 else cpu.encode_mxint8(xb)
+    want = (q.astype(np.float64) * np.repeat(np.ldexp(1.0, s.astype(np.int64) - 133), 32, axis=1))
+    want[np.repeat(s < 6, 32, axis=1)] = 0.0
+    want = want[:, :n].astype(np.float32)
+    if quant == 0:
+        assert (s < 6).any()         # the subnormal-only block is covered
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
