@@ -299,7 +299,8 @@ __device__ __forceinline__ uint32_t pack_e2m1x8(const float d[8]) {
 struct PlaneJob {
   const float* x;
   uint8_t* tiles;
-  uint32_t cols, ldx, k_steps, tile_rows, vec4, vec_rule;
+  uint32_t rows, cols, ldx, k_steps, tile_rows, vec4, vec_rule;
+  uint32_t block_bytes, plane_bytes;  // mx_act_block_bytes(tile_rows), tile_rows * 128
   uint64_t unit_begin, units;
 };
 
@@ -307,55 +308,62 @@ __device__ __forceinline__ PlaneJob plane_job(const QuantJob& j) {
   PlaneJob p;
   p.x = j.x;
   p.tiles = j.tiles;
+  p.rows = j.rows;
   p.cols = j.cols;
   p.ldx = j.ldx;
   p.k_steps = j.k_steps;
   p.tile_rows = j.tile_rows;
   p.vec4 = j.vec4;
   p.vec_rule = j.vec_rule;
+  p.block_bytes = mx_act_block_bytes(j.tile_rows);
+  p.plane_bytes = j.tile_rows * 128u;
   p.unit_begin = j.unit_begin;
   p.units = j.units;
   return p;
 }
 
-__device__ __forceinline__ void load8(const PlaneJob& j, uint32_t row, uint32_t col0,
-                                      uint32_t v[8]) {
-  const float* src = j.x + static_cast<size_t>(row) * j.ldx;
-  if (j.vec4 && col0 + 7u < j.cols) {
-    const float4 a = __ldcs(reinterpret_cast<const float4*>(src + col0));
-    const float4 b = __ldcs(reinterpret_cast<const float4*>(src + col0 + 4));
-    v[0] = __float_as_uint(a.x); v[1] = __float_as_uint(a.y);
-    v[2] = __float_as_uint(a.z); v[3] = __float_as_uint(a.w);
-    v[4] = __float_as_uint(b.x); v[5] = __float_as_uint(b.y);
-    v[6] = __float_as_uint(b.z); v[7] = __float_as_uint(b.w);
-  } else {
+// Where lane `lane`'s outputs for one row go (fixed while the row lasts):
+// the row's tile block of step 0, the lane's plane-word offset in a block,
+// and the offsets of its block's three scale bytes.
+struct PlaneOut {
+  uint8_t* blk0;
+  uint32_t off;
+  uint32_t sf[3];
+};
+
+__device__ __forceinline__ PlaneOut plane_out(const PlaneJob& j, uint32_t row, uint32_t lane) {
+  const uint32_t shift = j.tile_rows == 64 ? 6u : 7u;
+  const uint32_t rt = row >> shift, r = row & (j.tile_rows - 1u);
+  PlaneOut o;
+  o.blk0 = j.tiles + static_cast<size_t>(rt) * j.k_steps * j.block_bytes;
+  // Lane l's four bytes sit in logical 16-byte chunk l / 4 of the row.
+  o.off = r * 128u + (((lane >> 2) ^ (r & 7u)) << 4) + (lane & 3u) * 4u;
 #pragma unroll
-    for (uint32_t i = 0; i < 8; ++i) v[i] = col0 + i < j.cols ? __float_as_uint(src[col0 + i]) : 0u;
-  }
+  for (uint32_t p = 0; p < 3; ++p) o.sf[p] = mx_act_sf_offset(j.tile_rows, p * j.tile_rows + r, lane >> 2);
+  return o;
 }
 
 template <bool kVec>
-__device__ __forceinline__ void encode_planes(const PlaneJob& j, uint32_t row, uint32_t step,
-                                              uint32_t v[8], uint32_t lane, uint32_t* error_flag) {
+__device__ __forceinline__ void encode_planes(const PlaneJob& j, const PlaneOut& o, uint32_t step,
+                                              uint32_t v[8], uint32_t lane, uint32_t& bad) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
   uint32_t key = 0;  // host rule: max magnitude; VEC rule: max exponent field
-  bool bad = false;
 #pragma unroll
   for (uint32_t i = 0; i < 8; ++i) {
     const uint32_t mag = v[i] & 0x7FFFFFFFu;
-    bad |= (mag >> 23) == 0xFFu;
     if (kVec && (mag >> 23) == 0) v[i] = 0;  // the VEC pass reads subnormals as zero
     const uint32_t k = kVec ? (mag >> 23) : mag;
     key = k > key ? k : key;
   }
   key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 1));
   key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 2));
-  if (!kVec && __any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(error_flag, 1u);
   int32_t e;
   uint32_t scale;
   if (kVec) {
     e = static_cast<int32_t>(key) - 127;
     scale = key == 0 ? 127u : key;
   } else {
+    bad |= key >= 0x7F800000u;  // an Inf or NaN in the block
     e = key != 0 ? static_cast<int32_t>(key >> 23) - 127 : 0;
     scale = static_cast<uint32_t>(e + 127);
   }
@@ -366,10 +374,11 @@ __device__ __forceinline__ void encode_planes(const PlaneJob& j, uint32_t row, u
 #pragma unroll
     for (uint32_t i = 0; i < 8; ++i) qf[i] = 0.0f;
   } else if (e >= -120 && e < 128) {
+    // x * 2^(6 - e) is exact, so the fused add of 1.5 * 2^23 rounds it once.
     const float sc = __uint_as_float(static_cast<uint32_t>(133 - e) << 23);  // 2^(6 - e)
 #pragma unroll
     for (uint32_t i = 0; i < 8; ++i) {
-      qf[i] = fminf(rint_exact(__fmul_rn(__uint_as_float(v[i]), sc)), 127.0f);
+      qf[i] = fminf(__fadd_rn(__fmaf_rn(__uint_as_float(v[i]), sc, kMagic), -kMagic), 127.0f);
     }
   } else {
 #pragma unroll
@@ -380,98 +389,144 @@ __device__ __forceinline__ void encode_planes(const PlaneJob& j, uint32_t row, u
   float d0[8], d1[8], d2[8];
 #pragma unroll
   for (uint32_t i = 0; i < 8; ++i) {
-    d2[i] = rint_exact(__fmul_rn(qf[i], 0.015625f));
+    d2[i] = __fadd_rn(__fmaf_rn(qf[i], 0.015625f, kMagic), -kMagic);
     const float r = __fmaf_rn(d2[i], -64.0f, qf[i]);
-    d1[i] = rint_exact(__fmul_rn(r, 0.125f));
+    d1[i] = __fadd_rn(__fmaf_rn(r, 0.125f, kMagic), -kMagic);
     d0[i] = __fmaf_rn(d1[i], -8.0f, r);
   }
-  const uint32_t shift = j.tile_rows == 64 ? 6u : 7u;
-  const uint32_t rt = row >> shift, r = row & (j.tile_rows - 1u);
-  uint8_t* blk = j.tiles + static_cast<size_t>(rt * j.k_steps + step) *
-                               mx_act_block_bytes(j.tile_rows);
-  // Lane l's four bytes sit in logical 16-byte chunk l / 4 of the row.
-  const uint32_t off = r * 128u + (((lane >> 2) ^ (r & 7u)) << 4) + (lane & 3u) * 4u;
-  const uint32_t plane_bytes = j.tile_rows * 128u;
-  *reinterpret_cast<uint32_t*>(blk + off) = pack_e2m1x8(d0);
-  *reinterpret_cast<uint32_t*>(blk + plane_bytes + off) = pack_e2m1x8(d1);
-  *reinterpret_cast<uint32_t*>(blk + 2u * plane_bytes + off) = pack_e2m1x8(d2);
+  uint8_t* blk = o.blk0 + step * j.block_bytes;
+  *reinterpret_cast<uint32_t*>(blk + o.off) = pack_e2m1x8(d0);
+  *reinterpret_cast<uint32_t*>(blk + j.plane_bytes + o.off) = pack_e2m1x8(d1);
+  *reinterpret_cast<uint32_t*>(blk + 2u * j.plane_bytes + o.off) = pack_e2m1x8(d2);
   if ((lane & 3u) == 0) {
-    const uint32_t b = lane >> 2;
 #pragma unroll
     for (uint32_t p = 0; p < 3; ++p) {
       int32_t se = static_cast<int32_t>(scale) - 6 + 3 * static_cast<int32_t>(p);
-      se = se < 0 ? 0 : (se > 254 ? 254 : se);
-      blk[mx_act_sf_offset(j.tile_rows, p * j.tile_rows + r, b)] = static_cast<uint8_t>(se);
+      se = se > 254 ? 254 : se;  // scale >= 6 here or the block is zero
+      blk[o.sf[p]] = static_cast<uint8_t>(se < 0 ? 0 : se);
     }
   }
 }
 
-// Each warp walks a contiguous range of units; the next unit's loads are
-// issued before the current unit is encoded.
-__global__ void __launch_bounds__(256)
+// Position of a unit: its job (fields in registers), row and K step.
+struct PlaneCursor {
+  PlaneJob job;
+  uint32_t jx, row, step;
+};
+
+// Moves to the next unit; returns true when the row changed.
+__device__ __forceinline__ bool plane_cursor_next(PlaneCursor& c, const QuantJob* jobs,
+                                                  uint32_t njobs) {
+  if (++c.step < c.job.k_steps) return false;
+  c.step = 0;
+  if (++c.row == c.job.rows && jobs != nullptr && c.jx + 1 < njobs) {
+    c.job = plane_job(jobs[++c.jx]);
+    c.row = 0;
+  }
+  return true;
+}
+
+// Lane `lane`'s eight elements of a unit into its 32 bytes of the ring slot
+// with cp.async (16-byte pieces, zero-filled past the row's end); rows that
+// are not 16-byte aligned take plain loads.
+__device__ __forceinline__ void stage8(const PlaneCursor& c, uint32_t lane, uint32_t* slot) {
+  const uint32_t col0 = c.step * 256u + lane * 8u;
+  const float* src = c.job.x + static_cast<size_t>(c.row) * c.job.ldx + col0;
+  const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(slot));
+  if (c.job.vec4 && col0 + 8u <= c.job.cols) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n\t"
+                 "cp.async.cg.shared.global [%2], [%3], 16;" ::"r"(dst), "l"(src), "r"(dst + 16u),
+                 "l"(src + 4)
+                 : "memory");
+  } else if (c.job.vec4) {
+#pragma unroll
+    for (uint32_t h = 0; h < 2; ++h) {
+      const uint32_t col = col0 + 4u * h;
+      const uint32_t have = col < c.job.cols ? min(4u, c.job.cols - col) : 0u;
+      const float* from = have != 0 ? src + 4u * h : c.job.x;  // any valid address when empty
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst + 16u * h),
+                   "l"(from), "r"(4u * have)
+                   : "memory");
+    }
+  } else {
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) {
+      slot[i] = col0 + i < c.job.cols ? __float_as_uint(src[i]) : 0u;
+    }
+  }
+}
+
+constexpr uint32_t kPlaneDepth = 4;       // units in flight per warp
+constexpr uint32_t kPlaneWarps = 8;       // warps per CTA
+
+// Each warp walks a contiguous range of units.  Its inputs arrive through a
+// ring of kPlaneDepth units in shared memory filled by cp.async, so a warp
+// keeps kPlaneDepth KB of loads in flight without holding them in registers.
+__global__ void __launch_bounds__(kPlaneWarps * 32)
 k_quantize_planes(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ QuantJob inline_job,
                   uint32_t* error_flag) {
-  const uint32_t lane = threadIdx.x & 31u;
-  const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const uint32_t nwarps = (gridDim.x * blockDim.x) >> 5;
+  __shared__ __align__(16) uint32_t ring[kPlaneWarps][kPlaneDepth][256];
+  const uint32_t lane = threadIdx.x & 31u, wib = threadIdx.x >> 5;
+  const uint32_t warp = blockIdx.x * kPlaneWarps + wib;
+  const uint32_t nwarps = gridDim.x * kPlaneWarps;
   const uint64_t total = jobs != nullptr ? jobs[njobs - 1].unit_begin + jobs[njobs - 1].units
                                          : inline_job.units;
   const uint64_t per = (total + nwarps - 1) / nwarps;
   const uint64_t begin = static_cast<uint64_t>(warp) * per;
   const uint64_t end = begin + per < total ? begin + per : total;
   if (begin >= end) return;
-  uint32_t jx = 0;
+  const uint32_t count = static_cast<uint32_t>(end - begin);
+  PlaneCursor ld;
+  ld.jx = 0;
   if (jobs != nullptr) {
     uint32_t lo = 0, hi = njobs - 1;
     while (lo < hi) {
       const uint32_t mid = (lo + hi + 1) >> 1;
       if (jobs[mid].unit_begin <= begin) lo = mid; else hi = mid - 1;
     }
-    jx = lo;
+    ld.jx = lo;
   }
-  PlaneJob job = plane_job(jobs != nullptr ? jobs[jx] : inline_job);
-  uint32_t row, step;
+  ld.job = plane_job(jobs != nullptr ? jobs[ld.jx] : inline_job);
   {
-    const uint32_t u = static_cast<uint32_t>(begin - job.unit_begin);
-    row = u / job.k_steps;
-    step = u % job.k_steps;
+    const uint32_t u = static_cast<uint32_t>(begin - ld.job.unit_begin);
+    ld.row = u / ld.job.k_steps;
+    ld.step = u % ld.job.k_steps;
   }
-  // The unit after (row, step) of the current job, moving to the next job
-  // at the end of this one.
-  PlaneJob njob = job;
-  uint32_t nrow = row, nstep = step;
-  auto advance = [&](uint64_t next_unit) {
-    if (++nstep == njob.k_steps) {
-      nstep = 0;
-      ++nrow;
-    }
-    if (next_unit >= njob.unit_begin + njob.units && jobs != nullptr && jx + 1 < njobs) {
-      njob = plane_job(jobs[++jx]);
-      nrow = 0;
-      nstep = 0;
-    }
-  };
-  uint32_t v[8];
-  load8(job, row, step * 256u + lane * 8u, v);
-  for (uint64_t unit = begin; unit < end; ++unit) {
-    uint32_t w[8];
-    const bool more = unit + 1 < end;
-    if (more) {
-      advance(unit + 1);
-      load8(njob, nrow, nstep * 256u + lane * 8u, w);
-    }
-    if (job.vec_rule) {
-      encode_planes<true>(job, row, step, v, lane, error_flag);
-    } else {
-      encode_planes<false>(job, row, step, v, lane, error_flag);
-    }
-    if (!more) break;
-    job = njob;
-    row = nrow;
-    step = nstep;
+  PlaneCursor pr = ld;
+  PlaneOut out = plane_out(pr.job, pr.row, lane);
+  uint32_t bad = 0;
+  uint32_t* mine = &ring[wib][0][lane * 8u];
+  // One commit group per unit (empty past the range) keeps the group count
+  // uniform, so wait_group(kPlaneDepth - 1) always means "the oldest landed".
 #pragma unroll
-    for (uint32_t i = 0; i < 8; ++i) v[i] = w[i];
+  for (uint32_t d = 0; d < kPlaneDepth; ++d) {
+    if (d < count) {
+      stage8(ld, lane, mine + d * 256u);
+      plane_cursor_next(ld, jobs, njobs);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
   }
+  for (uint32_t i = 0; i < count; ++i) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kPlaneDepth - 1) : "memory");
+    uint32_t* slot = mine + (i % kPlaneDepth) * 256u;
+    uint32_t v[8];
+    const uint4 lo = *reinterpret_cast<const uint4*>(slot);
+    const uint4 hi = *reinterpret_cast<const uint4*>(slot + 4);
+    v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
+    v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
+    if (pr.job.vec_rule) {
+      encode_planes<true>(pr.job, out, pr.step, v, lane, bad);
+    } else {
+      encode_planes<false>(pr.job, out, pr.step, v, lane, bad);
+    }
+    if (plane_cursor_next(pr, jobs, njobs) && i + 1 < count) out = plane_out(pr.job, pr.row, lane);
+    if (i + kPlaneDepth < count) {
+      stage8(ld, lane, slot);
+      plane_cursor_next(ld, jobs, njobs);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  if (__any_sync(0xFFFFFFFFu, bad != 0) && lane == 0) atomicOr(error_flag, 1u);
 }
 
 }  // namespace
@@ -493,14 +548,25 @@ void launch_quantize(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* i
 void launch_quantize_planes(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* inline_job,
                             uint64_t total_units, uint32_t* error_flag, int sm_count,
                             cudaStream_t stream) {
-  uint64_t blocks = (total_units + 7) / 8;
-  const uint64_t cap = static_cast<uint64_t>(sm_count) * 8;
+  // As many CTAs as fit at once (no second wave); each warp takes a
+  // contiguous range of at least a few units.
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_quantize_planes, kPlaneWarps * 32, 0) !=
+            cudaSuccess || n < 1) {
+      n = 1;
+    }
+    per_sm = n;
+  }
+  uint64_t blocks = (total_units + 4 * kPlaneWarps - 1) / (4 * kPlaneWarps);
+  const uint64_t cap = static_cast<uint64_t>(sm_count) * per_sm;
   if (blocks > cap) blocks = cap;
   if (blocks == 0) blocks = 1;
   QuantJob one{};
   if (inline_job != nullptr) one = *inline_job;
-  k_quantize_planes<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(jobs_dev, njobs, one,
-                                                                      error_flag);
+  k_quantize_planes<<<static_cast<unsigned>(blocks), kPlaneWarps * 32, 0, stream>>>(jobs_dev, njobs,
+                                                                                    one, error_flag);
 }
 
 }  // namespace hrb
