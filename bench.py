@@ -274,7 +274,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     # Per-kernel device times (the dominant kernel's roofline): events around
     # each launch of the plan, a few runs (not the timed region).
-    kernel_ms = plan_full.profile(reps=5, stream=stream.cuda_stream)
+    kernel_ms = plan_full.profile(reps=20, stream=stream.cuda_stream)
     quant_ms, gemm_ms = kernel_ms[0], sum(kernel_ms[1:])
 
     if dist is not None:
@@ -321,7 +321,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         gemm_gbs = args.batch * ALG_BYTES_GEMM / (gemm_ms / 1e3) / 1e9
         quant_gbs = args.batch * ALG_BYTES_QUANT / (quant_ms / 1e3) / 1e9
         kname = "k_gemm_mxf4" if mode == capi.MODE_FAST else "k_dense_exact"
-        per_gemm_traffic = traffic_from_profiles(kname)
+        per_gemm_traffic = traffic_from_profiles(kname)  # ncu DRAM bytes per GEMM
         step_gbs = args.batch * ALG_BYTES_STEP / (ms / 1e3) / 1e9
         total_gemms = world * args.batch
         line = {
@@ -345,9 +345,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                                      else per_gemm_traffic * args.batch),
                          "alg_bytes_per_launch": args.batch * ALG_BYTES_GEMM,
                          "launch_ms": gemm_ms},
-            "encoder": {"kernel": "k_quantize", "launch_ms": quant_ms, "achieved_gbs": quant_gbs,
+            "encoder": {"kernel": "k_quantize_planes" if mode == capi.MODE_FAST else "k_quantize",
+                        "launch_ms": quant_ms, "achieved_gbs": quant_gbs,
                         "frac": quant_gbs / pk["hbm_gbs"],
-                        "alg_bytes_per_launch": args.batch * ALG_BYTES_QUANT},
+                        "alg_bytes_per_launch": args.batch * ALG_BYTES_QUANT,
+                        "traffic": (None if traffic_from_profiles("k_quantize_planes") is None
+                                    or mode != capi.MODE_FAST
+                                    else traffic_from_profiles("k_quantize_planes") * args.batch)},
             "e2e": e2e, "gpu_launches": launches,
             "clocks": clocks.summary(),
         }

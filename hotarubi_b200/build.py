@@ -66,5 +66,27 @@ def build(verbose: bool = False) -> str:
     return LIB
 
 
+HOST = os.path.join(PKG, "host")
+HOST_LIB = os.path.join(LIBDIR, "libhrb_iss.so")
+
+
+def build_host() -> str:
+    """libhrb_iss.so: the C++ mirror of the ISS GEMM interface (host/),
+    linked against libhrb_gemm.so (found next to it at run time)."""
+    gemm = build()
+    src = os.path.join(HOST, "gpu_gemm_array.cpp")
+    deps = [src, os.path.join(HOST, "gpu_gemm_array.hpp"), os.path.join(INCLUDE, "hrb_gemm.h"), gemm]
+    if os.path.exists(HOST_LIB) and os.path.getmtime(HOST_LIB) >= max(os.path.getmtime(d) for d in deps):
+        return HOST_LIB
+    cxx = shutil.which("g++") or "c++"
+    cmd = [cxx, "-std=c++20", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-I", INCLUDE,
+           "-I", HOST, src, "-L", LIBDIR, "-lhrb_gemm", "-Wl,-rpath,$ORIGIN", "-o", HOST_LIB]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"host library build failed:\n{r.stdout}\n{r.stderr}")
+    return HOST_LIB
+
+
 if __name__ == "__main__":
     print(build(verbose="-v" in sys.argv))
+    print(build_host())

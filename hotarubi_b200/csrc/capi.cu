@@ -66,15 +66,16 @@ struct hrb_plan {
 
 namespace {
 
+// Messages of calls made without a context (hrb_last_error(NULL)).
+thread_local std::string t_last_error;
+
 hrb_status fail(hrb_ctx* ctx, hrb_status status, const char* fmt, ...) {
-  if (ctx != nullptr) {
-    char buf[512];
-    va_list ap;
-    va_start(ap, fmt);
-    std::vsnprintf(buf, sizeof buf, fmt, ap);
-    va_end(ap);
-    ctx->last_error = buf;
-  }
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  (ctx != nullptr ? ctx->last_error : t_last_error) = buf;
   return status;
 }
 
@@ -418,7 +419,7 @@ hrb_status hrb_sync(hrb_ctx* ctx) {
 }
 
 const char* hrb_last_error(const hrb_ctx* ctx) {
-  return ctx == nullptr ? "" : ctx->last_error.c_str();
+  return ctx == nullptr ? t_last_error.c_str() : ctx->last_error.c_str();
 }
 
 void* hrb_get_stream(const hrb_ctx* ctx) { return ctx == nullptr ? nullptr : ctx->stream; }
@@ -865,40 +866,44 @@ namespace {
 
 // Launches every kernel of a plan on s; when `events` is given, records
 // events[i] before launch i and events[n] after the last.
-hrb_status plan_launch(hrb_plan* plan, cudaStream_t s, cudaEvent_t* events, uint32_t cap,
-                       uint32_t* launched) {
+// Launch steps of a plan: the encoders (FP32 -> MXINT8 / BF16 tiles, then
+// FP32 -> digit planes), then one GEMM launch per group.
+uint32_t plan_steps(const hrb_plan* plan) {
+  return (plan->nquant > 0 ? 1u : 0u) + (plan->nplanes > 0 ? 1u : 0u) +
+         static_cast<uint32_t>(plan->groups.size());
+}
+
+// Launches step `only` of a plan on s, or every step in order when `only`
+// is negative; adds the number of kernels launched to *launched.
+hrb_status plan_launch(hrb_plan* plan, cudaStream_t s, int64_t only, uint32_t* launched) {
   hrb_ctx* ctx = plan->ctx;
   uint32_t n = 0;
-  auto mark = [&]() {
-    if (events != nullptr && n <= cap) cudaEventRecord(events[n], s);
-  };
-  if (plan->nquant > 0) {
-    mark();
+  int64_t step = 0;
+  auto take = [&]() { return only < 0 || only == step++; };
+  if (plan->nquant > 0 && take()) {
     hrb::launch_quantize(plan->d_quant, plan->nquant, nullptr, plan->quant_units, ctx->d_error,
                          ctx->sm_count, s);
     ++n;
   }
-  if (plan->nplanes > 0) {
-    mark();
+  if (plan->nplanes > 0 && take()) {
     hrb::launch_quantize_planes(plan->d_planes, plan->nplanes, nullptr, plan->plane_units,
                                 ctx->d_error, ctx->sm_count, s);
     ++n;
   }
   for (auto& g : plan->groups) {
-    mark();
+    if (!take()) continue;
     if (g.kind == 0) {
       n += static_cast<uint32_t>(hrb::launch_dense_exact(
           static_cast<const hrb::DenseJob*>(g.d_jobs), g.njobs, nullptr, g.tiles, g.wfmt, s));
     } else {
-      const int k = tc_launch(g.kind == 2, static_cast<const hrb::TcJob*>(g.d_jobs), g.d_tiles, g.njobs,
-                              nullptr, g.nt, g.wfmt, g.tiles, ctx, s);
+      const int k = tc_launch(g.kind == 2, static_cast<const hrb::TcJob*>(g.d_jobs), g.d_tiles,
+                              g.njobs, nullptr, g.nt, g.wfmt, g.tiles, ctx, s);
       if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
       n += static_cast<uint32_t>(k);
     }
   }
-  mark();
   ctx->launches += n;
-  *launched = n;
+  *launched += n;
   HRB_CUDA(ctx, cudaGetLastError());
   return HRB_OK;
 }
@@ -911,7 +916,7 @@ hrb_status hrb_plan_run(hrb_plan* plan, void* stream, uint32_t* launches) {
   if (plan == nullptr) return HRB_EINVAL;
   HRB_CUDA(plan->ctx, cudaSetDevice(plan->ctx->device));
   uint32_t n = 0;
-  const hrb_status st = plan_launch(plan, pick(plan->ctx, stream), nullptr, 0, &n);
+  const hrb_status st = plan_launch(plan, pick(plan->ctx, stream), -1, &n);
   if (launches != nullptr) *launches = n;
   return st;
 }
@@ -924,31 +929,32 @@ hrb_status hrb_plan_profile(hrb_plan* plan, void* stream, uint32_t reps, float* 
   hrb_ctx* ctx = plan->ctx;
   HRB_CUDA(ctx, cudaSetDevice(ctx->device));
   cudaStream_t s = pick(ctx, stream);
-  // reps + 1 runs enqueued back to back (the first is not counted): the
-  // host stays ahead of the GPU, so no event waits on a launch still being
-  // submitted and each pair of events brackets one kernel alone.
-  const uint32_t runs = reps + 1;
-  std::vector<cudaEvent_t> ev(static_cast<size_t>(cap + 1) * runs);
-  for (auto& e : ev) HRB_CUDA(ctx, cudaEventCreate(&e));
-  std::vector<double> sum(cap, 0.0);
-  uint32_t n = 0;
+  const uint32_t steps = std::min(plan_steps(plan), cap);
+  cudaEvent_t ev[2];
+  HRB_CUDA(ctx, cudaEventCreate(&ev[0]));
+  HRB_CUDA(ctx, cudaEventCreate(&ev[1]));
   hrb_status st = HRB_OK;
-  for (uint32_t r = 0; r < runs && st == HRB_OK; ++r) {
-    st = plan_launch(plan, s, ev.data() + static_cast<size_t>(r) * (cap + 1), cap, &n);
-  }
-  if (st == HRB_OK && cudaStreamSynchronize(s) != cudaSuccess) st = HRB_ECUDA;
-  for (uint32_t r = 1; r < runs && st == HRB_OK; ++r) {
-    const cudaEvent_t* e = ev.data() + static_cast<size_t>(r) * (cap + 1);
-    for (uint32_t i = 0; i < std::min(n, cap); ++i) {
-      float t = 0;
-      if (cudaEventElapsedTime(&t, e[i], e[i + 1]) != cudaSuccess) st = HRB_ECUDA;
-      sum[i] += t;
+  uint32_t n = 0;
+  // A whole run first, so every step's inputs exist; then each step alone,
+  // `reps` launches back to back between two events (a step launched again
+  // recomputes the same outputs; GEMMs that accumulate onto C add again).
+  st = plan_launch(plan, s, -1, &n);
+  for (uint32_t i = 0; i < steps && st == HRB_OK; ++i) {
+    st = plan_launch(plan, s, i, &n);  // warm
+    if (st == HRB_OK && cudaEventRecord(ev[0], s) != cudaSuccess) st = HRB_ECUDA;
+    for (uint32_t r = 0; r < reps && st == HRB_OK; ++r) st = plan_launch(plan, s, i, &n);
+    if (st == HRB_OK && cudaEventRecord(ev[1], s) != cudaSuccess) st = HRB_ECUDA;
+    float t = 0;
+    if (st == HRB_OK && (cudaEventSynchronize(ev[1]) != cudaSuccess ||
+                         cudaEventElapsedTime(&t, ev[0], ev[1]) != cudaSuccess)) {
+      st = HRB_ECUDA;
     }
+    ms[i] = t / static_cast<float>(reps);
   }
-  for (auto& e : ev) cudaEventDestroy(e);
-  if (st != HRB_OK) return fail(ctx, st, "profiling run failed");
-  *nkernels = std::min(n, cap);
-  for (uint32_t i = 0; i < *nkernels; ++i) ms[i] = static_cast<float>(sum[i] / reps);
+  cudaEventDestroy(ev[0]);
+  cudaEventDestroy(ev[1]);
+  if (st != HRB_OK) return st == HRB_ECUDA ? fail(ctx, st, "profiling run failed") : st;
+  *nkernels = steps;
   return HRB_OK;
 }
 

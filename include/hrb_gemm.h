@@ -62,7 +62,8 @@ HRB_API hrb_status hrb_destroy(hrb_ctx* ctx);
 /* Waits for all work on the context's stream; returns HRB_EDATA when an
  * MXINT8 encode since the last sync met Inf/NaN. */
 HRB_API hrb_status hrb_sync(hrb_ctx* ctx);
-/* Message of the last failed call on this context ("" if none). */
+/* Message of the last failed call on this context ("" if none); with NULL,
+ * of the last failed call this thread made without a context. */
 HRB_API const char* hrb_last_error(const hrb_ctx* ctx);
 HRB_API const char* hrb_status_string(hrb_status status);
 /* The context's stream (a cudaStream_t) and a way to replace it. */
@@ -232,12 +233,13 @@ HRB_API hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs,
  * launched in *launches (may be NULL). */
 HRB_API hrb_status hrb_plan_run(hrb_plan* plan, void* stream, uint32_t* launches);
 HRB_API hrb_status hrb_plan_destroy(hrb_plan* plan);
-/* Measurement aid: enqueues the plan reps + 1 times back to back on
- * `stream` with CUDA events around each kernel launch, waits, and writes
- * the mean milliseconds of launch i over the last `reps` runs to ms[i] for
- * the first min(launches, cap) launches; *nkernels receives that count.
- * Launch 0 is the activation encoder when the plan has FP32 inputs, then one
- * GEMM launch per group. */
+/* Measurement aid: runs the plan once, then each of its launches alone,
+ * `reps` times back to back between two CUDA events on `stream`, and writes
+ * the mean milliseconds of launch i to ms[i] for the first min(launches, cap)
+ * launches; *nkernels receives that count.  Launch 0 is the activation
+ * encoder when the plan has FP32 inputs, then one GEMM launch per group.
+ * Repeated launches recompute the same outputs, except that GEMMs with
+ * `accumulate` set add onto C again. */
 HRB_API hrb_status hrb_plan_profile(hrb_plan* plan, void* stream, uint32_t reps, float* ms,
                                     uint32_t cap, uint32_t* nkernels);
 
