@@ -107,7 +107,7 @@ uint32_t hrbo_block_value(int64_t sum, uint32_t a_scale, uint32_t w_scale,
 }
 
 /* E2M1 magnitude times two, indexed by the low three bits of the code
- * (tools/iss/gemm_array.cpp:55). */
+ * (tools/iss/gemm_array.cpp:18). */
 static const int32_t kFp4Twice[8] = {0, 1, 2, 3, 4, 6, 8, 12};
 
 int32_t hrbo_weight_value(uint32_t nibble, uint32_t mode) {

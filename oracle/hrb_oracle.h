@@ -26,7 +26,7 @@ enum {
   HRBO_E4M3 = 4
 };
 
-/* Scale bias per weight mode: tools/iss/gemm_array.cpp:62-72 for the three
+/* Scale bias per weight mode: tools/iss/gemm_array.cpp:25-35 for the three
  * reference modes; -15 for E4M3 (activation 2^-6 times E4M3 read as an
  * integer multiple of 2^-9). */
 int32_t hrbo_scale_bias(uint32_t mode);
@@ -39,15 +39,15 @@ uint32_t hrbo_fp32_add(uint32_t a, uint32_t b);
 
 /* sum * 2^exponent rounded once to FP32 (nearest even), flushed to +0 below
  * 2^-126 and saturated to +-inf at 2^128.  For |sum| < 2^24 it is the exact
- * BlockValue of tools/iss/gemm_array.cpp:136-147 with
+ * BlockValue of tools/iss/gemm_array.cpp:99-110 with
  * exponent = a_scale + w_scale - 254 + SBIAS. */
 uint32_t hrbo_round_scaled(int64_t sum, int32_t exponent);
 
-/* BlockValue (tools/iss/gemm_array.cpp:136-147). */
+/* BlockValue (tools/iss/gemm_array.cpp:99-110). */
 uint32_t hrbo_block_value(int64_t sum, uint32_t a_scale, uint32_t w_scale,
                           uint32_t mode);
 
-/* WeightValue (tools/iss/gemm_array.cpp:121-134): nibble -> small integer. */
+/* WeightValue (tools/iss/gemm_array.cpp:84-97): nibble -> small integer. */
 int32_t hrbo_weight_value(uint32_t nibble, uint32_t mode);
 
 /* E4M3 byte -> value as an integer multiple of 2^-9 (OCP E4M3; the two NaN
@@ -60,10 +60,10 @@ typedef struct {
 } hrbo_cmd;
 
 /* 0 when ExecuteGemm would run the command, else 1, 2 or 3 for the three
- * Require checks of tools/iss/gemm_array.cpp:150-156 (m, kb, n8). */
+ * Require checks of tools/iss/gemm_array.cpp:113-119 (m, kb, n8). */
 int hrbo_check_command(const hrbo_cmd* cmd);
 
-/* ExecuteGemm (tools/iss/gemm_array.cpp:149-186) over full memories:
+/* ExecuteGemm (tools/iss/gemm_array.cpp:112-149) over full memories:
  * abuf 8192 x 132 bytes, wbuf 2048 x 144 bytes, fbuf 4096 x 32 FP32 bits.
  * Returns hrbo_check_command's code and leaves fbuf untouched on error. */
 int hrbo_execute_gemm(const hrbo_cmd* cmd, const uint8_t* abuf,
