@@ -1,27 +1,33 @@
 """Benchmark of the quantized GEMM hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--mode exact|fast] [--batch B]
+                    [--config c2|c1|c5] [--mode exact|fast] [--batch B]
 
-Workload (the MXFP4 GEMM the metric is quoted on):
-C = A . W^T with A FP32 [64, 2560] ~ N(0,1) encoded to MXINT8 on the device,
-W MXFP4 [960, 2560] (E2M1 codes, one E8M0 scale per 32-block, exponent in
-[-10, -4], canonicalised as hotarubi's compiler does), FP32 C [64, 960].
+Default workload (the MXFP4 GEMM the metric is
+quoted on): C = A . W^T with A FP32 [64, 2560] ~ N(0,1) encoded to MXINT8 on
+the device, W MXFP4 [960, 2560] (E2M1 codes, one E8M0 scale per 32-block,
+exponent in [-10, -4], canonicalised as hotarubi's compiler does), FP32 C
+[64, 960].  --config c1 runs BASELINE configs[0]'s W8 GEMM (64 x 960 -> 2560,
+per-channel int8 weights placed as hotarubi's compiler places a float
+matrix, with bias); --config c5 one large-M MXFP4 GEMM of the configs[4]
+sweep (4096 x 4096 x 4096), tensor-bound.
 
-One step = the hot path over one batch of B independent instances of that
-GEMM, each with its own activations, weights and output (B = 128: 282 MB of
-operands, more than twice the 126 MB L2, so every step streams from HBM and
-no L2 flush is needed).  Per rank the batch is fixed: weak scaling, no
+One step = the hot path over one batch of B independent instances of the
+GEMM, each with its own activations, weights and output (C2: B = 128, 282 MB
+of operands, more than twice the 126 MB L2, so every step streams from HBM
+and no L2 flush is needed).  Per rank the batch is fixed: weak scaling, no
 collective on the data path (the GEMMs are independent).
 
 Reported (one JSON line, rank 0):
   value       TFLOP/s (2*M*N*K per GEMM) over all ranks, operands resident
               in HBM, max over ranks of the device time of K steps.
-  e2e         the same metric through the host entry point hrb_gemm_dense_host
-              (pinned host buffers in, result back to the host, every step).
-  roofline    of the dominant kernel (the GEMM): its algorithmic bytes per
-              launch over its CUDA-event duration, against the measured HBM
-              copy bandwidth.
+  e2e         the same metric through the plan's host entry point
+              (hrb_plan_run_host): every step copies each GEMM's FP32
+              activations from pinned host memory, runs, and copies C back;
+              weights stay resident, as a loaded model's do.
+  roofline    of the dominant kernel (the GEMM): its algorithmic bytes (or
+              flops) per launch over its CUDA-event duration, against the
+              measured HBM copy bandwidth (or tensor peak).
   cpu_baseline  the reference's own ExecuteGemm (oracle/_ref) on the host's
               cores on a bounded sample, rank 0 only.
 
@@ -31,10 +37,10 @@ Reported (one JSON line, rank 0):
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -44,14 +50,58 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-M, N, K = 64, 960, 2560
-KB = K // 32
-FLOPS_PER_GEMM = 2 * M * N * K
-# Compulsory bytes of one GEMM: FP32 A in, MXFP4 W (4 bits), E8M0 scales, C out.
-ALG_BYTES_STEP = M * K * 4 + N * K // 2 + N * KB + M * N * 4
-# ... and of the GEMM kernel alone, which reads the MXINT8 activations.
-ALG_BYTES_GEMM = M * K + M * KB + N * K // 2 + N * KB + M * N * 4
-ALG_BYTES_QUANT = M * K * 4 + M * K + M * KB
+FMT_NAMES = {0: "mxfp4", 1: "w8", 2: "mxfp8"}
+
+
+@dataclasses.dataclass(frozen=True)
+class Workload:
+    key: str
+    name: str        # config.workload
+    label: str       # metric label
+    wfmt: int        # hrb_wfmt
+    M: int
+    N: int
+    K: int
+    bias: bool
+    batch: int       # GEMMs per step per GPU
+    bound: str       # "hbm" or "tensor"
+
+    @property
+    def kb(self) -> int:
+        return (self.K + 31) // 32
+
+    @property
+    def flops(self) -> int:
+        return 2 * self.M * self.N * self.K
+
+    def w_bytes(self) -> int:
+        return self.N * self.K // 2 if self.wfmt == 0 else self.N * self.K
+
+    def bytes_step(self) -> int:
+        """Compulsory bytes of one GEMM from FP32 activations."""
+        return (self.M * self.K * 4 + self.w_bytes() + self.N * self.kb
+                + (self.N * 4 if self.bias else 0) + self.M * self.N * 4)
+
+    def bytes_gemm(self) -> int:
+        """... of the GEMM kernel alone, which reads MXINT8 activations."""
+        return (self.M * self.K + self.M * self.kb + self.w_bytes() + self.N * self.kb
+                + (self.N * 4 if self.bias else 0) + self.M * self.N * 4)
+
+    def bytes_quant(self) -> int:
+        return self.M * self.K * 4 + self.M * self.K + self.M * self.kb
+
+    @property
+    def metric(self) -> str:
+        return f"{FMT_NAMES[self.wfmt].upper()} GEMM TFLOP/s ({self.label})"
+
+
+WORKLOADS = {
+    "c2": Workload("c2", "c2_mxfp4_64x2560x960", "C2 64x2560x960", 0, 64, 960, 2560, False, 128,
+                   "hbm"),
+    "c1": Workload("c1", "c1_w8_64x960x2560", "C1 64x960x2560", 1, 64, 2560, 960, True, 128, "hbm"),
+    "c5": Workload("c5", "c5_mxfp4_4096x4096x4096", "C5 4096x4096x4096", 0, 4096, 4096, 4096,
+                   False, 4, "tensor"),
+}
 
 
 def peaks() -> dict:
@@ -59,8 +109,8 @@ def peaks() -> dict:
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
 class ClockSampler:
@@ -119,69 +169,124 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
+# Synthetic operands (seeded; the survey's distributions)
+
+def host_operands(wl: Workload, i: int, place=None):
+    """Distinct operand set i: FP32 activations, weights and scales in the
+    dense formats of include/hrb_gemm.h, bias (or None).  `place` encodes a
+    float W8 matrix (default: this library's device encoder)."""
+    from hotarubi_b200 import workloads
+    x = workloads.activations(100 + i, wl.M, wl.K)
+    b = workloads.bias(300 + i, wl.N) if wl.bias else None
+    if wl.wfmt == 0:
+        w, ws = workloads.mxfp4_weights(200 + i, wl.N, wl.K)
+    elif wl.wfmt == 1:
+        q, s = workloads.w8_per_channel(200 + i, wl.N, wl.K)
+        w, ws = (place or place_w8)(workloads.dequantize_per_channel(q, s))
+    else:
+        w, ws = workloads.mxfp8_weights(200 + i, wl.N, wl.K)
+    return x, w, ws, b
+
+
+def place_w8(wf: np.ndarray):
+    """A float weight matrix placed as W8 the way hotarubi's compiler does
+    (PlaceW8: EncodeMxint8, then the HI/LO split the W8 format implies), with
+    this library's own device encoder."""
+    import torch
+
+    from hotarubi_b200 import capi
+    n, k = wf.shape
+    kb = (k + 31) // 32
+    lib = capi.Library(torch.cuda.current_device())
+    x = torch.from_numpy(np.ascontiguousarray(wf)).cuda()
+    q = torch.zeros((n, kb * 32), dtype=torch.int8, device="cuda")
+    s = torch.zeros((n, kb), dtype=torch.uint8, device="cuda")
+    lib.quantize(x, n, k, q, s)
+    lib.sync()
+    out = q.cpu().numpy().view(np.uint8), s.cpu().numpy()
+    lib.close()
+    return out
+
+
+# ---------------------------------------------------------------------------
 # The reference's CPU implementation (test infrastructure, timed only)
 
-def cpu_reference(min_seconds: float = 2.0, max_reps: int = 50) -> dict:
+def cpu_reference(wl: Workload, min_seconds: float = 2.0, max_reps: int = 50) -> dict:
     """hotarubi's ExecuteGemm, compiled from the reference sources
     (oracle/_ref), tiled into legal GEMM instructions over all host threads,
-    on C2 GEMMs until ~min_seconds of wall time."""
-    from hotarubi_b200 import workloads
+    on GEMMs of the workload until ~min_seconds of wall time; rows of large-M
+    workloads are sampled (rows are independent)."""
     from oracle import cpu
     ref = cpu.ref()
     threads = os.cpu_count() or 1
-    x = workloads.activations(0, M, K)
-    w, ws = workloads.mxfp4_weights(1, N, K)
-    q, s = cpu.encode_mxint8(x.view(np.uint32))
-    a_words = cpu.pack_abuf(q, s).reshape(-1)
-    codes = np.zeros((N, K), np.uint8)
-    codes[:, 0::2] = w & 0xF
-    codes[:, 1::2] = w >> 4
-    planes = cpu.pack_wbuf(codes, ws).reshape(-1)
-    c = np.zeros((M, N), np.uint32)
-    if ref is None:
-        # No reference build on this machine: the C restatement stands in.
-        kind = "port"
+
+    def place_cpu(wf):  # the same placement on the host (EncodeMxint8)
+        q, s = cpu.encode_mxint8(wf.view(np.uint32))
+        return q.view(np.uint8), s
+
+    x, w, ws, _ = host_operands(wl, 0, place_cpu)
+    rows = min(wl.M, 256)
+    q, s = cpu.encode_mxint8(x[:rows].view(np.uint32))
+    sample_flops = 2 * rows * wl.N * wl.K
+    label = f"{wl.label}" + ("" if rows == wl.M else f", first {rows} of {wl.M} rows")
+    if ref is None or wl.wfmt == 2:
+        # No reference build (or MXFP8, which the reference lacks): the C
+        # restatement stands in.
         t0 = time.perf_counter()
         reps = 0
         while reps < 1 or time.perf_counter() - t0 < min_seconds / 4:
-            cpu.gemm_dense(0, q, s, w, ws, N)
+            cpu.gemm_dense(wl.wfmt, q, s, w, ws, wl.N)
             reps += 1
         dt = time.perf_counter() - t0
-        return {"value": reps * FLOPS_PER_GEMM / dt / 1e12, "unit": "TFLOP/s", "cores": 1,
-                "kind": kind, "sample": f"{reps} x C2 GEMM (64x2560x960) on 1 thread",
-                "seconds": dt}
-    ref.hrbref_dense_gemm_iss(1, M, N, KB, a_words, planes, c, threads, 0, M)  # warm
+        return {"value": reps * sample_flops / dt / 1e12, "unit": "TFLOP/s", "cores": 1,
+                "kind": "port", "sample": f"{reps} x {label} on 1 thread", "seconds": dt}
+    a_words = cpu.pack_abuf(q, s).reshape(-1)
+    kp = wl.kb * 32
+    if wl.wfmt == 0:
+        codes = np.zeros((wl.N, kp), np.uint8)
+        codes[:, 0::2] = w & 0xF
+        codes[:, 1::2] = w >> 4
+        planes = cpu.pack_wbuf(codes, ws).reshape(-1)
+        nplanes = 1
+    else:
+        hi, lo = cpu.split_w8(w.view(np.int8))
+        planes = np.concatenate([cpu.pack_wbuf(hi, ws).reshape(-1),
+                                 cpu.pack_wbuf(lo, ws).reshape(-1)])
+        nplanes = 2
+    c = np.zeros((rows, wl.N), np.uint32)
+    ref.hrbref_dense_gemm_iss(nplanes, rows, wl.N, wl.kb, a_words, planes, c, threads, 0, rows)
     t0 = time.perf_counter()
     reps = 0
     while reps < max_reps and (reps < 1 or time.perf_counter() - t0 < min_seconds):
-        ref.hrbref_dense_gemm_iss(1, M, N, KB, a_words, planes, c, threads, 0, M)
+        ref.hrbref_dense_gemm_iss(nplanes, rows, wl.N, wl.kb, a_words, planes, c, threads, 0,
+                                  rows)
         reps += 1
     dt = time.perf_counter() - t0
-    return {"value": reps * FLOPS_PER_GEMM / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
+    return {"value": reps * sample_flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
             "kind": "reference",
-            "sample": f"{reps} x C2 GEMM (64x2560x960) through ExecuteGemm tiles on "
-                      f"{threads} threads", "seconds": dt}
+            "sample": f"{reps} x {label} through ExecuteGemm tiles on {threads} threads",
+            "seconds": dt}
 
 
-def run_reference(args, rank: int, world: int) -> None:
+def run_reference(args, wl: Workload, rank: int, world: int) -> None:
     if rank != 0:
         return
     steps = []
     for i in range(args.warmup + args.steps):
-        r = cpu_reference(min_seconds=0.5, max_reps=20)
+        r = cpu_reference(wl, min_seconds=0.25, max_reps=20)
         if i >= args.warmup:
             steps.append(r)
     value = statistics.median(r["value"] for r in steps)
     secs = statistics.median(r["seconds"] for r in steps)
     base = steps[-1]
     line = {
-        "impl": "reference", "metric": "MXFP4 GEMM TFLOP/s (C2 64x2560x960)",
+        "impl": "reference", "metric": wl.metric,
         "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": secs * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8 block dot + fp32 accumulate",
         "data": "synthetic",
-        "config": {"workload": "c2_mxfp4_64x2560x960", "M": M, "N": N, "K": K,
-                   "format": "mxfp4", "sample": base["sample"]},
+        "config": {"workload": wl.name, "M": wl.M, "N": wl.N, "K": wl.K,
+                   "format": FMT_NAMES[wl.wfmt], "sample": base["sample"]},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": base["cores"],
                          "kind": base["kind"], "sample": base["sample"]},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -193,76 +298,66 @@ def run_reference(args, rank: int, world: int) -> None:
 # ---------------------------------------------------------------------------
 # Our implementation
 
-def build_batch(torch, lib, capi, batch: int, mode: int, distinct: int = 4):
+def build_batch(torch, lib, capi, wl: Workload, batch: int, mode: int, distinct: int = 4):
     """B instances on the device: `distinct` seeded operand sets copied into
     B separate buffers (distinct memory, so every instance streams)."""
-    from hotarubi_b200 import workloads
-    sets = []
-    for i in range(distinct):
-        x = workloads.activations(100 + i, M, K)
-        w, ws = workloads.mxfp4_weights(200 + i, N, K)
-        sets.append((x, w, ws))
+    sets = [host_operands(wl, i) for i in range(min(distinct, batch))]
     inst = []
     for b in range(batch):
-        x, w, ws = sets[b % distinct]
+        x, w, ws, bias = sets[b % len(sets)]
         inst.append(dict(
             a=torch.from_numpy(x).cuda(), w=torch.from_numpy(w).cuda(),
             ws=torch.from_numpy(ws).cuda(),
-            c=torch.zeros((M, N), dtype=torch.float32, device="cuda")))
-    full = [capi.Library.desc(capi.WFMT_MXFP4, M, N, K, a=d["a"], w=d["w"], wscale=d["ws"],
-                              c=d["c"], mode=mode) for d in inst]
+            bias=None if bias is None else torch.from_numpy(bias).cuda(),
+            c=torch.zeros((wl.M, wl.N), dtype=torch.float32, device="cuda")))
+    descs = [capi.Library.desc(wl.wfmt, wl.M, wl.N, wl.K, a=d["a"], w=d["w"], wscale=d["ws"],
+                               bias=d["bias"], c=d["c"], mode=mode) for d in inst]
     torch.cuda.synchronize()
-    return inst, lib.plan(full), sets
+    return inst, lib.plan(descs), sets
 
 
-def traffic_from_profiles(kernel: str):
-    """DRAM bytes per launch of `kernel` on this workload, as summarised from
-    an ncu capture in profiles/dram_traffic.txt (kernel=bytes per GEMM)."""
+def traffic_from_profiles(kernel: str, wl: Workload):
+    """DRAM bytes per GEMM of `kernel` on this workload, as summarised from an
+    ncu capture in profiles/dram_traffic.txt (lines: kernel workload bytes)."""
     path = os.path.join(ROOT, "profiles", "dram_traffic.txt")
     if not os.path.exists(path):
         return None
     for line in open(path):
         parts = line.split()
-        if len(parts) >= 2 and parts[0] == kernel:
-            return float(parts[1])
+        if len(parts) >= 3 and parts[0] == kernel and parts[1] == wl.name:
+            return float(parts[2])
     return None
 
 
-def time_e2e(lib, capi, sets, batch: int, steps: int, warmup: int, mode: int) -> dict:
-    """hrb_gemm_dense_host over the batch: operands from pinned host memory
-    to the device, the GEMM, C back to the host, every step."""
-    import torch
-    pinned = []
-    for b in range(batch):
-        x, w, ws = sets[b % len(sets)]
-        pinned.append(dict(a=torch.from_numpy(x).pin_memory(), w=torch.from_numpy(w).pin_memory(),
-                           ws=torch.from_numpy(ws).pin_memory(),
-                           c=torch.zeros((M, N), dtype=torch.float32).pin_memory()))
-    descs = [capi.Library.desc(capi.WFMT_MXFP4, M, N, K, a=p["a"].data_ptr(),
-                               w=p["w"].data_ptr(), wscale=p["ws"].data_ptr(),
-                               c=p["c"].data_ptr(), mode=mode) for p in pinned]
+def time_e2e(torch, plan, wl: Workload, sets, batch: int, steps: int, warmup: int,
+             stream) -> dict:
+    """hrb_plan_run_host over the batch: every GEMM's FP32 activations from
+    pinned host memory to the device, the plan, C back to pinned memory."""
+    a_host = [torch.from_numpy(sets[b % len(sets)][0]).pin_memory() for b in range(batch)]
+    c_host = [torch.zeros((wl.M, wl.N), dtype=torch.float32).pin_memory() for _ in range(batch)]
     for _ in range(warmup):
-        for d in descs:
-            lib.dense_host(d)
+        plan.run_host(a_host, c_host, stream=stream.cuda_stream)
+    stream.synchronize()
     t0 = time.perf_counter()
     for _ in range(steps):
-        for d in descs:
-            lib.dense_host(d)
+        plan.run_host(a_host, c_host, stream=stream.cuda_stream)
+        stream.synchronize()
     dt = (time.perf_counter() - t0) / steps
-    h2d = batch * (M * K * 4 + N * K // 2 + N * KB)
-    d2h = batch * M * N * 4
-    return {"value": batch * FLOPS_PER_GEMM / dt / 1e12, "unit": "TFLOP/s",
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": dt * 1e3,
-            "entry_point": "hrb_gemm_dense_host"}
+    return {"value": batch * wl.flops / dt / 1e12, "unit": "TFLOP/s",
+            "h2d_bytes_per_step": batch * wl.M * wl.K * 4,
+            "d2h_bytes_per_step": batch * wl.M * wl.N * 4, "ms_per_step": dt * 1e3,
+            "entry_point": "hrb_plan_run_host (weights resident)"}
 
 
-def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None:
     import torch
+
     from hotarubi_b200 import capi
     torch.cuda.set_device(local_rank)
     dist = None
     if world > 1:
         import datetime
+
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
@@ -270,10 +365,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     mode = capi.MODE_FAST if args.mode == "fast" else capi.MODE_EXACT
     stream = torch.cuda.Stream()
     lib.set_stream(stream.cuda_stream)
-    inst, plan_full, sets = build_batch(torch, lib, capi, args.batch, mode)
+    batch = args.batch or wl.batch
+    inst, plan_full, sets = build_batch(torch, lib, capi, wl, batch, mode)
 
-    # Per-kernel device times (the dominant kernel's roofline): events around
-    # each launch of the plan, a few runs (not the timed region).
+    # Per-kernel device times (the dominant kernel's roofline): each launch
+    # of the plan repeated back to back between two events (not the timed
+    # region).
     kernel_ms = plan_full.profile(reps=20, stream=stream.cuda_stream)
     quant_ms, gemm_ms = kernel_ms[0], sum(kernel_ms[1:])
 
@@ -307,56 +404,74 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     e2e = None
     if not args.no_e2e:
-        e2e = time_e2e(lib, capi, sets, args.batch, max(1, min(args.steps, 3)), 1, mode)
+        e2e = time_e2e(torch, plan_full, wl, sets, batch, max(1, min(args.steps, 10)), 2, stream)
     if dist is not None and e2e is not None:
         t = torch.tensor([e2e["ms_per_step"]], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e["ms_per_step"] = float(t.item())
-        e2e["value"] = world * args.batch * FLOPS_PER_GEMM / (e2e["ms_per_step"] / 1e3) / 1e12
+        e2e["value"] = world * batch * wl.flops / (e2e["ms_per_step"] / 1e3) / 1e12
         e2e["h2d_bytes_per_step"] *= world
         e2e["d2h_bytes_per_step"] *= world
 
     if rank == 0:
         pk = peaks()
-        gemm_gbs = args.batch * ALG_BYTES_GEMM / (gemm_ms / 1e3) / 1e9
-        quant_gbs = args.batch * ALG_BYTES_QUANT / (quant_ms / 1e3) / 1e9
-        kname = "k_gemm_mxf4" if mode == capi.MODE_FAST else "k_dense_exact"
-        per_gemm_traffic = traffic_from_profiles(kname)  # ncu DRAM bytes per GEMM
-        step_gbs = args.batch * ALG_BYTES_STEP / (ms / 1e3) / 1e9
-        total_gemms = world * args.batch
+        fast = mode == capi.MODE_FAST
+        kname = ("k_gemm_mxf4" if wl.wfmt == 0 else "k_gemm_tc") if fast else "k_dense_exact"
+        qname = ("k_quantize_planes" if wl.wfmt == 0 else "k_quantize") if fast else "k_quantize"
+        gemm_gbs = batch * wl.bytes_gemm() / (gemm_ms / 1e3) / 1e9
+        quant_gbs = batch * wl.bytes_quant() / (quant_ms / 1e3) / 1e9
+        per_gemm_traffic = traffic_from_profiles(kname, wl) if fast else None
+        per_quant_traffic = traffic_from_profiles(qname, wl) if fast else None
+        step_gbs = batch * wl.bytes_step() / (ms / 1e3) / 1e9
+        if wl.bound == "hbm":
+            roof = {"bound": "hbm", "kernel": kname, "achieved": gemm_gbs, "peak": pk["hbm_gbs"],
+                    "unit": "GB/s", "frac": gemm_gbs / pk["hbm_gbs"],
+                    "peak_source": pk["source"] + " (HBM copy)",
+                    "alg_bytes_per_launch": batch * wl.bytes_gemm()}
+        else:
+            tflops = batch * wl.flops / (gemm_ms / 1e3) / 1e12
+            # kind::mxf4 runs at 4x the dense BF16 rate (nominal 9 vs 2.25
+            # PFLOP/s); each exact MXINT8 x E2M1 product takes three of its
+            # MMAs (the activation digit planes), so the useful ceiling is a
+            # third of that.
+            peak = pk["bf16_tflops"] * 4.0 / 3.0
+            roof = {"bound": "tensor", "kernel": kname, "achieved": tflops, "peak": peak,
+                    "unit": "TFLOP/s", "frac": tflops / peak,
+                    "peak_source": pk["source"] + " (cuBLAS BF16 x 4/3: FP4 MMA rate over "
+                                                  "three digit planes)",
+                    "frac_of_bf16_peak": tflops / pk["bf16_tflops"],
+                    "alg_flops_per_launch": batch * wl.flops}
+        roof.update({"traffic": (None if per_gemm_traffic is None
+                                 else per_gemm_traffic * batch),
+                     "launch_ms": gemm_ms})
+        total_gemms = world * batch
         line = {
-            "metric": "MXFP4 GEMM TFLOP/s (C2 64x2560x960)",
-            "value": total_gemms * FLOPS_PER_GEMM / (ms / 1e3) / 1e12,
+            "metric": wl.metric,
+            "value": total_gemms * wl.flops / (ms / 1e3) / 1e12,
             "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8 block dot + fp32 accumulate",
             "data": "synthetic",
-            "config": {"workload": "c2_mxfp4_64x2560x960", "batch_per_gpu": args.batch,
-                       "M": M, "N": N, "K": K, "format": "mxfp4", "mode": args.mode,
+            "config": {"workload": wl.name, "batch_per_gpu": batch,
+                       "M": wl.M, "N": wl.N, "K": wl.K, "format": FMT_NAMES[wl.wfmt],
+                       "bias": wl.bias, "mode": args.mode,
                        "activations": "fp32, encoded to mxint8 on device each step",
-                       "l2": f"working set {args.batch * ALG_BYTES_STEP / 1e6:.0f} MB per GPU "
-                             "> 2 x 126 MB L2, no flush",
+                       "l2": f"working set {batch * wl.bytes_step() / 1e6:.0f} MB per GPU"
+                             + (" > 2 x 126 MB L2, no flush" if batch * wl.bytes_step() > 252e6
+                                else ""),
                        "parallelism": f"replicas x{world} (independent GEMMs)"},
             "step_hbm_gbs": step_gbs,
-            "roofline": {"bound": "hbm", "kernel": kname,
-                         "achieved": gemm_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": gemm_gbs / pk["hbm_gbs"], "peak_source": pk["source"],
-                         "traffic": (None if per_gemm_traffic is None
-                                     else per_gemm_traffic * args.batch),
-                         "alg_bytes_per_launch": args.batch * ALG_BYTES_GEMM,
-                         "launch_ms": gemm_ms},
-            "encoder": {"kernel": "k_quantize_planes" if mode == capi.MODE_FAST else "k_quantize",
-                        "launch_ms": quant_ms, "achieved_gbs": quant_gbs,
+            "roofline": roof,
+            "encoder": {"kernel": qname, "launch_ms": quant_ms, "achieved_gbs": quant_gbs,
                         "frac": quant_gbs / pk["hbm_gbs"],
-                        "alg_bytes_per_launch": args.batch * ALG_BYTES_QUANT,
-                        "traffic": (None if traffic_from_profiles("k_quantize_planes") is None
-                                    or mode != capi.MODE_FAST
-                                    else traffic_from_profiles("k_quantize_planes") * args.batch)},
+                        "alg_bytes_per_launch": batch * wl.bytes_quant(),
+                        "traffic": (None if per_quant_traffic is None
+                                    else per_quant_traffic * batch)},
             "e2e": e2e, "gpu_launches": launches,
             "clocks": clocks.summary(),
         }
         if not args.no_cpu_baseline:
-            line["cpu_baseline"] = {k: v for k, v in cpu_reference().items() if k != "seconds"}
+            line["cpu_baseline"] = {k: v for k, v in cpu_reference(wl).items() if k != "seconds"}
         print(json.dumps(line), flush=True)
     plan_full.close()
     lib.close()
@@ -371,19 +486,22 @@ def main() -> None:
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", choices=sorted(WORKLOADS), default="c2")
     p.add_argument("--mode", choices=["exact", "fast"], default="fast")
-    p.add_argument("--batch", type=int, default=128)
+    p.add_argument("--batch", type=int, default=0, help="GEMMs per step per GPU (0: the "
+                   "config's default)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the host entry-point leg "
                    "(profiling runs)")
     args = p.parse_args()
+    wl = WORKLOADS[args.config]
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        run_reference(args, rank, world)
+        run_reference(args, wl, rank, world)
     else:
-        run_ours(args, rank, world, local_rank)
+        run_ours(args, wl, rank, world, local_rank)
 
 
 if __name__ == "__main__":

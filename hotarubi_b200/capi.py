@@ -94,6 +94,8 @@ def load() -> ctypes.CDLL:
             "hrb_plan_create": (ctypes.c_int, [P, ctypes.POINTER(GemmDesc), u32,
                                                ctypes.POINTER(P)]),
             "hrb_plan_run": (ctypes.c_int, [P, P, ctypes.POINTER(u32)]),
+            "hrb_plan_run_host": (ctypes.c_int, [P, P, ctypes.POINTER(P), ctypes.POINTER(P),
+                                                 ctypes.POINTER(P)]),
             "hrb_plan_destroy": (ctypes.c_int, [P]),
             "hrb_plan_profile": (ctypes.c_int, [P, P, u32, ctypes.POINTER(ctypes.c_float), u32,
                                                 ctypes.POINTER(u32)]),
@@ -275,6 +277,18 @@ class Plan:
         n = ctypes.c_uint32()
         self.owner._check(self.owner.lib.hrb_plan_run(self.h, stream or None, ctypes.byref(n)))
         return n.value
+
+    def run_host(self, a_host=None, c_host=None, ascale_host=None, stream: int = 0) -> None:
+        """hrb_plan_run_host: per GEMM (creation order) host activations in,
+        plan run, C out, asynchronous on `stream`.  Entries are host pointers
+        (ints), arrays/tensors, or None to skip."""
+        def arr(xs):
+            if xs is None:
+                return None
+            return (ctypes.c_void_p * len(xs))(*[_ptr(x) for x in xs])
+        self._host_args = (arr(a_host), arr(ascale_host), arr(c_host))  # alive until the call ends
+        a, sc, c = self._host_args
+        self.owner._check(self.owner.lib.hrb_plan_run_host(self.h, stream or None, a, sc, c))
 
     def profile(self, reps: int = 10, stream: int = 0) -> list[float]:
         """Mean milliseconds of each kernel launch of the plan."""

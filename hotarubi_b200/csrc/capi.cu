@@ -62,6 +62,17 @@ struct hrb_plan {
     const hrb::MxTile* d_tiles;  // kind 2: the launch's output tiles
   };
   std::vector<Group> groups;
+  // Per GEMM, in creation order: the device activations and output the
+  // descriptor names, for hrb_plan_run_host.
+  struct Io {
+    void* a;          // FP32 [M][lda], or MXINT8 codes [M][kp] when a is not given
+    size_t a_bytes;
+    void* ascale;     // MXINT8 scales [M][kb] (MXINT8 input only)
+    size_t ascale_bytes;
+    void* c;          // [M][ldc]
+    size_t c_bytes;
+  };
+  std::vector<Io> io;
 };
 
 namespace {
@@ -229,9 +240,12 @@ hrb_status run_dense(hrb_ctx* ctx, const hrb::DenseJob& job, cudaStream_t s) {
 // runs the exact kernel, whose results are within any tolerance.
 bool use_tc(const hrb_gemm_desc* d) { return d->mode == HRB_MODE_FAST && d->a != nullptr; }
 
-// MXFP4 weights in fast mode take the kind::mxf4 kernel (no decode);
-// W8 and MXFP8 take the BF16 kernel.
-bool use_mx(const hrb_gemm_desc* d) { return use_tc(d) && d->wfmt == HRB_WFMT_MXFP4; }
+// MXFP4 and W8 weights in fast mode take the kind::mxf4 kernel (MXFP4 codes
+// as they are, W8 as three E2M1 digit planes; no decode in the kernel);
+// MXFP8 takes the BF16 kernel.
+bool use_mx(const hrb_gemm_desc* d) {
+  return use_tc(d) && (d->wfmt == HRB_WFMT_MXFP4 || d->wfmt == HRB_WFMT_W8);
+}
 
 // Tensor-core bytes of one GEMM: prepared activations then weight chunks.
 size_t tc_act_bytes(const hrb_gemm_desc* d) {
@@ -240,7 +254,8 @@ size_t tc_act_bytes(const hrb_gemm_desc* d) {
 }
 size_t tc_weight_bytes(const hrb_gemm_desc* d) {
   const uint32_t kb = blocks_of(d->K);
-  return use_mx(d) ? hrb::mx_weight_bytes(d->N, kb) : hrb::tc_weight_tile_bytes(d->wfmt, d->N, kb);
+  return use_mx(d) ? hrb::mx_weight_bytes(d->wfmt, d->N, kb)
+                    : hrb::tc_weight_tile_bytes(d->wfmt, d->N, kb);
 }
 size_t tc_scratch_bytes(const hrb_gemm_desc* d) {
   return align_up(tc_act_bytes(d), 1024) + align_up(tc_weight_bytes(d), 1024);
@@ -285,7 +300,8 @@ void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJo
 void tc_translate(const hrb_gemm_desc* d, const hrb::TcJob& tj, cudaStream_t s) {
   const uint32_t kb = blocks_of(d->K);
   if (use_mx(d)) {
-    hrb::launch_tile_weights_mxf4(d->w, d->wscale, d->N, kb, const_cast<uint8_t*>(tj.w_tiles), s);
+    hrb::launch_tile_weights_mxf4(d->wfmt, d->w, d->wscale, d->N, kb,
+                                  const_cast<uint8_t*>(tj.w_tiles), s);
   } else {
     hrb::launch_tile_weights(d->w, d->wscale, d->N, kb, d->wfmt, const_cast<uint8_t*>(tj.w_tiles), s);
   }
@@ -295,7 +311,9 @@ void tc_translate(const hrb_gemm_desc* d, const hrb::TcJob& tj, cudaStream_t s) 
 int tc_launch(bool mx, const hrb::TcJob* jobs_dev, const hrb::MxTile* mx_tiles, uint32_t njobs,
               const hrb::TcJob* inline_job, uint32_t nt, uint32_t wfmt, uint32_t tiles,
               hrb_ctx* ctx, cudaStream_t s) {
-  if (mx) return hrb::launch_mxf4(mx_tiles, inline_job, nt, tiles, ctx->sm_count, ctx->d_error, s);
+  if (mx) {
+    return hrb::launch_mxf4(mx_tiles, inline_job, nt, wfmt, tiles, ctx->sm_count, ctx->d_error, s);
+  }
   return hrb::launch_tc_jobs(jobs_dev, njobs, inline_job, nt, wfmt, tiles, ctx->d_error, s);
 }
 
@@ -719,6 +737,23 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
   auto plan = new (std::nothrow) hrb_plan();
   if (plan == nullptr) return HRB_ENOMEM;
   plan->ctx = ctx;
+  for (uint32_t i = 0; i < count; ++i) {
+    const hrb_gemm_desc& d = descs[i];
+    const size_t kb = blocks_of(d.K);
+    hrb_plan::Io io{};
+    if (d.a != nullptr) {
+      io.a = const_cast<float*>(d.a);
+      io.a_bytes = (static_cast<size_t>(d.M - 1) * d.lda + d.K) * sizeof(float);
+    } else {
+      io.a = const_cast<int8_t*>(d.aq);
+      io.a_bytes = static_cast<size_t>(d.M) * kb * 32u;
+      io.ascale = const_cast<uint8_t*>(d.ascale);
+      io.ascale_bytes = static_cast<size_t>(d.M) * kb;
+    }
+    io.c = d.c;
+    io.c_bytes = (static_cast<size_t>(d.M - 1) * d.ldc + d.N) * sizeof(float);
+    plan->io.push_back(io);
+  }
   if (scratch > 0) {
     cudaError_t err = cudaMalloc(&plan->d_scratch, scratch);
     // Zero once: padding rows of the last activation tile are never written.
@@ -919,6 +954,34 @@ hrb_status hrb_plan_run(hrb_plan* plan, void* stream, uint32_t* launches) {
   const hrb_status st = plan_launch(plan, pick(plan->ctx, stream), -1, &n);
   if (launches != nullptr) *launches = n;
   return st;
+}
+
+hrb_status hrb_plan_run_host(hrb_plan* plan, void* stream, const void* const* a_host,
+                             const void* const* ascale_host, void* const* c_host) {
+  if (plan == nullptr) return HRB_EINVAL;
+  hrb_ctx* ctx = plan->ctx;
+  HRB_CUDA(ctx, cudaSetDevice(ctx->device));
+  cudaStream_t s = pick(ctx, stream);
+  const size_t n = plan->io.size();
+  for (size_t i = 0; i < n && a_host != nullptr; ++i) {
+    const hrb_plan::Io& io = plan->io[i];
+    if (a_host[i] != nullptr) {
+      HRB_CUDA(ctx, cudaMemcpyAsync(io.a, a_host[i], io.a_bytes, cudaMemcpyHostToDevice, s));
+    }
+    if (io.ascale != nullptr && ascale_host != nullptr && ascale_host[i] != nullptr) {
+      HRB_CUDA(ctx, cudaMemcpyAsync(io.ascale, ascale_host[i], io.ascale_bytes,
+                                    cudaMemcpyHostToDevice, s));
+    }
+  }
+  uint32_t launched = 0;
+  const hrb_status st = plan_launch(plan, s, -1, &launched);
+  if (st != HRB_OK) return st;
+  for (size_t i = 0; i < n && c_host != nullptr; ++i) {
+    if (c_host[i] == nullptr) continue;
+    HRB_CUDA(ctx, cudaMemcpyAsync(c_host[i], plan->io[i].c, plan->io[i].c_bytes,
+                                  cudaMemcpyDeviceToHost, s));
+  }
+  return HRB_OK;
 }
 
 hrb_status hrb_plan_profile(hrb_plan* plan, void* stream, uint32_t reps, float* ms, uint32_t cap,

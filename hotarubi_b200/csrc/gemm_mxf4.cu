@@ -49,32 +49,45 @@ namespace {
 using namespace sm100;
 
 constexpr uint32_t kTileW = 128;       // weight columns per tile (MMA M)
-constexpr uint32_t kStep = 256;        // K elements per step
 constexpr uint32_t kRowB = 128;        // bytes per operand row per step
 constexpr uint32_t kSfChunk = 512;     // 128 rows x 4 blocks
 constexpr uint32_t kWChunk = kTileW * kRowB + 2 * kSfChunk;  // 17408
+constexpr uint32_t kSmemLimit = 232448;
 
-template <uint32_t NT>
+// NT tokens per tile; WP weight planes per step (1: MXFP4 codes; 3: the E2M1
+// digit planes of W8 weights).
+//   WP = 1: one ring of stages, each a weight chunk and the activation block
+//   of one K step, filled by one producer thread.
+//   WP = 3: weights and activations stream through two rings of their own,
+//   filled by two producer threads, so the weight stream (from HBM, three
+//   chunks a step) runs several steps ahead of the activation blocks (L2).
+template <uint32_t NT, uint32_t WP>
 struct MxCfg {
+  static constexpr bool kSplit = WP > 1;
   static constexpr uint32_t kPlane = NT * kRowB;
   static constexpr uint32_t kParts = mx_parts(NT);               // 192-row MMAs per K slice
   static constexpr uint32_t kABlock = mx_act_block_bytes(NT);
-  static constexpr uint32_t kStageBytes = kWChunk + kABlock;    // multiple of 1024
-  static constexpr uint32_t kStages = NT == 64 ? 5u : 3u;
+  static constexpr uint32_t kASlots = kSplit ? (NT == 64 ? 3u : 2u) : 0u;
+  static constexpr uint32_t kOffW = kASlots * kABlock;            // W ring after the A ring
+  // A slot of the W ring: one weight chunk, plus the step's activation block
+  // when the rings are combined.
+  static constexpr uint32_t kWSlot = kWChunk + (kSplit ? 0u : kABlock);
+  static constexpr uint32_t kWSlots = (kSmemLimit - 1024 - 512 - kOffW) / kWSlot;
+  static_assert(kWSlots >= WP + 1, "weight ring");
   // Accumulator buffers of 3 NT columns (one per stacked plane row); two for
   // NT = 64 so one tile's epilogue overlaps the next tile's MMAs.
   static constexpr uint32_t kDBufs = NT == 64 ? 2u : 1u;
   static constexpr uint32_t kDCols = 3 * NT;
-  // TMEM columns: accumulators, weight scales (2 groups x 4), activation
-  // scales (per part, 2 groups x 8).
+  // TMEM columns: accumulators, weight scales (per plane, 2 groups x 4),
+  // activation scales (per part, 2 groups x 8).
   static constexpr uint32_t kColSfa = kDBufs * kDCols;
-  static constexpr uint32_t kColSfb = kColSfa + 8;
+  static constexpr uint32_t kColSfb = kColSfa + 8 * WP;
   static constexpr uint32_t kTmemCols = 512;
   static_assert(kColSfb + 16 * kParts <= kTmemCols, "TMEM columns");
-  static constexpr uint32_t kOffBar = kStages * kStageBytes;
-  static constexpr uint32_t kSmem = kOffBar + 256 + 1024;
-  static_assert(kStageBytes % 1024 == 0, "stage alignment");
-  static_assert(kSmem <= 232448, "shared memory");
+  static constexpr uint32_t kOffBar = kOffW + kWSlots * kWSlot;
+  static constexpr uint32_t kSmem = kOffBar + 512 + 1024;
+  static_assert(kABlock % 1024 == 0 && kWSlot % 1024 == 0, "ring alignment");
+  static_assert(kSmem <= kSmemLimit, "shared memory");
   static constexpr uint32_t kThreads = 224;
 };
 
@@ -85,11 +98,16 @@ struct MxParams {
   TcJob inline_job;
 };
 
+__host__ __device__ inline uint32_t mx_planes_of(uint32_t wfmt) {
+  return wfmt == HRB_WFMT_W8 ? 3u : 1u;
+}
+
 __host__ __device__ inline MxTile make_tile(const TcJob& job, uint32_t nt, uint32_t local) {
   const uint32_t mt = local / job.n_tiles, n_tile = local % job.n_tiles;
   const uint32_t row0 = mt * nt, col0 = n_tile * kTileW;
   MxTile t;
-  t.w = job.w_tiles + static_cast<size_t>(n_tile) * job.k_steps * kWChunk;
+  t.w = job.w_tiles +
+        static_cast<size_t>(n_tile) * job.k_steps * mx_planes_of(job.wfmt) * kWChunk;
   t.a = job.a_tiles + static_cast<size_t>(mt) * job.k_steps * mx_act_block_bytes(nt);
   t.c = job.c + static_cast<size_t>(row0) * job.ldc + col0;
   t.bias = job.bias != nullptr ? job.bias + col0 : nullptr;
@@ -155,24 +173,59 @@ __device__ __forceinline__ void sf_copy(uint32_t taddr, uint64_t desc) {
                : "memory");
 }
 
-template <uint32_t NT>
+// A ring of `slots` buffers with full/empty mbarriers, walked by a running
+// counter: slot = n % slots, phase parity = (n / slots) & 1.
+struct Ring {
+  uint64_t* full;
+  uint64_t* empty;
+  uint32_t slots;
+};
+
+// Producer side: waits until slot n is free (the consumer released the use
+// of it `slots` ago), then arms its full barrier for `bytes`.
+__device__ __forceinline__ bool ring_acquire(const Ring& r, uint32_t n, uint32_t bytes,
+                                             uint32_t* err) {
+  const uint32_t s = n % r.slots;
+  if (n >= r.slots && !mbar_wait(&r.empty[s], ((n / r.slots) - 1) & 1u, err)) return false;
+  mbar_arrive_expect_tx(&r.full[s], bytes);
+  return true;
+}
+
+// Producer side, at the end: every copy it issued has landed.
+__device__ __forceinline__ bool ring_drain(const Ring& r, uint32_t n, uint32_t* err) {
+  bool ok = true;
+  for (uint32_t k = (n > r.slots ? n - r.slots : 0); k < n && ok; ++k) {
+    ok = mbar_wait(&r.full[k % r.slots], (k / r.slots) & 1u, err);
+  }
+  return ok;
+}
+
+template <uint32_t NT, uint32_t WP>
 __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ MxParams p) {
-  using Cfg = MxCfg<NT>;
+  using Cfg = MxCfg<NT, WP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
-  uint64_t* full = bars;                           // [kStages] stage landed
-  uint64_t* empty = full + Cfg::kStages;           // [kStages] MMAs done with the stage
-  uint64_t* acc_full = empty + Cfg::kStages;       // [kDBufs] accumulator ready
-  uint64_t* acc_empty = acc_full + Cfg::kDBufs;    // [kDBufs] drained (128 arrivals)
+  const Ring aring{bars, bars + Cfg::kASlots, Cfg::kASlots};
+  const Ring wring{bars + 2 * Cfg::kASlots, bars + 2 * Cfg::kASlots + Cfg::kWSlots, Cfg::kWSlots};
+  uint64_t* acc_full = bars + 2 * (Cfg::kASlots + Cfg::kWSlots);  // [kDBufs] accumulator ready
+  uint64_t* acc_empty = acc_full + Cfg::kDBufs;                    // [kDBufs] drained (128)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + Cfg::kDBufs);
+  uint8_t* abase = smem;
+  uint8_t* wbase = smem + Cfg::kOffW;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
 
   if (threadIdx.x == 0) {
-    for (uint32_t s = 0; s < Cfg::kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    if constexpr (Cfg::kSplit) {
+      for (uint32_t s = 0; s < Cfg::kASlots; ++s) {
+        mbar_init(&aring.full[s], 1);
+        mbar_init(&aring.empty[s], 1);
+      }
+    }
+    for (uint32_t s = 0; s < Cfg::kWSlots; ++s) {
+      mbar_init(&wring.full[s], 1);
+      mbar_init(&wring.empty[s], 1);
     }
     for (uint32_t b = 0; b < Cfg::kDBufs; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -190,37 +243,48 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
 
-  if (warp == 0) {
+  if (warp == 0 || (Cfg::kSplit && warp == 2)) {
+    // Warp 0 lane 0 streams weight chunks (and, with combined rings, the
+    // activation blocks too); warp 2 lane 0 the activation blocks of split
+    // rings.  Each tile's fields are loaded one tile ahead.
     if (lane == 0) {
-      uint32_t g = 0;  // global step counter across this CTA's tiles
-      // Each tile's job fields are loaded one tile ahead, so their global
-      // memory latency overlaps the previous tile's copies.
+      const bool weights = warp == 0;
+      const Ring& ring = weights ? wring : aring;
+      uint32_t n = 0;  // uses of the ring so far
       MxTile next = tile_info<NT>(p, blockIdx.x);
       for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
         const MxTile ti = next;
         if (tile + gridDim.x < p.total_tiles) next = tile_info<NT>(p, tile + gridDim.x);
-        const uint8_t* wsrc = ti.w;
-        const uint8_t* asrc = ti.a;
         const uint32_t k_steps = ti.steps_acc & 0x7FFFFFFFu;
-        for (uint32_t i = 0; i < k_steps && ok; ++i, ++g) {
-          const uint32_t s = g % Cfg::kStages;
-          if (g >= Cfg::kStages) ok = mbar_wait(&empty[s], ((g / Cfg::kStages) - 1) & 1u, p.err);
-          if (!ok) break;
-          uint8_t* st = smem + s * Cfg::kStageBytes;
-          mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-          bulk_g2s(st, wsrc + static_cast<size_t>(i) * kWChunk, kWChunk, &full[s]);
-          bulk_g2s(st + kWChunk, asrc + static_cast<size_t>(i) * Cfg::kABlock, Cfg::kABlock,
-                   &full[s]);
+        if (weights) {
+          for (uint32_t c = 0; c < k_steps * WP && ok; ++c, ++n) {
+            const uint32_t sl = n % ring.slots;
+            ok = ring_acquire(ring, n, Cfg::kWSlot, p.err);
+            if (!ok) break;
+            bulk_g2s(wbase + sl * Cfg::kWSlot, ti.w + static_cast<size_t>(c) * kWChunk, kWChunk,
+                     &ring.full[sl]);
+            if (!Cfg::kSplit) {
+              bulk_g2s(wbase + sl * Cfg::kWSlot + kWChunk,
+                       ti.a + static_cast<size_t>(c) * Cfg::kABlock, Cfg::kABlock,
+                       &ring.full[sl]);
+            }
+          }
+        } else {
+          for (uint32_t i = 0; i < k_steps && ok; ++i, ++n) {
+            ok = ring_acquire(ring, n, Cfg::kABlock, p.err);
+            if (ok) {
+              bulk_g2s(abase + (n % ring.slots) * Cfg::kABlock,
+                       ti.a + static_cast<size_t>(i) * Cfg::kABlock, Cfg::kABlock,
+                       &ring.full[n % ring.slots]);
+            }
+          }
         }
       }
-      // Drain: every issued copy has landed before this thread leaves.
-      for (uint32_t k = (g > Cfg::kStages ? g - Cfg::kStages : 0); k < g && ok; ++k) {
-        ok = mbar_wait(&full[k % Cfg::kStages], (k / Cfg::kStages) & 1u, p.err);
-      }
+      if (ok) ring_drain(ring, n, p.err);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      uint32_t g = 0, t = 0;
+      uint32_t na = 0, nw = 0, t = 0;
       const uint32_t sfa = tmem + Cfg::kColSfa;
       uint32_t next_steps = tile_info<NT>(p, blockIdx.x).steps_acc & 0x7FFFFFFFu;
       for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++t) {
@@ -233,17 +297,32 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
         if (!ok) break;
         tc_fence_after();
         const uint32_t d = tmem + b * Cfg::kDCols;
-        for (uint32_t i = 0; i < k_steps && ok; ++i, ++g) {
-          const uint32_t s = g % Cfg::kStages;
-          ok = mbar_wait(&full[s], (g / Cfg::kStages) & 1u, p.err);
+        for (uint32_t i = 0; i < k_steps && ok; ++i, ++na, nw += WP) {
+          uint32_t as = 0;
+          if constexpr (Cfg::kSplit) {
+            as = na % Cfg::kASlots;
+            ok = mbar_wait(&aring.full[as], (na / Cfg::kASlots) & 1u, p.err);
+          }
+#pragma unroll
+          for (uint32_t pl = 0; pl < WP && ok; ++pl) {
+            const uint32_t n = nw + pl;
+            ok = mbar_wait(&wring.full[n % Cfg::kWSlots], (n / Cfg::kWSlots) & 1u, p.err);
+          }
           if (!ok) break;
           tc_fence_after();
-          const uint32_t st = smem_addr(smem + s * Cfg::kStageBytes);
-          const uint32_t w_tile = st, w_sf = st + kTileW * kRowB;
-          const uint32_t a_planes = st + kWChunk, a_sf = a_planes + 3 * Cfg::kPlane;
+          const uint32_t a_planes =
+              Cfg::kSplit ? smem_addr(abase + as * Cfg::kABlock)
+                          : smem_addr(wbase + (nw % Cfg::kWSlots) * Cfg::kWSlot + kWChunk);
+          const uint32_t a_sf = a_planes + 3 * Cfg::kPlane;
+          uint32_t w_tile[WP];
           // Scales of this step into TMEM (ordered before the MMAs below).
-          sf_copy(sfa, desc_sf_chunk(w_sf));
-          sf_copy(sfa + 4, desc_sf_chunk(w_sf + kSfChunk));
+#pragma unroll
+          for (uint32_t pl = 0; pl < WP; ++pl) {
+            w_tile[pl] = smem_addr(wbase + ((nw + pl) % Cfg::kWSlots) * Cfg::kWSlot);
+            const uint32_t w_sf = w_tile[pl] + kTileW * kRowB;
+            sf_copy(sfa + 8 * pl, desc_sf_chunk(w_sf));
+            sf_copy(sfa + 8 * pl + 4, desc_sf_chunk(w_sf + kSfChunk));
+          }
 #pragma unroll
           for (uint32_t c = 0; c < 4 * Cfg::kParts; ++c) {
             // chunk c = (part * 2 + group) * 2 + half -> columns 8 (part * 2 + group) + 4 half
@@ -253,16 +332,23 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
           for (uint32_t k = 0; k < 4; ++k) {
             const uint32_t grp = k / 2, sf_id = (k % 2) * 2;
             const uint32_t idesc = idesc_mxf4(kTileW, 192, sf_id);
-            const uint32_t sfa_k = (sfa + 4 * grp) | (sf_id << 30);
 #pragma unroll
-            for (uint32_t part = 0; part < Cfg::kParts; ++part) {
-              const uint32_t sfb_k = (tmem + Cfg::kColSfb + 8 * (part * 2 + grp)) | (sf_id << 30);
-              mma_mxf4(d + 192 * part, desc_sw128(w_tile + 32 * k),
-                       desc_sw128(a_planes + part * 192 * kRowB + 32 * k), idesc, sfa_k, sfb_k,
-                       (i > 0 || k > 0) ? 1u : 0u);
+            for (uint32_t pl = 0; pl < WP; ++pl) {
+              const uint32_t sfa_k = (sfa + 8 * pl + 4 * grp) | (sf_id << 30);
+#pragma unroll
+              for (uint32_t part = 0; part < Cfg::kParts; ++part) {
+                const uint32_t sfb_k =
+                    (tmem + Cfg::kColSfb + 8 * (part * 2 + grp)) | (sf_id << 30);
+                mma_mxf4(d + 192 * part, desc_sw128(w_tile[pl] + 32 * k),
+                         desc_sw128(a_planes + part * 192 * kRowB + 32 * k), idesc, sfa_k,
+                         sfb_k, (i > 0 || k > 0 || pl > 0) ? 1u : 0u);
+              }
             }
           }
-          mma_commit(&empty[s]);
+          // Release the step's slots once these MMAs have read them.
+#pragma unroll
+          for (uint32_t pl = 0; pl < WP; ++pl) mma_commit(&wring.empty[(nw + pl) % Cfg::kWSlots]);
+          if (Cfg::kSplit) mma_commit(&aring.empty[as]);
         }
         mma_commit(&acc_full[b]);
       }
@@ -316,33 +402,72 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
   }
 }
 
-// Dense MXFP4 weights [N][kp/2] + scales [N][kb] -> the per-(tile, step)
-// chunks above.  One thread per 16-byte output piece.
+// E2M1 code of a digit in [-4, 4]: 0, 1, 2, 3, 4 -> 0b000, 0b010, 0b100,
+// 0b101, 0b110; the sign in bit 3.
+__device__ __forceinline__ uint32_t e2m1_of_digit(int32_t d) {
+  const uint32_t m = static_cast<uint32_t>(d < 0 ? -d : d);
+  const uint32_t code = (0x65420u >> (4u * m)) & 0xFu;
+  return d < 0 ? (code | 8u) : code;
+}
+
+// Digit p of a W8 weight q = 64 d2 + 8 d1 + d0 (d2 = floor((q + 32) / 64),
+// d1 = floor((r + 4) / 8) of the rest r, all digits in [-4, 4]).
+__device__ __forceinline__ int32_t w8_digit(int32_t q, uint32_t p) {
+  const int32_t d2 = (q + 32) >> 6;
+  const int32_t r = q - 64 * d2;
+  const int32_t d1 = (r + 4) >> 3;
+  return p == 2 ? d2 : (p == 1 ? d1 : r - 8 * d1);
+}
+
+// Dense weights + scales [N][kb] -> the per-(tile, step, plane) chunks of
+// the kernel: MXFP4 [N][kp/2] codes as they are (one plane), or W8 [N][kp]
+// int8 as three E2M1 digit planes with scales e - 6 + 3p.  One thread per
+// 16-byte output piece.
 __global__ void k_tile_weights_mxf4(const uint8_t* __restrict__ w, const uint8_t* __restrict__ ws,
-                                    uint32_t N, uint32_t kb, uint32_t steps,
+                                    uint32_t N, uint32_t kb, uint32_t steps, uint32_t wp,
                                     uint8_t* __restrict__ out) {
   const uint32_t n_tiles = (N + kTileW - 1) / kTileW;
-  const uint64_t pieces = static_cast<uint64_t>(n_tiles) * steps * (kWChunk / 16u);
-  const size_t row_bytes = static_cast<size_t>(kb) * 16u;
+  const uint64_t pieces = static_cast<uint64_t>(n_tiles) * steps * wp * (kWChunk / 16u);
   for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < pieces;
        i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
     const uint64_t chunk = i / (kWChunk / 16u);
     const uint32_t piece = static_cast<uint32_t>(i % (kWChunk / 16u));
-    const uint32_t tile = static_cast<uint32_t>(chunk / steps), step = static_cast<uint32_t>(chunk % steps);
+    const uint32_t plane = static_cast<uint32_t>(chunk % wp);
+    const uint64_t ts = chunk / wp;
+    const uint32_t tile = static_cast<uint32_t>(ts / steps), step = static_cast<uint32_t>(ts % steps);
     uint8_t v[16];
     if (piece < kTileW * kRowB / 16u) {
       // Row r, stored 16-byte chunk p holds logical chunk c = p ^ (r % 8):
       // bytes 16c .. 16c+15 of the step's 128-byte row = elements 32c .. 32c+31.
       const uint32_t r = piece / 8u, pc = piece % 8u, c = pc ^ (r & 7u);
       const uint32_t n = tile * kTileW + r;
-      const size_t src = static_cast<size_t>(step) * kRowB + c * 16u;
+      const uint32_t e0 = step * 256u + c * 32u;  // first element of the piece
+      if (wp == 1) {
+        const size_t row_bytes = static_cast<size_t>(kb) * 16u;
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        v[k] = (n < N && src + k < row_bytes) ? w[static_cast<size_t>(n) * row_bytes + src + k] : 0;
+        for (int k = 0; k < 16; ++k) {
+          const size_t src = e0 / 2u + k;
+          v[k] = (n < N && src < row_bytes) ? w[static_cast<size_t>(n) * row_bytes + src] : 0;
+        }
+      } else {
+        const size_t kp = static_cast<size_t>(kb) * 32u;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          uint32_t nib[2] = {0u, 0u};
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const size_t e = e0 + 2u * k + h;
+            if (n < N && e < kp) {
+              const int32_t q = static_cast<int8_t>(w[static_cast<size_t>(n) * kp + e]);
+              nib[h] = e2m1_of_digit(w8_digit(q, plane));
+            }
+          }
+          v[k] = static_cast<uint8_t>(nib[0] | (nib[1] << 4));
+        }
       }
     } else {
       // Scale chunk grp, bytes 16i .. 16i+15: bytes 4j + s = scale of row
-      // i + 32 j, block 8 step + 4 grp + s.
+      // i + 32 j, block 8 step + 4 grp + s (plane p of W8: e - 6 + 3p).
       const uint32_t sp = piece - kTileW * kRowB / 16u;
       const uint32_t grp = sp / 32u, i32 = sp % 32u;
 #pragma unroll
@@ -350,7 +475,9 @@ __global__ void k_tile_weights_mxf4(const uint8_t* __restrict__ w, const uint8_t
         const uint32_t j = k / 4, s = k % 4;
         const uint32_t n = tile * kTileW + i32 + 32u * j;
         const uint32_t blk = step * 8u + grp * 4u + s;
-        v[k] = (n < N && blk < kb) ? ws[static_cast<size_t>(n) * kb + blk] : 127;
+        int32_t sc = (n < N && blk < kb) ? ws[static_cast<size_t>(n) * kb + blk] : 127;
+        if (wp == 3) sc = sc - 6 + 3 * static_cast<int32_t>(plane);
+        v[k] = static_cast<uint8_t>(sc < 0 ? 0 : (sc > 254 ? 254 : sc));
       }
     }
     uint4 o;
@@ -362,11 +489,11 @@ __global__ void k_tile_weights_mxf4(const uint8_t* __restrict__ w, const uint8_t
   }
 }
 
-template <uint32_t NT>
+template <uint32_t NT, uint32_t WP>
 int launch_mx(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, int sm_count,
               uint32_t* err, cudaStream_t s) {
-  using Cfg = MxCfg<NT>;
-  if (!set_smem_limit_once(reinterpret_cast<const void*>(k_gemm_mxf4<NT>), Cfg::kSmem)) {
+  using Cfg = MxCfg<NT, WP>;
+  if (!set_smem_limit_once(reinterpret_cast<const void*>(k_gemm_mxf4<NT, WP>), Cfg::kSmem)) {
     return -1;
   }
   MxParams p{};
@@ -375,7 +502,7 @@ int launch_mx(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, 
   p.err = err;
   if (inline_job != nullptr) p.inline_job = *inline_job;
   const uint32_t grid = std::min<uint32_t>(tiles, static_cast<uint32_t>(sm_count));
-  k_gemm_mxf4<NT><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(p);
+  k_gemm_mxf4<NT, WP><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? 1 : -1;
 }
 
@@ -385,8 +512,9 @@ uint32_t mx_tokens_per_tile(uint32_t M) { return M <= 64 ? 64u : 128u; }
 
 uint32_t mx_k_steps(uint32_t kb) { return (kb + 7) / 8; }
 
-size_t mx_weight_bytes(uint32_t N, uint32_t kb) {
-  return static_cast<size_t>((N + kTileW - 1) / kTileW) * mx_k_steps(kb) * kWChunk;
+size_t mx_weight_bytes(uint32_t wfmt, uint32_t N, uint32_t kb) {
+  return static_cast<size_t>((N + kTileW - 1) / kTileW) * mx_k_steps(kb) * mx_planes_of(wfmt) *
+         kWChunk;
 }
 
 size_t mx_act_bytes(uint32_t M, uint32_t kb) {
@@ -394,25 +522,28 @@ size_t mx_act_bytes(uint32_t M, uint32_t kb) {
   return static_cast<size_t>((M + nt - 1) / nt) * mx_k_steps(kb) * mx_act_block_bytes(nt);
 }
 
-void launch_tile_weights_mxf4(const uint8_t* w, const uint8_t* ws, uint32_t N, uint32_t kb,
-                              uint8_t* out, cudaStream_t s) {
-  const uint64_t pieces = mx_weight_bytes(N, kb) / 16u;
+void launch_tile_weights_mxf4(uint32_t wfmt, const uint8_t* w, const uint8_t* ws, uint32_t N,
+                              uint32_t kb, uint8_t* out, cudaStream_t s) {
+  const uint64_t pieces = mx_weight_bytes(wfmt, N, kb) / 16u;
   uint64_t grid = (pieces + 255) / 256;
   if (grid > 148u * 16u) grid = 148u * 16u;
-  k_tile_weights_mxf4<<<static_cast<unsigned>(grid ? grid : 1), 256, 0, s>>>(w, ws, N, kb,
-                                                                           mx_k_steps(kb), out);
+  k_tile_weights_mxf4<<<static_cast<unsigned>(grid ? grid : 1), 256, 0, s>>>(
+      w, ws, N, kb, mx_k_steps(kb), mx_planes_of(wfmt), out);
 }
 
 void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out) {
   for (uint32_t i = 0; i < job.m_tiles * job.n_tiles; ++i) out[i] = make_tile(job, nt, i);
 }
 
-int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t tiles,
-                int sm_count, uint32_t* err, cudaStream_t s) {
+int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t wfmt,
+                uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t s) {
   if (tiles == 0) return 0;
   if (tiles_dev == nullptr && inline_job == nullptr) return -1;
-  if (nt == 64) return launch_mx<64>(tiles_dev, inline_job, tiles, sm_count, err, s);
-  if (nt == 128) return launch_mx<128>(tiles_dev, inline_job, tiles, sm_count, err, s);
+  const uint32_t wp = mx_planes_of(wfmt);
+  if (nt == 64 && wp == 1) return launch_mx<64, 1>(tiles_dev, inline_job, tiles, sm_count, err, s);
+  if (nt == 128 && wp == 1) return launch_mx<128, 1>(tiles_dev, inline_job, tiles, sm_count, err, s);
+  if (nt == 64 && wp == 3) return launch_mx<64, 3>(tiles_dev, inline_job, tiles, sm_count, err, s);
+  if (nt == 128 && wp == 3) return launch_mx<128, 3>(tiles_dev, inline_job, tiles, sm_count, err, s);
   return -1;
 }
 

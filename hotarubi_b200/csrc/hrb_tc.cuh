@@ -31,9 +31,10 @@ size_t tc_weight_tile_bytes(uint32_t wfmt, uint32_t N, uint32_t kb);
 size_t tc_act_tile_bytes(uint32_t M, uint32_t kb);
 void tc_fill_job(TcJob& t, uint32_t wfmt, uint32_t M, uint32_t N, uint32_t kb);
 
-// The kind::mxf4 path for MXFP4 weights (gemm_mxf4.cu): tokens per tile
-// (64 or 128), 256-element K steps, prepared operand sizes, the weight
-// translation and the launch.
+// The kind::mxf4 path (gemm_mxf4.cu) for MXFP4 weights (their own E2M1
+// codes) and W8 weights (three E2M1 digit planes): tokens per tile (64 or
+// 128), 256-element K steps, prepared operand sizes, the weight translation
+// and the launch.
 uint32_t mx_tokens_per_tile(uint32_t M);
 uint32_t mx_k_steps(uint32_t kb);
 
@@ -56,10 +57,10 @@ __host__ __device__ inline uint32_t mx_act_sf_offset(uint32_t nt, uint32_t stack
   return 3u * nt * 128u + chunk * 512u + (r % 32u) * 16u + ((r % 128u) / 32u) * 4u +
          block_in_step % 4u;
 }
-size_t mx_weight_bytes(uint32_t N, uint32_t kb);
+size_t mx_weight_bytes(uint32_t wfmt, uint32_t N, uint32_t kb);
 size_t mx_act_bytes(uint32_t M, uint32_t kb);
-void launch_tile_weights_mxf4(const uint8_t* w, const uint8_t* ws, uint32_t N, uint32_t kb,
-                              uint8_t* out, cudaStream_t stream);
+void launch_tile_weights_mxf4(uint32_t wfmt, const uint8_t* w, const uint8_t* ws, uint32_t N,
+                              uint32_t kb, uint8_t* out, cudaStream_t stream);
 // One output tile of a kind::mxf4 launch with its operands located.  Plans
 // build the array on the host once, so the kernel's roles read a tile's
 // fields with independent loads, one tile ahead, instead of searching jobs.
@@ -77,8 +78,8 @@ static_assert(sizeof(MxTile) == 48, "MxTile is read as three 16-byte loads");
 void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out);
 // One launch over `tiles` output tiles: the device array tiles_dev, or, when
 // it is null, the tiles of the single *inline_job.
-int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t tiles,
-                int sm_count, uint32_t* err, cudaStream_t stream);
+int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t wfmt,
+                uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t stream);
 
 // Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current
 // device, once per (kernel, device).

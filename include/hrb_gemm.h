@@ -232,6 +232,14 @@ HRB_API hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs,
 /* Launches the whole batch on `stream`; returns the number of kernels it
  * launched in *launches (may be NULL). */
 HRB_API hrb_status hrb_plan_run(hrb_plan* plan, void* stream, uint32_t* launches);
+/* The plan end to end with host buffers, asynchronous on `stream`: for each
+ * GEMM i in creation order, copies a_host[i] into the activations the
+ * descriptor named (FP32 rows, or MXINT8 codes plus ascale_host[i]), runs the
+ * plan, and copies C (M rows of ldc floats) into c_host[i].  A NULL array or
+ * NULL entry skips that copy; weights and bias stay resident.  Host buffers
+ * should be pinned.  Wait with hrb_sync or on the stream. */
+HRB_API hrb_status hrb_plan_run_host(hrb_plan* plan, void* stream, const void* const* a_host,
+                                     const void* const* ascale_host, void* const* c_host);
 HRB_API hrb_status hrb_plan_destroy(hrb_plan* plan);
 /* Measurement aid: runs the plan once, then each of its launches alone,
  * `reps` times back to back between two CUDA events on `stream`, and writes

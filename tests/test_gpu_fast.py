@@ -200,3 +200,31 @@ def test_fast_mxfp4_activation_planes_are_exact(hrb, quant, m):
     if quant == 0:
         assert (s < 6).any()         # the subnormal-only block is covered
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("wfmt", [0, 1])
+def test_fast_weight_operands_are_exact(hrb, wfmt):
+    """A = I (every block's largest value 1.0: q = 64, scale 2^0), so output
+    C[r][n] is weight W[n][r] alone, which the tensor-core path must give
+    exactly: MXFP4 codes as they are, W8 as its three E2M1 digit planes with
+    scales e - 6 + 3p.  Bit-equality pins the weight translation."""
+    from hotarubi_b200 import capi
+    rng = np.random.default_rng(90 + wfmt)
+    m = k = 288                       # kb = 9: the second 256-element step is mostly padding
+    n = 200
+    x = np.eye(m, k, dtype=np.float32)
+    kb = k // 32
+    if wfmt == 0:
+        w, ws = weights(rng, 0, n, kb)
+    else:
+        w = rng.integers(-128, 128, (n, k)).astype(np.int8).view(np.uint8)
+        ws = rng.integers(100, 140, (n, kb)).astype(np.uint8)
+    c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    keep = [dev(x), dev(w), dev(ws)]
+    d = capi.Library.desc(wfmt, m, n, k, a=keep[0], w=keep[1], wscale=keep[2], c=c,
+                          mode=capi.MODE_FAST)
+    hrb.dense(d)
+    hrb.sync()
+    got = c.cpu().numpy()
+    want = dequant_w(wfmt, w, ws, n, k).T.astype(np.float32)  # [k][n] = W[n][k]
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
