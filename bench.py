@@ -302,14 +302,17 @@ def build_batch(torch, lib, capi, wl: Workload, batch: int, mode: int, distinct:
     """B instances on the device: `distinct` seeded operand sets copied into
     B separate buffers (distinct memory, so every instance streams)."""
     sets = [host_operands(wl, i) for i in range(min(distinct, batch))]
+    # Activations and outputs of the batch are one allocation each (a batch
+    # of requests arrives and leaves as one block); weights are separate.
+    a_all = torch.empty((batch, wl.M, wl.K), dtype=torch.float32, device="cuda")
+    c_all = torch.zeros((batch, wl.M, wl.N), dtype=torch.float32, device="cuda")
     inst = []
     for b in range(batch):
         x, w, ws, bias = sets[b % len(sets)]
+        a_all[b].copy_(torch.from_numpy(x))
         inst.append(dict(
-            a=torch.from_numpy(x).cuda(), w=torch.from_numpy(w).cuda(),
-            ws=torch.from_numpy(ws).cuda(),
-            bias=None if bias is None else torch.from_numpy(bias).cuda(),
-            c=torch.zeros((wl.M, wl.N), dtype=torch.float32, device="cuda")))
+            a=a_all[b], w=torch.from_numpy(w).cuda(), ws=torch.from_numpy(ws).cuda(),
+            bias=None if bias is None else torch.from_numpy(bias).cuda(), c=c_all[b]))
     descs = [capi.Library.desc(wl.wfmt, wl.M, wl.N, wl.K, a=d["a"], w=d["w"], wscale=d["ws"],
                                bias=d["bias"], c=d["c"], mode=mode) for d in inst]
     torch.cuda.synchronize()
@@ -333,8 +336,12 @@ def time_e2e(torch, plan, wl: Workload, sets, batch: int, steps: int, warmup: in
              stream) -> dict:
     """hrb_plan_run_host over the batch: every GEMM's FP32 activations from
     pinned host memory to the device, the plan, C back to pinned memory."""
-    a_host = [torch.from_numpy(sets[b % len(sets)][0]).pin_memory() for b in range(batch)]
-    c_host = [torch.zeros((wl.M, wl.N), dtype=torch.float32).pin_memory() for _ in range(batch)]
+    a_all = torch.empty((batch, wl.M, wl.K), dtype=torch.float32).pin_memory()
+    for b in range(batch):
+        a_all[b].copy_(torch.from_numpy(sets[b % len(sets)][0]))
+    c_all = torch.zeros((batch, wl.M, wl.N), dtype=torch.float32).pin_memory()
+    a_host = [a_all[b] for b in range(batch)]
+    c_host = [c_all[b] for b in range(batch)]
     for _ in range(warmup):
         plan.run_host(a_host, c_host, stream=stream.cuda_stream)
     stream.synchronize()

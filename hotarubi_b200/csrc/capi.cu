@@ -54,6 +54,7 @@ struct hrb_plan {
   uint32_t nplanes = 0;
   uint64_t plane_units = 0;
   const hrb::QuantJob* d_planes = nullptr;
+  std::vector<hrb::QuantJob> d_planes_host;  // the same jobs on the host
   struct Group {
     uint32_t wfmt;
     uint32_t kind;  // 0 exact kernel, 1 BF16 tensor-core kernel, 2 kind::mxf4 kernel
@@ -71,8 +72,14 @@ struct hrb_plan {
     size_t ascale_bytes;
     void* c;          // [M][ldc]
     size_t c_bytes;
+    uint32_t tile_begin, tiles;  // output tiles in the kind::mxf4 group
   };
   std::vector<Io> io;
+  // hrb_plan_run_host pipelines chunks of GEMMs (copy in / compute / copy
+  // out on three streams) when the plan is one kind::mxf4 group fed by the
+  // digit-plane encoder; created on first use.
+  cudaStream_t s_in = nullptr, s_out = nullptr;
+  std::vector<cudaEvent_t> events;
 };
 
 namespace {
@@ -805,6 +812,8 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
       tj.tile_begin = tc_tiles[g];
       tc_tiles[g] += tj.m_tiles * tj.n_tiles;
       tc_groups[g].push_back(tj);
+      plan->io[i].tile_begin = tj.tile_begin;
+      plan->io[i].tiles = tj.m_tiles * tj.n_tiles;
       continue;
     }
     const int8_t* aq = d.aq;
@@ -862,6 +871,7 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
                              cudaMemcpyHostToDevice));
     plan->d_planes = reinterpret_cast<const hrb::QuantJob*>(dst);
     plan->nplanes = static_cast<uint32_t>(planes.size());
+    plan->d_planes_host = planes;
     dst += planes.size() * sizeof(hrb::QuantJob);
   }
   for (uint32_t f = 0; f < 3; ++f) {
@@ -962,25 +972,117 @@ hrb_status hrb_plan_run_host(hrb_plan* plan, void* stream, const void* const* a_
   hrb_ctx* ctx = plan->ctx;
   HRB_CUDA(ctx, cudaSetDevice(ctx->device));
   cudaStream_t s = pick(ctx, stream);
-  const size_t n = plan->io.size();
-  for (size_t i = 0; i < n && a_host != nullptr; ++i) {
-    const hrb_plan::Io& io = plan->io[i];
-    if (a_host[i] != nullptr) {
-      HRB_CUDA(ctx, cudaMemcpyAsync(io.a, a_host[i], io.a_bytes, cudaMemcpyHostToDevice, s));
+  const uint32_t n = static_cast<uint32_t>(plan->io.size());
+  // Copies of GEMMs [g0, g1) in one direction, adjacent ranges merged.
+  auto copy_in = [&](uint32_t g0, uint32_t g1, cudaStream_t cs) -> hrb_status {
+    for (int part = 0; part < 2; ++part) {
+      const void* const* host = part == 0 ? a_host : ascale_host;
+      if (host == nullptr) continue;
+      char* dst = nullptr;
+      const char* src = nullptr;
+      size_t len = 0;
+      for (uint32_t i = g0; i <= g1; ++i) {
+        char* d = nullptr;
+        const char* h = nullptr;
+        size_t b = 0;
+        if (i < g1 && host[i] != nullptr) {
+          d = static_cast<char*>(part == 0 ? plan->io[i].a : plan->io[i].ascale);
+          h = static_cast<const char*>(host[i]);
+          b = part == 0 ? plan->io[i].a_bytes : plan->io[i].ascale_bytes;
+          if (d == nullptr) b = 0;
+        }
+        if (len > 0 && b > 0 && d == dst + len && h == src + len) {
+          len += b;
+          continue;
+        }
+        if (len > 0) HRB_CUDA(ctx, cudaMemcpyAsync(dst, src, len, cudaMemcpyHostToDevice, cs));
+        dst = d;
+        src = h;
+        len = b;
+      }
     }
-    if (io.ascale != nullptr && ascale_host != nullptr && ascale_host[i] != nullptr) {
-      HRB_CUDA(ctx, cudaMemcpyAsync(io.ascale, ascale_host[i], io.ascale_bytes,
-                                    cudaMemcpyHostToDevice, s));
+    return HRB_OK;
+  };
+  auto copy_out = [&](uint32_t g0, uint32_t g1, cudaStream_t cs) -> hrb_status {
+    if (c_host == nullptr) return HRB_OK;
+    char* dst = nullptr;
+    const char* src = nullptr;
+    size_t len = 0;
+    for (uint32_t i = g0; i <= g1; ++i) {
+      char* h = nullptr;
+      const char* d = nullptr;
+      size_t b = 0;
+      if (i < g1 && c_host[i] != nullptr) {
+        h = static_cast<char*>(c_host[i]);
+        d = static_cast<const char*>(plan->io[i].c);
+        b = plan->io[i].c_bytes;
+      }
+      if (len > 0 && b > 0 && h == dst + len && d == src + len) {
+        len += b;
+        continue;
+      }
+      if (len > 0) HRB_CUDA(ctx, cudaMemcpyAsync(dst, src, len, cudaMemcpyDeviceToHost, cs));
+      dst = h;
+      src = d;
+      len = b;
+    }
+    return HRB_OK;
+  };
+  const bool pipelined = plan->nquant == 0 && plan->nplanes == n && plan->groups.size() == 1 &&
+                         plan->groups[0].kind == 2 && n >= 8;
+  if (!pipelined) {
+    hrb_status st = copy_in(0, n, s);
+    if (st != HRB_OK) return st;
+    uint32_t launched = 0;
+    st = plan_launch(plan, s, -1, &launched);
+    if (st != HRB_OK) return st;
+    return copy_out(0, n, s);
+  }
+  // Chunks of GEMMs: copy-in of chunk c+1 and copy-out of chunk c-1 overlap
+  // the encoder and GEMM of chunk c.
+  constexpr uint32_t kChunks = 8;
+  const uint32_t chunks = std::min(kChunks, n / 2);
+  if (plan->s_in == nullptr) {
+    HRB_CUDA(ctx, cudaStreamCreateWithFlags(&plan->s_in, cudaStreamNonBlocking));
+    HRB_CUDA(ctx, cudaStreamCreateWithFlags(&plan->s_out, cudaStreamNonBlocking));
+    plan->events.resize(3 * kChunks + 1);
+    for (auto& e : plan->events) {
+      HRB_CUDA(ctx, cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     }
   }
-  uint32_t launched = 0;
-  const hrb_status st = plan_launch(plan, s, -1, &launched);
-  if (st != HRB_OK) return st;
-  for (size_t i = 0; i < n && c_host != nullptr; ++i) {
-    if (c_host[i] == nullptr) continue;
-    HRB_CUDA(ctx, cudaMemcpyAsync(c_host[i], plan->io[i].c, plan->io[i].c_bytes,
-                                  cudaMemcpyDeviceToHost, s));
+  cudaEvent_t* ev = plan->events.data();
+  cudaEvent_t entry = ev[3 * kChunks];
+  // Nothing of this run starts before the work already queued on s.
+  HRB_CUDA(ctx, cudaEventRecord(entry, s));
+  HRB_CUDA(ctx, cudaStreamWaitEvent(plan->s_in, entry, 0));
+  HRB_CUDA(ctx, cudaStreamWaitEvent(plan->s_out, entry, 0));
+  const auto& g = plan->groups[0];
+  for (uint32_t c = 0; c < chunks; ++c) {
+    const uint32_t g0 = static_cast<uint32_t>(static_cast<uint64_t>(n) * c / chunks);
+    const uint32_t g1 = static_cast<uint32_t>(static_cast<uint64_t>(n) * (c + 1) / chunks);
+    hrb_status st = copy_in(g0, g1, plan->s_in);
+    if (st != HRB_OK) return st;
+    HRB_CUDA(ctx, cudaEventRecord(ev[c], plan->s_in));
+    HRB_CUDA(ctx, cudaStreamWaitEvent(s, ev[c], 0));
+    uint64_t units = 0;
+    for (uint32_t i = g0; i < g1; ++i) units += plan->d_planes_host[i].units;
+    hrb::launch_quantize_planes(plan->d_planes + g0, g1 - g0, nullptr, units, ctx->d_error,
+                                ctx->sm_count, s);
+    const uint32_t t0 = plan->io[g0].tile_begin;
+    const uint32_t t1 = plan->io[g1 - 1].tile_begin + plan->io[g1 - 1].tiles;
+    const int k = hrb::launch_mxf4(g.d_tiles + t0, nullptr, g.nt, g.wfmt, t1 - t0,
+                                   ctx->sm_count, ctx->d_error, s);
+    if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
+    ctx->launches += 1u + static_cast<uint64_t>(k);
+    HRB_CUDA(ctx, cudaEventRecord(ev[kChunks + c], s));
+    HRB_CUDA(ctx, cudaStreamWaitEvent(plan->s_out, ev[kChunks + c], 0));
+    st = copy_out(g0, g1, plan->s_out);
+    if (st != HRB_OK) return st;
   }
+  // The caller's stream covers every copy: its next work follows them.
+  HRB_CUDA(ctx, cudaEventRecord(ev[2 * kChunks], plan->s_out));
+  HRB_CUDA(ctx, cudaStreamWaitEvent(s, ev[2 * kChunks], 0));
+  HRB_CUDA(ctx, cudaGetLastError());
   return HRB_OK;
 }
 
@@ -1025,6 +1127,13 @@ hrb_status hrb_plan_destroy(hrb_plan* plan) {
   if (plan == nullptr) return HRB_OK;
   cudaSetDevice(plan->ctx->device);
   cudaStreamSynchronize(plan->ctx->stream);
+  if (plan->s_in != nullptr) {
+    cudaStreamSynchronize(plan->s_in);
+    cudaStreamSynchronize(plan->s_out);
+    for (auto& e : plan->events) cudaEventDestroy(e);
+    cudaStreamDestroy(plan->s_in);
+    cudaStreamDestroy(plan->s_out);
+  }
   cudaFree(plan->d_jobs);
   cudaFree(plan->d_scratch);
   delete plan;

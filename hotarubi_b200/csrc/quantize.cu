@@ -469,11 +469,15 @@ k_quantize_planes(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ 
   const uint32_t lane = threadIdx.x & 31u, wib = threadIdx.x >> 5;
   const uint32_t warp = blockIdx.x * kPlaneWarps + wib;
   const uint32_t nwarps = gridDim.x * kPlaneWarps;
-  const uint64_t total = jobs != nullptr ? jobs[njobs - 1].unit_begin + jobs[njobs - 1].units
-                                         : inline_job.units;
+  // The jobs may be a consecutive subset of a larger launch's: their units
+  // are [first job's unit_begin, last job's end).
+  const uint64_t base = jobs != nullptr ? jobs[0].unit_begin : 0;
+  const uint64_t total = jobs != nullptr
+                             ? jobs[njobs - 1].unit_begin + jobs[njobs - 1].units - base
+                             : inline_job.units;
   const uint64_t per = (total + nwarps - 1) / nwarps;
-  const uint64_t begin = static_cast<uint64_t>(warp) * per;
-  const uint64_t end = begin + per < total ? begin + per : total;
+  const uint64_t begin = base + static_cast<uint64_t>(warp) * per;
+  const uint64_t end = begin + per < base + total ? begin + per : base + total;
   if (begin >= end) return;
   const uint32_t count = static_cast<uint32_t>(end - begin);
   PlaneCursor ld;

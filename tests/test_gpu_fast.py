@@ -228,3 +228,53 @@ def test_fast_weight_operands_are_exact(hrb, wfmt):
     got = c.cpu().numpy()
     want = dequant_w(wfmt, w, ws, n, k).T.astype(np.float32)  # [k][n] = W[n][k]
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("mixed", [False, True])
+def test_plan_run_host_matches_device_run(hrb, mixed):
+    """hrb_plan_run_host (host activations in, C out; pipelined in chunks
+    over three streams when the plan is one kind::mxf4 group) gives the
+    same bits as the plan run on device-resident operands."""
+    from hotarubi_b200 import capi
+    rng = np.random.default_rng(55 + mixed)
+    n_gemm = 12
+    m, n, k = 40, 136, 320
+    wfmts = [2 if (mixed and i % 3 == 0) else 0 for i in range(n_gemm)]
+    a_dev = torch.zeros((n_gemm, m, k), dtype=torch.float32, device="cuda")
+    c_dev = torch.zeros((n_gemm, m, n), dtype=torch.float32, device="cuda")
+    keep, descs = [], []
+    for i, f in enumerate(wfmts):
+        w, ws = weights(rng, f, n, k // 32)
+        t = [dev(w), dev(ws)]
+        keep += t
+        descs.append(capi.Library.desc(f, m, n, k, a=a_dev[i], w=t[0], wscale=t[1],
+                                       c=c_dev[i], mode=capi.MODE_FAST))
+    plan = hrb.plan(descs)
+    x = rng.standard_normal((n_gemm, m, k)).astype(np.float32)
+    # Device run for the expected bits.
+    a_dev.copy_(torch.from_numpy(x))
+    plan.run()
+    hrb.sync()
+    want = c_dev.cpu().numpy().copy()
+    c_dev.zero_()
+    # Host run: one contiguous pinned block, except one GEMM from its own
+    # buffer (breaks a coalesced copy) and one skipped output.
+    a_pin = torch.from_numpy(x).pin_memory()
+    lone = torch.from_numpy(x[5].copy()).pin_memory()
+    c_pin = torch.zeros((n_gemm, m, n), dtype=torch.float32).pin_memory()
+    a_host = [a_pin[i] for i in range(n_gemm)]
+    a_host[5] = lone
+    c_host = [c_pin[i] for i in range(n_gemm)]
+    c_host[7] = None
+    a_dev.zero_()
+    torch.cuda.synchronize()
+    for _ in range(2):  # twice: the second run reuses the plan's streams
+        plan.run_host(a_host, c_host)
+        hrb.sync()
+    got = c_pin.numpy()
+    for i in range(n_gemm):
+        if i == 7:
+            assert not got[i].any()
+        else:
+            assert np.array_equal(got[i].view(np.uint32), want[i].view(np.uint32)), i
+    plan.close()
