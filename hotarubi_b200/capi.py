@@ -40,6 +40,10 @@ class GemmCmd(ctypes.Structure):
         "a_base", "a_stride", "kb", "m", "w_base", "w_stride", "n8", "c_base", "wmode", "acc")]
 
 
+class IpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_uint8 * 64)]
+
+
 class GemmDesc(ctypes.Structure):
     """hrb_gemm_desc."""
     _fields_ = [
@@ -103,6 +107,13 @@ def load() -> ctypes.CDLL:
             "hrb_w8_planes_to_dense": (ctypes.c_int, [P, P, P, u32, u32, P, P, P]),
             "hrb_abuf_to_dense": (ctypes.c_int, [P, P, u32, u32, P, P, P]),
             "hrb_dense_to_fbuf": (ctypes.c_int, [P, P, u32, u32, P, P]),
+            "hrb_shared_alloc": (ctypes.c_int, [P, ctypes.c_size_t, ctypes.POINTER(P),
+                                                ctypes.POINTER(IpcHandle)]),
+            "hrb_shared_free": (ctypes.c_int, [P, P]),
+            "hrb_peer_open": (ctypes.c_int, [P, ctypes.POINTER(IpcHandle), ctypes.POINTER(P)]),
+            "hrb_peer_close": (ctypes.c_int, [P, P]),
+            "hrb_shard_columns": (None, [u32, u32, u32, ctypes.POINTER(u32), ctypes.POINTER(u32)]),
+            "hrb_plan_set_peers": (ctypes.c_int, [P, P, ctypes.POINTER(P), u32]),
         }
         for name, (res, args) in sigs.items():
             f = getattr(lib, name)
@@ -120,6 +131,14 @@ def _ptr(x) -> int | None:
     if isinstance(x, np.ndarray):
         return x.ctypes.data
     return x.data_ptr()  # torch tensor
+
+
+def shard_columns(n: int, rank: int, ranks: int) -> tuple[int, int]:
+    """hrb_shard_columns: output columns [n0, n1) of `rank` of `ranks`, in
+    whole 128-column tiles (no device needed)."""
+    n0, n1 = ctypes.c_uint32(), ctypes.c_uint32()
+    load().hrb_shard_columns(n, rank, ranks, ctypes.byref(n0), ctypes.byref(n1))
+    return n0.value, n1.value
 
 
 def gemm_check(cmd: GemmCmd) -> tuple[int, str]:
@@ -248,6 +267,26 @@ class Library:
         return Plan(self, descs)
 
     # -- translation ------------------------------------------------------
+    def shared_alloc(self, nbytes: int) -> tuple[int, bytes]:
+        """hrb_shared_alloc: (device pointer, 64-byte IPC handle)."""
+        ptr = ctypes.c_void_p()
+        h = IpcHandle()
+        self._check(self.lib.hrb_shared_alloc(self.ctx, nbytes, ctypes.byref(ptr), ctypes.byref(h)))
+        return ptr.value, bytes(h.bytes)
+
+    def shared_free(self, ptr: int) -> None:
+        self._check(self.lib.hrb_shared_free(self.ctx, ptr))
+
+    def peer_open(self, handle: bytes) -> int:
+        h = IpcHandle()
+        ctypes.memmove(h.bytes, handle, 64)
+        ptr = ctypes.c_void_p()
+        self._check(self.lib.hrb_peer_open(self.ctx, ctypes.byref(h), ctypes.byref(ptr)))
+        return ptr.value
+
+    def peer_close(self, ptr: int) -> None:
+        self._check(self.lib.hrb_peer_close(self.ctx, ptr))
+
     def wbuf_to_dense(self, words, groups, kb, codes, scales, stream=0):
         self._check(self.lib.hrb_wbuf_to_dense(self.ctx, _ptr(words), groups, kb, _ptr(codes),
                                                _ptr(scales), stream or None))
@@ -289,6 +328,13 @@ class Plan:
         self._host_args = (arr(a_host), arr(ascale_host), arr(c_host))  # alive until the call ends
         a, sc, c = self._host_args
         self.owner._check(self.owner.lib.hrb_plan_run_host(self.h, stream or None, a, sc, c))
+
+    def set_peers(self, local_base: int, peer_bases: list[int]) -> None:
+        """hrb_plan_set_peers: every output also goes to each peer base +
+        (its address - local_base)."""
+        arr = (ctypes.c_void_p * max(1, len(peer_bases)))(*peer_bases)
+        self.owner._check(self.owner.lib.hrb_plan_set_peers(self.h, local_base, arr,
+                                                            len(peer_bases)))
 
     def profile(self, reps: int = 10, stream: int = 0) -> list[float]:
         """Mean milliseconds of each kernel launch of the plan."""

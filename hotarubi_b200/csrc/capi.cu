@@ -80,6 +80,8 @@ struct hrb_plan {
   // digit-plane encoder; created on first use.
   cudaStream_t s_in = nullptr, s_out = nullptr;
   std::vector<cudaEvent_t> events;
+  // Peers that receive every output (hrb_plan_set_peers).
+  hrb::MxPeers peers{};
 };
 
 namespace {
@@ -317,9 +319,10 @@ void tc_translate(const hrb_gemm_desc* d, const hrb::TcJob& tj, cudaStream_t s) 
 // One launch of the tensor-core kernel for a group of jobs.
 int tc_launch(bool mx, const hrb::TcJob* jobs_dev, const hrb::MxTile* mx_tiles, uint32_t njobs,
               const hrb::TcJob* inline_job, uint32_t nt, uint32_t wfmt, uint32_t tiles,
-              hrb_ctx* ctx, cudaStream_t s) {
+              hrb_ctx* ctx, cudaStream_t s, const hrb::MxPeers* peers = nullptr) {
   if (mx) {
-    return hrb::launch_mxf4(mx_tiles, inline_job, nt, wfmt, tiles, ctx->sm_count, ctx->d_error, s);
+    return hrb::launch_mxf4(mx_tiles, inline_job, nt, wfmt, tiles, ctx->sm_count, ctx->d_error, s,
+                            peers);
   }
   return hrb::launch_tc_jobs(jobs_dev, njobs, inline_job, nt, wfmt, tiles, ctx->d_error, s);
 }
@@ -942,7 +945,7 @@ hrb_status plan_launch(hrb_plan* plan, cudaStream_t s, int64_t only, uint32_t* l
           static_cast<const hrb::DenseJob*>(g.d_jobs), g.njobs, nullptr, g.tiles, g.wfmt, s));
     } else {
       const int k = tc_launch(g.kind == 2, static_cast<const hrb::TcJob*>(g.d_jobs), g.d_tiles,
-                              g.njobs, nullptr, g.nt, g.wfmt, g.tiles, ctx, s);
+                              g.njobs, nullptr, g.nt, g.wfmt, g.tiles, ctx, s, &plan->peers);
       if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
       n += static_cast<uint32_t>(k);
     }
@@ -1071,7 +1074,7 @@ hrb_status hrb_plan_run_host(hrb_plan* plan, void* stream, const void* const* a_
     const uint32_t t0 = plan->io[g0].tile_begin;
     const uint32_t t1 = plan->io[g1 - 1].tile_begin + plan->io[g1 - 1].tiles;
     const int k = hrb::launch_mxf4(g.d_tiles + t0, nullptr, g.nt, g.wfmt, t1 - t0,
-                                   ctx->sm_count, ctx->d_error, s);
+                                   ctx->sm_count, ctx->d_error, s, &plan->peers);
     if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
     ctx->launches += 1u + static_cast<uint64_t>(k);
     HRB_CUDA(ctx, cudaEventRecord(ev[kChunks + c], s));
@@ -1121,6 +1124,84 @@ hrb_status hrb_plan_profile(hrb_plan* plan, void* stream, uint32_t reps, float* 
   if (st != HRB_OK) return st == HRB_ECUDA ? fail(ctx, st, "profiling run failed") : st;
   *nkernels = steps;
   return HRB_OK;
+}
+
+hrb_status hrb_plan_set_peers(hrb_plan* plan, const void* local_base, void* const* peer_bases,
+                              uint32_t npeers) {
+  if (plan == nullptr) return HRB_EINVAL;
+  hrb_ctx* ctx = plan->ctx;
+  if (npeers > hrb::kMaxPeers || (npeers > 0 && (local_base == nullptr || peer_bases == nullptr))) {
+    return fail(ctx, HRB_EINVAL, "at most %u peers, with a local base", hrb::kMaxPeers);
+  }
+  if (npeers > 0 && (plan->nquant > 0 || std::any_of(plan->groups.begin(), plan->groups.end(),
+                                                      [](const auto& g) { return g.kind != 2; }))) {
+    return fail(ctx, HRB_ENOTSUP,
+                "peer outputs need every GEMM on the MXFP4/W8 tensor-core path");
+  }
+  hrb::MxPeers peers{};
+  peers.count = npeers;
+  for (uint32_t i = 0; i < npeers; ++i) {
+    if (peer_bases[i] == nullptr) return fail(ctx, HRB_EINVAL, "null peer base");
+    peers.delta[i] = static_cast<const char*>(peer_bases[i]) - static_cast<const char*>(local_base);
+  }
+  HRB_CUDA(ctx, cudaStreamSynchronize(ctx->stream));  // no run in flight sees half a change
+  plan->peers = peers;
+  return HRB_OK;
+}
+
+hrb_status hrb_shared_alloc(hrb_ctx* ctx, size_t bytes, void** ptr, hrb_ipc_handle* handle) {
+  if (ctx == nullptr || ptr == nullptr || handle == nullptr || bytes == 0) return HRB_EINVAL;
+  static_assert(sizeof(cudaIpcMemHandle_t) <= sizeof(hrb_ipc_handle), "IPC handle size");
+  *ptr = nullptr;
+  HRB_CUDA(ctx, cudaSetDevice(ctx->device));
+  HRB_CUDA(ctx, cudaMalloc(ptr, bytes));
+  cudaIpcMemHandle_t h;
+  const cudaError_t err = cudaIpcGetMemHandle(&h, *ptr);
+  if (err != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return cuda_fail(ctx, err, "cudaIpcGetMemHandle");
+  }
+  std::memset(handle, 0, sizeof(*handle));
+  std::memcpy(handle->bytes, &h, sizeof(h));
+  return HRB_OK;
+}
+
+hrb_status hrb_shared_free(hrb_ctx* ctx, void* ptr) {
+  if (ctx == nullptr) return HRB_EINVAL;
+  HRB_CUDA(ctx, cudaSetDevice(ctx->device));
+  HRB_CUDA(ctx, cudaFree(ptr));
+  return HRB_OK;
+}
+
+hrb_status hrb_peer_open(hrb_ctx* ctx, const hrb_ipc_handle* handle, void** peer_ptr) {
+  if (ctx == nullptr || handle == nullptr || peer_ptr == nullptr) return HRB_EINVAL;
+  *peer_ptr = nullptr;
+  HRB_CUDA(ctx, cudaSetDevice(ctx->device));
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle->bytes, sizeof(h));
+  HRB_CUDA(ctx, cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return HRB_OK;
+}
+
+hrb_status hrb_peer_close(hrb_ctx* ctx, void* peer_ptr) {
+  if (ctx == nullptr) return HRB_EINVAL;
+  HRB_CUDA(ctx, cudaSetDevice(ctx->device));
+  HRB_CUDA(ctx, cudaIpcCloseMemHandle(peer_ptr));
+  return HRB_OK;
+}
+
+void hrb_shard_columns(uint32_t N, uint32_t rank, uint32_t ranks, uint32_t* n0, uint32_t* n1) {
+  if (n0 == nullptr || n1 == nullptr) return;
+  if (ranks == 0 || rank >= ranks) {
+    *n0 = *n1 = 0;
+    return;
+  }
+  const uint32_t tiles = (N + 127u) / 128u;
+  const uint32_t t0 = static_cast<uint32_t>(static_cast<uint64_t>(tiles) * rank / ranks);
+  const uint32_t t1 = static_cast<uint32_t>(static_cast<uint64_t>(tiles) * (rank + 1) / ranks);
+  *n0 = std::min(N, t0 * 128u);
+  *n1 = std::min(N, t1 * 128u);
 }
 
 hrb_status hrb_plan_destroy(hrb_plan* plan) {

@@ -95,6 +95,7 @@ struct MxParams {
   const MxTile* tiles;  // device tiles, or null: the tiles of inline_job
   uint32_t total_tiles;
   uint32_t* err;
+  MxPeers peers;        // outputs also stored at these byte offsets (peer GPUs)
   TcJob inline_job;
 };
 
@@ -386,13 +387,20 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
             float* dst = cbase + static_cast<size_t>(j0 + j) * ti.ldc;
             float x = (__uint_as_float(v0[j]) + __uint_as_float(v1[j])) + __uint_as_float(v2[j]);
             if (acc) x += *dst;
-            *dst = x + bias;
+            x += bias;
+            *dst = x;
+            // The same output into each peer's C (NVLink stores).
+            for (uint32_t q = 0; q < p.peers.count; ++q) {
+              *reinterpret_cast<float*>(reinterpret_cast<char*>(dst) + p.peers.delta[q]) = x;
+            }
           }
         }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);
     }
+    // Peer stores performed before the kernel is seen to finish.
+    if (p.peers.count != 0) __threadfence_system();
   }
   tc_fence_before();
   __syncthreads();
@@ -491,7 +499,7 @@ __global__ void k_tile_weights_mxf4(const uint8_t* __restrict__ w, const uint8_t
 
 template <uint32_t NT, uint32_t WP>
 int launch_mx(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, int sm_count,
-              uint32_t* err, cudaStream_t s) {
+              uint32_t* err, cudaStream_t s, const MxPeers* peers) {
   using Cfg = MxCfg<NT, WP>;
   if (!set_smem_limit_once(reinterpret_cast<const void*>(k_gemm_mxf4<NT, WP>), Cfg::kSmem)) {
     return -1;
@@ -500,6 +508,7 @@ int launch_mx(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, 
   p.tiles = tiles_dev;
   p.total_tiles = tiles;
   p.err = err;
+  if (peers != nullptr) p.peers = *peers;
   if (inline_job != nullptr) p.inline_job = *inline_job;
   const uint32_t grid = std::min<uint32_t>(tiles, static_cast<uint32_t>(sm_count));
   k_gemm_mxf4<NT, WP><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(p);
@@ -536,14 +545,24 @@ void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out) {
 }
 
 int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t wfmt,
-                uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t s) {
+                uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t s,
+                const MxPeers* peers) {
   if (tiles == 0) return 0;
   if (tiles_dev == nullptr && inline_job == nullptr) return -1;
+  if (peers != nullptr && peers->count > kMaxPeers) return -1;
   const uint32_t wp = mx_planes_of(wfmt);
-  if (nt == 64 && wp == 1) return launch_mx<64, 1>(tiles_dev, inline_job, tiles, sm_count, err, s);
-  if (nt == 128 && wp == 1) return launch_mx<128, 1>(tiles_dev, inline_job, tiles, sm_count, err, s);
-  if (nt == 64 && wp == 3) return launch_mx<64, 3>(tiles_dev, inline_job, tiles, sm_count, err, s);
-  if (nt == 128 && wp == 3) return launch_mx<128, 3>(tiles_dev, inline_job, tiles, sm_count, err, s);
+  if (nt == 64 && wp == 1) {
+    return launch_mx<64, 1>(tiles_dev, inline_job, tiles, sm_count, err, s, peers);
+  }
+  if (nt == 128 && wp == 1) {
+    return launch_mx<128, 1>(tiles_dev, inline_job, tiles, sm_count, err, s, peers);
+  }
+  if (nt == 64 && wp == 3) {
+    return launch_mx<64, 3>(tiles_dev, inline_job, tiles, sm_count, err, s, peers);
+  }
+  if (nt == 128 && wp == 3) {
+    return launch_mx<128, 3>(tiles_dev, inline_job, tiles, sm_count, err, s, peers);
+  }
   return -1;
 }
 

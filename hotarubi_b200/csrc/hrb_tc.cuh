@@ -76,10 +76,19 @@ struct MxTile {
 static_assert(sizeof(MxTile) == 48, "MxTile is read as three 16-byte loads");
 // The m_tiles * n_tiles tiles of one job (tile index mt * n_tiles + nt).
 void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out);
+// Peers that receive a copy of every output (the fused all-gather of a
+// column-sharded GEMM): output c is also stored at c + delta[i] bytes.
+constexpr uint32_t kMaxPeers = 7;
+struct MxPeers {
+  int64_t delta[kMaxPeers];
+  uint32_t count;
+};
+
 // One launch over `tiles` output tiles: the device array tiles_dev, or, when
-// it is null, the tiles of the single *inline_job.
+// it is null, the tiles of the single *inline_job.  `peers` may be null.
 int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t wfmt,
-                uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t stream);
+                uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t stream,
+                const MxPeers* peers = nullptr);
 
 // Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current
 // device, once per (kernel, device).

@@ -280,6 +280,42 @@ HRB_API hrb_status hrb_abuf_to_dense(hrb_ctx* ctx, const uint8_t* words,
 HRB_API hrb_status hrb_dense_to_fbuf(hrb_ctx* ctx, const float* c, uint32_t rows,
                              uint32_t cols, float* words, void* stream);
 
+/* ---------------------------------------------------------------------
+ * 5. Column-sharded GEMMs over the GPUs of one node (one process per GPU).
+ *    Rank r of G computes output columns [n0, n1) (hrb_shard_columns) of
+ *    every GEMM with its slice of W.  With peers set on a plan, the kernel's
+ *    epilogue stores each output into the local C and, over NVLink, into
+ *    every peer's C at the same offset: once every rank's run has finished
+ *    (the caller synchronises the ranks, e.g. a barrier), every rank holds
+ *    the whole of C.  This is the all-gather of the output slices fused into
+ *    the GEMM; peers' buffers are mapped with CUDA IPC handles.
+ * ------------------------------------------------------------------- */
+
+typedef struct hrb_ipc_handle {
+  uint8_t bytes[64];
+} hrb_ipc_handle;
+
+/* Device memory another process can map: `bytes` on the context's device,
+ * and the handle that names it. */
+HRB_API hrb_status hrb_shared_alloc(hrb_ctx* ctx, size_t bytes, void** ptr,
+                                    hrb_ipc_handle* handle);
+HRB_API hrb_status hrb_shared_free(hrb_ctx* ctx, void* ptr);
+/* Maps a peer's hrb_shared_alloc buffer into this process (peer access over
+ * NVLink enabled on first use); the pointer is valid on ctx's device. */
+HRB_API hrb_status hrb_peer_open(hrb_ctx* ctx, const hrb_ipc_handle* handle, void** peer_ptr);
+HRB_API hrb_status hrb_peer_close(hrb_ctx* ctx, void* peer_ptr);
+/* Output columns of rank `rank` of `ranks` for N columns: whole 128-column
+ * tiles, spread as evenly as possible (the last ranks may get none). */
+HRB_API void hrb_shard_columns(uint32_t N, uint32_t rank, uint32_t ranks, uint32_t* n0,
+                               uint32_t* n1);
+/* Makes every later run of `plan` also store each output to the peers: for
+ * an output at address c (in [local_base, ...)), also to
+ * peer_bases[i] + (c - local_base).  At most 7 peers; only plans whose GEMMs
+ * all take the tensor-core path for MXFP4 or W8 weights
+ * (HRB_MODE_FAST, FP32 activations) accept peers (else HRB_ENOTSUP). */
+HRB_API hrb_status hrb_plan_set_peers(hrb_plan* plan, const void* local_base,
+                                      void* const* peer_bases, uint32_t npeers);
+
 #ifdef __cplusplus
 }
 #endif
