@@ -487,6 +487,101 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
         dist.destroy_process_group()
 
 
+def run_shard(args, wl: Workload, rank: int, world: int, local_rank: int) -> None:
+    """--shard: the batch's GEMMs split along N over the ranks (strong
+    scaling: the total work is fixed); every rank's kernel also stores its
+    outputs into all other ranks' C over NVLink (the all-gather fused into
+    the GEMM), and a step ends when every rank holds all of C."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from hotarubi_b200 import capi, shard
+    torch.cuda.set_device(local_rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local_rank))
+    lib = capi.Library(local_rank)
+    stream = torch.cuda.Stream()
+    lib.set_stream(stream.cuda_stream)
+    batch = args.batch or wl.batch
+    n0, n1 = shard.columns(wl.N)
+    out = shard.PeerOutput(lib, (batch, wl.M, wl.N))
+    sets = [host_operands(wl, i) for i in range(min(4, batch))]
+    keep, descs = [], []
+    a_all = torch.empty((batch, wl.M, wl.K), dtype=torch.float32, device="cuda")
+    for b in range(batch):
+        x, w, ws, bias = sets[b % len(sets)]
+        a_all[b].copy_(torch.from_numpy(x))
+        t = [torch.from_numpy(w[n0:n1].copy()).cuda(), torch.from_numpy(ws[n0:n1].copy()).cuda(),
+             None if bias is None else torch.from_numpy(bias[n0:n1].copy()).cuda()]
+        keep += t
+        if n1 > n0:
+            descs.append(capi.Library.desc(wl.wfmt, wl.M, n1 - n0, wl.K, a=a_all[b], w=t[0],
+                                           wscale=t[1], bias=t[2],
+                                           c=out.tensor[b].data_ptr() + 4 * n0, ldc=wl.N,
+                                           mode=capi.MODE_FAST))
+    plan = lib.plan(descs) if descs else None
+    if plan is not None:
+        plan.set_peers(out.ptr, out.peer_bases)
+    torch.cuda.synchronize()
+    flag = torch.zeros(1, device="cuda")
+
+    def step():
+        if plan is not None:
+            plan.run(stream.cuda_stream)
+        with torch.cuda.stream(stream):
+            dist.all_reduce(flag)  # the step ends when every rank's stores are done
+
+    dist.barrier()
+    with ClockSampler(local_rank) as clocks:
+        for _ in range(args.warmup):
+            step()
+        stream.synchronize()
+        dist.barrier()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        end.synchronize()
+        dist.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    t = torch.tensor([ms], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    if rank == 0:
+        pk = peaks()
+        nvlink = (world - 1) * batch * wl.M * wl.N * 4 / world   # bytes each rank stores to peers
+        line = {
+            "metric": wl.metric, "value": batch * wl.flops / (ms / 1e3) / 1e12,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8 block dot + fp32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": wl.name, "batch": batch, "M": wl.M, "N": wl.N, "K": wl.K,
+                       "format": FMT_NAMES[wl.wfmt], "mode": "fast",
+                       "parallelism": f"N-sharded x{world}, all-gather fused into the GEMM "
+                                      "epilogue (NVLink peer stores)"},
+            "nvlink": {"bytes_per_rank_per_step": nvlink,
+                       "gbs_per_rank": nvlink / (ms / 1e3) / 1e9},
+            "tensor_peak_frac": batch * wl.flops / world / (ms / 1e3) / 1e12
+                                / (pk["bf16_tflops"] * 4.0 / 3.0),
+            "gpu_launches": 2 * args.steps if plan is not None else 0,
+            "e2e": None, "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    if plan is not None:
+        plan.close()
+    torch.cuda.synchronize()
+    dist.barrier()
+    out.close()
+    lib.close()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -500,6 +595,8 @@ def main() -> None:
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the host entry-point leg "
                    "(profiling runs)")
+    p.add_argument("--shard", action="store_true", help="split each GEMM along N over the "
+                   "ranks, with the all-gather fused into the kernel (strong scaling)")
     args = p.parse_args()
     wl = WORKLOADS[args.config]
     rank = int(os.environ.get("RANK", "0"))
@@ -507,6 +604,8 @@ def main() -> None:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, wl, rank, world)
+    elif args.shard:
+        run_shard(args, wl, rank, world, local_rank)
     else:
         run_ours(args, wl, rank, world, local_rank)
 
