@@ -1,7 +1,7 @@
 """Benchmark of the quantized GEMM hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c1|c5] [--mode exact|fast] [--batch B]
+                    [--config c2|c1|c4|c5] [--mode exact|fast] [--batch B]
 
 Default workload (the MXFP4 GEMM the metric is
 quoted on): C = A . W^T with A FP32 [64, 2560] ~ N(0,1) encoded to MXINT8 on
@@ -101,6 +101,11 @@ WORKLOADS = {
     "c1": Workload("c1", "c1_w8_64x960x2560", "C1 64x960x2560", 1, 64, 2560, 960, True, 128, "hbm"),
     "c5": Workload("c5", "c5_mxfp4_4096x4096x4096", "C5 4096x4096x4096", 0, 4096, 4096, 4096,
                    False, 4, "tensor"),
+    # C4's largest GEMM (the action expert's MLP 720 -> 2048, MXFP8) for one
+    # GPU's share of the 256 requests at 8 GPUs: 32 requests x 50 tokens,
+    # one GEMM per layer of a flow step (16).
+    "c4": Workload("c4", "c4_mxfp8_1600x720x2048", "C4 1600x720x2048", 2, 1600, 2048, 720,
+                   False, 16, "tensor"),
 }
 
 
@@ -437,15 +442,21 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
                     "alg_bytes_per_launch": batch * wl.bytes_gemm()}
         else:
             tflops = batch * wl.flops / (gemm_ms / 1e3) / 1e12
-            # kind::mxf4 runs at 4x the dense BF16 rate (nominal 9 vs 2.25
-            # PFLOP/s); each exact MXINT8 x E2M1 product takes three of its
-            # MMAs (the activation digit planes), so the useful ceiling is a
-            # third of that.
-            peak = pk["bf16_tflops"] * 4.0 / 3.0
+            if wl.wfmt == 2:
+                # MXFP8 runs kind::f16 (BF16 operands): the BF16 peak.
+                peak, how = pk["bf16_tflops"], " (cuBLAS BF16)"
+            else:
+                # kind::mxf4 runs at 4x the dense BF16 rate (nominal 9 vs
+                # 2.25 PFLOP/s); each exact MXINT8 x E2M1 product takes three
+                # of its MMAs (the activation digit planes; W8 weights add
+                # three planes more), so the useful ceiling is a third (a
+                # ninth) of that.
+                peak = pk["bf16_tflops"] * 4.0 / (3.0 if wl.wfmt == 0 else 9.0)
+                how = (" (cuBLAS BF16 x 4/3: FP4 MMA rate over three digit planes)"
+                       if wl.wfmt == 0 else " (cuBLAS BF16 x 4/9: FP4 MMA rate over 3 x 3 planes)")
             roof = {"bound": "tensor", "kernel": kname, "achieved": tflops, "peak": peak,
                     "unit": "TFLOP/s", "frac": tflops / peak,
-                    "peak_source": pk["source"] + " (cuBLAS BF16 x 4/3: FP4 MMA rate over "
-                                                  "three digit planes)",
+                    "peak_source": pk["source"] + how,
                     "frac_of_bf16_peak": tflops / pk["bf16_tflops"],
                     "alg_flops_per_launch": batch * wl.flops}
         roof.update({"traffic": (None if per_gemm_traffic is None

@@ -249,17 +249,15 @@ hrb_status run_dense(hrb_ctx* ctx, const hrb::DenseJob& job, cudaStream_t s) {
 // runs the exact kernel, whose results are within any tolerance.
 bool use_tc(const hrb_gemm_desc* d) { return d->mode == HRB_MODE_FAST && d->a != nullptr; }
 
-// MXFP4 and W8 weights in fast mode take the kind::mxf4 kernel (MXFP4 codes
-// as they are, W8 as three E2M1 digit planes; no decode in the kernel);
-// MXFP8 takes the BF16 kernel.
-bool use_mx(const hrb_gemm_desc* d) {
-  return use_tc(d) && (d->wfmt == HRB_WFMT_MXFP4 || d->wfmt == HRB_WFMT_W8);
-}
+// Every weight format in fast mode takes the block-scaled kernel with no
+// decode in it: MXFP4 codes and W8 (three E2M1 digit planes) on
+// kind::mxf4, MXFP8 codes on kind::mxf8f6f4.
+bool use_mx(const hrb_gemm_desc* d) { return use_tc(d); }
 
 // Tensor-core bytes of one GEMM: prepared activations then weight chunks.
 size_t tc_act_bytes(const hrb_gemm_desc* d) {
   const uint32_t kb = blocks_of(d->K);
-  return use_mx(d) ? hrb::mx_act_bytes(d->M, kb) : hrb::tc_act_tile_bytes(d->M, kb);
+  return use_mx(d) ? hrb::mx_act_bytes(d->wfmt, d->M, kb) : hrb::tc_act_tile_bytes(d->M, kb);
 }
 size_t tc_weight_bytes(const hrb_gemm_desc* d) {
   const uint32_t kb = blocks_of(d->K);
@@ -281,10 +279,11 @@ void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJo
   *tj = hrb::TcJob{};
   hrb::tc_fill_job(*tj, d->wfmt, d->M, d->N, kb);
   if (use_mx(d)) {
-    qj->tiles_kind = 2;
+    const bool f8 = d->wfmt == HRB_WFMT_MXFP8;
+    qj->tiles_kind = f8 ? 3 : 2;
     qj->tile_rows = hrb::mx_tokens_per_tile(d->M);
-    qj->k_steps = hrb::mx_k_steps(kb);
-    qj->cover_blocks = 8u * qj->k_steps;
+    qj->k_steps = hrb::mx_steps_of(d->wfmt, kb);
+    qj->cover_blocks = (f8 ? 4u : 8u) * qj->k_steps;
     tj->k_steps = qj->k_steps;
     tj->m_tiles = (d->M + qj->tile_rows - 1) / qj->tile_rows;
   } else {
@@ -295,8 +294,10 @@ void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJo
   }
   // Units of the encoders: (row, 256-element step) for the digit planes,
   // (row, 128 elements) for the BF16 tiles.
-  qj->units = use_mx(d) ? static_cast<uint64_t>(qj->rows) * qj->k_steps
-                        : static_cast<uint64_t>(qj->rows) * ((qj->cover_blocks + 3u) / 4u);
+  // (MXFP8's 128-element steps are encoded two per unit.)
+  qj->units = !use_mx(d) ? static_cast<uint64_t>(qj->rows) * ((qj->cover_blocks + 3u) / 4u)
+              : d->wfmt == HRB_WFMT_MXFP8 ? static_cast<uint64_t>(qj->rows) * ((qj->k_steps + 1u) / 2u)
+                                          : static_cast<uint64_t>(qj->rows) * qj->k_steps;
   tj->a_tiles = act;
   tj->w_tiles = wt;
   tj->bias = d->bias;

@@ -54,19 +54,26 @@ constexpr uint32_t kSfChunk = 512;     // 128 rows x 4 blocks
 constexpr uint32_t kWChunk = kTileW * kRowB + 2 * kSfChunk;  // 17408
 constexpr uint32_t kSmemLimit = 232448;
 
-// NT tokens per tile; WP weight planes per step (1: MXFP4 codes; 3: the E2M1
-// digit planes of W8 weights).
+// NT tokens per tile; WP weight planes per step (1: MXFP4 or MXFP8 codes;
+// 3: the E2M1 digit planes of W8 weights); KB the operand bits (4:
+// kind::mxf4 with three E2M1 activation planes and 256-element steps; 8:
+// kind::mxf8f6f4 with two E4M3 activation planes and 128-element steps).
 //   WP = 1: one ring of stages, each a weight chunk and the activation block
 //   of one K step, filled by one producer thread.
 //   WP = 3: weights and activations stream through two rings of their own,
 //   filled by two producer threads, so the weight stream (from HBM, three
 //   chunks a step) runs several steps ahead of the activation blocks (L2).
-template <uint32_t NT, uint32_t WP>
+template <uint32_t NT, uint32_t WP, uint32_t KB>
 struct MxCfg {
+  static constexpr bool kF8 = KB == 8;
   static constexpr bool kSplit = WP > 1;
   static constexpr uint32_t kPlane = NT * kRowB;
-  static constexpr uint32_t kParts = mx_parts(NT);               // 192-row MMAs per K slice
-  static constexpr uint32_t kABlock = mx_act_block_bytes(NT);
+  static constexpr uint32_t kAPlanes = kF8 ? 2u : 3u;            // activation digit planes
+  static constexpr uint32_t kPartRows = kF8 ? 2u * NT : 192u;    // stacked rows per MMA (N)
+  static constexpr uint32_t kParts = kF8 ? 1u : mx_parts(NT);     // MMAs per K slice
+  static constexpr uint32_t kABlock = kF8 ? mx8_act_block_bytes(NT) : mx_act_block_bytes(NT);
+  static constexpr uint32_t kWSf = kF8 ? 1u : 2u;                 // weight scale chunks a step
+  static constexpr uint32_t kASf = kF8 ? 2u * NT / 128u : 4u * kParts;  // activation chunks
   static constexpr uint32_t kASlots = kSplit ? (NT == 64 ? 3u : 2u) : 0u;
   static constexpr uint32_t kOffW = kASlots * kABlock;            // W ring after the A ring
   // A slot of the W ring: one weight chunk, plus the step's activation block
@@ -74,16 +81,16 @@ struct MxCfg {
   static constexpr uint32_t kWSlot = kWChunk + (kSplit ? 0u : kABlock);
   static constexpr uint32_t kWSlots = (kSmemLimit - 1024 - 512 - kOffW) / kWSlot;
   static_assert(kWSlots >= WP + 1, "weight ring");
-  // Accumulator buffers of 3 NT columns (one per stacked plane row); two for
-  // NT = 64 so one tile's epilogue overlaps the next tile's MMAs.
+  // Accumulator buffers of kAPlanes NT columns (one per stacked plane row);
+  // two for NT = 64 so one tile's epilogue overlaps the next tile's MMAs.
   static constexpr uint32_t kDBufs = NT == 64 ? 2u : 1u;
-  static constexpr uint32_t kDCols = 3 * NT;
-  // TMEM columns: accumulators, weight scales (per plane, 2 groups x 4),
-  // activation scales (per part, 2 groups x 8).
+  static constexpr uint32_t kDCols = kAPlanes * NT;
+  // TMEM columns: accumulators, weight scales (4 per chunk per plane),
+  // activation scales (4 per chunk).
   static constexpr uint32_t kColSfa = kDBufs * kDCols;
-  static constexpr uint32_t kColSfb = kColSfa + 8 * WP;
+  static constexpr uint32_t kColSfb = kColSfa + 4 * kWSf * WP;
   static constexpr uint32_t kTmemCols = 512;
-  static_assert(kColSfb + 16 * kParts <= kTmemCols, "TMEM columns");
+  static_assert(kColSfb + 4 * kASf <= kTmemCols, "TMEM columns");
   static constexpr uint32_t kOffBar = kOffW + kWSlots * kWSlot;
   static constexpr uint32_t kSmem = kOffBar + 512 + 1024;
   static_assert(kABlock % 1024 == 0 && kWSlot % 1024 == 0, "ring alignment");
@@ -103,13 +110,17 @@ __host__ __device__ inline uint32_t mx_planes_of(uint32_t wfmt) {
   return wfmt == HRB_WFMT_W8 ? 3u : 1u;
 }
 
+__host__ __device__ inline uint32_t act_block_bytes(uint32_t wfmt, uint32_t nt) {
+  return wfmt == HRB_WFMT_MXFP8 ? mx8_act_block_bytes(nt) : mx_act_block_bytes(nt);
+}
+
 __host__ __device__ inline MxTile make_tile(const TcJob& job, uint32_t nt, uint32_t local) {
   const uint32_t mt = local / job.n_tiles, n_tile = local % job.n_tiles;
   const uint32_t row0 = mt * nt, col0 = n_tile * kTileW;
   MxTile t;
   t.w = job.w_tiles +
         static_cast<size_t>(n_tile) * job.k_steps * mx_planes_of(job.wfmt) * kWChunk;
-  t.a = job.a_tiles + static_cast<size_t>(mt) * job.k_steps * mx_act_block_bytes(nt);
+  t.a = job.a_tiles + static_cast<size_t>(mt) * job.k_steps * act_block_bytes(job.wfmt, nt);
   t.c = job.c + static_cast<size_t>(row0) * job.ldc + col0;
   t.bias = job.bias != nullptr ? job.bias + col0 : nullptr;
   t.rows = job.M - row0 < nt ? job.M - row0 : nt;
@@ -153,6 +164,24 @@ __device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t a_desc, uint6
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %6, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%4], [%5], p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor of kind::mxf8f6f4 block-scaled with E4M3 A and B
+// (format 0 at [7,10) and [10,13)) and E8M0 scales (bit 23), K = 32: B scale
+// id [4,6), N >> 3 at [17,23), M >> 4 at [24,29), A scale id [29,31).
+__device__ __forceinline__ uint32_t idesc_mxf8(uint32_t m, uint32_t n, uint32_t sf_id) {
+  return (sf_id << 4) | ((n >> 3) << 17) | (1u << 23) | ((m >> 4) << 24) | (sf_id << 29);
+}
+
+__device__ __forceinline__ void mma_mxf8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale.scale_vec::1X [%0], %1, %2, %3, [%4], [%5], p;\n\t}"
       ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
       : "memory");
 }
@@ -201,9 +230,9 @@ __device__ __forceinline__ bool ring_drain(const Ring& r, uint32_t n, uint32_t* 
   return ok;
 }
 
-template <uint32_t NT, uint32_t WP>
+template <uint32_t NT, uint32_t WP, uint32_t KB>
 __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ MxParams p) {
-  using Cfg = MxCfg<NT, WP>;
+  using Cfg = MxCfg<NT, WP, KB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -314,35 +343,47 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
           const uint32_t a_planes =
               Cfg::kSplit ? smem_addr(abase + as * Cfg::kABlock)
                           : smem_addr(wbase + (nw % Cfg::kWSlots) * Cfg::kWSlot + kWChunk);
-          const uint32_t a_sf = a_planes + 3 * Cfg::kPlane;
+          const uint32_t a_sf = a_planes + Cfg::kAPlanes * Cfg::kPlane;
           uint32_t w_tile[WP];
           // Scales of this step into TMEM (ordered before the MMAs below).
 #pragma unroll
           for (uint32_t pl = 0; pl < WP; ++pl) {
             w_tile[pl] = smem_addr(wbase + ((nw + pl) % Cfg::kWSlots) * Cfg::kWSlot);
             const uint32_t w_sf = w_tile[pl] + kTileW * kRowB;
-            sf_copy(sfa + 8 * pl, desc_sf_chunk(w_sf));
-            sf_copy(sfa + 8 * pl + 4, desc_sf_chunk(w_sf + kSfChunk));
+#pragma unroll
+            for (uint32_t c = 0; c < Cfg::kWSf; ++c) {
+              sf_copy(sfa + 4 * Cfg::kWSf * pl + 4 * c, desc_sf_chunk(w_sf + c * kSfChunk));
+            }
           }
 #pragma unroll
-          for (uint32_t c = 0; c < 4 * Cfg::kParts; ++c) {
-            // chunk c = (part * 2 + group) * 2 + half -> columns 8 (part * 2 + group) + 4 half
+          for (uint32_t c = 0; c < Cfg::kASf; ++c) {
+            // E2M1: chunk c = (part * 2 + group) * 2 + half -> columns
+            // 8 (part * 2 + group) + 4 half.  E4M3: chunk c (stacked rows
+            // 128 c ..) -> columns 4 c.
             sf_copy(tmem + Cfg::kColSfb + 4 * c, desc_sf_chunk(a_sf + c * kSfChunk));
           }
 #pragma unroll
           for (uint32_t k = 0; k < 4; ++k) {
-            const uint32_t grp = k / 2, sf_id = (k % 2) * 2;
-            const uint32_t idesc = idesc_mxf4(kTileW, 192, sf_id);
+            // E2M1: MMA k covers blocks 2k, 2k+1 (group k / 2, bytes 2 (k % 2)
+            // of its columns); E4M3: block k (byte k).
+            const uint32_t grp = Cfg::kF8 ? 0u : k / 2, sf_id = Cfg::kF8 ? k : (k % 2) * 2;
+            const uint32_t idesc = Cfg::kF8 ? idesc_mxf8(kTileW, Cfg::kPartRows, sf_id)
+                                            : idesc_mxf4(kTileW, Cfg::kPartRows, sf_id);
 #pragma unroll
             for (uint32_t pl = 0; pl < WP; ++pl) {
-              const uint32_t sfa_k = (sfa + 8 * pl + 4 * grp) | (sf_id << 30);
+              const uint32_t sfa_k = (sfa + 4 * Cfg::kWSf * pl + 4 * grp) | (sf_id << 30);
 #pragma unroll
               for (uint32_t part = 0; part < Cfg::kParts; ++part) {
                 const uint32_t sfb_k =
                     (tmem + Cfg::kColSfb + 8 * (part * 2 + grp)) | (sf_id << 30);
-                mma_mxf4(d + 192 * part, desc_sw128(w_tile[pl] + 32 * k),
-                         desc_sw128(a_planes + part * 192 * kRowB + 32 * k), idesc, sfa_k,
-                         sfb_k, (i > 0 || k > 0 || pl > 0) ? 1u : 0u);
+                const uint64_t wd = desc_sw128(w_tile[pl] + 32 * k);
+                const uint64_t ad = desc_sw128(a_planes + part * Cfg::kPartRows * kRowB + 32 * k);
+                const uint32_t acc = (i > 0 || k > 0 || pl > 0) ? 1u : 0u;
+                if constexpr (Cfg::kF8) {
+                  mma_mxf8(d + Cfg::kPartRows * part, wd, ad, idesc, sfa_k, sfb_k, acc);
+                } else {
+                  mma_mxf4(d + Cfg::kPartRows * part, wd, ad, idesc, sfa_k, sfb_k, acc);
+                }
               }
             }
           }
@@ -371,27 +412,43 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
       const bool acc = (ti.steps_acc >> 31) != 0;
       const float bias = (ti.bias != nullptr && col_ok) ? ti.bias[col] : 0.0f;
       float* cbase = ti.c + col;
+      const uint32_t npeers = p.peers.count;
 #pragma unroll 1
       for (uint32_t j0 = 0; j0 < NT; j0 += 16) {
-        // The three digit-plane partial sums of tokens j0..j0+15, added
-        // smallest scale first.
+        // The digit-plane partial sums of tokens j0..j0+15, added smallest
+        // scale first.
         uint32_t v0[16], v1[16], v2[16];
         const uint32_t taddr = tmem + ((sp * 32u) << 16) + b * Cfg::kDCols + j0;
         tmem_ld16(taddr, v0);
         tmem_ld16(taddr + NT, v1);
-        tmem_ld16(taddr + 2 * NT, v2);
+        if constexpr (!Cfg::kF8) tmem_ld16(taddr + 2 * NT, v2);
         tmem_wait_ld();
+        float x[16];
 #pragma unroll
         for (uint32_t j = 0; j < 16; ++j) {
-          if (col_ok && j0 + j < ti.rows) {
-            float* dst = cbase + static_cast<size_t>(j0 + j) * ti.ldc;
-            float x = (__uint_as_float(v0[j]) + __uint_as_float(v1[j])) + __uint_as_float(v2[j]);
-            if (acc) x += *dst;
-            x += bias;
-            *dst = x;
-            // The same output into each peer's C (NVLink stores).
-            for (uint32_t q = 0; q < p.peers.count; ++q) {
-              *reinterpret_cast<float*>(reinterpret_cast<char*>(dst) + p.peers.delta[q]) = x;
+          x[j] = __uint_as_float(v0[j]) + __uint_as_float(v1[j]);
+          if constexpr (!Cfg::kF8) x[j] += __uint_as_float(v2[j]);
+        }
+        if (col_ok) {
+#pragma unroll
+          for (uint32_t j = 0; j < 16; ++j) {
+            if (j0 + j < ti.rows) {
+              float* dst = cbase + static_cast<size_t>(j0 + j) * ti.ldc;
+              if (acc) x[j] += *dst;
+              x[j] += bias;
+              *dst = x[j];
+            }
+          }
+          if (npeers != 0) {
+            // The same outputs into each peer's C (NVLink stores).
+            for (uint32_t q = 0; q < npeers; ++q) {
+              char* peer = reinterpret_cast<char*>(cbase) + p.peers.delta[q];
+#pragma unroll
+              for (uint32_t j = 0; j < 16; ++j) {
+                if (j0 + j < ti.rows) {
+                  *reinterpret_cast<float*>(peer + static_cast<size_t>(j0 + j) * ti.ldc * 4u) = x[j];
+                }
+              }
             }
           }
         }
@@ -428,12 +485,14 @@ __device__ __forceinline__ int32_t w8_digit(int32_t q, uint32_t p) {
 }
 
 // Dense weights + scales [N][kb] -> the per-(tile, step, plane) chunks of
-// the kernel: MXFP4 [N][kp/2] codes as they are (one plane), or W8 [N][kp]
-// int8 as three E2M1 digit planes with scales e - 6 + 3p.  One thread per
-// 16-byte output piece.
+// the kernel: MXFP4 [N][kp/2] codes as they are (one plane, 256-element
+// steps), W8 [N][kp] int8 as three E2M1 digit planes with scales e - 6 + 3p,
+// or MXFP8 [N][kp] E4M3 codes as they are (one plane, 128-element steps:
+// one scale chunk, then 512 bytes of padding).  One thread per 16-byte
+// output piece.
 __global__ void k_tile_weights_mxf4(const uint8_t* __restrict__ w, const uint8_t* __restrict__ ws,
                                     uint32_t N, uint32_t kb, uint32_t steps, uint32_t wp,
-                                    uint8_t* __restrict__ out) {
+                                    uint32_t f8, uint8_t* __restrict__ out) {
   const uint32_t n_tiles = (N + kTileW - 1) / kTileW;
   const uint64_t pieces = static_cast<uint64_t>(n_tiles) * steps * wp * (kWChunk / 16u);
   for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < pieces;
@@ -450,7 +509,14 @@ __global__ void k_tile_weights_mxf4(const uint8_t* __restrict__ w, const uint8_t
       const uint32_t r = piece / 8u, pc = piece % 8u, c = pc ^ (r & 7u);
       const uint32_t n = tile * kTileW + r;
       const uint32_t e0 = step * 256u + c * 32u;  // first element of the piece
-      if (wp == 1) {
+      if (f8) {
+        const size_t kp = static_cast<size_t>(kb) * 32u;
+        const size_t e8 = static_cast<size_t>(step) * 128u + c * 16u;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          v[k] = (n < N && e8 + k < kp) ? w[static_cast<size_t>(n) * kp + e8 + k] : 0;
+        }
+      } else if (wp == 1) {
         const size_t row_bytes = static_cast<size_t>(kb) * 16u;
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
@@ -482,8 +548,9 @@ __global__ void k_tile_weights_mxf4(const uint8_t* __restrict__ w, const uint8_t
       for (int k = 0; k < 16; ++k) {
         const uint32_t j = k / 4, s = k % 4;
         const uint32_t n = tile * kTileW + i32 + 32u * j;
-        const uint32_t blk = step * 8u + grp * 4u + s;
+        const uint32_t blk = f8 ? (grp == 0 ? step * 4u + s : kb) : step * 8u + grp * 4u + s;
         int32_t sc = (n < N && blk < kb) ? ws[static_cast<size_t>(n) * kb + blk] : 127;
+        if (f8 && grp != 0) sc = 0;  // padding after the one scale chunk
         if (wp == 3) sc = sc - 6 + 3 * static_cast<int32_t>(plane);
         v[k] = static_cast<uint8_t>(sc < 0 ? 0 : (sc > 254 ? 254 : sc));
       }
@@ -497,11 +564,11 @@ __global__ void k_tile_weights_mxf4(const uint8_t* __restrict__ w, const uint8_t
   }
 }
 
-template <uint32_t NT, uint32_t WP>
+template <uint32_t NT, uint32_t WP, uint32_t KB>
 int launch_mx(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, int sm_count,
               uint32_t* err, cudaStream_t s, const MxPeers* peers) {
-  using Cfg = MxCfg<NT, WP>;
-  if (!set_smem_limit_once(reinterpret_cast<const void*>(k_gemm_mxf4<NT, WP>), Cfg::kSmem)) {
+  using Cfg = MxCfg<NT, WP, KB>;
+  if (!set_smem_limit_once(reinterpret_cast<const void*>(k_gemm_mxf4<NT, WP, KB>), Cfg::kSmem)) {
     return -1;
   }
   MxParams p{};
@@ -511,9 +578,14 @@ int launch_mx(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, 
   if (peers != nullptr) p.peers = *peers;
   if (inline_job != nullptr) p.inline_job = *inline_job;
   const uint32_t grid = std::min<uint32_t>(tiles, static_cast<uint32_t>(sm_count));
-  k_gemm_mxf4<NT, WP><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(p);
+  k_gemm_mxf4<NT, WP, KB><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? 1 : -1;
 }
+
+template <uint32_t NT, uint32_t WP, uint32_t KB>
+struct Pick {
+  static constexpr uint32_t kNt = NT, kWp = WP, kKb = KB;
+};
 
 }  // namespace
 
@@ -521,14 +593,23 @@ uint32_t mx_tokens_per_tile(uint32_t M) { return M <= 64 ? 64u : 128u; }
 
 uint32_t mx_k_steps(uint32_t kb) { return (kb + 7) / 8; }
 
-size_t mx_weight_bytes(uint32_t wfmt, uint32_t N, uint32_t kb) {
-  return static_cast<size_t>((N + kTileW - 1) / kTileW) * mx_k_steps(kb) * mx_planes_of(wfmt) *
-         kWChunk;
+uint32_t mx8_k_steps(uint32_t kb) { return (kb + 3) / 4; }
+
+uint32_t mx_steps_of(uint32_t wfmt, uint32_t kb) {
+  return wfmt == HRB_WFMT_MXFP8 ? mx8_k_steps(kb) : mx_k_steps(kb);
 }
 
-size_t mx_act_bytes(uint32_t M, uint32_t kb) {
+uint32_t mx_block_bytes_of(uint32_t wfmt, uint32_t nt) { return act_block_bytes(wfmt, nt); }
+
+size_t mx_weight_bytes(uint32_t wfmt, uint32_t N, uint32_t kb) {
+  return static_cast<size_t>((N + kTileW - 1) / kTileW) * mx_steps_of(wfmt, kb) *
+         mx_planes_of(wfmt) * kWChunk;
+}
+
+size_t mx_act_bytes(uint32_t wfmt, uint32_t M, uint32_t kb) {
   const uint32_t nt = mx_tokens_per_tile(M);
-  return static_cast<size_t>((M + nt - 1) / nt) * mx_k_steps(kb) * mx_act_block_bytes(nt);
+  return static_cast<size_t>((M + nt - 1) / nt) * mx_steps_of(wfmt, kb) *
+         act_block_bytes(wfmt, nt);
 }
 
 void launch_tile_weights_mxf4(uint32_t wfmt, const uint8_t* w, const uint8_t* ws, uint32_t N,
@@ -537,7 +618,8 @@ void launch_tile_weights_mxf4(uint32_t wfmt, const uint8_t* w, const uint8_t* ws
   uint64_t grid = (pieces + 255) / 256;
   if (grid > 148u * 16u) grid = 148u * 16u;
   k_tile_weights_mxf4<<<static_cast<unsigned>(grid ? grid : 1), 256, 0, s>>>(
-      w, ws, N, kb, mx_k_steps(kb), mx_planes_of(wfmt), out);
+      w, ws, N, kb, mx_steps_of(wfmt, kb), mx_planes_of(wfmt), wfmt == HRB_WFMT_MXFP8 ? 1u : 0u,
+      out);
 }
 
 void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out) {
@@ -550,20 +632,20 @@ int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, u
   if (tiles == 0) return 0;
   if (tiles_dev == nullptr && inline_job == nullptr) return -1;
   if (peers != nullptr && peers->count > kMaxPeers) return -1;
-  const uint32_t wp = mx_planes_of(wfmt);
-  if (nt == 64 && wp == 1) {
-    return launch_mx<64, 1>(tiles_dev, inline_job, tiles, sm_count, err, s, peers);
+  const auto go = [&](auto cfg) {
+    using C = decltype(cfg);
+    return launch_mx<C::kNt, C::kWp, C::kKb>(tiles_dev, inline_job, tiles, sm_count, err, s,
+                                             peers);
+  };
+  switch (wfmt * 1000u + nt) {
+    case HRB_WFMT_MXFP4 * 1000u + 64: return go(Pick<64, 1, 4>{});
+    case HRB_WFMT_MXFP4 * 1000u + 128: return go(Pick<128, 1, 4>{});
+    case HRB_WFMT_W8 * 1000u + 64: return go(Pick<64, 3, 4>{});
+    case HRB_WFMT_W8 * 1000u + 128: return go(Pick<128, 3, 4>{});
+    case HRB_WFMT_MXFP8 * 1000u + 64: return go(Pick<64, 1, 8>{});
+    case HRB_WFMT_MXFP8 * 1000u + 128: return go(Pick<128, 1, 8>{});
+    default: return -1;
   }
-  if (nt == 128 && wp == 1) {
-    return launch_mx<128, 1>(tiles_dev, inline_job, tiles, sm_count, err, s, peers);
-  }
-  if (nt == 64 && wp == 3) {
-    return launch_mx<64, 3>(tiles_dev, inline_job, tiles, sm_count, err, s, peers);
-  }
-  if (nt == 128 && wp == 3) {
-    return launch_mx<128, 3>(tiles_dev, inline_job, tiles, sm_count, err, s, peers);
-  }
-  return -1;
 }
 
 }  // namespace hrb

@@ -28,7 +28,8 @@ struct QuantJob {
   uint32_t tile_rows, k_steps;
   // tiles_kind 1: the BF16 tiles above (64-element K steps).  tiles_kind 2:
   // the activations as three E2M1 digit planes for kind::mxf4 (see
-  // gemm_mxf4.cu), 256-element K steps, with their E8M0 scales.
+  // gemm_mxf4.cu), 256-element K steps, with their E8M0 scales.  tiles_kind
+  // 3: two E4M3 digit planes for kind::mxf8f6f4, 128-element K steps.
   uint32_t tiles_kind;
   uint32_t cover_blocks;  // K blocks written (kb plus the steps' zero padding)
 };

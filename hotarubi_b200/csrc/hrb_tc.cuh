@@ -31,10 +31,11 @@ size_t tc_weight_tile_bytes(uint32_t wfmt, uint32_t N, uint32_t kb);
 size_t tc_act_tile_bytes(uint32_t M, uint32_t kb);
 void tc_fill_job(TcJob& t, uint32_t wfmt, uint32_t M, uint32_t N, uint32_t kb);
 
-// The kind::mxf4 path (gemm_mxf4.cu) for MXFP4 weights (their own E2M1
-// codes) and W8 weights (three E2M1 digit planes): tokens per tile (64 or
-// 128), 256-element K steps, prepared operand sizes, the weight translation
-// and the launch.
+// The block-scaled tensor-core path (gemm_mxf4.cu): kind::mxf4 for MXFP4
+// weights (their own E2M1 codes) and W8 weights (three E2M1 digit planes),
+// kind::mxf8f6f4 for MXFP8 weights (their own E4M3 codes): tokens per tile
+// (64 or 128), K steps, prepared operand sizes, the weight translation and
+// the launch.
 uint32_t mx_tokens_per_tile(uint32_t M);
 uint32_t mx_k_steps(uint32_t kb);
 
@@ -57,8 +58,29 @@ __host__ __device__ inline uint32_t mx_act_sf_offset(uint32_t nt, uint32_t stack
   return 3u * nt * 128u + chunk * 512u + (r % 32u) * 16u + ((r % 128u) / 32u) * 4u +
          block_in_step % 4u;
 }
+
+// The same kernel for MXFP8 (E4M3) weights runs kind::mxf8f6f4 with
+// 128-element K steps (one 128-byte row of E4M3 per operand row).  The
+// activations are two E4M3 digit planes, q = 16 h + l with h, l in [-8, 8]
+// (integers E4M3 holds exactly), stacked as 2 nt operand rows (one MMA of
+// N = 2 nt per 32 elements of K).  Block: the 2 nt rows, then per 128
+// stacked rows one 512-byte scale chunk (the step's 4 blocks), padded to
+// 1024 bytes.
+uint32_t mx8_k_steps(uint32_t kb);
+__host__ __device__ constexpr uint32_t mx8_act_block_bytes(uint32_t nt) {
+  return 2u * nt * 128u + 1024u;
+}
+__host__ __device__ inline uint32_t mx8_act_sf_offset(uint32_t nt, uint32_t stacked_row,
+                                                      uint32_t block_in_step) {
+  return 2u * nt * 128u + (stacked_row / 128u) * 512u + (stacked_row % 32u) * 16u +
+         ((stacked_row % 128u) / 32u) * 4u + block_in_step;
+}
+// K steps and activation block bytes of a weight format on this path.
+uint32_t mx_steps_of(uint32_t wfmt, uint32_t kb);
+uint32_t mx_block_bytes_of(uint32_t wfmt, uint32_t nt);
+
 size_t mx_weight_bytes(uint32_t wfmt, uint32_t N, uint32_t kb);
-size_t mx_act_bytes(uint32_t M, uint32_t kb);
+size_t mx_act_bytes(uint32_t wfmt, uint32_t M, uint32_t kb);
 void launch_tile_weights_mxf4(uint32_t wfmt, const uint8_t* w, const uint8_t* ws, uint32_t N,
                               uint32_t kb, uint8_t* out, cudaStream_t stream);
 // One output tile of a kind::mxf4 launch with its operands located.  Plans

@@ -299,8 +299,11 @@ __device__ __forceinline__ uint32_t pack_e2m1x8(const float d[8]) {
 struct PlaneJob {
   const float* x;
   uint8_t* tiles;
-  uint32_t rows, cols, ldx, k_steps, tile_rows, vec4, vec_rule;
-  uint32_t block_bytes, plane_bytes;  // mx_act_block_bytes(tile_rows), tile_rows * 128
+  uint32_t rows, cols, ldx, tile_rows, vec4, vec_rule;
+  uint32_t f8;        // E4M3 planes (tiles_kind 3), else E2M1 planes
+  uint32_t steps;     // operand K steps per row tile (256 elements E2M1, 128 E4M3)
+  uint32_t k_steps;   // units per row: 256-element groups
+  uint32_t block_bytes, plane_bytes;  // the activation block, tile_rows * 128
   uint64_t unit_begin, units;
 };
 
@@ -311,11 +314,13 @@ __device__ __forceinline__ PlaneJob plane_job(const QuantJob& j) {
   p.rows = j.rows;
   p.cols = j.cols;
   p.ldx = j.ldx;
-  p.k_steps = j.k_steps;
+  p.f8 = j.tiles_kind == 3;
+  p.steps = j.k_steps;
+  p.k_steps = p.f8 ? (j.k_steps + 1u) / 2u : j.k_steps;
   p.tile_rows = j.tile_rows;
   p.vec4 = j.vec4;
   p.vec_rule = j.vec_rule;
-  p.block_bytes = mx_act_block_bytes(j.tile_rows);
+  p.block_bytes = p.f8 ? mx8_act_block_bytes(j.tile_rows) : mx_act_block_bytes(j.tile_rows);
   p.plane_bytes = j.tile_rows * 128u;
   p.unit_begin = j.unit_begin;
   p.units = j.units;
@@ -335,12 +340,36 @@ __device__ __forceinline__ PlaneOut plane_out(const PlaneJob& j, uint32_t row, u
   const uint32_t shift = j.tile_rows == 64 ? 6u : 7u;
   const uint32_t rt = row >> shift, r = row & (j.tile_rows - 1u);
   PlaneOut o;
-  o.blk0 = j.tiles + static_cast<size_t>(rt) * j.k_steps * j.block_bytes;
-  // Lane l's four bytes sit in logical 16-byte chunk l / 4 of the row.
-  o.off = r * 128u + (((lane >> 2) ^ (r & 7u)) << 4) + (lane & 3u) * 4u;
+  o.blk0 = j.tiles + static_cast<size_t>(rt) * j.steps * j.block_bytes;
+  if (j.f8) {
+    // E4M3: lane l's eight bytes are bytes 8 (l % 16) .. of the row of step
+    // 2 u + l / 16: logical 16-byte chunk (l % 16) / 2, half l % 2.
+    o.off = r * 128u + ((((lane & 15u) >> 1) ^ (r & 7u)) << 4) + (lane & 1u) * 8u;
 #pragma unroll
-  for (uint32_t p = 0; p < 3; ++p) o.sf[p] = mx_act_sf_offset(j.tile_rows, p * j.tile_rows + r, lane >> 2);
+    for (uint32_t p = 0; p < 2; ++p) {
+      o.sf[p] = mx8_act_sf_offset(j.tile_rows, p * j.tile_rows + r, (lane >> 2) & 3u);
+    }
+    o.sf[2] = 0;
+  } else {
+    // E2M1: lane l's four bytes sit in logical 16-byte chunk l / 4 of the row.
+    o.off = r * 128u + (((lane >> 2) ^ (r & 7u)) << 4) + (lane & 3u) * 4u;
+#pragma unroll
+    for (uint32_t p = 0; p < 3; ++p) {
+      o.sf[p] = mx_act_sf_offset(j.tile_rows, p * j.tile_rows + r, lane >> 2);
+    }
+  }
   return o;
+}
+
+__device__ __forceinline__ uint32_t pack_e4m3x4(float a0, float a1, float a2, float a3) {
+  uint32_t out;
+  asm("{\n\t.reg .b16 lo, hi;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 lo, %2, %1;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 hi, %4, %3;\n\t"
+      "mov.b32 %0, {lo, hi};\n\t}"
+      : "=r"(out)
+      : "f"(a0), "f"(a1), "f"(a2), "f"(a3));
+  return out;
 }
 
 template <bool kVec>
@@ -385,6 +414,32 @@ __device__ __forceinline__ void encode_planes(const PlaneJob& j, const PlaneOut&
     for (uint32_t i = 0; i < 8; ++i) {
       qf[i] = static_cast<float>(kVec ? quantize_vec_rule(v[i], key) : quantize_host_rule(v[i], e));
     }
+  }
+  if (j.f8) {
+    // Two E4M3 digits: h = RNE(q / 16), l = q - 16 h, both in [-8, 8].
+    float h[8], l[8];
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) {
+      h[i] = __fadd_rn(__fmaf_rn(qf[i], 0.0625f, kMagic), -kMagic);
+      l[i] = __fmaf_rn(h[i], -16.0f, qf[i]);
+    }
+    const uint32_t st = 2u * step + (lane >> 4);  // this lane's 128-element step
+    if (st < j.steps) {
+      uint8_t* blk = o.blk0 + st * j.block_bytes;
+      *reinterpret_cast<uint2*>(blk + o.off) =
+          make_uint2(pack_e4m3x4(l[0], l[1], l[2], l[3]), pack_e4m3x4(l[4], l[5], l[6], l[7]));
+      *reinterpret_cast<uint2*>(blk + j.plane_bytes + o.off) =
+          make_uint2(pack_e4m3x4(h[0], h[1], h[2], h[3]), pack_e4m3x4(h[4], h[5], h[6], h[7]));
+      if ((lane & 3u) == 0) {
+#pragma unroll
+        for (uint32_t p = 0; p < 2; ++p) {
+          int32_t se = static_cast<int32_t>(scale) - 6 + 4 * static_cast<int32_t>(p);
+          se = se > 254 ? 254 : se;  // scale >= 6 here or the block is zero
+          blk[o.sf[p]] = static_cast<uint8_t>(se < 0 ? 0 : se);
+        }
+      }
+    }
+    return;
   }
   float d0[8], d1[8], d2[8];
 #pragma unroll

@@ -162,16 +162,18 @@ def test_fast_batched_plan_of_mixed_shapes(hrb):
     plan.close()
 
 
+@pytest.mark.parametrize("wfmt", [0, 2])
 @pytest.mark.parametrize("quant", [0, 1])
 @pytest.mark.parametrize("m", [64, 70, 130])
-def test_fast_mxfp4_activation_planes_are_exact(hrb, quant, m):
-    """W = I (E2M1 code of 1.0, scale byte 127), so every output is a single
-    activation: C[r][i] = q[r][i] * 2^(e_r - 6), which the three digit-plane
-    products and their FP32 sum give exactly.  Bit-equality with the oracle's
-    MXINT8 encoding pins the plane encoder (both rounding rules, padded K
-    steps, ragged token tiles).  The one exception is the fast path's rule
-    for blocks whose scale byte is below 6 (largest magnitude under
-    2^-121): they are encoded as zero."""
+def test_fast_activation_planes_are_exact(hrb, wfmt, quant, m):
+    """W = I (the code of 1.0: E2M1 0x2 or E4M3 0x38, scale byte 127), so
+    every output is a single activation: C[r][i] = q[r][i] * 2^(e_r - 6),
+    which the digit-plane products (three E2M1 planes for MXFP4, two E4M3
+    planes for MXFP8) and their FP32 sum give exactly.  Bit-equality with the
+    oracle's MXINT8 encoding pins the plane encoder (both rounding rules,
+    padded K steps, ragged token tiles).  The one exception is the fast
+    path's rule for blocks whose scale byte is below 6 (largest magnitude
+    under 2^-121): they are encoded as zero."""
     from hotarubi_b200 import capi
     rng = np.random.default_rng(70 + m + quant)
     n = k = 544                      # kb = 17: the third 256-element step is mostly padding
@@ -181,13 +183,17 @@ def test_fast_mxfp4_activation_planes_are_exact(hrb, quant, m):
     x[:, 64:96] = 0.0                # an all-zero block
     sub = rng.random((m, k)) < 0.01  # subnormal inputs: the VEC rule reads them as zero
     x[sub] = np.float32(1e-40)
-    codes = np.zeros((n, k), np.uint8)
-    codes[np.arange(n), np.arange(n)] = 2
-    w = cpu.pack_nibbles(codes)
+    if wfmt == 0:
+        codes = np.zeros((n, k), np.uint8)
+        codes[np.arange(n), np.arange(n)] = 2
+        w = cpu.pack_nibbles(codes)
+    else:
+        w = np.zeros((n, k), np.uint8)
+        w[np.arange(n), np.arange(n)] = 0x38
     ws = np.full((n, k // 32), 127, np.uint8)
     c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
     keep = [dev(x), dev(w), dev(ws)]
-    d = capi.Library.desc(0, m, n, k, a=keep[0], w=keep[1], wscale=keep[2], c=c,
+    d = capi.Library.desc(wfmt, m, n, k, a=keep[0], w=keep[1], wscale=keep[2], c=c,
                           mode=capi.MODE_FAST, quant=quant)
     hrb.dense(d)
     hrb.sync()
@@ -202,23 +208,24 @@ def test_fast_mxfp4_activation_planes_are_exact(hrb, quant, m):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
-@pytest.mark.parametrize("wfmt", [0, 1])
+@pytest.mark.parametrize("wfmt", [0, 1, 2])
 def test_fast_weight_operands_are_exact(hrb, wfmt):
     """A = I (every block's largest value 1.0: q = 64, scale 2^0), so output
     C[r][n] is weight W[n][r] alone, which the tensor-core path must give
-    exactly: MXFP4 codes as they are, W8 as its three E2M1 digit planes with
-    scales e - 6 + 3p.  Bit-equality pins the weight translation."""
+    exactly: MXFP4 and MXFP8 codes as they are, W8 as its three E2M1 digit
+    planes with scales e - 6 + 3p.  Bit-equality pins the weight
+    translation."""
     from hotarubi_b200 import capi
     rng = np.random.default_rng(90 + wfmt)
     m = k = 288                       # kb = 9: the second 256-element step is mostly padding
     n = 200
     x = np.eye(m, k, dtype=np.float32)
     kb = k // 32
-    if wfmt == 0:
-        w, ws = weights(rng, 0, n, kb)
-    else:
+    if wfmt == 1:
         w = rng.integers(-128, 128, (n, k)).astype(np.int8).view(np.uint8)
         ws = rng.integers(100, 140, (n, kb)).astype(np.uint8)
+    else:
+        w, ws = weights(rng, wfmt, n, kb)
     c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
     keep = [dev(x), dev(w), dev(ws)]
     d = capi.Library.desc(wfmt, m, n, k, a=keep[0], w=keep[1], wscale=keep[2], c=c,
