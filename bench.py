@@ -428,8 +428,8 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
     if rank == 0:
         pk = peaks()
         fast = mode == capi.MODE_FAST
-        kname = ("k_gemm_mxf4" if wl.wfmt == 0 else "k_gemm_tc") if fast else "k_dense_exact"
-        qname = ("k_quantize_planes" if wl.wfmt == 0 else "k_quantize") if fast else "k_quantize"
+        kname = "k_gemm_mxf4" if fast else "k_dense_exact"
+        qname = "k_quantize_planes" if fast else "k_quantize"
         gemm_gbs = batch * wl.bytes_gemm() / (gemm_ms / 1e3) / 1e9
         quant_gbs = batch * wl.bytes_quant() / (quant_ms / 1e3) / 1e9
         per_gemm_traffic = traffic_from_profiles(kname, wl) if fast else None
@@ -443,8 +443,9 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
         else:
             tflops = batch * wl.flops / (gemm_ms / 1e3) / 1e12
             if wl.wfmt == 2:
-                # MXFP8 runs kind::f16 (BF16 operands): the BF16 peak.
-                peak, how = pk["bf16_tflops"], " (cuBLAS BF16)"
+                # MXFP8 runs kind::mxf8f6f4 at 2x the dense BF16 rate, with two
+                # E4M3 digit planes per exact product: the BF16 peak.
+                peak, how = pk["bf16_tflops"], " (cuBLAS BF16: FP8 MMA rate over two digit planes)"
             else:
                 # kind::mxf4 runs at 4x the dense BF16 rate (nominal 9 vs
                 # 2.25 PFLOP/s); each exact MXINT8 x E2M1 product takes three

@@ -57,7 +57,7 @@ struct hrb_plan {
   std::vector<hrb::QuantJob> d_planes_host;  // the same jobs on the host
   struct Group {
     uint32_t wfmt;
-    uint32_t kind;  // 0 exact kernel, 1 BF16 tensor-core kernel, 2 kind::mxf4 kernel
+    uint32_t kind;  // 0 exact kernel, 2 block-scaled tensor-core kernel
     uint32_t nt, njobs, tiles;
     const void* d_jobs;  // DenseJob (exact) or TcJob (tensor-core) array
     const hrb::MxTile* d_tiles;  // kind 2: the launch's output tiles
@@ -245,59 +245,46 @@ hrb_status run_dense(hrb_ctx* ctx, const hrb::DenseJob& job, cudaStream_t s) {
 }
 
 // The tensor-core path serves HRB_MODE_FAST GEMMs whose activations arrive
-// as FP32 (the encoder then writes the BF16 tiles it streams); MXINT8 input
+// as FP32 (the encoder then writes the digit planes it streams); MXINT8 input
 // runs the exact kernel, whose results are within any tolerance.
 bool use_tc(const hrb_gemm_desc* d) { return d->mode == HRB_MODE_FAST && d->a != nullptr; }
 
-// Every weight format in fast mode takes the block-scaled kernel with no
-// decode in it: MXFP4 codes and W8 (three E2M1 digit planes) on
-// kind::mxf4, MXFP8 codes on kind::mxf8f6f4.
-bool use_mx(const hrb_gemm_desc* d) { return use_tc(d); }
-
 // Tensor-core bytes of one GEMM: prepared activations then weight chunks.
 size_t tc_act_bytes(const hrb_gemm_desc* d) {
-  const uint32_t kb = blocks_of(d->K);
-  return use_mx(d) ? hrb::mx_act_bytes(d->wfmt, d->M, kb) : hrb::tc_act_tile_bytes(d->M, kb);
+  return hrb::mx_act_bytes(d->wfmt, d->M, blocks_of(d->K));
 }
 size_t tc_weight_bytes(const hrb_gemm_desc* d) {
-  const uint32_t kb = blocks_of(d->K);
-  return use_mx(d) ? hrb::mx_weight_bytes(d->wfmt, d->N, kb)
-                    : hrb::tc_weight_tile_bytes(d->wfmt, d->N, kb);
+  return hrb::mx_weight_bytes(d->wfmt, d->N, blocks_of(d->K));
 }
 size_t tc_scratch_bytes(const hrb_gemm_desc* d) {
   return align_up(tc_act_bytes(d), 1024) + align_up(tc_weight_bytes(d), 1024);
 }
 
 // Fills the encoder job and the tensor-core job of one GEMM whose prepared
-// operands live at `base` (tc_scratch_bytes of them).
+// operands live at `base` (tc_scratch_bytes of them).  Every weight format
+// takes the block-scaled kernel with no decode in it: MXFP4 codes and W8
+// (three E2M1 digit planes) on kind::mxf4, MXFP8 codes on kind::mxf8f6f4.
 void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJob* tj) {
   const uint32_t kb = blocks_of(d->K);
   uint8_t* act = base;
   uint8_t* wt = base + align_up(tc_act_bytes(d), 1024);
+  const bool f8 = d->wfmt == HRB_WFMT_MXFP8;
   *qj = make_quant_job(d->a, d->M, d->K, d->lda, d->quant, nullptr, nullptr);
   qj->tiles = act;
+  qj->tiles_kind = f8 ? 3 : 2;
+  qj->tile_rows = hrb::mx_tokens_per_tile(d->M);
+  qj->k_steps = hrb::mx_steps_of(d->wfmt, kb);
+  qj->cover_blocks = (f8 ? 4u : 8u) * qj->k_steps;
+  // Encoder units: (row, 256 elements), i.e. one E2M1 step or two E4M3 steps.
+  qj->units = static_cast<uint64_t>(qj->rows) * (f8 ? (qj->k_steps + 1u) / 2u : qj->k_steps);
   *tj = hrb::TcJob{};
-  hrb::tc_fill_job(*tj, d->wfmt, d->M, d->N, kb);
-  if (use_mx(d)) {
-    const bool f8 = d->wfmt == HRB_WFMT_MXFP8;
-    qj->tiles_kind = f8 ? 3 : 2;
-    qj->tile_rows = hrb::mx_tokens_per_tile(d->M);
-    qj->k_steps = hrb::mx_steps_of(d->wfmt, kb);
-    qj->cover_blocks = (f8 ? 4u : 8u) * qj->k_steps;
-    tj->k_steps = qj->k_steps;
-    tj->m_tiles = (d->M + qj->tile_rows - 1) / qj->tile_rows;
-  } else {
-    qj->tiles_kind = 1;
-    qj->tile_rows = hrb::tc_tokens_per_tile(d->M);
-    qj->k_steps = hrb::tc_k_steps(kb);
-    qj->cover_blocks = 2u * qj->k_steps;
-  }
-  // Units of the encoders: (row, 256-element step) for the digit planes,
-  // (row, 128 elements) for the BF16 tiles.
-  // (MXFP8's 128-element steps are encoded two per unit.)
-  qj->units = !use_mx(d) ? static_cast<uint64_t>(qj->rows) * ((qj->cover_blocks + 3u) / 4u)
-              : d->wfmt == HRB_WFMT_MXFP8 ? static_cast<uint64_t>(qj->rows) * ((qj->k_steps + 1u) / 2u)
-                                          : static_cast<uint64_t>(qj->rows) * qj->k_steps;
+  tj->wfmt = d->wfmt;
+  tj->M = d->M;
+  tj->N = d->N;
+  tj->kb = kb;
+  tj->k_steps = qj->k_steps;
+  tj->n_tiles = (d->N + 127u) / 128u;
+  tj->m_tiles = (d->M + qj->tile_rows - 1) / qj->tile_rows;
   tj->a_tiles = act;
   tj->w_tiles = wt;
   tj->bias = d->bias;
@@ -308,24 +295,8 @@ void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJo
 
 // Translates the weights of one tensor-core GEMM into the chunk layout.
 void tc_translate(const hrb_gemm_desc* d, const hrb::TcJob& tj, cudaStream_t s) {
-  const uint32_t kb = blocks_of(d->K);
-  if (use_mx(d)) {
-    hrb::launch_tile_weights_mxf4(d->wfmt, d->w, d->wscale, d->N, kb,
-                                  const_cast<uint8_t*>(tj.w_tiles), s);
-  } else {
-    hrb::launch_tile_weights(d->w, d->wscale, d->N, kb, d->wfmt, const_cast<uint8_t*>(tj.w_tiles), s);
-  }
-}
-
-// One launch of the tensor-core kernel for a group of jobs.
-int tc_launch(bool mx, const hrb::TcJob* jobs_dev, const hrb::MxTile* mx_tiles, uint32_t njobs,
-              const hrb::TcJob* inline_job, uint32_t nt, uint32_t wfmt, uint32_t tiles,
-              hrb_ctx* ctx, cudaStream_t s, const hrb::MxPeers* peers = nullptr) {
-  if (mx) {
-    return hrb::launch_mxf4(mx_tiles, inline_job, nt, wfmt, tiles, ctx->sm_count, ctx->d_error, s,
-                            peers);
-  }
-  return hrb::launch_tc_jobs(jobs_dev, njobs, inline_job, nt, wfmt, tiles, ctx->d_error, s);
+  hrb::launch_tile_weights_mxf4(d->wfmt, d->w, d->wscale, d->N, blocks_of(d->K),
+                                const_cast<uint8_t*>(tj.w_tiles), s);
 }
 
 // ABUF/WBUF/FBUF words a command touches: the circular span from `base` of
@@ -633,14 +604,10 @@ hrb_status hrb_gemm_dense(hrb_ctx* ctx, const hrb_gemm_desc* d, void* stream) {
     // Rows of the last activation tile past M stay zero.
     HRB_CUDA(ctx, cudaMemsetAsync(ctx->scratch, 0, align_up(tc_act_bytes(d), 1024), s));
     tc_translate(d, tj, s);
-    if (use_mx(d)) {
-      hrb::launch_quantize_planes(nullptr, 1, &qj, qj.units, ctx->d_error, ctx->sm_count, s);
-    } else {
-      hrb::launch_quantize(nullptr, 1, &qj, qj.units, ctx->d_error, ctx->sm_count, s);
-    }
+    hrb::launch_quantize_planes(nullptr, 1, &qj, qj.units, ctx->d_error, ctx->sm_count, s);
     tj.tile_begin = 0;
-    const int n = tc_launch(use_mx(d), nullptr, nullptr, 1, &tj, qj.tile_rows, d->wfmt,
-                            tj.m_tiles * tj.n_tiles, ctx, s);
+    const int n = hrb::launch_mxf4(nullptr, &tj, qj.tile_rows, d->wfmt, tj.m_tiles * tj.n_tiles,
+                                   ctx->sm_count, ctx->d_error, s);
     if (n < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
     ctx->launches += 2u + static_cast<uint64_t>(n);
     HRB_CUDA(ctx, cudaGetLastError());
@@ -793,17 +760,11 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
       tc_jobs(&d, sbase + soff, &qj, &tj);
       soff += tc_scratch_bytes(&d);
       tc_translate(&d, tj, ctx->stream);
-      if (use_mx(&d)) {
-        qj.unit_begin = plan->plane_units;
-        plan->plane_units += qj.units;
-        planes.push_back(qj);
-      } else {
-        qj.unit_begin = plan->quant_units;
-        plan->quant_units += qj.units;
-        quant.push_back(qj);
-      }
+      qj.unit_begin = plan->plane_units;
+      plan->plane_units += qj.units;
+      planes.push_back(qj);
       size_t g = 0;
-      const uint32_t kind = use_mx(&d) ? 2u : 1u;
+      const uint32_t kind = 2u;
       while (g < tc_keys.size() && !(tc_keys[g].nt == qj.tile_rows && tc_keys[g].wfmt == d.wfmt &&
                                      tc_keys[g].kind == kind)) {
         ++g;
@@ -915,7 +876,7 @@ namespace {
 
 // Launches every kernel of a plan on s; when `events` is given, records
 // events[i] before launch i and events[n] after the last.
-// Launch steps of a plan: the encoders (FP32 -> MXINT8 / BF16 tiles, then
+// Launch steps of a plan: the encoders (FP32 -> MXINT8 codes, then
 // FP32 -> digit planes), then one GEMM launch per group.
 uint32_t plan_steps(const hrb_plan* plan) {
   return (plan->nquant > 0 ? 1u : 0u) + (plan->nplanes > 0 ? 1u : 0u) +
@@ -945,8 +906,8 @@ hrb_status plan_launch(hrb_plan* plan, cudaStream_t s, int64_t only, uint32_t* l
       n += static_cast<uint32_t>(hrb::launch_dense_exact(
           static_cast<const hrb::DenseJob*>(g.d_jobs), g.njobs, nullptr, g.tiles, g.wfmt, s));
     } else {
-      const int k = tc_launch(g.kind == 2, static_cast<const hrb::TcJob*>(g.d_jobs), g.d_tiles,
-                              g.njobs, nullptr, g.nt, g.wfmt, g.tiles, ctx, s, &plan->peers);
+      const int k = hrb::launch_mxf4(g.d_tiles, nullptr, g.nt, g.wfmt, g.tiles, ctx->sm_count,
+                                     ctx->d_error, s, &plan->peers);
       if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
       n += static_cast<uint32_t>(k);
     }

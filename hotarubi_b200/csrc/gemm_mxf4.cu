@@ -38,6 +38,9 @@
 // the next tile's MMAs).  Every wait is bounded.
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
+#include <tuple>
+#include <vector>
 
 #include "hrb_kernels.cuh"
 #include "hrb_tc.cuh"
@@ -588,6 +591,25 @@ struct Pick {
 };
 
 }  // namespace
+
+bool set_smem_limit_once(const void* kernel, uint32_t bytes) {
+  // The limit is a per-(kernel, device) attribute; the host call is not free
+  // (it would sit between back-to-back launches), so it is made once.
+  static std::mutex mu;
+  static std::vector<std::tuple<const void*, int, uint32_t>> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& d : done) {
+    if (std::get<0>(d) == kernel && std::get<1>(d) == dev && std::get<2>(d) >= bytes) return true;
+  }
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(bytes)) != cudaSuccess) {
+    return false;
+  }
+  done.emplace_back(kernel, dev, bytes);
+  return true;
+}
 
 uint32_t mx_tokens_per_tile(uint32_t M) { return M <= 64 ? 64u : 128u; }
 

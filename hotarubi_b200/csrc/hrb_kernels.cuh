@@ -16,20 +16,18 @@ struct QuantJob {
   const float* x;
   int8_t* q;          // [rows][kb * 32], or null
   uint8_t* scale;     // [rows][kb], or null
-  // Optional second output for the tensor-core path: the exact values
-  // q * 2^(e - 133) as BF16 tiles of tile_rows rows x 64 K, each row 128
-  // bytes in the 128-byte swizzle: [row tiles][k_steps][tile_rows][128 B].
+  // The tensor-core operands (launch_quantize_planes): the activations as
+  // digit planes with their E8M0 scales in the activation blocks of
+  // hrb_tc.cuh, [row tiles of tile_rows][k_steps][block].  tiles_kind 2:
+  // three E2M1 planes, 256-element K steps (kind::mxf4); tiles_kind 3: two
+  // E4M3 planes, 128-element K steps (kind::mxf8f6f4).
   uint8_t* tiles;
   uint64_t unit_begin;
-  uint64_t units;     // rows * ceil(cover_blocks / 4); planes: rows * k_steps
+  uint64_t units;     // rows * ceil(kb / 4); planes: rows * 256-element groups
   uint32_t rows, cols, ldx, kb;
   uint32_t vec_rule;  // 0: EncodeMxint8, 1: VEC 'q' pass
   uint32_t vec4;      // x rows are 16-byte aligned: load float4
   uint32_t tile_rows, k_steps;
-  // tiles_kind 1: the BF16 tiles above (64-element K steps).  tiles_kind 2:
-  // the activations as three E2M1 digit planes for kind::mxf4 (see
-  // gemm_mxf4.cu), 256-element K steps, with their E8M0 scales.  tiles_kind
-  // 3: two E4M3 digit planes for kind::mxf8f6f4, 128-element K steps.
   uint32_t tiles_kind;
   uint32_t cover_blocks;  // K blocks written (kb plus the steps' zero padding)
 };

@@ -10,8 +10,8 @@
 
 namespace hrb {
 
-// One GEMM for the tensor-core kernel.  Operands are the prepared tiles of
-// gemm_tc.cu: activations as swizzled BF16 tiles, weights as raw chunks.
+// One GEMM for the block-scaled tensor-core kernel (gemm_mxf4.cu), with its
+// prepared operands: activation digit planes and translated weight chunks.
 struct TcJob {
   const uint8_t* a_tiles;  // [m_tiles][k_steps][NT rows][128 B]
   const uint8_t* w_tiles;  // [n_tiles][k_steps][chunk]
@@ -23,13 +23,6 @@ struct TcJob {
   uint32_t m_tiles, n_tiles, k_steps;
   uint32_t tile_begin;     // prefix over the jobs of one launch
 };
-
-// Token rows per activation tile for a GEMM of M tokens (64, 128 or 256).
-uint32_t tc_tokens_per_tile(uint32_t M);
-uint32_t tc_k_steps(uint32_t kb);
-size_t tc_weight_tile_bytes(uint32_t wfmt, uint32_t N, uint32_t kb);
-size_t tc_act_tile_bytes(uint32_t M, uint32_t kb);
-void tc_fill_job(TcJob& t, uint32_t wfmt, uint32_t M, uint32_t N, uint32_t kb);
 
 // The block-scaled tensor-core path (gemm_mxf4.cu): kind::mxf4 for MXFP4
 // weights (their own E2M1 codes) and W8 weights (three E2M1 digit planes),
@@ -115,16 +108,5 @@ int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, u
 // Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current
 // device, once per (kernel, device).
 bool set_smem_limit_once(const void* kernel, uint32_t bytes);
-
-// Dense weights -> the chunk layout the kernel streams.
-void launch_tile_weights(const uint8_t* w, const uint8_t* ws, uint32_t N, uint32_t kb,
-                         uint32_t wfmt, uint8_t* out, cudaStream_t stream);
-
-// One launch over `njobs` device-resident jobs (or, with jobs_dev null, the
-// single *inline_job passed as a kernel parameter) with the same
-// tokens-per-tile `nt` and weight format; `tiles` is the total CTA count.
-// Returns the number of kernels launched or -1.
-int launch_tc_jobs(const TcJob* jobs_dev, uint32_t njobs, const TcJob* inline_job, uint32_t nt,
-                   uint32_t wfmt, uint32_t tiles, uint32_t* err, cudaStream_t stream);
 
 }  // namespace hrb

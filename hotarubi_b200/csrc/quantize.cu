@@ -61,36 +61,6 @@ __device__ __forceinline__ int32_t quantize_vec_rule(uint32_t bits, uint32_t ema
   return mag >= 128u ? 127 : static_cast<int32_t>(mag);
 }
 
-// BF16 bits of q * 2^(scale - 133), exact: |q| <= 128 has at most 8
-// significant bits.  Values below the normal range read as 0.
-__device__ __forceinline__ uint32_t bf16_of(int32_t q, uint32_t scale) {
-  if (q == 0) return 0u;
-  const uint32_t m = static_cast<uint32_t>(q < 0 ? -q : q);
-  const int32_t msb = 31 - __clz(m);
-  const int32_t field = msb + static_cast<int32_t>(scale) - 6;
-  if (field <= 0) return 0u;
-  if (field >= 255) return (q < 0 ? 0x8000u : 0u) | 0x7F80u;
-  const uint32_t mant = (m << (7 - msb)) & 0x7Fu;
-  return (q < 0 ? 0x8000u : 0u) | (static_cast<uint32_t>(field) << 7) | mant;
-}
-
-__device__ __forceinline__ uint32_t bf16_pair(int32_t lo, int32_t hi, uint32_t scale) {
-  return bf16_of(lo, scale) | (bf16_of(hi, scale) << 16);
-}
-
-// Four BF16 (elements col0..col0+3 of `row`) into the swizzled tile layout:
-// tile (row / tile_rows, col0 / 64), row r = row % tile_rows, 16-byte chunk c
-// of the 128-byte row stored at chunk c ^ (r % 8).
-__device__ __forceinline__ void write_tile(const QuantJob& job, uint32_t row, uint32_t col0,
-                                           uint32_t w0, uint32_t w1) {
-  const uint32_t rt = row / job.tile_rows, r = row % job.tile_rows;
-  const uint32_t step = col0 / 64u, within = col0 % 64u;
-  const uint32_t c = within / 8u, half = (within % 8u) / 4u;
-  const size_t tile = static_cast<size_t>(rt) * job.k_steps + step;
-  uint8_t* dst = job.tiles + tile * job.tile_rows * 128u + r * 128u + ((c ^ (r & 7u)) << 4) + half * 8u;
-  *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);
-}
-
 // One unit of work: 128 consecutive elements (four blocks) of one row.
 struct Unit {
   const QuantJob* job;
@@ -166,12 +136,7 @@ __device__ __forceinline__ void finish_unit(const Unit& t, const uint32_t v[4], 
   key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 4));
   if (!vec_rule && __any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(error_flag, 1u);
   const uint32_t block = t.chunk * 4u + (lane >> 3);
-  if (block >= job.kb) {
-    // The tensor-core operands run K in whole steps: blocks past kb up to
-    // the step boundary are zero padding.
-    if (job.tiles != nullptr && block < job.cover_blocks) write_tile(job, t.row, t.col0, 0u, 0u);
-    return;
-  }
+  if (block >= job.kb) return;  // past the last block of the row
   int32_t q[4];
   uint32_t scale;
   quantize4(v, key, vec_rule, q, scale);
@@ -184,9 +149,7 @@ __device__ __forceinline__ void finish_unit(const Unit& t, const uint32_t v[4], 
     *reinterpret_cast<uint32_t*>(job.q + static_cast<size_t>(t.row) * kp + t.col0) = packed;
     if ((lane & 7u) == 0) job.scale[static_cast<size_t>(t.row) * job.kb + block] = static_cast<uint8_t>(scale);
   }
-  if (job.tiles != nullptr) {
-    write_tile(job, t.row, t.col0, bf16_pair(q[0], q[1], scale), bf16_pair(q[2], q[3], scale));
-  }
+
 }
 
 // Each warp walks a contiguous range of units, so the job a unit belongs to
