@@ -55,6 +55,7 @@ class GemmDesc(ctypes.Structure):
         ("bias", ctypes.c_void_p), ("c", ctypes.c_void_p), ("ldc", ctypes.c_uint32),
         ("accumulate", ctypes.c_uint32),
         ("pieces", ctypes.c_void_p), ("npieces", ctypes.c_uint32),
+        ("cq", ctypes.c_void_p), ("cscale", ctypes.c_void_p), ("cquant", ctypes.c_uint32),
     ]
 
 
@@ -235,7 +236,7 @@ class Library:
     @staticmethod
     def desc(wfmt, M, N, K, *, a=None, lda=None, quant=QUANT_HOST, aq=None, ascale=None,
              w=None, wscale=None, bias=None, c=None, ldc=None, accumulate=False,
-             pieces=None, mode=MODE_EXACT):
+             pieces=None, mode=MODE_EXACT, cq=None, cscale=None, cquant=QUANT_VEC):
         d = GemmDesc()
         d.wfmt, d.mode, d.M, d.N, d.K = wfmt, mode, M, N, K
         d.a = _ptr(a)
@@ -247,6 +248,7 @@ class Library:
         d.c = _ptr(c)
         d.ldc = ldc if ldc is not None else N
         d.accumulate = 1 if accumulate else 0
+        d.cq, d.cscale, d.cquant = _ptr(cq), _ptr(cscale), cquant
         if pieces is not None:
             arr = np.ascontiguousarray(pieces, dtype=np.uint32)
             d._pieces_keep = arr  # keep alive

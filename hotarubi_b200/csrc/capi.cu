@@ -55,6 +55,10 @@ struct hrb_plan {
   uint64_t plane_units = 0;
   const hrb::QuantJob* d_planes = nullptr;
   std::vector<hrb::QuantJob> d_planes_host;  // the same jobs on the host
+  // MXINT8 copies of the exact GEMMs' outputs, encoded after them.
+  uint32_t npost = 0;
+  uint64_t post_units = 0;
+  const hrb::QuantJob* d_post = nullptr;
   struct Group {
     uint32_t wfmt;
     uint32_t kind;  // 0 exact kernel, 2 block-scaled tensor-core kernel
@@ -162,11 +166,26 @@ hrb_status check_desc(hrb_ctx* ctx, const hrb_gemm_desc* d, uint32_t* pieces,
     }
     if (!aligned(d->aq, 16)) return fail(ctx, HRB_EINVAL, "MXINT8 activations are not 16-byte aligned");
   }
-  if (d->w == nullptr || d->wscale == nullptr || d->c == nullptr) {
-    return fail(ctx, HRB_EINVAL, "missing weights, weight scales or output");
+  if (d->w == nullptr || d->wscale == nullptr) {
+    return fail(ctx, HRB_EINVAL, "missing weights or weight scales");
+  }
+  if ((d->cq == nullptr) != (d->cscale == nullptr)) {
+    return fail(ctx, HRB_EINVAL, "give both MXINT8 output codes and scales, or neither");
+  }
+  if (d->cq != nullptr && d->cquant > HRB_QUANT_VEC) {
+    return fail(ctx, HRB_EINVAL, "unknown output quantizer %u", d->cquant);
+  }
+  if (d->c == nullptr) {
+    // Only the fused re-quantisation may stand in for the FP32 output.
+    if (d->cq == nullptr || d->mode != HRB_MODE_FAST || d->a == nullptr || d->accumulate) {
+      return fail(ctx, HRB_EINVAL, "missing output (an MXINT8-only output needs HRB_MODE_FAST, "
+                                   "FP32 activations and no accumulate)");
+    }
   }
   if (!aligned(d->w, 16)) return fail(ctx, HRB_EINVAL, "weights are not 16-byte aligned");
-  if (d->ldc < d->N) return fail(ctx, HRB_EINVAL, "ldc %u < N %u", d->ldc, d->N);
+  if (d->c != nullptr && d->ldc < d->N) {
+    return fail(ctx, HRB_EINVAL, "ldc %u < N %u", d->ldc, d->N);
+  }
   if (d->pieces == nullptr || d->npieces == 0) {
     pieces[0] = kb;
     *npieces = 1;
@@ -231,6 +250,12 @@ size_t act_scratch_bytes(uint32_t M, uint32_t K) {
   return align_up(size_t{M} * kb * 32u, 256) + align_up(size_t{M} * kb, 256);
 }
 
+// The MXINT8 copy of C for GEMMs that do not take the tensor-core path (its
+// epilogue makes the copy itself): the encoder over C, after the GEMM.
+hrb::QuantJob post_quant_job(const hrb_gemm_desc* d) {
+  return make_quant_job(d->c, d->M, d->N, d->ldc, d->cquant, d->cq, d->cscale);
+}
+
 // The exact GEMM, once activations are MXINT8 on the device.
 hrb_status run_dense(hrb_ctx* ctx, const hrb::DenseJob& job, cudaStream_t s) {
   hrb::DenseJob one = job;
@@ -291,6 +316,9 @@ void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJo
   tj->c = d->c;
   tj->ldc = d->ldc;
   tj->accumulate = d->accumulate != 0;
+  tj->cq = d->cq;
+  tj->cscale = d->cscale;
+  tj->cquant = d->cquant;
 }
 
 // Translates the weights of one tensor-core GEMM into the chunk layout.
@@ -342,6 +370,8 @@ hrb_status check_desc_for_noalloc(const hrb_gemm_desc* desc, uint32_t* pieces,
 QuantJob make_quant_job_for_noalloc(const hrb_gemm_desc* d, int8_t* q, uint8_t* scale) {
   return make_quant_job(d->a, d->M, d->K, d->lda, d->quant, q, scale);
 }
+
+QuantJob make_post_quant_job_for_noalloc(const hrb_gemm_desc* d) { return post_quant_job(d); }
 
 DenseJob make_dense_job_for_noalloc(const hrb_gemm_desc* d, const int8_t* aq,
                                     const uint8_t* ascale, const uint32_t* pieces,
@@ -627,7 +657,13 @@ hrb_status hrb_gemm_dense(hrb_ctx* ctx, const hrb_gemm_desc* d, void* stream) {
     aq = q;
     ascale = sc;
   }
-  return run_dense(ctx, make_dense_job(d, aq, ascale, pieces, npieces), s);
+  st = run_dense(ctx, make_dense_job(d, aq, ascale, pieces, npieces), s);
+  if (st != HRB_OK || d->cq == nullptr) return st;
+  const hrb::QuantJob pq = post_quant_job(d);
+  hrb::launch_quantize(nullptr, 1, &pq, pq.units, ctx->d_error, ctx->sm_count, s);
+  ctx->launches += 1;
+  HRB_CUDA(ctx, cudaGetLastError());
+  return HRB_OK;
 }
 
 hrb_status hrb_gemm_dense_host(hrb_ctx* ctx, const hrb_gemm_desc* d) {
@@ -646,7 +682,10 @@ hrb_status hrb_gemm_dense_host(hrb_ctx* ctx, const hrb_gemm_desc* d) {
   const size_t w_bytes = size_t{d->N} * weight_row_bytes(d->wfmt, kb);
   const size_t ws_bytes = size_t{d->N} * kb;
   const size_t b_bytes = d->bias ? size_t{d->N} * 4u : 0;
-  const size_t c_bytes = size_t{d->M} * d->N * 4u;
+  const size_t c_bytes = d->c ? size_t{d->M} * d->N * 4u : 0;
+  const uint32_t kbq = blocks_of(d->N);
+  const size_t q_bytes = d->cq ? size_t{d->M} * kbq * 32u : 0;
+  const size_t qs_bytes = d->cq ? size_t{d->M} * kbq : 0;
   size_t off = 0;
   const size_t o_a = off; off = align_up(off + a_bytes, 256);
   const size_t o_as = off; off = align_up(off + as_bytes, 256);
@@ -654,6 +693,8 @@ hrb_status hrb_gemm_dense_host(hrb_ctx* ctx, const hrb_gemm_desc* d) {
   const size_t o_ws = off; off = align_up(off + ws_bytes, 256);
   const size_t o_b = off; off = align_up(off + b_bytes, 256);
   const size_t o_c = off; off = align_up(off + c_bytes, 256);
+  const size_t o_q = off; off = align_up(off + q_bytes, 256);
+  const size_t o_qs = off; off = align_up(off + qs_bytes, 256);
   st = grow(ctx, &ctx->staging, &ctx->staging_bytes, off);
   if (st != HRB_OK) return st;
   auto* base = static_cast<uint8_t*>(ctx->staging);
@@ -678,16 +719,26 @@ hrb_status hrb_gemm_dense_host(hrb_ctx* ctx, const hrb_gemm_desc* d) {
     HRB_CUDA(ctx, cudaMemcpyAsync(base + o_b, d->bias, b_bytes, cudaMemcpyHostToDevice, s));
     dd.bias = reinterpret_cast<const float*>(base + o_b);
   }
-  dd.c = reinterpret_cast<float*>(base + o_c);
+  dd.c = d->c ? reinterpret_cast<float*>(base + o_c) : nullptr;
   dd.ldc = d->N;
   if (d->accumulate) {
     HRB_CUDA(ctx, cudaMemcpy2DAsync(dd.c, size_t{d->N} * 4u, d->c, size_t{d->ldc} * 4u,
                                     size_t{d->N} * 4u, d->M, cudaMemcpyHostToDevice, s));
   }
+  if (d->cq) {
+    dd.cq = reinterpret_cast<int8_t*>(base + o_q);
+    dd.cscale = base + o_qs;
+  }
   st = hrb_gemm_dense(ctx, &dd, s);
   if (st != HRB_OK) return st;
-  HRB_CUDA(ctx, cudaMemcpy2DAsync(d->c, size_t{d->ldc} * 4u, dd.c, size_t{d->N} * 4u,
-                                  size_t{d->N} * 4u, d->M, cudaMemcpyDeviceToHost, s));
+  if (d->c) {
+    HRB_CUDA(ctx, cudaMemcpy2DAsync(d->c, size_t{d->ldc} * 4u, dd.c, size_t{d->N} * 4u,
+                                    size_t{d->N} * 4u, d->M, cudaMemcpyDeviceToHost, s));
+  }
+  if (d->cq) {
+    HRB_CUDA(ctx, cudaMemcpyAsync(d->cq, dd.cq, q_bytes, cudaMemcpyDeviceToHost, s));
+    HRB_CUDA(ctx, cudaMemcpyAsync(d->cscale, dd.cscale, qs_bytes, cudaMemcpyDeviceToHost, s));
+  }
   return hrb_sync(ctx);
 }
 
@@ -743,7 +794,7 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
   }
   // Encoder jobs, exact-kernel jobs per format, tensor-core jobs per
   // (tokens per tile, format).  Tensor-core weights are translated now, once.
-  std::vector<hrb::QuantJob> quant, planes;
+  std::vector<hrb::QuantJob> quant, planes, post;
   std::vector<std::vector<hrb::DenseJob>> exact(3);
   uint32_t exact_tiles[3] = {0, 0, 0};
   struct TcKey { uint32_t nt, wfmt, kind; };
@@ -795,6 +846,12 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
       aq = q;
       as = sc;
     }
+    if (d.cq != nullptr) {
+      hrb::QuantJob pq = post_quant_job(&d);
+      pq.unit_begin = plan->post_units;
+      plan->post_units += pq.units;
+      post.push_back(pq);
+    }
     hrb::DenseJob j = make_dense_job(&d, aq, as, pieces[i].data(), npieces[i]);
     uint32_t tiles_n = 0;
     const uint32_t tiles = hrb::dense_exact_tiles(j.M, j.N, tiles_n);
@@ -803,7 +860,7 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
     exact_tiles[j.wfmt] += tiles;
     exact[j.wfmt].push_back(j);
   }
-  size_t bytes = (quant.size() + planes.size()) * sizeof(hrb::QuantJob);
+  size_t bytes = (quant.size() + planes.size() + post.size()) * sizeof(hrb::QuantJob);
   for (auto& g : exact) bytes += g.size() * sizeof(hrb::DenseJob);
   for (auto& g : tc_groups) bytes += g.size() * sizeof(hrb::TcJob);
   // kind::mxf4 groups also get their output tiles located on the host.
@@ -838,6 +895,13 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
     plan->nplanes = static_cast<uint32_t>(planes.size());
     plan->d_planes_host = planes;
     dst += planes.size() * sizeof(hrb::QuantJob);
+  }
+  if (!post.empty()) {
+    HRB_CUDA(ctx, cudaMemcpy(dst, post.data(), post.size() * sizeof(hrb::QuantJob),
+                             cudaMemcpyHostToDevice));
+    plan->d_post = reinterpret_cast<const hrb::QuantJob*>(dst);
+    plan->npost = static_cast<uint32_t>(post.size());
+    dst += post.size() * sizeof(hrb::QuantJob);
   }
   for (uint32_t f = 0; f < 3; ++f) {
     auto& g = exact[f];
@@ -880,7 +944,7 @@ namespace {
 // FP32 -> digit planes), then one GEMM launch per group.
 uint32_t plan_steps(const hrb_plan* plan) {
   return (plan->nquant > 0 ? 1u : 0u) + (plan->nplanes > 0 ? 1u : 0u) +
-         static_cast<uint32_t>(plan->groups.size());
+         static_cast<uint32_t>(plan->groups.size()) + (plan->npost > 0 ? 1u : 0u);
 }
 
 // Launches step `only` of a plan on s, or every step in order when `only`
@@ -911,6 +975,11 @@ hrb_status plan_launch(hrb_plan* plan, cudaStream_t s, int64_t only, uint32_t* l
       if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
       n += static_cast<uint32_t>(k);
     }
+  }
+  if (plan->npost > 0 && take()) {
+    hrb::launch_quantize(plan->d_post, plan->npost, nullptr, plan->post_units, ctx->d_error,
+                         ctx->sm_count, s);
+    ++n;
   }
   ctx->launches += n;
   *launched += n;
@@ -994,7 +1063,7 @@ hrb_status hrb_plan_run_host(hrb_plan* plan, void* stream, const void* const* a_
     return HRB_OK;
   };
   const bool pipelined = plan->nquant == 0 && plan->nplanes == n && plan->groups.size() == 1 &&
-                         plan->groups[0].kind == 2 && n >= 8;
+                         plan->groups[0].kind == 2 && plan->npost == 0 && n >= 8;
   if (!pipelined) {
     hrb_status st = copy_in(0, n, s);
     if (st != HRB_OK) return st;

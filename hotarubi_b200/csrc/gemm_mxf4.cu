@@ -43,6 +43,7 @@
 #include <vector>
 
 #include "hrb_kernels.cuh"
+#include "hrb_quant.cuh"
 #include "hrb_tc.cuh"
 #include "sm100.cuh"
 
@@ -124,31 +125,38 @@ __host__ __device__ inline MxTile make_tile(const TcJob& job, uint32_t nt, uint3
   t.w = job.w_tiles +
         static_cast<size_t>(n_tile) * job.k_steps * mx_planes_of(job.wfmt) * kWChunk;
   t.a = job.a_tiles + static_cast<size_t>(mt) * job.k_steps * act_block_bytes(job.wfmt, nt);
-  t.c = job.c + static_cast<size_t>(row0) * job.ldc + col0;
+  t.c = job.c != nullptr ? job.c + static_cast<size_t>(row0) * job.ldc + col0 : nullptr;
   t.bias = job.bias != nullptr ? job.bias + col0 : nullptr;
+  const uint32_t kbq = (job.N + 31u) / 32u;  // blocks per row of the MXINT8 copy
+  t.cq = job.cq != nullptr ? job.cq + static_cast<size_t>(row0) * kbq * 32u + col0 : nullptr;
+  t.cscale = job.cq != nullptr ? job.cscale + static_cast<size_t>(row0) * kbq + col0 / 32u
+                               : nullptr;
   t.rows = job.M - row0 < nt ? job.M - row0 : nt;
-  t.cols = job.N - col0 < kTileW ? job.N - col0 : kTileW;
+  t.cols_kbq = (job.N - col0 < kTileW ? job.N - col0 : kTileW) | (kbq << 8);
   t.ldc = job.ldc;
-  t.steps_acc = job.k_steps | (job.accumulate ? 0x80000000u : 0u);
+  t.flags = job.k_steps | (job.cquant == HRB_QUANT_VEC ? 0x40000000u : 0u) |
+            (job.accumulate ? 0x80000000u : 0u);
   return t;
 }
 
 template <uint32_t NT>
 __device__ __forceinline__ MxTile tile_info(const MxParams& p, uint32_t tile) {
   if (p.tiles == nullptr) return make_tile(p.inline_job, NT, tile);
-  // Three independent 16-byte loads; nothing consumes them until the tile
+  // Four independent 16-byte loads; nothing consumes them until the tile
   // is reached.
   const uint4* src = reinterpret_cast<const uint4*>(p.tiles + tile);
-  const uint4 x = __ldg(src), y = __ldg(src + 1), z = __ldg(src + 2);
+  const uint4 x = __ldg(src), y = __ldg(src + 1), z = __ldg(src + 2), u = __ldg(src + 3);
   MxTile t;
   t.w = reinterpret_cast<const uint8_t*>((static_cast<uint64_t>(x.y) << 32) | x.x);
   t.a = reinterpret_cast<const uint8_t*>((static_cast<uint64_t>(x.w) << 32) | x.z);
   t.c = reinterpret_cast<float*>((static_cast<uint64_t>(y.y) << 32) | y.x);
   t.bias = reinterpret_cast<const float*>((static_cast<uint64_t>(y.w) << 32) | y.z);
-  t.rows = z.x;
-  t.cols = z.y;
-  t.ldc = z.z;
-  t.steps_acc = z.w;
+  t.cq = reinterpret_cast<int8_t*>((static_cast<uint64_t>(z.y) << 32) | z.x);
+  t.cscale = reinterpret_cast<uint8_t*>((static_cast<uint64_t>(z.w) << 32) | z.z);
+  t.rows = u.x;
+  t.cols_kbq = u.y;
+  t.ldc = u.z;
+  t.flags = u.w;
   return t;
 }
 
@@ -204,6 +212,31 @@ __device__ __forceinline__ uint64_t desc_sf_chunk(uint32_t smem_byte_addr) {
 __device__ __forceinline__ void sf_copy(uint32_t taddr, uint64_t desc) {
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc)
                : "memory");
+}
+
+// The MXINT8 copy of rows j0 .. j0 + 15 of this warp's output block (32
+// columns, one per lane; columns past N count as zero): the block's key is a
+// warp max, each lane encodes its element (QuantizeBlock / EncodeMxint8 rules,
+// hrb_quant.cuh).  Non-finite values under the host rule set error bit 1.
+__device__ __forceinline__ void requant_rows(const MxTile& ti, const float (&x)[16], uint32_t j0,
+                                             uint32_t sp, uint32_t lane, bool col_ok,
+                                             uint32_t kbq, uint32_t* err) {
+  const bool vec = ((ti.flags >> 30) & 1u) != 0;
+  bool bad = false;
+#pragma unroll
+  for (uint32_t j = 0; j < 16; ++j) {
+    if (j0 + j >= ti.rows) break;  // the same for the whole warp
+    const uint32_t bits = col_ok ? __float_as_uint(x[j]) : 0u;
+    const uint32_t mag = bits & 0x7FFFFFFFu;
+    const uint32_t key = __reduce_max_sync(0xFFFFFFFFu, vec ? (mag >> 23) : mag);
+    bad |= !vec && key >= 0x7F800000u;
+    uint32_t scale;
+    const int32_t q = mxint8_code(bits, key, vec, scale);
+    const size_t row = j0 + j;
+    ti.cq[row * kbq * 32u + sp * 32u + lane] = static_cast<int8_t>(q);
+    if (lane == 0) ti.cscale[row * kbq + sp] = static_cast<uint8_t>(scale);
+  }
+  if (bad && lane == 0) atomicOr(err, 1u);
 }
 
 // A ring of `slots` buffers with full/empty mbarriers, walked by a running
@@ -288,7 +321,7 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
       for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
         const MxTile ti = next;
         if (tile + gridDim.x < p.total_tiles) next = tile_info<NT>(p, tile + gridDim.x);
-        const uint32_t k_steps = ti.steps_acc & 0x7FFFFFFFu;
+        const uint32_t k_steps = (ti.flags & 0x3FFFFFFFu);
         if (weights) {
           for (uint32_t c = 0; c < k_steps * WP && ok; ++c, ++n) {
             const uint32_t sl = n % ring.slots;
@@ -319,11 +352,11 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
     if (lane == 0) {
       uint32_t na = 0, nw = 0, t = 0;
       const uint32_t sfa = tmem + Cfg::kColSfa;
-      uint32_t next_steps = tile_info<NT>(p, blockIdx.x).steps_acc & 0x7FFFFFFFu;
+      uint32_t next_steps = tile_info<NT>(p, blockIdx.x).flags & 0x3FFFFFFFu;
       for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++t) {
         const uint32_t k_steps = next_steps;
         if (tile + gridDim.x < p.total_tiles) {
-          next_steps = tile_info<NT>(p, tile + gridDim.x).steps_acc & 0x7FFFFFFFu;
+          next_steps = tile_info<NT>(p, tile + gridDim.x).flags & 0x3FFFFFFFu;
         }
         const uint32_t b = t % Cfg::kDBufs;
         if (t >= Cfg::kDBufs) ok = mbar_wait(&acc_empty[b], ((t / Cfg::kDBufs) - 1) & 1u, p.err);
@@ -411,11 +444,16 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
       if (!ok) break;
       tc_fence_after();
       const uint32_t col = sp * 32u + lane;
-      const bool col_ok = col < ti.cols;
-      const bool acc = (ti.steps_acc >> 31) != 0;
+      const uint32_t cols = ti.cols_kbq & 0xFFu, kbq = ti.cols_kbq >> 8;
+      const bool col_ok = col < cols;
+      const bool acc = (ti.flags >> 31) != 0;
       const float bias = (ti.bias != nullptr && col_ok) ? ti.bias[col] : 0.0f;
       float* cbase = ti.c + col;
       const uint32_t npeers = p.peers.count;
+      // The MXINT8 copy: this warp's 32 columns are one block of the next
+      // layer's K (tiles start on 128-column boundaries); the block exists
+      // when it starts before column N.
+      const bool requant = ti.cq != nullptr && sp * 32u < cols;
 #pragma unroll 1
       for (uint32_t j0 = 0; j0 < NT; j0 += 16) {
         // The digit-plane partial sums of tokens j0..j0+15, added smallest
@@ -436,10 +474,9 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
 #pragma unroll
           for (uint32_t j = 0; j < 16; ++j) {
             if (j0 + j < ti.rows) {
-              float* dst = cbase + static_cast<size_t>(j0 + j) * ti.ldc;
-              if (acc) x[j] += *dst;
+              if (acc) x[j] += cbase[static_cast<size_t>(j0 + j) * ti.ldc];
               x[j] += bias;
-              *dst = x[j];
+              if (ti.c != nullptr) cbase[static_cast<size_t>(j0 + j) * ti.ldc] = x[j];
             }
           }
           if (npeers != 0) {
@@ -455,6 +492,7 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
             }
           }
         }
+        if (requant) requant_rows(ti, x, j0, sp, lane, col_ok, kbq, p.err);
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);

@@ -90,6 +90,8 @@ namespace hrb {
 hrb_status check_desc_for_noalloc(const hrb_gemm_desc* desc, uint32_t* pieces,
                                   uint32_t* npieces);
 QuantJob make_quant_job_for_noalloc(const hrb_gemm_desc* desc, int8_t* q, uint8_t* scale);
+// The encoder over C for the MXINT8 copy (desc->cq).
+QuantJob make_post_quant_job_for_noalloc(const hrb_gemm_desc* desc);
 DenseJob make_dense_job_for_noalloc(const hrb_gemm_desc* desc, const int8_t* aq,
                                     const uint8_t* ascale, const uint32_t* pieces,
                                     uint32_t npieces);

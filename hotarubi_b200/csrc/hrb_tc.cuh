@@ -22,6 +22,9 @@ struct TcJob {
   uint32_t accumulate;
   uint32_t m_tiles, n_tiles, k_steps;
   uint32_t tile_begin;     // prefix over the jobs of one launch
+  int8_t* cq;              // MXINT8 copy of C [M][kpN] or null
+  uint8_t* cscale;         // [M][kpN / 32]
+  uint32_t cquant;         // hrb_quant of the copy
 };
 
 // The block-scaled tensor-core path (gemm_mxf4.cu): kind::mxf4 for MXFP4
@@ -82,13 +85,16 @@ void launch_tile_weights_mxf4(uint32_t wfmt, const uint8_t* w, const uint8_t* ws
 struct MxTile {
   const uint8_t* w;     // the tile's first weight chunk
   const uint8_t* a;     // its first activation block
-  float* c;             // C at the tile's first row and column
+  float* c;             // C at the tile's first row and column, or null
   const float* bias;    // bias at the tile's first column, or null
-  uint32_t rows, cols;  // valid token rows and weight columns
+  int8_t* cq;           // MXINT8 copy at the tile's first row and column, or null
+  uint8_t* cscale;      // its scale at the tile's first row and block
+  uint32_t rows;        // valid token rows
+  uint32_t cols_kbq;    // valid weight columns | blocks per cq row << 8
   uint32_t ldc;
-  uint32_t steps_acc;   // K steps | accumulate << 31
+  uint32_t flags;       // K steps | VEC rule for cq << 30 | accumulate << 31
 };
-static_assert(sizeof(MxTile) == 48, "MxTile is read as three 16-byte loads");
+static_assert(sizeof(MxTile) == 64, "MxTile is read as four 16-byte loads");
 // The m_tiles * n_tiles tiles of one job (tile index mt * n_tiles + nt).
 void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out);
 // Peers that receive a copy of every output (the fused all-gather of a

@@ -82,6 +82,7 @@ extern "C" hrb_status hrb_gemm_dense_noalloc(const hrb_gemm_desc* desc, void* st
   uint32_t npieces = 0;
   hrb_status st = hrb::check_desc_for_noalloc(desc, pieces, &npieces);
   if (st != HRB_OK) return st;
+  if (desc->c == nullptr) return HRB_EINVAL;  // the exact kernel writes C
   const uint32_t kb = (desc->K + 31u) / 32u;
   const size_t code_bytes = align_up(size_t{desc->M} * kb * 32u, 256);
   const size_t scale_bytes = align_up(size_t{desc->M} * kb, 256);
@@ -112,5 +113,13 @@ extern "C" hrb_status hrb_gemm_dense_noalloc(const hrb_gemm_desc* desc, void* st
   job.tiles_n = tiles_n;
   job.tile_begin = 0;
   hrb::launch_dense_exact(nullptr, 1, &job, tiles, job.wfmt, s);
+  if (desc->cq != nullptr) {
+    // The MXINT8 copy of C, encoded after the GEMM (its flag word is the
+    // scratch's, unreported as above).
+    const hrb::QuantJob pq = hrb::make_post_quant_job_for_noalloc(desc);
+    hrb::launch_quantize(nullptr, 1, &pq, pq.units,
+                         reinterpret_cast<uint32_t*>(setup.scratch + kScratchBytes),
+                         setup.sm_count, s);
+  }
   return cudaGetLastError() == cudaSuccess ? HRB_OK : HRB_ECUDA;
 }

@@ -17,49 +17,11 @@
 #include <cstdint>
 
 #include "hrb_kernels.cuh"
+#include "hrb_quant.cuh"
 #include "hrb_tc.cuh"
 
 namespace hrb {
 namespace {
-
-__device__ __forceinline__ int32_t quantize_host_rule(uint32_t bits, int32_t e) {
-  const uint32_t f = (bits >> 23) & 0xFFu;
-  const uint32_t sig = f == 0 ? (bits & 0x7FFFFFu) : ((bits & 0x7FFFFFu) | 0x800000u);
-  // shift = (f == 0 ? -149 : f - 150) + 6 - e; inside a block it is <= -16.
-  const int32_t shift = (f == 0 ? -149 : static_cast<int32_t>(f) - 150) + 6 - e;
-  uint32_t mag;
-  if (shift >= 0) {
-    mag = shift > 8 ? 256u : (sig << shift);
-  } else {
-    const int32_t s = -shift;
-    if (s >= 32) {
-      mag = 0;
-    } else {
-      const uint32_t kept = sig >> s;
-      const uint32_t rest = sig & ((1u << s) - 1u);
-      const uint32_t half = 1u << (s - 1);
-      mag = kept + ((rest > half || (rest == half && (kept & 1u))) ? 1u : 0u);
-    }
-  }
-  const int32_t v = (bits >> 31) ? -static_cast<int32_t>(mag) : static_cast<int32_t>(mag);
-  return v < -128 ? -128 : (v > 127 ? 127 : v);
-}
-
-__device__ __forceinline__ int32_t quantize_vec_rule(uint32_t bits, uint32_t emax) {
-  const uint32_t f = (bits >> 23) & 0xFFu;
-  if (f == 0) return 0;
-  const uint32_t sig = (bits & 0x7FFFFFu) | 0x800000u;
-  const uint32_t shift = emax - f + 17u;
-  uint32_t mag = 0;
-  if (shift < 25u) {
-    const uint32_t whole = sig >> shift;
-    const uint32_t guard = (sig >> (shift - 1u)) & 1u;
-    const uint32_t sticky = (sig & ((1u << (shift - 1u)) - 1u)) != 0u;
-    mag = whole + ((guard && (sticky || (whole & 1u))) ? 1u : 0u);
-  }
-  if (bits >> 31) return mag >= 128u ? -128 : -static_cast<int32_t>(mag);
-  return mag >= 128u ? 127 : static_cast<int32_t>(mag);
-}
 
 // One unit of work: 128 consecutive elements (four blocks) of one row.
 struct Unit {

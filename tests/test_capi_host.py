@@ -123,3 +123,37 @@ def test_workload_canonicalisation_matches_the_reference_restatement():
     a = workloads.canonical_mxfp4(code, e)
     b = cpu.canonical_mxfp4(code, e)
     assert (a[0] == b[0]).all() and (a[1] == b[1]).all()
+
+
+def test_ctypes_structs_match_the_header(tmp_path):
+    """The ctypes mirrors of hrb_gemm_desc, hrb_gemm_cmd and hrb_ipc_handle
+    have the C layout: a C program built against include/hrb_gemm.h prints
+    every field's offset and the sizes."""
+    import ctypes
+    import shutil
+    import subprocess
+
+    from hotarubi_b200 import capi
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    structs = {"hrb_gemm_desc": capi.GemmDesc, "hrb_gemm_cmd": capi.GemmCmd,
+               "hrb_ipc_handle": capi.IpcHandle}
+    lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "hrb_gemm.h"',
+             "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for f in py._fields_:
+            lines.append(f'  printf("{cname} {f[0]} %zu\\n", offsetof({cname}, {f[0]}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    include = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+    subprocess.run([cc, "-I", include, str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
+    for line in filter(None, out):
+        cname, field, value = line.split()
+        py = structs[cname]
+        got = ctypes.sizeof(py) if field == "size" else getattr(py, field).offset
+        assert got == int(value), (cname, field, got, value)

@@ -66,3 +66,25 @@ def test_noalloc_refuses_more_than_its_scratch():
     c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
     d = capi.Library.desc(capi.WFMT_MXFP4, m, n, k, a=x, w=w, wscale=ws, c=c)
     assert lib.hrb_gemm_dense_noalloc(ctypes.byref(d), None) == capi.HRB_EINVAL
+
+
+@pytest.mark.gpu
+def test_no_alloc_mxint8_copy_of_the_output(hrb):
+    """hrb_gemm_dense_noalloc with cq: the encoder over C after the GEMM,
+    equal to the oracle's VEC encoding of C."""
+    from hotarubi_b200 import capi
+    from oracle import cpu
+    rng = np.random.default_rng(12)
+    m, n, k = 40, 90, 256
+    x = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).cuda()
+    w = torch.from_numpy(rng.integers(0, 256, (n, k // 2)).astype(np.uint8)).cuda()
+    ws = torch.from_numpy(rng.integers(118, 124, (n, k // 32)).astype(np.uint8)).cuda()
+    c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    cq = torch.zeros((m, 96), dtype=torch.int8, device="cuda")
+    cs = torch.zeros((m, 3), dtype=torch.uint8, device="cuda")
+    d = capi.Library.desc(0, m, n, k, a=x, w=w, wscale=ws, c=c, cq=cq, cscale=cs, cquant=1)
+    st = capi.load().hrb_gemm_dense_noalloc(ctypes.byref(d), None)
+    assert st == capi.HRB_OK
+    torch.cuda.synchronize()
+    q, s = cpu.quantize_vec(c.cpu().numpy().view(np.uint32))
+    assert np.array_equal(cq.cpu().numpy(), q) and np.array_equal(cs.cpu().numpy(), s)
