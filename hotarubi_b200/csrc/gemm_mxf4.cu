@@ -99,7 +99,13 @@ struct MxCfg {
   static constexpr uint32_t kSmem = kOffBar + 512 + 1024;
   static_assert(kABlock % 1024 == 0 && kWSlot % 1024 == 0, "ring alignment");
   static_assert(kSmem <= kSmemLimit, "shared memory");
-  static constexpr uint32_t kThreads = 224;
+  // Warps: 0 weight producer, 1 TMEM owner and MMA issuer, 2 activation
+  // producer (split rings), then kEpiWarps epilogue warps: warp w drains TMEM
+  // lane quarter w % 4, token rows of its share of the tile.  NT = 128 has a
+  // single accumulator buffer, whose drain holds up the next tile's MMAs:
+  // more warps drain it.
+  static constexpr uint32_t kEpiWarps = NT == 64 ? 8u : 16u;
+  static constexpr uint32_t kThreads = 32 * (3 + kEpiWarps);
 };
 
 struct MxParams {
@@ -267,7 +273,8 @@ __device__ __forceinline__ bool ring_drain(const Ring& r, uint32_t n, uint32_t* 
 }
 
 template <uint32_t NT, uint32_t WP, uint32_t KB>
-__global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ MxParams p) {
+__global__ void __launch_bounds__(MxCfg<NT, WP, KB>::kThreads, 1)
+    k_gemm_mxf4(const __grid_constant__ MxParams p) {
   using Cfg = MxCfg<NT, WP, KB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -295,7 +302,7 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
     }
     for (uint32_t b = 0; b < Cfg::kDBufs; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], 32 * Cfg::kEpiWarps);
     }
     fence_barrier_init();
   }
@@ -433,6 +440,10 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
     }
   } else if (warp >= 3) {
     const uint32_t sp = warp & 3u;
+    // Token rows [r0, r1) of each tile: the epilogue warps of a lane quarter
+    // split the tile's rows.
+    constexpr uint32_t kRowsPer = NT / (Cfg::kEpiWarps / 4);
+    const uint32_t r0 = ((warp - 3u) / 4u) * kRowsPer, r1 = r0 + kRowsPer;
     uint32_t t = 0;
     MxTile next = tile_info<NT>(p, blockIdx.x);
     for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++t) {
@@ -455,7 +466,7 @@ __global__ void __launch_bounds__(224, 1) k_gemm_mxf4(const __grid_constant__ Mx
       // when it starts before column N.
       const bool requant = ti.cq != nullptr && sp * 32u < cols;
 #pragma unroll 1
-      for (uint32_t j0 = 0; j0 < NT; j0 += 16) {
+      for (uint32_t j0 = r0; j0 < r1; j0 += 16) {
         // The digit-plane partial sums of tokens j0..j0+15, added smallest
         // scale first.
         uint32_t v0[16], v1[16], v2[16];

@@ -297,17 +297,37 @@ __device__ __forceinline__ uint32_t pack_e4m3x4(float a0, float a1, float a2, fl
   return out;
 }
 
+// max(|a|, |b|) of two FP32 bit patterns with NaN propagation (the sign of
+// the result is not used).
+__device__ __forceinline__ float max_nan_abs(uint32_t a, uint32_t b) {
+  float r;
+  asm("max.NaN.xorsign.abs.f32 %0, %1, %2;" : "=f"(r) : "f"(__uint_as_float(a)),
+      "f"(__uint_as_float(b)));
+  return r;
+}
+
 template <bool kVec>
 __device__ __forceinline__ void encode_planes(const PlaneJob& j, const PlaneOut& o, uint32_t step,
                                               uint32_t v[8], uint32_t lane, uint32_t& bad) {
   constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-  uint32_t key = 0;  // host rule: max magnitude; VEC rule: max exponent field
+  // The largest magnitude as an FP32 max of magnitudes (NaN-propagating, so
+  // a NaN or an Inf still shows in the key); the VEC rule's key is its
+  // exponent field (subnormals have field 0 either way).
+  float m[4];
 #pragma unroll
-  for (uint32_t i = 0; i < 8; ++i) {
-    const uint32_t mag = v[i] & 0x7FFFFFFFu;
-    if (kVec && (mag >> 23) == 0) v[i] = 0;  // the VEC pass reads subnormals as zero
-    const uint32_t k = kVec ? (mag >> 23) : mag;
-    key = k > key ? k : key;
+  for (uint32_t i = 0; i < 4; ++i) m[i] = max_nan_abs(v[2 * i], v[2 * i + 1]);
+  uint32_t key =
+      __float_as_uint(max_nan_abs(__float_as_uint(max_nan_abs(__float_as_uint(m[0]),
+                                                              __float_as_uint(m[1]))),
+                                  __float_as_uint(max_nan_abs(__float_as_uint(m[2]),
+                                                              __float_as_uint(m[3]))))) &
+      0x7FFFFFFFu;
+  if (kVec) {
+    key >>= 23;
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) {
+      if (((v[i] >> 23) & 0xFFu) == 0) v[i] = 0;  // the VEC pass reads subnormals as zero
+    }
   }
   key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 1));
   key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 2));
