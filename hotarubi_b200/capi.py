@@ -107,6 +107,7 @@ def load() -> ctypes.CDLL:
             "hrb_wbuf_to_dense": (ctypes.c_int, [P, P, u32, u32, P, P, P]),
             "hrb_w8_planes_to_dense": (ctypes.c_int, [P, P, P, u32, u32, P, P, P]),
             "hrb_abuf_to_dense": (ctypes.c_int, [P, P, u32, u32, P, P, P]),
+            "hrb_t32_split8_dense": (ctypes.c_int, [P, P, P, u32, u32, u32, P, P, P]),
             "hrb_dense_to_fbuf": (ctypes.c_int, [P, P, u32, u32, P, P]),
             "hrb_shared_alloc": (ctypes.c_int, [P, ctypes.c_size_t, ctypes.POINTER(P),
                                                 ctypes.POINTER(IpcHandle)]),
@@ -302,6 +303,13 @@ class Library:
     def abuf_to_dense(self, words, quads, kb, q, scales, stream=0):
         self._check(self.lib.hrb_abuf_to_dense(self.ctx, _ptr(words), quads, kb, _ptr(q),
                                                _ptr(scales), stream or None))
+
+    def t32_split8(self, vq, vscale, tokens, hd, wq, wscale, ldv=None, stream=0):
+        """T32_SPLIT8 in dense form: V cache codes [tokens][ldv] + scales ->
+        the W8 operand of P.V, codes [hd][tokens] + scales [hd][tokens/32]."""
+        self._check(self.lib.hrb_t32_split8_dense(self.ctx, _ptr(vq), _ptr(vscale), tokens, hd,
+                                                  hd if ldv is None else ldv, _ptr(wq),
+                                                  _ptr(wscale), stream or None))
 
     def dense_to_fbuf(self, c, rows, cols, words, stream=0):
         self._check(self.lib.hrb_dense_to_fbuf(self.ctx, _ptr(c), rows, cols, _ptr(words),

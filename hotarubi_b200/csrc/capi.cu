@@ -1289,6 +1289,31 @@ hrb_status hrb_abuf_to_dense(hrb_ctx* ctx, const uint8_t* words, uint32_t quads,
   return HRB_OK;
 }
 
+hrb_status hrb_t32_split8_dense(hrb_ctx* ctx, const int8_t* vq, const uint8_t* vscale,
+                                uint32_t tokens, uint32_t hd, uint32_t ldv, int8_t* wq,
+                                uint8_t* wscale, void* stream) {
+  if (ctx == nullptr) return HRB_EINVAL;
+  if (!vq || !vscale || !wq || !wscale) return fail(ctx, HRB_EINVAL, "null buffer");
+  if (tokens == 0 || hd == 0) return fail(ctx, HRB_EINVAL, "empty V cache %u x %u", tokens, hd);
+  if (tokens % 4u != 0) {
+    return fail(ctx, HRB_EINVAL, "%u tokens do not fill DMA rows of 4 tokens", tokens);
+  }
+  // LoadT32's own check (dma_engine.cpp:380-382), on DMA rows of 4 tokens.
+  if (tokens % 32u != 0) {
+    return fail(ctx, HRB_EINVAL, "T32_SPLIT8 with %u rows, not a multiple of 8", tokens / 4u);
+  }
+  if (hd % 32u != 0 || ldv % 32u != 0 || ldv < hd) {
+    return fail(ctx, HRB_EINVAL, "head dim %u / row stride %u are not whole blocks of 32", hd, ldv);
+  }
+  if (!aligned(vq, 16) || !aligned(wq, 16)) return fail(ctx, HRB_EINVAL, "misaligned buffer");
+  HRB_CUDA(ctx, cudaSetDevice(ctx->device));
+  hrb::launch_t32_split8(vq, vscale, tokens, hd, ldv, wq, wscale, ctx->sm_count,
+                         pick(ctx, stream));
+  ctx->launches += 1;
+  HRB_CUDA(ctx, cudaGetLastError());
+  return HRB_OK;
+}
+
 hrb_status hrb_dense_to_fbuf(hrb_ctx* ctx, const float* c, uint32_t rows, uint32_t cols,
                              float* words, void* stream) {
   if (ctx == nullptr) return HRB_EINVAL;

@@ -106,4 +106,9 @@ void launch_abuf_to_dense(const uint8_t* words, uint32_t quads, uint32_t kb, int
 void launch_dense_to_fbuf(const float* c, uint32_t rows, uint32_t cols, float* words,
                           cudaStream_t stream);
 
+// T32_SPLIT8 in dense form (kv_operands.cu).
+void launch_t32_split8(const int8_t* vq, const uint8_t* vs, uint32_t tokens, uint32_t hd,
+                       uint32_t ldv, int8_t* wq, uint8_t* ws, int sm_count,
+                       cudaStream_t stream);
+
 }  // namespace hrb
