@@ -82,6 +82,12 @@ def oracle() -> ctypes.CDLL:
         lib.hrbo_round_scaled_n.argtypes = [_i64p, _i32p, _u32p, ctypes.c_size_t]
         lib.hrbo_align_element.restype = ctypes.c_uint8
         lib.hrbo_align_element.argtypes = [ctypes.c_uint8, ctypes.c_uint32]
+        lib.hrbo_conv_im2col.restype = ctypes.c_int
+        lib.hrbo_conv_im2col.argtypes = [ctypes.c_uint32] * 7 + [_i8p, _u8p, _i8p, _u8p]
+        lib.hrbo_conv_weights.restype = None
+        lib.hrbo_conv_weights.argtypes = [ctypes.c_uint32] * 4 + [_u8p, _u8p, _u8p, _u8p]
+        lib.hrbo_relu_n.restype = None
+        lib.hrbo_relu_n.argtypes = [_u32p, ctypes.c_size_t]
         lib.hrbo_t32_split8.restype = ctypes.c_int
         lib.hrbo_t32_split8.argtypes = [_i8p, _u8p, ctypes.c_uint32, ctypes.c_uint32,
                                         ctypes.c_uint32, _i8p, _u8p]
@@ -145,6 +151,9 @@ def ref() -> ctypes.CDLL | None:
         lib.hrbref_dma_load_wbuf.argtypes = [ctypes.c_uint32, _u8p, ctypes.c_uint32,
                                              ctypes.c_uint32, ctypes.c_uint32,
                                              ctypes.c_uint32, ctypes.c_uint32, _u8p]
+        lib.hrbref_conv_iss.restype = ctypes.c_int
+        lib.hrbref_conv_iss.argtypes = [ctypes.c_uint32] * 6 + [
+            _i8p, _u8p, _u8p, _i32p, _u32p, ctypes.c_void_p, ctypes.c_int, _u32p]
         lib.hrbref_dense_gemm_iss.restype = ctypes.c_int
         lib.hrbref_dense_gemm_iss.argtypes = [
             ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
@@ -380,6 +389,63 @@ def t32_split8(vq: np.ndarray, vs: np.ndarray, hd: int | None = None) -> tuple[n
                                 ws.ravel()) != 0:
         raise ValueError(f"T32_SPLIT8 shape {tokens} x {hd} (ldv {ldv}) is not whole 32 x 32 blocks")
     return wq, ws
+
+
+# ---------------------------------------------------------------------------
+# Convolution (ConvEmitter, tools/compiler/sparsedrive_encoder.cpp)
+
+def conv_geometry(H: int, W: int, cin: int, kh: int, stride: int):
+    """(Ho, Wo, planes, K' blocks per output) of a conv the emitter accepts."""
+    plane = min(cin, 256)
+    return H // stride, W // stride, cin // plane, kh * kh * cin // 32
+
+
+def conv_im2col(aq: np.ndarray, ascale: np.ndarray, images: int, H: int, W: int, cin: int,
+                kh: int, stride: int, order: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    """hrbo_conv_im2col: the gathered activations [images*Ho*Wo, kh*kh*cin]
+    in chain order (plane, tap, channel) and their scales."""
+    ho, wo, _, kbo = conv_geometry(H, W, cin, kh, stride)
+    m = images * ho * wo
+    q = np.empty((m, kbo * 32), np.int8)
+    sc = np.empty((m, kbo), np.uint8)
+    if oracle().hrbo_conv_im2col(images, H, W, cin, kh, stride, order,
+                                 np.ascontiguousarray(aq, np.int8).ravel(),
+                                 np.ascontiguousarray(ascale, np.uint8).ravel(),
+                                 q.ravel(), sc.ravel()) != 0:
+        raise ValueError("conv shape not supported")
+    return q, sc
+
+
+def conv_weights(wfmt: int, w: np.ndarray, wscale: np.ndarray, cout: int, cin: int,
+                 kh: int) -> tuple[np.ndarray, np.ndarray]:
+    """hrbo_conv_weights: the [cout, kh*kh*cin] weight matrix in chain order."""
+    bpb = 16 if wfmt == WFMT_MXFP4 else 32
+    w = np.ascontiguousarray(w, np.uint8)
+    out = np.empty_like(w)
+    osc = np.empty_like(np.ascontiguousarray(wscale, np.uint8))
+    oracle().hrbo_conv_weights(cout, cin, kh, bpb, w.ravel(),
+                               np.ascontiguousarray(wscale, np.uint8).ravel(), out.ravel(),
+                               osc.ravel())
+    return out, osc
+
+
+def relu(bits: np.ndarray) -> np.ndarray:
+    out = np.ascontiguousarray(bits, np.uint32).copy()
+    oracle().hrbo_relu_n(out.ravel(), out.size)
+    return out
+
+
+def conv_dense(wfmt: int, aq, ascale, images, H, W, cin, cout, kh, stride, w, wscale,
+               order=0, bias_bits=None, c_init=None, relu_out=False) -> np.ndarray:
+    """The conv chain: gathered activations x reordered weights, one K
+    piece per (plane, tap) job (W8: HI then LO per job), bias, RELU."""
+    q, sc = conv_im2col(aq, ascale, images, H, W, cin, kh, stride, order)
+    wq, ws = conv_weights(wfmt, w, wscale, cout, cin, kh)
+    _, _, planes, _ = conv_geometry(H, W, cin, kh, stride)
+    pieces = [min(cin, 256) // 32] * (planes * kh * kh)
+    c = gemm_dense(wfmt, q, sc, wq, ws, cout, bias_bits=bias_bits, c_init=c_init,
+                   pieces=pieces)
+    return relu(c) if relu_out else c
 
 
 def split_w8(q: np.ndarray) -> tuple[np.ndarray, np.ndarray]:

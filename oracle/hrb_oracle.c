@@ -415,3 +415,84 @@ int hrbo_t32_split8(const int8_t* vq, const uint8_t* vs, uint32_t tokens,
   }
   return 0;
 }
+
+/* Source position of output o's tap (ky, kx), or -1 outside the map:
+ * FaceListS1 / FaceListStrided (sparsedrive_encoder.cpp:114-150) with
+ * padding (kh-1)/2. */
+static int64_t conv_source(uint32_t H, uint32_t W, uint32_t kh, uint32_t stride,
+                           uint32_t order, uint32_t o, uint32_t ky, uint32_t kx) {
+  const uint32_t Ho = H / stride, Wo = W / stride;
+  const uint32_t yo = order == 0 ? o % Ho : o / Wo;
+  const uint32_t xo = order == 0 ? o / Ho : o % Wo;
+  const int64_t pad = (int64_t)(kh - 1u) / 2;
+  const int64_t yi = (int64_t)stride * yo + ky - pad;
+  const int64_t xi = (int64_t)stride * xo + kx - pad;
+  if (yi < 0 || yi >= H || xi < 0 || xi >= W) return -1;
+  return order == 0 ? xi * H + yi : yi * W + xi;
+}
+
+int hrbo_conv_im2col(uint32_t images, uint32_t H, uint32_t W, uint32_t cin,
+                     uint32_t kh, uint32_t stride, uint32_t order,
+                     const int8_t* aq, const uint8_t* ascale,
+                     int8_t* out_q, uint8_t* out_scale) {
+  if ((kh != 1 && kh != 3) || (stride != 1 && stride != 2) || cin % 32u != 0 ||
+      (cin > 256u && cin % 256u != 0) || H / stride == 0 || W / stride == 0) {
+    return -1;
+  }
+  const uint32_t taps = kh * kh, plane = cin < 256u ? cin : 256u, planes = cin / plane;
+  const uint32_t kbi = cin / 32u, kbo = taps * kbi, out_per = (H / stride) * (W / stride);
+  for (uint32_t img = 0; img < images; ++img) {
+    for (uint32_t o = 0; o < out_per; ++o) {
+      const size_t row = (size_t)img * out_per + o;
+      uint32_t b = 0;
+      for (uint32_t p = 0; p < planes; ++p) {
+        for (uint32_t t = 0; t < taps; ++t) {
+          const int64_t src = conv_source(H, W, kh, stride, order, o, t / kh, t % kh);
+          for (uint32_t cb = 0; cb < plane / 32u; ++cb, ++b) {
+            const uint32_t ib = p * (plane / 32u) + cb;
+            const size_t pos = (size_t)img * H * W + (size_t)(src < 0 ? 0 : src);
+            for (uint32_t k = 0; k < 32; ++k) {
+              out_q[row * kbo * 32u + (size_t)b * 32u + k] =
+                  src < 0 ? 0 : aq[pos * cin + ib * 32u + k];
+            }
+            /* A null entry's token carries scale byte 127 (kNullScale). */
+            out_scale[row * kbo + b] = src < 0 ? 127 : ascale[pos * kbi + ib];
+          }
+        }
+      }
+    }
+  }
+  return 0;
+}
+
+void hrbo_conv_weights(uint32_t cout, uint32_t cin, uint32_t kh,
+                       uint32_t bytes_per_block, const uint8_t* w,
+                       const uint8_t* wscale, uint8_t* out_w,
+                       uint8_t* out_scale) {
+  const uint32_t taps = kh * kh, plane = cin < 256u ? cin : 256u, planes = cin / plane;
+  const uint32_t kbi = cin / 32u, kbo = taps * kbi;
+  for (uint32_t n = 0; n < cout; ++n) {
+    uint32_t b = 0;
+    for (uint32_t p = 0; p < planes; ++p) {
+      for (uint32_t t = 0; t < taps; ++t) {
+        for (uint32_t cb = 0; cb < plane / 32u; ++cb, ++b) {
+          const uint32_t src = t * kbi + p * (plane / 32u) + cb;
+          for (uint32_t i = 0; i < bytes_per_block; ++i) {
+            out_w[((size_t)n * kbo + b) * bytes_per_block + i] =
+                w[((size_t)n * kbo + src) * bytes_per_block + i];
+          }
+          out_scale[(size_t)n * kbo + b] = wscale[(size_t)n * kbo + src];
+        }
+      }
+    }
+  }
+}
+
+void hrbo_relu_n(uint32_t* x, size_t n) {
+  /* MaxGreaterEqual(x, +0) (lane.cpp:57-70) keeps x unless x is negative
+   * with a nonzero magnitude; the pass then adds +0 (lane.cpp:325). */
+  for (size_t i = 0; i < n; ++i) {
+    const uint32_t keep = (x[i] >> 31) == 0 || (x[i] & 0x7FFFFFFFu) == 0;
+    x[i] = hrbo_fp32_add(keep ? x[i] : 0u, 0u);
+  }
+}

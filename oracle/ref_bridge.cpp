@@ -26,6 +26,7 @@
 #include "lane.hpp"       // tools/iss/lane.hpp
 #include "memories.hpp"   // tools/iss/memories.hpp
 #include "reference.hpp"  // tools/iss/reference.hpp
+#include "tensors.hpp"    // tools/compiler/tensors.hpp
 #include "weights.hpp"    // tools/compiler/weights.hpp
 
 #include "tb_types.hpp"
@@ -487,6 +488,190 @@ void hrbref_dma_load_wbuf(uint32_t kind, uint8_t* ddr, uint32_t ddr_bytes,
     std::memcpy(wbuf + size_t{i} * iss::kWbufWordBytes, memories->wbuf[i].data(),
                 iss::kWbufWordBytes);
   }
+}
+
+// A convolution lowered the way the compiler's ConvEmitter lowers it
+// (tools/compiler/sparsedrive_encoder.cpp) and run on the reference's own DMA
+// engine and GEMM array, one output tile of 64 positions at a time:
+//
+//   * faces and taps as MakeSrc builds them (:78-111), their index lists as
+//     FaceListS1 / FaceListStrided write them (:114-150, restated here: both
+//     are file-local in the reference), the map in DDR row format
+//     (TokenBytes, sparsedrive_common.cpp:28-33);
+//   * each face gathered into ABUF by DmaEngine::Execute with a ROW_INDEXED
+//     load (dma_engine.cpp:231-262, null entries included);
+//   * per (plane, face, tap) job one ExecuteGemm with the fields of
+//     ConvEmitter::Group (:384-398), the weight tile being the conv matrix's
+//     columns [tap*cin + c0, +channels) (ConvTile, sparsedrive_common.cpp:
+//     136-158, restated) packed by the reference's PackWbuf;
+//   * then ADDP of the bias and, with relu, the RELU pass (restated from
+//     lane.cpp:57-70,325 around the reference's Fp32Add).
+//
+// One x-major map (position x*H + y) of H x W x cin MXINT8 codes aq and
+// scale bytes ascale; FP4 weight codes wcode [cout][kh*kh*cin] (one code per
+// byte) with exponents we [cout][kh*kh*cin/32]; bias [cout] FP32 bits;
+// residual (or null) and c: [Ho*Wo][cout] FP32 bits.  Returns 0, or -1 for a
+// shape the emitter rejects.
+int hrbref_conv_iss(uint32_t H, uint32_t W, uint32_t cin, uint32_t cout,
+                    uint32_t kh, uint32_t stride, const int8_t* aq,
+                    const uint8_t* ascale, const uint8_t* wcode,
+                    const int32_t* we, const uint32_t* bias,
+                    const uint32_t* residual, int relu, uint32_t* c) {
+  namespace iss = hotarubi::iss;
+  if (H % 4 != 0 || cin % 32 != 0 || (cin > 256 && cin % 256 != 0) ||
+      (kh != 1 && kh != 3) || (stride != 1 && stride != 2) || cout % 8 != 0 ||
+      (cout > 256 && cout % 256 != 0)) {
+    return -1;
+  }
+  struct Face { int32_t dy; bool strided; int32_t dx; };
+  struct Tap { uint32_t ky, kx, qoff; };
+  std::vector<Face> faces;
+  std::vector<std::vector<Tap>> taps;
+  if (kh == 1) {
+    faces.push_back({0, true, 0});
+    taps.push_back({{0, 0, 0}});
+  } else if (stride == 1) {
+    for (int32_t dy = -1; dy <= 1; ++dy) {
+      faces.push_back({dy, false, 0});
+      std::vector<Tap> row;
+      for (int32_t dx = -1; dx <= 1; ++dx) {
+        row.push_back({static_cast<uint32_t>(dy + 1), static_cast<uint32_t>(dx + 1),
+                       static_cast<uint32_t>(dx + 1) * H / 4});
+      }
+      taps.push_back(row);
+    }
+  } else {
+    for (int32_t dy = -1; dy <= 1; ++dy) {
+      for (int32_t dx = -1; dx <= 1; ++dx) {
+        faces.push_back({dy, true, dx});
+        taps.push_back({{static_cast<uint32_t>(dy + 1), static_cast<uint32_t>(dx + 1), 0}});
+      }
+    }
+  }
+  constexpr uint32_t mt = 64;
+  constexpr uint64_t kBase = 0x20000000;
+  const uint32_t plane = std::min(cin, 256u), planes = cin / plane, tok = plane / 32;
+  const uint64_t tb = uint64_t{tok} * 32 + (tok + 15) / 16 * 16;
+  const uint32_t tokens = H * W, ho = H / stride, wo = W / stride, n_out = ho * wo;
+  const uint32_t nt = std::min(cout, 256u), n8 = nt / 8;
+  const uint32_t face_tokens = (kh == 3 && stride == 1) ? mt + 2 * H : mt;
+  const uint32_t face_words = face_tokens / 4 * tok;
+  if (uint64_t{planes} * faces.size() * face_words > iss::kAbufDepth) return -1;
+  const uint64_t map_bytes = (uint64_t{tokens} + 64) * tb;
+  const uint64_t list_off = planes * map_bytes;
+  std::vector<std::byte> bytes(list_off + (uint64_t{face_tokens} * 4 + 15) / 16 * 16 + 64);
+  for (uint32_t p = 0; p < planes; ++p) {
+    for (uint32_t j = 0; j < tokens; ++j) {
+      std::byte* tokp = bytes.data() + p * map_bytes + j * tb;
+      for (uint32_t k = 0; k < plane; ++k) {
+        tokp[k] = static_cast<std::byte>(aq[size_t{j} * cin + p * plane + k]);
+      }
+      for (uint32_t b = 0; b < tok; ++b) {
+        tokp[tok * 32 + b] = static_cast<std::byte>(ascale[size_t{j} * (cin / 32) + p * tok + b]);
+      }
+    }
+  }
+  iss::Ddr ddr{std::span<std::byte>(bytes), kBase};
+  auto memories = std::make_unique<iss::Memories>();
+  iss::DmaEngine engine;
+  const uint32_t kbw = kh * kh * cin / 32;  // weight blocks per row
+  for (uint32_t i0 = 0; i0 < n_out; i0 += mt) {
+    // LoadFaces: every (plane, face) gathered into its own ABUF range.
+    for (uint32_t p = 0; p < planes; ++p) {
+      for (size_t f = 0; f < faces.size(); ++f) {
+        std::vector<uint32_t> list;
+        const Face& face = faces[f];
+        auto entry = [&](int64_t token) {
+          return static_cast<uint32_t>((kBase + p * map_bytes + token * tb) / 16);
+        };
+        if (!face.strided) {
+          for (int64_t e = 0; e < face_tokens; ++e) {
+            const int64_t j = int64_t{i0} - H + e;
+            const bool ok = j >= 0 && j < tokens && (j % H) + face.dy >= 0 &&
+                            (j % H) + face.dy < H;
+            list.push_back(ok ? entry(j + face.dy) : hotarubi::isa::kNullEntry);
+          }
+        } else {
+          for (int64_t o = i0; o < int64_t{i0} + mt; ++o) {
+            const int64_t xo = o / ho, yo = o % ho;
+            const int64_t yi = int64_t{stride} * yo + face.dy;
+            const int64_t xi = int64_t{stride} * xo + face.dx;
+            const bool ok = o < int64_t{ho} * wo && yi >= 0 && yi < H && xi >= 0 && xi < W;
+            list.push_back(ok ? entry(xi * H + yi) : hotarubi::isa::kNullEntry);
+          }
+        }
+        for (size_t u = 0; u < list.size(); ++u) {
+          for (uint32_t b = 0; b < 4; ++b) {
+            bytes[list_off + u * 4 + b] = static_cast<std::byte>((list[u] >> (8 * b)) & 0xFF);
+          }
+        }
+        iss::DmaCommand command{};
+        command.ddr_addr = static_cast<uint32_t>((kBase + list_off) / 16);
+        command.mem = 0;  // ABUF
+        command.onchip = static_cast<uint32_t>((p * faces.size() + f) * face_words);
+        command.rows = 1;
+        command.row_words = face_tokens;
+        command.kind = hotarubi::isa::dma::kKindRowIndexed;
+        command.tok = tok;
+        engine.Execute(command, ddr, *memories);
+      }
+    }
+    for (uint32_t n0 = 0; n0 < cout; n0 += nt) {
+      if (residual != nullptr) {
+        for (uint32_t r = 0; r < mt; ++r) {
+          for (uint32_t n = 0; n < nt; ++n) {
+            const uint32_t o = i0 + r;
+            memories->fbuf[(r / 4) * n8 + n / 8][(r % 4) * 8 + n % 8] =
+                o < n_out ? residual[size_t{o} * cout + n0 + n] : 0;
+          }
+        }
+      }
+      uint32_t k = 0;
+      for (uint32_t p = 0; p < planes; ++p) {
+        for (size_t f = 0; f < faces.size(); ++f) {
+          for (const Tap& tap : taps[f]) {
+            const uint32_t first = (tap.ky * kh + tap.kx) * cin + p * plane;
+            hotarubi::compiler::Mxfp4Matrix tile{.rows = nt, .cols = plane, .code = {}, .e = {}};
+            for (uint32_t r = n0; r < n0 + nt; ++r) {
+              tile.code.insert(tile.code.end(), wcode + size_t{r} * kh * kh * cin + first,
+                               wcode + size_t{r} * kh * kh * cin + first + plane);
+              for (uint32_t b = 0; b < tok; ++b) tile.e.push_back(we[size_t{r} * kbw + first / 32 + b]);
+            }
+            const std::vector<std::byte> words = hotarubi::compiler::PackWbuf(tile);
+            for (size_t wd = 0; wd < words.size() / iss::kWbufWordBytes; ++wd) {
+              std::memcpy(memories->wbuf[wd].data(), words.data() + wd * iss::kWbufWordBytes,
+                          iss::kWbufWordBytes);
+            }
+            const GemmCommand gemm{
+                .a_base = static_cast<uint32_t>((p * faces.size() + f) * face_words + tap.qoff * tok),
+                .a_stride = tok,
+                .kb = tok,
+                .m = mt,
+                .w_base = 0,
+                .w_stride = tok,
+                .n8 = n8,
+                .c_base = 0,
+                .wmode = 0,
+                .acc = k > 0 || residual != nullptr};
+            iss::ExecuteGemm(gemm, *memories);
+            ++k;
+          }
+        }
+      }
+      for (uint32_t r = 0; r < mt && i0 + r < n_out; ++r) {
+        for (uint32_t n = 0; n < nt; ++n) {
+          uint32_t v = memories->fbuf[(r / 4) * n8 + n / 8][(r % 4) * 8 + n % 8];
+          v = iss::Fp32Add(v, bias[n0 + n]);
+          if (relu) {
+            const bool keep = (v >> 31) == 0 || (v & 0x7FFFFFFFu) == 0;
+            v = iss::Fp32Add(keep ? v : 0u, 0u);
+          }
+          c[size_t{i0 + r} * cout + n0 + n] = v;
+        }
+      }
+    }
+  }
+  return 0;
 }
 
 }  // extern "C"

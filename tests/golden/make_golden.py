@@ -380,6 +380,51 @@ def kv_dma_cases(ref):
     np.savez_compressed(os.path.join(OUT, "kv_dma.npz"), **out)
 
 
+CONV_SPECS = (  # name, H, W, cin, cout, kh, stride, residual, relu
+    ("s1_3x3_16x12x64x32", 16, 12, 64, 32, 3, 1, False, False),
+    ("s1_3x3_4x4x512x16_res_relu", 4, 4, 512, 16, 3, 1, True, True),
+    ("s2_3x3_8x6x64x256_relu", 8, 6, 64, 256, 3, 2, False, True),
+    ("s1_1x1_4x4x256x512_res", 4, 4, 256, 512, 1, 1, True, False),
+    ("s2_1x1_12x8x64x24_relu", 12, 8, 64, 24, 1, 2, False, True),
+)
+
+
+def conv_cases(ref):
+    """Convolutions lowered as ConvEmitter lowers them and run by the
+    reference's DMA engine and ExecuteGemm (oracle/ref_bridge.cpp
+    hrbref_conv_iss): MXINT8 map from EncodeMxint8, CanonicalMxfp4 weights."""
+    rng = np.random.default_rng(21)
+    out = {}
+    for name, H, W, cin, cout, kh, stride, res, relu in CONV_SPECS:
+        x = rng.standard_normal((H * W, cin)).astype(np.float32)
+        aq = np.empty((H * W, cin), np.int8)
+        e_a = np.empty((H * W, cin // 32), np.int32)
+        ref.hrbref_encode_mxint8(x.view(np.uint32).ravel(), H * W, cin, aq.ravel(), e_a.ravel())
+        code = rng.integers(0, 16, (cout, kh * kh * cin)).astype(np.uint8)
+        e = rng.integers(-10, -3, (cout, kh * kh * cin // 32)).astype(np.int32)
+        co = np.empty_like(code)
+        eo = np.empty_like(e)
+        ref.hrbref_canonical_mxfp4(code.ravel(), e.ravel(), cout, kh * kh * cin, 0, cout,
+                                   co.ravel(), eo.ravel())
+        bias = (rng.standard_normal(cout) * 0.1).astype(np.float32).view(np.uint32)
+        ho, wo = H // stride, W // stride
+        resid = (rng.standard_normal((ho * wo, cout)).astype(np.float32).view(np.uint32)
+                 if res else None)
+        c = np.zeros((ho * wo, cout), np.uint32)
+        assert ref.hrbref_conv_iss(H, W, cin, cout, kh, stride, aq.ravel(),
+                                   (e_a + 127).astype(np.uint8).ravel(), co.ravel(), eo.ravel(),
+                                   bias, None if resid is None else resid.ctypes.data,
+                                   int(relu), c.ravel()) == 0
+        out[f"{name}/x"] = x
+        out[f"{name}/w"] = cpu.pack_nibbles(co)
+        out[f"{name}/wscale"] = (eo + 127).astype(np.uint8)
+        out[f"{name}/bias"] = bias
+        if resid is not None:
+            out[f"{name}/residual"] = resid
+        out[f"{name}/c"] = c
+    np.savez_compressed(os.path.join(OUT, "conv.npz"), **out)
+
+
 def main() -> None:
     ref = cpu.ref()
     if ref is None:
@@ -391,6 +436,7 @@ def main() -> None:
     weights_cases(ref)
     dense_cases(ref)
     kv_dma_cases(ref)
+    conv_cases(ref)
     dense_mxfp8_case()
     for f in sorted(os.listdir(OUT)):
         if f.endswith(".npz"):

@@ -1,0 +1,106 @@
+"""Pins the CPU restatement of the convolution chain (hrbo_conv_im2col,
+hrbo_conv_weights, hrbo_relu_n + the dense chain; oracle/cpu.py conv_dense)
+to hotarubi's own code: a conv lowered as ConvEmitter lowers it
+(tools/compiler/sparsedrive_encoder.cpp:78-168,384-428) and executed by the
+reference's DMA engine (ROW_INDEXED gathers with null entries,
+tools/iss/dma_engine.cpp:231-262) and ExecuteGemm, through
+oracle/ref_bridge.cpp hrbref_conv_iss.
+
+* tests/golden/conv.npz: that composition's outputs (make_golden.py
+  ``conv_cases``), always available;
+* the compiled reference (``ref_lib``) on further random shapes.
+"""
+import numpy as np
+import pytest
+
+from oracle import cpu
+
+SPECS = ["s1_3x3_16x12x64x32", "s1_3x3_4x4x512x16_res_relu", "s2_3x3_8x6x64x256_relu",
+         "s1_1x1_4x4x256x512_res", "s2_1x1_12x8x64x24_relu"]
+
+
+def parse(name):
+    parts = name.split("_")
+    stride = int(parts[0][1:])
+    kh = int(parts[1][0])
+    H, W, cin, cout = (int(v) for v in parts[2].split("x"))
+    return H, W, cin, cout, kh, stride, "res" in parts, "relu" in parts
+
+
+@pytest.mark.parametrize("name", SPECS)
+def test_conv_chain_on_reference_golden(golden, name):
+    g = golden("conv.npz")
+    H, W, cin, cout, kh, stride, res, relu = parse(name)
+    aq, asc = cpu.encode_mxint8(g[f"{name}/x"].view(np.uint32))
+    c = cpu.conv_dense(cpu.WFMT_MXFP4, aq, asc, 1, H, W, cin, cout, kh, stride,
+                       g[f"{name}/w"], g[f"{name}/wscale"], bias_bits=g[f"{name}/bias"],
+                       c_init=g.get(f"{name}/residual"), relu_out=relu)
+    assert (c == g[f"{name}/c"]).all()
+
+
+@pytest.mark.parametrize("H,W,cin,cout,kh,stride,res,relu,seed", [
+    (4, 3, 32, 8, 3, 1, False, True, 1),
+    (12, 5, 256, 40, 3, 1, True, False, 2),
+    (8, 9, 128, 16, 3, 2, True, True, 3),
+    (20, 4, 768, 8, 1, 1, False, False, 4),
+])
+def test_conv_chain_vs_reference(ref_lib, H, W, cin, cout, kh, stride, res, relu, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((H * W, cin)).astype(np.float32)
+    x[rng.random(H * W) < 0.1] = 0.0          # all-zero tokens as well as null entries
+    aq, asc = cpu.encode_mxint8(x.view(np.uint32))
+    code = rng.integers(0, 16, (cout, kh * kh * cin)).astype(np.uint8)
+    e = rng.integers(-10, -3, (cout, kh * kh * cin // 32))
+    code, e = cpu.canonical_mxfp4(code, e)
+    bias = (rng.standard_normal(cout) * 0.1).astype(np.float32).view(np.uint32)
+    ho, wo = H // stride, W // stride
+    resid = rng.standard_normal((ho * wo, cout)).astype(np.float32).view(np.uint32) if res else None
+    want = np.zeros((ho * wo, cout), np.uint32)
+    assert ref_lib.hrbref_conv_iss(H, W, cin, cout, kh, stride, aq.ravel(), asc.ravel(),
+                                   code.ravel(), e.astype(np.int32).ravel(), bias,
+                                   None if resid is None else resid.ctypes.data, int(relu),
+                                   want.ravel()) == 0
+    got = cpu.conv_dense(cpu.WFMT_MXFP4, aq, asc, 1, H, W, cin, cout, kh, stride,
+                         cpu.pack_nibbles(code), (e + 127).astype(np.uint8), bias_bits=bias,
+                         c_init=resid, relu_out=relu)
+    assert (got == want).all()
+
+
+def test_im2col_null_entries_and_chain_order():
+    H, W, cin = 4, 4, 64
+    aq = np.arange(H * W * cin, dtype=np.int64).astype(np.int8).reshape(H * W, cin)
+    asc = (np.arange(H * W * 2) % 50 + 100).astype(np.uint8).reshape(H * W, 2)
+    q, s = cpu.conv_im2col(aq, asc, 1, H, W, cin, 3, 1, order=0)
+    # Output 0 is (x, y) = (0, 0): taps with ky = 0 or kx = 0 fall outside.
+    for tap in range(9):
+        ky, kx = divmod(tap, 3)
+        blk = q[0, tap * cin:(tap + 1) * cin]
+        if ky == 0 or kx == 0:
+            assert (blk == 0).all() and (s[0, tap * 2:tap * 2 + 2] == 127).all()
+        else:
+            src = (kx - 1) * H + (ky - 1)  # x-major position
+            assert (blk == aq[src]).all() and (s[0, tap * 2:tap * 2 + 2] == asc[src]).all()
+
+
+def test_position_orders_agree():
+    rng = np.random.default_rng(8)
+    H, W, cin, cout = 8, 12, 64, 16
+    x = rng.standard_normal((H, W, cin)).astype(np.float32)
+    code = rng.integers(0, 16, (cout, 9 * cin)).astype(np.uint8)
+    e = rng.integers(-10, -3, (cout, 9 * cin // 32))
+    code, e = cpu.canonical_mxfp4(code, e)
+    w, ws = cpu.pack_nibbles(code), (e + 127).astype(np.uint8)
+    outs = []
+    for order, xm in ((0, x.transpose(1, 0, 2)), (1, x)):   # x-major, y-major
+        aq, asc = cpu.encode_mxint8(np.ascontiguousarray(xm).reshape(H * W, cin).view(np.uint32))
+        c = cpu.conv_dense(cpu.WFMT_MXFP4, aq, asc, 1, H, W, cin, cout, 3, 1, w, ws, order=order)
+        outs.append(c.reshape(*((W, H) if order == 0 else (H, W)), cout))
+    assert (outs[0].transpose(1, 0, 2) == outs[1]).all()
+
+
+def test_conv_rejects_unsupported_shapes():
+    with pytest.raises(ValueError):
+        cpu.conv_im2col(np.zeros((16, 32), np.int8), np.zeros((16, 1), np.uint8), 1, 4, 4, 32, 5, 1)
+    with pytest.raises(ValueError):
+        cpu.conv_im2col(np.zeros((16, 320), np.int8), np.zeros((16, 10), np.uint8), 1, 4, 4, 320,
+                        3, 1)
