@@ -1,7 +1,7 @@
 """Benchmark of the quantized GEMM hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c1|c4|c5] [--mode exact|fast] [--batch B]
+                    [--config c2|c1|c4|c5|c5conv] [--mode exact|fast] [--batch B]
 
 Default workload (the MXFP4 GEMM the metric is
 quoted on): C = A . W^T with A FP32 [64, 2560] ~ N(0,1) encoded to MXINT8 on
@@ -10,7 +10,8 @@ exponent in [-10, -4], canonicalised as hotarubi's compiler does), FP32 C
 [64, 960].  --config c1 runs BASELINE configs[0]'s W8 GEMM (64 x 960 -> 2560,
 per-channel int8 weights placed as hotarubi's compiler places a float
 matrix, with bias); --config c5 one large-M MXFP4 GEMM of the configs[4]
-sweep (4096 x 4096 x 4096), tensor-bound.
+sweep (4096 x 4096 x 4096), tensor-bound; --config c5conv the configs[4]
+conv (3x3, 256 -> 256 channels, 48 maps of 16 x 44) as an implicit GEMM.
 
 One step = the hot path over one batch of B independent instances of the
 GEMM, each with its own activations, weights and output (C2: B = 128, 282 MB
@@ -107,6 +108,46 @@ WORKLOADS = {
     "c4": Workload("c4", "c4_mxfp8_1600x720x2048", "C4 1600x720x2048", 2, 1600, 2048, 720,
                    False, 16, "tensor"),
 }
+
+
+@dataclasses.dataclass(frozen=True)
+class ConvWorkload:
+    """The C5 conv (3x3, 256 -> 256 channels, 16 x 44 maps,
+    6 cameras x batch 8), MXFP4 weights, bias, FP32 NHWC input."""
+    key: str = "c5conv"
+    name: str = "c5_conv3x3_48x16x44x256_mxfp4"
+    images: int = 48
+    H: int = 16
+    W: int = 44
+    cin: int = 256
+    cout: int = 256
+    kh: int = 3
+    stride: int = 1
+    wfmt: int = 0
+    instances: int = 3   # rotated per step: 3 x ~190 MB > 2 x L2
+
+    @property
+    def M(self) -> int:
+        return self.images * (self.H // self.stride) * (self.W // self.stride)
+
+    @property
+    def K(self) -> int:
+        return self.kh * self.kh * self.cin
+
+    @property
+    def flops(self) -> int:
+        return 2 * self.M * self.cout * self.K
+
+    @property
+    def metric(self) -> str:
+        return "MXFP4 implicit-GEMM conv TFLOP/s (C5 conv 3x3 256->256, 48 x 16x44)"
+
+    def bytes_step(self) -> int:
+        return (self.images * self.H * self.W * self.cin * 4 + self.cout * self.K // 2
+                + self.cout * self.K // 32 + self.cout * 4 + self.M * self.cout * 4)
+
+
+CONV = ConvWorkload()
 
 
 def peaks() -> dict:
@@ -499,6 +540,194 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
         dist.destroy_process_group()
 
 
+def conv_operands(cw: ConvWorkload, i: int):
+    from hotarubi_b200 import workloads
+    x = workloads.activations(500 + i, cw.images * cw.H * cw.W, cw.cin)
+    w, ws = workloads.mxfp4_weights(600 + i, cw.cout, cw.K)
+    b = workloads.bias(700 + i, cw.cout)
+    return x, w, ws, b
+
+
+def conv_cpu_reference(cw: ConvWorkload, min_seconds: float = 2.0) -> dict:
+    """The conv lowered as ConvEmitter lowers it and run on the reference's
+    own DMA engine and ExecuteGemm (oracle/_ref hrbref_conv_iss, one thread),
+    on one image of the batch."""
+    from oracle import cpu
+    ref = cpu.ref()
+    x, w, ws, b = conv_operands(cw, 0)
+    hw = cw.H * cw.W
+    # One image, x-major as the compiler's maps are (the conv is the same).
+    img = x[:hw].reshape(cw.H, cw.W, cw.cin).transpose(1, 0, 2).reshape(hw, cw.cin)
+    q, s = cpu.encode_mxint8(np.ascontiguousarray(img).view(np.uint32))
+    codes = np.zeros((cw.cout, cw.K), np.uint8)
+    codes[:, 0::2] = w & 0xF
+    codes[:, 1::2] = w >> 4
+    e = ws.astype(np.int32) - 127
+    flops = 2 * hw // (cw.stride * cw.stride) * cw.cout * cw.K
+    c = np.zeros((hw // (cw.stride * cw.stride), cw.cout), np.uint32)
+    if ref is None:
+        t0 = time.perf_counter()
+        cpu.conv_dense(cw.wfmt, q, s, 1, cw.H, cw.W, cw.cin, cw.cout, cw.kh, cw.stride, w, ws,
+                       bias_bits=b.view(np.uint32))
+        dt = time.perf_counter() - t0
+        return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+                "sample": "1 of 48 images on 1 thread", "seconds": dt}
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < 1 or time.perf_counter() - t0 < min_seconds:
+        ref.hrbref_conv_iss(cw.H, cw.W, cw.cin, cw.cout, cw.kh, cw.stride, q.ravel(), s.ravel(),
+                            codes.ravel(), e.ravel(), b.view(np.uint32), None, 0, c.ravel())
+        reps += 1
+    dt = time.perf_counter() - t0
+    return {"value": reps * flops / dt / 1e12, "unit": "TFLOP/s", "cores": 1,
+            "kind": "reference",
+            "sample": f"{reps} x 1 of 48 images through the reference's DMA gathers and "
+                      "ExecuteGemm on 1 thread", "seconds": dt}
+
+
+def run_conv(args, rank: int, world: int, local_rank: int) -> None:
+    """--config c5conv: the C5 conv through hrb_conv_plan_* (fast mode:
+    the FP32 map encoded once into operand blocks, the 3x3 taps' blocks
+    gathered per output row, the tcgen05 GEMM over K = 9 x 256).  One step = one conv over the 48 images; the
+    instances rotate so no step finds its operands in L2.  Replicas for
+    N > 1 (weak scaling)."""
+    import torch
+
+    from hotarubi_b200 import capi
+    cw = CONV
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        runs = [conv_cpu_reference(cw, 0.5) for _ in range(args.warmup + args.steps)]
+        runs = runs[args.warmup:]
+        value = statistics.median(r["value"] for r in runs)
+        base = runs[-1]
+        print(json.dumps({
+            "impl": "reference", "metric": cw.metric, "value": value, "unit": "TFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": statistics.median(r["seconds"] for r in runs) * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 block dot + fp32 accumulate", "data": "synthetic",
+            "config": {"workload": cw.name, "sample": base["sample"]},
+            "cpu_baseline": {k: v for k, v in base.items() if k != "seconds"} | {"value": value},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    lib = capi.Library(local_rank)
+    mode = capi.MODE_FAST if args.mode == "fast" else capi.MODE_EXACT
+    stream = torch.cuda.Stream()
+    lib.set_stream(stream.cuda_stream)
+    inst = []
+    for i in range(cw.instances):
+        x, w, ws, b = conv_operands(cw, i)
+        t = {"x": torch.from_numpy(x).cuda(), "w": torch.from_numpy(w).cuda(),
+             "ws": torch.from_numpy(ws).cuda(), "b": torch.from_numpy(b).cuda(),
+             "c": torch.zeros((cw.M, cw.cout), dtype=torch.float32, device="cuda")}
+        d = capi.conv_desc(cw.wfmt, cw.images, cw.H, cw.W, cw.cin, cw.cout, cw.kh, cw.stride,
+                           order=capi.CONV_YMAJOR, a=t["x"], w=t["w"], wscale=t["ws"],
+                           bias=t["b"], c=t["c"], mode=mode)
+        t["plan"] = lib.conv_plan(d)
+        inst.append(t)
+    torch.cuda.synchronize()
+    kernel_ms = inst[0]["plan"].profile(reps=10, stream=stream.cuda_stream)
+    gemm_ms = kernel_ms[-1] if mode == capi.MODE_FAST else max(kernel_ms)
+    prep_ms = sum(kernel_ms) - gemm_ms
+    if dist is not None:
+        dist.barrier()
+    with ClockSampler(local_rank) as clocks:
+        for i in range(args.warmup):
+            inst[i % cw.instances]["plan"].run(stream.cuda_stream)
+        stream.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        launches = 0
+        for i in range(args.steps):
+            launches += inst[i % cw.instances]["plan"].run(stream.cuda_stream)
+        end.record(stream)
+        end.synchronize()
+        if dist is not None:
+            dist.barrier()
+    lib.sync()
+    ms = start.elapsed_time(end) / args.steps
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # End to end: the FP32 map from pinned host memory, the conv, C back.
+    e2e = None
+    if not args.no_e2e:
+        xh = torch.from_numpy(conv_operands(cw, 0)[0]).pin_memory()
+        ch = torch.empty((cw.M, cw.cout), dtype=torch.float32).pin_memory()
+        t0 = inst[0]
+        n_e2e = max(1, min(args.steps, 10))
+        for k in range(2 + n_e2e):
+            if k == 2:
+                stream.synchronize()
+                w0 = time.perf_counter()
+            with torch.cuda.stream(stream):
+                t0["x"].copy_(xh, non_blocking=True)
+                t0["plan"].run(stream.cuda_stream)
+                ch.copy_(t0["c"], non_blocking=True)
+            stream.synchronize()
+        dt = (time.perf_counter() - w0) / n_e2e
+        e2e = {"value": world * cw.flops / dt / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": world * xh.numel() * 4,
+               "d2h_bytes_per_step": world * ch.numel() * 4, "ms_per_step": dt * 1e3,
+               "entry_point": "pinned copies + hrb_conv_plan_run (weights resident)"}
+    if rank == 0:
+        pk = peaks()
+        tflops = cw.flops / (gemm_ms / 1e3) / 1e12
+        peak = pk["bf16_tflops"] * 4.0 / 3.0
+        line = {
+            "metric": cw.metric, "value": world * cw.flops / (ms / 1e3) / 1e12,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 block dot + fp32 accumulate", "data": "synthetic",
+            "config": {"workload": cw.name, "M": cw.M, "N": cw.cout, "K": cw.K,
+                       "images": cw.images, "map": f"{cw.H}x{cw.W}x{cw.cin}",
+                       "kernel": f"{cw.kh}x{cw.kh}", "format": "mxfp4", "bias": True,
+                       "mode": args.mode, "activations": "fp32 NHWC map, encoded and gathered "
+                                                         "on device each step",
+                       "l2": f"{cw.instances} instances rotated, ~"
+                             f"{cw.instances * (cw.bytes_step() + cw.M * cw.K * 1.5) / 1e6:.0f}"
+                             " MB > 2 x 126 MB L2",
+                       "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "tensor", "kernel": "k_gemm_mxf4" if mode == capi.MODE_FAST
+                         else "k_dense_exact", "achieved": tflops, "peak": peak,
+                         "unit": "TFLOP/s", "frac": tflops / peak,
+                         "peak_source": pk["source"] + " (cuBLAS BF16 x 4/3: FP4 MMA rate over "
+                                                       "three digit planes)",
+                         "alg_flops_per_launch": cw.flops, "traffic": None,
+                         "launch_ms": gemm_ms},
+            "encoder": {"kernels": "k_quantize_planes (map) + k_conv_gather_tiles"
+                                   if mode == capi.MODE_FAST else "encoder + im2col",
+                        "launch_ms": prep_ms, "per_kernel_ms": kernel_ms},
+            "e2e": e2e, "gpu_launches": launches, "clocks": clocks.summary(),
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = {k: v for k, v in conv_cpu_reference(cw).items()
+                                    if k != "seconds"}
+        print(json.dumps(line), flush=True)
+    for t in inst:
+        t["plan"].close()
+    lib.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_shard(args, wl: Workload, rank: int, world: int, local_rank: int) -> None:
     """--shard: the batch's GEMMs split along N over the ranks (strong
     scaling: the total work is fixed); every rank's kernel also stores its
@@ -600,7 +829,7 @@ def main() -> None:
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", choices=sorted(WORKLOADS), default="c2")
+    p.add_argument("--config", choices=sorted(WORKLOADS) + [CONV.key], default="c2")
     p.add_argument("--mode", choices=["exact", "fast"], default="fast")
     p.add_argument("--batch", type=int, default=0, help="GEMMs per step per GPU (0: the "
                    "config's default)")
@@ -610,10 +839,13 @@ def main() -> None:
     p.add_argument("--shard", action="store_true", help="split each GEMM along N over the "
                    "ranks, with the all-gather fused into the kernel (strong scaling)")
     args = p.parse_args()
-    wl = WORKLOADS[args.config]
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.config == CONV.key:
+        run_conv(args, rank, world, local_rank)
+        return
+    wl = WORKLOADS[args.config]
     if args.impl == "reference":
         run_reference(args, wl, rank, world)
     elif args.shard:

@@ -59,6 +59,25 @@ class GemmDesc(ctypes.Structure):
     ]
 
 
+class ConvDesc(ctypes.Structure):
+    """hrb_conv_desc."""
+    _fields_ = [
+        ("wfmt", ctypes.c_uint32), ("mode", ctypes.c_uint32),
+        ("images", ctypes.c_uint32), ("H", ctypes.c_uint32), ("W", ctypes.c_uint32),
+        ("cin", ctypes.c_uint32), ("cout", ctypes.c_uint32),
+        ("kh", ctypes.c_uint32), ("stride", ctypes.c_uint32), ("order", ctypes.c_uint32),
+        ("a", ctypes.c_void_p), ("quant", ctypes.c_uint32),
+        ("aq", ctypes.c_void_p), ("ascale", ctypes.c_void_p),
+        ("w", ctypes.c_void_p), ("wscale", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p), ("c", ctypes.c_void_p),
+        ("accumulate", ctypes.c_uint32), ("relu", ctypes.c_uint32),
+        ("cq", ctypes.c_void_p), ("cscale", ctypes.c_void_p), ("cquant", ctypes.c_uint32),
+    ]
+
+
+CONV_XMAJOR, CONV_YMAJOR = 0, 1
+
+
 def header_functions() -> list[str]:
     """Every function include/hrb_gemm.h declares."""
     text = open(HEADER).read()
@@ -109,6 +128,13 @@ def load() -> ctypes.CDLL:
             "hrb_abuf_to_dense": (ctypes.c_int, [P, P, u32, u32, P, P, P]),
             "hrb_t32_split8_dense": (ctypes.c_int, [P, P, P, u32, u32, u32, P, P, P]),
             "hrb_dense_to_fbuf": (ctypes.c_int, [P, P, u32, u32, P, P]),
+            "hrb_conv_dense": (ctypes.c_int, [P, ctypes.POINTER(ConvDesc), P]),
+            "hrb_conv_plan_create": (ctypes.c_int, [P, ctypes.POINTER(ConvDesc),
+                                                    ctypes.POINTER(P)]),
+            "hrb_conv_plan_run": (ctypes.c_int, [P, P, ctypes.POINTER(u32)]),
+            "hrb_conv_plan_destroy": (ctypes.c_int, [P]),
+            "hrb_conv_plan_profile": (ctypes.c_int, [P, P, u32, ctypes.POINTER(ctypes.c_float),
+                                                     u32, ctypes.POINTER(u32)]),
             "hrb_shared_alloc": (ctypes.c_int, [P, ctypes.c_size_t, ctypes.POINTER(P),
                                                 ctypes.POINTER(IpcHandle)]),
             "hrb_shared_free": (ctypes.c_int, [P, P]),
@@ -311,9 +337,62 @@ class Library:
                                                   hd if ldv is None else ldv, _ptr(wq),
                                                   _ptr(wscale), stream or None))
 
+    def conv(self, d: ConvDesc, stream: int = 0) -> None:
+        self._check(self.lib.hrb_conv_dense(self.ctx, ctypes.byref(d), stream or None))
+
+    def conv_plan(self, d: ConvDesc) -> ConvPlan:
+        return ConvPlan(self, d)
+
     def dense_to_fbuf(self, c, rows, cols, words, stream=0):
         self._check(self.lib.hrb_dense_to_fbuf(self.ctx, _ptr(c), rows, cols, _ptr(words),
                                                stream or None))
+
+
+def conv_desc(wfmt, images, H, W, cin, cout, kh, stride, *, order=CONV_XMAJOR, a=None,
+              quant=QUANT_HOST, aq=None, ascale=None, w=None, wscale=None, bias=None, c=None,
+              accumulate=False, relu=False, mode=MODE_EXACT, cq=None, cscale=None,
+              cquant=QUANT_VEC) -> ConvDesc:
+    d = ConvDesc()
+    d.wfmt, d.mode = wfmt, mode
+    d.images, d.H, d.W, d.cin, d.cout, d.kh, d.stride, d.order = (
+        images, H, W, cin, cout, kh, stride, order)
+    d.a, d.quant = _ptr(a), quant
+    d.aq, d.ascale = _ptr(aq), _ptr(ascale)
+    d.w, d.wscale = _ptr(w), _ptr(wscale)
+    d.bias, d.c = _ptr(bias), _ptr(c)
+    d.accumulate = 1 if accumulate else 0
+    d.relu = 1 if relu else 0
+    d.cq, d.cscale, d.cquant = _ptr(cq), _ptr(cscale), cquant
+    return d
+
+
+class ConvPlan:
+    def __init__(self, owner: "Library", desc: ConvDesc):
+        self.owner = owner
+        self.desc = desc
+        h = ctypes.c_void_p()
+        owner._check(owner.lib.hrb_conv_plan_create(owner.ctx, ctypes.byref(desc),
+                                                    ctypes.byref(h)))
+        self.handle = h
+
+    def run(self, stream: int = 0) -> int:
+        n = ctypes.c_uint32()
+        self.owner._check(self.owner.lib.hrb_conv_plan_run(self.handle, stream or None,
+                                                           ctypes.byref(n)))
+        return n.value
+
+    def profile(self, reps: int = 20, stream: int = 0) -> list[float]:
+        """Mean ms of each launch of a run (hrb_conv_plan_profile)."""
+        ms = (ctypes.c_float * 8)()
+        n = ctypes.c_uint32()
+        self.owner._check(self.owner.lib.hrb_conv_plan_profile(self.handle, stream or None, reps,
+                                                               ms, 8, ctypes.byref(n)))
+        return [ms[i] for i in range(n.value)]
+
+    def close(self) -> None:
+        if self.handle:
+            self.owner.lib.hrb_conv_plan_destroy(self.handle)
+            self.handle = None
 
 
 class Plan:

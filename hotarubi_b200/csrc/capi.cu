@@ -43,6 +43,12 @@ struct hrb_ctx {
   uint32_t* d_error = nullptr;
 };
 
+struct hrb_conv_plan {
+  hrb_ctx* ctx = nullptr;
+  hrb_conv_desc desc{};
+  void* d_scratch = nullptr;
+};
+
 struct hrb_plan {
   hrb_ctx* ctx = nullptr;
   void* d_jobs = nullptr;   // QuantJobs then DenseJobs
@@ -285,6 +291,22 @@ size_t tc_scratch_bytes(const hrb_gemm_desc* d) {
   return align_up(tc_act_bytes(d), 1024) + align_up(tc_weight_bytes(d), 1024);
 }
 
+// The encoder job writing the tensor-core operand blocks of an M x K FP32
+// activation matrix (layout of hrb_tc.cuh for the weight format's kind).
+hrb::QuantJob tc_quant_job(const float* a, uint32_t M, uint32_t K, uint32_t lda, uint32_t quant,
+                           uint32_t wfmt, uint8_t* tiles) {
+  const bool f8 = wfmt == HRB_WFMT_MXFP8;
+  hrb::QuantJob j = make_quant_job(a, M, K, lda, quant, nullptr, nullptr);
+  j.tiles = tiles;
+  j.tiles_kind = f8 ? 3 : 2;
+  j.tile_rows = hrb::mx_tokens_per_tile(M);
+  j.k_steps = hrb::mx_steps_of(wfmt, blocks_of(K));
+  j.cover_blocks = (f8 ? 4u : 8u) * j.k_steps;
+  // Encoder units: (row, 256 elements), i.e. one E2M1 step or two E4M3 steps.
+  j.units = static_cast<uint64_t>(j.rows) * (f8 ? (j.k_steps + 1u) / 2u : j.k_steps);
+  return j;
+}
+
 // Fills the encoder job and the tensor-core job of one GEMM whose prepared
 // operands live at `base` (tc_scratch_bytes of them).  Every weight format
 // takes the block-scaled kernel with no decode in it: MXFP4 codes and W8
@@ -293,15 +315,7 @@ void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJo
   const uint32_t kb = blocks_of(d->K);
   uint8_t* act = base;
   uint8_t* wt = base + align_up(tc_act_bytes(d), 1024);
-  const bool f8 = d->wfmt == HRB_WFMT_MXFP8;
-  *qj = make_quant_job(d->a, d->M, d->K, d->lda, d->quant, nullptr, nullptr);
-  qj->tiles = act;
-  qj->tiles_kind = f8 ? 3 : 2;
-  qj->tile_rows = hrb::mx_tokens_per_tile(d->M);
-  qj->k_steps = hrb::mx_steps_of(d->wfmt, kb);
-  qj->cover_blocks = (f8 ? 4u : 8u) * qj->k_steps;
-  // Encoder units: (row, 256 elements), i.e. one E2M1 step or two E4M3 steps.
-  qj->units = static_cast<uint64_t>(qj->rows) * (f8 ? (qj->k_steps + 1u) / 2u : qj->k_steps);
+  *qj = tc_quant_job(d->a, d->M, d->K, d->lda, d->quant, d->wfmt, act);
   *tj = hrb::TcJob{};
   tj->wfmt = d->wfmt;
   tj->M = d->M;
@@ -325,6 +339,257 @@ void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJo
 void tc_translate(const hrb_gemm_desc* d, const hrb::TcJob& tj, cudaStream_t s) {
   hrb::launch_tile_weights_mxf4(d->wfmt, d->w, d->wscale, d->N, blocks_of(d->K),
                                 const_cast<uint8_t*>(tj.w_tiles), s);
+}
+
+// ---------------------------------------------------------------------------
+// Convolutions: one GEMM with gathered activation rows (conv.cu).
+
+struct ConvRun {
+  hrb::ConvGeom g{};
+  uint32_t M = 0, N = 0, K = 0;
+  bool tc = false;       // HRB_MODE_FAST with FP32 input: the tensor cores
+  bool reorder = false;  // more than one channel plane: weights reordered
+  uint32_t bpb = 16;     // weight bytes per K block
+  uint32_t npieces = 0;  // K pieces of the exact chain (W8: one per (plane, tap) job)
+  uint32_t pieces[hrb::kMaxPieces];
+  // Scratch, as offsets from the run's base.
+  size_t o_w = 0, o_ws = 0;      // reordered weights and scales
+  size_t o_map = 0, o_maps = 0;  // exact path, FP32 input: the MXINT8 map
+  size_t o_aq = 0, o_as = 0;     // exact path: the gathered MXINT8 rows
+  size_t o_tc = 0;               // tensor cores: activation tiles, weight chunks
+  size_t o_mt = 0;               // tensor cores: the input map's own operand blocks
+  size_t bytes = 0;
+};
+
+// The GEMM a convolution runs: M output positions x cout x K gathered.
+hrb_gemm_desc conv_gemm(const hrb_conv_desc* d, const ConvRun& r, uint8_t* base) {
+  hrb_gemm_desc g{};
+  g.wfmt = d->wfmt;
+  g.mode = d->mode;
+  g.M = r.M;
+  g.N = r.N;
+  g.K = r.K;
+  g.quant = d->quant;
+  if (r.tc) {
+    g.a = d->a;
+    g.lda = r.K;
+  } else {
+    g.aq = reinterpret_cast<const int8_t*>(base + r.o_aq);
+    g.ascale = base + r.o_as;
+  }
+  g.w = r.reorder ? base + r.o_w : d->w;
+  g.wscale = r.reorder ? base + r.o_ws : d->wscale;
+  g.bias = d->bias;
+  g.c = d->c;
+  g.ldc = r.N;
+  g.accumulate = d->accumulate;
+  g.pieces = r.npieces != 0 ? r.pieces : nullptr;
+  g.npieces = r.npieces;
+  g.cq = d->cq;
+  g.cscale = d->cscale;
+  g.cquant = d->cquant;
+  return g;
+}
+
+hrb_status check_conv(hrb_ctx* ctx, const hrb_conv_desc* d, ConvRun* r) {
+  if (d == nullptr) return fail(ctx, HRB_EINVAL, "null conv descriptor");
+  if (d->wfmt > HRB_WFMT_MXFP8) return fail(ctx, HRB_EINVAL, "unknown weight format %u", d->wfmt);
+  if (d->mode > HRB_MODE_FAST) return fail(ctx, HRB_EINVAL, "unknown mode %u", d->mode);
+  if (d->kh != 1 && d->kh != 3) {
+    return fail(ctx, HRB_EINVAL, "conv with a %ux%u kernel (1x1 and 3x3 only)", d->kh, d->kh);
+  }
+  if (d->stride != 1 && d->stride != 2) {
+    return fail(ctx, HRB_EINVAL, "conv with stride %u (1 and 2 only)", d->stride);
+  }
+  if (d->order > HRB_CONV_YMAJOR) return fail(ctx, HRB_EINVAL, "unknown position order %u", d->order);
+  if (d->images == 0 || d->H / d->stride == 0 || d->W / d->stride == 0 || d->cout == 0) {
+    return fail(ctx, HRB_EINVAL, "empty conv");
+  }
+  // MakeMap's rule (sparsedrive_common.cpp:49-51).
+  if (d->cin == 0 || d->cin % 32u != 0 || (d->cin > 256u && d->cin % 256u != 0)) {
+    return fail(ctx, HRB_EINVAL, "feature map of %ux%ux%u is not supported", d->H, d->W, d->cin);
+  }
+  if (d->a != nullptr) {
+    if (d->aq != nullptr || d->ascale != nullptr) {
+      return fail(ctx, HRB_EINVAL, "give either an FP32 map or an MXINT8 one, not both");
+    }
+    if (d->quant > HRB_QUANT_VEC) return fail(ctx, HRB_EINVAL, "unknown quantizer %u", d->quant);
+    if (!aligned(d->a, 16)) return fail(ctx, HRB_EINVAL, "the FP32 map is not 16-byte aligned");
+  } else {
+    if (d->aq == nullptr || d->ascale == nullptr) return fail(ctx, HRB_EINVAL, "no input map");
+    if (!aligned(d->aq, 16)) return fail(ctx, HRB_EINVAL, "the MXINT8 map is not 16-byte aligned");
+  }
+  if (d->w == nullptr || d->wscale == nullptr) {
+    return fail(ctx, HRB_EINVAL, "missing weights or weight scales");
+  }
+  if (!aligned(d->w, 16)) return fail(ctx, HRB_EINVAL, "weights are not 16-byte aligned");
+  if ((d->cq == nullptr) != (d->cscale == nullptr)) {
+    return fail(ctx, HRB_EINVAL, "give both MXINT8 output codes and scales, or neither");
+  }
+  if (d->cq != nullptr && d->cquant > HRB_QUANT_VEC) {
+    return fail(ctx, HRB_EINVAL, "unknown output quantizer %u", d->cquant);
+  }
+  const bool tc = d->mode == HRB_MODE_FAST && d->a != nullptr;
+  if (d->c == nullptr && (d->cq == nullptr || !tc || d->accumulate)) {
+    return fail(ctx, HRB_EINVAL, "missing output (an MXINT8-only output needs HRB_MODE_FAST, "
+                                 "an FP32 map and no accumulate)");
+  }
+  ConvRun& x = *r;
+  x = ConvRun{};
+  const uint32_t plane = d->cin < 256u ? d->cin : 256u;
+  x.g = hrb::ConvGeom{d->images, d->H,  d->W,      d->H / d->stride, d->W / d->stride,
+                      d->cin,    d->kh, d->stride, d->order,         plane / 32u};
+  const uint64_t M = uint64_t{d->images} * x.g.Ho * x.g.Wo;
+  const uint64_t K = uint64_t{d->kh} * d->kh * d->cin;
+  if (M > (1u << 30) || K > (1u << 20)) return fail(ctx, HRB_EINVAL, "conv too large");
+  x.M = static_cast<uint32_t>(M);
+  x.N = d->cout;
+  x.K = static_cast<uint32_t>(K);
+  x.tc = tc;
+  x.reorder = d->cin > 256u;
+  x.bpb = d->wfmt == HRB_WFMT_MXFP4 ? 16u : 32u;
+  const uint32_t jobs = (d->cin / plane) * d->kh * d->kh;
+  if (d->wfmt == HRB_WFMT_W8 && !tc) {
+    // W8 chains HI then LO per (plane, tap) job (kernels.cpp:35-37).
+    if (jobs > hrb::kMaxPieces) {
+      return fail(ctx, HRB_EINVAL, "W8 conv with %u (plane, tap) jobs (at most %u)", jobs,
+                  hrb::kMaxPieces);
+    }
+    x.npieces = jobs;
+    for (uint32_t i = 0; i < jobs; ++i) x.pieces[i] = x.g.bp;
+  } else {
+    x.npieces = 1;  // one plane of weights: the chain is the same in any split
+    x.pieces[0] = x.K / 32u;
+  }
+  const size_t kb = K / 32u;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 1024);
+    return o;
+  };
+  if (x.reorder) {
+    x.o_w = take(size_t{x.N} * kb * x.bpb);
+    x.o_ws = take(size_t{x.N} * kb);
+  }
+  if (tc) {
+    const hrb_gemm_desc g = conv_gemm(d, x, nullptr);
+    x.o_tc = take(tc_scratch_bytes(&g));
+    x.o_mt = take(hrb::mx_act_bytes(d->wfmt, d->images * d->H * d->W, d->cin / 32u));
+  } else {
+    if (d->a != nullptr) {
+      const size_t positions = size_t{d->images} * d->H * d->W;
+      x.o_map = take(positions * d->cin);
+      x.o_maps = take(positions * (d->cin / 32u));
+    }
+    x.o_aq = take(size_t{x.M} * kb * 32u);
+    x.o_as = take(size_t{x.M} * kb);
+  }
+  x.bytes = off;
+  return HRB_OK;
+}
+
+// Launches that depend on the weights only: the reorder and, on the tensor
+// cores, the translation into chunks (plus zeroing the activation tiles,
+// whose rows past M are never written).
+hrb_status conv_prepare(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, uint8_t* base,
+                        cudaStream_t s, uint32_t* launched) {
+  if (r.reorder) {
+    hrb::launch_conv_weights(d->w, d->wscale, r.N, r.g, r.bpb, base + r.o_w, base + r.o_ws, s);
+    *launched += 1;
+  }
+  if (r.tc) {
+    const hrb_gemm_desc g = conv_gemm(d, r, base);
+    hrb::QuantJob qj;
+    hrb::TcJob tj;
+    tc_jobs(&g, base + r.o_tc, &qj, &tj);
+    HRB_CUDA(ctx, cudaMemsetAsync(base + r.o_tc, 0, align_up(tc_act_bytes(&g), 1024), s));
+    tc_translate(&g, tj, s);
+    *launched += 1;
+  }
+  HRB_CUDA(ctx, cudaGetLastError());
+  return HRB_OK;
+}
+
+// The convolution proper, once prepared.  With `only` >= 0 just that launch
+// of the sequence (a profiling aid, as hrb_plan_profile's).
+hrb_status conv_execute(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, uint8_t* base,
+                        cudaStream_t s, uint32_t* launched, int only = -1) {
+  const hrb_gemm_desc g = conv_gemm(d, r, base);
+  int index = 0;
+  auto take = [&]() { return only < 0 || index++ == only; };
+  if (r.tc) {
+    // The map encoded once into operand blocks, the GEMM's blocks gathered
+    // from them, then the GEMM.
+    hrb::QuantJob qj;
+    hrb::TcJob tj;
+    tc_jobs(&g, base + r.o_tc, &qj, &tj);
+    tj.relu = d->relu != 0;
+    const hrb::QuantJob mj = tc_quant_job(d->a, d->images * d->H * d->W, d->cin, d->cin,
+                                          d->quant, d->wfmt, base + r.o_mt);
+    if (take()) {
+      hrb::launch_quantize_planes(nullptr, 1, &mj, mj.units, ctx->d_error, ctx->sm_count, s);
+      *launched += 1;
+    }
+    if (take()) {
+      hrb::launch_conv_gather_tiles(base + r.o_mt, mj.tile_rows, mj.k_steps, base + r.o_tc,
+                                    qj.tile_rows, qj.k_steps, d->wfmt == HRB_WFMT_MXFP8, r.g, s);
+      *launched += 1;
+    }
+    if (take()) {
+      tj.tile_begin = 0;
+      const int n = hrb::launch_mxf4(nullptr, &tj, qj.tile_rows, d->wfmt, tj.m_tiles * tj.n_tiles,
+                                     ctx->sm_count, ctx->d_error, s);
+      if (n < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
+      *launched += static_cast<uint32_t>(n);
+    }
+    HRB_CUDA(ctx, cudaGetLastError());
+    return HRB_OK;
+  }
+  const int8_t* map = d->aq;
+  const uint8_t* maps = d->ascale;
+  if (d->a != nullptr) {
+    auto* q = reinterpret_cast<int8_t*>(base + r.o_map);
+    uint8_t* sc = base + r.o_maps;
+    if (take()) {
+      const hrb::QuantJob j = make_quant_job(d->a, d->images * d->H * d->W, d->cin, d->cin,
+                                             d->quant, q, sc);
+      hrb::launch_quantize(nullptr, 1, &j, j.units, ctx->d_error, ctx->sm_count, s);
+      *launched += 1;
+    }
+    map = q;
+    maps = sc;
+  }
+  if (take()) {
+    hrb::launch_conv_im2col(map, maps, r.g, reinterpret_cast<int8_t*>(base + r.o_aq),
+                            base + r.o_as, s);
+    *launched += 1;
+  }
+  if (take()) {
+    const uint64_t before = ctx->launches;
+    const hrb_status st =
+        run_dense(ctx, make_dense_job(&g, g.aq, g.ascale, r.pieces, r.npieces), s);
+    *launched += static_cast<uint32_t>(ctx->launches - before);
+    ctx->launches = before;
+    if (st != HRB_OK) return st;
+  }
+  if (d->relu && take()) {
+    hrb::launch_relu_exact(d->c, r.M, r.N, r.N, s);
+    *launched += 1;
+  }
+  if (d->cq != nullptr && take()) {
+    const hrb::QuantJob pq = post_quant_job(&g);
+    hrb::launch_quantize(nullptr, 1, &pq, pq.units, ctx->d_error, ctx->sm_count, s);
+    *launched += 1;
+  }
+  HRB_CUDA(ctx, cudaGetLastError());
+  return HRB_OK;
+}
+
+// Launches of one conv run (the sequence conv_execute walks).
+uint32_t conv_launches(const hrb_conv_desc* d, const ConvRun& r) {
+  if (r.tc) return 3;
+  return (d->a != nullptr ? 1u : 0u) + 2u + (d->relu ? 1u : 0u) + (d->cq != nullptr ? 1u : 0u);
 }
 
 // ABUF/WBUF/FBUF words a command touches: the circular span from `base` of
@@ -1311,6 +1576,123 @@ hrb_status hrb_t32_split8_dense(hrb_ctx* ctx, const int8_t* vq, const uint8_t* v
                          pick(ctx, stream));
   ctx->launches += 1;
   HRB_CUDA(ctx, cudaGetLastError());
+  return HRB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Convolutions
+
+hrb_status hrb_conv_dense(hrb_ctx* ctx, const hrb_conv_desc* d, void* stream) {
+  if (ctx == nullptr) return HRB_EINVAL;
+  ConvRun r;
+  hrb_status st = check_conv(ctx, d, &r);
+  if (st != HRB_OK) return st;
+  HRB_CUDA(ctx, cudaSetDevice(ctx->device));
+  cudaStream_t s = pick(ctx, stream);
+  st = grow(ctx, &ctx->scratch, &ctx->scratch_bytes, r.bytes);
+  if (st != HRB_OK) return st;
+  auto* base = static_cast<uint8_t*>(ctx->scratch);
+  uint32_t launched = 0;
+  st = conv_prepare(ctx, d, r, base, s, &launched);
+  if (st == HRB_OK) st = conv_execute(ctx, d, r, base, s, &launched);
+  ctx->launches += launched;
+  return st;
+}
+
+hrb_status hrb_conv_plan_create(hrb_ctx* ctx, const hrb_conv_desc* d, hrb_conv_plan** out) {
+  if (ctx == nullptr || out == nullptr) return HRB_EINVAL;
+  *out = nullptr;
+  ConvRun r;
+  hrb_status st = check_conv(ctx, d, &r);
+  if (st != HRB_OK) return st;
+  HRB_CUDA(ctx, cudaSetDevice(ctx->device));
+  auto* plan = new hrb_conv_plan;
+  plan->ctx = ctx;
+  plan->desc = *d;
+  if (r.bytes != 0) {
+    const cudaError_t e = cudaMalloc(&plan->d_scratch, r.bytes);
+    if (e != cudaSuccess) {
+      delete plan;
+      return cuda_fail(ctx, e, "cudaMalloc");
+    }
+  }
+  uint32_t launched = 0;
+  st = conv_prepare(ctx, d, r, static_cast<uint8_t*>(plan->d_scratch), ctx->stream, &launched);
+  if (st == HRB_OK) {
+    const cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) st = cuda_fail(ctx, e, "conv plan preparation");
+  }
+  ctx->launches += launched;
+  if (st != HRB_OK) {
+    cudaFree(plan->d_scratch);
+    delete plan;
+    return st;
+  }
+  *out = plan;
+  return HRB_OK;
+}
+
+hrb_status hrb_conv_plan_run(hrb_conv_plan* plan, void* stream, uint32_t* launched) {
+  if (plan == nullptr) return HRB_EINVAL;
+  hrb_ctx* ctx = plan->ctx;
+  ConvRun r;
+  hrb_status st = check_conv(ctx, &plan->desc, &r);
+  if (st != HRB_OK) return st;
+  HRB_CUDA(ctx, cudaSetDevice(ctx->device));
+  uint32_t n = 0;
+  st = conv_execute(ctx, &plan->desc, r, static_cast<uint8_t*>(plan->d_scratch),
+                    pick(ctx, stream), &n);
+  ctx->launches += n;
+  if (launched != nullptr) *launched = n;
+  return st;
+}
+
+hrb_status hrb_conv_plan_profile(hrb_conv_plan* plan, void* stream, uint32_t reps, float* ms,
+                                 uint32_t cap, uint32_t* nkernels) {
+  if (plan == nullptr || ms == nullptr || nkernels == nullptr || reps == 0 || cap == 0) {
+    return HRB_EINVAL;
+  }
+  hrb_ctx* ctx = plan->ctx;
+  ConvRun r;
+  hrb_status st = check_conv(ctx, &plan->desc, &r);
+  if (st != HRB_OK) return st;
+  HRB_CUDA(ctx, cudaSetDevice(ctx->device));
+  cudaStream_t s = pick(ctx, stream);
+  auto* base = static_cast<uint8_t*>(plan->d_scratch);
+  const uint32_t steps = std::min(conv_launches(&plan->desc, r), cap);
+  cudaEvent_t ev[2];
+  HRB_CUDA(ctx, cudaEventCreate(&ev[0]));
+  HRB_CUDA(ctx, cudaEventCreate(&ev[1]));
+  uint32_t n = 0;
+  st = conv_execute(ctx, &plan->desc, r, base, s, &n);
+  for (uint32_t i = 0; i < steps && st == HRB_OK; ++i) {
+    st = conv_execute(ctx, &plan->desc, r, base, s, &n, static_cast<int>(i));  // warm
+    if (st == HRB_OK && cudaEventRecord(ev[0], s) != cudaSuccess) st = HRB_ECUDA;
+    for (uint32_t k = 0; k < reps && st == HRB_OK; ++k) {
+      st = conv_execute(ctx, &plan->desc, r, base, s, &n, static_cast<int>(i));
+    }
+    if (st == HRB_OK && cudaEventRecord(ev[1], s) != cudaSuccess) st = HRB_ECUDA;
+    float t = 0;
+    if (st == HRB_OK && (cudaEventSynchronize(ev[1]) != cudaSuccess ||
+                         cudaEventElapsedTime(&t, ev[0], ev[1]) != cudaSuccess)) {
+      st = HRB_ECUDA;
+    }
+    ms[i] = t / static_cast<float>(reps);
+  }
+  cudaEventDestroy(ev[0]);
+  cudaEventDestroy(ev[1]);
+  ctx->launches += n;
+  if (st != HRB_OK) return st == HRB_ECUDA ? fail(ctx, st, "profiling run failed") : st;
+  *nkernels = steps;
+  return HRB_OK;
+}
+
+hrb_status hrb_conv_plan_destroy(hrb_conv_plan* plan) {
+  if (plan == nullptr) return HRB_OK;
+  cudaSetDevice(plan->ctx->device);
+  cudaStreamSynchronize(plan->ctx->stream);
+  cudaFree(plan->d_scratch);
+  delete plan;
   return HRB_OK;
 }
 

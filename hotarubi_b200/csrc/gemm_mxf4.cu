@@ -140,8 +140,8 @@ __host__ __device__ inline MxTile make_tile(const TcJob& job, uint32_t nt, uint3
   t.rows = job.M - row0 < nt ? job.M - row0 : nt;
   t.cols_kbq = (job.N - col0 < kTileW ? job.N - col0 : kTileW) | (kbq << 8);
   t.ldc = job.ldc;
-  t.flags = job.k_steps | (job.cquant == HRB_QUANT_VEC ? 0x40000000u : 0u) |
-            (job.accumulate ? 0x80000000u : 0u);
+  t.flags = job.k_steps | (job.relu ? 0x20000000u : 0u) |
+            (job.cquant == HRB_QUANT_VEC ? 0x40000000u : 0u) | (job.accumulate ? 0x80000000u : 0u);
   return t;
 }
 
@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(MxCfg<NT, WP, KB>::kThreads, 1)
       for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
         const MxTile ti = next;
         if (tile + gridDim.x < p.total_tiles) next = tile_info<NT>(p, tile + gridDim.x);
-        const uint32_t k_steps = (ti.flags & 0x3FFFFFFFu);
+        const uint32_t k_steps = (ti.flags & 0x1FFFFFFFu);
         if (weights) {
           for (uint32_t c = 0; c < k_steps * WP && ok; ++c, ++n) {
             const uint32_t sl = n % ring.slots;
@@ -359,11 +359,11 @@ __global__ void __launch_bounds__(MxCfg<NT, WP, KB>::kThreads, 1)
     if (lane == 0) {
       uint32_t na = 0, nw = 0, t = 0;
       const uint32_t sfa = tmem + Cfg::kColSfa;
-      uint32_t next_steps = tile_info<NT>(p, blockIdx.x).flags & 0x3FFFFFFFu;
+      uint32_t next_steps = tile_info<NT>(p, blockIdx.x).flags & 0x1FFFFFFFu;
       for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++t) {
         const uint32_t k_steps = next_steps;
         if (tile + gridDim.x < p.total_tiles) {
-          next_steps = tile_info<NT>(p, tile + gridDim.x).flags & 0x3FFFFFFFu;
+          next_steps = tile_info<NT>(p, tile + gridDim.x).flags & 0x1FFFFFFFu;
         }
         const uint32_t b = t % Cfg::kDBufs;
         if (t >= Cfg::kDBufs) ok = mbar_wait(&acc_empty[b], ((t / Cfg::kDBufs) - 1) & 1u, p.err);
@@ -458,6 +458,7 @@ __global__ void __launch_bounds__(MxCfg<NT, WP, KB>::kThreads, 1)
       const uint32_t cols = ti.cols_kbq & 0xFFu, kbq = ti.cols_kbq >> 8;
       const bool col_ok = col < cols;
       const bool acc = (ti.flags >> 31) != 0;
+      const bool relu = ((ti.flags >> 29) & 1u) != 0;
       const float bias = (ti.bias != nullptr && col_ok) ? ti.bias[col] : 0.0f;
       float* cbase = ti.c + col;
       const uint32_t npeers = p.peers.count;
@@ -487,6 +488,7 @@ __global__ void __launch_bounds__(MxCfg<NT, WP, KB>::kThreads, 1)
             if (j0 + j < ti.rows) {
               if (acc) x[j] += cbase[static_cast<size_t>(j0 + j) * ti.ldc];
               x[j] += bias;
+              if (relu) x[j] = x[j] > 0.0f ? x[j] : 0.0f;
               if (ti.c != nullptr) cbase[static_cast<size_t>(j0 + j) * ti.ldc] = x[j];
             }
           }

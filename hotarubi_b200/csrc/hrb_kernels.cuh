@@ -10,6 +10,51 @@
 
 namespace hrb {
 
+// Geometry of a convolution run as a GEMM whose activation rows are
+// gathered (hotarubi's ConvEmitter, tools/compiler/sparsedrive_encoder.cpp):
+// output row img * Ho * Wo + o reads, for K column (plane, tap, channel in
+// plane), channel plane * 32 * bp + channel of the input position under tap
+// (ky, kx) = (tap / kh, tap % kh) with padding (kh - 1) / 2, or zero outside
+// the map.  Positions are x-major (order 0: x * H + y) or y-major (y * W + x).
+struct ConvGeom {
+  uint32_t images, H, W, Ho, Wo, cin, kh, stride, order;
+  uint32_t bp;      // K blocks per channel plane (min(cin, 256) / 32)
+};
+
+// Input position of output row `row` under tap `tap`, or -1 outside the map.
+__host__ __device__ inline int64_t conv_source_row(const ConvGeom& g, uint32_t row, uint32_t tap) {
+  const uint32_t out_per = g.Ho * g.Wo;
+  const uint32_t img = row / out_per, o = row - img * out_per;
+  uint32_t yo, xo;
+  if (g.order == 0) {
+    xo = o / g.Ho;
+    yo = o - xo * g.Ho;
+  } else {
+    yo = o / g.Wo;
+    xo = o - yo * g.Wo;
+  }
+  const uint32_t ky = tap / g.kh, kx = tap - ky * g.kh, pad = (g.kh - 1u) / 2u;
+  const int32_t yi = static_cast<int32_t>(g.stride * yo + ky) - static_cast<int32_t>(pad);
+  const int32_t xi = static_cast<int32_t>(g.stride * xo + kx) - static_cast<int32_t>(pad);
+  if (yi < 0 || yi >= static_cast<int32_t>(g.H) || xi < 0 || xi >= static_cast<int32_t>(g.W)) {
+    return -1;
+  }
+  const uint32_t pos = g.order == 0 ? static_cast<uint32_t>(xi) * g.H + static_cast<uint32_t>(yi)
+                                    : static_cast<uint32_t>(yi) * g.W + static_cast<uint32_t>(xi);
+  return static_cast<int64_t>(img) * g.H * g.W + pos;
+}
+
+// The (input row, input K block) of gathered K block `b` of output row `row`,
+// or -1 when it falls outside the map.
+__host__ __device__ inline int64_t conv_source_block(const ConvGeom& g, uint32_t row, uint32_t b,
+                                                     uint32_t* in_block) {
+  const uint32_t taps = g.kh * g.kh, per_plane = taps * g.bp;
+  const uint32_t plane = b / per_plane, rem = b - plane * per_plane;
+  const uint32_t tap = rem / g.bp, cb = rem - tap * g.bp;
+  *in_block = plane * g.bp + cb;
+  return conv_source_row(g, row, tap);
+}
+
 // One FP32 -> MXINT8 encode.  Units are (row, 128-column chunk) pairs;
 // `unit_begin` is the prefix sum over the jobs of a launch.
 struct QuantJob {
@@ -105,6 +150,23 @@ void launch_abuf_to_dense(const uint8_t* words, uint32_t quads, uint32_t kb, int
                           uint8_t* scales, cudaStream_t stream);
 void launch_dense_to_fbuf(const float* c, uint32_t rows, uint32_t cols, float* words,
                           cudaStream_t stream);
+
+// Convolution helpers (conv.cu): the gathered MXINT8 rows of the exact path,
+// the weight matrix reordered to the chain's (plane, tap, channel) order,
+// and the VEC RELU pass over an exact output.
+void launch_conv_im2col(const int8_t* aq, const uint8_t* ascale, const ConvGeom& g, int8_t* q,
+                        uint8_t* scale, cudaStream_t stream);
+void launch_conv_weights(const uint8_t* w, const uint8_t* ws, uint32_t N, const ConvGeom& g,
+                         uint32_t bytes_per_block, uint8_t* out_w, uint8_t* out_ws,
+                         cudaStream_t stream);
+void launch_relu_exact(float* c, uint32_t M, uint32_t N, uint32_t ldc, cudaStream_t stream);
+// The tensor-core path's gather: the conv GEMM's activation blocks (nt-row
+// tiles, `steps` K steps) assembled block by block from the input map's own
+// activation blocks (map_nt-row tiles, map_steps K steps), both in the
+// layout of hrb_tc.cuh (f8: the two-E4M3-plane layout, else three E2M1).
+void launch_conv_gather_tiles(const uint8_t* map_tiles, uint32_t map_nt, uint32_t map_steps,
+                              uint8_t* tiles, uint32_t nt, uint32_t steps, uint32_t f8,
+                              const ConvGeom& g, cudaStream_t stream);
 
 // T32_SPLIT8 in dense form (kv_operands.cu).
 void launch_t32_split8(const int8_t* vq, const uint8_t* vs, uint32_t tokens, uint32_t hd,

@@ -25,6 +25,7 @@ struct TcJob {
   int8_t* cq;              // MXINT8 copy of C [M][kpN] or null
   uint8_t* cscale;         // [M][kpN / 32]
   uint32_t cquant;         // hrb_quant of the copy
+  uint32_t relu;           // RELU after the bias (before the copy)
 };
 
 // The block-scaled tensor-core path (gemm_mxf4.cu): kind::mxf4 for MXFP4
@@ -92,7 +93,7 @@ struct MxTile {
   uint32_t rows;        // valid token rows
   uint32_t cols_kbq;    // valid weight columns | blocks per cq row << 8
   uint32_t ldc;
-  uint32_t flags;       // K steps | VEC rule for cq << 30 | accumulate << 31
+  uint32_t flags;       // K steps | RELU << 29 | VEC rule for cq << 30 | accumulate << 31
 };
 static_assert(sizeof(MxTile) == 64, "MxTile is read as four 16-byte loads");
 // The m_tiles * n_tiles tiles of one job (tile index mt * n_tiles + nt).

@@ -315,7 +315,80 @@ HRB_API hrb_status hrb_dense_to_fbuf(hrb_ctx* ctx, const float* c, uint32_t rows
                              uint32_t cols, float* words, void* stream);
 
 /* ---------------------------------------------------------------------
- * 5. Column-sharded GEMMs over the GPUs of one node (one process per GPU).
+ * 5. Convolutions as hotarubi's compiler lowers them (ConvEmitter,
+ *    tools/compiler/sparsedrive_encoder.cpp:78-168,384-428): one GEMM per
+ *    (channel plane, tap) over activations gathered per tap, all chaining
+ *    into the same outputs, then ADDP of the bias, then optionally RELU and
+ *    the VEC 'q' pass.  A position outside the map reads as the DMA engine's
+ *    null entry (a zero token, dma_engine.cpp:247-256), i.e. zero padding
+ *    (kh - 1) / 2.  Here the whole conv is one GEMM with gathered activation
+ *    rows: M = images * Ho * Wo output positions, N = cout, K = kh * kh * cin
+ *    in the chain's order (plane of 256 channels, tap, channel).
+ * ------------------------------------------------------------------- */
+
+/* Position order of a feature map (and of the output rows). */
+typedef enum hrb_conv_order {
+  HRB_CONV_XMAJOR = 0,  /* position x * H + y: the compiler's FMap order */
+  HRB_CONV_YMAJOR = 1   /* position y * W + x: NHWC */
+} hrb_conv_order;
+
+typedef struct hrb_conv_desc {
+  uint32_t wfmt;        /* hrb_wfmt (the compiler's convs are MXFP4) */
+  uint32_t mode;        /* hrb_mode */
+  uint32_t images, H, W;
+  uint32_t cin, cout;   /* cin a multiple of 32, and of 256 when above 256
+                           (MakeMap's channel planes, sparsedrive_common.cpp:
+                           47-68) */
+  uint32_t kh;          /* 1 or 3 */
+  uint32_t stride;      /* 1 or 2: Ho = H / stride, Wo = W / stride */
+  uint32_t order;       /* hrb_conv_order */
+  /* The input map: FP32 `a` [images][H * W][cin] (16-byte aligned), encoded
+   * with `quant`, or MXINT8 `aq` [images][H * W][cin] with `ascale`
+   * [images][H * W][cin / 32]. */
+  const float* a;
+  uint32_t quant;
+  const int8_t* aq;
+  const uint8_t* ascale;
+  /* The conv matrix [cout][kh * kh * cin] in `wfmt`, tap-major columns
+   * (tap = ky * kh + kx, ConvTile, sparsedrive_common.cpp:136-158), and its
+   * scales [cout][kh * kh * cin / 32].  16-byte aligned. */
+  const uint8_t* w;
+  const uint8_t* wscale;
+  const float* bias;    /* [cout] or NULL */
+  float* c;             /* [images * Ho * Wo][cout], positions in `order` */
+  uint32_t accumulate;  /* chains start from C: a residual (the emitter's
+                           residual load into FBUF, :385-390) */
+  uint32_t relu;        /* RELU after the bias (lane.cpp:57-70,322-326) */
+  int8_t* cq;           /* optional MXINT8 copy [M][kpN] + [M][kpN / 32] of */
+  uint8_t* cscale;      /* the final output, as hrb_gemm_desc's */
+  uint32_t cquant;
+} hrb_conv_desc;
+
+/* One convolution, device pointers, asynchronous on `stream`: HRB_MODE_EXACT
+ * gives the compiler's chain bit for bit; HRB_MODE_FAST with FP32 `a` runs
+ * the tensor cores (the map is encoded once, each output row's taps are
+ * gathered as operand blocks), within the tolerance of hrb_gemm_desc for
+ * K = kh * kh * cin. */
+HRB_API hrb_status hrb_conv_dense(hrb_ctx* ctx, const hrb_conv_desc* desc, void* stream);
+
+/* A convolution prepared once (weights reordered and translated, scratch
+ * allocated), then run many times with no allocation or host sync; the
+ * descriptor's pointers must stay valid.  *launched receives the kernels of
+ * one run. */
+typedef struct hrb_conv_plan hrb_conv_plan;
+HRB_API hrb_status hrb_conv_plan_create(hrb_ctx* ctx, const hrb_conv_desc* desc,
+                                        hrb_conv_plan** out);
+HRB_API hrb_status hrb_conv_plan_run(hrb_conv_plan* plan, void* stream, uint32_t* launched);
+/* Measurement aid, as hrb_plan_profile: one run, then each of the run's
+ * launches alone `reps` times back to back between two events; ms[i] is the
+ * mean of launch i (fast mode: 0 the map's encoder, 1 the gather of the
+ * GEMM's operand blocks, 2 the GEMM). */
+HRB_API hrb_status hrb_conv_plan_profile(hrb_conv_plan* plan, void* stream, uint32_t reps,
+                                         float* ms, uint32_t cap, uint32_t* nkernels);
+HRB_API hrb_status hrb_conv_plan_destroy(hrb_conv_plan* plan);
+
+/* ---------------------------------------------------------------------
+ * 6. Column-sharded GEMMs over the GPUs of one node (one process per GPU).
  *    Rank r of G computes output columns [n0, n1) (hrb_shard_columns) of
  *    every GEMM with its slice of W.  With peers set on a plan, the kernel's
  *    epilogue stores each output into the local C and, over NVLink, into

@@ -126,7 +126,7 @@ def test_workload_canonicalisation_matches_the_reference_restatement():
 
 
 def test_ctypes_structs_match_the_header(tmp_path):
-    """The ctypes mirrors of hrb_gemm_desc, hrb_gemm_cmd and hrb_ipc_handle
+    """The ctypes mirrors of hrb_gemm_desc, hrb_conv_desc, hrb_gemm_cmd and hrb_ipc_handle
     have the C layout: a C program built against include/hrb_gemm.h prints
     every field's offset and the sizes."""
     import ctypes
@@ -138,7 +138,7 @@ def test_ctypes_structs_match_the_header(tmp_path):
     if cc is None:
         pytest.skip("no C compiler")
     structs = {"hrb_gemm_desc": capi.GemmDesc, "hrb_gemm_cmd": capi.GemmCmd,
-               "hrb_ipc_handle": capi.IpcHandle}
+               "hrb_ipc_handle": capi.IpcHandle, "hrb_conv_desc": capi.ConvDesc}
     lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "hrb_gemm.h"',
              "int main(void) {"]
     for cname, py in structs.items():
