@@ -128,6 +128,8 @@ def load() -> ctypes.CDLL:
             "hrb_abuf_to_dense": (ctypes.c_int, [P, P, u32, u32, P, P, P]),
             "hrb_t32_split8_dense": (ctypes.c_int, [P, P, P, u32, u32, u32, P, P, P]),
             "hrb_dense_to_fbuf": (ctypes.c_int, [P, P, u32, u32, P, P]),
+            "hrb_gemm_npu_cycles": (ctypes.c_uint64, [ctypes.POINTER(GemmCmd)]),
+            "hrb_dense_npu_cycles": (ctypes.c_uint64, [u32, u32, u32, u32]),
             "hrb_conv_dense": (ctypes.c_int, [P, ctypes.POINTER(ConvDesc), P]),
             "hrb_conv_plan_create": (ctypes.c_int, [P, ctypes.POINTER(ConvDesc),
                                                     ctypes.POINTER(P)]),
@@ -446,3 +448,16 @@ class Plan:
             self.close()
         except Exception:
             pass
+
+
+NPU_CLOCK_HZ = 250e6  # the NPU's PL clock (the reference's docs/design.md:27)
+
+
+def npu_cycles(cmd_fields) -> int:
+    """hrb_gemm_npu_cycles of one GEMM instruction (10 fields)."""
+    return int(load().hrb_gemm_npu_cycles(ctypes.byref(GemmCmd(*[int(v) for v in cmd_fields]))))
+
+
+def dense_npu_cycles(wfmt: int, M: int, N: int, K: int) -> int:
+    """hrb_dense_npu_cycles: NPU cycles of a dense GEMM as GEMM instructions."""
+    return int(load().hrb_dense_npu_cycles(wfmt, M, N, K))

@@ -154,6 +154,10 @@ def ref() -> ctypes.CDLL | None:
         lib.hrbref_conv_iss.restype = ctypes.c_int
         lib.hrbref_conv_iss.argtypes = [ctypes.c_uint32] * 6 + [
             _i8p, _u8p, _u8p, _i32p, _u32p, ctypes.c_void_p, ctypes.c_int, _u32p]
+        lib.hrbref_gemm_cycles.restype = ctypes.c_uint64
+        lib.hrbref_gemm_cycles.argtypes = [_u32p, ctypes.c_void_p]
+        lib.hrbref_dense_gemm_cycles.restype = ctypes.c_uint64
+        lib.hrbref_dense_gemm_cycles.argtypes = [ctypes.c_uint32] * 4
         lib.hrbref_dense_gemm_iss.restype = ctypes.c_int
         lib.hrbref_dense_gemm_iss.argtypes = [
             ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
