@@ -78,6 +78,16 @@ class ConvDesc(ctypes.Structure):
 CONV_XMAJOR, CONV_YMAJOR = 0, 1
 
 
+class GaccDesc(ctypes.Structure):
+    """hrb_gacc_desc."""
+    _fields_ = [
+        ("tokens", ctypes.c_uint32), ("slots", ctypes.c_uint32), ("corners", ctypes.c_uint32),
+        ("blocks", ctypes.c_uint32), ("entries", ctypes.c_void_p), ("w", ctypes.c_void_p),
+        ("rows", ctypes.c_void_p), ("row_stride", ctypes.c_uint64), ("nrows", ctypes.c_uint32),
+        ("out", ctypes.c_void_p), ("accumulate", ctypes.c_uint32),
+    ]
+
+
 def header_functions() -> list[str]:
     """Every function include/hrb_gemm.h declares."""
     text = open(HEADER).read()
@@ -131,6 +141,7 @@ def load() -> ctypes.CDLL:
             "hrb_gemm_npu_cycles": (ctypes.c_uint64, [ctypes.POINTER(GemmCmd)]),
             "hrb_dense_npu_cycles": (ctypes.c_uint64, [u32, u32, u32, u32]),
             "hrb_conv_dense": (ctypes.c_int, [P, ctypes.POINTER(ConvDesc), P]),
+            "hrb_gacc_dense": (ctypes.c_int, [P, ctypes.POINTER(GaccDesc), P]),
             "hrb_conv_plan_create": (ctypes.c_int, [P, ctypes.POINTER(ConvDesc),
                                                     ctypes.POINTER(P)]),
             "hrb_conv_plan_run": (ctypes.c_int, [P, P, ctypes.POINTER(u32)]),
@@ -338,6 +349,13 @@ class Library:
         self._check(self.lib.hrb_t32_split8_dense(self.ctx, _ptr(vq), _ptr(vscale), tokens, hd,
                                                   hd if ldv is None else ldv, _ptr(wq),
                                                   _ptr(wscale), stream or None))
+
+    def gacc(self, entries, w, rows, out, *, tokens, slots, corners, blocks, row_stride, nrows,
+             accumulate=False, stream: int = 0) -> None:
+        """hrb_gacc_dense on device buffers."""
+        d = GaccDesc(tokens, slots, corners, blocks, _ptr(entries), _ptr(w), _ptr(rows),
+                     row_stride, nrows, _ptr(out), 1 if accumulate else 0)
+        self._check(self.lib.hrb_gacc_dense(self.ctx, ctypes.byref(d), stream or None))
 
     def conv(self, d: ConvDesc, stream: int = 0) -> None:
         self._check(self.lib.hrb_conv_dense(self.ctx, ctypes.byref(d), stream or None))

@@ -708,6 +708,7 @@ hrb_status hrb_sync(hrb_ctx* ctx) {
   if (flag != 0) {
     HRB_CUDA(ctx, cudaMemset(ctx->d_error, 0, sizeof(uint32_t)));
     if (flag & 2u) return fail(ctx, HRB_ECUDA, "a tensor-core GEMM timed out waiting");
+    if (flag & 4u) return fail(ctx, HRB_EDATA, "a GACC entry names a row outside the feature rows");
     return fail(ctx, HRB_EDATA, "MXINT8 input is infinite or NaN");
   }
   return HRB_OK;
@@ -1611,6 +1612,39 @@ hrb_status hrb_t32_split8_dense(hrb_ctx* ctx, const int8_t* vq, const uint8_t* v
   HRB_CUDA(ctx, cudaSetDevice(ctx->device));
   hrb::launch_t32_split8(vq, vscale, tokens, hd, ldv, wq, wscale, ctx->sm_count,
                          pick(ctx, stream));
+  ctx->launches += 1;
+  HRB_CUDA(ctx, cudaGetLastError());
+  return HRB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Gather-accumulate
+
+hrb_status hrb_gacc_dense(hrb_ctx* ctx, const hrb_gacc_desc* d, void* stream) {
+  if (ctx == nullptr) return HRB_EINVAL;
+  if (d == nullptr) return fail(ctx, HRB_EINVAL, "null GACC descriptor");
+  if (d->tokens == 0 || d->slots == 0 || d->corners == 0) return HRB_OK;
+  if (d->blocks == 0) return fail(ctx, HRB_EINVAL, "GACC with 0 blocks per token");
+  if (!d->entries || !d->w || !d->rows || !d->out) return fail(ctx, HRB_EINVAL, "null buffer");
+  if (d->row_stride % 8u != 0 || d->row_stride < uint64_t{d->blocks} * 33u ||
+      !aligned(d->rows, 8) || !aligned(d->entries, 8) || !aligned(d->w, 4) || !aligned(d->out, 4)) {
+    return fail(ctx, HRB_EINVAL, "GACC rows of %llu bytes for %u blocks, or a misaligned buffer",
+                static_cast<unsigned long long>(d->row_stride), d->blocks);
+  }
+  HRB_CUDA(ctx, cudaSetDevice(ctx->device));
+  hrb::GaccJob j{};
+  j.entries = d->entries;
+  j.w = reinterpret_cast<const uint32_t*>(d->w);
+  j.rows = d->rows;
+  j.row_stride = d->row_stride;
+  j.nrows = d->nrows;
+  j.out = d->out;
+  j.tokens = d->tokens;
+  j.slots = d->slots;
+  j.corners = d->corners;
+  j.blocks = d->blocks;
+  j.accumulate = d->accumulate != 0;
+  hrb::launch_gacc(j, ctx->d_error, ctx->sm_count, pick(ctx, stream));
   ctx->launches += 1;
   HRB_CUDA(ctx, cudaGetLastError());
   return HRB_OK;

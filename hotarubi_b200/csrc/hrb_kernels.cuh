@@ -168,6 +168,18 @@ void launch_conv_gather_tiles(const uint8_t* map_tiles, uint32_t map_nt, uint32_
                               uint8_t* tiles, uint32_t nt, uint32_t steps, uint32_t f8,
                               const ConvGeom& g, cudaStream_t stream);
 
+// GACC in dense form (gacc.cu): see hrb_gacc_desc.
+struct GaccJob {
+  const uint64_t* entries;  // [tokens][slots][corners]
+  const uint32_t* w;        // FP32 bits [tokens][slots][blocks]
+  const uint8_t* rows;      // feature rows, row_stride bytes apart
+  uint64_t row_stride;
+  uint32_t nrows;
+  float* out;               // [tokens][blocks * 32]
+  uint32_t tokens, slots, corners, blocks, accumulate;
+};
+void launch_gacc(const GaccJob& job, uint32_t* error_flag, int sm_count, cudaStream_t stream);
+
 // T32_SPLIT8 in dense form (kv_operands.cu).
 void launch_t32_split8(const int8_t* vq, const uint8_t* vs, uint32_t tokens, uint32_t hd,
                        uint32_t ldv, int8_t* wq, uint8_t* ws, int sm_count,

@@ -88,6 +88,12 @@ def oracle() -> ctypes.CDLL:
         lib.hrbo_conv_weights.argtypes = [ctypes.c_uint32] * 4 + [_u8p, _u8p, _u8p, _u8p]
         lib.hrbo_relu_n.restype = None
         lib.hrbo_relu_n.argtypes = [_u32p, ctypes.c_size_t]
+        lib.hrbo_fp32_mul.restype = ctypes.c_uint32
+        lib.hrbo_fp32_mul.argtypes = [ctypes.c_uint32, ctypes.c_uint32]
+        lib.hrbo_gacc_dense.restype = None
+        lib.hrbo_gacc_dense.argtypes = [ctypes.c_uint32] * 4 + [
+            np.ctypeslib.ndpointer(np.uint64, flags="C_CONTIGUOUS"), _u32p, _u8p, ctypes.c_uint64,
+            _u32p, ctypes.c_int]
         lib.hrbo_t32_split8.restype = ctypes.c_int
         lib.hrbo_t32_split8.argtypes = [_i8p, _u8p, ctypes.c_uint32, ctypes.c_uint32,
                                         ctypes.c_uint32, _i8p, _u8p]
@@ -158,6 +164,10 @@ def ref() -> ctypes.CDLL | None:
         lib.hrbref_gemm_cycles.argtypes = [_u32p, ctypes.c_void_p]
         lib.hrbref_dense_gemm_cycles.restype = ctypes.c_uint64
         lib.hrbref_dense_gemm_cycles.argtypes = [ctypes.c_uint32] * 4
+        lib.hrbref_gacc_iss.restype = ctypes.c_int
+        lib.hrbref_gacc_iss.argtypes = [ctypes.c_uint32] * 3 + [
+            np.ctypeslib.ndpointer(np.uint64, flags="C_CONTIGUOUS"), _u32p, _u8p,
+            ctypes.c_uint32, ctypes.c_uint32, _u32p]
         lib.hrbref_dense_gemm_iss.restype = ctypes.c_int
         lib.hrbref_dense_gemm_iss.argtypes = [
             ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
@@ -450,6 +460,22 @@ def conv_dense(wfmt: int, aq, ascale, images, H, W, cin, cout, kh, stride, w, ws
     c = gemm_dense(wfmt, q, sc, wq, ws, cout, bias_bits=bias_bits, c_init=c_init,
                    pieces=pieces)
     return relu(c) if relu_out else c
+
+
+def gacc_dense(entries: np.ndarray, w: np.ndarray, rows: np.ndarray, blocks: int,
+               out_init=None) -> np.ndarray:
+    """hrbo_gacc_dense: entries uint64 [tokens, slots, corners], w FP32 bits
+    [tokens, slots, blocks], rows uint8 [nrows, row_stride]; returns FP32
+    bits [tokens, blocks * 32]."""
+    entries = np.ascontiguousarray(entries, np.uint64)
+    tokens, slots, corners = entries.shape
+    out = (np.zeros((tokens, blocks * 32), np.uint32) if out_init is None
+           else np.ascontiguousarray(out_init, np.uint32).copy())
+    rows = np.ascontiguousarray(rows, np.uint8)
+    oracle().hrbo_gacc_dense(tokens, slots, corners, blocks, entries.ravel(),
+                             np.ascontiguousarray(w, np.uint32).ravel(), rows.ravel(),
+                             rows.shape[1], out.ravel(), 0 if out_init is None else 1)
+    return out
 
 
 def split_w8(q: np.ndarray) -> tuple[np.ndarray, np.ndarray]:

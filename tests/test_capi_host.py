@@ -138,7 +138,8 @@ def test_ctypes_structs_match_the_header(tmp_path):
     if cc is None:
         pytest.skip("no C compiler")
     structs = {"hrb_gemm_desc": capi.GemmDesc, "hrb_gemm_cmd": capi.GemmCmd,
-               "hrb_ipc_handle": capi.IpcHandle, "hrb_conv_desc": capi.ConvDesc}
+               "hrb_ipc_handle": capi.IpcHandle, "hrb_conv_desc": capi.ConvDesc,
+               "hrb_gacc_desc": capi.GaccDesc}
     lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "hrb_gemm.h"',
              "int main(void) {"]
     for cname, py in structs.items():
