@@ -1,7 +1,7 @@
 """Benchmark of the quantized GEMM hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c1|c4|c5|c5conv] [--mode exact|fast] [--batch B]
+                    [--config c2|c1|c4|c5|c5conv|gacc] [--mode exact|fast] [--batch B]
 
 Default workload (the MXFP4 GEMM the metric is
 quoted on): C = A . W^T with A FP32 [64, 2560] ~ N(0,1) encoded to MXINT8 on
@@ -11,7 +11,9 @@ exponent in [-10, -4], canonicalised as hotarubi's compiler does), FP32 C
 per-channel int8 weights placed as hotarubi's compiler places a float
 matrix, with bias); --config c5 one large-M MXFP4 GEMM of the configs[4]
 sweep (4096 x 4096 x 4096), tensor-bound; --config c5conv the configs[4]
-conv (3x3, 256 -> 256 channels, 48 maps of 16 x 44) as an implicit GEMM.
+conv (3x3, 256 -> 256 channels, 48 maps of 16 x 44) as an implicit GEMM;
+--config gacc the DMA engine's gather-accumulate on SparseDrive's detection
+head sampling.
 
 One step = the hot path over one batch of B independent instances of the
 GEMM, each with its own activations, weights and output (C2: B = 128, 282 MB
@@ -148,6 +150,43 @@ class ConvWorkload:
 
 
 CONV = ConvWorkload()
+
+
+@dataclasses.dataclass(frozen=True)
+class GaccWorkload:
+    """SparseDrive's detection head deformable sampling as GACC runs it
+    (tools/compiler/sparsedrive_head.cpp:1177-1196: 928 padded anchors, per
+    camera one GACC of 56 slots (4 levels x 13 points, padded) x 4 corners,
+    8 blocks = 256 channels, chained over the 6 cameras).  Feature rows: the
+    6 cameras' 4 levels of a 256 x 704 input (64x176 ... 8x22), MXINT8 row
+    format; entries uniformly random (corners are not made adjacent)."""
+    key: str = "gacc"
+    name: str = "gacc_sparsedrive_det_928x336x4x256"
+    tokens: int = 928
+    slots: int = 6 * 56
+    corners: int = 4
+    blocks: int = 8
+    nrows: int = 6 * (64 * 176 + 32 * 88 + 16 * 44 + 8 * 22)
+    instances: int = 6    # rotated per step: 6 x ~45 MB > 2 x L2
+
+    @property
+    def entries(self) -> int:
+        return self.tokens * self.slots * self.corners
+
+    @property
+    def row_stride(self) -> int:
+        return (2 * self.blocks + 1) * 16
+
+    @property
+    def gathered_bytes(self) -> int:
+        return self.entries * self.blocks * 33
+
+    @property
+    def metric(self) -> str:
+        return "GACC gathered-row throughput GB/s (SparseDrive det head, 928 x 6 cams x 56 x 4)"
+
+
+GACC = GaccWorkload()
 
 
 def peaks() -> dict:
@@ -737,6 +776,165 @@ def run_conv(args, rank: int, world: int, local_rank: int) -> None:
         dist.destroy_process_group()
 
 
+def gacc_operands(gw: GaccWorkload, i: int):
+    rng = np.random.default_rng(800 + i)
+    rows = rng.integers(0, 256, (gw.nrows, gw.row_stride), dtype=np.uint8)
+    rows[:, 32 * gw.blocks:33 * gw.blocks] = rng.integers(118, 134, (gw.nrows, gw.blocks))
+    idx = rng.integers(0, gw.nrows, (gw.tokens, gw.slots, gw.corners)).astype(np.uint64)
+    idx[:, 52::56, :] = 0xFFFFFFFF      # the 4 padding slots of each camera are null
+    idx[:, 53::56, :] = 0xFFFFFFFF
+    idx[:, 54::56, :] = 0xFFFFFFFF
+    idx[:, 55::56, :] = 0xFFFFFFFF
+    bw = (rng.random((gw.tokens, gw.slots, gw.corners)).astype(np.float32) * 0.25)
+    w = rng.random((gw.tokens, gw.slots, gw.blocks)).astype(np.float32) / 52.0
+    entries = idx | (bw.view(np.uint32).astype(np.uint64) << np.uint64(32))
+    return entries, w, rows
+
+
+def run_gacc(args, rank: int, world: int, local_rank: int) -> None:
+    """--config gacc: hrb_gacc_dense on the SparseDrive detection head's
+    sampling (replicas for N > 1, weak scaling).  The metric is the gathered
+    feature-row bytes per second; the FP32 chain adds 2 flops per gathered
+    code."""
+    import torch
+
+    from hotarubi_b200 import capi
+    gw = GACC
+    live = gw.entries - gw.tokens * 6 * 4 * gw.corners   # null padding slots excluded
+    def cpu_sample(reps: int, warm: int):
+        """The C restatement on 1 thread over 16 of the tokens (GB/s, s)."""
+        from oracle import cpu
+        e, w, rows = gacc_operands(gw, 0)
+        sample = 16
+        runs = []
+        for _ in range(warm + reps):
+            t0 = time.perf_counter()
+            cpu.gacc_dense(e[:sample], w[:sample].view(np.uint32), rows, gw.blocks)
+            runs.append(time.perf_counter() - t0)
+        dt = statistics.median(runs[warm:])
+        return (live * sample / gw.tokens * gw.blocks * 33 / dt / 1e9, dt,
+                f"{sample} of {gw.tokens} tokens through the C restatement on 1 thread")
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        value, dt, desc = cpu_sample(args.steps, args.warmup)
+        print(json.dumps({
+            "impl": "reference", "metric": gw.metric, "value": value, "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32 chain over int8 rows", "data": "synthetic",
+            "config": {"workload": gw.name, "sample": desc},
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": 1, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    lib = capi.Library(local_rank)
+    stream = torch.cuda.Stream()
+    lib.set_stream(stream.cuda_stream)
+    inst = []
+    for i in range(gw.instances):
+        e, w, rows = gacc_operands(gw, i)
+        inst.append({"e": torch.from_numpy(e.view(np.int64)).cuda(),
+                     "w": torch.from_numpy(w).cuda(), "rows": torch.from_numpy(rows).cuda(),
+                     "out": torch.zeros((gw.tokens, gw.blocks * 32), device="cuda")})
+
+    def launch(t):
+        lib.gacc(t["e"], t["w"], t["rows"], t["out"], tokens=gw.tokens, slots=gw.slots,
+                 corners=gw.corners, blocks=gw.blocks, row_stride=gw.row_stride,
+                 nrows=gw.nrows, stream=stream.cuda_stream)
+
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    with ClockSampler(local_rank) as clocks:
+        for i in range(args.warmup):
+            launch(inst[i % gw.instances])
+        stream.synchronize()
+        if dist is not None:
+            dist.barrier()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for i in range(args.steps):
+            launch(inst[i % gw.instances])
+        end.record(stream)
+        end.synchronize()
+        if dist is not None:
+            dist.barrier()
+    lib.sync()
+    ms = start.elapsed_time(end) / args.steps
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    e2e = None
+    if not args.no_e2e:
+        e, w, _ = gacc_operands(gw, 0)
+        eh = torch.from_numpy(e.view(np.int64)).pin_memory()
+        wh = torch.from_numpy(w).pin_memory()
+        oh = torch.empty((gw.tokens, gw.blocks * 32)).pin_memory()
+        t0 = inst[0]
+        n_e2e = max(1, min(args.steps, 10))
+        for k in range(2 + n_e2e):
+            if k == 2:
+                stream.synchronize()
+                w0 = time.perf_counter()
+            with torch.cuda.stream(stream):
+                t0["e"].copy_(eh, non_blocking=True)
+                t0["w"].copy_(wh, non_blocking=True)
+                launch(t0)
+                oh.copy_(t0["out"], non_blocking=True)
+            stream.synchronize()
+        dt = (time.perf_counter() - w0) / n_e2e
+        e2e = {"value": world * live * gw.blocks * 33 / dt / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": world * (eh.numel() * 8 + wh.numel() * 4),
+               "d2h_bytes_per_step": world * oh.numel() * 4, "ms_per_step": dt * 1e3,
+               "entry_point": "pinned copies of entries and coefficients + hrb_gacc_dense "
+                              "(feature rows resident)"}
+    if rank == 0:
+        pk = peaks()
+        gbs = world * live * gw.blocks * 33 / (ms / 1e3) / 1e9
+        per_gpu = live * gw.blocks * 33 / (ms / 1e3) / 1e9
+        line = {
+            "metric": gw.metric, "value": gbs, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp32 chain over int8 rows (bit-exact)", "data": "synthetic",
+            "config": {"workload": gw.name, "tokens": gw.tokens, "slots": gw.slots,
+                       "corners": gw.corners, "channels": gw.blocks * 32,
+                       "feature_rows": gw.nrows, "live_entries": live,
+                       "l2": f"{gw.instances} instances rotated (> 2 x 126 MB L2)",
+                       "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "hbm", "kernel": "k_gacc", "achieved": per_gpu,
+                         "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": per_gpu / pk["hbm_gbs"],
+                         "peak_source": pk["source"] + " (HBM copy; a 24 MB row table is "
+                                                       "gathered mostly from L2)",
+                         "alg_bytes_per_launch": live * gw.blocks * 33, "traffic": None,
+                         "launch_ms": ms},
+            "gflops": live * gw.blocks * 32 * 2 / (ms / 1e3) / 1e9,
+            "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks.summary(),
+        }
+        if not args.no_cpu_baseline:
+            value, _, desc = cpu_sample(3, 1)
+            line["cpu_baseline"] = {"value": value, "unit": "GB/s", "cores": 1, "kind": "port",
+                                    "sample": desc}
+        print(json.dumps(line), flush=True)
+    lib.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_shard(args, wl: Workload, rank: int, world: int, local_rank: int) -> None:
     """--shard: the batch's GEMMs split along N over the ranks (strong
     scaling: the total work is fixed); every rank's kernel also stores its
@@ -838,7 +1036,7 @@ def main() -> None:
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", choices=sorted(WORKLOADS) + [CONV.key], default="c2")
+    p.add_argument("--config", choices=sorted(WORKLOADS) + [CONV.key, GACC.key], default="c2")
     p.add_argument("--mode", choices=["exact", "fast"], default="fast")
     p.add_argument("--batch", type=int, default=0, help="GEMMs per step per GPU (0: the "
                    "config's default)")
@@ -853,6 +1051,9 @@ def main() -> None:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.config == CONV.key:
         run_conv(args, rank, world, local_rank)
+        return
+    if args.config == GACC.key:
+        run_gacc(args, rank, world, local_rank)
         return
     wl = WORKLOADS[args.config]
     if args.impl == "reference":
