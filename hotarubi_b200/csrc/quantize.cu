@@ -308,7 +308,8 @@ __device__ __forceinline__ float max_nan_abs(uint32_t a, uint32_t b) {
 
 template <bool kVec>
 __device__ __forceinline__ void encode_planes(const PlaneJob& j, const PlaneOut& o, uint32_t step,
-                                              uint32_t v[8], uint32_t lane, uint32_t& bad) {
+                                              uint32_t v[8], uint32_t lane, uint32_t& bad,
+                                              const uint32_t* lut) {
   constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
   // The largest magnitude as an FP32 max of magnitudes (NaN-propagating, so
   // a NaN or an Inf still shows in the key); the VEC rule's key is its
@@ -341,23 +342,26 @@ __device__ __forceinline__ void encode_planes(const PlaneJob& j, const PlaneOut&
     e = key != 0 ? static_cast<int32_t>(key >> 23) - 127 : 0;
     scale = static_cast<uint32_t>(e + 127);
   }
-  float qf[8];
+  // t = q + 1.5 * 2^23: q in the low byte of its bits (two's complement).
+  float t[8];
   if (scale < 6u) {
     // The planes' scales 2^(e - 6 + 3p) start below E8M0's 2^-127: such a
     // block (largest magnitude under 2^-121) is encoded as zero.
 #pragma unroll
-    for (uint32_t i = 0; i < 8; ++i) qf[i] = 0.0f;
+    for (uint32_t i = 0; i < 8; ++i) t[i] = kMagic;
   } else if (e >= -120 && e < 128) {
-    // x * 2^(6 - e) is exact, so the fused add of 1.5 * 2^23 rounds it once.
+    // x * 2^(6 - e) is exact, so the fused add of 1.5 * 2^23 rounds it once;
+    // q >= -128 always, and 128 clamps to 127.
     const float sc = __uint_as_float(static_cast<uint32_t>(133 - e) << 23);  // 2^(6 - e)
 #pragma unroll
     for (uint32_t i = 0; i < 8; ++i) {
-      qf[i] = fminf(__fadd_rn(__fmaf_rn(__uint_as_float(v[i]), sc, kMagic), -kMagic), 127.0f);
+      t[i] = fminf(__fmaf_rn(__uint_as_float(v[i]), sc, kMagic), kMagic + 127.0f);
     }
   } else {
 #pragma unroll
     for (uint32_t i = 0; i < 8; ++i) {
-      qf[i] = static_cast<float>(kVec ? quantize_vec_rule(v[i], key) : quantize_host_rule(v[i], e));
+      t[i] = kMagic + static_cast<float>(kVec ? quantize_vec_rule(v[i], key)
+                                               : quantize_host_rule(v[i], e));
     }
   }
   if (j.f8) {
@@ -365,8 +369,9 @@ __device__ __forceinline__ void encode_planes(const PlaneJob& j, const PlaneOut&
     float h[8], l[8];
 #pragma unroll
     for (uint32_t i = 0; i < 8; ++i) {
-      h[i] = __fadd_rn(__fmaf_rn(qf[i], 0.0625f, kMagic), -kMagic);
-      l[i] = __fmaf_rn(h[i], -16.0f, qf[i]);
+      const float qf = __fadd_rn(t[i], -kMagic);
+      h[i] = __fadd_rn(__fmaf_rn(qf, 0.0625f, kMagic), -kMagic);
+      l[i] = __fmaf_rn(h[i], -16.0f, qf);
     }
     const uint32_t st = 2u * step + (lane >> 4);  // this lane's 128-element step
     if (st < j.steps) {
@@ -386,18 +391,25 @@ __device__ __forceinline__ void encode_planes(const PlaneJob& j, const PlaneOut&
     }
     return;
   }
-  float d0[8], d1[8], d2[8];
+  // The three E2M1 digit codes of each q from the table (bytes 0, 1, 2 of
+  // lut[q & 0xFF]); pairs of elements merge into one word whose byte p is
+  // plane p's byte for the pair (low nibble the even element), and byte
+  // permutes gather each plane's four bytes.
+  uint32_t pair[4];
 #pragma unroll
-  for (uint32_t i = 0; i < 8; ++i) {
-    d2[i] = __fadd_rn(__fmaf_rn(qf[i], 0.015625f, kMagic), -kMagic);
-    const float r = __fmaf_rn(d2[i], -64.0f, qf[i]);
-    d1[i] = __fadd_rn(__fmaf_rn(r, 0.125f, kMagic), -kMagic);
-    d0[i] = __fmaf_rn(d1[i], -8.0f, r);
+  for (uint32_t k = 0; k < 4; ++k) {
+    const uint32_t lo = lut[__float_as_uint(t[2 * k]) & 0xFFu];
+    const uint32_t hi = lut[__float_as_uint(t[2 * k + 1]) & 0xFFu];
+    pair[k] = lo | (hi << 4);
   }
+  const uint32_t a01 = __byte_perm(pair[0], pair[1], 0x5140u);  // p0: 0,4  p1: 1,5
+  const uint32_t a23 = __byte_perm(pair[2], pair[3], 0x5140u);
+  const uint32_t b01 = __byte_perm(pair[0], pair[1], 0x0062u);  // p2: 2,6
+  const uint32_t b23 = __byte_perm(pair[2], pair[3], 0x0062u);
   uint8_t* blk = o.blk0 + step * j.block_bytes;
-  *reinterpret_cast<uint32_t*>(blk + o.off) = pack_e2m1x8(d0);
-  *reinterpret_cast<uint32_t*>(blk + j.plane_bytes + o.off) = pack_e2m1x8(d1);
-  *reinterpret_cast<uint32_t*>(blk + 2u * j.plane_bytes + o.off) = pack_e2m1x8(d2);
+  *reinterpret_cast<uint32_t*>(blk + o.off) = __byte_perm(a01, a23, 0x5410u);
+  *reinterpret_cast<uint32_t*>(blk + j.plane_bytes + o.off) = __byte_perm(a01, a23, 0x7632u);
+  *reinterpret_cast<uint32_t*>(blk + 2u * j.plane_bytes + o.off) = __byte_perm(b01, b23, 0x5410u);
   if ((lane & 3u) == 0) {
 #pragma unroll
     for (uint32_t p = 0; p < 3; ++p) {
@@ -466,6 +478,23 @@ __global__ void __launch_bounds__(kPlaneWarps * 32)
 k_quantize_planes(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ QuantJob inline_job,
                   uint32_t* error_flag) {
   __shared__ __align__(16) uint32_t ring[kPlaneWarps][kPlaneDepth][256];
+  // lut[q & 0xFF]: the E2M1 codes of q's digits d0, d1, d2 in bytes 0, 1, 2,
+  // with q = 64 d2 + 8 d1 + d0, d2 = RNE(q / 64), d1 = RNE((q - 64 d2) / 8).
+  __shared__ uint32_t lut[256];
+  {
+    constexpr float kMagic = 12582912.0f;
+    const float q = static_cast<float>(static_cast<int8_t>(threadIdx.x & 0xFFu));
+    const float d2 = __fadd_rn(__fmaf_rn(q, 0.015625f, kMagic), -kMagic);
+    const float r = __fmaf_rn(d2, -64.0f, q);
+    const float d1 = __fadd_rn(__fmaf_rn(r, 0.125f, kMagic), -kMagic);
+    const float d0 = __fmaf_rn(d1, -8.0f, r);
+    const float d[8] = {d0, d1, d2, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    const uint32_t packed = pack_e2m1x8(d);  // nibble i = digit i's code
+    if (threadIdx.x < 256u) {
+      lut[threadIdx.x] = (packed & 0xFu) | ((packed >> 4) & 0xFu) << 8 | ((packed >> 8) & 0xFu) << 16;
+    }
+  }
+  __syncthreads();
   const uint32_t lane = threadIdx.x & 31u, wib = threadIdx.x >> 5;
   const uint32_t warp = blockIdx.x * kPlaneWarps + wib;
   const uint32_t nwarps = gridDim.x * kPlaneWarps;
@@ -519,9 +548,9 @@ k_quantize_planes(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ 
     v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
     v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
     if (pr.job.vec_rule) {
-      encode_planes<true>(pr.job, out, pr.step, v, lane, bad);
+      encode_planes<true>(pr.job, out, pr.step, v, lane, bad, lut);
     } else {
-      encode_planes<false>(pr.job, out, pr.step, v, lane, bad);
+      encode_planes<false>(pr.job, out, pr.step, v, lane, bad, lut);
     }
     if (plane_cursor_next(pr, jobs, njobs) && i + 1 < count) out = plane_out(pr.job, pr.row, lane);
     if (i + kPlaneDepth < count) {
