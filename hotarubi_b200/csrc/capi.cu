@@ -437,11 +437,12 @@ hrb_status check_conv(hrb_ctx* ctx, const hrb_conv_desc* d, ConvRun* r) {
   ConvRun& x = *r;
   x = ConvRun{};
   const uint32_t plane = d->cin < 256u ? d->cin : 256u;
-  x.g = hrb::ConvGeom{d->images, d->H,  d->W,      d->H / d->stride, d->W / d->stride,
-                      d->cin,    d->kh, d->stride, d->order,         plane / 32u};
+  x.g = hrb::make_conv_geom(d->images, d->H, d->W, d->cin, d->kh, d->stride, d->order);
   const uint64_t M = uint64_t{d->images} * x.g.Ho * x.g.Wo;
   const uint64_t K = uint64_t{d->kh} * d->kh * d->cin;
-  if (M > (1u << 30) || K > (1u << 20)) return fail(ctx, HRB_EINVAL, "conv too large");
+  if (M > (1u << 30) || K > (1u << 20) || M * (K / 32u) >= (uint64_t{1} << 32)) {
+    return fail(ctx, HRB_EINVAL, "conv too large");
+  }
   x.M = static_cast<uint32_t>(M);
   x.N = d->cout;
   x.K = static_cast<uint32_t>(K);

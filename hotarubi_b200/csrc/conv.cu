@@ -39,12 +39,13 @@ unsigned grid_of(uint64_t n) {
 __global__ void k_conv_im2col(const int8_t* __restrict__ aq, const uint8_t* __restrict__ as,
                               const ConvGeom g, int8_t* __restrict__ q,
                               uint8_t* __restrict__ scale) {
-  const uint32_t kbi = g.cin / 32u, kbo = g.kh * g.kh * kbi;
+  const uint32_t kbi = g.cin / 32u;
   const uint64_t rows = static_cast<uint64_t>(g.images) * g.Ho * g.Wo;
-  const uint64_t total = rows * kbo;
+  const uint64_t total = rows * g.kbo;
   for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-    const uint32_t row = static_cast<uint32_t>(i / kbo), b = static_cast<uint32_t>(i % kbo);
+    const uint64_t row64 = i / g.kbo;
+    const uint32_t row = static_cast<uint32_t>(row64), b = static_cast<uint32_t>(i - row64 * g.kbo);
     uint32_t ib = 0;
     const int64_t src = conv_source_block(g, row, b, &ib);
     uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
@@ -107,27 +108,30 @@ __global__ void k_relu_exact(float* __restrict__ c, uint32_t M, uint32_t N, uint
 __global__ void k_conv_gather_tiles(const uint8_t* __restrict__ map_tiles, uint32_t map_nt,
                                     uint32_t map_steps, uint8_t* __restrict__ tiles, uint32_t nt,
                                     uint32_t steps, uint32_t f8, const ConvGeom g) {
-  const uint32_t kbo = g.kh * g.kh * g.cin / 32u;
   const uint32_t bps = f8 ? 4u : 8u;        // blocks per K step
+  const uint32_t bps_shift = f8 ? 2u : 3u;
+  const uint32_t nt_shift = nt == 64u ? 6u : 7u, map_shift = map_nt == 64u ? 6u : 7u;
   const uint32_t planes = f8 ? 2u : 3u;
   const uint32_t chunks = f8 ? 2u : 1u;     // 16-byte chunks per block and plane
   const uint32_t bb = f8 ? mx8_act_block_bytes(nt) : mx_act_block_bytes(nt);
   const uint32_t mbb = f8 ? mx8_act_block_bytes(map_nt) : mx_act_block_bytes(map_nt);
-  const uint64_t total = static_cast<uint64_t>(g.images) * g.Ho * g.Wo * kbo;
-  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-    const uint32_t row = static_cast<uint32_t>(i / kbo), b = static_cast<uint32_t>(i % kbo);
+  // 32-bit indices (the launch keeps rows * kbo below 2^32).
+  const uint32_t total = g.images * g.Ho * g.Wo * g.kbo;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t row = fast_div(i, g.kbo_div), b = i - row * g.kbo;
     uint32_t ib = 0;
     const int64_t src = conv_source_block(g, row, b, &ib);
-    const uint32_t dr = row % nt, db = b % bps;
-    uint8_t* dblk = tiles + (static_cast<size_t>(row / nt) * steps + b / bps) * bb;
+    // Tile heights (64 or 128) and blocks per step (4 or 8) are powers of 2.
+    const uint32_t dr = row & (nt - 1u), db = b & (bps - 1u);
+    uint8_t* dblk = tiles + (static_cast<size_t>(row >> nt_shift) * steps + (b >> bps_shift)) * bb;
     const uint8_t* sblk = nullptr;
     uint32_t sr = 0, sb = 0;
     if (src >= 0) {
       const uint32_t pos = static_cast<uint32_t>(src);
-      sr = pos % map_nt;
-      sb = ib % bps;
-      sblk = map_tiles + (static_cast<size_t>(pos / map_nt) * map_steps + ib / bps) * mbb;
+      sr = pos & (map_nt - 1u);
+      sb = ib & (bps - 1u);
+      sblk = map_tiles +
+             (static_cast<size_t>(pos >> map_shift) * map_steps + (ib >> bps_shift)) * mbb;
     }
     for (uint32_t p = 0; p < planes; ++p) {
       for (uint32_t c = 0; c < chunks; ++c) {

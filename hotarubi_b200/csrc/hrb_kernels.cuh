@@ -10,30 +10,82 @@
 
 namespace hrb {
 
+// Unsigned 32-bit division by a divisor fixed for a launch, as a multiply
+// and shifts (Granlund and Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994, section 4): for d >= 1 with l = ceil(log2 d),
+// m = floor(2^32 (2^l - d) / d) + 1, n / d = (t + ((n - t) >> 1)) >> (l - 1)
+// where t = mulhi(m, n); d = 1 takes l = 0 and the shifts degenerate.
+struct FastDiv {
+  uint32_t d, m, s1, s2;
+};
+inline FastDiv make_fast_div(uint32_t d) {
+  uint32_t l = 0;
+  while (l < 32 && (uint64_t{1} << l) < d) ++l;
+  FastDiv f;
+  f.d = d;
+  f.m = static_cast<uint32_t>(((uint64_t{1} << 32) * ((uint64_t{1} << l) - d)) / d + 1);
+  f.s1 = l > 0 ? 1u : 0u;
+  f.s2 = l > 0 ? l - 1u : 0u;
+  return f;
+}
+__host__ __device__ inline uint32_t fast_div(uint32_t n, const FastDiv& f) {
+#ifdef __CUDA_ARCH__
+  const uint32_t t = __umulhi(f.m, n);
+#else
+  const uint32_t t = static_cast<uint32_t>((uint64_t{f.m} * n) >> 32);
+#endif
+  return (t + ((n - t) >> f.s1)) >> f.s2;
+}
+
 // Geometry of a convolution run as a GEMM whose activation rows are
 // gathered (hotarubi's ConvEmitter, tools/compiler/sparsedrive_encoder.cpp):
 // output row img * Ho * Wo + o reads, for K column (plane, tap, channel in
 // plane), channel plane * 32 * bp + channel of the input position under tap
 // (ky, kx) = (tap / kh, tap % kh) with padding (kh - 1) / 2, or zero outside
 // the map.  Positions are x-major (order 0: x * H + y) or y-major (y * W + x).
+// The divisors the index arithmetic needs come precomputed (make_conv_geom).
 struct ConvGeom {
   uint32_t images, H, W, Ho, Wo, cin, kh, stride, order;
   uint32_t bp;      // K blocks per channel plane (min(cin, 256) / 32)
+  uint32_t kbo;     // gathered K blocks per output row: kh * kh * cin / 32
+  FastDiv out_per;  // Ho * Wo
+  FastDiv minor;    // Ho (x-major) or Wo (y-major)
+  FastDiv kh_div;   // kh
+  FastDiv bp_div;   // bp
+  FastDiv plane_k;  // kh * kh * bp, gathered blocks per channel plane
+  FastDiv kbo_div;  // kbo
 };
+
+inline ConvGeom make_conv_geom(uint32_t images, uint32_t H, uint32_t W, uint32_t cin, uint32_t kh,
+                               uint32_t stride, uint32_t order) {
+  ConvGeom g{};
+  g.images = images;
+  g.H = H;
+  g.W = W;
+  g.Ho = H / stride;
+  g.Wo = W / stride;
+  g.cin = cin;
+  g.kh = kh;
+  g.stride = stride;
+  g.order = order;
+  g.bp = (cin < 256u ? cin : 256u) / 32u;
+  g.kbo = kh * kh * cin / 32u;
+  g.out_per = make_fast_div(g.Ho * g.Wo);
+  g.minor = make_fast_div(order == 0 ? g.Ho : g.Wo);
+  g.kh_div = make_fast_div(kh);
+  g.bp_div = make_fast_div(g.bp);
+  g.plane_k = make_fast_div(kh * kh * g.bp);
+  g.kbo_div = make_fast_div(g.kbo);
+  return g;
+}
 
 // Input position of output row `row` under tap `tap`, or -1 outside the map.
 __host__ __device__ inline int64_t conv_source_row(const ConvGeom& g, uint32_t row, uint32_t tap) {
-  const uint32_t out_per = g.Ho * g.Wo;
-  const uint32_t img = row / out_per, o = row - img * out_per;
-  uint32_t yo, xo;
-  if (g.order == 0) {
-    xo = o / g.Ho;
-    yo = o - xo * g.Ho;
-  } else {
-    yo = o / g.Wo;
-    xo = o - yo * g.Wo;
-  }
-  const uint32_t ky = tap / g.kh, kx = tap - ky * g.kh, pad = (g.kh - 1u) / 2u;
+  const uint32_t img = fast_div(row, g.out_per), o = row - img * g.out_per.d;
+  const uint32_t major = fast_div(o, g.minor), minor = o - major * g.minor.d;
+  const uint32_t yo = g.order == 0 ? minor : major;
+  const uint32_t xo = g.order == 0 ? major : minor;
+  const uint32_t ky = fast_div(tap, g.kh_div), kx = tap - ky * g.kh, pad = (g.kh - 1u) / 2u;
   const int32_t yi = static_cast<int32_t>(g.stride * yo + ky) - static_cast<int32_t>(pad);
   const int32_t xi = static_cast<int32_t>(g.stride * xo + kx) - static_cast<int32_t>(pad);
   if (yi < 0 || yi >= static_cast<int32_t>(g.H) || xi < 0 || xi >= static_cast<int32_t>(g.W)) {
@@ -48,9 +100,8 @@ __host__ __device__ inline int64_t conv_source_row(const ConvGeom& g, uint32_t r
 // or -1 when it falls outside the map.
 __host__ __device__ inline int64_t conv_source_block(const ConvGeom& g, uint32_t row, uint32_t b,
                                                      uint32_t* in_block) {
-  const uint32_t taps = g.kh * g.kh, per_plane = taps * g.bp;
-  const uint32_t plane = b / per_plane, rem = b - plane * per_plane;
-  const uint32_t tap = rem / g.bp, cb = rem - tap * g.bp;
+  const uint32_t plane = fast_div(b, g.plane_k), rem = b - plane * g.plane_k.d;
+  const uint32_t tap = fast_div(rem, g.bp_div), cb = rem - tap * g.bp;
   *in_block = plane * g.bp + cb;
   return conv_source_row(g, row, tap);
 }
