@@ -349,6 +349,7 @@ struct ConvRun {
   uint32_t M = 0, N = 0, K = 0;
   bool tc = false;       // HRB_MODE_FAST with FP32 input: the tensor cores
   bool reorder = false;  // more than one channel plane: weights reordered
+  bool gather = false;   // MXFP4 with 256-channel planes: the GEMM gathers its own blocks
   uint32_t bpb = 16;     // weight bytes per K block
   uint32_t npieces = 0;  // K pieces of the exact chain (W8: one per (plane, tap) job)
   uint32_t pieces[hrb::kMaxPieces];
@@ -475,7 +476,10 @@ hrb_status check_conv(hrb_ctx* ctx, const hrb_conv_desc* d, ConvRun* r) {
   }
   if (tc) {
     const hrb_gemm_desc g = conv_gemm(d, x, nullptr);
-    x.o_tc = take(tc_scratch_bytes(&g));
+    // With 256-channel planes one MXFP4 K step is one (plane, tap), and the
+    // GEMM assembles its activation blocks itself from the encoded map.
+    x.gather = d->wfmt == HRB_WFMT_MXFP4 && x.g.bp == 8u;
+    x.o_tc = take(x.gather ? hrb::mx_weight_bytes(d->wfmt, x.N, x.K / 32u) : tc_scratch_bytes(&g));
     x.o_mt = take(hrb::mx_act_bytes(d->wfmt, d->images * d->H * d->W, d->cin / 32u));
   } else {
     if (d->a != nullptr) {
@@ -504,7 +508,11 @@ hrb_status conv_prepare(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, 
     hrb::QuantJob qj;
     hrb::TcJob tj;
     tc_jobs(&g, base + r.o_tc, &qj, &tj);
-    HRB_CUDA(ctx, cudaMemsetAsync(base + r.o_tc, 0, align_up(tc_act_bytes(&g), 1024), s));
+    if (r.gather) {
+      tj.w_tiles = base + r.o_tc;  // no prepared activation blocks
+    } else {
+      HRB_CUDA(ctx, cudaMemsetAsync(base + r.o_tc, 0, align_up(tc_act_bytes(&g), 1024), s));
+    }
     tc_translate(&g, tj, s);
     *launched += 1;
   }
@@ -531,6 +539,25 @@ hrb_status conv_execute(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, 
     if (take()) {
       hrb::launch_quantize_planes(nullptr, 1, &mj, mj.units, ctx->d_error, ctx->sm_count, s);
       *launched += 1;
+    }
+    if (r.gather) {
+      if (take()) {
+        hrb::MxGather mg{};
+        mg.map_tiles = base + r.o_mt;
+        mg.map_shift = mj.tile_rows == 64u ? 6u : 7u;
+        mg.map_steps = mj.k_steps;
+        mg.map_block_bytes = hrb::mx_act_block_bytes(mj.tile_rows);
+        mg.rows = r.M;
+        mg.geom = r.g;
+        tj.w_tiles = base + r.o_tc;
+        tj.a_tiles = mg.map_tiles;  // not read: the kernel gathers
+        const int n = hrb::launch_mxf4_gather(tj, qj.tile_rows, tj.m_tiles * tj.n_tiles,
+                                              ctx->sm_count, ctx->d_error, s, mg);
+        if (n < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
+        *launched += static_cast<uint32_t>(n);
+      }
+      HRB_CUDA(ctx, cudaGetLastError());
+      return HRB_OK;
     }
     if (take()) {
       hrb::launch_conv_gather_tiles(base + r.o_mt, mj.tile_rows, mj.k_steps, base + r.o_tc,
@@ -589,7 +616,7 @@ hrb_status conv_execute(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, 
 
 // Launches of one conv run (the sequence conv_execute walks).
 uint32_t conv_launches(const hrb_conv_desc* d, const ConvRun& r) {
-  if (r.tc) return 3;
+  if (r.tc) return r.gather ? 2u : 3u;
   return (d->a != nullptr ? 1u : 0u) + 2u + (d->relu ? 1u : 0u) + (d->cq != nullptr ? 1u : 0u);
 }
 

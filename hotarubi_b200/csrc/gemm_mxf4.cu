@@ -105,7 +105,6 @@ struct MxCfg {
   // single accumulator buffer, whose drain holds up the next tile's MMAs:
   // more warps drain it.
   static constexpr uint32_t kEpiWarps = NT == 64 ? 8u : 16u;
-  static constexpr uint32_t kThreads = 32 * (3 + kEpiWarps);
 };
 
 struct MxParams {
@@ -114,6 +113,7 @@ struct MxParams {
   uint32_t* err;
   MxPeers peers;        // outputs also stored at these byte offsets (peer GPUs)
   TcJob inline_job;
+  MxGather gather;      // the gathering variant's source (convolutions)
 };
 
 __host__ __device__ inline uint32_t mx_planes_of(uint32_t wfmt) {
@@ -220,6 +220,68 @@ __device__ __forceinline__ void sf_copy(uint32_t taddr, uint64_t desc) {
                : "memory");
 }
 
+// Global -> shared copies of 16 and 4 bytes that complete asynchronously;
+// `bytes` of the source are read and the rest zero-filled (0: all zeros,
+// the source is not read).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(bytes)
+               : "memory");
+}
+// Arrives on the mbarrier once this thread's earlier cp.async copies have
+// landed (the barrier's expected count includes this arrival).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// The gathering variant's activation block of one K step (MXFP4, 256-channel
+// planes, so a step is one (channel plane, tap) of the convolution): lane l
+// copies, for tile rows l, l + 32 kWarps, ..., the step's three digit-plane rows
+// (8 chunks of 16 bytes each, re-swizzled from the map's row to the tile's
+// row) and their scale words from the encoded input map; rows outside the
+// map or past M are zero-filled.
+template <uint32_t NT, uint32_t kWarps>
+__device__ __forceinline__ void gather_block(const MxGather& g, uint8_t* blk, uint32_t row0,
+                                             uint32_t step, uint32_t lane) {
+  const ConvGeom& geom = g.geom;
+  const uint32_t taps = geom.kh * geom.kh;
+  const uint32_t tap = step % taps, plane_in = step / taps;  // bp = 8: one map step
+  const uint32_t map_nt = 1u << g.map_shift;
+  const uint32_t dst0 = smem_addr(blk);
+#pragma unroll 1
+  for (uint32_t dr = lane; dr < NT; dr += 32u * kWarps) {
+    const uint32_t row = row0 + dr;
+    const int64_t src = row < g.rows ? conv_source_row(geom, row, tap) : -1;
+    const uint32_t pos = src >= 0 ? static_cast<uint32_t>(src) : 0u;
+    const uint32_t sr = pos & (map_nt - 1u);
+    const uint8_t* sblk =
+        g.map_tiles + (static_cast<size_t>(pos >> g.map_shift) * g.map_steps + plane_in) *
+                          g.map_block_bytes;
+    const uint32_t n16 = src >= 0 ? 16u : 0u, n4 = src >= 0 ? 4u : 0u;
+#pragma unroll
+    for (uint32_t p = 0; p < 3; ++p) {
+      const uint8_t* srow = sblk + (p * map_nt + sr) * kRowB;
+      const uint32_t drow = dst0 + (p * NT + dr) * kRowB;
+#pragma unroll
+      for (uint32_t c = 0; c < 8; ++c) {
+        cp_async16(drow + ((c ^ (dr & 7u)) << 4), srow + ((c ^ (sr & 7u)) << 4), n16);
+      }
+#pragma unroll
+      for (uint32_t h = 0; h < 2; ++h) {
+        cp_async4(dst0 + mx_act_sf_offset(NT, p * NT + dr, 4u * h),
+                  sblk + mx_act_sf_offset(map_nt, p * map_nt + sr, 4u * h), n4);
+      }
+    }
+  }
+}
+
 // The MXINT8 copy of rows j0 .. j0 + 15 of this warp's output block (32
 // columns, one per lane; columns past N count as zero): the block's key is a
 // warp max, each lane encodes its element (QuantizeBlock / EncodeMxint8 rules,
@@ -272,9 +334,21 @@ __device__ __forceinline__ bool ring_drain(const Ring& r, uint32_t n, uint32_t* 
   return ok;
 }
 
-template <uint32_t NT, uint32_t WP, uint32_t KB>
-__global__ void __launch_bounds__(MxCfg<NT, WP, KB>::kThreads, 1)
+// Warps of a launch: the role warps (0 producer, 1 MMA, 2 split-ring
+// producer or, gathering, the first gathering warp), the extra gathering
+// warps, then the epilogue warps.
+constexpr uint32_t kGatherWarps = 2;
+template <uint32_t NT, uint32_t WP, uint32_t KB, bool kGather>
+struct MxWarps {
+  static constexpr uint32_t kFirstEpi = kGather ? 2u + kGatherWarps : 3u;
+  static constexpr uint32_t kThreads = 32u * (kFirstEpi + MxCfg<NT, WP, KB>::kEpiWarps);
+};
+
+template <uint32_t NT, uint32_t WP, uint32_t KB, bool kGather>
+__global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
     k_gemm_mxf4(const __grid_constant__ MxParams p) {
+  static_assert(!kGather || (WP == 1 && KB == 4), "the gathering variant is MXFP4 only");
+  constexpr uint32_t kFirstEpi = MxWarps<NT, WP, KB, kGather>::kFirstEpi;
   using Cfg = MxCfg<NT, WP, KB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -297,7 +371,8 @@ __global__ void __launch_bounds__(MxCfg<NT, WP, KB>::kThreads, 1)
       }
     }
     for (uint32_t s = 0; s < Cfg::kWSlots; ++s) {
-      mbar_init(&wring.full[s], 1);
+      // Gathering: the weight producer's arrival and one per gathering lane.
+      mbar_init(&wring.full[s], kGather ? 1u + 32u * kGatherWarps : 1u);
       mbar_init(&wring.empty[s], 1);
     }
     for (uint32_t b = 0; b < Cfg::kDBufs; ++b) {
@@ -316,7 +391,26 @@ __global__ void __launch_bounds__(MxCfg<NT, WP, KB>::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
 
-  if (warp == 0 || (Cfg::kSplit && warp == 2)) {
+  if (kGather && warp >= 2 && warp < 2 + kGatherWarps) {
+    // Gathering lanes: the activation half of every ring slot, in the weight
+    // producer's order, once the slot is free; gathering warp g takes every
+    // kGatherWarps-th group of 32 tile rows.
+    const TcJob& job = p.inline_job;
+    uint32_t n = 0;
+    for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+      const uint32_t row0 = (tile / job.n_tiles) * NT;
+      for (uint32_t i = 0; i < job.k_steps && ok; ++i, ++n) {
+        const uint32_t sl = n % wring.slots;
+        if (n >= wring.slots) ok = mbar_wait(&wring.empty[sl], ((n / wring.slots) - 1) & 1u, p.err);
+        ok = __all_sync(0xFFFFFFFFu, ok);
+        if (!ok) break;
+        gather_block<NT, kGatherWarps>(p.gather, wbase + sl * Cfg::kWSlot + kWChunk, row0, i,
+                                       lane + 32u * (warp - 2u));
+        cp_async_arrive(&wring.full[sl]);
+      }
+    }
+    cp_async_wait_all();
+  } else if (warp == 0 || (Cfg::kSplit && warp == 2)) {
     // Warp 0 lane 0 streams weight chunks (and, with combined rings, the
     // activation blocks too); warp 2 lane 0 the activation blocks of split
     // rings.  Each tile's fields are loaded one tile ahead.
@@ -332,11 +426,11 @@ __global__ void __launch_bounds__(MxCfg<NT, WP, KB>::kThreads, 1)
         if (weights) {
           for (uint32_t c = 0; c < k_steps * WP && ok; ++c, ++n) {
             const uint32_t sl = n % ring.slots;
-            ok = ring_acquire(ring, n, Cfg::kWSlot, p.err);
+            ok = ring_acquire(ring, n, kGather ? kWChunk : Cfg::kWSlot, p.err);
             if (!ok) break;
             bulk_g2s(wbase + sl * Cfg::kWSlot, ti.w + static_cast<size_t>(c) * kWChunk, kWChunk,
                      &ring.full[sl]);
-            if (!Cfg::kSplit) {
+            if (!Cfg::kSplit && !kGather) {
               bulk_g2s(wbase + sl * Cfg::kWSlot + kWChunk,
                        ti.a + static_cast<size_t>(c) * Cfg::kABlock, Cfg::kABlock,
                        &ring.full[sl]);
@@ -383,6 +477,8 @@ __global__ void __launch_bounds__(MxCfg<NT, WP, KB>::kThreads, 1)
           }
           if (!ok) break;
           tc_fence_after();
+          // Gathered blocks were written through the generic proxy.
+          if constexpr (kGather) fence_proxy_async_smem();
           const uint32_t a_planes =
               Cfg::kSplit ? smem_addr(abase + as * Cfg::kABlock)
                           : smem_addr(wbase + (nw % Cfg::kWSlots) * Cfg::kWSlot + kWChunk);
@@ -438,12 +534,12 @@ __global__ void __launch_bounds__(MxCfg<NT, WP, KB>::kThreads, 1)
         mma_commit(&acc_full[b]);
       }
     }
-  } else if (warp >= 3) {
+  } else if (warp >= kFirstEpi) {
     const uint32_t sp = warp & 3u;
     // Token rows [r0, r1) of each tile: the epilogue warps of a lane quarter
     // split the tile's rows.
     constexpr uint32_t kRowsPer = NT / (Cfg::kEpiWarps / 4);
-    const uint32_t r0 = ((warp - 3u) / 4u) * kRowsPer, r1 = r0 + kRowsPer;
+    const uint32_t r0 = ((warp - kFirstEpi) / 4u) * kRowsPer, r1 = r0 + kRowsPer;
     uint32_t t = 0;
     MxTile next = tile_info<NT>(p, blockIdx.x);
     for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++t) {
@@ -620,11 +716,9 @@ __global__ void k_tile_weights_mxf4(const uint8_t* __restrict__ w, const uint8_t
 
 template <uint32_t NT, uint32_t WP, uint32_t KB>
 int launch_mx(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, int sm_count,
-              uint32_t* err, cudaStream_t s, const MxPeers* peers) {
+              uint32_t* err, cudaStream_t s, const MxPeers* peers,
+              const MxGather* gather = nullptr) {
   using Cfg = MxCfg<NT, WP, KB>;
-  if (!set_smem_limit_once(reinterpret_cast<const void*>(k_gemm_mxf4<NT, WP, KB>), Cfg::kSmem)) {
-    return -1;
-  }
   MxParams p{};
   p.tiles = tiles_dev;
   p.total_tiles = tiles;
@@ -632,7 +726,22 @@ int launch_mx(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, 
   if (peers != nullptr) p.peers = *peers;
   if (inline_job != nullptr) p.inline_job = *inline_job;
   const uint32_t grid = std::min<uint32_t>(tiles, static_cast<uint32_t>(sm_count));
-  k_gemm_mxf4<NT, WP, KB><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(p);
+  if constexpr (WP == 1 && KB == 4) {
+    if (gather != nullptr) {
+      p.gather = *gather;
+      const void* fn = reinterpret_cast<const void*>(k_gemm_mxf4<NT, WP, KB, true>);
+      if (!set_smem_limit_once(fn, Cfg::kSmem)) return -1;
+      k_gemm_mxf4<NT, WP, KB, true>
+          <<<grid, MxWarps<NT, WP, KB, true>::kThreads, Cfg::kSmem, s>>>(p);
+      return cudaPeekAtLastError() == cudaSuccess ? 1 : -1;
+    }
+  }
+  if (gather != nullptr) return -1;
+  if (!set_smem_limit_once(reinterpret_cast<const void*>(k_gemm_mxf4<NT, WP, KB, false>),
+                           Cfg::kSmem)) {
+    return -1;
+  }
+  k_gemm_mxf4<NT, WP, KB, false><<<grid, MxWarps<NT, WP, KB, false>::kThreads, Cfg::kSmem, s>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? 1 : -1;
 }
 
@@ -697,6 +806,15 @@ void launch_tile_weights_mxf4(uint32_t wfmt, const uint8_t* w, const uint8_t* ws
 
 void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out) {
   for (uint32_t i = 0; i < job.m_tiles * job.n_tiles; ++i) out[i] = make_tile(job, nt, i);
+}
+
+int launch_mxf4_gather(const TcJob& inline_job, uint32_t nt, uint32_t tiles, int sm_count,
+                       uint32_t* err, cudaStream_t s, const MxGather& gather) {
+  if (tiles == 0) return 0;
+  if (inline_job.wfmt != HRB_WFMT_MXFP4 || gather.geom.bp != 8u) return -1;
+  if (nt == 64) return launch_mx<64, 1, 4>(nullptr, &inline_job, tiles, sm_count, err, s, nullptr, &gather);
+  if (nt == 128) return launch_mx<128, 1, 4>(nullptr, &inline_job, tiles, sm_count, err, s, nullptr, &gather);
+  return -1;
 }
 
 int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t wfmt,

@@ -106,6 +106,20 @@ struct MxPeers {
   uint32_t count;
 };
 
+// The gathering variant of the MXFP4 kernel (convolutions whose channel
+// planes are 256 wide, so one K step is one (plane, tap)): the activation
+// block of each (tile, step) is assembled in shared memory from the input
+// map's own operand blocks (map_shift: log2 of their tile height) instead of
+// being read as one prepared block.  `rows` = M.
+struct MxGather {
+  const uint8_t* map_tiles;
+  uint32_t map_shift, map_steps, map_block_bytes, rows;
+  ConvGeom geom;
+};
+// One inline job (inline_job.a_tiles unused), nt = 64 or 128.
+int launch_mxf4_gather(const TcJob& inline_job, uint32_t nt, uint32_t tiles, int sm_count,
+                       uint32_t* err, cudaStream_t stream, const MxGather& gather);
+
 // One launch over `tiles` output tiles: the device array tiles_dev, or, when
 // it is null, the tiles of the single *inline_job.  `peers` may be null.
 int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t wfmt,

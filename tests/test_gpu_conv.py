@@ -119,6 +119,8 @@ CASES = [  # wfmt, images, H, W, cin, cout, kh, stride, order, bias, residual, r
     (0, 1, 8, 4, 512, 24, 3, 1, 0, True, False, True),      # two channel planes
     (1, 1, 4, 8, 512, 16, 1, 2, 1, True, True, False),
     (2, 4, 12, 6, 32, 8, 1, 1, 0, False, False, True),
+    (0, 3, 10, 14, 256, 136, 3, 2, 1, True, True, True),    # the GEMM gathers its own blocks
+    (0, 2, 16, 20, 256, 64, 1, 1, 0, False, False, False),
 ]
 
 
