@@ -56,6 +56,7 @@ class GemmDesc(ctypes.Structure):
         ("accumulate", ctypes.c_uint32),
         ("pieces", ctypes.c_void_p), ("npieces", ctypes.c_uint32),
         ("cq", ctypes.c_void_p), ("cscale", ctypes.c_void_p), ("cquant", ctypes.c_uint32),
+        ("wcol_scale", ctypes.c_void_p),
     ]
 
 
@@ -276,7 +277,8 @@ class Library:
     @staticmethod
     def desc(wfmt, M, N, K, *, a=None, lda=None, quant=QUANT_HOST, aq=None, ascale=None,
              w=None, wscale=None, bias=None, c=None, ldc=None, accumulate=False,
-             pieces=None, mode=MODE_EXACT, cq=None, cscale=None, cquant=QUANT_VEC):
+             pieces=None, mode=MODE_EXACT, cq=None, cscale=None, cquant=QUANT_VEC,
+             wcol_scale=None):
         d = GemmDesc()
         d.wfmt, d.mode, d.M, d.N, d.K = wfmt, mode, M, N, K
         d.a = _ptr(a)
@@ -289,6 +291,7 @@ class Library:
         d.ldc = ldc if ldc is not None else N
         d.accumulate = 1 if accumulate else 0
         d.cq, d.cscale, d.cquant = _ptr(cq), _ptr(cscale), cquant
+        d.wcol_scale = _ptr(wcol_scale)
         if pieces is not None:
             arr = np.ascontiguousarray(pieces, dtype=np.uint32)
             d._pieces_keep = arr  # keep alive

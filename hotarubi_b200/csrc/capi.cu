@@ -189,6 +189,14 @@ hrb_status check_desc(hrb_ctx* ctx, const hrb_gemm_desc* d, uint32_t* pieces,
     }
   }
   if (!aligned(d->w, 16)) return fail(ctx, HRB_EINVAL, "weights are not 16-byte aligned");
+  if (d->wcol_scale != nullptr) {
+    if (d->accumulate) {
+      return fail(ctx, HRB_EINVAL, "per-column weight scales do not combine with accumulate");
+    }
+    if (!aligned(d->wcol_scale, 4)) {
+      return fail(ctx, HRB_EINVAL, "per-column weight scales are not 4-byte aligned");
+    }
+  }
   if (d->c != nullptr && d->ldc < d->N) {
     return fail(ctx, HRB_EINVAL, "ldc %u < N %u", d->ldc, d->N);
   }
@@ -221,6 +229,7 @@ hrb::DenseJob make_dense_job(const hrb_gemm_desc* d, const int8_t* aq, const uin
   j.w = d->w;
   j.wscale = d->wscale;
   j.bias = d->bias;
+  j.colscale = d->wcol_scale;
   j.c = d->c;
   j.M = d->M;
   j.N = d->N;
@@ -287,8 +296,12 @@ size_t tc_act_bytes(const hrb_gemm_desc* d) {
 size_t tc_weight_bytes(const hrb_gemm_desc* d) {
   return hrb::mx_weight_bytes(d->wfmt, d->N, blocks_of(d->K));
 }
+// (scale, bias) pairs of a GEMM with per-column scales: 8 bytes a column.
+size_t tc_epv_bytes(const hrb_gemm_desc* d) {
+  return d->wcol_scale != nullptr ? align_up(size_t{d->N} * 8u, 1024) : 0u;
+}
 size_t tc_scratch_bytes(const hrb_gemm_desc* d) {
-  return align_up(tc_act_bytes(d), 1024) + align_up(tc_weight_bytes(d), 1024);
+  return align_up(tc_act_bytes(d), 1024) + align_up(tc_weight_bytes(d), 1024) + tc_epv_bytes(d);
 }
 
 // The encoder job writing the tensor-core operand blocks of an M x K FP32
@@ -327,6 +340,11 @@ void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJo
   tj->a_tiles = act;
   tj->w_tiles = wt;
   tj->bias = d->bias;
+  if (d->wcol_scale != nullptr) {
+    tj->epv = reinterpret_cast<const float*>(
+        wt + align_up(tc_weight_bytes(d), 1024));  // (scale, bias) pairs after the weights
+    tj->bias = nullptr;
+  }
   tj->c = d->c;
   tj->ldc = d->ldc;
   tj->accumulate = d->accumulate != 0;
@@ -336,9 +354,20 @@ void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJo
 }
 
 // Translates the weights of one tensor-core GEMM into the chunk layout.
+// With per-column scales, also interleaves (scale, bias) pairs (bias 0 when
+// there is none) with two strided copies.
 void tc_translate(const hrb_gemm_desc* d, const hrb::TcJob& tj, cudaStream_t s) {
   hrb::launch_tile_weights_mxf4(d->wfmt, d->w, d->wscale, d->N, blocks_of(d->K),
                                 const_cast<uint8_t*>(tj.w_tiles), s);
+  if (tj.epv != nullptr) {
+    auto* ep = const_cast<float*>(tj.epv);
+    cudaMemcpy2DAsync(ep, 8, d->wcol_scale, 4, 4, d->N, cudaMemcpyDeviceToDevice, s);
+    if (d->bias != nullptr) {
+      cudaMemcpy2DAsync(ep + 1, 8, d->bias, 4, 4, d->N, cudaMemcpyDeviceToDevice, s);
+    } else {
+      cudaMemset2DAsync(ep + 1, 8, 0, 4, d->N, s);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -1013,6 +1042,7 @@ hrb_status hrb_gemm_dense_host(hrb_ctx* ctx, const hrb_gemm_desc* d) {
   const size_t w_bytes = size_t{d->N} * weight_row_bytes(d->wfmt, kb);
   const size_t ws_bytes = size_t{d->N} * kb;
   const size_t b_bytes = d->bias ? size_t{d->N} * 4u : 0;
+  const size_t cs_bytes = d->wcol_scale ? size_t{d->N} * 4u : 0;
   const size_t c_bytes = d->c ? size_t{d->M} * d->N * 4u : 0;
   const uint32_t kbq = blocks_of(d->N);
   const size_t q_bytes = d->cq ? size_t{d->M} * kbq * 32u : 0;
@@ -1023,6 +1053,7 @@ hrb_status hrb_gemm_dense_host(hrb_ctx* ctx, const hrb_gemm_desc* d) {
   const size_t o_w = off; off = align_up(off + w_bytes, 256);
   const size_t o_ws = off; off = align_up(off + ws_bytes, 256);
   const size_t o_b = off; off = align_up(off + b_bytes, 256);
+  const size_t o_cs = off; off = align_up(off + cs_bytes, 256);
   const size_t o_c = off; off = align_up(off + c_bytes, 256);
   const size_t o_q = off; off = align_up(off + q_bytes, 256);
   const size_t o_qs = off; off = align_up(off + qs_bytes, 256);
@@ -1049,6 +1080,10 @@ hrb_status hrb_gemm_dense_host(hrb_ctx* ctx, const hrb_gemm_desc* d) {
   if (d->bias) {
     HRB_CUDA(ctx, cudaMemcpyAsync(base + o_b, d->bias, b_bytes, cudaMemcpyHostToDevice, s));
     dd.bias = reinterpret_cast<const float*>(base + o_b);
+  }
+  if (d->wcol_scale) {
+    HRB_CUDA(ctx, cudaMemcpyAsync(base + o_cs, d->wcol_scale, cs_bytes, cudaMemcpyHostToDevice, s));
+    dd.wcol_scale = reinterpret_cast<const float*>(base + o_cs);
   }
   dd.c = d->c ? reinterpret_cast<float*>(base + o_c) : nullptr;
   dd.ldc = d->N;

@@ -132,7 +132,7 @@ __host__ __device__ inline MxTile make_tile(const TcJob& job, uint32_t nt, uint3
         static_cast<size_t>(n_tile) * job.k_steps * mx_planes_of(job.wfmt) * kWChunk;
   t.a = job.a_tiles + static_cast<size_t>(mt) * job.k_steps * act_block_bytes(job.wfmt, nt);
   t.c = job.c != nullptr ? job.c + static_cast<size_t>(row0) * job.ldc + col0 : nullptr;
-  t.bias = job.bias != nullptr ? job.bias + col0 : nullptr;
+  t.bias = job.epv != nullptr ? job.epv + 2u * col0 : (job.bias != nullptr ? job.bias + col0 : nullptr);
   const uint32_t kbq = (job.N + 31u) / 32u;  // blocks per row of the MXINT8 copy
   t.cq = job.cq != nullptr ? job.cq + static_cast<size_t>(row0) * kbq * 32u + col0 : nullptr;
   t.cscale = job.cq != nullptr ? job.cscale + static_cast<size_t>(row0) * kbq + col0 / 32u
@@ -140,7 +140,7 @@ __host__ __device__ inline MxTile make_tile(const TcJob& job, uint32_t nt, uint3
   t.rows = job.M - row0 < nt ? job.M - row0 : nt;
   t.cols_kbq = (job.N - col0 < kTileW ? job.N - col0 : kTileW) | (kbq << 8);
   t.ldc = job.ldc;
-  t.flags = job.k_steps | (job.relu ? 0x20000000u : 0u) |
+  t.flags = job.k_steps | (job.epv != nullptr ? 0x10000000u : 0u) | (job.relu ? 0x20000000u : 0u) |
             (job.cquant == HRB_QUANT_VEC ? 0x40000000u : 0u) | (job.accumulate ? 0x80000000u : 0u);
   return t;
 }
@@ -422,7 +422,7 @@ __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
       for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
         const MxTile ti = next;
         if (tile + gridDim.x < p.total_tiles) next = tile_info<NT>(p, tile + gridDim.x);
-        const uint32_t k_steps = (ti.flags & 0x1FFFFFFFu);
+        const uint32_t k_steps = (ti.flags & 0x0FFFFFFFu);
         if (weights) {
           for (uint32_t c = 0; c < k_steps * WP && ok; ++c, ++n) {
             const uint32_t sl = n % ring.slots;
@@ -453,11 +453,11 @@ __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
     if (lane == 0) {
       uint32_t na = 0, nw = 0, t = 0;
       const uint32_t sfa = tmem + Cfg::kColSfa;
-      uint32_t next_steps = tile_info<NT>(p, blockIdx.x).flags & 0x1FFFFFFFu;
+      uint32_t next_steps = tile_info<NT>(p, blockIdx.x).flags & 0x0FFFFFFFu;
       for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++t) {
         const uint32_t k_steps = next_steps;
         if (tile + gridDim.x < p.total_tiles) {
-          next_steps = tile_info<NT>(p, tile + gridDim.x).flags & 0x1FFFFFFFu;
+          next_steps = tile_info<NT>(p, tile + gridDim.x).flags & 0x0FFFFFFFu;
         }
         const uint32_t b = t % Cfg::kDBufs;
         if (t >= Cfg::kDBufs) ok = mbar_wait(&acc_empty[b], ((t / Cfg::kDBufs) - 1) & 1u, p.err);
@@ -555,7 +555,17 @@ __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
       const bool col_ok = col < cols;
       const bool acc = (ti.flags >> 31) != 0;
       const bool relu = ((ti.flags >> 29) & 1u) != 0;
-      const float bias = (ti.bias != nullptr && col_ok) ? ti.bias[col] : 0.0f;
+      const bool scaled = ((ti.flags >> 28) & 1u) != 0;
+      float bias = 0.0f, scale = 1.0f;
+      if (ti.bias != nullptr && col_ok) {
+        if (scaled) {
+          const float2 sb = reinterpret_cast<const float2*>(ti.bias)[col];
+          scale = sb.x;
+          bias = sb.y;
+        } else {
+          bias = ti.bias[col];
+        }
+      }
       float* cbase = ti.c + col;
       const uint32_t npeers = p.peers.count;
       // The MXINT8 copy: this warp's 32 columns are one block of the next
@@ -583,7 +593,8 @@ __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
           for (uint32_t j = 0; j < 16; ++j) {
             if (j0 + j < ti.rows) {
               if (acc) x[j] += cbase[static_cast<size_t>(j0 + j) * ti.ldc];
-              x[j] += bias;
+              if (scaled) x[j] = __fmul_rn(x[j], scale);
+              x[j] = __fadd_rn(x[j], bias);
               if (relu) x[j] = x[j] > 0.0f ? x[j] : 0.0f;
               if (ti.c != nullptr) cbase[static_cast<size_t>(j0 + j) * ti.ldc] = x[j];
             }

@@ -138,6 +138,7 @@ struct DenseJob {
   const uint8_t* w;       // format dependent, [N][...]
   const uint8_t* wscale;  // [N][kb]
   const float* bias;      // [N] or null
+  const float* colscale;  // [N] or null: the chain times colscale[n], then the bias
   float* c;               // [M][ldc]
   uint32_t tile_begin;
   uint32_t tiles_n;       // column tiles

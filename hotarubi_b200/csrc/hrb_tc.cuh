@@ -16,6 +16,10 @@ struct TcJob {
   const uint8_t* a_tiles;  // [m_tiles][k_steps][NT rows][128 B]
   const uint8_t* w_tiles;  // [n_tiles][k_steps][chunk]
   const float* bias;       // [N] or null
+  // Per-column scale and bias as interleaved pairs [N][2] (hrb_gemm_desc
+  // wcol_scale): the epilogue computes out * scale + bias in two roundings.
+  // Replaces `bias` when set.
+  const float* epv;
   float* c;                // [M][ldc]
   uint32_t M, N, kb, ldc;
   uint32_t wfmt;
@@ -93,7 +97,8 @@ struct MxTile {
   uint32_t rows;        // valid token rows
   uint32_t cols_kbq;    // valid weight columns | blocks per cq row << 8
   uint32_t ldc;
-  uint32_t flags;       // K steps | RELU << 29 | VEC rule for cq << 30 | accumulate << 31
+  uint32_t flags;       // K steps | (scale, bias) pairs << 28 | RELU << 29 | VEC rule for cq << 30
+                        // | accumulate << 31
 };
 static_assert(sizeof(MxTile) == 64, "MxTile is read as four 16-byte loads");
 // The m_tiles * n_tiles tiles of one job (tile index mt * n_tiles + nt).

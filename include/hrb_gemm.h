@@ -209,6 +209,16 @@ typedef struct hrb_gemm_desc {
   int8_t* cq;
   uint8_t* cscale;
   uint32_t cquant;
+  /* Optional FP32 scale per output column [N] (NULL: none): each output's
+   * finished chain is multiplied by wcol_scale[n] before the bias is added,
+   * in HRB_MODE_EXACT with the ISS's FP32 multiply (fp32.hpp:77-92, bit for
+   * bit), in HRB_MODE_FAST with the IEEE multiply (round to nearest even).
+   * With W8 codes whose block scale bytes are all 133 (2^6, so every code
+   * counts as its integer value) this is int8 weights with a per-output-
+   * channel scale and a fused scale/bias epilogue, a format the reference
+   * does not have (hotarubi places such a matrix as MXINT8 blocks, PlaceW8).
+   * Not with accumulate.  4-byte aligned. */
+  const float* wcol_scale;
 } hrb_gemm_desc;
 
 /* One dense GEMM, all pointers device pointers, asynchronous on `stream`. */
@@ -251,6 +261,9 @@ HRB_API hrb_status hrb_quantize_mxint8(hrb_ctx* ctx, const float* x, uint32_t ro
 
 typedef struct hrb_plan hrb_plan;
 
+/* Weights are translated once, here: they must not change while the plan
+ * lives.  HRB_MODE_FAST GEMMs with wcol_scale also read the column scales
+ * and the bias here. */
 HRB_API hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs,
                            uint32_t count, hrb_plan** out);
 /* Launches the whole batch on `stream`; returns the number of kernels it

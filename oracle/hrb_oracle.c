@@ -361,6 +361,11 @@ void hrbo_fp32_add_n(const uint32_t* a, const uint32_t* b, uint32_t* out,
   for (size_t i = 0; i < n; ++i) out[i] = hrbo_fp32_add(a[i], b[i]);
 }
 
+void hrbo_fp32_mul_n(const uint32_t* a, const uint32_t* b, uint32_t* out,
+                     size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = hrbo_fp32_mul(a[i], b[i]);
+}
+
 void hrbo_round_scaled_n(const int64_t* sum, const int32_t* exponent,
                          uint32_t* out, size_t n) {
   for (size_t i = 0; i < n; ++i) out[i] = hrbo_round_scaled(sum[i], exponent[i]);

@@ -191,8 +191,11 @@ void hrbo_gacc_dense(uint32_t tokens, uint32_t slots, uint32_t corners,
                      const uint32_t* w, const uint8_t* rows,
                      uint64_t row_stride, uint32_t* out, int accumulate);
 
-/* Element-wise array forms of hrbo_fp32_add and hrbo_round_scaled. */
+/* Element-wise array forms of hrbo_fp32_add, hrbo_fp32_mul and
+ * hrbo_round_scaled. */
 void hrbo_fp32_add_n(const uint32_t* a, const uint32_t* b, uint32_t* out,
+                     size_t n);
+void hrbo_fp32_mul_n(const uint32_t* a, const uint32_t* b, uint32_t* out,
                      size_t n);
 void hrbo_round_scaled_n(const int64_t* sum, const int32_t* exponent,
                          uint32_t* out, size_t n);

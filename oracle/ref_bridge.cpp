@@ -262,6 +262,12 @@ void hrbref_fp32_add_n(const uint32_t* a, const uint32_t* b, uint32_t* out,
   for (size_t i = 0; i < n; ++i) out[i] = hotarubi::iss::Fp32Add(a[i], b[i]);
 }
 
+// tools/iss/fp32.hpp:77-92
+void hrbref_fp32_mul_n(const uint32_t* a, const uint32_t* b, uint32_t* out,
+                       size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = hotarubi::iss::Fp32Mul(a[i], b[i]);
+}
+
 void hrbref_tb_fp32_add_n(const uint32_t* a, const uint32_t* b, uint32_t* out,
                           size_t n) {
   for (size_t i = 0; i < n; ++i) out[i] = hotarubi::tb::Fp32Add(a[i], b[i]);

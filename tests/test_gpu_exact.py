@@ -240,14 +240,15 @@ def _weights(rng, wfmt, n, kb):
 
 
 def _run_dense(hrb, wfmt, x, w, ws, n, *, bias=None, c_init=None, pieces=None,
-               mode=0, fp32_input=True):
+               mode=0, fp32_input=True, colscale=None):
     from hotarubi_b200 import capi
     m, k = x.shape
     c = dev(c_init.view(np.float32)) if c_init is not None else torch.zeros(
         (m, n), dtype=torch.float32, device="cuda")
     kw = dict(w=dev(w), wscale=dev(ws), c=c, bias=None if bias is None else dev(bias),
-              accumulate=c_init is not None, pieces=pieces, mode=mode)
-    keep = [kw["w"], kw["wscale"], kw["bias"]]
+              accumulate=c_init is not None, pieces=pieces, mode=mode,
+              wcol_scale=None if colscale is None else dev(colscale))
+    keep = [kw["w"], kw["wscale"], kw["bias"], kw["wcol_scale"]]
     if fp32_input:
         a = dev(x.view(np.float32))
         keep.append(a)
@@ -289,6 +290,88 @@ def test_dense_exact_bias_accumulate_pieces(hrb, wfmt):
     want = cpu.gemm_dense(wfmt, q, s, w, ws, n, bias_bits=bias, c_init=c0, pieces=[2, 4, 3])
     got = _run_dense(hrb, wfmt, x, w, ws, n, bias=bias, c_init=c0, pieces=[2, 4, 3])
     assert (got == want).all()
+
+
+def _boundary_scales(rng, c, n):
+    """Column scales: random magnitudes, zeros, ones that overflow, and ones
+    that put row 0's product a few ulps either side of 2^-126 (where the
+    ISS, rounding to 24 bits before it flushes, and an IEEE multiply with
+    flush to zero part ways)."""
+    cs = (rng.uniform(0.5, 2.0, n) * np.ldexp(1.0, rng.integers(-20, 20, n))).astype(np.float32)
+    cs[rng.random(n) < 0.3] *= -1
+    cs[5] = 0.0
+    cs[6] = np.float32(3e38)
+    v = c[0].view(np.float32).astype(np.float64)
+    for j in range(8, min(n, 40)):
+        if v[j] == 0 or not np.isfinite(v[j]):
+            continue
+        base = np.float32(2.0**-126 / abs(v[j]))
+        cs[j] = np.frombuffer(np.array([base.view(np.uint32) + (j % 7) - 3], np.uint32).tobytes(),
+                              np.float32)[0]
+    return cs
+
+
+@pytest.mark.parametrize("wfmt", [0, 1, 2])
+def test_dense_exact_column_scales(hrb, wfmt):
+    """wcol_scale in the exact mode: the ISS's FP32 multiply, then the bias
+    add, bit for bit (FP32 and MXINT8 inputs, ragged sizes)."""
+    rng = np.random.default_rng(300 + wfmt)
+    for m, n, kb in ((70, 72, 9), (1, 40, 3), (130, 200, 17)):
+        x = rng.standard_normal((m, kb * 32 - 3)).astype(np.float32).view(np.uint32)
+        w, ws = _weights(rng, wfmt, n, kb)
+        bias = (rng.standard_normal(n).astype(np.float32) * 0.01).view(np.uint32)
+        q, s = cpu.encode_mxint8(x)
+        plain = cpu.gemm_dense(wfmt, q, s, w, ws, n)
+        cs = _boundary_scales(rng, plain, n)
+        for b in (None, bias):
+            want = cpu.gemm_dense(wfmt, q, s, w, ws, n, bias_bits=b,
+                                  colscale_bits=cs.view(np.uint32))
+            got = _run_dense(hrb, wfmt, x, w, ws, n, bias=b, colscale=cs)
+            assert (got == want).all(), (m, n, kb, b is None)
+            got = _run_dense(hrb, wfmt, x, w, ws, n, bias=b, colscale=cs, fp32_input=False)
+            assert (got == want).all(), (m, n, kb, b is None)
+
+
+def test_dense_exact_column_scales_with_special_chains(hrb):
+    """Chains at infinity or NaN (block scales that overflow) through the
+    column scale: the integer slow path applies the same multiply."""
+    rng = np.random.default_rng(17)
+    m, n, kb = 32, 64, 6
+    for wfmt in (0, 1, 2):
+        x = rng.standard_normal((m, kb * 32)).astype(np.float32).view(np.uint32)
+        w, ws = _weights(rng, wfmt, n, kb)
+        ws[::5, 2] = 254
+        q, s = cpu.encode_mxint8(x)
+        cs = (rng.standard_normal(n) * 4).astype(np.float32)
+        cs[::9] = 0.0
+        bias = (rng.standard_normal(n).astype(np.float32)).view(np.uint32)
+        want = cpu.gemm_dense(wfmt, q, s, w, ws, n, bias_bits=bias, colscale_bits=cs.view(np.uint32))
+        got = _run_dense(hrb, wfmt, x, w, ws, n, bias=bias, colscale=cs)
+        assert (got == want).all(), wfmt
+
+
+def test_dense_column_scales_host_entry_and_accumulate_refused(hrb):
+    from hotarubi_b200 import capi
+    rng = np.random.default_rng(23)
+    m, n, kb = 48, 80, 7
+    x = rng.standard_normal((m, kb * 32)).astype(np.float32)
+    w, ws = _weights(rng, 1, n, kb)
+    ws[:] = 133  # int8 weights: every code counts as its integer value
+    bias = (rng.standard_normal(n) * 0.01).astype(np.float32)
+    cs = (rng.uniform(0.5, 2.0, n) * 2.0**-10).astype(np.float32)
+    q, s = cpu.encode_mxint8(x.view(np.uint32))
+    want = cpu.gemm_dense(1, q, s, w, ws, n, bias_bits=bias.view(np.uint32),
+                          colscale_bits=cs.view(np.uint32))
+    c = np.zeros((m, n), np.float32)
+    hrb.dense_host(capi.Library.desc(1, m, n, kb * 32, a=x, w=w, wscale=ws, bias=bias, c=c,
+                                     wcol_scale=cs))
+    assert (c.view(np.uint32) == want).all()
+    t = [dev(x), dev(w), dev(ws), dev(bias), dev(cs)]
+    cd = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    d = capi.Library.desc(1, m, n, kb * 32, a=t[0], w=t[1], wscale=t[2], c=cd, wcol_scale=t[4],
+                          accumulate=True)
+    with pytest.raises(capi.HrbError):
+        hrb.dense(d)
 
 
 def test_dense_on_reference_iss_fixtures(hrb, golden):

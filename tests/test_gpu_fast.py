@@ -72,19 +72,33 @@ def ulp_hist(got, want):
             "4-15": int(((d >= 4) & (d < 16)).sum()), ">=16": int((d >= 16).sum())}
 
 
-def check_fast(hrb, wfmt, m, n, k, *, bias=False, accumulate=False, seed=0, plan=False):
+def check_fast(hrb, wfmt, m, n, k, *, bias=False, accumulate=False, seed=0, plan=False,
+               colscale=False, per_channel_w8=False):
+    """colscale: a random FP32 scale per output column (wcol_scale), applied
+    before the bias (one more rounding, inside the tolerance's slack).
+    per_channel_w8: W8 weights whose block scale bytes are all 133, so the
+    weights are plain int8 values and wcol_scale carries their scale."""
     from hotarubi_b200 import capi
     rng = np.random.default_rng(seed)
     kb = (k + 31) // 32
     kp = kb * 32
     x = rng.standard_normal((m, k)).astype(np.float32)
     w, ws = weights(rng, wfmt, n, kb)
+    if per_channel_w8:
+        ws[:] = 133
     b = (rng.standard_normal(n) * 0.01).astype(np.float32) if bias else None
     c0 = rng.standard_normal((m, n)).astype(np.float32) if accumulate else None
+    cs = None
+    if colscale:
+        cs = (rng.uniform(0.5, 2.0, n) * np.where(rng.random(n) < 0.3, -1.0, 1.0)
+              * np.ldexp(1.0, rng.integers(-12, 4, n))).astype(np.float32)
     a_deq, q, s = dequant_a(x.view(np.uint32))
     w_deq = dequant_w(wfmt, w, ws, n, kp)
     ref = a_deq @ w_deq.T
     absref = np.abs(a_deq) @ np.abs(w_deq).T
+    if cs is not None:
+        ref *= cs.astype(np.float64)
+        absref *= np.abs(cs.astype(np.float64))
     if c0 is not None:
         ref += c0
         absref += np.abs(c0)
@@ -92,9 +106,10 @@ def check_fast(hrb, wfmt, m, n, k, *, bias=False, accumulate=False, seed=0, plan
         ref += b
         absref += np.abs(b)
     c = dev(c0) if c0 is not None else torch.zeros((m, n), dtype=torch.float32, device="cuda")
-    keep = [dev(x), dev(w), dev(ws), None if b is None else dev(b)]
+    keep = [dev(x), dev(w), dev(ws), None if b is None else dev(b),
+            None if cs is None else dev(cs)]
     d = capi.Library.desc(wfmt, m, n, k, a=keep[0], w=keep[1], wscale=keep[2], bias=keep[3],
-                          c=c, accumulate=accumulate, mode=capi.MODE_FAST)
+                          c=c, accumulate=accumulate, mode=capi.MODE_FAST, wcol_scale=keep[4])
     if plan:
         p = hrb.plan([d])
         p.run()
@@ -111,7 +126,8 @@ def check_fast(hrb, wfmt, m, n, k, *, bias=False, accumulate=False, seed=0, plan
                            f"{(err / (absref + 1e-30)).max():.3e} tol {tol:.3e}")
     exact = cpu.gemm_dense(wfmt, q, s, w, ws, n,
                            bias_bits=None if b is None else b.view(np.uint32),
-                           c_init=None if c0 is None else c0.view(np.uint32))
+                           c_init=None if c0 is None else c0.view(np.uint32),
+                           colscale_bits=None if cs is None else cs.view(np.uint32))
     ex = exact.view(np.float32).astype(np.float64)
     rel = np.abs(got - ex) / (np.abs(ex) + 1e-30)
     return {"max_rel_vs_exact": float(rel.max()), "ulp": ulp_hist(got, exact.view(np.float32))}
@@ -133,6 +149,21 @@ def test_fast_bias_and_accumulate(hrb, wfmt):
 @pytest.mark.parametrize("wfmt", [0, 1, 2])
 def test_fast_through_a_plan(hrb, wfmt):
     check_fast(hrb, wfmt, 64, 256, 512, bias=True, plan=True, seed=9 + wfmt)
+
+
+@pytest.mark.parametrize("wfmt", [0, 1, 2])
+@pytest.mark.parametrize("plan", [False, True])
+def test_fast_column_scales(hrb, wfmt, plan):
+    check_fast(hrb, wfmt, 130, 200, 480, bias=True, colscale=True, plan=plan, seed=31 + wfmt)
+    check_fast(hrb, wfmt, 64, 256, 256, colscale=True, plan=plan, seed=41 + wfmt)
+
+
+@pytest.mark.parametrize("shape", [(64, 960, 2560), (1, 16, 64), (200, 136, 416)])
+def test_fast_per_channel_int8_weights(hrb, shape):
+    """int8 weights with a per-output-channel FP32 scale and a fused
+    scale/bias epilogue: W8 codes with block scale bytes 133 plus wcol_scale."""
+    m, n, k = shape
+    check_fast(hrb, 1, m, n, k, bias=True, colscale=True, per_channel_w8=True, seed=m + n)
 
 
 def test_fast_batched_plan_of_mixed_shapes(hrb):

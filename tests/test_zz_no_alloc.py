@@ -88,3 +88,30 @@ def test_no_alloc_mxint8_copy_of_the_output(hrb):
     torch.cuda.synchronize()
     q, s = cpu.quantize_vec(c.cpu().numpy().view(np.uint32))
     assert np.array_equal(cq.cpu().numpy(), q) and np.array_equal(cs.cpu().numpy(), s)
+
+
+def test_noalloc_column_scales_match_the_oracle():
+    """wcol_scale through the no-alloc entry: int8 weights (W8 block scale
+    bytes 133) with a per-column FP32 scale, bit for bit with the oracle."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from hotarubi_b200 import capi
+    from oracle import cpu
+    torch.cuda.set_device(0)
+    rng = np.random.default_rng(99)
+    m, n, kb = 48, 80, 7
+    x = rng.standard_normal((m, kb * 32)).astype(np.float32)
+    w = rng.integers(-128, 128, (n, kb * 32)).astype(np.int8).view(np.uint8)
+    ws = np.full((n, kb), 133, np.uint8)
+    bias = (rng.standard_normal(n) * 0.01).astype(np.float32)
+    cs = (rng.uniform(0.5, 2.0, n) * 2.0**-10).astype(np.float32)
+    q, s = cpu.encode_mxint8(x.view(np.uint32))
+    want = cpu.gemm_dense(1, q, s, w, ws, n, bias_bits=bias.view(np.uint32),
+                          colscale_bits=cs.view(np.uint32))
+    t = [torch.from_numpy(v).cuda() for v in (x, w, ws, bias, cs)]
+    got = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    d = capi.Library.desc(capi.WFMT_W8, m, n, kb * 32, a=t[0], w=t[1], wscale=t[2], bias=t[3],
+                          c=got, wcol_scale=t[4])
+    assert capi.load().hrb_gemm_dense_noalloc(ctypes.byref(d), None) == capi.HRB_OK
+    torch.cuda.synchronize()
+    assert (got.cpu().numpy().view(np.uint32) == want).all()
