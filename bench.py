@@ -383,7 +383,8 @@ def run_reference(args, wl: Workload, rank: int, world: int) -> None:
 # ---------------------------------------------------------------------------
 # Our implementation
 
-def build_batch(torch, lib, capi, wl: Workload, batch: int, mode: int, distinct: int = 4):
+def build_batch(torch, lib, capi, wl: Workload, batch: int, mode: int, distinct: int = 4,
+                w8_kernel: int = 0):
     """B instances on the device: `distinct` seeded operand sets copied into
     B separate buffers (distinct memory, so every instance streams)."""
     sets = [host_operands(wl, i) for i in range(min(distinct, batch))]
@@ -399,7 +400,8 @@ def build_batch(torch, lib, capi, wl: Workload, batch: int, mode: int, distinct:
             a=a_all[b], w=torch.from_numpy(w).cuda(), ws=torch.from_numpy(ws).cuda(),
             bias=None if bias is None else torch.from_numpy(bias).cuda(), c=c_all[b]))
     descs = [capi.Library.desc(wl.wfmt, wl.M, wl.N, wl.K, a=d["a"], w=d["w"], wscale=d["ws"],
-                               bias=d["bias"], c=d["c"], mode=mode) for d in inst]
+                               bias=d["bias"], c=d["c"], mode=mode, w8_kernel=w8_kernel)
+             for d in inst]
     torch.cuda.synchronize()
     return inst, lib.plan(descs), sets
 
@@ -458,7 +460,9 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
     stream = torch.cuda.Stream()
     lib.set_stream(stream.cuda_stream)
     batch = args.batch or wl.batch
-    inst, plan_full, sets = build_batch(torch, lib, capi, wl, batch, mode)
+    w8_bf16 = args.w8_kernel == "bf16" and wl.wfmt == capi.WFMT_W8 and wl.M <= 64
+    inst, plan_full, sets = build_batch(torch, lib, capi, wl, batch, mode,
+                                        w8_kernel=capi.W8_BF16 if w8_bf16 else capi.W8_DIGIT_PLANES)
 
     # Per-kernel device times (the dominant kernel's roofline): each launch
     # of the plan repeated back to back between two events (not the timed
@@ -508,7 +512,7 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
     if rank == 0:
         pk = peaks()
         fast = mode == capi.MODE_FAST
-        kname = "k_gemm_mxf4" if fast else "k_dense_exact"
+        kname = ("k_gemm_w8bf" if w8_bf16 else "k_gemm_mxf4") if fast else "k_dense_exact"
         qname = "k_quantize_planes" if fast else "k_quantize"
         gemm_gbs = batch * wl.bytes_gemm() / (gemm_ms / 1e3) / 1e9
         quant_gbs = batch * wl.bytes_quant() / (quant_ms / 1e3) / 1e9
@@ -554,6 +558,7 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
             "config": {"workload": wl.name, "batch_per_gpu": batch,
                        "M": wl.M, "N": wl.N, "K": wl.K, "format": FMT_NAMES[wl.wfmt],
                        "bias": wl.bias, "mode": args.mode,
+                       **({"w8_kernel": args.w8_kernel} if wl.wfmt == capi.WFMT_W8 else {}),
                        "activations": "fp32, encoded to mxint8 on device each step",
                        "l2": f"working set {batch * wl.bytes_step() / 1e6:.0f} MB per GPU"
                              + (" > 2 x 126 MB L2, no flush" if batch * wl.bytes_step() > 252e6
@@ -1038,6 +1043,9 @@ def main() -> None:
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--config", choices=sorted(WORKLOADS) + [CONV.key, GACC.key], default="c2")
     p.add_argument("--mode", choices=["exact", "fast"], default="fast")
+    p.add_argument("--w8-kernel", choices=["planes", "bf16"], default="planes",
+                   help="W8 with at most 64 tokens: E2M1 digit planes (kind::mxf4) or int8 "
+                        "converted to BF16 in the kernel (kind::f16)")
     p.add_argument("--batch", type=int, default=0, help="GEMMs per step per GPU (0: the "
                    "config's default)")
     p.add_argument("--no-cpu-baseline", action="store_true")

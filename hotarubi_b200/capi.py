@@ -56,7 +56,7 @@ class GemmDesc(ctypes.Structure):
         ("accumulate", ctypes.c_uint32),
         ("pieces", ctypes.c_void_p), ("npieces", ctypes.c_uint32),
         ("cq", ctypes.c_void_p), ("cscale", ctypes.c_void_p), ("cquant", ctypes.c_uint32),
-        ("wcol_scale", ctypes.c_void_p),
+        ("wcol_scale", ctypes.c_void_p), ("w8_kernel", ctypes.c_uint32),
     ]
 
 
@@ -77,6 +77,7 @@ class ConvDesc(ctypes.Structure):
 
 
 CONV_XMAJOR, CONV_YMAJOR = 0, 1
+W8_DIGIT_PLANES, W8_BF16 = 0, 1
 
 
 class GaccDesc(ctypes.Structure):
@@ -278,7 +279,7 @@ class Library:
     def desc(wfmt, M, N, K, *, a=None, lda=None, quant=QUANT_HOST, aq=None, ascale=None,
              w=None, wscale=None, bias=None, c=None, ldc=None, accumulate=False,
              pieces=None, mode=MODE_EXACT, cq=None, cscale=None, cquant=QUANT_VEC,
-             wcol_scale=None):
+             wcol_scale=None, w8_kernel=0):
         d = GemmDesc()
         d.wfmt, d.mode, d.M, d.N, d.K = wfmt, mode, M, N, K
         d.a = _ptr(a)
@@ -292,6 +293,7 @@ class Library:
         d.accumulate = 1 if accumulate else 0
         d.cq, d.cscale, d.cquant = _ptr(cq), _ptr(cscale), cquant
         d.wcol_scale = _ptr(wcol_scale)
+        d.w8_kernel = w8_kernel
         if pieces is not None:
             arr = np.ascontiguousarray(pieces, dtype=np.uint32)
             d._pieces_keep = arr  # keep alive

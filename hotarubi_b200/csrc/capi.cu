@@ -189,6 +189,9 @@ hrb_status check_desc(hrb_ctx* ctx, const hrb_gemm_desc* d, uint32_t* pieces,
     }
   }
   if (!aligned(d->w, 16)) return fail(ctx, HRB_EINVAL, "weights are not 16-byte aligned");
+  if (d->w8_kernel > HRB_W8_BF16) {
+    return fail(ctx, HRB_EINVAL, "unknown W8 kernel %u", d->w8_kernel);
+  }
   if (d->wcol_scale != nullptr) {
     if (d->accumulate) {
       return fail(ctx, HRB_EINVAL, "per-column weight scales do not combine with accumulate");
@@ -289,48 +292,62 @@ hrb_status run_dense(hrb_ctx* ctx, const hrb::DenseJob& job, cudaStream_t s) {
 // runs the exact kernel, whose results are within any tolerance.
 bool use_tc(const hrb_gemm_desc* d) { return d->mode == HRB_MODE_FAST && d->a != nullptr; }
 
-// Tensor-core bytes of one GEMM: prepared activations then weight chunks.
-size_t tc_act_bytes(const hrb_gemm_desc* d) {
-  return hrb::mx_act_bytes(d->wfmt, d->M, blocks_of(d->K));
+// The tensor-core path format of a GEMM (hrb_tc.cuh): its weight format,
+// or kTcW8Bf16 for W8 with at most 64 tokens and w8_kernel HRB_W8_BF16.
+// Convolutions keep the weight format (their operand gathering writes digit
+// planes).
+uint32_t tc_fmt(const hrb_gemm_desc* d) {
+  return hrb::tc_path_format(d->wfmt, d->M, d->w8_kernel);
 }
-size_t tc_weight_bytes(const hrb_gemm_desc* d) {
-  return hrb::mx_weight_bytes(d->wfmt, d->N, blocks_of(d->K));
+
+// Tensor-core bytes of one GEMM in path format pf: prepared activations then
+// weight chunks.
+size_t tc_act_bytes(const hrb_gemm_desc* d, uint32_t pf) {
+  return hrb::mx_act_bytes(pf, d->M, blocks_of(d->K));
+}
+size_t tc_weight_bytes(const hrb_gemm_desc* d, uint32_t pf) {
+  return hrb::mx_weight_bytes(pf, d->N, blocks_of(d->K));
 }
 // (scale, bias) pairs of a GEMM with per-column scales: 8 bytes a column.
 size_t tc_epv_bytes(const hrb_gemm_desc* d) {
   return d->wcol_scale != nullptr ? align_up(size_t{d->N} * 8u, 1024) : 0u;
 }
-size_t tc_scratch_bytes(const hrb_gemm_desc* d) {
-  return align_up(tc_act_bytes(d), 1024) + align_up(tc_weight_bytes(d), 1024) + tc_epv_bytes(d);
+size_t tc_scratch_bytes(const hrb_gemm_desc* d, uint32_t pf) {
+  return align_up(tc_act_bytes(d, pf), 1024) + align_up(tc_weight_bytes(d, pf), 1024) +
+         tc_epv_bytes(d);
 }
+size_t tc_scratch_bytes(const hrb_gemm_desc* d) { return tc_scratch_bytes(d, tc_fmt(d)); }
 
 // The encoder job writing the tensor-core operand blocks of an M x K FP32
-// activation matrix (layout of hrb_tc.cuh for the weight format's kind).
+// activation matrix (layout of hrb_tc.cuh for path format pf).
 hrb::QuantJob tc_quant_job(const float* a, uint32_t M, uint32_t K, uint32_t lda, uint32_t quant,
-                           uint32_t wfmt, uint8_t* tiles) {
-  const bool f8 = wfmt == HRB_WFMT_MXFP8;
+                           uint32_t pf, uint8_t* tiles) {
+  const bool f8 = pf == HRB_WFMT_MXFP8, bf = pf == hrb::kTcW8Bf16;
   hrb::QuantJob j = make_quant_job(a, M, K, lda, quant, nullptr, nullptr);
   j.tiles = tiles;
-  j.tiles_kind = f8 ? 3 : 2;
+  j.tiles_kind = bf ? 4 : f8 ? 3 : 2;
   j.tile_rows = hrb::mx_tokens_per_tile(M);
-  j.k_steps = hrb::mx_steps_of(wfmt, blocks_of(K));
-  j.cover_blocks = (f8 ? 4u : 8u) * j.k_steps;
-  // Encoder units: (row, 256 elements), i.e. one E2M1 step or two E4M3 steps.
-  j.units = static_cast<uint64_t>(j.rows) * (f8 ? (j.k_steps + 1u) / 2u : j.k_steps);
+  j.k_steps = hrb::mx_steps_of(pf, blocks_of(K));
+  j.cover_blocks = (f8 || bf ? 4u : 8u) * j.k_steps;
+  // Encoder units: (row, 256 elements), i.e. one E2M1 step or two 128-element steps.
+  j.units = static_cast<uint64_t>(j.rows) * (f8 || bf ? (j.k_steps + 1u) / 2u : j.k_steps);
   return j;
 }
 
 // Fills the encoder job and the tensor-core job of one GEMM whose prepared
-// operands live at `base` (tc_scratch_bytes of them).  Every weight format
-// takes the block-scaled kernel with no decode in it: MXFP4 codes and W8
-// (three E2M1 digit planes) on kind::mxf4, MXFP8 codes on kind::mxf8f6f4.
-void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJob* tj) {
+// operands live at `base` (tc_scratch_bytes of them), in path format pf.
+// MXFP4 codes and W8 (three E2M1 digit planes) run kind::mxf4, MXFP8 codes
+// kind::mxf8f6f4, all with no decode in the kernel; W8 with at most 64
+// tokens streams its int8 codes and runs kind::f16 on BF16 converted in
+// shared memory.
+void tc_jobs(const hrb_gemm_desc* d, uint32_t pf, uint8_t* base, hrb::QuantJob* qj,
+             hrb::TcJob* tj) {
   const uint32_t kb = blocks_of(d->K);
   uint8_t* act = base;
-  uint8_t* wt = base + align_up(tc_act_bytes(d), 1024);
-  *qj = tc_quant_job(d->a, d->M, d->K, d->lda, d->quant, d->wfmt, act);
+  uint8_t* wt = base + align_up(tc_act_bytes(d, pf), 1024);
+  *qj = tc_quant_job(d->a, d->M, d->K, d->lda, d->quant, pf, act);
   *tj = hrb::TcJob{};
-  tj->wfmt = d->wfmt;
+  tj->wfmt = pf;
   tj->M = d->M;
   tj->N = d->N;
   tj->kb = kb;
@@ -342,7 +359,7 @@ void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJo
   tj->bias = d->bias;
   if (d->wcol_scale != nullptr) {
     tj->epv = reinterpret_cast<const float*>(
-        wt + align_up(tc_weight_bytes(d), 1024));  // (scale, bias) pairs after the weights
+        wt + align_up(tc_weight_bytes(d, pf), 1024));  // (scale, bias) pairs after the weights
     tj->bias = nullptr;
   }
   tj->c = d->c;
@@ -357,7 +374,7 @@ void tc_jobs(const hrb_gemm_desc* d, uint8_t* base, hrb::QuantJob* qj, hrb::TcJo
 // With per-column scales, also interleaves (scale, bias) pairs (bias 0 when
 // there is none) with two strided copies.
 void tc_translate(const hrb_gemm_desc* d, const hrb::TcJob& tj, cudaStream_t s) {
-  hrb::launch_tile_weights_mxf4(d->wfmt, d->w, d->wscale, d->N, blocks_of(d->K),
+  hrb::launch_tile_weights_mxf4(tj.wfmt, d->w, d->wscale, d->N, blocks_of(d->K),
                                 const_cast<uint8_t*>(tj.w_tiles), s);
   if (tj.epv != nullptr) {
     auto* ep = const_cast<float*>(tj.epv);
@@ -508,7 +525,8 @@ hrb_status check_conv(hrb_ctx* ctx, const hrb_conv_desc* d, ConvRun* r) {
     // With 256-channel planes one MXFP4 K step is one (plane, tap), and the
     // GEMM assembles its activation blocks itself from the encoded map.
     x.gather = d->wfmt == HRB_WFMT_MXFP4 && x.g.bp == 8u;
-    x.o_tc = take(x.gather ? hrb::mx_weight_bytes(d->wfmt, x.N, x.K / 32u) : tc_scratch_bytes(&g));
+    x.o_tc = take(x.gather ? hrb::mx_weight_bytes(d->wfmt, x.N, x.K / 32u)
+                          : tc_scratch_bytes(&g, g.wfmt));
     x.o_mt = take(hrb::mx_act_bytes(d->wfmt, d->images * d->H * d->W, d->cin / 32u));
   } else {
     if (d->a != nullptr) {
@@ -536,11 +554,11 @@ hrb_status conv_prepare(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, 
     const hrb_gemm_desc g = conv_gemm(d, r, base);
     hrb::QuantJob qj;
     hrb::TcJob tj;
-    tc_jobs(&g, base + r.o_tc, &qj, &tj);
+    tc_jobs(&g, g.wfmt, base + r.o_tc, &qj, &tj);
     if (r.gather) {
       tj.w_tiles = base + r.o_tc;  // no prepared activation blocks
     } else {
-      HRB_CUDA(ctx, cudaMemsetAsync(base + r.o_tc, 0, align_up(tc_act_bytes(&g), 1024), s));
+      HRB_CUDA(ctx, cudaMemsetAsync(base + r.o_tc, 0, align_up(tc_act_bytes(&g, g.wfmt), 1024), s));
     }
     tc_translate(&g, tj, s);
     *launched += 1;
@@ -561,7 +579,7 @@ hrb_status conv_execute(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, 
     // from them, then the GEMM.
     hrb::QuantJob qj;
     hrb::TcJob tj;
-    tc_jobs(&g, base + r.o_tc, &qj, &tj);
+    tc_jobs(&g, g.wfmt, base + r.o_tc, &qj, &tj);
     tj.relu = d->relu != 0;
     const hrb::QuantJob mj = tc_quant_job(d->a, d->images * d->H * d->W, d->cin, d->cin,
                                           d->quant, d->wfmt, base + r.o_mt);
@@ -990,13 +1008,13 @@ hrb_status hrb_gemm_dense(hrb_ctx* ctx, const hrb_gemm_desc* d, void* stream) {
     if (st != HRB_OK) return st;
     hrb::QuantJob qj;
     hrb::TcJob tj;
-    tc_jobs(d, static_cast<uint8_t*>(ctx->scratch), &qj, &tj);
+    tc_jobs(d, tc_fmt(d), static_cast<uint8_t*>(ctx->scratch), &qj, &tj);
     // Rows of the last activation tile past M stay zero.
-    HRB_CUDA(ctx, cudaMemsetAsync(ctx->scratch, 0, align_up(tc_act_bytes(d), 1024), s));
+    HRB_CUDA(ctx, cudaMemsetAsync(ctx->scratch, 0, align_up(tc_act_bytes(d, tj.wfmt), 1024), s));
     tc_translate(d, tj, s);
     hrb::launch_quantize_planes(nullptr, 1, &qj, qj.units, ctx->d_error, ctx->sm_count, s);
     tj.tile_begin = 0;
-    const int n = hrb::launch_mxf4(nullptr, &tj, qj.tile_rows, d->wfmt, tj.m_tiles * tj.n_tiles,
+    const int n = hrb::launch_mxf4(nullptr, &tj, qj.tile_rows, tj.wfmt, tj.m_tiles * tj.n_tiles,
                                    ctx->sm_count, ctx->d_error, s);
     if (n < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
     ctx->launches += 2u + static_cast<uint64_t>(n);
@@ -1174,7 +1192,7 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
     if (use_tc(&d)) {
       hrb::QuantJob qj;
       hrb::TcJob tj;
-      tc_jobs(&d, sbase + soff, &qj, &tj);
+      tc_jobs(&d, tc_fmt(&d), sbase + soff, &qj, &tj);
       soff += tc_scratch_bytes(&d);
       tc_translate(&d, tj, ctx->stream);
       qj.unit_begin = plan->plane_units;
@@ -1182,12 +1200,12 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
       planes.push_back(qj);
       size_t g = 0;
       const uint32_t kind = 2u;
-      while (g < tc_keys.size() && !(tc_keys[g].nt == qj.tile_rows && tc_keys[g].wfmt == d.wfmt &&
+      while (g < tc_keys.size() && !(tc_keys[g].nt == qj.tile_rows && tc_keys[g].wfmt == tj.wfmt &&
                                      tc_keys[g].kind == kind)) {
         ++g;
       }
       if (g == tc_keys.size()) {
-        tc_keys.push_back({qj.tile_rows, d.wfmt, kind});
+        tc_keys.push_back({qj.tile_rows, tj.wfmt, kind});
         tc_groups.emplace_back();
         tc_tiles.push_back(0);
       }

@@ -120,16 +120,23 @@ __host__ __device__ inline uint32_t mx_planes_of(uint32_t wfmt) {
   return wfmt == HRB_WFMT_W8 ? 3u : 1u;
 }
 
+// Weight bytes of one (tile, K step) and activation block bytes of a path
+// format.
+__host__ __device__ inline uint32_t w_step_bytes(uint32_t wfmt) {
+  return wfmt == kTcW8Bf16 ? kMxRawChunk : mx_planes_of(wfmt) * kWChunk;
+}
+
 __host__ __device__ inline uint32_t act_block_bytes(uint32_t wfmt, uint32_t nt) {
-  return wfmt == HRB_WFMT_MXFP8 ? mx8_act_block_bytes(nt) : mx_act_block_bytes(nt);
+  return wfmt == HRB_WFMT_MXFP8 ? mx8_act_block_bytes(nt)
+         : wfmt == kTcW8Bf16    ? mxbf_act_block_bytes(nt)
+                                : mx_act_block_bytes(nt);
 }
 
 __host__ __device__ inline MxTile make_tile(const TcJob& job, uint32_t nt, uint32_t local) {
   const uint32_t mt = local / job.n_tiles, n_tile = local % job.n_tiles;
   const uint32_t row0 = mt * nt, col0 = n_tile * kTileW;
   MxTile t;
-  t.w = job.w_tiles +
-        static_cast<size_t>(n_tile) * job.k_steps * mx_planes_of(job.wfmt) * kWChunk;
+  t.w = job.w_tiles + static_cast<size_t>(n_tile) * job.k_steps * w_step_bytes(job.wfmt);
   t.a = job.a_tiles + static_cast<size_t>(mt) * job.k_steps * act_block_bytes(job.wfmt, nt);
   t.c = job.c != nullptr ? job.c + static_cast<size_t>(row0) * job.ldc + col0 : nullptr;
   t.bias = job.epv != nullptr ? job.epv + 2u * col0 : (job.bias != nullptr ? job.bias + col0 : nullptr);
@@ -305,6 +312,79 @@ __device__ __forceinline__ void requant_rows(const MxTile& ti, const float (&x)[
     if (lane == 0) ti.cscale[row * kbq + sp] = static_cast<uint8_t>(scale);
   }
   if (bad && lane == 0) atomicOr(err, 1u);
+}
+
+// One epilogue warp's share of a finished tile: token rows [r0, r1) of the
+// warp's 32 weight columns (TMEM lane quarter sp).  The accumulator holds
+// kSums partial sums per output (the digit-plane products, at TMEM columns
+// taddr, taddr + NT, taddr + 2 NT), added smallest scale first; then C (with
+// accumulate), the column scale, the bias and RELU, and the stores: C, the
+// peers' copies of C and the MXINT8 copy.
+template <uint32_t NT, uint32_t kSums>
+__device__ __forceinline__ void drain_tile(const MxParams& p, const MxTile& ti, uint32_t taddr,
+                                           uint32_t r0, uint32_t r1, uint32_t sp, uint32_t lane) {
+  const uint32_t col = sp * 32u + lane;
+  const uint32_t cols = ti.cols_kbq & 0xFFu, kbq = ti.cols_kbq >> 8;
+  const bool col_ok = col < cols;
+  const bool acc = (ti.flags >> 31) != 0;
+  const bool relu = ((ti.flags >> 29) & 1u) != 0;
+  const bool scaled = ((ti.flags >> 28) & 1u) != 0;
+  float bias = 0.0f, scale = 1.0f;
+  if (ti.bias != nullptr && col_ok) {
+    if (scaled) {
+      const float2 sb = reinterpret_cast<const float2*>(ti.bias)[col];
+      scale = sb.x;
+      bias = sb.y;
+    } else {
+      bias = ti.bias[col];
+    }
+  }
+  float* cbase = ti.c + col;
+  const uint32_t npeers = p.peers.count;
+  // The MXINT8 copy: this warp's 32 columns are one block of the next
+  // layer's K (tiles start on 128-column boundaries); the block exists when
+  // it starts before column N.
+  const bool requant = ti.cq != nullptr && sp * 32u < cols;
+#pragma unroll 1
+  for (uint32_t j0 = r0; j0 < r1; j0 += 16) {
+    uint32_t v0[16], v1[16], v2[16];
+    tmem_ld16(taddr + j0, v0);
+    if constexpr (kSums > 1) tmem_ld16(taddr + NT + j0, v1);
+    if constexpr (kSums > 2) tmem_ld16(taddr + 2 * NT + j0, v2);
+    tmem_wait_ld();
+    float x[16];
+#pragma unroll
+    for (uint32_t j = 0; j < 16; ++j) {
+      x[j] = __uint_as_float(v0[j]);
+      if constexpr (kSums > 1) x[j] = x[j] + __uint_as_float(v1[j]);
+      if constexpr (kSums > 2) x[j] += __uint_as_float(v2[j]);
+    }
+    if (col_ok) {
+#pragma unroll
+      for (uint32_t j = 0; j < 16; ++j) {
+        if (j0 + j < ti.rows) {
+          if (acc) x[j] += cbase[static_cast<size_t>(j0 + j) * ti.ldc];
+          if (scaled) x[j] = __fmul_rn(x[j], scale);
+          x[j] = __fadd_rn(x[j], bias);
+          if (relu) x[j] = x[j] > 0.0f ? x[j] : 0.0f;
+          if (ti.c != nullptr) cbase[static_cast<size_t>(j0 + j) * ti.ldc] = x[j];
+        }
+      }
+      if (npeers != 0) {
+        // The same outputs into each peer's C (NVLink stores).
+        for (uint32_t q = 0; q < npeers; ++q) {
+          char* peer = reinterpret_cast<char*>(cbase) + p.peers.delta[q];
+#pragma unroll
+          for (uint32_t j = 0; j < 16; ++j) {
+            if (j0 + j < ti.rows) {
+              *reinterpret_cast<float*>(peer + static_cast<size_t>(j0 + j) * ti.ldc * 4u) = x[j];
+            }
+          }
+        }
+      }
+    }
+    if (requant) requant_rows(ti, x, j0, sp, lane, col_ok, kbq, p.err);
+  }
 }
 
 // A ring of `slots` buffers with full/empty mbarriers, walked by a running
@@ -550,70 +630,8 @@ __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
       ok = __all_sync(0xFFFFFFFFu, ok);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t col = sp * 32u + lane;
-      const uint32_t cols = ti.cols_kbq & 0xFFu, kbq = ti.cols_kbq >> 8;
-      const bool col_ok = col < cols;
-      const bool acc = (ti.flags >> 31) != 0;
-      const bool relu = ((ti.flags >> 29) & 1u) != 0;
-      const bool scaled = ((ti.flags >> 28) & 1u) != 0;
-      float bias = 0.0f, scale = 1.0f;
-      if (ti.bias != nullptr && col_ok) {
-        if (scaled) {
-          const float2 sb = reinterpret_cast<const float2*>(ti.bias)[col];
-          scale = sb.x;
-          bias = sb.y;
-        } else {
-          bias = ti.bias[col];
-        }
-      }
-      float* cbase = ti.c + col;
-      const uint32_t npeers = p.peers.count;
-      // The MXINT8 copy: this warp's 32 columns are one block of the next
-      // layer's K (tiles start on 128-column boundaries); the block exists
-      // when it starts before column N.
-      const bool requant = ti.cq != nullptr && sp * 32u < cols;
-#pragma unroll 1
-      for (uint32_t j0 = r0; j0 < r1; j0 += 16) {
-        // The digit-plane partial sums of tokens j0..j0+15, added smallest
-        // scale first.
-        uint32_t v0[16], v1[16], v2[16];
-        const uint32_t taddr = tmem + ((sp * 32u) << 16) + b * Cfg::kDCols + j0;
-        tmem_ld16(taddr, v0);
-        tmem_ld16(taddr + NT, v1);
-        if constexpr (!Cfg::kF8) tmem_ld16(taddr + 2 * NT, v2);
-        tmem_wait_ld();
-        float x[16];
-#pragma unroll
-        for (uint32_t j = 0; j < 16; ++j) {
-          x[j] = __uint_as_float(v0[j]) + __uint_as_float(v1[j]);
-          if constexpr (!Cfg::kF8) x[j] += __uint_as_float(v2[j]);
-        }
-        if (col_ok) {
-#pragma unroll
-          for (uint32_t j = 0; j < 16; ++j) {
-            if (j0 + j < ti.rows) {
-              if (acc) x[j] += cbase[static_cast<size_t>(j0 + j) * ti.ldc];
-              if (scaled) x[j] = __fmul_rn(x[j], scale);
-              x[j] = __fadd_rn(x[j], bias);
-              if (relu) x[j] = x[j] > 0.0f ? x[j] : 0.0f;
-              if (ti.c != nullptr) cbase[static_cast<size_t>(j0 + j) * ti.ldc] = x[j];
-            }
-          }
-          if (npeers != 0) {
-            // The same outputs into each peer's C (NVLink stores).
-            for (uint32_t q = 0; q < npeers; ++q) {
-              char* peer = reinterpret_cast<char*>(cbase) + p.peers.delta[q];
-#pragma unroll
-              for (uint32_t j = 0; j < 16; ++j) {
-                if (j0 + j < ti.rows) {
-                  *reinterpret_cast<float*>(peer + static_cast<size_t>(j0 + j) * ti.ldc * 4u) = x[j];
-                }
-              }
-            }
-          }
-        }
-        if (requant) requant_rows(ti, x, j0, sp, lane, col_ok, kbq, p.err);
-      }
+      drain_tile<NT, Cfg::kAPlanes>(p, ti, tmem + ((sp * 32u) << 16) + b * Cfg::kDCols, r0, r1, sp,
+                                    lane);
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);
     }
@@ -626,6 +644,327 @@ __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
   }
+}
+
+// ---------------------------------------------------------------------------
+// W8 with at most 64 tokens (path format kTcW8Bf16): kind::f16 on BF16.
+//
+// These GEMMs are bound by the weight stream, so the weights travel as the
+// int8 codes themselves (one byte a weight, against 1.5 for the three E2M1
+// digit planes) and converter warps turn each K step of a tile into BF16
+// rows of the MMA's A operand, written straight into tensor memory (no
+// shared-memory round trip for the converted weights); one M = 128, N = 64,
+// K = 16 MMA per 16 elements of K then multiplies them by the BF16
+// activations from shared memory, one product per weight instead of nine
+// digit-plane products.
+//
+// Warps: 0 streams raw weight chunks and 2 activation blocks (bulk copies
+// into two rings, so neither waits on the other's consumers), 1 owns TMEM
+// and issues the MMAs, 3 .. 10 convert, 11 .. 18 drain the two
+// accumulators.  TMEM columns: accumulators 0-63 and 64-127, then 4 A
+// buffers of 64 columns (128 rows x 128 BF16 values).  Converter warp w owns
+// lane quarter w % 4 (TMEM's access rule) and half (w - 3) / 4 of each
+// step's K: 32 columns, 64 values of one weight row per thread.
+constexpr uint32_t kCvtWarps = 8;
+constexpr uint32_t kBfNt = 64;
+constexpr uint32_t kBfRawSlot = 17408;  // kMxRawChunk rounded up to 1 KB
+constexpr uint32_t kBfRawSlots = 6;
+constexpr uint32_t kBfAOp = mxbf_act_block_bytes(kBfNt);
+constexpr uint32_t kBfActSlots = 6;
+constexpr uint32_t kBfSlots = 4;        // A buffers in TMEM
+constexpr uint32_t kBfOffAct = kBfRawSlots * kBfRawSlot;
+constexpr uint32_t kBfOffBar = kBfOffAct + kBfActSlots * kBfAOp;
+constexpr uint32_t kBfSmem = kBfOffBar + 512 + 1024;
+constexpr uint32_t kBfFirstCvt = 3;
+constexpr uint32_t kBfEpiWarps = 8;
+constexpr uint32_t kBfFirstEpi = kBfFirstCvt + kCvtWarps;
+constexpr uint32_t kBfThreads = 32u * (kBfFirstEpi + kBfEpiWarps);
+constexpr uint32_t kBfColA = 2u * kBfNt;  // first A buffer column
+constexpr uint32_t kBfTmemCols = 512;
+static_assert(kBfColA + 64u * kBfSlots <= kBfTmemCols, "TMEM columns");
+static_assert(kMxRawChunk <= kBfRawSlot && kBfSmem <= kSmemLimit, "shared memory");
+static_assert(kBfAOp % 1024 == 0, "activation slots hold 1 KB-aligned swizzle atoms");
+
+// 16 int8 codes w (x, first code in the low byte) of one scale block -> 16
+// BF16 values w * s, s = 2^(e - 133), two to a word, low half first.  With
+// u = w + 128 (the sign bit flipped), the FP32 value 2^23 + u is assembled
+// from bytes, and (2^23 + u) s - (2^23 + 128) s = w s is one fused
+// multiply-add, exact: w s has at most 8 significant bits and s is a power
+// of two, so it is representable (as a subnormal too) and its low 16 bits
+// are zero, which makes its high half the exact BF16 value.  kWide (e > 237,
+// where (2^23 + 128) s overflows): the subtraction first, then the product.
+template <bool kWide>
+__device__ __forceinline__ void w8_piece_to_bf16(const uint4 x, float s, uint32_t* o) {
+  const float c = -8388736.0f * s;
+  const uint32_t in[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+  for (uint32_t q = 0; q < 4; ++q) {
+    const uint32_t u = in[q] ^ 0x80808080u;
+    float f[4];
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      const float m = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u + j));
+      f[j] = kWide ? __fmul_rn(__fadd_rn(m, -8388736.0f), s) : __fmaf_rn(m, s, c);
+    }
+    o[2 * q] = __byte_perm(__float_as_uint(f[0]), __float_as_uint(f[1]), 0x7632u);
+    o[2 * q + 1] = __byte_perm(__float_as_uint(f[2]), __float_as_uint(f[3]), 0x7632u);
+  }
+}
+
+// 2^(e - 133) as FP32 (a subnormal for e < 7).
+__device__ __forceinline__ float w8_scale(uint32_t e) {
+  return __uint_as_float(e >= 7u ? (e - 6u) << 23 : 1u << (e + 16u));
+}
+
+__global__ void __launch_bounds__(kBfThreads, 1) k_gemm_w8bf(const __grid_constant__ MxParams p) {
+  constexpr uint32_t NT = kBfNt;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBfOffBar);
+  const Ring raw{bars, bars + kBfRawSlots, kBfRawSlots};
+  const Ring actr{bars + 2 * kBfRawSlots, bars + 2 * kBfRawSlots + kBfActSlots, kBfActSlots};
+  uint64_t* a_full = bars + 2 * (kBfRawSlots + kBfActSlots);  // [kBfSlots] converted A
+  uint64_t* a_empty = a_full + kBfSlots;       // [kBfSlots] the step's MMAs done
+  uint64_t* acc_full = a_empty + kBfSlots;     // [2]
+  uint64_t* acc_empty = acc_full + 2;          // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint8_t* rbase = smem;
+  uint8_t* abase = smem + kBfOffAct;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < kBfRawSlots; ++s) {
+      mbar_init(&raw.full[s], 1);
+      mbar_init(&raw.empty[s], kCvtWarps);
+    }
+    for (uint32_t s = 0; s < kBfActSlots; ++s) {
+      mbar_init(&actr.full[s], 1);
+      mbar_init(&actr.empty[s], 1);
+    }
+    for (uint32_t s = 0; s < kBfSlots; ++s) {
+      mbar_init(&a_full[s], kCvtWarps);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (uint32_t b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 32 * kBfEpiWarps);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kBfTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0 || warp == 2) {
+    // Lane 0 of warp 0: the raw weight chunks; of warp 2: the activation
+    // blocks.  Each tile's fields are loaded one tile ahead.
+    if (lane == 0) {
+      const bool weights = warp == 0;
+      const Ring& ring = weights ? raw : actr;
+      uint32_t n = 0;
+      MxTile next = tile_info<NT>(p, blockIdx.x);
+      for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+        const MxTile ti = next;
+        if (tile + gridDim.x < p.total_tiles) next = tile_info<NT>(p, tile + gridDim.x);
+        const uint32_t k_steps = ti.flags & 0x0FFFFFFFu;
+        for (uint32_t i = 0; i < k_steps && ok; ++i, ++n) {
+          const uint32_t sl = n % ring.slots;
+          ok = ring_acquire(ring, n, weights ? kMxRawChunk : kBfAOp, p.err);
+          if (!ok) break;
+          if (weights) {
+            bulk_g2s(rbase + sl * kBfRawSlot, ti.w + static_cast<size_t>(i) * kMxRawChunk,
+                     kMxRawChunk, &ring.full[sl]);
+          } else {
+            bulk_g2s(abase + sl * kBfAOp, ti.a + static_cast<size_t>(i) * kBfAOp, kBfAOp,
+                     &ring.full[sl]);
+          }
+        }
+      }
+      if (ok) ring_drain(ring, n, p.err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      uint32_t n = 0, t = 0;
+      uint32_t next_steps = tile_info<NT>(p, blockIdx.x).flags & 0x0FFFFFFFu;
+      for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++t) {
+        const uint32_t k_steps = next_steps;
+        if (tile + gridDim.x < p.total_tiles) {
+          next_steps = tile_info<NT>(p, tile + gridDim.x).flags & 0x0FFFFFFFu;
+        }
+        const uint32_t b = t & 1u;
+        if (t >= 2) ok = mbar_wait(&acc_empty[b], ((t >> 1) - 1) & 1u, p.err);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d = tmem + b * NT;
+        for (uint32_t i = 0; i < k_steps && ok; ++i, ++n) {
+          const uint32_t sl = n % kBfSlots, as = n % kBfActSlots;
+          ok = mbar_wait(&actr.full[as], (n / kBfActSlots) & 1u, p.err) &&
+               mbar_wait(&a_full[sl], (n / kBfSlots) & 1u, p.err);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t a_tm = tmem + kBfColA + 64u * sl;
+          const uint32_t act = smem_addr(abase + as * kBfAOp);
+#pragma unroll
+          for (uint32_t k = 0; k < 8; ++k) {
+            // K = 16 slice k: A columns 8k .. 8k + 7; activation atom k / 4,
+            // 32 bytes in.
+            mma_bf16_ts(d, a_tm + 8u * k, desc_sw128(act + (k >> 2) * (NT * kRowB) + 32u * (k & 3u)),
+                        idesc_bf16(kTileW, NT), (i > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&a_empty[sl]);
+          mma_commit(&actr.empty[as]);
+        }
+        mma_commit(&acc_full[b]);
+      }
+    }
+  } else if (warp >= kBfFirstCvt && warp < kBfFirstEpi) {
+    // Converters, all in step: per K step, once the A buffer is free and the
+    // raw chunk has landed, each thread loads its row's 64 codes and 2 scale
+    // bytes (16-byte chunk c of row r sits at c ^ (r % 8), so 8 consecutive
+    // rows read conflict-free), releases the raw slot, converts and stores
+    // 32 TMEM columns.  A step's store is waited for, and its buffer
+    // signalled, after the next step's conversion, which so overlaps it.
+    const uint32_t quarter = warp & 3u, half = (warp - kBfFirstCvt) >> 2;
+    const uint32_t r = quarter * 32u + lane;
+    constexpr uint32_t kNone = 0xFFFFFFFFu;
+    uint32_t pending = kNone;  // the A buffer whose store is in flight
+    const auto publish = [&]() {
+      if (pending == kNone) return;
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[pending]);
+      pending = kNone;
+    };
+    uint32_t n = 0;
+    uint32_t next_steps = tile_info<NT>(p, blockIdx.x).flags & 0x0FFFFFFFu;
+    for (uint32_t tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+      const uint32_t k_steps = next_steps;
+      if (tile + gridDim.x < p.total_tiles) {
+        next_steps = tile_info<NT>(p, tile + gridDim.x).flags & 0x0FFFFFFFu;
+      }
+      for (uint32_t i = 0; i < k_steps && ok; ++i, ++n) {
+        const uint32_t sl = n % kBfSlots, rs = n % kBfRawSlots;
+        if (n >= kBfSlots) ok = mbar_wait(&a_empty[sl], ((n / kBfSlots) - 1) & 1u, p.err);
+        if (ok) ok = mbar_wait(&raw.full[rs], (n / kBfRawSlots) & 1u, p.err);
+        ok = __all_sync(0xFFFFFFFFu, ok);
+        if (!ok) break;
+        const uint8_t* row = rbase + rs * kBfRawSlot + r * kRowB;
+        uint4 x[4];
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+          x[j] = *reinterpret_cast<const uint4*>(row + (((4u * half + j) ^ (r & 7u)) << 4));
+        }
+        const uint32_t sc = *reinterpret_cast<const uint16_t*>(rbase + rs * kBfRawSlot +
+                                                                kTileW * kRowB + r * 4u + 2u * half);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw.empty[rs]);
+        uint32_t o[32];
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+          const uint32_t e = (sc >> (8u * (j >> 1))) & 0xFFu;  // block 2 half + j / 2
+          if (e <= 237u) {
+            w8_piece_to_bf16<false>(x[j], w8_scale(e), o + 8u * j);
+          } else {
+            w8_piece_to_bf16<true>(x[j], w8_scale(e), o + 8u * j);
+          }
+        }
+        publish();
+        tc_fence_after();  // after the wait for the A buffer's last readers
+        tmem_st32(tmem + ((quarter * 32u) << 16) + kBfColA + 64u * sl + 32u * half, o);
+        pending = sl;
+      }
+    }
+    publish();
+  } else {
+    const uint32_t sp = warp & 3u;
+    constexpr uint32_t kRowsPer = NT / (kBfEpiWarps / 4);
+    const uint32_t r0 = ((warp - kBfFirstEpi) / 4u) * kRowsPer, r1 = r0 + kRowsPer;
+    uint32_t t = 0;
+    MxTile next = tile_info<NT>(p, blockIdx.x);
+    for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++t) {
+      const MxTile ti = next;
+      if (tile + gridDim.x < p.total_tiles) next = tile_info<NT>(p, tile + gridDim.x);
+      const uint32_t b = t & 1u;
+      if (ok) ok = mbar_wait_sleep(&acc_full[b], (t >> 1) & 1u, p.err);
+      ok = __all_sync(0xFFFFFFFFu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      drain_tile<NT, 1>(p, ti, tmem + ((sp * 32u) << 16) + b * NT, r0, r1, sp, lane);
+      tc_fence_before();
+      mbar_arrive(&acc_empty[b]);
+    }
+    if (p.peers.count != 0) __threadfence_system();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kBfTmemCols);
+  }
+}
+
+// Dense W8 weights [N][kp] + scales [N][kb] -> the raw chunks of the
+// kind::f16 kernel, per (128-column tile, 128-element step): 128 rows of 128
+// codes (zero past K or N), 16-byte chunk c of row r stored at c ^ (r % 8),
+// then the rows' four scale bytes (127 past K or N).  One thread per
+// 16-byte output piece.
+__global__ void k_tile_weights_w8raw(const uint8_t* __restrict__ w, const uint8_t* __restrict__ ws,
+                                     uint32_t N, uint32_t kb, uint32_t steps,
+                                     uint8_t* __restrict__ out) {
+  constexpr uint32_t kPieces = kMxRawChunk / 16u;
+  const uint32_t n_tiles = (N + kTileW - 1) / kTileW;
+  const uint64_t pieces = static_cast<uint64_t>(n_tiles) * steps * kPieces;
+  const size_t kp = static_cast<size_t>(kb) * 32u;
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < pieces;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t chunk = i / kPieces;
+    const uint32_t piece = static_cast<uint32_t>(i % kPieces);
+    const uint32_t tile = static_cast<uint32_t>(chunk / steps), step = static_cast<uint32_t>(chunk % steps);
+    uint8_t v[16];
+    if (piece < kTileW * kRowB / 16u) {
+      const uint32_t r = piece / 8u, n = tile * kTileW + r;
+      const size_t e0 = static_cast<size_t>(step) * 128u + ((piece % 8u) ^ (r & 7u)) * 16u;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        v[k] = (n < N && e0 + k < kp) ? w[static_cast<size_t>(n) * kp + e0 + k] : 0;
+      }
+    } else {
+      const uint32_t r0 = (piece - kTileW * kRowB / 16u) * 4u;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const uint32_t n = tile * kTileW + r0 + k / 4, blk = step * 4u + k % 4;
+        v[k] = (n < N && blk < kb) ? ws[static_cast<size_t>(n) * kb + blk] : 127;
+      }
+    }
+    uint4 o;
+    o.x = v[0] | (v[1] << 8) | (v[2] << 16) | (static_cast<uint32_t>(v[3]) << 24);
+    o.y = v[4] | (v[5] << 8) | (v[6] << 16) | (static_cast<uint32_t>(v[7]) << 24);
+    o.z = v[8] | (v[9] << 8) | (v[10] << 16) | (static_cast<uint32_t>(v[11]) << 24);
+    o.w = v[12] | (v[13] << 8) | (v[14] << 16) | (static_cast<uint32_t>(v[15]) << 24);
+    reinterpret_cast<uint4*>(out)[i] = o;
+  }
+}
+
+int launch_w8bf(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, int sm_count,
+                uint32_t* err, cudaStream_t s, const MxPeers* peers) {
+  MxParams p{};
+  p.tiles = tiles_dev;
+  p.total_tiles = tiles;
+  p.err = err;
+  if (peers != nullptr) p.peers = *peers;
+  if (inline_job != nullptr) p.inline_job = *inline_job;
+  const uint32_t grid = std::min<uint32_t>(tiles, static_cast<uint32_t>(sm_count));
+  if (!set_smem_limit_once(reinterpret_cast<const void*>(k_gemm_w8bf), kBfSmem)) return -1;
+  k_gemm_w8bf<<<grid, kBfThreads, kBfSmem, s>>>(p);
+  return cudaPeekAtLastError() == cudaSuccess ? 1 : -1;
 }
 
 // E2M1 code of a digit in [-4, 4]: 0, 1, 2, 3, 4 -> 0b000, 0b010, 0b100,
@@ -789,18 +1128,18 @@ uint32_t mx_k_steps(uint32_t kb) { return (kb + 7) / 8; }
 uint32_t mx8_k_steps(uint32_t kb) { return (kb + 3) / 4; }
 
 uint32_t mx_steps_of(uint32_t wfmt, uint32_t kb) {
-  return wfmt == HRB_WFMT_MXFP8 ? mx8_k_steps(kb) : mx_k_steps(kb);
+  return wfmt == HRB_WFMT_MXFP8 || wfmt == kTcW8Bf16 ? mx8_k_steps(kb) : mx_k_steps(kb);
 }
 
 uint32_t mx_block_bytes_of(uint32_t wfmt, uint32_t nt) { return act_block_bytes(wfmt, nt); }
 
 size_t mx_weight_bytes(uint32_t wfmt, uint32_t N, uint32_t kb) {
   return static_cast<size_t>((N + kTileW - 1) / kTileW) * mx_steps_of(wfmt, kb) *
-         mx_planes_of(wfmt) * kWChunk;
+         w_step_bytes(wfmt);
 }
 
 size_t mx_act_bytes(uint32_t wfmt, uint32_t M, uint32_t kb) {
-  const uint32_t nt = mx_tokens_per_tile(M);
+  const uint32_t nt = wfmt == kTcW8Bf16 ? kBfNt : mx_tokens_per_tile(M);
   return static_cast<size_t>((M + nt - 1) / nt) * mx_steps_of(wfmt, kb) *
          act_block_bytes(wfmt, nt);
 }
@@ -810,6 +1149,11 @@ void launch_tile_weights_mxf4(uint32_t wfmt, const uint8_t* w, const uint8_t* ws
   const uint64_t pieces = mx_weight_bytes(wfmt, N, kb) / 16u;
   uint64_t grid = (pieces + 255) / 256;
   if (grid > 148u * 16u) grid = 148u * 16u;
+  if (wfmt == kTcW8Bf16) {
+    k_tile_weights_w8raw<<<static_cast<unsigned>(grid ? grid : 1), 256, 0, s>>>(
+        w, ws, N, kb, mx_steps_of(wfmt, kb), out);
+    return;
+  }
   k_tile_weights_mxf4<<<static_cast<unsigned>(grid ? grid : 1), 256, 0, s>>>(
       w, ws, N, kb, mx_steps_of(wfmt, kb), mx_planes_of(wfmt), wfmt == HRB_WFMT_MXFP8 ? 1u : 0u,
       out);
@@ -846,6 +1190,8 @@ int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, u
     case HRB_WFMT_W8 * 1000u + 128: return go(Pick<128, 3, 4>{});
     case HRB_WFMT_MXFP8 * 1000u + 64: return go(Pick<64, 1, 8>{});
     case HRB_WFMT_MXFP8 * 1000u + 128: return go(Pick<128, 1, 8>{});
+    case kTcW8Bf16 * 1000u + kBfNt:
+      return launch_w8bf(tiles_dev, inline_job, tiles, sm_count, err, s, peers);
     default: return -1;
   }
 }

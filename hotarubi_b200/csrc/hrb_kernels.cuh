@@ -116,7 +116,8 @@ struct QuantJob {
   // digit planes with their E8M0 scales in the activation blocks of
   // hrb_tc.cuh, [row tiles of tile_rows][k_steps][block].  tiles_kind 2:
   // three E2M1 planes, 256-element K steps (kind::mxf4); tiles_kind 3: two
-  // E4M3 planes, 128-element K steps (kind::mxf8f6f4).
+  // E4M3 planes, 128-element K steps (kind::mxf8f6f4); tiles_kind 4: BF16
+  // values, 128-element K steps (kind::f16).
   uint8_t* tiles;
   uint64_t unit_begin;
   uint64_t units;     // rows * ceil(kb / 4); planes: rows * 256-element groups

@@ -12,6 +12,15 @@ namespace hrb {
 
 // One GEMM for the block-scaled tensor-core kernel (gemm_mxf4.cu), with its
 // prepared operands: activation digit planes and translated weight chunks.
+// Path formats: the hrb_wfmt values, plus W8 with at most 64 tokens on
+// request (hrb_gemm_desc.w8_kernel), whose int8 weights stream from HBM as
+// they are and become BF16 in the kernel.
+constexpr uint32_t kTcW8Bf16 = 3;
+__host__ __device__ constexpr uint32_t tc_path_format(uint32_t wfmt, uint32_t M,
+                                                      uint32_t w8_kernel) {
+  return wfmt == HRB_WFMT_W8 && M <= 64u && w8_kernel == HRB_W8_BF16 ? kTcW8Bf16 : wfmt;
+}
+
 struct TcJob {
   const uint8_t* a_tiles;  // [m_tiles][k_steps][NT rows][128 B]
   const uint8_t* w_tiles;  // [n_tiles][k_steps][chunk]
@@ -22,7 +31,7 @@ struct TcJob {
   const float* epv;
   float* c;                // [M][ldc]
   uint32_t M, N, kb, ldc;
-  uint32_t wfmt;
+  uint32_t wfmt;           // path format (tc_path_format)
   uint32_t accumulate;
   uint32_t m_tiles, n_tiles, k_steps;
   uint32_t tile_begin;     // prefix over the jobs of one launch
@@ -76,7 +85,19 @@ __host__ __device__ inline uint32_t mx8_act_sf_offset(uint32_t nt, uint32_t stac
   return 2u * nt * 128u + (stacked_row / 128u) * 512u + (stacked_row % 32u) * 16u +
          ((stacked_row % 128u) / 32u) * 4u + block_in_step;
 }
-// K steps and activation block bytes of a weight format on this path.
+// W8 with at most 64 tokens (path format kTcW8Bf16) runs kind::f16 on BF16
+// operands, which hold every MXINT8 activation q * 2^(e-6) and every W8
+// weight q * 2^(e-133) exactly, so the products are exact as on the other
+// kinds.  K steps of 128 elements.  Activations: per (64-row tile, step) two
+// 128-byte-swizzled atoms of 64 rows x 64 BF16 values (elements 64 a ..
+// 64 a + 63 of the step in atom a), prepared by the encoder.  Weights: per
+// (128-column tile, step) the int8 codes as they are, 128 rows x 128 bytes,
+// then the rows' scale bytes [128][4] (kMxRawChunk bytes); the kernel
+// converts them to BF16 in shared memory.
+constexpr uint32_t kMxRawChunk = 128u * 128u + 512u;
+__host__ __device__ constexpr uint32_t mxbf_act_block_bytes(uint32_t nt) { return nt * 256u; }
+
+// K steps and activation block bytes of a path format.
 uint32_t mx_steps_of(uint32_t wfmt, uint32_t kb);
 uint32_t mx_block_bytes_of(uint32_t wfmt, uint32_t nt);
 

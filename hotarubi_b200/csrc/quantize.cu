@@ -226,7 +226,8 @@ struct PlaneJob {
   uint8_t* tiles;
   uint32_t rows, cols, ldx, tile_rows, vec4, vec_rule;
   uint32_t f8;        // E4M3 planes (tiles_kind 3), else E2M1 planes
-  uint32_t steps;     // operand K steps per row tile (256 elements E2M1, 128 E4M3)
+  uint32_t bf16;      // BF16 values (tiles_kind 4)
+  uint32_t steps;     // operand K steps per row tile (256 elements E2M1, 128 E4M3 or BF16)
   uint32_t k_steps;   // units per row: 256-element groups
   uint32_t block_bytes, plane_bytes;  // the activation block, tile_rows * 128
   uint64_t unit_begin, units;
@@ -240,12 +241,15 @@ __device__ __forceinline__ PlaneJob plane_job(const QuantJob& j) {
   p.cols = j.cols;
   p.ldx = j.ldx;
   p.f8 = j.tiles_kind == 3;
+  p.bf16 = j.tiles_kind == 4;
   p.steps = j.k_steps;
-  p.k_steps = p.f8 ? (j.k_steps + 1u) / 2u : j.k_steps;
+  p.k_steps = p.f8 || p.bf16 ? (j.k_steps + 1u) / 2u : j.k_steps;
   p.tile_rows = j.tile_rows;
   p.vec4 = j.vec4;
   p.vec_rule = j.vec_rule;
-  p.block_bytes = p.f8 ? mx8_act_block_bytes(j.tile_rows) : mx_act_block_bytes(j.tile_rows);
+  p.block_bytes = p.f8     ? mx8_act_block_bytes(j.tile_rows)
+                  : p.bf16 ? mxbf_act_block_bytes(j.tile_rows)
+                           : mx_act_block_bytes(j.tile_rows);
   p.plane_bytes = j.tile_rows * 128u;
   p.unit_begin = j.unit_begin;
   p.units = j.units;
@@ -266,7 +270,12 @@ __device__ __forceinline__ PlaneOut plane_out(const PlaneJob& j, uint32_t row, u
   const uint32_t rt = row >> shift, r = row & (j.tile_rows - 1u);
   PlaneOut o;
   o.blk0 = j.tiles + static_cast<size_t>(rt) * j.steps * j.block_bytes;
-  if (j.f8) {
+  if (j.bf16) {
+    // BF16: lane l's eight values (16 bytes) are logical chunk l % 8 of row
+    // r of atom (l / 8) % 2 of step 2 u + l / 16.
+    o.off = ((lane >> 3) & 1u) * j.plane_bytes + r * 128u + (((lane & 7u) ^ (r & 7u)) << 4);
+    o.sf[0] = o.sf[1] = o.sf[2] = 0;
+  } else if (j.f8) {
     // E4M3: lane l's eight bytes are bytes 8 (l % 16) .. of the row of step
     // 2 u + l / 16: logical 16-byte chunk (l % 16) / 2, half l % 2.
     o.off = r * 128u + ((((lane & 15u) >> 1) ^ (r & 7u)) << 4) + (lane & 1u) * 8u;
@@ -344,7 +353,7 @@ __device__ __forceinline__ void encode_planes(const PlaneJob& j, const PlaneOut&
   }
   // t = q + 1.5 * 2^23: q in the low byte of its bits (two's complement).
   float t[8];
-  if (scale < 6u) {
+  if (scale < 6u && !j.bf16) {
     // The planes' scales 2^(e - 6 + 3p) start below E8M0's 2^-127: such a
     // block (largest magnitude under 2^-121) is encoded as zero.
 #pragma unroll
@@ -363,6 +372,27 @@ __device__ __forceinline__ void encode_planes(const PlaneJob& j, const PlaneOut&
       t[i] = kMagic + static_cast<float>(kVec ? quantize_vec_rule(v[i], key)
                                                : quantize_host_rule(v[i], e));
     }
+  }
+  if (j.bf16) {
+    // q * 2^(scale - 133) in FP32, exact (a power-of-two multiple of an
+    // integer below 2^8, at least 2^-133: a subnormal at worst, with the
+    // IEEE multiply), whose low 16 bits are then zero: the high half is
+    // the exact BF16 value.
+    const float sc = __uint_as_float(scale >= 7u ? (scale - 6u) << 23 : 1u << (scale + 16u));
+    uint32_t h[8];
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) {
+      float y;
+      asm("mul.rn.f32 %0, %1, %2;" : "=f"(y) : "f"(__fadd_rn(t[i], -kMagic)), "f"(sc));
+      h[i] = __float_as_uint(y);
+    }
+    const uint32_t st = 2u * step + (lane >> 4);  // this lane's 128-element step
+    if (st < j.steps) {
+      *reinterpret_cast<uint4*>(o.blk0 + st * j.block_bytes + o.off) =
+          make_uint4(__byte_perm(h[0], h[1], 0x7632u), __byte_perm(h[2], h[3], 0x7632u),
+                     __byte_perm(h[4], h[5], 0x7632u), __byte_perm(h[6], h[7], 0x7632u));
+    }
+    return;
   }
   if (j.f8) {
     // Two E4M3 digits: h = RNE(q / 16), l = q - 16 h, both in [-8, 8].

@@ -219,7 +219,16 @@ typedef struct hrb_gemm_desc {
    * does not have (hotarubi places such a matrix as MXINT8 blocks, PlaceW8).
    * Not with accumulate.  4-byte aligned. */
   const float* wcol_scale;
+  /* HRB_MODE_FAST, W8, M <= 64 only (ignored otherwise): which tensor-core
+   * kernel runs.  HRB_W8_DIGIT_PLANES (0, the default): the weights as three
+   * E2M1 digit planes translated once, kind::mxf4.  HRB_W8_BF16: the int8
+   * codes stream as they are (one byte a weight) and the kernel converts
+   * them to BF16 in tensor memory, kind::f16.  Both are exact in their
+   * products; on the B200 the digit planes are the faster of the two. */
+  uint32_t w8_kernel;
 } hrb_gemm_desc;
+
+enum { HRB_W8_DIGIT_PLANES = 0, HRB_W8_BF16 = 1 };
 
 /* One dense GEMM, all pointers device pointers, asynchronous on `stream`. */
 HRB_API hrb_status hrb_gemm_dense(hrb_ctx* ctx, const hrb_gemm_desc* desc, void* stream);

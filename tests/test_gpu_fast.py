@@ -73,7 +73,7 @@ def ulp_hist(got, want):
 
 
 def check_fast(hrb, wfmt, m, n, k, *, bias=False, accumulate=False, seed=0, plan=False,
-               colscale=False, per_channel_w8=False):
+               colscale=False, per_channel_w8=False, w8_kernel=0):
     """colscale: a random FP32 scale per output column (wcol_scale), applied
     before the bias (one more rounding, inside the tolerance's slack).
     per_channel_w8: W8 weights whose block scale bytes are all 133, so the
@@ -109,7 +109,8 @@ def check_fast(hrb, wfmt, m, n, k, *, bias=False, accumulate=False, seed=0, plan
     keep = [dev(x), dev(w), dev(ws), None if b is None else dev(b),
             None if cs is None else dev(cs)]
     d = capi.Library.desc(wfmt, m, n, k, a=keep[0], w=keep[1], wscale=keep[2], bias=keep[3],
-                          c=c, accumulate=accumulate, mode=capi.MODE_FAST, wcol_scale=keep[4])
+                          c=c, accumulate=accumulate, mode=capi.MODE_FAST, wcol_scale=keep[4],
+                          w8_kernel=w8_kernel)
     if plan:
         p = hrb.plan([d])
         p.run()
@@ -159,11 +160,24 @@ def test_fast_column_scales(hrb, wfmt, plan):
 
 
 @pytest.mark.parametrize("shape", [(64, 960, 2560), (1, 16, 64), (200, 136, 416)])
-def test_fast_per_channel_int8_weights(hrb, shape):
+@pytest.mark.parametrize("w8_kernel", [0, 1])
+def test_fast_per_channel_int8_weights(hrb, shape, w8_kernel):
     """int8 weights with a per-output-channel FP32 scale and a fused
     scale/bias epilogue: W8 codes with block scale bytes 133 plus wcol_scale."""
     m, n, k = shape
-    check_fast(hrb, 1, m, n, k, bias=True, colscale=True, per_channel_w8=True, seed=m + n)
+    check_fast(hrb, 1, m, n, k, bias=True, colscale=True, per_channel_w8=True, seed=m + n,
+               w8_kernel=w8_kernel)
+
+
+@pytest.mark.parametrize("shape", [(64, 960, 2560), (64, 2560, 960), (1, 8, 32), (33, 130, 224),
+                                   (64, 72, 720)])
+def test_fast_w8_bf16_kernel_within_tolerance(hrb, shape):
+    """W8 with at most 64 tokens on the BF16 kernel (w8_kernel = HRB_W8_BF16):
+    the same bound as every fast GEMM; with bias, column scales and plans."""
+    m, n, k = shape
+    check_fast(hrb, 1, m, n, k, seed=hash(shape) % 1000, w8_kernel=1)
+    check_fast(hrb, 1, m, n, k, bias=True, colscale=True, seed=7, w8_kernel=1)
+    check_fast(hrb, 1, m, n, k, bias=True, plan=True, seed=8, w8_kernel=1)
 
 
 def test_fast_batched_plan_of_mixed_shapes(hrb):
@@ -193,18 +207,20 @@ def test_fast_batched_plan_of_mixed_shapes(hrb):
     plan.close()
 
 
-@pytest.mark.parametrize("wfmt", [0, 2])
+@pytest.mark.parametrize("wfmt,w8_kernel", [(0, 0), (1, 0), (1, 1), (2, 0)])
 @pytest.mark.parametrize("quant", [0, 1])
 @pytest.mark.parametrize("m", [64, 70, 130])
-def test_fast_activation_planes_are_exact(hrb, wfmt, quant, m):
-    """W = I (the code of 1.0: E2M1 0x2 or E4M3 0x38, scale byte 127), so
-    every output is a single activation: C[r][i] = q[r][i] * 2^(e_r - 6),
-    which the digit-plane products (three E2M1 planes for MXFP4, two E4M3
-    planes for MXFP8) and their FP32 sum give exactly.  Bit-equality with the
-    oracle's MXINT8 encoding pins the plane encoder (both rounding rules,
-    padded K steps, ragged token tiles).  The one exception is the fast
-    path's rule for blocks whose scale byte is below 6 (largest magnitude
-    under 2^-121): they are encoded as zero."""
+def test_fast_activation_planes_are_exact(hrb, wfmt, w8_kernel, quant, m):
+    """W = I (the code of 1.0: E2M1 0x2, W8 64 or E4M3 0x38, scale byte
+    127), so every output is a single activation: C[r][i] = q[r][i] *
+    2^(e_r - 6), which the digit-plane products (three E2M1 planes for MXFP4
+    and W8, two E4M3 planes for MXFP8) and their FP32 sum give exactly, and
+    so do the BF16 values of W8 with at most 64 tokens.  Bit-equality with
+    the oracle's MXINT8 encoding pins the encoder (both rounding rules,
+    padded K steps, ragged token tiles).  The exceptions: the digit planes
+    encode blocks whose scale byte is below 6 (largest magnitude under
+    2^-121) as zero; the BF16 path keeps them, and outputs under 2^-126 may
+    come out of the tensor cores flushed to zero."""
     from hotarubi_b200 import capi
     rng = np.random.default_rng(70 + m + quant)
     n = k = 544                      # kb = 17: the third 256-element step is mostly padding
@@ -220,35 +236,43 @@ def test_fast_activation_planes_are_exact(hrb, wfmt, quant, m):
         w = cpu.pack_nibbles(codes)
     else:
         w = np.zeros((n, k), np.uint8)
-        w[np.arange(n), np.arange(n)] = 0x38
+        w[np.arange(n), np.arange(n)] = 64 if wfmt == 1 else 0x38
     ws = np.full((n, k // 32), 127, np.uint8)
     c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
     keep = [dev(x), dev(w), dev(ws)]
     d = capi.Library.desc(wfmt, m, n, k, a=keep[0], w=keep[1], wscale=keep[2], c=c,
-                          mode=capi.MODE_FAST, quant=quant)
+                          mode=capi.MODE_FAST, quant=quant, w8_kernel=w8_kernel)
     hrb.dense(d)
     hrb.sync()
     got = c.cpu().numpy()
     xb = x.view(np.uint32)
     q, s = cpu.quantize_vec(xb) if quant == 1 else cpu.encode_mxint8(xb)
     want = (q.astype(np.float64) * np.repeat(np.ldexp(1.0, s.astype(np.int64) - 133), 32, axis=1))
-    want[np.repeat(s < 6, 32, axis=1)] = 0.0
+    bf16_path = wfmt == 1 and m <= 64 and w8_kernel == 1
+    if not bf16_path:
+        want[np.repeat(s < 6, 32, axis=1)] = 0.0
     want = want[:, :n].astype(np.float32)
     if quant == 0:
         assert (s < 6).any()         # the subnormal-only block is covered
-    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    if bf16_path:
+        flushed = (got == 0) & (np.abs(want) < 2.0**-126)
+        assert np.array_equal(np.where(flushed, 0, got.view(np.uint32)),
+                              np.where(flushed, 0, want.view(np.uint32)))
+    else:
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
-@pytest.mark.parametrize("wfmt", [0, 1, 2])
-def test_fast_weight_operands_are_exact(hrb, wfmt):
+@pytest.mark.parametrize("wfmt,w8_kernel", [(0, 0), (1, 0), (1, 1), (2, 0)])
+@pytest.mark.parametrize("m", [288, 64])
+def test_fast_weight_operands_are_exact(hrb, wfmt, w8_kernel, m):
     """A = I (every block's largest value 1.0: q = 64, scale 2^0), so output
     C[r][n] is weight W[n][r] alone, which the tensor-core path must give
     exactly: MXFP4 and MXFP8 codes as they are, W8 as its three E2M1 digit
-    planes with scales e - 6 + 3p.  Bit-equality pins the weight
-    translation."""
+    planes with scales e - 6 + 3p or, with at most 64 tokens, converted to
+    BF16 in the kernel.  Bit-equality pins the weight translation."""
     from hotarubi_b200 import capi
-    rng = np.random.default_rng(90 + wfmt)
-    m = k = 288                       # kb = 9: the second 256-element step is mostly padding
+    rng = np.random.default_rng(90 + wfmt + m)
+    k = 288                           # kb = 9: the second 256-element step is mostly padding
     n = 200
     x = np.eye(m, k, dtype=np.float32)
     kb = k // 32
@@ -260,12 +284,40 @@ def test_fast_weight_operands_are_exact(hrb, wfmt):
     c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
     keep = [dev(x), dev(w), dev(ws)]
     d = capi.Library.desc(wfmt, m, n, k, a=keep[0], w=keep[1], wscale=keep[2], c=c,
-                          mode=capi.MODE_FAST)
+                          mode=capi.MODE_FAST, w8_kernel=w8_kernel)
     hrb.dense(d)
     hrb.sync()
     got = c.cpu().numpy()
-    want = dequant_w(wfmt, w, ws, n, k).T.astype(np.float32)  # [k][n] = W[n][k]
+    want = dequant_w(wfmt, w, ws, n, k).T[:m].astype(np.float32)  # [r][n] = W[n][r]
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_fast_w8_bf16_extreme_scales(hrb):
+    """W8 with at most 64 tokens converts w * 2^(e - 133) to BF16 in the
+    kernel by a fused multiply-add (e <= 237) or a subtract and multiply
+    (e > 237), with subnormal multipliers for e < 7: A = I shows each
+    converted weight exactly (outputs under 2^-126 may come out flushed)."""
+    from hotarubi_b200 import capi
+    rng = np.random.default_rng(123)
+    m, k, n = 64, 256, 136
+    kb = k // 32
+    x = np.eye(m, k, dtype=np.float32)
+    w = rng.integers(-128, 128, (n, k)).astype(np.int8).view(np.uint8)
+    # Up to 253: with 254, -128 * 2^121 overflows, and 0 * inf in the other
+    # products of a column would make it NaN.
+    ws = np.where(rng.random((n, kb)) < 0.5, rng.integers(0, 12, (n, kb)),
+                  rng.integers(226, 254, (n, kb))).astype(np.uint8)
+    c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    keep = [dev(x), dev(w), dev(ws)]
+    d = capi.Library.desc(1, m, n, k, a=keep[0], w=keep[1], wscale=keep[2], c=c,
+                          mode=capi.MODE_FAST, w8_kernel=capi.W8_BF16)
+    hrb.dense(d)
+    hrb.sync()
+    got = c.cpu().numpy()
+    want = dequant_w(1, w, ws, n, k).T[:m].astype(np.float32)
+    flushed = (got == 0) & (np.abs(want) < 2.0**-126)
+    assert np.array_equal(np.where(flushed, 0, got.view(np.uint32)),
+                          np.where(flushed, 0, want.view(np.uint32)))
 
 
 @pytest.mark.parametrize("mixed", [False, True])
