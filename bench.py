@@ -189,6 +189,46 @@ class GaccWorkload:
 GACC = GaccWorkload()
 
 
+@dataclasses.dataclass(frozen=True)
+class PrefixWorkload:
+    """C3: the SmolVLA-shaped VLM prefix stream, 16 decoder layers over M =
+    141 tokens (2 cameras x 64 image tokens + 12 language + 1 state), hidden
+    960, 15 query / 5 KV heads of 64, SiLU-gated MLP of 2560; Q/K/V/O in W8,
+    the MLP in MXFP4, no bias (the model's linears have none).  Per layer the
+    GEMMs run in their dependency groups: Q, K, V (one input), O (the
+    attention output), gate and up (one input), down (the gated product);
+    the attention, RMSNorm and SiLU between them are outside the GEMM path,
+    so each group's input is a seeded synthetic activation with the shape the
+    model gives it (N(0,1) rows renormalised to RMS 1, as each layer's norm
+    leaves them)."""
+    key: str = "c3"
+    name: str = "c3_smolvla_prefix_16x141"
+    M: int = 141
+    layers: int = 16
+    # (name, wfmt, K, N, group)
+    gemms: tuple = (("q", 1, 960, 960, 0), ("k", 1, 960, 320, 0), ("v", 1, 960, 320, 0),
+                    ("o", 1, 960, 960, 1), ("gate", 0, 960, 2560, 2), ("up", 0, 960, 2560, 2),
+                    ("down", 0, 2560, 960, 3))
+    streams: int = 2   # independent prefix streams, alternated so no step finds its weights in L2
+
+    @property
+    def flops(self) -> int:
+        return self.layers * sum(2 * self.M * n * k for _, _, k, n, _ in self.gemms)
+
+    @property
+    def metric(self) -> str:
+        return "W8/MXFP4 GEMM TFLOP/s (C3 SmolVLA prefix stream, 16 layers x 141 tokens)"
+
+    def gemm_bytes(self, wfmt: int, k: int, n: int) -> int:
+        """Compulsory bytes of one GEMM kernel launch (MXINT8 activations)."""
+        kb = (k + 31) // 32
+        w = n * k // 2 if wfmt == 0 else n * k
+        return self.M * k + self.M * kb + w + n * kb + self.M * n * 4
+
+
+PREFIX = PrefixWorkload()
+
+
 def peaks() -> dict:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -325,6 +365,14 @@ def cpu_reference(wl: Workload, min_seconds: float = 2.0, max_reps: int = 50) ->
         dt = time.perf_counter() - t0
         return {"value": reps * sample_flops / dt / 1e12, "unit": "TFLOP/s", "cores": 1,
                 "kind": "port", "sample": f"{reps} x {label} on 1 thread", "seconds": dt}
+    # The ISS runs tokens in multiples of 32 (GemmCommand.m): pad with zero
+    # rows (scale byte 127) as a runtime would; the flops counted stay the
+    # real rows'.
+    prow = (rows + 31) // 32 * 32
+    if prow != rows:
+        q = np.concatenate([q, np.zeros((prow - rows, q.shape[1]), q.dtype)])
+        s = np.concatenate([s, np.full((prow - rows, s.shape[1]), 127, s.dtype)])
+        label += f", padded to {prow} rows"
     a_words = cpu.pack_abuf(q, s).reshape(-1)
     kp = wl.kb * 32
     if wl.wfmt == 0:
@@ -338,13 +386,13 @@ def cpu_reference(wl: Workload, min_seconds: float = 2.0, max_reps: int = 50) ->
         planes = np.concatenate([cpu.pack_wbuf(hi, ws).reshape(-1),
                                  cpu.pack_wbuf(lo, ws).reshape(-1)])
         nplanes = 2
-    c = np.zeros((rows, wl.N), np.uint32)
-    ref.hrbref_dense_gemm_iss(nplanes, rows, wl.N, wl.kb, a_words, planes, c, threads, 0, rows)
+    c = np.zeros((prow, wl.N), np.uint32)
+    ref.hrbref_dense_gemm_iss(nplanes, prow, wl.N, wl.kb, a_words, planes, c, threads, 0, prow)
     t0 = time.perf_counter()
     reps = 0
     while reps < max_reps and (reps < 1 or time.perf_counter() - t0 < min_seconds):
-        ref.hrbref_dense_gemm_iss(nplanes, rows, wl.N, wl.kb, a_words, planes, c, threads, 0,
-                                  rows)
+        ref.hrbref_dense_gemm_iss(nplanes, prow, wl.N, wl.kb, a_words, planes, c, threads, 0,
+                                  prow)
         reps += 1
     dt = time.perf_counter() - t0
     return {"value": reps * sample_flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
@@ -781,6 +829,227 @@ def run_conv(args, rank: int, world: int, local_rank: int) -> None:
         dist.destroy_process_group()
 
 
+def prefix_operands(pw: PrefixWorkload, stream_id: int):
+    """Per layer and GEMM: weights in the dense formats (W8 placed from
+    per-channel int8 the way hotarubi's compiler places it, MXFP4 through
+    CanonicalMxfp4) and per group one FP32 input of RMS-1 rows."""
+    from hotarubi_b200 import workloads
+    layers = []
+    for layer in range(pw.layers):
+        seed = 10000 * (stream_id + 1) + 100 * layer
+        gemms = []
+        for j, (name, wfmt, k, n, group) in enumerate(pw.gemms):
+            if wfmt == 1:
+                q, sc = workloads.w8_per_channel(seed + j, n, k)
+                w, ws = place_w8(workloads.dequantize_per_channel(q, sc))
+            else:
+                w, ws = workloads.mxfp4_weights(seed + j, n, k)
+            gemms.append((name, wfmt, k, n, group, w, ws))
+        inputs = {}
+        for _, _, k, _, group in pw.gemms:
+            if group not in inputs:
+                x = workloads.activations(seed + 50 + group, pw.M, k)
+                x /= np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=1, keepdims=True)).astype(
+                    np.float32)
+                inputs[group] = x
+        layers.append((gemms, inputs))
+    return layers
+
+
+def prefix_cpu_reference(pw: PrefixWorkload, min_seconds: float = 1.0) -> dict:
+    """The reference's ExecuteGemm (oracle/_ref) on one layer's seven GEMM
+    shapes at M = 141 (cpu_reference per shape); the stream's rate is its
+    flops over the summed per-shape times (all layers have the same shapes)."""
+    total_s = 0.0
+    layer_flops = 0
+    parts = []
+    for name, wfmt, k, n, _ in pw.gemms:
+        wl = Workload(f"c3{name}", f"c3_{name}", f"C3 {name} {pw.M}x{k}x{n}", wfmt, pw.M, n, k,
+                      False, 1, "hbm")
+        r = cpu_reference(wl, min_seconds=min_seconds, max_reps=20)
+        flops = 2 * pw.M * n * k
+        total_s += flops / (r["value"] * 1e12)
+        layer_flops += flops
+        parts.append(r)
+    return {"value": layer_flops / total_s / 1e12, "unit": "TFLOP/s", "cores": parts[0]["cores"],
+            "kind": parts[0]["kind"],
+            "sample": f"one layer's 7 GEMMs ({pw.M} rows) through ExecuteGemm tiles on "
+                      f"{parts[0]['cores']} threads, each timed >= {min_seconds} s",
+            "seconds": total_s}
+
+
+def run_prefix(args, rank: int, world: int, local_rank: int) -> None:
+    """--config c3: the 16-layer prefix stream as 64 dependent plan runs (one
+    plan per layer and group) captured in a CUDA graph; one step = one
+    stream.  Two independent streams alternate so that no step finds its
+    weights (about 118 MB) in L2.  Replicas for N > 1 (weak scaling)."""
+    import torch
+
+    from hotarubi_b200 import capi
+    pw = PREFIX
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        # Each run times the seven shapes (about 2 s of CPU work): a few runs.
+        warm, timed = min(args.warmup, 1), max(1, min(args.steps, 5))
+        runs = [prefix_cpu_reference(pw, 0.25) for _ in range(warm + timed)]
+        runs = runs[warm:]
+        value = statistics.median(r["value"] for r in runs)
+        base = runs[-1]
+        print(json.dumps({
+            "impl": "reference", "metric": pw.metric, "value": value, "unit": "TFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": pw.flops / (value * 1e12) * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 block dot + fp32 accumulate", "data": "synthetic",
+            "config": {"workload": pw.name, "sample": base["sample"]},
+            "cpu_baseline": {k: v for k, v in base.items() if k != "seconds"} | {"value": value},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    lib = capi.Library(local_rank)
+    mode = capi.MODE_FAST if args.mode == "fast" else capi.MODE_EXACT
+    stream = torch.cuda.Stream()
+    lib.set_stream(stream.cuda_stream)
+    streams = []
+    keep = []
+    for sid in range(pw.streams):
+        plans, first_x, last_c = [], None, None
+        for gemms, inputs in prefix_operands(pw, sid):
+            xs = {g: torch.from_numpy(x).cuda() for g, x in inputs.items()}
+            keep.append(xs)
+            for group in range(4):
+                descs = []
+                for name, wfmt, k, n, g, w, ws in gemms:
+                    if g != group:
+                        continue
+                    t = {"w": torch.from_numpy(w).cuda(), "ws": torch.from_numpy(ws).cuda(),
+                         "c": torch.zeros((pw.M, n), dtype=torch.float32, device="cuda")}
+                    keep.append(t)
+                    descs.append(capi.Library.desc(wfmt, pw.M, n, k, a=xs[group], w=t["w"],
+                                                   wscale=t["ws"], c=t["c"], mode=mode))
+                    last_c = t["c"]
+                plans.append(lib.plan(descs))
+            if first_x is None:
+                first_x = xs[0]
+        streams.append({"plans": plans, "x0": first_x, "c_last": last_c})
+    torch.cuda.synchronize()
+    # Warm-up outside the graph (kernel attributes are set on first launch),
+    # then one graph per stream.
+    launches_per_step = 0
+    for st in streams:
+        launches_per_step = sum(pl.run(stream.cuda_stream) for pl in st["plans"])
+    stream.synchronize()
+    graphs = []
+    for st in streams:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for pl in st["plans"]:
+                pl.run(stream.cuda_stream)
+        graphs.append(g)
+    torch.cuda.synchronize()
+    # The heaviest launch: the MLP's gate + up GEMMs (group 2), profiled alone.
+    per_plan = streams[0]["plans"][2].profile(reps=20, stream=stream.cuda_stream)
+    gemm_ms = per_plan[-1] if mode == capi.MODE_FAST else max(per_plan)
+    if dist is not None:
+        dist.barrier()
+    with ClockSampler(local_rank) as clocks:
+        with torch.cuda.stream(stream):
+            for i in range(args.warmup):
+                graphs[i % pw.streams].replay()
+        stream.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for i in range(args.steps):
+                graphs[i % pw.streams].replay()
+            end.record(stream)
+        end.synchronize()
+        if dist is not None:
+            dist.barrier()
+    lib.sync()
+    ms = start.elapsed_time(end) / args.steps
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # End to end: the first layer's input from pinned host memory, the
+    # stream, the last GEMM's output back.
+    e2e = None
+    if not args.no_e2e:
+        st = streams[0]
+        xh = st["x0"].cpu().pin_memory()
+        ch = torch.empty(tuple(st["c_last"].shape), dtype=torch.float32).pin_memory()
+        n_e2e = max(1, min(args.steps, 10))
+        for k in range(2 + n_e2e):
+            if k == 2:
+                stream.synchronize()
+                w0 = time.perf_counter()
+            with torch.cuda.stream(stream):
+                st["x0"].copy_(xh, non_blocking=True)
+                graphs[0].replay()
+                ch.copy_(st["c_last"], non_blocking=True)
+            stream.synchronize()
+        dt = (time.perf_counter() - w0) / n_e2e
+        e2e = {"value": world * pw.flops / dt / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": world * xh.numel() * 4,
+               "d2h_bytes_per_step": world * ch.numel() * 4, "ms_per_step": dt * 1e3,
+               "entry_point": "pinned copies + the stream's hrb_plan_run calls in a CUDA graph "
+                              "(weights resident)"}
+    if rank == 0:
+        pk = peaks()
+        mlp_bytes = sum(pw.gemm_bytes(wfmt, k, n) for _, wfmt, k, n, g in pw.gemms if g == 2)
+        achieved = mlp_bytes / (gemm_ms / 1e3) / 1e9
+        w_bytes = pw.layers * sum((n * k // 2 if wfmt == 0 else n * k) + n * ((k + 31) // 32)
+                                  for _, wfmt, k, n, _ in pw.gemms)
+        line = {
+            "metric": pw.metric, "value": world * pw.flops / (ms / 1e3) / 1e12,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 block dot + fp32 accumulate", "data": "synthetic",
+            "config": {"workload": pw.name, "M": pw.M, "layers": pw.layers,
+                       "gemms_per_layer": "q k v (w8) | o (w8) | gate up (mxfp4) | down (mxfp4)",
+                       "formats": "w8 + mxfp4", "bias": False, "mode": args.mode,
+                       "activations": "fp32 per group, encoded on device each step",
+                       "l2": f"{pw.streams} streams alternated, {w_bytes / 1e6:.0f} MB of "
+                             "weights each",
+                       "parallelism": f"replicas x{world}",
+                       "launch": f"{pw.layers * 4} dependent plan runs in a CUDA graph"},
+            "roofline": {"bound": "hbm", "kernel": "k_gemm_mxf4 (gate + up, one launch)"
+                         if mode == capi.MODE_FAST else "k_dense_exact",
+                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / pk["hbm_gbs"], "peak_source": pk["source"] +
+                         " (HBM copy)", "alg_bytes_per_launch": mlp_bytes, "traffic": None,
+                         "launch_ms": gemm_ms},
+            "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = {k: v for k, v in prefix_cpu_reference(pw).items()
+                                    if k != "seconds"}
+        print(json.dumps(line), flush=True)
+    del graphs
+    for st in streams:
+        for pl in st["plans"]:
+            pl.close()
+    lib.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def gacc_operands(gw: GaccWorkload, i: int):
     rng = np.random.default_rng(800 + i)
     rows = rng.integers(0, 256, (gw.nrows, gw.row_stride), dtype=np.uint8)
@@ -1041,7 +1310,8 @@ def main() -> None:
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", choices=sorted(WORKLOADS) + [CONV.key, GACC.key], default="c2")
+    p.add_argument("--config", choices=sorted(WORKLOADS) + [PREFIX.key, CONV.key, GACC.key],
+                   default="c2")
     p.add_argument("--mode", choices=["exact", "fast"], default="fast")
     p.add_argument("--w8-kernel", choices=["planes", "bf16"], default="planes",
                    help="W8 with at most 64 tokens: E2M1 digit planes (kind::mxf4) or int8 "
@@ -1062,6 +1332,9 @@ def main() -> None:
         return
     if args.config == GACC.key:
         run_gacc(args, rank, world, local_rank)
+        return
+    if args.config == PREFIX.key:
+        run_prefix(args, rank, world, local_rank)
         return
     wl = WORKLOADS[args.config]
     if args.impl == "reference":

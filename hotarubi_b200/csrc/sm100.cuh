@@ -62,25 +62,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return false;
 }
 
-// The same with a plain test in a tight loop: no suspension, so the thread
-// sees the phase complete at once (waiters on the critical path).
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, uint32_t* err,
-                                               uint32_t limit = 200000000u) {
-  for (uint32_t i = 0; i < limit; ++i) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    if (ok != 0) return true;
-  }
-  atomicOr(err, kErrTimeout);
-  return false;
-}
-
 // The same for waiters off the critical path (whole warps that wait for a
 // tile at a time): between tests the thread sleeps `sleep_ns`, so it takes
 // no issue slots from the warps doing work.  Gives up after `limit` tests
