@@ -470,6 +470,10 @@ __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
+  // Launch setup, barriers and TMEM overlap the kernel before; its outputs
+  // (this kernel's activations) and its reads of C come before any access.
+  griddep_launch_dependents();
+  griddep_wait();
 
   if (kGather && warp >= 2 && warp < 2 + kGatherWarps) {
     // Gathering lanes: the activation half of every ring slot, in the weight
@@ -761,6 +765,8 @@ __global__ void __launch_bounds__(kBfThreads, 1) k_gemm_w8bf(const __grid_consta
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
+  griddep_launch_dependents();
+  griddep_wait();
 
   if (warp == 0 || warp == 2) {
     // Lane 0 of warp 0: the raw weight chunks; of warp 2: the activation
@@ -953,6 +959,24 @@ __global__ void k_tile_weights_w8raw(const uint8_t* __restrict__ w, const uint8_
   }
 }
 
+// One launch with programmatic stream serialisation (the kernels call
+// griddep_wait before touching memory): 1 on success, -1 on a launch error.
+int launch_pdl(const void* fn, uint32_t grid, uint32_t threads, uint32_t smem, cudaStream_t s,
+               const MxParams& p) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* args[] = {const_cast<MxParams*>(&p)};
+  return cudaLaunchKernelExC(&cfg, fn, args) == cudaSuccess ? 1 : -1;
+}
+
 int launch_w8bf(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, int sm_count,
                 uint32_t* err, cudaStream_t s, const MxPeers* peers) {
   MxParams p{};
@@ -963,8 +987,7 @@ int launch_w8bf(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles
   if (inline_job != nullptr) p.inline_job = *inline_job;
   const uint32_t grid = std::min<uint32_t>(tiles, static_cast<uint32_t>(sm_count));
   if (!set_smem_limit_once(reinterpret_cast<const void*>(k_gemm_w8bf), kBfSmem)) return -1;
-  k_gemm_w8bf<<<grid, kBfThreads, kBfSmem, s>>>(p);
-  return cudaPeekAtLastError() == cudaSuccess ? 1 : -1;
+  return launch_pdl(reinterpret_cast<const void*>(k_gemm_w8bf), grid, kBfThreads, kBfSmem, s, p);
 }
 
 // E2M1 code of a digit in [-4, 4]: 0, 1, 2, 3, 4 -> 0b000, 0b010, 0b100,
@@ -1081,9 +1104,7 @@ int launch_mx(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, 
       p.gather = *gather;
       const void* fn = reinterpret_cast<const void*>(k_gemm_mxf4<NT, WP, KB, true>);
       if (!set_smem_limit_once(fn, Cfg::kSmem)) return -1;
-      k_gemm_mxf4<NT, WP, KB, true>
-          <<<grid, MxWarps<NT, WP, KB, true>::kThreads, Cfg::kSmem, s>>>(p);
-      return cudaPeekAtLastError() == cudaSuccess ? 1 : -1;
+      return launch_pdl(fn, grid, MxWarps<NT, WP, KB, true>::kThreads, Cfg::kSmem, s, p);
     }
   }
   if (gather != nullptr) return -1;
@@ -1091,8 +1112,8 @@ int launch_mx(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, 
                            Cfg::kSmem)) {
     return -1;
   }
-  k_gemm_mxf4<NT, WP, KB, false><<<grid, MxWarps<NT, WP, KB, false>::kThreads, Cfg::kSmem, s>>>(p);
-  return cudaPeekAtLastError() == cudaSuccess ? 1 : -1;
+  return launch_pdl(reinterpret_cast<const void*>(k_gemm_mxf4<NT, WP, KB, false>), grid,
+                    MxWarps<NT, WP, KB, false>::kThreads, Cfg::kSmem, s, p);
 }
 
 template <uint32_t NT, uint32_t WP, uint32_t KB>

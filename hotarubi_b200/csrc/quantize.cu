@@ -19,6 +19,7 @@
 #include "hrb_kernels.cuh"
 #include "hrb_quant.cuh"
 #include "hrb_tc.cuh"
+#include "sm100.cuh"
 
 namespace hrb {
 namespace {
@@ -525,6 +526,10 @@ k_quantize_planes(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ 
     }
   }
   __syncthreads();
+  // The table overlaps the kernel before; the activations it may have
+  // written, and the operand blocks it may still read, come after.
+  sm100::griddep_launch_dependents();
+  sm100::griddep_wait();
   const uint32_t lane = threadIdx.x & 31u, wib = threadIdx.x >> 5;
   const uint32_t warp = blockIdx.x * kPlaneWarps + wib;
   const uint32_t nwarps = gridDim.x * kPlaneWarps;
@@ -628,8 +633,18 @@ void launch_quantize_planes(const QuantJob* jobs_dev, uint32_t njobs, const Quan
   if (blocks == 0) blocks = 1;
   QuantJob one{};
   if (inline_job != nullptr) one = *inline_job;
-  k_quantize_planes<<<static_cast<unsigned>(blocks), kPlaneWarps * 32, 0, stream>>>(jobs_dev, njobs,
-                                                                                    one, error_flag);
+  // Programmatic stream serialisation: the kernel waits (griddep_wait)
+  // before it touches memory.
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(kPlaneWarps * 32);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, k_quantize_planes, jobs_dev, njobs, one, error_flag);
 }
 
 }  // namespace hrb

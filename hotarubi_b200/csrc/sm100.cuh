@@ -86,6 +86,22 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialisation may start while the kernel before it in the stream still
+// runs; griddep_wait() returns once that kernel has completed and its
+// memory operations are visible, so every access to memory another kernel
+// writes or reads comes after it.  griddep_launch_dependents() lets the next
+// kernel start its own prologue early.  Both are no-ops in a normal launch.
+
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // Bulk copy global -> shared, completing on an mbarrier (transaction bytes).
 // Both addresses 16-byte aligned, size a multiple of 16.
 
