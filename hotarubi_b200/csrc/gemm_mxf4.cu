@@ -96,7 +96,11 @@ struct MxCfg {
   static constexpr uint32_t kTmemCols = 512;
   static_assert(kColSfb + 4 * kASf <= kTmemCols, "TMEM columns");
   static constexpr uint32_t kOffBar = kOffW + kWSlots * kWSlot;
-  static constexpr uint32_t kSmem = kOffBar + 512 + 1024;
+  // NT = 64: after the barriers, 512 bytes per epilogue warp to regroup
+  // outputs for 16-byte stores.
+  static constexpr uint32_t kOffStage = kOffBar + 512;
+  static constexpr uint32_t kStage = NT == 64 ? 512u * 8u : 0u;
+  static constexpr uint32_t kSmem = kOffStage + kStage + 1024;
   static_assert(kABlock % 1024 == 0 && kWSlot % 1024 == 0, "ring alignment");
   static_assert(kSmem <= kSmemLimit, "shared memory");
   // Warps: 0 weight producer, 1 TMEM owner and MMA issuer, 2 activation
@@ -105,6 +109,7 @@ struct MxCfg {
   // single accumulator buffer, whose drain holds up the next tile's MMAs:
   // more warps drain it.
   static constexpr uint32_t kEpiWarps = NT == 64 ? 8u : 16u;
+  static_assert(kStage == 0 || kStage == 512u * kEpiWarps, "a staging buffer per epilogue warp");
 };
 
 struct MxParams {
@@ -320,9 +325,15 @@ __device__ __forceinline__ void requant_rows(const MxTile& ti, const float (&x)[
 // taddr, taddr + NT, taddr + 2 NT), added smallest scale first; then C (with
 // accumulate), the column scale, the bias and RELU, and the stores: C, the
 // peers' copies of C and the MXINT8 copy.
+//
+// With `stage` (512 bytes of shared memory for this warp), a full chunk of
+// 16 rows x 32 columns of a plain output (no accumulate, no peers, C 16-byte
+// aligned) is regrouped through shared memory, four rows at a time, into
+// 16-byte stores: lane l writes row l / 8, columns 4 (l % 8) .. + 3.
 template <uint32_t NT, uint32_t kSums>
 __device__ __forceinline__ void drain_tile(const MxParams& p, const MxTile& ti, uint32_t taddr,
-                                           uint32_t r0, uint32_t r1, uint32_t sp, uint32_t lane) {
+                                           uint32_t r0, uint32_t r1, uint32_t sp, uint32_t lane,
+                                           float* stage = nullptr) {
   const uint32_t col = sp * 32u + lane;
   const uint32_t cols = ti.cols_kbq & 0xFFu, kbq = ti.cols_kbq >> 8;
   const bool col_ok = col < cols;
@@ -345,6 +356,9 @@ __device__ __forceinline__ void drain_tile(const MxParams& p, const MxTile& ti, 
   // layer's K (tiles start on 128-column boundaries); the block exists when
   // it starts before column N.
   const bool requant = ti.cq != nullptr && sp * 32u < cols;
+  const bool staged = stage != nullptr && !acc && npeers == 0 && ti.c != nullptr &&
+                      cols == kTileW && (ti.ldc & 3u) == 0 &&
+                      (reinterpret_cast<uintptr_t>(ti.c) & 15u) == 0;
 #pragma unroll 1
   for (uint32_t j0 = r0; j0 < r1; j0 += 16) {
     uint32_t v0[16], v1[16], v2[16];
@@ -358,6 +372,26 @@ __device__ __forceinline__ void drain_tile(const MxParams& p, const MxTile& ti, 
       x[j] = __uint_as_float(v0[j]);
       if constexpr (kSums > 1) x[j] = x[j] + __uint_as_float(v1[j]);
       if constexpr (kSums > 2) x[j] += __uint_as_float(v2[j]);
+    }
+    if (staged && j0 + 16u <= ti.rows) {
+#pragma unroll
+      for (uint32_t j = 0; j < 16; ++j) {
+        if (scaled) x[j] = __fmul_rn(x[j], scale);
+        x[j] = __fadd_rn(x[j], bias);
+        if (relu) x[j] = x[j] > 0.0f ? x[j] : 0.0f;
+      }
+#pragma unroll
+      for (uint32_t q = 0; q < 4; ++q) {
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) stage[j * 32u + lane] = x[4u * q + j];
+        __syncwarp();
+        const float4 v = reinterpret_cast<const float4*>(stage)[lane];
+        __syncwarp();
+        const size_t row = j0 + 4u * q + (lane >> 3);
+        *reinterpret_cast<float4*>(ti.c + row * ti.ldc + sp * 32u + 4u * (lane & 7u)) = v;
+      }
+      if (requant) requant_rows(ti, x, j0, sp, lane, col_ok, kbq, p.err);
+      continue;
     }
     if (col_ok) {
 #pragma unroll
@@ -634,8 +668,10 @@ __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
       ok = __all_sync(0xFFFFFFFFu, ok);
       if (!ok) break;
       tc_fence_after();
-      drain_tile<NT, Cfg::kAPlanes>(p, ti, tmem + ((sp * 32u) << 16) + b * Cfg::kDCols, r0, r1, sp,
-                                    lane);
+      drain_tile<NT, Cfg::kAPlanes>(
+          p, ti, tmem + ((sp * 32u) << 16) + b * Cfg::kDCols, r0, r1, sp, lane,
+          Cfg::kStage != 0 ? reinterpret_cast<float*>(smem + Cfg::kOffStage) + (warp - kFirstEpi) * 128u
+                           : nullptr);
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);
     }
