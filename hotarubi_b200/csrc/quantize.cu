@@ -286,12 +286,12 @@ __device__ __forceinline__ PlaneOut plane_out(const PlaneJob& j, uint32_t row, u
     }
     o.sf[2] = 0;
   } else {
-    // E2M1: lane l's four bytes sit in logical 16-byte chunk l / 4 of the row.
+    // E2M1: lane l's four bytes sit in logical 16-byte chunk l / 4 of the row;
+    // lanes l % 4 = p < 3 of a block write plane p's scale byte.
     o.off = r * 128u + (((lane >> 2) ^ (r & 7u)) << 4) + (lane & 3u) * 4u;
-#pragma unroll
-    for (uint32_t p = 0; p < 3; ++p) {
-      o.sf[p] = mx_act_sf_offset(j.tile_rows, p * j.tile_rows + r, lane >> 2);
-    }
+    const uint32_t p = lane & 3u;
+    o.sf[0] = p < 3u ? mx_act_sf_offset(j.tile_rows, p * j.tile_rows + r, lane >> 2) : 0u;
+    o.sf[1] = o.sf[2] = 0;
   }
   return o;
 }
@@ -441,13 +441,10 @@ __device__ __forceinline__ void encode_planes(const PlaneJob& j, const PlaneOut&
   *reinterpret_cast<uint32_t*>(blk + o.off) = __byte_perm(a01, a23, 0x5410u);
   *reinterpret_cast<uint32_t*>(blk + j.plane_bytes + o.off) = __byte_perm(a01, a23, 0x7632u);
   *reinterpret_cast<uint32_t*>(blk + 2u * j.plane_bytes + o.off) = __byte_perm(b01, b23, 0x5410u);
-  if ((lane & 3u) == 0) {
-#pragma unroll
-    for (uint32_t p = 0; p < 3; ++p) {
-      int32_t se = static_cast<int32_t>(scale) - 6 + 3 * static_cast<int32_t>(p);
-      se = se > 254 ? 254 : se;  // scale >= 6 here or the block is zero
-      blk[o.sf[p]] = static_cast<uint8_t>(se < 0 ? 0 : se);
-    }
+  if ((lane & 3u) < 3u) {
+    int32_t se = static_cast<int32_t>(scale) - 6 + 3 * static_cast<int32_t>(lane & 3u);
+    se = se > 254 ? 254 : se;  // scale >= 6 here or the block is zero
+    blk[o.sf[0]] = static_cast<uint8_t>(se < 0 ? 0 : se);
   }
 }
 
