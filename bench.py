@@ -303,13 +303,17 @@ def host_operands(wl: Workload, i: int, place=None):
     from hotarubi_b200 import workloads
     x = workloads.activations(100 + i, wl.M, wl.K)
     b = workloads.bias(300 + i, wl.N) if wl.bias else None
+    kp = wl.kb * 32  # the dense formats store K padded to whole blocks
     if wl.wfmt == 0:
-        w, ws = workloads.mxfp4_weights(200 + i, wl.N, wl.K)
+        w, ws = workloads.mxfp4_weights(200 + i, wl.N, kp)
+        if kp != wl.K:
+            w[:, wl.K // 2:] = 0
     elif wl.wfmt == 1:
         q, s = workloads.w8_per_channel(200 + i, wl.N, wl.K)
         w, ws = (place or place_w8)(workloads.dequantize_per_channel(q, s))
     else:
-        w, ws = workloads.mxfp8_weights(200 + i, wl.N, wl.K)
+        w, ws = workloads.mxfp8_weights(200 + i, wl.N, kp)
+        w[:, wl.K:] = 0
     return x, w, ws, b
 
 
@@ -454,6 +458,65 @@ def build_batch(torch, lib, capi, wl: Workload, batch: int, mode: int, distinct:
     return inst, lib.plan(descs), sets
 
 
+_E2M1 = np.array([0, 0.5, 1, 1.5, 2, 3, 4, 6], np.float64)
+
+
+def dequant_weights(wfmt: int, w: np.ndarray, ws: np.ndarray, n: int, kp: int) -> np.ndarray:
+    """[N][kp] float64 values of the dense weight formats (include/hrb_gemm.h)."""
+    sc = np.repeat(np.ldexp(1.0, ws.astype(np.int64) - 127), 32, axis=1)
+    if wfmt == 0:
+        codes = np.zeros((n, kp), np.uint8)
+        codes[:, 0::2] = w & 0xF
+        codes[:, 1::2] = w >> 4
+        return _E2M1[codes & 7] * np.where(codes & 8, -1.0, 1.0) * sc
+    if wfmt == 1:
+        return w.view(np.int8).astype(np.float64) * sc * 2.0**-6
+    e = ((w >> 3) & 0xF).astype(np.int64)
+    m = (w & 7).astype(np.float64)
+    v = np.where(e == 0, m / 8 * 2.0**-6, (1 + m / 8) * np.ldexp(1.0, e - 7))
+    return np.where(w & 0x80, -v, v) * sc
+
+
+def fast_parity(torch, lib, wl: Workload, x, w, ws, bias, c_dev, rows: int = 64) -> dict:
+    """GEMM 0's fast-mode output on its first rows against the float64 dot
+    product of its dequantized operands (activation codes from the library's
+    own MXINT8 encoder): the max relative error, the stated bound
+    (K/16 + 4) 2^-23 sum|a w| per output, and the ulp histogram against
+    that product rounded to FP32."""
+    m = min(rows, wl.M)
+    kb, kp = wl.kb, wl.kb * 32
+    xd = torch.from_numpy(np.ascontiguousarray(x[:m])).cuda()
+    q = torch.zeros((m, kp), dtype=torch.int8, device="cuda")
+    s = torch.zeros((m, kb), dtype=torch.uint8, device="cuda")
+    lib.quantize(xd, m, wl.K, q, s)
+    lib.sync()
+    a = q.cpu().numpy().astype(np.float64) * np.repeat(
+        np.ldexp(1.0, s.cpu().numpy().astype(np.int64) - 133), 32, axis=1)
+    wd = dequant_weights(wl.wfmt, w, ws, wl.N, kp)
+    ref = a @ wd.T
+    absref = np.abs(a) @ np.abs(wd).T
+    if bias is not None:
+        ref += bias.astype(np.float64)
+        absref += np.abs(bias.astype(np.float64))
+    got = c_dev[:m].cpu().numpy()
+    err = np.abs(got.astype(np.float64) - ref)
+    bound = (kp / 16 + 4) * 2.0**-23 * absref + 1e-30
+    rel = err / (absref + 1e-30)
+
+    def ordered(v):
+        i = v.view(np.int32).astype(np.int64)
+        return np.where(i < 0, -(i & 0x7FFFFFFF), i)
+    d = np.abs(ordered(got.astype(np.float32)) - ordered(ref.astype(np.float32)))
+    return {"reference": "float64 dot of the dequantized operands (library MXINT8 encoder)",
+            "rows": m, "outputs": int(err.size), "max_rel_err": float(rel.max()),
+            "bound": "(K/16 + 4) * 2^-23 * sum|a w| per output",
+            "within_bound": bool((err <= bound).all()),
+            "ulp_hist_vs_fp32_rounded": {"0": int((d == 0).sum()), "1": int((d == 1).sum()),
+                                         "2-3": int(((d >= 2) & (d < 4)).sum()),
+                                         "4-15": int(((d >= 4) & (d < 16)).sum()),
+                                         ">=16": int((d >= 16).sum())}}
+
+
 def traffic_from_profiles(kernel: str, wl: Workload):
     """DRAM bytes per GEMM of `kernel` on this workload, as summarised from an
     ncu capture in profiles/dram_traffic.txt (lines: kernel workload bytes)."""
@@ -545,6 +608,10 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+    parity = None
+    if rank == 0 and mode == capi.MODE_FAST:
+        x0, w0, ws0, b0 = sets[0]
+        parity = fast_parity(torch, lib, wl, x0, w0, ws0, b0, inst[0]["c"])
 
     e2e = None
     if not args.no_e2e:
@@ -622,6 +689,8 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
             "e2e": e2e, "gpu_launches": launches,
             "clocks": clocks.summary(),
         }
+        if parity is not None:
+            line["parity"] = parity
         # The same batch on hotarubi's NPU, by the ISS cycle model of its GEMM
         # instructions at the 250 MHz PL clock (none for MXFP8).
         npu = capi.dense_npu_cycles(wl.wfmt, wl.M, wl.N, wl.K)
