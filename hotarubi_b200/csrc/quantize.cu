@@ -14,6 +14,7 @@
 // 32-element block, a warp covers 128 elements (4 blocks) of one row.  The
 // block maximum is an integer max over the magnitude bits across 8 lanes.
 // Traffic is the compulsory 4 bytes in and 1 + 1/32 bytes out per element.
+#include <algorithm>
 #include <cstdint>
 
 #include "hrb_kernels.cuh"
@@ -624,8 +625,14 @@ void launch_quantize_planes(const QuantJob* jobs_dev, uint32_t njobs, const Quan
     }
     per_sm = n;
   }
+  // Four units a warp or more when that fills the GPU; a smaller job (a few
+  // hundred rows) spreads down to one unit a warp, so a warp waits for one
+  // load, not four in a row.
   uint64_t blocks = (total_units + 4 * kPlaneWarps - 1) / (4 * kPlaneWarps);
   const uint64_t cap = static_cast<uint64_t>(sm_count) * per_sm;
+  if (blocks < cap) {
+    blocks = std::min<uint64_t>(cap, (total_units + kPlaneWarps - 1) / kPlaneWarps);
+  }
   if (blocks > cap) blocks = cap;
   if (blocks == 0) blocks = 1;
   QuantJob one{};
