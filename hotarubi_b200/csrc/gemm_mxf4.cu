@@ -83,7 +83,11 @@ struct MxCfg {
   // A slot of the W ring: one weight chunk, plus the step's activation block
   // when the rings are combined.
   static constexpr uint32_t kWSlot = kWChunk + (kSplit ? 0u : kABlock);
-  static constexpr uint32_t kWSlots = (kSmemLimit - 1024 - 512 - kOffW) / kWSlot;
+  // After the barriers, 512 bytes per epilogue warp to regroup outputs for
+  // 16-byte stores, where that costs no ring slot (not for W8 at NT = 128,
+  // whose weight ring would lose one).
+  static constexpr uint32_t kStage = (NT == 128 && kSplit) ? 0u : 512u * (NT == 64 ? 8u : 16u);
+  static constexpr uint32_t kWSlots = (kSmemLimit - 1024 - 512 - kStage - kOffW) / kWSlot;
   static_assert(kWSlots >= WP + 1, "weight ring");
   // Accumulator buffers of kAPlanes NT columns (one per stacked plane row);
   // two for NT = 64 so one tile's epilogue overlaps the next tile's MMAs.
@@ -96,10 +100,7 @@ struct MxCfg {
   static constexpr uint32_t kTmemCols = 512;
   static_assert(kColSfb + 4 * kASf <= kTmemCols, "TMEM columns");
   static constexpr uint32_t kOffBar = kOffW + kWSlots * kWSlot;
-  // NT = 64: after the barriers, 512 bytes per epilogue warp to regroup
-  // outputs for 16-byte stores.
   static constexpr uint32_t kOffStage = kOffBar + 512;
-  static constexpr uint32_t kStage = NT == 64 ? 512u * 8u : 0u;
   static constexpr uint32_t kSmem = kOffStage + kStage + 1024;
   static_assert(kABlock % 1024 == 0 && kWSlot % 1024 == 0, "ring alignment");
   static_assert(kSmem <= kSmemLimit, "shared memory");
