@@ -331,10 +331,14 @@ __device__ __forceinline__ void requant_rows(const MxTile& ti, const float (&x)[
 // 16 rows x 32 columns of a plain output (no accumulate, no peers, C 16-byte
 // aligned) is regrouped through shared memory, four rows at a time, into
 // 16-byte stores: lane l writes row l / 8, columns 4 (l % 8) .. + 3.
-template <uint32_t NT, uint32_t kSums>
-__device__ __forceinline__ void drain_tile(const MxParams& p, const MxTile& ti, uint32_t taddr,
+//
+// With `release` and 32 rows for this warp, both chunks are read out of TMEM
+// first and the accumulator is released (an arrival on `release`) before
+// the stores, so the next tile's MMAs overlap them; returns whether it was.
+template <uint32_t NT, uint32_t kSums, bool kEarly = false>
+__device__ __forceinline__ bool drain_tile(const MxParams& p, const MxTile& ti, uint32_t taddr,
                                            uint32_t r0, uint32_t r1, uint32_t sp, uint32_t lane,
-                                           float* stage = nullptr) {
+                                           float* stage = nullptr, uint64_t* release = nullptr) {
   const uint32_t col = sp * 32u + lane;
   const uint32_t cols = ti.cols_kbq & 0xFFu, kbq = ti.cols_kbq >> 8;
   const bool col_ok = col < cols;
@@ -360,20 +364,22 @@ __device__ __forceinline__ void drain_tile(const MxParams& p, const MxTile& ti, 
   const bool staged = stage != nullptr && !acc && npeers == 0 && ti.c != nullptr &&
                       cols == kTileW && (ti.ldc & 3u) == 0 &&
                       (reinterpret_cast<uintptr_t>(ti.c) & 15u) == 0;
-#pragma unroll 1
-  for (uint32_t j0 = r0; j0 < r1; j0 += 16) {
+  // The plane sums of rows j0 .. j0 + 15 out of TMEM.
+  const auto load = [&](uint32_t j0, float (&x)[16]) {
     uint32_t v0[16], v1[16], v2[16];
     tmem_ld16(taddr + j0, v0);
     if constexpr (kSums > 1) tmem_ld16(taddr + NT + j0, v1);
     if constexpr (kSums > 2) tmem_ld16(taddr + 2 * NT + j0, v2);
     tmem_wait_ld();
-    float x[16];
 #pragma unroll
     for (uint32_t j = 0; j < 16; ++j) {
       x[j] = __uint_as_float(v0[j]);
       if constexpr (kSums > 1) x[j] = x[j] + __uint_as_float(v1[j]);
       if constexpr (kSums > 2) x[j] += __uint_as_float(v2[j]);
     }
+  };
+  // Accumulate, scale, bias, RELU and the stores of those rows.
+  const auto finish = [&](uint32_t j0, float (&x)[16]) {
     if (staged && j0 + 16u <= ti.rows) {
 #pragma unroll
       for (uint32_t j = 0; j < 16; ++j) {
@@ -392,7 +398,7 @@ __device__ __forceinline__ void drain_tile(const MxParams& p, const MxTile& ti, 
         *reinterpret_cast<float4*>(ti.c + row * ti.ldc + sp * 32u + 4u * (lane & 7u)) = v;
       }
       if (requant) requant_rows(ti, x, j0, sp, lane, col_ok, kbq, p.err);
-      continue;
+      return;
     }
     if (col_ok) {
 #pragma unroll
@@ -419,7 +425,26 @@ __device__ __forceinline__ void drain_tile(const MxParams& p, const MxTile& ti, 
       }
     }
     if (requant) requant_rows(ti, x, j0, sp, lane, col_ok, kbq, p.err);
+  };
+  if constexpr (kEarly) {
+    if (release != nullptr && r1 - r0 == 32u) {
+      float xa[16], xb[16];
+      load(r0, xa);
+      load(r0 + 16u, xb);
+      tc_fence_before();
+      mbar_arrive(release);
+      finish(r0, xa);
+      finish(r0 + 16u, xb);
+      return true;
+    }
   }
+#pragma unroll 1
+  for (uint32_t j0 = r0; j0 < r1; j0 += 16) {
+    float x[16];
+    load(j0, x);
+    finish(j0, x);
+  }
+  return false;
 }
 
 // A ring of `slots` buffers with full/empty mbarriers, walked by a running
@@ -459,7 +484,9 @@ struct MxWarps {
   static constexpr uint32_t kThreads = 32u * (kFirstEpi + MxCfg<NT, WP, KB>::kEpiWarps);
 };
 
-template <uint32_t NT, uint32_t WP, uint32_t KB, bool kGather>
+// kEarly (NT = 128 launches with several tiles a CTA): the epilogue releases
+// the single accumulator before its stores (drain_tile).
+template <uint32_t NT, uint32_t WP, uint32_t KB, bool kGather, bool kEarly = false>
 __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
     k_gemm_mxf4(const __grid_constant__ MxParams p) {
   static_assert(!kGather || (WP == 1 && KB == 4), "the gathering variant is MXFP4 only");
@@ -669,12 +696,18 @@ __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
       ok = __all_sync(0xFFFFFFFFu, ok);
       if (!ok) break;
       tc_fence_after();
-      drain_tile<NT, Cfg::kAPlanes>(
+      // A single accumulator (NT = 128) is released as soon as it is read
+      // when another tile follows.
+      const bool more = tile + gridDim.x < p.total_tiles;
+      const bool released = drain_tile<NT, Cfg::kAPlanes, kEarly>(
           p, ti, tmem + ((sp * 32u) << 16) + b * Cfg::kDCols, r0, r1, sp, lane,
           Cfg::kStage != 0 ? reinterpret_cast<float*>(smem + Cfg::kOffStage) + (warp - kFirstEpi) * 128u
-                           : nullptr);
-      tc_fence_before();
-      mbar_arrive(&acc_empty[b]);
+                           : nullptr,
+          Cfg::kDBufs == 1 && more ? &acc_empty[b] : nullptr);
+      if (!released) {
+        tc_fence_before();
+        mbar_arrive(&acc_empty[b]);
+      }
     }
     // Peer stores performed before the kernel is seen to finish.
     if (p.peers.count != 0) __threadfence_system();
@@ -1145,12 +1178,13 @@ int launch_mx(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, 
     }
   }
   if (gather != nullptr) return -1;
-  if (!set_smem_limit_once(reinterpret_cast<const void*>(k_gemm_mxf4<NT, WP, KB, false>),
-                           Cfg::kSmem)) {
-    return -1;
-  }
-  return launch_pdl(reinterpret_cast<const void*>(k_gemm_mxf4<NT, WP, KB, false>), grid,
-                    MxWarps<NT, WP, KB, false>::kThreads, Cfg::kSmem, s, p);
+  // Early accumulator release pays where CTAs run several tiles; launches
+  // of one or two tiles a CTA take the plain (smaller) kernel.
+  const void* fn = Cfg::kDBufs == 1 && tiles >= 3u * grid
+                       ? reinterpret_cast<const void*>(k_gemm_mxf4<NT, WP, KB, false, true>)
+                       : reinterpret_cast<const void*>(k_gemm_mxf4<NT, WP, KB, false, false>);
+  if (!set_smem_limit_once(fn, Cfg::kSmem)) return -1;
+  return launch_pdl(fn, grid, MxWarps<NT, WP, KB, false>::kThreads, Cfg::kSmem, s, p);
 }
 
 template <uint32_t NT, uint32_t WP, uint32_t KB>
