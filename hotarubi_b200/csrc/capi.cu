@@ -713,6 +713,14 @@ QuantJob make_quant_job_for_noalloc(const hrb_gemm_desc* d, int8_t* q, uint8_t* 
 
 QuantJob make_post_quant_job_for_noalloc(const hrb_gemm_desc* d) { return post_quant_job(d); }
 
+hrb_status noalloc_fail(hrb_status status, const char* message) {
+  return fail(nullptr, status, "%s", message);
+}
+
+hrb_status noalloc_cuda_fail(cudaError_t err, const char* what) {
+  return cuda_fail(nullptr, err, what);
+}
+
 DenseJob make_dense_job_for_noalloc(const hrb_gemm_desc* d, const int8_t* aq,
                                     const uint8_t* ascale, const uint32_t* pieces,
                                     uint32_t npieces) {

@@ -193,6 +193,9 @@ QuantJob make_post_quant_job_for_noalloc(const hrb_gemm_desc* desc);
 DenseJob make_dense_job_for_noalloc(const hrb_gemm_desc* desc, const int8_t* aq,
                                     const uint8_t* ascale, const uint32_t* pieces,
                                     uint32_t npieces);
+// The message of a failed context-free call (hrb_last_error(NULL)).
+hrb_status noalloc_fail(hrb_status status, const char* message);
+hrb_status noalloc_cuda_fail(cudaError_t err, const char* what);
 
 // Layout translation kernels.
 void launch_wbuf_to_dense(const uint8_t* words, uint32_t groups, uint32_t kb, uint8_t* codes,

@@ -23,13 +23,22 @@
 //     threads) race on it: serialise them on one stream.
 //   * The first call on a device looks the array's device address up with
 //     cudaGetSymbolAddress (host code cannot use the symbol itself as a
-//     device pointer) with that device current, and caches it; make that
-//     first call before any stream capture.
+//     device pointer) with that device current, and caches it per device
+//     ordinal; make that first call before any stream capture.  The address
+//     belongs to the context current at that moment: the runtime's primary
+//     context, the only one this entry point supports.  A host that makes
+//     its own driver context current, or resets the device
+//     (cudaDeviceReset), must not use it afterwards: the cached address is
+//     not looked up again.
+//   * A CUDA error already pending on the calling thread (an earlier launch
+//     of someone else's that failed) is not taken for this call's: the call
+//     returns HRB_ECUDA naming it, launches nothing and leaves it pending.
 //   * Non-finite activations are not reported (there is no context to hold
 //     the flag); hrb_gemm_dense reports them through hrb_sync.
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdio>
 #include <mutex>
 
 #include "hrb_gemm.h"
@@ -56,17 +65,21 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Once per device, with that device current: the array's device address.
 hrb_status setup_device(int device, DeviceSetup* out) {
-  if (device < 0 || device >= kMaxDevices) return HRB_EINVAL;
+  if (device < 0 || device >= kMaxDevices) {
+    return hrb::noalloc_fail(HRB_EINVAL, "hrb_gemm_dense_noalloc: device ordinal out of range");
+  }
   std::lock_guard<std::mutex> lock(g_setup_mutex);
   DeviceSetup& s = g_setup[device];
   if (s.scratch == nullptr) {
     void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) {
-      return HRB_ECUDA;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || ptr == nullptr) {
+      return hrb::noalloc_cuda_fail(e, "hrb_gemm_dense_noalloc: cudaGetSymbolAddress of the scratch");
     }
     int sms = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
-      return HRB_ECUDA;
+    const cudaError_t a = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (a != cudaSuccess) {
+      return hrb::noalloc_cuda_fail(a, "hrb_gemm_dense_noalloc: SM count");
     }
     s.sm_count = sms;
     s.scratch = static_cast<uint8_t*>(ptr);
@@ -82,13 +95,26 @@ extern "C" hrb_status hrb_gemm_dense_noalloc(const hrb_gemm_desc* desc, void* st
   uint32_t npieces = 0;
   hrb_status st = hrb::check_desc_for_noalloc(desc, pieces, &npieces);
   if (st != HRB_OK) return st;
-  if (desc->c == nullptr) return HRB_EINVAL;  // the exact kernel writes C
+  if (desc->c == nullptr) {  // the exact kernel writes C
+    return hrb::noalloc_fail(HRB_EINVAL, "hrb_gemm_dense_noalloc: c is required");
+  }
   const uint32_t kb = (desc->K + 31u) / 32u;
   const size_t code_bytes = align_up(size_t{desc->M} * kb * 32u, 256);
   const size_t scale_bytes = align_up(size_t{desc->M} * kb, 256);
-  if (desc->a != nullptr && code_bytes + scale_bytes > kScratchBytes) return HRB_EINVAL;
+  if (desc->a != nullptr && code_bytes + scale_bytes > kScratchBytes) {
+    char msg[160];
+    std::snprintf(msg, sizeof msg,
+                  "hrb_gemm_dense_noalloc: activation encoding needs %zu bytes, scratch holds %zu",
+                  code_bytes + scale_bytes, kScratchBytes);
+    return hrb::noalloc_fail(HRB_EINVAL, msg);
+  }
+  const cudaError_t pending = cudaPeekAtLastError();
+  if (pending != cudaSuccess) {
+    return hrb::noalloc_cuda_fail(pending, "hrb_gemm_dense_noalloc: an earlier CUDA error is pending");
+  }
   int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess) return HRB_ECUDA;
+  const cudaError_t g = cudaGetDevice(&device);
+  if (g != cudaSuccess) return hrb::noalloc_cuda_fail(g, "hrb_gemm_dense_noalloc: cudaGetDevice");
   DeviceSetup setup;
   st = setup_device(device, &setup);
   if (st != HRB_OK) return st;
@@ -121,5 +147,6 @@ extern "C" hrb_status hrb_gemm_dense_noalloc(const hrb_gemm_desc* desc, void* st
                          reinterpret_cast<uint32_t*>(setup.scratch + kScratchBytes),
                          setup.sm_count, s);
   }
-  return cudaGetLastError() == cudaSuccess ? HRB_OK : HRB_ECUDA;
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HRB_OK : hrb::noalloc_cuda_fail(e, "hrb_gemm_dense_noalloc: launch");
 }

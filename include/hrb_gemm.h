@@ -251,8 +251,12 @@ HRB_API hrb_status hrb_gemm_dense_host(hrb_ctx* ctx, const hrb_gemm_desc* desc);
  * All calls share that array: calls that overlap on the GPU race, so
  * serialise them on one stream.  The first call on a device (the current
  * device) looks the array's address up; make it before any stream capture.
- * Runs on `stream` (NULL: the default stream).  Non-finite activations are
- * not reported. */
+ * That address belongs to the runtime's primary context, the only context
+ * this entry point supports; it is not looked up again after a
+ * cudaDeviceReset.  Runs on `stream` (NULL: the default stream).  Failures
+ * leave a message for hrb_last_error(NULL); a CUDA error already pending on
+ * the calling thread makes the call return HRB_ECUDA without launching.
+ * Non-finite activations are not reported. */
 #define HRB_NOALLOC_SCRATCH_BYTES (4u << 20)
 HRB_API hrb_status hrb_gemm_dense_noalloc(const hrb_gemm_desc* desc, void* stream);
 

@@ -115,3 +115,66 @@ def test_noalloc_column_scales_match_the_oracle():
     assert capi.load().hrb_gemm_dense_noalloc(ctypes.byref(d), None) == capi.HRB_OK
     torch.cuda.synchronize()
     assert (got.cpu().numpy().view(np.uint32) == want).all()
+
+
+def test_noalloc_mxint8_input_on_a_caller_stream():
+    """Pre-encoded MXINT8 activations (aq/ascale: the scratch is not used) on
+    a caller-supplied stream, bit for bit with hrb_gemm_dense."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from hotarubi_b200 import capi, workloads
+    from oracle import cpu
+    lib = capi.load()
+    ctx = capi.Library(0)
+    torch.cuda.set_device(0)
+    rng = np.random.default_rng(77)
+    m, n, k = 96, 136, 640
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    q, s = cpu.encode_mxint8(x.view(np.uint32))
+    w, ws = workloads.mxfp4_weights(5, n, k)
+    aq, asc, dw, dws = (torch.from_numpy(v).cuda() for v in (q, s, w, ws))
+    want = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    ctx.dense(capi.Library.desc(capi.WFMT_MXFP4, m, n, k, aq=aq, ascale=asc, w=dw, wscale=dws,
+                                c=want))
+    ctx.sync()
+    stream = torch.cuda.Stream()
+    got = torch.full((m, n), -1.0, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    d = capi.Library.desc(capi.WFMT_MXFP4, m, n, k, aq=aq, ascale=asc, w=dw, wscale=dws, c=got)
+    assert lib.hrb_gemm_dense_noalloc(ctypes.byref(d), ctypes.c_void_p(stream.cuda_stream)) \
+        == capi.HRB_OK
+    stream.synchronize()
+    assert torch.equal(got.view(torch.int32), want.view(torch.int32))
+    ctx.close()
+
+
+def test_noalloc_encoding_that_just_fits_the_scratch():
+    """M = 992 at K = 4096 needs 4,190,208 of the scratch's 4,194,304 bytes
+    (codes and scales, each rounded up to 256): accepted and equal to
+    hrb_gemm_dense; M = 993 needs 4,194,560 and is refused with a message."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from hotarubi_b200 import capi, workloads
+    lib = capi.load()
+    ctx = capi.Library(0)
+    torch.cuda.set_device(0)
+    n, k = 24, 4096
+    w, ws = workloads.mxfp4_weights(9, n, k)
+    dw, dws = torch.from_numpy(w).cuda(), torch.from_numpy(ws).cuda()
+    x = torch.from_numpy(np.random.default_rng(3).standard_normal((993, k))
+                         .astype(np.float32)).cuda()
+    m = 992
+    want = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    ctx.dense(capi.Library.desc(capi.WFMT_MXFP4, m, n, k, a=x[:m], w=dw, wscale=dws, c=want))
+    ctx.sync()
+    got = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    d = capi.Library.desc(capi.WFMT_MXFP4, m, n, k, a=x[:m], w=dw, wscale=dws, c=got)
+    assert lib.hrb_gemm_dense_noalloc(ctypes.byref(d), None) == capi.HRB_OK
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int32), want.view(torch.int32))
+    over = torch.zeros((993, n), dtype=torch.float32, device="cuda")
+    d = capi.Library.desc(capi.WFMT_MXFP4, 993, n, k, a=x, w=dw, wscale=dws, c=over)
+    assert lib.hrb_gemm_dense_noalloc(ctypes.byref(d), None) == capi.HRB_EINVAL
+    msg = lib.hrb_last_error(None).decode()
+    assert "4194560" in msg and "4194304" in msg, msg
+    ctx.close()
