@@ -1353,7 +1353,7 @@ hrb_status plan_launch(hrb_plan* plan, cudaStream_t s, int64_t only, uint32_t* l
   }
   if (plan->nplanes > 0 && take()) {
     hrb::launch_quantize_planes(plan->d_planes, plan->nplanes, nullptr, plan->plane_units,
-                                ctx->d_error, ctx->sm_count, s);
+                                ctx->d_error, ctx->sm_count, s, plan->d_planes_host.data());
     ++n;
   }
   for (auto& g : plan->groups) {
@@ -1493,7 +1493,7 @@ hrb_status hrb_plan_run_host(hrb_plan* plan, void* stream, const void* const* a_
     uint64_t units = 0;
     for (uint32_t i = g0; i < g1; ++i) units += plan->d_planes_host[i].units;
     hrb::launch_quantize_planes(plan->d_planes + g0, g1 - g0, nullptr, units, ctx->d_error,
-                                ctx->sm_count, s);
+                                ctx->sm_count, s, plan->d_planes_host.data() + g0);
     const uint32_t t0 = plan->io[g0].tile_begin;
     const uint32_t t1 = plan->io[g1 - 1].tile_begin + plan->io[g1 - 1].tiles;
     const int k = hrb::launch_mxf4(g.d_tiles + t0, nullptr, g.nt, g.wfmt, t1 - t0,

@@ -160,9 +160,11 @@ void launch_quantize(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* i
 // The activations of kind::mxf4 GEMMs (tiles_kind 2): E2M1 digit planes and
 // their scales, no MXINT8 output.  A unit is one (row, 256-element K step):
 // units = rows * k_steps per job, unit_begin the prefix over the launch.
+// jobs_host: a host copy of jobs_dev (or null), from which the launch picks
+// the specialised encoder when every job allows it.
 void launch_quantize_planes(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* inline_job,
                             uint64_t total_units, uint32_t* error_flag, int sm_count,
-                            cudaStream_t stream);
+                            cudaStream_t stream, const QuantJob* jobs_host = nullptr);
 
 // The exact (bit-identical) dense GEMM on CUDA cores, all GEMMs of one weight
 // format per launch.  Returns the number of kernels launched.

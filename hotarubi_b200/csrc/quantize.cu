@@ -595,6 +595,309 @@ k_quantize_planes(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ 
   if (__any_sync(0xFFFFFFFFu, bad != 0) && lane == 0) atomicOr(error_flag, 1u);
 }
 
+
+// ---------------------------------------------------------------------------
+// The plane encoder's common case, specialised: E2M1 planes (kind::mxf4) of
+// 16-byte-aligned FP32 rows, every job of the launch with NT-row tiles and
+// one rounding rule.  Units, unit ranges, the staging ring and the outputs
+// are those of k_quantize_planes; what changes is the work per unit:
+//   * q comes out of one fused multiply-add scaled by 4.  t = x 2^(8 - e) +
+//     6 2^23 lies in [2^25, 2^26), where FP32 steps by 4, so its one rounding
+//     gives t = 6 2^23 + 4 RNE(x 2^(6 - e)) exactly (x 2^(6 - e) is exact
+//     and ties go to the even multiple of 4, i.e. to even q), and the bits of
+//     t masked with 0x3FC are (q & 0xFF) * 4: the byte offset of q's entry
+//     in a table of 4-byte words, with no shift;
+//   * two tables, the digit codes in the low nibble of each plane byte and
+//     the same in the high nibble, merge an element pair with one OR;
+//   * the tile height is a template parameter, so the three plane stores and
+//     the scale store take constant offsets from one block pointer, and both
+//     walks (loads and stores) advance by additions.
+// Blocks whose scale 2^(8 - e) leaves the FP32 range (largest magnitude
+// below 2^-119, or Inf/NaN) take the integer rules, as in k_quantize_planes.
+
+// The load side of a warp's walk over units: the lane's first element of
+// the current unit, for the cp.async staging.
+struct E2m1Loads {
+  const float* x;
+  const float* src;
+  uint32_t ldx, cols, rows, k_steps;
+  uint32_t jx, row, step, col0;
+};
+
+// The store side: the current unit's activation block and the lane's
+// offsets in it (plane word, scale byte).
+struct E2m1Stores {
+  uint8_t* tiles;
+  uint8_t* blk;
+  uint32_t rows, k_steps;
+  uint32_t jx, row, step, off, sf;
+};
+
+__device__ __forceinline__ void e2m1_loads_at(E2m1Loads& w, const QuantJob& j, uint32_t row,
+                                              uint32_t step, uint32_t lane) {
+  w.x = j.x;
+  w.ldx = j.ldx;
+  w.cols = j.cols;
+  w.rows = j.rows;
+  w.k_steps = j.k_steps;
+  w.row = row;
+  w.step = step;
+  w.col0 = step * 256u + lane * 8u;
+  w.src = j.x + static_cast<size_t>(row) * j.ldx + w.col0;
+}
+
+template <uint32_t NT>
+__device__ __forceinline__ void e2m1_stores_row(E2m1Stores& w, uint32_t lane) {
+  const uint32_t r = w.row % NT;
+  w.blk = w.tiles + (static_cast<size_t>(w.row / NT) * w.k_steps + w.step) * mx_act_block_bytes(NT);
+  w.off = r * 128u + (((lane >> 2) ^ (r & 7u)) << 4) + (lane & 3u) * 4u;
+  const uint32_t p = lane & 3u;
+  w.sf = p < 3u ? mx_act_sf_offset(NT, p * NT + r, lane >> 2) : 0u;
+}
+
+template <uint32_t NT>
+__device__ __forceinline__ void e2m1_stores_at(E2m1Stores& w, const QuantJob& j, uint32_t row,
+                                               uint32_t step, uint32_t lane) {
+  w.tiles = j.tiles;
+  w.rows = j.rows;
+  w.k_steps = j.k_steps;
+  w.row = row;
+  w.step = step;
+  e2m1_stores_row<NT>(w, lane);
+}
+
+__device__ __forceinline__ void e2m1_loads_next(E2m1Loads& w, const QuantJob* jobs, uint32_t njobs,
+                                                uint32_t lane) {
+  w.col0 += 256u;
+  w.src += 256;
+  if (++w.step < w.k_steps) return;
+  uint32_t row = w.row + 1u;
+  if (row == w.rows && jobs != nullptr && w.jx + 1u < njobs) {
+    ++w.jx;
+    const QuantJob& j = jobs[w.jx];
+    w.x = j.x;
+    w.ldx = j.ldx;
+    w.cols = j.cols;
+    w.rows = j.rows;
+    w.k_steps = j.k_steps;
+    row = 0;
+  }
+  w.row = row;
+  w.step = 0;
+  w.col0 = lane * 8u;
+  w.src = w.x + static_cast<size_t>(row) * w.ldx + w.col0;
+}
+
+template <uint32_t NT>
+__device__ __forceinline__ void e2m1_stores_next(E2m1Stores& w, const QuantJob* jobs,
+                                                 uint32_t njobs, uint32_t lane) {
+  w.blk += mx_act_block_bytes(NT);
+  if (++w.step < w.k_steps) return;
+  uint32_t row = w.row + 1u;
+  if (row == w.rows && jobs != nullptr && w.jx + 1u < njobs) {
+    ++w.jx;
+    const QuantJob& j = jobs[w.jx];
+    w.tiles = j.tiles;
+    w.rows = j.rows;
+    w.k_steps = j.k_steps;
+    row = 0;
+  }
+  w.row = row;
+  w.step = 0;
+  if (row < w.rows) e2m1_stores_row<NT>(w, lane);
+}
+
+// The lane's eight elements of the current unit into its 32 bytes of a ring
+// slot (16-byte rows: cp.async, zero-filled past the row's end).
+__device__ __forceinline__ void e2m1_stage(const E2m1Loads& w, uint32_t dst) {
+  if (w.col0 + 8u <= w.cols) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n\t"
+                 "cp.async.cg.shared.global [%2], [%3], 16;" ::"r"(dst), "l"(w.src),
+                 "r"(dst + 16u), "l"(w.src + 4)
+                 : "memory");
+  } else {
+#pragma unroll
+    for (uint32_t h = 0; h < 2; ++h) {
+      const uint32_t col = w.col0 + 4u * h;
+      const uint32_t have = col < w.cols ? min(4u, w.cols - col) : 0u;
+      const float* from = have != 0 ? w.src + 4u * h : w.x;  // any valid address when empty
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst + 16u * h),
+                   "l"(from), "r"(4u * have)
+                   : "memory");
+    }
+  }
+}
+
+template <uint32_t NT, bool kVec>
+__device__ __forceinline__ void e2m1_encode(const E2m1Stores& w, uint32_t v[8], uint32_t lane,
+                                            uint32_t sadd, uint32_t& bad, const uint8_t* lut) {
+  constexpr float kM4 = 50331648.0f;  // 6 * 2^23
+  constexpr uint32_t kPlane = NT * 128u;
+  float m[4];
+#pragma unroll
+  for (uint32_t i = 0; i < 4; ++i) m[i] = max_nan_abs(v[2 * i], v[2 * i + 1]);
+  const uint32_t mb =
+      __float_as_uint(max_nan_abs(__float_as_uint(max_nan_abs(__float_as_uint(m[0]),
+                                                              __float_as_uint(m[1]))),
+                                  __float_as_uint(max_nan_abs(__float_as_uint(m[2]),
+                                                              __float_as_uint(m[3]))))) &
+      0x7FFFFFFFu;
+  // Host rule: the key is the largest magnitude (an Inf or NaN shows as a
+  // key >= 0x7F800000); VEC rule: its exponent field, subnormals reading as
+  // zero.
+  uint32_t key = kVec ? (mb >> 23) : mb;
+  key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 1));
+  key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 2));
+  if (!kVec) bad = max(bad, key);
+  const uint32_t field = kVec ? key : (key >> 23);
+  const uint32_t scale = key == 0 ? 127u : field;  // e = scale - 127
+  if (kVec) {
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) {
+      if ((v[i] & 0x7F800000u) == 0) v[i] = 0;
+    }
+  }
+  uint32_t b[8];  // (q & 0xFF) * 4
+  uint8_t* blk = w.blk;
+  if (scale - 8u < 247u) {
+    // 8 <= scale <= 254: 2^(8 - e) = 2^(135 - scale) is a normal FP32.
+    const float sc = __uint_as_float((262u - scale) << 23);
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) {
+      // q >= -128 always; 128 clamps to 127.
+      b[i] = __float_as_uint(fminf(__fmaf_rn(__uint_as_float(v[i]), sc, kM4), kM4 + 508.0f)) &
+             0x3FCu;
+    }
+    if ((lane & 3u) < 3u) blk[w.sf] = static_cast<uint8_t>(scale + sadd);
+  } else {
+    // The planes' scales 2^(e - 6 + 3p) start below E8M0's 2^-127 when
+    // scale < 6: such a block is encoded as zero.
+    const int32_t e = static_cast<int32_t>(scale) - 127;
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) {
+      const int32_t q = scale < 6u ? 0
+                        : kVec     ? quantize_vec_rule(v[i], key)
+                                   : quantize_host_rule(v[i], e);
+      b[i] = (static_cast<uint32_t>(q) & 0xFFu) << 2;
+    }
+    if ((lane & 3u) < 3u) {
+      int32_t se = static_cast<int32_t>(scale + sadd);
+      se = se > 254 ? 254 : se;
+      blk[w.sf] = static_cast<uint8_t>(se < 0 ? 0 : se);
+    }
+  }
+  uint32_t pair[4];
+#pragma unroll
+  for (uint32_t k = 0; k < 4; ++k) {
+    pair[k] = *reinterpret_cast<const uint32_t*>(lut + b[2 * k]) |
+              *reinterpret_cast<const uint32_t*>(lut + 1024u + b[2 * k + 1]);
+  }
+  const uint32_t a01 = __byte_perm(pair[0], pair[1], 0x5140u);  // p0: 0,4  p1: 1,5
+  const uint32_t a23 = __byte_perm(pair[2], pair[3], 0x5140u);
+  const uint32_t b01 = __byte_perm(pair[0], pair[1], 0x0062u);  // p2: 2,6
+  const uint32_t b23 = __byte_perm(pair[2], pair[3], 0x0062u);
+  uint8_t* out = blk + w.off;
+  *reinterpret_cast<uint32_t*>(out) = __byte_perm(a01, a23, 0x5410u);
+  *reinterpret_cast<uint32_t*>(out + kPlane) = __byte_perm(a01, a23, 0x7632u);
+  *reinterpret_cast<uint32_t*>(out + 2u * kPlane) = __byte_perm(b01, b23, 0x5410u);
+}
+
+template <uint32_t NT, bool kVec>
+__global__ void __launch_bounds__(kPlaneWarps * 32)
+k_quantize_planes_e2m1(const QuantJob* jobs, uint32_t njobs,
+                       const __grid_constant__ QuantJob inline_job, uint32_t* error_flag) {
+  __shared__ __align__(16) uint32_t ring[kPlaneWarps][kPlaneDepth][256];
+  // Byte offset 4 (q & 0xFF): the E2M1 codes of q's digits d0, d1, d2 (q =
+  // 64 d2 + 8 d1 + d0, d2 = RNE(q / 64), d1 = RNE((q - 64 d2) / 8)) in the
+  // low nibbles of bytes 0, 1, 2; from byte 1024 on, the same in the high
+  // nibbles.
+  __shared__ __align__(16) uint32_t lut[512];
+  {
+    constexpr float kMagic = 12582912.0f;
+    const float q = static_cast<float>(static_cast<int8_t>(threadIdx.x & 0xFFu));
+    const float d2 = __fadd_rn(__fmaf_rn(q, 0.015625f, kMagic), -kMagic);
+    const float r = __fmaf_rn(d2, -64.0f, q);
+    const float d1 = __fadd_rn(__fmaf_rn(r, 0.125f, kMagic), -kMagic);
+    const float d0 = __fmaf_rn(d1, -8.0f, r);
+    const float d[8] = {d0, d1, d2, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    const uint32_t packed = pack_e2m1x8(d);  // nibble i = digit i's code
+    const uint32_t codes =
+        (packed & 0xFu) | ((packed >> 4) & 0xFu) << 8 | ((packed >> 8) & 0xFu) << 16;
+    if (threadIdx.x < 256u) {
+      lut[threadIdx.x] = codes;
+      lut[256u + threadIdx.x] = codes << 4;
+    }
+  }
+  __syncthreads();
+  // The tables overlap the kernel before; the activations it may have
+  // written, and the operand blocks it may still read, come after.
+  sm100::griddep_launch_dependents();
+  sm100::griddep_wait();
+  const uint32_t lane = threadIdx.x & 31u, wib = threadIdx.x >> 5;
+  const uint32_t warp = blockIdx.x * kPlaneWarps + wib;
+  const uint32_t nwarps = gridDim.x * kPlaneWarps;
+  const uint64_t base = jobs != nullptr ? jobs[0].unit_begin : 0;
+  const uint64_t total = jobs != nullptr
+                             ? jobs[njobs - 1].unit_begin + jobs[njobs - 1].units - base
+                             : inline_job.units;
+  const uint64_t per = (total + nwarps - 1) / nwarps;
+  const uint64_t begin = base + static_cast<uint64_t>(warp) * per;
+  const uint64_t end = begin + per < base + total ? begin + per : base + total;
+  if (begin >= end) return;
+  const uint32_t count = static_cast<uint32_t>(end - begin);
+  uint32_t jx = 0;
+  if (jobs != nullptr) {
+    uint32_t lo = 0, hi = njobs - 1;
+    while (lo < hi) {
+      const uint32_t mid = (lo + hi + 1) >> 1;
+      if (jobs[mid].unit_begin <= begin) lo = mid; else hi = mid - 1;
+    }
+    jx = lo;
+  }
+  const QuantJob& j0 = jobs != nullptr ? jobs[jx] : inline_job;
+  const uint32_t u = static_cast<uint32_t>(begin - j0.unit_begin);
+  E2m1Loads ld;
+  E2m1Stores st;
+  ld.jx = st.jx = jx;
+  e2m1_loads_at(ld, j0, u / j0.k_steps, u % j0.k_steps, lane);
+  e2m1_stores_at<NT>(st, j0, u / j0.k_steps, u % j0.k_steps, lane);
+  const uint32_t sadd = 3u * (lane & 3u) - 6u;  // plane p's scale: scale - 6 + 3p
+  const uint8_t* lutb = reinterpret_cast<const uint8_t*>(lut);
+  uint32_t bad = 0;
+  const uint32_t mine = static_cast<uint32_t>(__cvta_generic_to_shared(&ring[wib][0][lane * 8u]));
+  // One commit group per unit slot, empty past the range, so that
+  // wait_group(kPlaneDepth - 1) always means "the oldest has landed".
+#pragma unroll
+  for (uint32_t d = 0; d < kPlaneDepth; ++d) {
+    if (d < count) {
+      e2m1_stage(ld, mine + d * 1024u);
+      e2m1_loads_next(ld, jobs, njobs, lane);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  for (uint32_t i0 = 0; i0 < count; i0 += kPlaneDepth) {
+#pragma unroll
+    for (uint32_t d = 0; d < kPlaneDepth; ++d) {
+      const uint32_t i = i0 + d;
+      if (i < count) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(kPlaneDepth - 1) : "memory");
+        const uint32_t* slot = &ring[wib][d][lane * 8u];
+        const uint4 lo = *reinterpret_cast<const uint4*>(slot);
+        const uint4 hi = *reinterpret_cast<const uint4*>(slot + 4);
+        uint32_t v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        e2m1_encode<NT, kVec>(st, v, lane, sadd, bad, lutb);
+        e2m1_stores_next<NT>(st, jobs, njobs, lane);
+        if (i + kPlaneDepth < count) {
+          e2m1_stage(ld, mine + d * 1024u);
+          e2m1_loads_next(ld, jobs, njobs, lane);
+        }
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+  }
+  if (!kVec && __any_sync(0xFFFFFFFFu, bad >= 0x7F800000u) && lane == 0) atomicOr(error_flag, 1u);
+}
+
 }  // namespace
 
 void launch_quantize(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* inline_job,
@@ -611,25 +914,55 @@ void launch_quantize(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* i
   k_quantize<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(jobs_dev, njobs, one, error_flag);
 }
 
+namespace {
+
+// Which plane encoder serves a launch: 0 the general k_quantize_planes; else
+// the specialised E2M1 kernel, 1 + 2 (tiles of 128 rows) + 1 (VEC rule), when
+// every job holds E2M1 planes of 16-byte-aligned rows with one tile height
+// and one rule.
+uint32_t planes_variant(const QuantJob* jobs, uint32_t n) {
+  if (jobs == nullptr || n == 0) return 0;
+  const QuantJob& f = jobs[0];
+  if (f.tile_rows != 64u && f.tile_rows != 128u) return 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    const QuantJob& j = jobs[i];
+    if (j.tiles_kind != 2u || !j.vec4 || j.tile_rows != f.tile_rows || j.vec_rule != f.vec_rule) {
+      return 0;
+    }
+  }
+  return 1u + (f.tile_rows == 128u ? 2u : 0u) + (f.vec_rule ? 1u : 0u);
+}
+
+template <typename K>
+int occupancy_of(K kernel) {
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kPlaneWarps * 32, 0) !=
+          cudaSuccess || n < 1) {
+    n = 1;
+  }
+  return n;
+}
+
+}  // namespace
+
 void launch_quantize_planes(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* inline_job,
                             uint64_t total_units, uint32_t* error_flag, int sm_count,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, const QuantJob* jobs_host) {
+  const uint32_t variant =
+      inline_job != nullptr ? planes_variant(inline_job, 1) : planes_variant(jobs_host, njobs);
+  using Fn = void (*)(const QuantJob*, uint32_t, const QuantJob, uint32_t*);
+  static const Fn kFns[5] = {k_quantize_planes, k_quantize_planes_e2m1<64, false>,
+                             k_quantize_planes_e2m1<64, true>, k_quantize_planes_e2m1<128, false>,
+                             k_quantize_planes_e2m1<128, true>};
   // As many CTAs as fit at once (no second wave); each warp takes a
   // contiguous range of at least a few units.
-  static int per_sm = 0;
-  if (per_sm == 0) {
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_quantize_planes, kPlaneWarps * 32, 0) !=
-            cudaSuccess || n < 1) {
-      n = 1;
-    }
-    per_sm = n;
-  }
+  static int per_sm[5] = {0, 0, 0, 0, 0};
+  if (per_sm[variant] == 0) per_sm[variant] = occupancy_of(kFns[variant]);
   // Four units a warp or more when that fills the GPU; a smaller job (a few
   // hundred rows) spreads down to one unit a warp, so a warp waits for one
   // load, not four in a row.
   uint64_t blocks = (total_units + 4 * kPlaneWarps - 1) / (4 * kPlaneWarps);
-  const uint64_t cap = static_cast<uint64_t>(sm_count) * per_sm;
+  const uint64_t cap = static_cast<uint64_t>(sm_count) * per_sm[variant];
   if (blocks < cap) {
     blocks = std::min<uint64_t>(cap, (total_units + kPlaneWarps - 1) / kPlaneWarps);
   }
@@ -648,7 +981,7 @@ void launch_quantize_planes(const QuantJob* jobs_dev, uint32_t njobs, const Quan
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, k_quantize_planes, jobs_dev, njobs, one, error_flag);
+  cudaLaunchKernelEx(&cfg, kFns[variant], jobs_dev, njobs, one, error_flag);
 }
 
 }  // namespace hrb

@@ -262,6 +262,51 @@ def test_fast_activation_planes_are_exact(hrb, wfmt, w8_kernel, quant, m):
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+@pytest.mark.parametrize("quant", [0, 1])
+@pytest.mark.parametrize("m,lda", [(70, 544), (64, 544), (130, 545)])
+def test_fast_e2m1_planes_at_scale_boundaries(hrb, quant, m, lda):
+    """W = I with MXFP4 weights as above, activation blocks whose largest
+    magnitude has exponent field 5 .. 9 or 253: the E2M1 plane encoder's
+    scaled rounding holds from field 8 on, fields 6 and 7 take the integer
+    rules, fields below 6 encode as zero.  (At field 254 the top digit
+    plane's partial product, up to 2 * 2^127, would overflow FP32 in the
+    tensor cores whatever the encoder does.)  Rows of lda = 545 floats are not
+    16-byte aligned and run the general encoder instead of the specialised
+    one; both must give the oracle's MXINT8 codes."""
+    from hotarubi_b200 import capi
+    rng = np.random.default_rng(300 + m + quant + lda)
+    n = k = 544
+    kb = k // 32
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    fields = np.array([5, 6, 7, 8, 9, 253, 127, 100])
+    f = fields[rng.integers(0, fields.size, (m, kb))]
+    # Each block scaled so that its largest magnitude is 1.5 * 2^(f - 127).
+    blocks = x.reshape(m, kb, 32).astype(np.float64)
+    top = np.abs(blocks).max(axis=2, keepdims=True)
+    blocks = blocks / top * 1.5 * np.ldexp(1.0, (f - 127)[..., None].astype(np.int64))
+    x = blocks.reshape(m, k).astype(np.float32)
+    xs = np.zeros((m, lda), np.float32)
+    xs[:, :k] = x
+    codes = np.zeros((n, k), np.uint8)
+    codes[np.arange(n), np.arange(n)] = 2
+    w = cpu.pack_nibbles(codes)
+    ws = np.full((n, kb), 127, np.uint8)
+    c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    keep = [dev(xs), dev(w), dev(ws)]
+    d = capi.Library.desc(0, m, n, k, a=keep[0], lda=lda, w=keep[1], wscale=keep[2], c=c,
+                          mode=capi.MODE_FAST, quant=quant)
+    hrb.dense(d)
+    hrb.sync()
+    got = c.cpu().numpy()
+    xb = x.view(np.uint32)
+    q, s = cpu.quantize_vec(xb) if quant == 1 else cpu.encode_mxint8(xb)
+    assert set(np.unique(s)) >= {5, 6, 7, 8, 9, 253}
+    want = q.astype(np.float64) * np.repeat(np.ldexp(1.0, s.astype(np.int64) - 133), 32, axis=1)
+    want[np.repeat(s < 6, 32, axis=1)] = 0.0
+    want = want[:, :n].astype(np.float32)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 @pytest.mark.parametrize("wfmt,w8_kernel", [(0, 0), (1, 0), (1, 1), (2, 0)])
 @pytest.mark.parametrize("m", [288, 64])
 def test_fast_weight_operands_are_exact(hrb, wfmt, w8_kernel, m):
