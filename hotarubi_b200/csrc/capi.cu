@@ -1363,7 +1363,7 @@ hrb_status plan_launch(hrb_plan* plan, cudaStream_t s, int64_t only, uint32_t* l
           static_cast<const hrb::DenseJob*>(g.d_jobs), g.njobs, nullptr, g.tiles, g.wfmt, s));
     } else {
       const int k = hrb::launch_mxf4(g.d_tiles, nullptr, g.nt, g.wfmt, g.tiles, ctx->sm_count,
-                                     ctx->d_error, s, &plan->peers);
+                                     ctx->d_error, s, &plan->peers, true);
       if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
       n += static_cast<uint32_t>(k);
     }
@@ -1497,7 +1497,7 @@ hrb_status hrb_plan_run_host(hrb_plan* plan, void* stream, const void* const* a_
     const uint32_t t0 = plan->io[g0].tile_begin;
     const uint32_t t1 = plan->io[g1 - 1].tile_begin + plan->io[g1 - 1].tiles;
     const int k = hrb::launch_mxf4(g.d_tiles + t0, nullptr, g.nt, g.wfmt, t1 - t0,
-                                   ctx->sm_count, ctx->d_error, s, &plan->peers);
+                                   ctx->sm_count, ctx->d_error, s, &plan->peers, true);
     if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
     ctx->launches += 1u + static_cast<uint64_t>(k);
     HRB_CUDA(ctx, cudaEventRecord(ev[kChunks + c], s));

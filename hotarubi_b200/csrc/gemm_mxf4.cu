@@ -120,6 +120,10 @@ struct MxParams {
   MxPeers peers;        // outputs also stored at these byte offsets (peer GPUs)
   TcJob inline_job;
   MxGather gather;      // the gathering variant's source (convolutions)
+  // The weight chunks were written and synchronised before this launch's
+  // stream work began (plans translate them at creation): the weight stream
+  // may start before griddep_wait, overlapping the kernel before.
+  uint32_t weights_ready;
 };
 
 __host__ __device__ inline uint32_t mx_planes_of(uint32_t wfmt) {
@@ -534,8 +538,12 @@ __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
   bool ok = true;
   // Launch setup, barriers and TMEM overlap the kernel before; its outputs
   // (this kernel's activations) and its reads of C come before any access.
+  // With ready weights the weight producer waits later (combined rings:
+  // after issuing the weight halves of its first stages) or not at all
+  // (split rings: it reads nothing else).
   griddep_launch_dependents();
-  griddep_wait();
+  const bool early_weights = !kGather && p.weights_ready != 0 && warp == 0;
+  if (!early_weights) griddep_wait();
 
   if (kGather && warp >= 2 && warp < 2 + kGatherWarps) {
     // Gathering lanes: the activation half of every ring slot, in the weight
@@ -570,12 +578,26 @@ __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
         if (tile + gridDim.x < p.total_tiles) next = tile_info<NT>(p, tile + gridDim.x);
         const uint32_t k_steps = (ti.flags & 0x0FFFFFFFu);
         if (weights) {
+          // Stages of the first tile whose weight half went out before the
+          // dependency wait (combined rings with ready weights).
+          uint32_t pre = 0;
+          if (early_weights && !Cfg::kSplit && n == 0) {
+            pre = k_steps * WP < ring.slots ? k_steps * WP : ring.slots;
+            for (uint32_t c = 0; c < pre; ++c) {
+              mbar_arrive_expect_tx(&ring.full[c], Cfg::kWSlot);
+              bulk_g2s(wbase + c * Cfg::kWSlot, ti.w + static_cast<size_t>(c) * kWChunk, kWChunk,
+                       &ring.full[c]);
+            }
+            griddep_wait();
+          }
           for (uint32_t c = 0; c < k_steps * WP && ok; ++c, ++n) {
             const uint32_t sl = n % ring.slots;
-            ok = ring_acquire(ring, n, kGather ? kWChunk : Cfg::kWSlot, p.err);
-            if (!ok) break;
-            bulk_g2s(wbase + sl * Cfg::kWSlot, ti.w + static_cast<size_t>(c) * kWChunk, kWChunk,
-                     &ring.full[sl]);
+            if (c >= pre) {
+              ok = ring_acquire(ring, n, kGather ? kWChunk : Cfg::kWSlot, p.err);
+              if (!ok) break;
+              bulk_g2s(wbase + sl * Cfg::kWSlot, ti.w + static_cast<size_t>(c) * kWChunk, kWChunk,
+                       &ring.full[sl]);
+            }
             if (!Cfg::kSplit && !kGather) {
               bulk_g2s(wbase + sl * Cfg::kWSlot + kWChunk,
                        ti.a + static_cast<size_t>(c) * Cfg::kABlock, Cfg::kABlock,
@@ -1160,9 +1182,10 @@ __global__ void k_tile_weights_mxf4(const uint8_t* __restrict__ w, const uint8_t
 template <uint32_t NT, uint32_t WP, uint32_t KB>
 int launch_mx(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, int sm_count,
               uint32_t* err, cudaStream_t s, const MxPeers* peers,
-              const MxGather* gather = nullptr) {
+              const MxGather* gather = nullptr, bool weights_ready = false) {
   using Cfg = MxCfg<NT, WP, KB>;
   MxParams p{};
+  p.weights_ready = weights_ready ? 1u : 0u;
   p.tiles = tiles_dev;
   p.total_tiles = tiles;
   p.err = err;
@@ -1266,14 +1289,14 @@ int launch_mxf4_gather(const TcJob& inline_job, uint32_t nt, uint32_t tiles, int
 
 int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t wfmt,
                 uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t s,
-                const MxPeers* peers) {
+                const MxPeers* peers, bool weights_ready) {
   if (tiles == 0) return 0;
   if (tiles_dev == nullptr && inline_job == nullptr) return -1;
   if (peers != nullptr && peers->count > kMaxPeers) return -1;
   const auto go = [&](auto cfg) {
     using C = decltype(cfg);
     return launch_mx<C::kNt, C::kWp, C::kKb>(tiles_dev, inline_job, tiles, sm_count, err, s,
-                                             peers);
+                                             peers, nullptr, weights_ready);
   };
   switch (wfmt * 1000u + nt) {
     case HRB_WFMT_MXFP4 * 1000u + 64: return go(Pick<64, 1, 4>{});

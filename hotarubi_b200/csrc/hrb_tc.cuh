@@ -148,9 +148,11 @@ int launch_mxf4_gather(const TcJob& inline_job, uint32_t nt, uint32_t tiles, int
 
 // One launch over `tiles` output tiles: the device array tiles_dev, or, when
 // it is null, the tiles of the single *inline_job.  `peers` may be null.
+// weights_ready: the weight chunks were written and the stream synchronised
+// before (a plan's), so the kernel may read them before its dependency wait.
 int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t wfmt,
                 uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t stream,
-                const MxPeers* peers = nullptr);
+                const MxPeers* peers = nullptr, bool weights_ready = false);
 
 // Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current
 // device, once per (kernel, device).
