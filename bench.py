@@ -1295,9 +1295,10 @@ def run_shard(args, wl: Workload, rank: int, world: int, local_rank: int) -> Non
     lib = capi.Library(local_rank)
     stream = torch.cuda.Stream()
     lib.set_stream(stream.cuda_stream)
+    group = shard.Group(lib)   # the library's communicator (NCCL through the C ABI)
     batch = args.batch or wl.batch
     n0, n1 = shard.columns(wl.N)
-    out = shard.PeerOutput(lib, (batch, wl.M, wl.N))
+    out = shard.PeerOutput(lib, group, (batch, wl.M, wl.N))
     sets = [host_operands(wl, i) for i in range(min(4, batch))]
     keep, descs = [], []
     a_all = torch.empty((batch, wl.M, wl.K), dtype=torch.float32, device="cuda")
@@ -1316,13 +1317,11 @@ def run_shard(args, wl: Workload, rank: int, world: int, local_rank: int) -> Non
     if plan is not None:
         plan.set_peers(out.ptr, out.peer_bases)
     torch.cuda.synchronize()
-    flag = torch.zeros(1, device="cuda")
 
     def step():
         if plan is not None:
             plan.run(stream.cuda_stream)
-        with torch.cuda.stream(stream):
-            dist.all_reduce(flag)  # the step ends when every rank's stores are done
+        group.fence(stream.cuda_stream)  # the step ends when every rank's stores are done
 
     dist.barrier()
     with ClockSampler(local_rank) as clocks:
@@ -1369,6 +1368,93 @@ def run_shard(args, wl: Workload, rank: int, world: int, local_rank: int) -> Non
     torch.cuda.synchronize()
     dist.barrier()
     out.close()
+    group.close()
+    lib.close()
+    dist.destroy_process_group()
+
+
+def run_conv_shard(args, rank: int, world: int, local_rank: int) -> None:
+    """--config c5conv --shard: the C5 conv's 48 images split over the ranks
+    (shard.rows; strong scaling, the total work is fixed).  Each rank's conv
+    plan covers its images and its epilogue stores every output row into all
+    ranks' C over NVLink (the all-gather along M fused into the kernel,
+    ConvPlan.set_peers); a step ends when every rank holds all 33,792 rows
+    (Group.fence)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from hotarubi_b200 import capi, shard
+    cw = CONV
+    torch.cuda.set_device(local_rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local_rank))
+    lib = capi.Library(local_rank)
+    stream = torch.cuda.Stream()
+    lib.set_stream(stream.cuda_stream)
+    group = shard.Group(lib)
+    per = (cw.H // cw.stride) * (cw.W // cw.stride)
+    i0, i1 = shard.rows(cw.images)
+    x, w, ws, b = conv_operands(cw, 0)
+    hw = cw.H * cw.W
+    out = shard.PeerOutput(lib, group, (cw.M, cw.cout))
+    t = {"x": torch.from_numpy(x[i0 * hw:i1 * hw].copy()).cuda(), "w": torch.from_numpy(w).cuda(),
+         "ws": torch.from_numpy(ws).cuda(), "b": torch.from_numpy(b).cuda()}
+    plan = None
+    if i1 > i0:
+        d = capi.conv_desc(cw.wfmt, i1 - i0, cw.H, cw.W, cw.cin, cw.cout, cw.kh, cw.stride,
+                           order=capi.CONV_YMAJOR, a=t["x"], w=t["w"], wscale=t["ws"],
+                           bias=t["b"], c=out.tensor[i0 * per:i1 * per], mode=capi.MODE_FAST)
+        plan = lib.conv_plan(d)
+        plan.set_peers(out.ptr, out.peer_bases)
+    torch.cuda.synchronize()
+
+    def step():
+        n = plan.run(stream.cuda_stream) if plan is not None else 0
+        group.fence(stream.cuda_stream)
+        return n
+
+    dist.barrier()
+    with ClockSampler(local_rank) as clocks:
+        for _ in range(args.warmup):
+            step()
+        stream.synchronize()
+        dist.barrier()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        launches = 0
+        for _ in range(args.steps):
+            launches += step()
+        end.record(stream)
+        end.synchronize()
+        dist.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    tm = torch.tensor([ms], device="cuda")
+    dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+    ms = float(tm.item())
+    if rank == 0:
+        nvlink = (world - 1) * cw.M * cw.cout * 4 / world   # bytes each rank stores to peers
+        print(json.dumps({
+            "metric": cw.metric, "value": cw.flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8 block dot + fp32 accumulate", "data": "synthetic",
+            "config": {"workload": cw.name, "M": cw.M, "N": cw.cout, "K": cw.K,
+                       "images": cw.images, "format": "mxfp4", "bias": True, "mode": "fast",
+                       "parallelism": f"M-sharded (images) x{world}, all-gather along M fused "
+                                      "into the GEMM epilogue (NVLink peer stores)"},
+            "nvlink": {"bytes_per_rank_per_step": nvlink,
+                       "gbs_per_rank": nvlink / (ms / 1e3) / 1e9},
+            "gpu_launches": launches, "e2e": None, "clocks": clocks.summary()}), flush=True)
+    dist.barrier()
+    if plan is not None:
+        plan.close()
+    torch.cuda.synchronize()
+    dist.barrier()
+    out.close()
+    group.close()
     lib.close()
     dist.destroy_process_group()
 
@@ -1390,14 +1476,18 @@ def main() -> None:
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the host entry-point leg "
                    "(profiling runs)")
-    p.add_argument("--shard", action="store_true", help="split each GEMM along N over the "
-                   "ranks, with the all-gather fused into the kernel (strong scaling)")
+    p.add_argument("--shard", action="store_true", help="split each GEMM along N (c5conv: the "
+                   "images along M) over the ranks, with the all-gather fused into the kernel "
+                   "(strong scaling)")
     args = p.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.config == CONV.key:
-        run_conv(args, rank, world, local_rank)
+        if args.shard and args.impl != "reference":
+            run_conv_shard(args, rank, world, local_rank)
+        else:
+            run_conv(args, rank, world, local_rank)
         return
     if args.config == GACC.key:
         run_gacc(args, rank, world, local_rank)

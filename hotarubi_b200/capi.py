@@ -44,6 +44,11 @@ class IpcHandle(ctypes.Structure):
     _fields_ = [("bytes", ctypes.c_uint8 * 64)]
 
 
+class CommId(ctypes.Structure):
+    """hrb_comm_id: the 128-byte bootstrap id of a communicator."""
+    _fields_ = [("bytes", ctypes.c_uint8 * 128)]
+
+
 class GemmDesc(ctypes.Structure):
     """hrb_gemm_desc."""
     _fields_ = [
@@ -157,6 +162,16 @@ def load() -> ctypes.CDLL:
             "hrb_peer_close": (ctypes.c_int, [P, P]),
             "hrb_shard_columns": (None, [u32, u32, u32, ctypes.POINTER(u32), ctypes.POINTER(u32)]),
             "hrb_plan_set_peers": (ctypes.c_int, [P, P, ctypes.POINTER(P), u32]),
+            "hrb_conv_plan_set_peers": (ctypes.c_int, [P, P, ctypes.POINTER(P), u32]),
+            "hrb_comm_id_new": (ctypes.c_int, [ctypes.POINTER(CommId)]),
+            "hrb_comm_create": (ctypes.c_int, [P, ctypes.POINTER(CommId), u32, u32,
+                                               ctypes.POINTER(P)]),
+            "hrb_comm_destroy": (ctypes.c_int, [P]),
+            "hrb_comm_exchange": (ctypes.c_int, [P, P, P, ctypes.c_size_t]),
+            "hrb_comm_barrier": (ctypes.c_int, [P]),
+            "hrb_comm_fence": (ctypes.c_int, [P, P]),
+            "hrb_comm_allgather": (ctypes.c_int, [P, P, ctypes.POINTER(ctypes.c_uint64), P]),
+            "hrb_shard_rows": (None, [u32, u32, u32, ctypes.POINTER(u32), ctypes.POINTER(u32)]),
         }
         for name, (res, args) in sigs.items():
             f = getattr(lib, name, None)
@@ -184,6 +199,64 @@ def shard_columns(n: int, rank: int, ranks: int) -> tuple[int, int]:
     n0, n1 = ctypes.c_uint32(), ctypes.c_uint32()
     load().hrb_shard_columns(n, rank, ranks, ctypes.byref(n0), ctypes.byref(n1))
     return n0.value, n1.value
+
+
+def shard_rows(units: int, rank: int, ranks: int) -> tuple[int, int]:
+    """hrb_shard_rows: units (e.g. images) [u0, u1) of `rank` of `ranks`."""
+    u0, u1 = ctypes.c_uint32(), ctypes.c_uint32()
+    load().hrb_shard_rows(units, rank, ranks, ctypes.byref(u0), ctypes.byref(u1))
+    return u0.value, u1.value
+
+
+def comm_id_new() -> bytes:
+    """hrb_comm_id_new: a fresh bootstrap id (rank 0 makes it)."""
+    cid = CommId()
+    st = load().hrb_comm_id_new(ctypes.byref(cid))
+    if st != HRB_OK:
+        raise HrbError(st, (load().hrb_last_error(None) or b"").decode())
+    return bytes(cid.bytes)
+
+
+class Comm:
+    """An hrb_comm over a context: NCCL among the ranks of one node."""
+
+    def __init__(self, owner: "Library", comm_id: bytes, rank: int, ranks: int):
+        self.owner = owner
+        self.rank, self.ranks = rank, ranks
+        cid = CommId.from_buffer_copy(comm_id)
+        h = ctypes.c_void_p()
+        owner._check(owner.lib.hrb_comm_create(owner.ctx, ctypes.byref(cid), rank, ranks,
+                                               ctypes.byref(h)))
+        self.h = h
+
+    def exchange(self, mine: bytes) -> list[bytes]:
+        """Every rank's record (all the same length), in rank order."""
+        n = len(mine)
+        src = ctypes.create_string_buffer(mine, n)
+        dst = ctypes.create_string_buffer(n * self.ranks)
+        self.owner._check(self.owner.lib.hrb_comm_exchange(self.h, src, dst, n))
+        raw = dst.raw
+        return [raw[i * n:(i + 1) * n] for i in range(self.ranks)]
+
+    def barrier(self) -> None:
+        self.owner._check(self.owner.lib.hrb_comm_barrier(self.h))
+
+    def fence(self, stream: int = 0) -> None:
+        """hrb_comm_fence: later work on `stream` waits for every rank's
+        earlier work on its stream."""
+        self.owner._check(self.owner.lib.hrb_comm_fence(self.h, stream or None))
+
+    def allgather(self, buf, offsets: list[int], stream: int = 0) -> None:
+        """In place: rank r's bytes [offsets[r], offsets[r + 1]) of `buf`
+        to every rank."""
+        arr = (ctypes.c_uint64 * len(offsets))(*offsets)
+        self.owner._check(self.owner.lib.hrb_comm_allgather(self.h, _ptr(buf), arr,
+                                                            stream or None))
+
+    def close(self) -> None:
+        if self.h:
+            self.owner.lib.hrb_comm_destroy(self.h)
+            self.h = None
 
 
 def gemm_check(cmd: GemmCmd) -> tuple[int, str]:
@@ -413,6 +486,13 @@ class ConvPlan:
         self.owner._check(self.owner.lib.hrb_conv_plan_profile(self.handle, stream or None, reps,
                                                                ms, 8, ctypes.byref(n)))
         return [ms[i] for i in range(n.value)]
+
+    def set_peers(self, local_base: int, peer_bases: list[int]) -> None:
+        """hrb_conv_plan_set_peers: every output byte also goes to each peer
+        base + (its address - local_base)."""
+        arr = (ctypes.c_void_p * max(1, len(peer_bases)))(*peer_bases)
+        self.owner._check(self.owner.lib.hrb_conv_plan_set_peers(self.handle, local_base, arr,
+                                                                 len(peer_bases)))
 
     def close(self) -> None:
         if self.handle:

@@ -47,6 +47,8 @@ struct hrb_conv_plan {
   hrb_ctx* ctx = nullptr;
   hrb_conv_desc desc{};
   void* d_scratch = nullptr;
+  // Peers that receive every output (hrb_conv_plan_set_peers).
+  hrb::MxPeers peers{};
 };
 
 struct hrb_plan {
@@ -570,7 +572,8 @@ hrb_status conv_prepare(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, 
 // The convolution proper, once prepared.  With `only` >= 0 just that launch
 // of the sequence (a profiling aid, as hrb_plan_profile's).
 hrb_status conv_execute(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, uint8_t* base,
-                        cudaStream_t s, uint32_t* launched, int only = -1) {
+                        cudaStream_t s, uint32_t* launched, int only = -1,
+                        const hrb::MxPeers* peers = nullptr) {
   const hrb_gemm_desc g = conv_gemm(d, r, base);
   int index = 0;
   auto take = [&]() { return only < 0 || index++ == only; };
@@ -599,7 +602,7 @@ hrb_status conv_execute(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, 
         tj.w_tiles = base + r.o_tc;
         tj.a_tiles = mg.map_tiles;  // not read: the kernel gathers
         const int n = hrb::launch_mxf4_gather(tj, qj.tile_rows, tj.m_tiles * tj.n_tiles,
-                                              ctx->sm_count, ctx->d_error, s, mg);
+                                              ctx->sm_count, ctx->d_error, s, mg, peers);
         if (n < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
         *launched += static_cast<uint32_t>(n);
       }
@@ -614,7 +617,7 @@ hrb_status conv_execute(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, 
     if (take()) {
       tj.tile_begin = 0;
       const int n = hrb::launch_mxf4(nullptr, &tj, qj.tile_rows, d->wfmt, tj.m_tiles * tj.n_tiles,
-                                     ctx->sm_count, ctx->d_error, s);
+                                     ctx->sm_count, ctx->d_error, s, peers);
       if (n < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
       *launched += static_cast<uint32_t>(n);
     }
@@ -712,6 +715,12 @@ QuantJob make_quant_job_for_noalloc(const hrb_gemm_desc* d, int8_t* q, uint8_t* 
 }
 
 QuantJob make_post_quant_job_for_noalloc(const hrb_gemm_desc* d) { return post_quant_job(d); }
+
+int ctx_device(const hrb_ctx* ctx) { return ctx->device; }
+
+hrb_status ctx_fail(hrb_ctx* ctx, hrb_status status, const char* message) {
+  return fail(ctx, status, "%s", message);
+}
 
 hrb_status noalloc_fail(hrb_status status, const char* message) {
   return fail(nullptr, status, "%s", message);
@@ -1801,10 +1810,34 @@ hrb_status hrb_conv_plan_run(hrb_conv_plan* plan, void* stream, uint32_t* launch
   HRB_CUDA(ctx, cudaSetDevice(ctx->device));
   uint32_t n = 0;
   st = conv_execute(ctx, &plan->desc, r, static_cast<uint8_t*>(plan->d_scratch),
-                    pick(ctx, stream), &n);
+                    pick(ctx, stream), &n, -1, &plan->peers);
   ctx->launches += n;
   if (launched != nullptr) *launched = n;
   return st;
+}
+
+hrb_status hrb_conv_plan_set_peers(hrb_conv_plan* plan, const void* local_base,
+                                   void* const* peer_bases, uint32_t npeers) {
+  if (plan == nullptr) return HRB_EINVAL;
+  hrb_ctx* ctx = plan->ctx;
+  if (npeers > hrb::kMaxPeers || (npeers > 0 && (local_base == nullptr || peer_bases == nullptr))) {
+    return fail(ctx, HRB_EINVAL, "at most %u peers, with a local base", hrb::kMaxPeers);
+  }
+  ConvRun r;
+  const hrb_status st = check_conv(ctx, &plan->desc, &r);
+  if (st != HRB_OK) return st;
+  if (npeers > 0 && !r.tc) {
+    return fail(ctx, HRB_ENOTSUP, "peer outputs need the tensor-core convolution");
+  }
+  hrb::MxPeers peers{};
+  peers.count = npeers;
+  for (uint32_t i = 0; i < npeers; ++i) {
+    if (peer_bases[i] == nullptr) return fail(ctx, HRB_EINVAL, "null peer base");
+    peers.delta[i] = static_cast<const char*>(peer_bases[i]) - static_cast<const char*>(local_base);
+  }
+  HRB_CUDA(ctx, cudaStreamSynchronize(ctx->stream));  // no run in flight sees half a change
+  plan->peers = peers;
+  return HRB_OK;
 }
 
 hrb_status hrb_conv_plan_profile(hrb_conv_plan* plan, void* stream, uint32_t reps, float* ms,

@@ -303,9 +303,11 @@ __device__ __forceinline__ void gather_block(const MxGather& g, uint8_t* blk, ui
 // columns, one per lane; columns past N count as zero): the block's key is a
 // warp max, each lane encodes its element (QuantizeBlock / EncodeMxint8 rules,
 // hrb_quant.cuh).  Non-finite values under the host rule set error bit 1.
+// With peers, each byte also goes to every peer's copy (the fused
+// all-gather of a sharded layer's MXINT8 output).
 __device__ __forceinline__ void requant_rows(const MxTile& ti, const float (&x)[16], uint32_t j0,
                                              uint32_t sp, uint32_t lane, bool col_ok,
-                                             uint32_t kbq, uint32_t* err) {
+                                             uint32_t kbq, uint32_t* err, const MxPeers& peers) {
   const bool vec = ((ti.flags >> 30) & 1u) != 0;
   bool bad = false;
 #pragma unroll
@@ -318,8 +320,18 @@ __device__ __forceinline__ void requant_rows(const MxTile& ti, const float (&x)[
     uint32_t scale;
     const int32_t q = mxint8_code(bits, key, vec, scale);
     const size_t row = j0 + j;
-    ti.cq[row * kbq * 32u + sp * 32u + lane] = static_cast<int8_t>(q);
-    if (lane == 0) ti.cscale[row * kbq + sp] = static_cast<uint8_t>(scale);
+    int8_t* qd = ti.cq + row * kbq * 32u + sp * 32u + lane;
+    uint8_t* sd = ti.cscale + row * kbq + sp;
+    *qd = static_cast<int8_t>(q);
+    if (lane == 0) *sd = static_cast<uint8_t>(scale);
+    for (uint32_t r = 0; r < peers.count; ++r) {
+      reinterpret_cast<int8_t*>(reinterpret_cast<char*>(qd) + peers.delta[r])[0] =
+          static_cast<int8_t>(q);
+      if (lane == 0) {
+        reinterpret_cast<uint8_t*>(reinterpret_cast<char*>(sd) + peers.delta[r])[0] =
+            static_cast<uint8_t>(scale);
+      }
+    }
   }
   if (bad && lane == 0) atomicOr(err, 1u);
 }
@@ -332,9 +344,10 @@ __device__ __forceinline__ void requant_rows(const MxTile& ti, const float (&x)[
 // peers' copies of C and the MXINT8 copy.
 //
 // With `stage` (512 bytes of shared memory for this warp), a full chunk of
-// 16 rows x 32 columns of a plain output (no accumulate, no peers, C 16-byte
-// aligned) is regrouped through shared memory, four rows at a time, into
-// 16-byte stores: lane l writes row l / 8, columns 4 (l % 8) .. + 3.
+// 16 rows x 32 columns of an output without accumulate, C and the peers'
+// copies 16-byte aligned, is regrouped through shared memory, four rows at a
+// time, into 16-byte stores (local, then each peer): lane l writes row l / 8,
+// columns 4 (l % 8) .. + 3.
 //
 // With `release` and 32 rows for this warp, both chunks are read out of TMEM
 // first and the accumulator is released (an arrival on `release`) before
@@ -365,7 +378,11 @@ __device__ __forceinline__ bool drain_tile(const MxParams& p, const MxTile& ti, 
   // layer's K (tiles start on 128-column boundaries); the block exists when
   // it starts before column N.
   const bool requant = ti.cq != nullptr && sp * 32u < cols;
-  const bool staged = stage != nullptr && !acc && npeers == 0 && ti.c != nullptr &&
+  // Peers' copies (the fused all-gather) take the same 16-byte stores when
+  // every peer buffer sits at a 16-byte multiple from the local one.
+  bool peers16 = true;
+  for (uint32_t q = 0; q < npeers; ++q) peers16 &= (p.peers.delta[q] & 15) == 0;
+  const bool staged = stage != nullptr && !acc && peers16 && ti.c != nullptr &&
                       cols == kTileW && (ti.ldc & 3u) == 0 &&
                       (reinterpret_cast<uintptr_t>(ti.c) & 15u) == 0;
   // The plane sums of rows j0 .. j0 + 15 out of TMEM.
@@ -399,9 +416,13 @@ __device__ __forceinline__ bool drain_tile(const MxParams& p, const MxTile& ti, 
         const float4 v = reinterpret_cast<const float4*>(stage)[lane];
         __syncwarp();
         const size_t row = j0 + 4u * q + (lane >> 3);
-        *reinterpret_cast<float4*>(ti.c + row * ti.ldc + sp * 32u + 4u * (lane & 7u)) = v;
+        float* dst = ti.c + row * ti.ldc + sp * 32u + 4u * (lane & 7u);
+        *reinterpret_cast<float4*>(dst) = v;
+        for (uint32_t r = 0; r < npeers; ++r) {
+          *reinterpret_cast<float4*>(reinterpret_cast<char*>(dst) + p.peers.delta[r]) = v;
+        }
       }
-      if (requant) requant_rows(ti, x, j0, sp, lane, col_ok, kbq, p.err);
+      if (requant) requant_rows(ti, x, j0, sp, lane, col_ok, kbq, p.err, p.peers);
       return;
     }
     if (col_ok) {
@@ -428,7 +449,7 @@ __device__ __forceinline__ bool drain_tile(const MxParams& p, const MxTile& ti, 
         }
       }
     }
-    if (requant) requant_rows(ti, x, j0, sp, lane, col_ok, kbq, p.err);
+    if (requant) requant_rows(ti, x, j0, sp, lane, col_ok, kbq, p.err, p.peers);
   };
   if constexpr (kEarly) {
     if (release != nullptr && r1 - r0 == 32u) {
@@ -1279,11 +1300,13 @@ void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out) {
 }
 
 int launch_mxf4_gather(const TcJob& inline_job, uint32_t nt, uint32_t tiles, int sm_count,
-                       uint32_t* err, cudaStream_t s, const MxGather& gather) {
+                       uint32_t* err, cudaStream_t s, const MxGather& gather,
+                       const MxPeers* peers) {
   if (tiles == 0) return 0;
   if (inline_job.wfmt != HRB_WFMT_MXFP4 || gather.geom.bp != 8u) return -1;
-  if (nt == 64) return launch_mx<64, 1, 4>(nullptr, &inline_job, tiles, sm_count, err, s, nullptr, &gather);
-  if (nt == 128) return launch_mx<128, 1, 4>(nullptr, &inline_job, tiles, sm_count, err, s, nullptr, &gather);
+  if (peers != nullptr && peers->count > kMaxPeers) return -1;
+  if (nt == 64) return launch_mx<64, 1, 4>(nullptr, &inline_job, tiles, sm_count, err, s, peers, &gather);
+  if (nt == 128) return launch_mx<128, 1, 4>(nullptr, &inline_job, tiles, sm_count, err, s, peers, &gather);
   return -1;
 }
 

@@ -195,6 +195,11 @@ QuantJob make_post_quant_job_for_noalloc(const hrb_gemm_desc* desc);
 DenseJob make_dense_job_for_noalloc(const hrb_gemm_desc* desc, const int8_t* aq,
                                     const uint8_t* ascale, const uint32_t* pieces,
                                     uint32_t npieces);
+// Context fields for the entry points outside capi.cu (comm.cu): the
+// device, and a failure that leaves `message` for hrb_last_error (ctx may
+// be null: the calling thread's message).
+int ctx_device(const hrb_ctx* ctx);
+hrb_status ctx_fail(hrb_ctx* ctx, hrb_status status, const char* message);
 // The message of a failed context-free call (hrb_last_error(NULL)).
 hrb_status noalloc_fail(hrb_status status, const char* message);
 hrb_status noalloc_cuda_fail(cudaError_t err, const char* what);

@@ -125,7 +125,8 @@ static_assert(sizeof(MxTile) == 64, "MxTile is read as four 16-byte loads");
 // The m_tiles * n_tiles tiles of one job (tile index mt * n_tiles + nt).
 void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out);
 // Peers that receive a copy of every output (the fused all-gather of a
-// column-sharded GEMM): output c is also stored at c + delta[i] bytes.
+// column- or row-sharded layer): an output byte at address x (C or the
+// MXINT8 copy) is also stored at x + delta[i].
 constexpr uint32_t kMaxPeers = 7;
 struct MxPeers {
   int64_t delta[kMaxPeers];
@@ -144,7 +145,8 @@ struct MxGather {
 };
 // One inline job (inline_job.a_tiles unused), nt = 64 or 128.
 int launch_mxf4_gather(const TcJob& inline_job, uint32_t nt, uint32_t tiles, int sm_count,
-                       uint32_t* err, cudaStream_t stream, const MxGather& gather);
+                       uint32_t* err, cudaStream_t stream, const MxGather& gather,
+                       const MxPeers* peers = nullptr);
 
 // One launch over `tiles` output tiles: the device array tiles_dev, or, when
 // it is null, the tiles of the single *inline_job.  `peers` may be null.

@@ -425,6 +425,18 @@ HRB_API hrb_status hrb_conv_plan_run(hrb_conv_plan* plan, void* stream, uint32_t
 HRB_API hrb_status hrb_conv_plan_profile(hrb_conv_plan* plan, void* stream, uint32_t reps,
                                          float* ms, uint32_t cap, uint32_t* nkernels);
 HRB_API hrb_status hrb_conv_plan_destroy(hrb_conv_plan* plan);
+/* Row-sharded convolutions (the images of a batch split over the GPUs of a
+ * node, hrb_shard_rows; each rank's plan covers its images, with `c`, `cq`
+ * and `cscale` pointing at its rows of full-size buffers): every later run
+ * also stores each output byte at address x (C and the MXINT8 copy) into
+ * peer_bases[i] + (x - local_base) over NVLink, so that once every rank's
+ * run has finished every rank holds all rows.  The outputs must lie in one
+ * buffer from local_base (hrb_shared_alloc) whose layout is the same on
+ * every rank.  At most 7 peers; HRB_MODE_FAST with FP32 input only (else
+ * HRB_ENOTSUP).  With 16-byte aligned buffers the FP32 outputs travel as
+ * 16-byte stores. */
+HRB_API hrb_status hrb_conv_plan_set_peers(hrb_conv_plan* plan, const void* local_base,
+                                           void* const* peer_bases, uint32_t npeers);
 
 /* ---------------------------------------------------------------------
  * 7. GACC, the DMA engine's gather-accumulate (DmaEngine::Gather,
@@ -490,12 +502,57 @@ HRB_API hrb_status hrb_peer_close(hrb_ctx* ctx, void* peer_ptr);
 HRB_API void hrb_shard_columns(uint32_t N, uint32_t rank, uint32_t ranks, uint32_t* n0,
                                uint32_t* n1);
 /* Makes every later run of `plan` also store each output to the peers: for
- * an output at address c (in [local_base, ...)), also to
- * peer_bases[i] + (c - local_base).  At most 7 peers; only plans whose GEMMs
+ * an output byte at address x (C, and the MXINT8 copy when the descriptors
+ * ask for one; all in one buffer from local_base), also to
+ * peer_bases[i] + (x - local_base).  At most 7 peers; only plans whose GEMMs
  * all take the tensor-core path for MXFP4 or W8 weights
  * (HRB_MODE_FAST, FP32 activations) accept peers (else HRB_ENOTSUP). */
 HRB_API hrb_status hrb_plan_set_peers(hrb_plan* plan, const void* local_base,
                                       void* const* peer_bases, uint32_t npeers);
+
+/* ---------------------------------------------------------------------
+ * 8. A communicator for hosts without a framework (one process per GPU,
+ *    NCCL over NVLink; no counterpart in the reference, whose NPU has no
+ *    collective).  It carries what the sharded paths need around their
+ *    kernels: the exchange of IPC handles for hrb_plan_set_peers and
+ *    hrb_conv_plan_set_peers, a barrier, and an in-place all-gather.  NCCL
+ *    is loaded at the first call; without it these return HRB_ENOTSUP and
+ *    everything else works.
+ * ------------------------------------------------------------------- */
+
+typedef struct hrb_comm hrb_comm;
+typedef struct hrb_comm_id {
+  uint8_t bytes[128];
+} hrb_comm_id;
+
+/* Rank 0 makes the id and hands it to the other ranks by its own means. */
+HRB_API hrb_status hrb_comm_id_new(hrb_comm_id* out);
+/* Every rank, with the same id and rank count, on the context's device;
+ * blocks until all ranks have joined. */
+HRB_API hrb_status hrb_comm_create(hrb_ctx* ctx, const hrb_comm_id* id, uint32_t rank,
+                                   uint32_t ranks, hrb_comm** out);
+HRB_API hrb_status hrb_comm_destroy(hrb_comm* comm);
+/* Synchronous: `bytes` of host record `mine` from every rank into host
+ * `all` [ranks][bytes], in rank order (e.g. hrb_ipc_handle values). */
+HRB_API hrb_status hrb_comm_exchange(hrb_comm* comm, const void* mine, void* all, size_t bytes);
+/* Returns once the work queued on every rank's context stream before the
+ * call has finished. */
+HRB_API hrb_status hrb_comm_barrier(hrb_comm* comm);
+/* Asynchronous on `stream` (NULL: the context's): work queued on the
+ * stream after the fence starts once every rank's stream has reached its
+ * fence (the end of a sharded step whose kernels store into the peers). */
+HRB_API hrb_status hrb_comm_fence(hrb_comm* comm, void* stream);
+/* In-place all-gather on `stream` (NULL: the context's): rank r has written
+ * bytes [offsets[r], offsets[r + 1]) of the device buffer `buf` (offsets:
+ * ranks + 1 entries, non-decreasing); afterwards every rank holds all of
+ * [offsets[0], offsets[ranks]).  Equal parts take one all-gather, ragged
+ * ones a group of broadcasts. */
+HRB_API hrb_status hrb_comm_allgather(hrb_comm* comm, void* buf, const uint64_t* offsets,
+                                      void* stream);
+/* Units (e.g. the images of a convolution batch) of rank `rank` of `ranks`:
+ * [u0, u1), as even as possible. */
+HRB_API void hrb_shard_rows(uint32_t units, uint32_t rank, uint32_t ranks, uint32_t* u0,
+                            uint32_t* u1);
 
 #ifdef __cplusplus
 }

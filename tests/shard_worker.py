@@ -1,14 +1,24 @@
 """Worker for the multi-process tests of hotarubi_b200.shard, launched with
 torch.distributed.run (one process per rank, rendezvous on 127.0.0.1).
 
-    --mode cpu   gloo ranks: each computes its column slice of a GEMM with
-                 the CPU oracle; the slices are gathered with
-                 shard.gather_columns and compared with the whole GEMM.
-    --mode gpu   NCCL ranks, one GPU each: a batch of column-sharded GEMMs
-                 whose epilogues store every output into all ranks' C
-                 (shard.PeerOutput + Plan.set_peers); every rank's C must equal
-                 the unsharded GEMM bit for bit, and so must the library
-                 all-gather of the slices.
+    --mode cpu   gloo ranks, host logic only:
+                 columns: each rank computes its column slice of a GEMM with
+                 the CPU oracle; shard.gather_columns must rebuild the whole
+                 GEMM;
+                 rows: each rank convolves its images (shard.rows) with the
+                 oracle; the row ranges (shard.row_offsets) gathered must
+                 rebuild the whole convolution.
+    --mode gpu   NCCL ranks, one GPU each, data plane through the library's
+                 communicator (shard.Group):
+                 columns: a batch of column-sharded GEMMs whose epilogues
+                 store every output into all ranks' C (PeerOutput +
+                 Plan.set_peers); every rank's C must equal the unsharded
+                 GEMM bit for bit, and so must the library all-gather;
+                 rows: the C5-shaped convolution (smaller batch) split by
+                 images, FP32 output and its MXINT8 copy stored into all
+                 ranks by the epilogue (ConvPlan.set_peers); both equal the
+                 unsharded convolution bit for bit, and so does the
+                 communicator's in-place all-gather of the row ranges.
 Exits non-zero on a mismatch.
 """
 import argparse
@@ -24,6 +34,10 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 from hotarubi_b200 import shard, workloads  # noqa: E402
+
+# The row-sharded convolution of the tests: 3x3, 256 -> 256 channels (the C5
+# conv's layer) on 2 x 3 images of 8 x 12.
+CONV = dict(images=6, H=8, W=12, cin=256, cout=256, kh=3, stride=1)
 
 
 def run_cpu() -> None:
@@ -43,14 +57,35 @@ def run_cpu() -> None:
     full = shard.gather_columns(torch.from_numpy(local.view(np.int32)), n).numpy()
     want = cpu.gemm_dense(0, q, s, w, ws, n)
     assert np.array_equal(full.view(np.uint32), want), "gathered columns differ"
+    # Rows: images split over the ranks, outputs contiguous along M.
+    c = CONV
+    hw, per = c["H"] * c["W"], (c["H"] // c["stride"]) * (c["W"] // c["stride"])
+    spans = [shard.rows(c["images"], r, ranks) for r in range(ranks)]
+    assert spans[0][0] == 0 and spans[-1][1] == c["images"]
+    assert all(spans[i][1] == spans[i + 1][0] for i in range(ranks - 1))
+    offs = shard.row_offsets(c["images"], per * c["cout"] * 4, ranks)
+    assert offs == [a * per * c["cout"] * 4 for a, _ in spans] + [c["images"] * per * c["cout"] * 4]
+    xa = workloads.activations(3, c["images"] * hw, c["cin"])
+    aq, asc = cpu.encode_mxint8(xa.view(np.uint32))
+    wc, wcs = workloads.mxfp4_weights(4, c["cout"], c["kh"] ** 2 * c["cin"])
+    i0, i1 = shard.rows(c["images"])
+    geo = (c["H"], c["W"], c["cin"], c["cout"], c["kh"], c["stride"])
+    mine = cpu.conv_dense(0, aq[i0 * hw:i1 * hw], asc[i0 * hw:i1 * hw], i1 - i0, *geo, wc, wcs)
+    width = max(b - a for a, b in spans) * per
+    padded = np.zeros((width, c["cout"]), np.uint32)
+    padded[:mine.shape[0]] = mine
+    parts = [torch.empty((width, c["cout"]), dtype=torch.int32) for _ in range(ranks)]
+    dist.all_gather(parts, torch.from_numpy(padded.view(np.int32)))
+    got = np.concatenate([parts[r].numpy()[:(b - a) * per] for r, (a, b) in enumerate(spans)])
+    want = cpu.conv_dense(0, aq, asc, c["images"], *geo, wc, wcs)
+    assert np.array_equal(got.view(np.uint32), want), "gathered rows differ"
 
 
-def run_gpu() -> None:
+def run_gpu_columns(lib, group) -> None:
     from hotarubi_b200 import capi
-    rank, ranks = dist.get_rank(), dist.get_world_size()
-    lib = capi.Library(torch.cuda.current_device())
+    rank = group.rank
     batch, m, n, k = 3, 96, 1000, 768
-    out = shard.PeerOutput(lib, (batch, m, n))
+    out = shard.PeerOutput(lib, group, (batch, m, n))
     out.tensor.zero_()
     n0, n1 = shard.columns(n)
     keep, local_descs, full_descs = [], [], []
@@ -86,26 +121,89 @@ def run_gpu() -> None:
             p = lib.plan(ds)
             p.set_peers(out.ptr, out.peer_bases)
             plans.append(p)
-    dist.barrier()
+    group.barrier()
     for p in plans:
         p.run()
+    group.fence()
     lib.sync()
-    shard.complete()
     got = out.tensor.cpu().numpy()
     want = ref.cpu().numpy()
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"rank {rank}: fused gather"
-    # The library baseline: gather this rank's slices with NCCL.
+    # The library baseline: gather this rank's slices with torch's NCCL.
     for b in range(batch):
         g = shard.gather_columns(out.tensor[b][:, n0:n1].contiguous(), n)
         assert torch.equal(g.view(torch.int32), ref[b].view(torch.int32)), f"rank {rank}: nccl"
-    dist.barrier()
+    group.barrier()
     for p in plans:
         p.close()
     full.close()
     torch.cuda.synchronize()
-    dist.barrier()
+    group.barrier()
     out.close()
-    lib.close()
+
+
+def run_gpu_rows(lib, group) -> None:
+    from hotarubi_b200 import capi
+    rank, ranks = group.rank, group.ranks
+    c = CONV
+    hw = c["H"] * c["W"]
+    per = (c["H"] // c["stride"]) * (c["W"] // c["stride"])
+    m = c["images"] * per
+    kpn = (c["cout"] + 31) // 32 * 32
+    geo = (c["H"], c["W"], c["cin"], c["cout"], c["kh"], c["stride"])
+    xa = torch.from_numpy(workloads.activations(5, c["images"] * hw, c["cin"])).cuda()
+    w, ws = workloads.mxfp4_weights(6, c["cout"], c["kh"] ** 2 * c["cin"])
+    bias = (np.random.default_rng(7).standard_normal(c["cout"]) * 0.01).astype(np.float32)
+    wd, wsd, bd = (torch.from_numpy(v).cuda() for v in (w, ws, bias))
+    # The unsharded convolution on this GPU.
+    ref = torch.zeros((m, c["cout"]), dtype=torch.float32, device="cuda")
+    ref_q = torch.zeros((m, kpn), dtype=torch.int8, device="cuda")
+    ref_s = torch.zeros((m, kpn // 32), dtype=torch.uint8, device="cuda")
+    full = lib.conv_plan(capi.conv_desc(0, c["images"], *geo, order=capi.CONV_YMAJOR, a=xa,
+                                        w=wd, wscale=wsd, bias=bd, c=ref, relu=True,
+                                        mode=capi.MODE_FAST, cq=ref_q, cscale=ref_s))
+    full.run()
+    lib.sync()
+    # This rank's images, outputs into the shared buffer at their rows.
+    out = shard.PeerOutput(lib, group, (m, c["cout"]), mx_shape=(m, kpn))
+    out.tensor.zero_()
+    out.q.zero_()
+    out.s.zero_()
+    i0, i1 = shard.rows(c["images"])
+    r0, r1 = i0 * per, i1 * per
+    plan = None
+    if i1 > i0:
+        plan = lib.conv_plan(capi.conv_desc(0, i1 - i0, *geo, order=capi.CONV_YMAJOR,
+                                            a=xa[i0 * hw:i1 * hw], w=wd, wscale=wsd, bias=bd,
+                                            c=out.tensor[r0:r1], relu=True, mode=capi.MODE_FAST,
+                                            cq=out.q[r0:r1], cscale=out.s[r0:r1]))
+        plan.set_peers(out.ptr, out.peer_bases)
+    torch.cuda.synchronize()
+    group.barrier()
+    if plan is not None:
+        plan.run()
+    group.fence()
+    lib.sync()
+    assert torch.equal(out.tensor.view(torch.int32), ref.view(torch.int32)), \
+        f"rank {rank}: fused row gather (FP32)"
+    assert torch.equal(out.q, ref_q) and torch.equal(out.s, ref_s), \
+        f"rank {rank}: fused row gather (MXINT8 copy)"
+    # The communicator's in-place all-gather of the row ranges.
+    group.barrier()
+    loose = torch.zeros((m, c["cout"]), dtype=torch.float32, device="cuda")
+    loose[r0:r1] = ref[r0:r1]
+    torch.cuda.synchronize()
+    group.allgather(loose, shard.row_offsets(c["images"], per * c["cout"] * 4, ranks))
+    lib.sync()
+    assert torch.equal(loose.view(torch.int32), ref.view(torch.int32)), \
+        f"rank {rank}: communicator all-gather"
+    group.barrier()
+    if plan is not None:
+        plan.close()
+    full.close()
+    torch.cuda.synchronize()
+    group.barrier()
+    out.close()
 
 
 def main() -> None:
@@ -114,10 +212,19 @@ def main() -> None:
     args = ap.parse_args()
     timeout = datetime.timedelta(seconds=60)
     if args.mode == "gpu":
-        torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
-        dist.init_process_group("nccl", timeout=timeout,
-                                device_id=torch.device("cuda", int(os.environ["LOCAL_RANK"])))
-        run_gpu()
+        from hotarubi_b200 import capi
+        local = int(os.environ["LOCAL_RANK"])
+        torch.cuda.set_device(local)
+        # torch.distributed carries the communicator's bootstrap id and the
+        # column baseline (gather_columns); the rest is the library's.
+        dist.init_process_group("nccl", timeout=timeout, device_id=torch.device("cuda", local))
+        lib = capi.Library(local)
+        group = shard.Group(lib)
+        run_gpu_columns(lib, group)
+        run_gpu_rows(lib, group)
+        group.barrier()
+        group.close()
+        lib.close()
     else:
         dist.init_process_group("gloo", timeout=timeout)
         run_cpu()
