@@ -47,3 +47,21 @@ def test_two_gpus_fused_all_gather():
         pytest.skip("needs two GPUs")
     r = launch("gpu", 2, 400)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+
+
+@pytest.mark.gpu
+def test_cpp_host_shards_on_two_gpus():
+    """The C++ host side with no framework (tests/cpp/test_shard_host.cpp):
+    forked ranks, communicator bootstrap through pipes, a column-sharded GEMM
+    and a row-sharded convolution with the all-gather fused into their
+    epilogues, and the communicator's all-gather, each bit for bit with the
+    unsharded result."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    exe = os.path.join(ROOT, "tests", "cpp", "_build", "test_shard_host")
+    if not os.path.exists(exe):
+        pytest.skip("tests/cpp not built")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([exe, "2"], capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
