@@ -172,6 +172,16 @@ def load() -> ctypes.CDLL:
             "hrb_comm_fence": (ctypes.c_int, [P, P]),
             "hrb_comm_allgather": (ctypes.c_int, [P, P, ctypes.POINTER(ctypes.c_uint64), P]),
             "hrb_shard_rows": (None, [u32, u32, u32, ctypes.POINTER(u32), ctypes.POINTER(u32)]),
+            "hrb_image_region": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p,
+                                                ctypes.POINTER(ctypes.c_uint64),
+                                                ctypes.POINTER(ctypes.c_uint64)]),
+            "hrb_image_upload": (ctypes.c_int, [P, P, ctypes.c_size_t, ctypes.POINTER(P)]),
+            "hrb_image_destroy": (ctypes.c_int, [P]),
+            "hrb_image_data": (P, [P]),
+            "hrb_image_weights": (ctypes.c_int, [P, P, u32, ctypes.c_uint64, ctypes.c_uint64,
+                                                 u32, u32, P, P, P]),
+            "hrb_gemm_image": (ctypes.c_int, [P, P, ctypes.POINTER(GemmDesc), ctypes.c_uint64,
+                                              ctypes.c_uint64, P]),
         }
         for name, (res, args) in sigs.items():
             f = getattr(lib, name, None)
@@ -206,6 +216,43 @@ def shard_rows(units: int, rank: int, ranks: int) -> tuple[int, int]:
     u0, u1 = ctypes.c_uint32(), ctypes.c_uint32()
     load().hrb_shard_rows(units, rank, ranks, ctypes.byref(u0), ctypes.byref(u1))
     return u0.value, u1.value
+
+
+def image_region(meta_json: str, name: str) -> tuple[int, int]:
+    """hrb_image_region: [offset, size] of region `name` in meta.json text."""
+    off, size = ctypes.c_uint64(), ctypes.c_uint64()
+    st = load().hrb_image_region(meta_json.encode(), name.encode(), ctypes.byref(off),
+                                 ctypes.byref(size))
+    if st != HRB_OK:
+        raise HrbError(st, (load().hrb_last_error(None) or b"").decode())
+    return off.value, size.value
+
+
+class Image:
+    """An hrb_image: a compiled program's image.bin on the context's device."""
+
+    def __init__(self, owner: "Library", data: bytes | np.ndarray):
+        self.owner = owner
+        buf = np.frombuffer(bytes(data), np.uint8) if isinstance(data, bytes) else data
+        buf = np.ascontiguousarray(buf, np.uint8)
+        h = ctypes.c_void_p()
+        owner._check(owner.lib.hrb_image_upload(owner.ctx, buf.ctypes.data, buf.size,
+                                                ctypes.byref(h)))
+        self.h = h
+
+    def weights(self, wfmt, offset, N, K, w, wscale, offset_lo=0, stream=0) -> None:
+        self.owner._check(self.owner.lib.hrb_image_weights(
+            self.owner.ctx, self.h, wfmt, offset, offset_lo, N, K, _ptr(w), _ptr(wscale),
+            stream or None))
+
+    def gemm(self, d: "GemmDesc", offset: int, offset_lo: int = 0, stream: int = 0) -> None:
+        self.owner._check(self.owner.lib.hrb_gemm_image(self.owner.ctx, self.h, ctypes.byref(d),
+                                                        offset, offset_lo, stream or None))
+
+    def close(self) -> None:
+        if self.h:
+            self.owner.lib.hrb_image_destroy(self.h)
+            self.h = None
 
 
 def comm_id_new() -> bytes:

@@ -554,6 +554,42 @@ HRB_API hrb_status hrb_comm_allgather(hrb_comm* comm, void* buf, const uint64_t*
 HRB_API void hrb_shard_rows(uint32_t units, uint32_t rank, uint32_t ranks, uint32_t* u0,
                             uint32_t* u1);
 
+/* ---------------------------------------------------------------------
+ * 9. Weights straight from a compiled program: image.bin, the compiler's DDR
+ *    image, and meta.json, whose "regions" maps each allocation's name to
+ *    [offset, size] (MetaJson, tools/compiler/output.cpp:57-62; LoadProgram,
+ *    include/hotarubi/runtime.hpp:44-56).  A Linear's weights are a region of
+ *    WBUF words in PackWbuf order (tools/compiler/tensors.cpp:66-90, groups
+ *    of 8 columns x kb words of 144 bytes): MXFP4 one region, W8 two,
+ *    "<name>_hi" and "<name>_lo" (PlaceW8, smolvla_common.cpp:95-103).
+ * ------------------------------------------------------------------- */
+
+typedef struct hrb_image hrb_image;
+
+/* The [offset, size] of region `name` in the text of a meta.json (host
+ * only; HRB_EINVAL with a message when it is missing or malformed). */
+HRB_API hrb_status hrb_image_region(const char* meta_json, const char* name, uint64_t* offset,
+                                    uint64_t* size);
+/* Copies image.bin (n host bytes) to the context's device, once. */
+HRB_API hrb_status hrb_image_upload(hrb_ctx* ctx, const void* bytes, size_t n, hrb_image** out);
+HRB_API hrb_status hrb_image_destroy(hrb_image* image);
+/* The device copy of the image. */
+HRB_API const void* hrb_image_data(const hrb_image* image);
+/* The weights of one Linear from the image, as the dense format of `wfmt`
+ * (device buffers w [N][kp(/2)] and wscale [N][kb]): MXFP4 from the region
+ * at `offset`, W8 from the HI plane at `offset` and the LO plane at
+ * `offset_lo`.  N a multiple of 8, K of 32; MXFP8 has no image format
+ * (HRB_ENOTSUP).  Asynchronous on `stream`. */
+HRB_API hrb_status hrb_image_weights(hrb_ctx* ctx, const hrb_image* image, uint32_t wfmt,
+                                     uint64_t offset, uint64_t offset_lo, uint32_t N,
+                                     uint32_t K, uint8_t* w, uint8_t* wscale, void* stream);
+/* hrb_gemm_dense with the weights of the region(s) at offset (offset_lo
+ * for W8's LO plane) of the image: desc->w and desc->wscale must be NULL.
+ * The region becomes dense weights on the device the first time (kept in the
+ * image for the calls after); N is rounded up to whole groups of 8 there. */
+HRB_API hrb_status hrb_gemm_image(hrb_ctx* ctx, hrb_image* image, const hrb_gemm_desc* desc,
+                                  uint64_t offset, uint64_t offset_lo, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

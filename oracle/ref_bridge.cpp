@@ -23,6 +23,7 @@
 #include "gemm_array.hpp"      // tools/iss/gemm_array.hpp
 #include "hotarubi/exact.hpp"  // include/hotarubi/exact.hpp
 #include "hotarubi/formats.hpp"
+#include "hotarubi/json.hpp"  // include/hotarubi/json.hpp
 #include "lane.hpp"       // tools/iss/lane.hpp
 #include "memories.hpp"   // tools/iss/memories.hpp
 #include "reference.hpp"  // tools/iss/reference.hpp
@@ -816,6 +817,47 @@ int hrbref_gacc_iss(uint32_t tokens, uint32_t slots, uint32_t blocks, const uint
       }
     }
   }
+  return 0;
+}
+
+
+// The regions part of a meta.json as the compiler writes it (MetaJson,
+// tools/compiler/output.cpp:57-89: base, instr_off, n_instr, image_bytes,
+// listings, then "regions": name -> [offset, size]) with hotarubi's Json
+// writer; returns the text length, or -1 when `cap` is too small.
+int64_t hrbref_meta_json(const char* const* names, const uint64_t* offsets,
+                         const uint64_t* sizes, uint32_t n, uint64_t image_bytes, char* out,
+                         size_t cap) {
+  using hotarubi::Json;
+  Json::Object regions;
+  for (uint32_t i = 0; i < n; ++i) {
+    regions.emplace_back(names[i], Json(Json::Array{Json(static_cast<double>(offsets[i])),
+                                                    Json(static_cast<double>(sizes[i]))}));
+  }
+  Json::Object meta = {{"base", Json(static_cast<double>(0x40000000ULL))},
+                       {"instr_off", Json(0.0)},
+                       {"n_instr", Json(0.0)},
+                       {"image_bytes", Json(static_cast<double>(image_bytes))}};
+  meta.emplace_back("listings", Json(Json::Object{{"main", Json(std::string("main.listing.json"))}}));
+  meta.emplace_back("regions", Json(std::move(regions)));
+  const std::string text = Json(std::move(meta)).Dump() + "\n";
+  if (text.size() + 1 > cap) return -1;
+  std::memcpy(out, text.c_str(), text.size() + 1);
+  return static_cast<int64_t>(text.size());
+}
+
+// A region of a meta.json as LoadProgram reads it (tools/runtime/runtime.cpp:
+// 132-150): Json::Parse, then regions -> name -> [offset, size].  0 when
+// found, 1 when missing, 2 when the text does not parse.
+int hrbref_find_region(const char* meta, const char* name, uint64_t* offset, uint64_t* size) {
+  auto json = hotarubi::Json::Parse(meta);
+  if (!json) return 2;
+  const hotarubi::Json* regions = json->Find("regions");
+  if (regions == nullptr) return 1;
+  const hotarubi::Json* r = regions->Find(name);
+  if (r == nullptr || !r->IsArray() || r->Items().size() != 2) return 1;
+  *offset = static_cast<uint64_t>(r->Items()[0].Number());
+  *size = static_cast<uint64_t>(r->Items()[1].Number());
   return 0;
 }
 
