@@ -601,19 +601,17 @@ k_quantize_planes(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ 
 // 16-byte-aligned FP32 rows, every job of the launch with NT-row tiles and
 // one rounding rule.  Units, unit ranges, the staging ring and the outputs
 // are those of k_quantize_planes; what changes is the work per unit:
-//   * q comes out of one fused multiply-add scaled by 4.  t = x 2^(8 - e) +
-//     6 2^23 lies in [2^25, 2^26), where FP32 steps by 4, so its one rounding
-//     gives t = 6 2^23 + 4 RNE(x 2^(6 - e)) exactly (x 2^(6 - e) is exact
-//     and ties go to the even multiple of 4, i.e. to even q), and the bits of
-//     t masked with 0x3FC are (q & 0xFF) * 4: the byte offset of q's entry
-//     in a table of 4-byte words, with no shift;
+//   * q comes out of one fused multiply-add: t = x 2^(6 - e) + 1.5 2^23 is
+//     rounded once to an integer (x 2^(6 - e) is exact), so the low byte of
+//     t's bits is q in two's complement; (bits & 0xFF) * 4 is the byte offset
+//     of q's entry in a table of 4-byte words;
 //   * two tables, the digit codes in the low nibble of each plane byte and
 //     the same in the high nibble, merge an element pair with one OR;
 //   * the tile height is a template parameter, so the three plane stores and
 //     the scale store take constant offsets from one block pointer, and both
 //     walks (loads and stores) advance by additions.
-// Blocks whose scale 2^(8 - e) leaves the FP32 range (largest magnitude
-// below 2^-119, or Inf/NaN) take the integer rules, as in k_quantize_planes.
+// Blocks whose scale 2^(6 - e) leaves the FP32 range (largest magnitude
+// below 2^-120, or Inf/NaN) take the integer rules, as in k_quantize_planes.
 
 // The load side of a warp's walk over units: the lane's first element of
 // the current unit, for the cp.async staging.
@@ -731,7 +729,7 @@ __device__ __forceinline__ void e2m1_stage(const E2m1Loads& w, uint32_t dst) {
 template <uint32_t NT, bool kVec>
 __device__ __forceinline__ void e2m1_encode(const E2m1Stores& w, uint32_t v[8], uint32_t lane,
                                             uint32_t sadd, uint32_t& bad, const uint8_t* lut) {
-  constexpr float kM4 = 50331648.0f;  // 6 * 2^23
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
   constexpr uint32_t kPlane = NT * 128u;
   float m[4];
 #pragma unroll
@@ -759,14 +757,14 @@ __device__ __forceinline__ void e2m1_encode(const E2m1Stores& w, uint32_t v[8], 
   }
   uint32_t b[8];  // (q & 0xFF) * 4
   uint8_t* blk = w.blk;
-  if (scale - 8u < 247u) {
-    // 8 <= scale <= 254: 2^(8 - e) = 2^(135 - scale) is a normal FP32.
-    const float sc = __uint_as_float((262u - scale) << 23);
+  if (scale - 7u < 248u) {
+    // 7 <= scale <= 254: 2^(6 - e) = 2^(133 - scale) is a normal FP32.
+    const float sc = __uint_as_float((260u - scale) << 23);
 #pragma unroll
     for (uint32_t i = 0; i < 8; ++i) {
       // q >= -128 always; 128 clamps to 127.
-      b[i] = __float_as_uint(fminf(__fmaf_rn(__uint_as_float(v[i]), sc, kM4), kM4 + 508.0f)) &
-             0x3FCu;
+      b[i] = (__float_as_uint(fminf(__fmaf_rn(__uint_as_float(v[i]), sc, kMagic),
+                                    kMagic + 127.0f)) & 0xFFu) << 2;
     }
     if ((lane & 3u) < 3u) blk[w.sf] = static_cast<uint8_t>(scale + sadd);
   } else {
