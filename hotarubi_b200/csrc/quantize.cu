@@ -632,7 +632,7 @@ struct E2m1Stores {
 };
 
 __device__ __forceinline__ void e2m1_loads_at(E2m1Loads& w, const QuantJob& j, uint32_t row,
-                                              uint32_t step, uint32_t lane) {
+                                              uint32_t step) {
   w.x = j.x;
   w.ldx = j.ldx;
   w.cols = j.cols;
@@ -640,7 +640,7 @@ __device__ __forceinline__ void e2m1_loads_at(E2m1Loads& w, const QuantJob& j, u
   w.k_steps = j.k_steps;
   w.row = row;
   w.step = step;
-  w.col0 = step * 256u + lane * 8u;
+  w.col0 = step * 256u;
   w.src = j.x + static_cast<size_t>(row) * j.ldx + w.col0;
 }
 
@@ -664,8 +664,8 @@ __device__ __forceinline__ void e2m1_stores_at(E2m1Stores& w, const QuantJob& j,
   e2m1_stores_row<NT>(w, lane);
 }
 
-__device__ __forceinline__ void e2m1_loads_next(E2m1Loads& w, const QuantJob* jobs, uint32_t njobs,
-                                                uint32_t lane) {
+__device__ __forceinline__ void e2m1_loads_next(E2m1Loads& w, const QuantJob* jobs,
+                                                uint32_t njobs) {
   w.col0 += 256u;
   w.src += 256;
   if (++w.step < w.k_steps) return;
@@ -682,8 +682,8 @@ __device__ __forceinline__ void e2m1_loads_next(E2m1Loads& w, const QuantJob* jo
   }
   w.row = row;
   w.step = 0;
-  w.col0 = lane * 8u;
-  w.src = w.x + static_cast<size_t>(row) * w.ldx + w.col0;
+  w.col0 = 0;
+  w.src = w.x + static_cast<size_t>(row) * w.ldx;
 }
 
 template <uint32_t NT>
@@ -705,21 +705,31 @@ __device__ __forceinline__ void e2m1_stores_next(E2m1Stores& w, const QuantJob* 
   if (row < w.rows) e2m1_stores_row<NT>(w, lane);
 }
 
-// The lane's eight elements of the current unit into its 32 bytes of a ring
-// slot (16-byte rows: cp.async, zero-filled past the row's end).
-__device__ __forceinline__ void e2m1_stage(const E2m1Loads& w, uint32_t dst) {
-  if (w.col0 + 8u <= w.cols) {
+// A unit's 256 FP32 values into a 1 KB ring slot, copied by the whole warp
+// in two coalesced 16-byte copies per lane: lane l copies 16-byte chunks l
+// and 32 + l.  Chunk c lands at 16-byte position c ^ ((c >> 3) & 1) of the
+// slot, so that each lane later reads its own two chunks 2l, 2l + 1 (its
+// eight consecutive elements) without bank conflicts: within a quarter
+// warp the eight positions read together cover all eight 16-byte bank
+// groups.  Rows end with zero-filled chunks (16-byte aligned rows).
+__device__ __forceinline__ uint32_t e2m1_chunk_pos(uint32_t c) { return c ^ ((c >> 3) & 1u); }
+
+__device__ __forceinline__ void e2m1_stage(const E2m1Loads& w, uint32_t slot, uint32_t lane) {
+  const uint32_t d0 = slot + 16u * e2m1_chunk_pos(lane);
+  const uint32_t d1 = slot + 16u * e2m1_chunk_pos(32u + lane);
+  if (w.col0 + 256u <= w.cols) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n\t"
-                 "cp.async.cg.shared.global [%2], [%3], 16;" ::"r"(dst), "l"(w.src),
-                 "r"(dst + 16u), "l"(w.src + 4)
+                 "cp.async.cg.shared.global [%2], [%3], 16;" ::"r"(d0), "l"(w.src + 4u * lane),
+                 "r"(d1), "l"(w.src + 128u + 4u * lane)
                  : "memory");
   } else {
 #pragma unroll
     for (uint32_t h = 0; h < 2; ++h) {
-      const uint32_t col = w.col0 + 4u * h;
+      const uint32_t c = 32u * h + lane;
+      const uint32_t col = w.col0 + 4u * c;
       const uint32_t have = col < w.cols ? min(4u, w.cols - col) : 0u;
-      const float* from = have != 0 ? w.src + 4u * h : w.x;  // any valid address when empty
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst + 16u * h),
+      const float* from = have != 0 ? w.src + 4u * c : w.x;  // any valid address when empty
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(h == 0 ? d0 : d1),
                    "l"(from), "r"(4u * have)
                    : "memory");
     }
@@ -800,11 +810,14 @@ __device__ __forceinline__ void e2m1_encode(const E2m1Stores& w, uint32_t v[8], 
   *reinterpret_cast<uint32_t*>(out + 2u * kPlane) = __byte_perm(b01, b23, 0x5410u);
 }
 
+// Units in flight per warp in the specialised encoder.
+constexpr uint32_t kE2m1Depth = 6;
+
 template <uint32_t NT, bool kVec>
 __global__ void __launch_bounds__(kPlaneWarps * 32)
 k_quantize_planes_e2m1(const QuantJob* jobs, uint32_t njobs,
                        const __grid_constant__ QuantJob inline_job, uint32_t* error_flag) {
-  __shared__ __align__(16) uint32_t ring[kPlaneWarps][kPlaneDepth][256];
+  __shared__ __align__(16) uint32_t ring[kPlaneWarps][kE2m1Depth][256];
   // Byte offset 4 (q & 0xFF): the E2M1 codes of q's digits d0, d1, d2 (q =
   // 64 d2 + 8 d1 + d0, d2 = RNE(q / 64), d1 = RNE((q - 64 d2) / 8)) in the
   // low nibbles of bytes 0, 1, 2; from byte 1024 on, the same in the high
@@ -857,37 +870,41 @@ k_quantize_planes_e2m1(const QuantJob* jobs, uint32_t njobs,
   E2m1Loads ld;
   E2m1Stores st;
   ld.jx = st.jx = jx;
-  e2m1_loads_at(ld, j0, u / j0.k_steps, u % j0.k_steps, lane);
+  e2m1_loads_at(ld, j0, u / j0.k_steps, u % j0.k_steps);
   e2m1_stores_at<NT>(st, j0, u / j0.k_steps, u % j0.k_steps, lane);
   const uint32_t sadd = 3u * (lane & 3u) - 6u;  // plane p's scale: scale - 6 + 3p
   const uint8_t* lutb = reinterpret_cast<const uint8_t*>(lut);
   uint32_t bad = 0;
-  const uint32_t mine = static_cast<uint32_t>(__cvta_generic_to_shared(&ring[wib][0][lane * 8u]));
+  const uint32_t mine = static_cast<uint32_t>(__cvta_generic_to_shared(&ring[wib][0][0]));
+  // This lane's eight elements in a slot: chunks 2 lane and 2 lane + 1.
+  const uint32_t r0 = 4u * e2m1_chunk_pos(2u * lane), r1 = 4u * e2m1_chunk_pos(2u * lane + 1u);
   // One commit group per unit slot, empty past the range, so that
-  // wait_group(kPlaneDepth - 1) always means "the oldest has landed".
+  // wait_group(kE2m1Depth - 1) always means "the oldest has landed".
 #pragma unroll
-  for (uint32_t d = 0; d < kPlaneDepth; ++d) {
+  for (uint32_t d = 0; d < kE2m1Depth; ++d) {
     if (d < count) {
-      e2m1_stage(ld, mine + d * 1024u);
-      e2m1_loads_next(ld, jobs, njobs, lane);
+      e2m1_stage(ld, mine + d * 1024u, lane);
+      e2m1_loads_next(ld, jobs, njobs);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
-  for (uint32_t i0 = 0; i0 < count; i0 += kPlaneDepth) {
+  for (uint32_t i0 = 0; i0 < count; i0 += kE2m1Depth) {
 #pragma unroll
-    for (uint32_t d = 0; d < kPlaneDepth; ++d) {
+    for (uint32_t d = 0; d < kE2m1Depth; ++d) {
       const uint32_t i = i0 + d;
       if (i < count) {
-        asm volatile("cp.async.wait_group %0;" ::"n"(kPlaneDepth - 1) : "memory");
-        const uint32_t* slot = &ring[wib][d][lane * 8u];
-        const uint4 lo = *reinterpret_cast<const uint4*>(slot);
-        const uint4 hi = *reinterpret_cast<const uint4*>(slot + 4);
+        asm volatile("cp.async.wait_group %0;" ::"n"(kE2m1Depth - 1) : "memory");
+        __syncwarp();  // the slot was filled by every lane's copies
+        const uint32_t* slot = &ring[wib][d][0];
+        const uint4 lo = *reinterpret_cast<const uint4*>(slot + r0);
+        const uint4 hi = *reinterpret_cast<const uint4*>(slot + r1);
         uint32_t v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        __syncwarp();  // every lane has read the slot before it is refilled
         e2m1_encode<NT, kVec>(st, v, lane, sadd, bad, lutb);
         e2m1_stores_next<NT>(st, jobs, njobs, lane);
-        if (i + kPlaneDepth < count) {
-          e2m1_stage(ld, mine + d * 1024u);
-          e2m1_loads_next(ld, jobs, njobs, lane);
+        if (i + kE2m1Depth < count) {
+          e2m1_stage(ld, mine + d * 1024u, lane);
+          e2m1_loads_next(ld, jobs, njobs);
         }
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
