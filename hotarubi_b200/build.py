@@ -9,6 +9,7 @@ statically so that the library loads wherever the driver is present.
 from __future__ import annotations
 
 import concurrent.futures
+import hashlib
 import os
 import shutil
 import subprocess
@@ -34,18 +35,44 @@ def nvcc() -> str:
     return path
 
 
+def _key(cmd: list[str], files: list[str]) -> str:
+    """What an output is built from: the command and the contents of its
+    inputs (not their timestamps, which a clock step can make lie)."""
+    h = hashlib.sha256("\0".join(cmd).encode())
+    for f in files:
+        with open(f, "rb") as fh:
+            h.update(hashlib.sha256(fh.read()).digest())
+    return h.hexdigest()
+
+
+def _fresh(out: str, key: str) -> bool:
+    try:
+        with open(out + ".key") as fh:
+            return os.path.exists(out) and fh.read() == key
+    except OSError:
+        return False
+
+
+def _stamp(out: str, key: str) -> None:
+    with open(out + ".key", "w") as fh:
+        fh.write(key)
+
+
 def _compile(src: str, verbose: bool) -> str:
     obj = os.path.join(OBJDIR, os.path.basename(src).replace(".cu", ".o"))
-    deps = [src] + [os.path.join(CSRC, f) for f in os.listdir(CSRC)
-                    if f.endswith((".cuh", ".h"))] + [os.path.join(INCLUDE, "hrb_gemm.h")]
-    if os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(d) for d in deps):
+    deps = [src] + sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC)
+                          if f.endswith((".cuh", ".h"))) + [os.path.join(INCLUDE, "hrb_gemm.h")]
+    cmd = [nvcc()] + NVCC_FLAGS + ["-c", src, "-o", obj]
+    key = _key(cmd, deps)
+    if _fresh(obj, key) and not verbose:
         return obj
-    cmd = [nvcc()] + NVCC_FLAGS + (["-Xptxas", "-v"] if verbose else []) + ["-c", src, "-o", obj]
-    r = subprocess.run(cmd, capture_output=True, text=True)
+    run = cmd[:-4] + (["-Xptxas", "-v"] if verbose else []) + cmd[-4:]
+    r = subprocess.run(run, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed on {src}:\n{r.stdout}\n{r.stderr}")
     if verbose:
         sys.stderr.write(r.stderr)
+    _stamp(obj, key)
     return obj
 
 
@@ -55,14 +82,16 @@ def build(verbose: bool = False) -> str:
     sources = sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
     with concurrent.futures.ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as pool:
         objs = list(pool.map(lambda s: _compile(s, verbose), sources))
-    if os.path.exists(LIB) and os.path.getmtime(LIB) >= max(os.path.getmtime(o) for o in objs):
-        return LIB
     tmp = LIB + ".tmp"
     cmd = [nvcc()] + ARCH + ["-shared", "-cudart", "static", "-o", tmp] + objs + ["-ldl"]
+    key = _key(cmd, objs)
+    if _fresh(LIB, key):
+        return LIB
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
     os.replace(tmp, LIB)
+    _stamp(LIB, key)
     return LIB
 
 
@@ -76,14 +105,16 @@ def build_host() -> str:
     gemm = build()
     src = os.path.join(HOST, "gpu_gemm_array.cpp")
     deps = [src, os.path.join(HOST, "gpu_gemm_array.hpp"), os.path.join(INCLUDE, "hrb_gemm.h"), gemm]
-    if os.path.exists(HOST_LIB) and os.path.getmtime(HOST_LIB) >= max(os.path.getmtime(d) for d in deps):
-        return HOST_LIB
     cxx = shutil.which("g++") or "c++"
     cmd = [cxx, "-std=c++20", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-I", INCLUDE,
            "-I", HOST, src, "-L", LIBDIR, "-lhrb_gemm", "-Wl,-rpath,$ORIGIN", "-o", HOST_LIB]
+    key = _key(cmd, deps)
+    if _fresh(HOST_LIB, key):
+        return HOST_LIB
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"host library build failed:\n{r.stdout}\n{r.stderr}")
+    _stamp(HOST_LIB, key)
     return HOST_LIB
 
 

@@ -811,7 +811,7 @@ __device__ __forceinline__ void e2m1_encode(const E2m1Stores& w, uint32_t v[8], 
 }
 
 // Units in flight per warp in the specialised encoder.
-constexpr uint32_t kE2m1Depth = 6;
+constexpr uint32_t kE2m1Depth = 5;
 
 template <uint32_t NT, bool kVec>
 __global__ void __launch_bounds__(kPlaneWarps * 32)
