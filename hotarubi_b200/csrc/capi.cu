@@ -61,6 +61,7 @@ struct hrb_plan {
   // Activations of kind::mxf4 GEMMs: the digit-plane encoder's jobs.
   uint32_t nplanes = 0;
   uint64_t plane_units = 0;
+  uint64_t plane_groups = 0;  // the same jobs counted in 4-step groups
   const hrb::QuantJob* d_planes = nullptr;
   std::vector<hrb::QuantJob> d_planes_host;  // the same jobs on the host
   // MXINT8 copies of the exact GEMMs' outputs, encoded after them.
@@ -1214,6 +1215,8 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
       tc_translate(&d, tj, ctx->stream);
       qj.unit_begin = plan->plane_units;
       plan->plane_units += qj.units;
+      qj.group_begin = plan->plane_groups;
+      plan->plane_groups += static_cast<uint64_t>(qj.rows) * ((qj.k_steps + 3u) / 4u);
       planes.push_back(qj);
       size_t g = 0;
       const uint32_t kind = 2u;

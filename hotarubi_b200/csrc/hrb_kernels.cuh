@@ -127,6 +127,10 @@ struct QuantJob {
   uint32_t tile_rows, k_steps;
   uint32_t tiles_kind;
   uint32_t cover_blocks;  // K blocks written (kb plus the steps' zero padding)
+  // E2M1 planes: prefix over a launch's jobs of their (row, group of four
+  // 256-element steps) items, rows * ceil(k_steps / 4) per job; the
+  // specialised encoder's unit of work.
+  uint64_t group_begin;
 };
 
 constexpr uint32_t kMaxPieces = 64;

@@ -599,230 +599,176 @@ k_quantize_planes(const QuantJob* jobs, uint32_t njobs, const __grid_constant__ 
 // ---------------------------------------------------------------------------
 // The plane encoder's common case, specialised: E2M1 planes (kind::mxf4) of
 // 16-byte-aligned FP32 rows, every job of the launch with NT-row tiles and
-// one rounding rule.  Units, unit ranges, the staging ring and the outputs
-// are those of k_quantize_planes; what changes is the work per unit:
+// one rounding rule.  Same outputs as k_quantize_planes; the work is laid
+// out for fewer instructions per element:
+//   * a warp takes one item at a time, one row's group of four 256-element
+//     K steps (1024 values, 32 blocks), and lane l owns block l whole: the
+//     block's largest magnitude is a max over the lane's own 32 values (no
+//     shuffles), its scale is worked out once, and its three plane chunks
+//     (a block is one 16-byte chunk of a plane row) leave as 16-byte stores;
+//   * the item's 4 KB arrive by coalesced cp.async copies (lane l copies
+//     16-byte chunks l + 32 j) into a ring slot, chunk c at position
+//     c ^ ((c >> 3) & 7), so that each lane's eight chunks 8 l .. 8 l + 7 are
+//     read without bank conflicts;
 //   * q comes out of one fused multiply-add: t = x 2^(6 - e) + 1.5 2^23 is
 //     rounded once to an integer (x 2^(6 - e) is exact), so the low byte of
-//     t's bits is q in two's complement; (bits & 0xFF) * 4 is the byte offset
-//     of q's entry in a table of 4-byte words;
-//   * two tables, the digit codes in the low nibble of each plane byte and
-//     the same in the high nibble, merge an element pair with one OR;
-//   * the tile height is a template parameter, so the three plane stores and
-//     the scale store take constant offsets from one block pointer, and both
-//     walks (loads and stores) advance by additions.
-// Blocks whose scale 2^(6 - e) leaves the FP32 range (largest magnitude
-// below 2^-120, or Inf/NaN) take the integer rules, as in k_quantize_planes.
+//     t's bits is q in two's complement and (bits & 0xFF) * 4 is the byte
+//     offset of q's digit codes in a table of words; a second table holds
+//     the codes in the high nibbles, so an element pair merges with one OR;
+//   * the job that holds a warp's first item is found with ballots over 32
+//     jobs at a time instead of a serial search.
+// Blocks whose scale 2^(6 - e) leaves the FP32 range (largest magnitude below
+// 2^-120, or Inf/NaN) take the integer rules, as in k_quantize_planes.
+constexpr uint32_t kE2m1Warps = 8;
+constexpr uint32_t kE2m1Depth = 2;     // items in flight per warp
+constexpr uint32_t kE2m1Slot = 4096;   // bytes of one item
+constexpr uint32_t kE2m1Smem = 2048 + kE2m1Warps * kE2m1Depth * kE2m1Slot;  // tables, ring
 
-// The load side of a warp's walk over units: the lane's first element of
-// the current unit, for the cp.async staging.
-struct E2m1Loads {
+__device__ __forceinline__ uint32_t e2m1_pos(uint32_t c) { return c ^ ((c >> 3) & 7u); }
+
+// A warp's walk over items (job jx, row, group of four K steps).
+struct E2m1Walk {
   const float* x;
-  const float* src;
-  uint32_t ldx, cols, rows, k_steps;
-  uint32_t jx, row, step, col0;
-};
-
-// The store side: the current unit's activation block and the lane's
-// offsets in it (plane word, scale byte).
-struct E2m1Stores {
   uint8_t* tiles;
-  uint8_t* blk;
-  uint32_t rows, k_steps;
-  uint32_t jx, row, step, off, sf;
+  uint32_t ldx, cols, rows, k_steps, groups;
+  uint32_t jx, row, grp;
 };
 
-__device__ __forceinline__ void e2m1_loads_at(E2m1Loads& w, const QuantJob& j, uint32_t row,
-                                              uint32_t step) {
+__device__ __forceinline__ void e2m1_job(E2m1Walk& w, const QuantJob& j) {
   w.x = j.x;
+  w.tiles = j.tiles;
   w.ldx = j.ldx;
   w.cols = j.cols;
   w.rows = j.rows;
   w.k_steps = j.k_steps;
-  w.row = row;
-  w.step = step;
-  w.col0 = step * 256u;
-  w.src = j.x + static_cast<size_t>(row) * j.ldx + w.col0;
+  w.groups = (j.k_steps + 3u) / 4u;
 }
 
-template <uint32_t NT>
-__device__ __forceinline__ void e2m1_stores_row(E2m1Stores& w, uint32_t lane) {
-  const uint32_t r = w.row % NT;
-  w.blk = w.tiles + (static_cast<size_t>(w.row / NT) * w.k_steps + w.step) * mx_act_block_bytes(NT);
-  w.off = r * 128u + (((lane >> 2) ^ (r & 7u)) << 4) + (lane & 3u) * 4u;
-  const uint32_t p = lane & 3u;
-  w.sf = p < 3u ? mx_act_sf_offset(NT, p * NT + r, lane >> 2) : 0u;
-}
-
-template <uint32_t NT>
-__device__ __forceinline__ void e2m1_stores_at(E2m1Stores& w, const QuantJob& j, uint32_t row,
-                                               uint32_t step, uint32_t lane) {
-  w.tiles = j.tiles;
-  w.rows = j.rows;
-  w.k_steps = j.k_steps;
-  w.row = row;
-  w.step = step;
-  e2m1_stores_row<NT>(w, lane);
-}
-
-__device__ __forceinline__ void e2m1_loads_next(E2m1Loads& w, const QuantJob* jobs,
-                                                uint32_t njobs) {
-  w.col0 += 256u;
-  w.src += 256;
-  if (++w.step < w.k_steps) return;
-  uint32_t row = w.row + 1u;
-  if (row == w.rows && jobs != nullptr && w.jx + 1u < njobs) {
-    ++w.jx;
-    const QuantJob& j = jobs[w.jx];
-    w.x = j.x;
-    w.ldx = j.ldx;
-    w.cols = j.cols;
-    w.rows = j.rows;
-    w.k_steps = j.k_steps;
-    row = 0;
+__device__ __forceinline__ void e2m1_next(E2m1Walk& w, const QuantJob* jobs, uint32_t njobs) {
+  if (++w.grp < w.groups) return;
+  w.grp = 0;
+  if (++w.row == w.rows && jobs != nullptr && w.jx + 1u < njobs) {
+    e2m1_job(w, jobs[++w.jx]);
+    w.row = 0;
   }
-  w.row = row;
-  w.step = 0;
-  w.col0 = 0;
-  w.src = w.x + static_cast<size_t>(row) * w.ldx;
 }
 
-template <uint32_t NT>
-__device__ __forceinline__ void e2m1_stores_next(E2m1Stores& w, const QuantJob* jobs,
-                                                 uint32_t njobs, uint32_t lane) {
-  w.blk += mx_act_block_bytes(NT);
-  if (++w.step < w.k_steps) return;
-  uint32_t row = w.row + 1u;
-  if (row == w.rows && jobs != nullptr && w.jx + 1u < njobs) {
-    ++w.jx;
-    const QuantJob& j = jobs[w.jx];
-    w.tiles = j.tiles;
-    w.rows = j.rows;
-    w.k_steps = j.k_steps;
-    row = 0;
-  }
-  w.row = row;
-  w.step = 0;
-  if (row < w.rows) e2m1_stores_row<NT>(w, lane);
-}
-
-// A unit's 256 FP32 values into a 1 KB ring slot, copied by the whole warp
-// in two coalesced 16-byte copies per lane: lane l copies 16-byte chunks l
-// and 32 + l.  Chunk c lands at 16-byte position c ^ ((c >> 3) & 1) of the
-// slot, so that each lane later reads its own two chunks 2l, 2l + 1 (its
-// eight consecutive elements) without bank conflicts: within a quarter
-// warp the eight positions read together cover all eight 16-byte bank
-// groups.  Rows end with zero-filled chunks (16-byte aligned rows).
-__device__ __forceinline__ uint32_t e2m1_chunk_pos(uint32_t c) { return c ^ ((c >> 3) & 1u); }
-
-__device__ __forceinline__ void e2m1_stage(const E2m1Loads& w, uint32_t slot, uint32_t lane) {
-  const uint32_t d0 = slot + 16u * e2m1_chunk_pos(lane);
-  const uint32_t d1 = slot + 16u * e2m1_chunk_pos(32u + lane);
-  if (w.col0 + 256u <= w.cols) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n\t"
-                 "cp.async.cg.shared.global [%2], [%3], 16;" ::"r"(d0), "l"(w.src + 4u * lane),
-                 "r"(d1), "l"(w.src + 128u + 4u * lane)
-                 : "memory");
+// The item's 1024 values into a ring slot, zero past the row's end.
+__device__ __forceinline__ void e2m1_stage(const E2m1Walk& w, uint32_t slot, uint32_t lane) {
+  const uint32_t col0 = w.grp * 1024u;
+  const float* src = w.x + static_cast<size_t>(w.row) * w.ldx + col0;
+  if (col0 + 1024u <= w.cols) {
+#pragma unroll
+    for (uint32_t j = 0; j < 8; ++j) {
+      const uint32_t c = lane + 32u * j;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(slot + 16u * e2m1_pos(c)),
+                   "l"(src + 4u * c)
+                   : "memory");
+    }
   } else {
 #pragma unroll
-    for (uint32_t h = 0; h < 2; ++h) {
-      const uint32_t c = 32u * h + lane;
-      const uint32_t col = w.col0 + 4u * c;
+    for (uint32_t j = 0; j < 8; ++j) {
+      const uint32_t c = lane + 32u * j;
+      const uint32_t col = col0 + 4u * c;
       const uint32_t have = col < w.cols ? min(4u, w.cols - col) : 0u;
-      const float* from = have != 0 ? w.src + 4u * c : w.x;  // any valid address when empty
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(h == 0 ? d0 : d1),
+      const float* from = have != 0 ? src + 4u * c : w.x;  // any valid address when empty
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(slot + 16u * e2m1_pos(c)),
                    "l"(from), "r"(4u * have)
                    : "memory");
     }
   }
 }
 
+// Lane `lane`'s block of the item: its 32 values v into the three digit
+// planes and their scale bytes.
 template <uint32_t NT, bool kVec>
-__device__ __forceinline__ void e2m1_encode(const E2m1Stores& w, uint32_t v[8], uint32_t lane,
-                                            uint32_t sadd, uint32_t& bad, const uint8_t* lut) {
+__device__ __forceinline__ void e2m1_block(const E2m1Walk& w, uint32_t (&v)[32], uint32_t lane,
+                                           uint32_t& bad, const uint8_t* lut) {
   constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
   constexpr uint32_t kPlane = NT * 128u;
-  float m[4];
+  float m[16];
 #pragma unroll
-  for (uint32_t i = 0; i < 4; ++i) m[i] = max_nan_abs(v[2 * i], v[2 * i + 1]);
-  const uint32_t mb =
-      __float_as_uint(max_nan_abs(__float_as_uint(max_nan_abs(__float_as_uint(m[0]),
-                                                              __float_as_uint(m[1]))),
-                                  __float_as_uint(max_nan_abs(__float_as_uint(m[2]),
-                                                              __float_as_uint(m[3]))))) &
-      0x7FFFFFFFu;
+  for (uint32_t i = 0; i < 16; ++i) m[i] = max_nan_abs(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+  for (uint32_t s = 8; s >= 1; s /= 2) {
+#pragma unroll
+    for (uint32_t i = 0; i < s; ++i) m[i] = max_nan_abs(__float_as_uint(m[i]), __float_as_uint(m[i + s]));
+  }
+  const uint32_t mb = __float_as_uint(m[0]) & 0x7FFFFFFFu;
   // Host rule: the key is the largest magnitude (an Inf or NaN shows as a
   // key >= 0x7F800000); VEC rule: its exponent field, subnormals reading as
   // zero.
-  uint32_t key = kVec ? (mb >> 23) : mb;
-  key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 1));
-  key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, 2));
+  const uint32_t key = kVec ? (mb >> 23) : mb;
   if (!kVec) bad = max(bad, key);
-  const uint32_t field = kVec ? key : (key >> 23);
-  const uint32_t scale = key == 0 ? 127u : field;  // e = scale - 127
+  const uint32_t step = w.grp * 4u + (lane >> 3);
+  if (step >= w.k_steps) return;  // past the row's last K step: no operand block
+  const uint32_t scale = key == 0 ? 127u : (kVec ? key : (key >> 23));  // e = scale - 127
   if (kVec) {
 #pragma unroll
-    for (uint32_t i = 0; i < 8; ++i) {
+    for (uint32_t i = 0; i < 32; ++i) {
       if ((v[i] & 0x7F800000u) == 0) v[i] = 0;
     }
   }
-  uint32_t b[8];  // (q & 0xFF) * 4
-  uint8_t* blk = w.blk;
-  if (scale - 7u < 248u) {
-    // 7 <= scale <= 254: 2^(6 - e) = 2^(133 - scale) is a normal FP32.
-    const float sc = __uint_as_float((260u - scale) << 23);
-#pragma unroll
-    for (uint32_t i = 0; i < 8; ++i) {
-      // q >= -128 always; 128 clamps to 127.
-      b[i] = (__float_as_uint(fminf(__fmaf_rn(__uint_as_float(v[i]), sc, kMagic),
-                                    kMagic + 127.0f)) & 0xFFu) << 2;
-    }
-    if ((lane & 3u) < 3u) blk[w.sf] = static_cast<uint8_t>(scale + sadd);
-  } else {
-    // The planes' scales 2^(e - 6 + 3p) start below E8M0's 2^-127 when
-    // scale < 6: such a block is encoded as zero.
-    const int32_t e = static_cast<int32_t>(scale) - 127;
-#pragma unroll
-    for (uint32_t i = 0; i < 8; ++i) {
-      const int32_t q = scale < 6u ? 0
-                        : kVec     ? quantize_vec_rule(v[i], key)
-                                   : quantize_host_rule(v[i], e);
-      b[i] = (static_cast<uint32_t>(q) & 0xFFu) << 2;
-    }
-    if ((lane & 3u) < 3u) {
-      int32_t se = static_cast<int32_t>(scale + sadd);
-      se = se > 254 ? 254 : se;
-      blk[w.sf] = static_cast<uint8_t>(se < 0 ? 0 : se);
-    }
-  }
-  uint32_t pair[4];
+  const uint32_t r = w.row % NT, b = lane & 7u;
+  uint8_t* blk = w.tiles + (static_cast<size_t>(w.row / NT) * w.k_steps + step) * mx_act_block_bytes(NT);
+  const bool fast = scale - 7u < 248u;  // 7 <= scale <= 254: 2^(6 - e) is a normal FP32
+  const float sc = __uint_as_float((260u - scale) << 23);
+  const int32_t e = static_cast<int32_t>(scale) - 127;
+  uint32_t p0[4], p1[4], p2[4];
 #pragma unroll
   for (uint32_t k = 0; k < 4; ++k) {
-    pair[k] = *reinterpret_cast<const uint32_t*>(lut + b[2 * k]) |
-              *reinterpret_cast<const uint32_t*>(lut + 1024u + b[2 * k + 1]);
+    uint32_t o[8];  // (q & 0xFF) * 4 of elements 8 k .. 8 k + 7
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) {
+      const uint32_t x = v[8 * k + i];
+      int32_t q;
+      if (fast) {
+        // q >= -128 always; 128 clamps to 127.
+        q = static_cast<int32_t>(
+            __float_as_uint(fminf(__fmaf_rn(__uint_as_float(x), sc, kMagic), kMagic + 127.0f)));
+      } else {
+        // The planes' scales 2^(e - 6 + 3p) start below E8M0's 2^-127 when
+        // scale < 6: such a block is encoded as zero.
+        q = scale < 6u ? 0 : kVec ? quantize_vec_rule(x, key) : quantize_host_rule(x, e);
+      }
+      o[i] = (static_cast<uint32_t>(q) & 0xFFu) << 2;
+    }
+    uint32_t pair[4];
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      pair[j] = *reinterpret_cast<const uint32_t*>(lut + o[2 * j]) |
+                *reinterpret_cast<const uint32_t*>(lut + 1024u + o[2 * j + 1]);
+    }
+    const uint32_t a01 = __byte_perm(pair[0], pair[1], 0x5140u);  // p0: 0,4  p1: 1,5
+    const uint32_t a23 = __byte_perm(pair[2], pair[3], 0x5140u);
+    const uint32_t b01 = __byte_perm(pair[0], pair[1], 0x0062u);  // p2: 2,6
+    const uint32_t b23 = __byte_perm(pair[2], pair[3], 0x0062u);
+    p0[k] = __byte_perm(a01, a23, 0x5410u);
+    p1[k] = __byte_perm(a01, a23, 0x7632u);
+    p2[k] = __byte_perm(b01, b23, 0x5410u);
   }
-  const uint32_t a01 = __byte_perm(pair[0], pair[1], 0x5140u);  // p0: 0,4  p1: 1,5
-  const uint32_t a23 = __byte_perm(pair[2], pair[3], 0x5140u);
-  const uint32_t b01 = __byte_perm(pair[0], pair[1], 0x0062u);  // p2: 2,6
-  const uint32_t b23 = __byte_perm(pair[2], pair[3], 0x0062u);
-  uint8_t* out = blk + w.off;
-  *reinterpret_cast<uint32_t*>(out) = __byte_perm(a01, a23, 0x5410u);
-  *reinterpret_cast<uint32_t*>(out + kPlane) = __byte_perm(a01, a23, 0x7632u);
-  *reinterpret_cast<uint32_t*>(out + 2u * kPlane) = __byte_perm(b01, b23, 0x5410u);
+  uint8_t* out = blk + r * 128u + ((b ^ (r & 7u)) << 4);
+  *reinterpret_cast<uint4*>(out) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
+  *reinterpret_cast<uint4*>(out + kPlane) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+  *reinterpret_cast<uint4*>(out + 2u * kPlane) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
+#pragma unroll
+  for (uint32_t p = 0; p < 3; ++p) {
+    int32_t se = static_cast<int32_t>(scale) - 6 + 3 * static_cast<int32_t>(p);
+    if (!fast) se = se < 0 ? 0 : (se > 254 ? 254 : se);  // fast: always in [1, 254]
+    blk[mx_act_sf_offset(NT, p * NT + r, b)] = static_cast<uint8_t>(se);
+  }
 }
 
-// Units in flight per warp in the specialised encoder.
-constexpr uint32_t kE2m1Depth = 5;
-
 template <uint32_t NT, bool kVec>
-__global__ void __launch_bounds__(kPlaneWarps * 32)
+__global__ void __launch_bounds__(kE2m1Warps * 32)
 k_quantize_planes_e2m1(const QuantJob* jobs, uint32_t njobs,
                        const __grid_constant__ QuantJob inline_job, uint32_t* error_flag) {
-  __shared__ __align__(16) uint32_t ring[kPlaneWarps][kE2m1Depth][256];
+  extern __shared__ __align__(16) uint8_t e2m1_smem[];
   // Byte offset 4 (q & 0xFF): the E2M1 codes of q's digits d0, d1, d2 (q =
   // 64 d2 + 8 d1 + d0, d2 = RNE(q / 64), d1 = RNE((q - 64 d2) / 8)) in the
   // low nibbles of bytes 0, 1, 2; from byte 1024 on, the same in the high
-  // nibbles.
-  __shared__ __align__(16) uint32_t lut[512];
+  // nibbles.  Then the ring: per warp kE2m1Depth slots of one item.
+  uint32_t* lut = reinterpret_cast<uint32_t*>(e2m1_smem);
   {
     constexpr float kMagic = 12582912.0f;
     const float q = static_cast<float>(static_cast<int8_t>(threadIdx.x & 0xFFu));
@@ -845,46 +791,57 @@ k_quantize_planes_e2m1(const QuantJob* jobs, uint32_t njobs,
   sm100::griddep_launch_dependents();
   sm100::griddep_wait();
   const uint32_t lane = threadIdx.x & 31u, wib = threadIdx.x >> 5;
-  const uint32_t warp = blockIdx.x * kPlaneWarps + wib;
-  const uint32_t nwarps = gridDim.x * kPlaneWarps;
-  const uint64_t base = jobs != nullptr ? jobs[0].unit_begin : 0;
-  const uint64_t total = jobs != nullptr
-                             ? jobs[njobs - 1].unit_begin + jobs[njobs - 1].units - base
-                             : inline_job.units;
+  const uint32_t warp = blockIdx.x * kE2m1Warps + wib;
+  const uint32_t nwarps = gridDim.x * kE2m1Warps;
+  const uint64_t base = jobs != nullptr ? jobs[0].group_begin : 0;
+  uint64_t total;
+  if (jobs != nullptr) {
+    const QuantJob& last = jobs[njobs - 1];
+    total = last.group_begin + static_cast<uint64_t>(last.rows) * ((last.k_steps + 3u) / 4u) - base;
+  } else {
+    total = static_cast<uint64_t>(inline_job.rows) * ((inline_job.k_steps + 3u) / 4u);
+  }
   const uint64_t per = (total + nwarps - 1) / nwarps;
   const uint64_t begin = base + static_cast<uint64_t>(warp) * per;
   const uint64_t end = begin + per < base + total ? begin + per : base + total;
   if (begin >= end) return;
   const uint32_t count = static_cast<uint32_t>(end - begin);
+  // The job of the first item: the last job starting at or before it,
+  // narrowed 32 jobs a ballot.
   uint32_t jx = 0;
   if (jobs != nullptr) {
-    uint32_t lo = 0, hi = njobs - 1;
-    while (lo < hi) {
-      const uint32_t mid = (lo + hi + 1) >> 1;
-      if (jobs[mid].unit_begin <= begin) lo = mid; else hi = mid - 1;
+    uint32_t lo = 0, span = njobs;
+    while (span > 1) {
+      const uint32_t stride = (span + 31u) / 32u;
+      const bool in = lane * stride < span;
+      const bool le = in && jobs[lo + lane * stride].group_begin <= begin;
+      const uint32_t k = 31u - __clz(__ballot_sync(0xFFFFFFFFu, le));  // lane 0 always holds
+      lo += k * stride;
+      span = min(stride, span - k * stride);
     }
     jx = lo;
   }
+  E2m1Walk w;
   const QuantJob& j0 = jobs != nullptr ? jobs[jx] : inline_job;
-  const uint32_t u = static_cast<uint32_t>(begin - j0.unit_begin);
-  E2m1Loads ld;
-  E2m1Stores st;
-  ld.jx = st.jx = jx;
-  e2m1_loads_at(ld, j0, u / j0.k_steps, u % j0.k_steps);
-  e2m1_stores_at<NT>(st, j0, u / j0.k_steps, u % j0.k_steps, lane);
-  const uint32_t sadd = 3u * (lane & 3u) - 6u;  // plane p's scale: scale - 6 + 3p
-  const uint8_t* lutb = reinterpret_cast<const uint8_t*>(lut);
+  e2m1_job(w, j0);
+  w.jx = jx;
+  {
+    const uint32_t u = static_cast<uint32_t>(begin - j0.group_begin);
+    w.row = u / w.groups;
+    w.grp = u % w.groups;
+  }
+  E2m1Walk ld = w;
+  const uint8_t* lutb = e2m1_smem;
+  uint8_t* ring = e2m1_smem + 2048 + wib * kE2m1Depth * kE2m1Slot;
+  const uint32_t mine = static_cast<uint32_t>(__cvta_generic_to_shared(ring));
   uint32_t bad = 0;
-  const uint32_t mine = static_cast<uint32_t>(__cvta_generic_to_shared(&ring[wib][0][0]));
-  // This lane's eight elements in a slot: chunks 2 lane and 2 lane + 1.
-  const uint32_t r0 = 4u * e2m1_chunk_pos(2u * lane), r1 = 4u * e2m1_chunk_pos(2u * lane + 1u);
-  // One commit group per unit slot, empty past the range, so that
+  // One commit group per slot use, empty past the range, so that
   // wait_group(kE2m1Depth - 1) always means "the oldest has landed".
 #pragma unroll
   for (uint32_t d = 0; d < kE2m1Depth; ++d) {
     if (d < count) {
-      e2m1_stage(ld, mine + d * 1024u, lane);
-      e2m1_loads_next(ld, jobs, njobs);
+      e2m1_stage(ld, mine + d * kE2m1Slot, lane);
+      e2m1_next(ld, jobs, njobs);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
@@ -895,17 +852,24 @@ k_quantize_planes_e2m1(const QuantJob* jobs, uint32_t njobs,
       if (i < count) {
         asm volatile("cp.async.wait_group %0;" ::"n"(kE2m1Depth - 1) : "memory");
         __syncwarp();  // the slot was filled by every lane's copies
-        const uint32_t* slot = &ring[wib][d][0];
-        const uint4 lo = *reinterpret_cast<const uint4*>(slot + r0);
-        const uint4 hi = *reinterpret_cast<const uint4*>(slot + r1);
-        uint32_t v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-        __syncwarp();  // every lane has read the slot before it is refilled
-        e2m1_encode<NT, kVec>(st, v, lane, sadd, bad, lutb);
-        e2m1_stores_next<NT>(st, jobs, njobs, lane);
-        if (i + kE2m1Depth < count) {
-          e2m1_stage(ld, mine + d * 1024u, lane);
-          e2m1_loads_next(ld, jobs, njobs);
+        const uint8_t* slot = ring + d * kE2m1Slot;
+        uint32_t v[32];
+#pragma unroll
+        for (uint32_t j = 0; j < 8; ++j) {
+          const uint4 t =
+              *reinterpret_cast<const uint4*>(slot + 16u * (8u * lane + (j ^ (lane & 7u))));
+          v[4 * j] = t.x;
+          v[4 * j + 1] = t.y;
+          v[4 * j + 2] = t.z;
+          v[4 * j + 3] = t.w;
         }
+        __syncwarp();  // every lane has read the slot before it is refilled
+        if (i + kE2m1Depth < count) {
+          e2m1_stage(ld, mine + d * kE2m1Slot, lane);
+          e2m1_next(ld, jobs, njobs);
+        }
+        e2m1_block<NT, kVec>(w, v, lane, bad, lutb);
+        e2m1_next(w, jobs, njobs);
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
     }
@@ -949,10 +913,10 @@ uint32_t planes_variant(const QuantJob* jobs, uint32_t n) {
 }
 
 template <typename K>
-int occupancy_of(K kernel) {
+int occupancy_of(K kernel, uint32_t threads, uint32_t smem) {
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kPlaneWarps * 32, 0) !=
-          cudaSuccess || n < 1) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess ||
+      n < 1) {
     n = 1;
   }
   return n;
@@ -963,24 +927,36 @@ int occupancy_of(K kernel) {
 void launch_quantize_planes(const QuantJob* jobs_dev, uint32_t njobs, const QuantJob* inline_job,
                             uint64_t total_units, uint32_t* error_flag, int sm_count,
                             cudaStream_t stream, const QuantJob* jobs_host) {
-  const uint32_t variant =
-      inline_job != nullptr ? planes_variant(inline_job, 1) : planes_variant(jobs_host, njobs);
+  const QuantJob* host = inline_job != nullptr ? inline_job : jobs_host;
+  const uint32_t n = inline_job != nullptr ? 1u : njobs;
+  const uint32_t variant = planes_variant(host, n);
   using Fn = void (*)(const QuantJob*, uint32_t, const QuantJob, uint32_t*);
   static const Fn kFns[5] = {k_quantize_planes, k_quantize_planes_e2m1<64, false>,
                              k_quantize_planes_e2m1<64, true>, k_quantize_planes_e2m1<128, false>,
                              k_quantize_planes_e2m1<128, true>};
+  const uint32_t warps = variant == 0 ? kPlaneWarps : kE2m1Warps;
+  const uint32_t smem = variant == 0 ? 0u : kE2m1Smem;
+  if (smem != 0 && !set_smem_limit_once(reinterpret_cast<const void*>(kFns[variant]), smem)) {
+    return;  // the launch error surfaces through cudaGetLastError
+  }
+  // Work units: (row, 256-element step) for the general kernel, (row, group
+  // of four steps) for the specialised one.
+  uint64_t units = total_units;
+  if (variant != 0) {
+    units = 0;
+    for (uint32_t i = 0; i < n; ++i) units += uint64_t{host[i].rows} * ((host[i].k_steps + 3u) / 4u);
+  }
   // As many CTAs as fit at once (no second wave); each warp takes a
   // contiguous range of at least a few units.
   static int per_sm[5] = {0, 0, 0, 0, 0};
-  if (per_sm[variant] == 0) per_sm[variant] = occupancy_of(kFns[variant]);
-  // Four units a warp or more when that fills the GPU; a smaller job (a few
+  if (per_sm[variant] == 0) per_sm[variant] = occupancy_of(kFns[variant], warps * 32u, smem);
+  // Several units a warp when that fills the GPU; a smaller job (a few
   // hundred rows) spreads down to one unit a warp, so a warp waits for one
-  // load, not four in a row.
-  uint64_t blocks = (total_units + 4 * kPlaneWarps - 1) / (4 * kPlaneWarps);
+  // load, not several in a row.
+  const uint64_t each = variant == 0 ? 4u : 2u;
+  uint64_t blocks = (units + each * warps - 1) / (each * warps);
   const uint64_t cap = static_cast<uint64_t>(sm_count) * per_sm[variant];
-  if (blocks < cap) {
-    blocks = std::min<uint64_t>(cap, (total_units + kPlaneWarps - 1) / kPlaneWarps);
-  }
+  if (blocks < cap) blocks = std::min<uint64_t>(cap, (units + warps - 1) / warps);
   if (blocks > cap) blocks = cap;
   if (blocks == 0) blocks = 1;
   QuantJob one{};
@@ -989,7 +965,8 @@ void launch_quantize_planes(const QuantJob* jobs_dev, uint32_t njobs, const Quan
   // before it touches memory.
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(blocks));
-  cfg.blockDim = dim3(kPlaneWarps * 32);
+  cfg.blockDim = dim3(warps * 32u);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
