@@ -679,6 +679,19 @@ __device__ __forceinline__ void e2m1_stage(const E2m1Walk& w, uint32_t slot, uin
   }
 }
 
+// The integer rules for one element of a block whose scale 2^(6 - e) leaves
+// the FP32 range: (q & 0xFF) * 4.  Out of line: it is rare, and inlined for
+// each element it would crowd the instruction cache.  The planes' scales
+// 2^(e - 6 + 3p) start below E8M0's 2^-127 when scale < 6: such a block is
+// encoded as zero.
+template <bool kVec>
+__device__ __noinline__ uint32_t e2m1_slow_code(uint32_t x, uint32_t key, uint32_t scale) {
+  const int32_t q = scale < 6u ? 0
+                    : kVec     ? quantize_vec_rule(x, key)
+                               : quantize_host_rule(x, static_cast<int32_t>(scale) - 127);
+  return (static_cast<uint32_t>(q) & 0xFFu) << 2;
+}
+
 // Lane `lane`'s block of the item: its 32 values v into the three digit
 // planes and their scale bytes.
 template <uint32_t NT, bool kVec>
@@ -712,32 +725,27 @@ __device__ __forceinline__ void e2m1_block(const E2m1Walk& w, uint32_t (&v)[32],
   const uint32_t r = w.row % NT, b = lane & 7u;
   uint8_t* blk = w.tiles + (static_cast<size_t>(w.row / NT) * w.k_steps + step) * mx_act_block_bytes(NT);
   const bool fast = scale - 7u < 248u;  // 7 <= scale <= 254: 2^(6 - e) is a normal FP32
-  const float sc = __uint_as_float((260u - scale) << 23);
-  const int32_t e = static_cast<int32_t>(scale) - 127;
+  // v[i] becomes (q & 0xFF) * 4.
+  if (fast) {
+    const float sc = __uint_as_float((260u - scale) << 23);
+#pragma unroll
+    for (uint32_t i = 0; i < 32; ++i) {
+      // q >= -128 always; 128 clamps to 127.
+      v[i] = (__float_as_uint(fminf(__fmaf_rn(__uint_as_float(v[i]), sc, kMagic),
+                                    kMagic + 127.0f)) & 0xFFu) << 2;
+    }
+  } else {
+#pragma unroll
+    for (uint32_t i = 0; i < 32; ++i) v[i] = e2m1_slow_code<kVec>(v[i], key, scale);
+  }
   uint32_t p0[4], p1[4], p2[4];
 #pragma unroll
   for (uint32_t k = 0; k < 4; ++k) {
-    uint32_t o[8];  // (q & 0xFF) * 4 of elements 8 k .. 8 k + 7
-#pragma unroll
-    for (uint32_t i = 0; i < 8; ++i) {
-      const uint32_t x = v[8 * k + i];
-      int32_t q;
-      if (fast) {
-        // q >= -128 always; 128 clamps to 127.
-        q = static_cast<int32_t>(
-            __float_as_uint(fminf(__fmaf_rn(__uint_as_float(x), sc, kMagic), kMagic + 127.0f)));
-      } else {
-        // The planes' scales 2^(e - 6 + 3p) start below E8M0's 2^-127 when
-        // scale < 6: such a block is encoded as zero.
-        q = scale < 6u ? 0 : kVec ? quantize_vec_rule(x, key) : quantize_host_rule(x, e);
-      }
-      o[i] = (static_cast<uint32_t>(q) & 0xFFu) << 2;
-    }
     uint32_t pair[4];
 #pragma unroll
     for (uint32_t j = 0; j < 4; ++j) {
-      pair[j] = *reinterpret_cast<const uint32_t*>(lut + o[2 * j]) |
-                *reinterpret_cast<const uint32_t*>(lut + 1024u + o[2 * j + 1]);
+      pair[j] = *reinterpret_cast<const uint32_t*>(lut + v[8 * k + 2 * j]) |
+                *reinterpret_cast<const uint32_t*>(lut + 1024u + v[8 * k + 2 * j + 1]);
     }
     const uint32_t a01 = __byte_perm(pair[0], pair[1], 0x5140u);  // p0: 0,4  p1: 1,5
     const uint32_t a23 = __byte_perm(pair[2], pair[3], 0x5140u);
@@ -760,7 +768,7 @@ __device__ __forceinline__ void e2m1_block(const E2m1Walk& w, uint32_t (&v)[32],
 }
 
 template <uint32_t NT, bool kVec>
-__global__ void __launch_bounds__(kE2m1Warps * 32)
+__global__ void __launch_bounds__(kE2m1Warps * 32, 3)
 k_quantize_planes_e2m1(const QuantJob* jobs, uint32_t njobs,
                        const __grid_constant__ QuantJob inline_job, uint32_t* error_flag) {
   extern __shared__ __align__(16) uint8_t e2m1_smem[];
@@ -845,34 +853,29 @@ k_quantize_planes_e2m1(const QuantJob* jobs, uint32_t njobs,
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
-  for (uint32_t i0 = 0; i0 < count; i0 += kE2m1Depth) {
+#pragma unroll 1
+  for (uint32_t i = 0; i < count; ++i) {
+    const uint32_t d = i % kE2m1Depth;
+    asm volatile("cp.async.wait_group %0;" ::"n"(kE2m1Depth - 1) : "memory");
+    __syncwarp();  // the slot was filled by every lane's copies
+    const uint8_t* slot = ring + d * kE2m1Slot;
+    uint32_t v[32];
 #pragma unroll
-    for (uint32_t d = 0; d < kE2m1Depth; ++d) {
-      const uint32_t i = i0 + d;
-      if (i < count) {
-        asm volatile("cp.async.wait_group %0;" ::"n"(kE2m1Depth - 1) : "memory");
-        __syncwarp();  // the slot was filled by every lane's copies
-        const uint8_t* slot = ring + d * kE2m1Slot;
-        uint32_t v[32];
-#pragma unroll
-        for (uint32_t j = 0; j < 8; ++j) {
-          const uint4 t =
-              *reinterpret_cast<const uint4*>(slot + 16u * (8u * lane + (j ^ (lane & 7u))));
-          v[4 * j] = t.x;
-          v[4 * j + 1] = t.y;
-          v[4 * j + 2] = t.z;
-          v[4 * j + 3] = t.w;
-        }
-        __syncwarp();  // every lane has read the slot before it is refilled
-        if (i + kE2m1Depth < count) {
-          e2m1_stage(ld, mine + d * kE2m1Slot, lane);
-          e2m1_next(ld, jobs, njobs);
-        }
-        e2m1_block<NT, kVec>(w, v, lane, bad, lutb);
-        e2m1_next(w, jobs, njobs);
-      }
-      asm volatile("cp.async.commit_group;" ::: "memory");
+    for (uint32_t j = 0; j < 8; ++j) {
+      const uint4 t = *reinterpret_cast<const uint4*>(slot + 16u * (8u * lane + (j ^ (lane & 7u))));
+      v[4 * j] = t.x;
+      v[4 * j + 1] = t.y;
+      v[4 * j + 2] = t.z;
+      v[4 * j + 3] = t.w;
     }
+    __syncwarp();  // every lane has read the slot before it is refilled
+    if (i + kE2m1Depth < count) {
+      e2m1_stage(ld, mine + d * kE2m1Slot, lane);
+      e2m1_next(ld, jobs, njobs);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    e2m1_block<NT, kVec>(w, v, lane, bad, lutb);
+    e2m1_next(w, jobs, njobs);
   }
   if (!kVec && __any_sync(0xFFFFFFFFu, bad >= 0x7F800000u) && lane == 0) atomicOr(error_flag, 1u);
 }
