@@ -336,57 +336,66 @@ __device__ __forceinline__ void requant_rows(const MxTile& ti, const float (&x)[
   if (bad && lane == 0) atomicOr(err, 1u);
 }
 
-// One epilogue warp's share of a finished tile: token rows [r0, r1) of the
-// warp's 32 weight columns (TMEM lane quarter sp).  The accumulator holds
+// One epilogue warp's view of a finished tile: its 32 weight columns (TMEM
+// lane quarter sp) with the tile's epilogue fields.  The accumulator holds
 // kSums partial sums per output (the digit-plane products, at TMEM columns
-// taddr, taddr + NT, taddr + 2 NT), added smallest scale first; then C (with
-// accumulate), the column scale, the bias and RELU, and the stores: C, the
-// peers' copies of C and the MXINT8 copy.
+// taddr, taddr + NT, taddr + 2 NT), added smallest scale first (load); then
+// C (with accumulate), the column scale, the bias and RELU, and the stores:
+// C, the peers' copies of C and the MXINT8 copy (finish).
 //
 // With `stage` (512 bytes of shared memory for this warp), a full chunk of
 // 16 rows x 32 columns of an output without accumulate, C and the peers'
 // copies 16-byte aligned, is regrouped through shared memory, four rows at a
 // time, into 16-byte stores (local, then each peer): lane l writes row l / 8,
 // columns 4 (l % 8) .. + 3.
-//
-// With `release` and 32 rows for this warp, both chunks are read out of TMEM
-// first and the accumulator is released (an arrival on `release`) before
-// the stores, so the next tile's MMAs overlap them; returns whether it was.
-template <uint32_t NT, uint32_t kSums, bool kEarly = false>
-__device__ __forceinline__ bool drain_tile(const MxParams& p, const MxTile& ti, uint32_t taddr,
-                                           uint32_t r0, uint32_t r1, uint32_t sp, uint32_t lane,
-                                           float* stage = nullptr, uint64_t* release = nullptr) {
-  const uint32_t col = sp * 32u + lane;
-  const uint32_t cols = ti.cols_kbq & 0xFFu, kbq = ti.cols_kbq >> 8;
-  const bool col_ok = col < cols;
-  const bool acc = (ti.flags >> 31) != 0;
-  const bool relu = ((ti.flags >> 29) & 1u) != 0;
-  const bool scaled = ((ti.flags >> 28) & 1u) != 0;
-  float bias = 0.0f, scale = 1.0f;
-  if (ti.bias != nullptr && col_ok) {
-    if (scaled) {
-      const float2 sb = reinterpret_cast<const float2*>(ti.bias)[col];
-      scale = sb.x;
-      bias = sb.y;
-    } else {
-      bias = ti.bias[col];
+template <uint32_t NT, uint32_t kSums>
+struct TileDrain {
+  const MxParams& p;
+  const MxTile& ti;
+  uint32_t taddr, sp, lane;
+  float* stage;
+  uint32_t col, cols, kbq, npeers;
+  bool col_ok, acc, relu, scaled, requant, staged;
+  float bias, scale;
+  float* cbase;
+
+  __device__ __forceinline__ TileDrain(const MxParams& p_, const MxTile& ti_, uint32_t taddr_,
+                                       uint32_t sp_, uint32_t lane_, float* stage_)
+      : p(p_), ti(ti_), taddr(taddr_), sp(sp_), lane(lane_), stage(stage_) {
+    col = sp * 32u + lane;
+    cols = ti.cols_kbq & 0xFFu;
+    kbq = ti.cols_kbq >> 8;
+    col_ok = col < cols;
+    acc = (ti.flags >> 31) != 0;
+    relu = ((ti.flags >> 29) & 1u) != 0;
+    scaled = ((ti.flags >> 28) & 1u) != 0;
+    bias = 0.0f;
+    scale = 1.0f;
+    if (ti.bias != nullptr && col_ok) {
+      if (scaled) {
+        const float2 sb = reinterpret_cast<const float2*>(ti.bias)[col];
+        scale = sb.x;
+        bias = sb.y;
+      } else {
+        bias = ti.bias[col];
+      }
     }
+    cbase = ti.c + col;
+    npeers = p.peers.count;
+    // The MXINT8 copy: this warp's 32 columns are one block of the next
+    // layer's K (tiles start on 128-column boundaries); the block exists
+    // when it starts before column N.
+    requant = ti.cq != nullptr && sp * 32u < cols;
+    // Peers' copies (the fused all-gather) take the same 16-byte stores when
+    // every peer buffer sits at a 16-byte multiple from the local one.
+    bool peers16 = true;
+    for (uint32_t q = 0; q < npeers; ++q) peers16 &= (p.peers.delta[q] & 15) == 0;
+    staged = stage != nullptr && !acc && peers16 && ti.c != nullptr && cols == kTileW &&
+             (ti.ldc & 3u) == 0 && (reinterpret_cast<uintptr_t>(ti.c) & 15u) == 0;
   }
-  float* cbase = ti.c + col;
-  const uint32_t npeers = p.peers.count;
-  // The MXINT8 copy: this warp's 32 columns are one block of the next
-  // layer's K (tiles start on 128-column boundaries); the block exists when
-  // it starts before column N.
-  const bool requant = ti.cq != nullptr && sp * 32u < cols;
-  // Peers' copies (the fused all-gather) take the same 16-byte stores when
-  // every peer buffer sits at a 16-byte multiple from the local one.
-  bool peers16 = true;
-  for (uint32_t q = 0; q < npeers; ++q) peers16 &= (p.peers.delta[q] & 15) == 0;
-  const bool staged = stage != nullptr && !acc && peers16 && ti.c != nullptr &&
-                      cols == kTileW && (ti.ldc & 3u) == 0 &&
-                      (reinterpret_cast<uintptr_t>(ti.c) & 15u) == 0;
+
   // The plane sums of rows j0 .. j0 + 15 out of TMEM.
-  const auto load = [&](uint32_t j0, float (&x)[16]) {
+  __device__ __forceinline__ void load(uint32_t j0, float (&x)[16]) const {
     uint32_t v0[16], v1[16], v2[16];
     tmem_ld16(taddr + j0, v0);
     if constexpr (kSums > 1) tmem_ld16(taddr + NT + j0, v1);
@@ -398,9 +407,10 @@ __device__ __forceinline__ bool drain_tile(const MxParams& p, const MxTile& ti, 
       if constexpr (kSums > 1) x[j] = x[j] + __uint_as_float(v1[j]);
       if constexpr (kSums > 2) x[j] += __uint_as_float(v2[j]);
     }
-  };
-  // Accumulate, scale, bias, RELU and the stores of those rows.
-  const auto finish = [&](uint32_t j0, float (&x)[16]) {
+  }
+
+  // Accumulate, scale, bias, RELU and the stores of rows j0 .. j0 + 15.
+  __device__ __forceinline__ void finish(uint32_t j0, float (&x)[16]) const {
     if (staged && j0 + 16u <= ti.rows) {
 #pragma unroll
       for (uint32_t j = 0; j < 16; ++j) {
@@ -450,24 +460,36 @@ __device__ __forceinline__ bool drain_tile(const MxParams& p, const MxTile& ti, 
       }
     }
     if (requant) requant_rows(ti, x, j0, sp, lane, col_ok, kbq, p.err, p.peers);
-  };
+  }
+};
+
+// One epilogue warp's share of a finished tile: token rows [r0, r1) of the
+// warp's 32 weight columns (TileDrain).  With `release` and 32 rows for this
+// warp, both chunks are read out of TMEM first and the accumulator is
+// released (an arrival on `release`) before the stores, so the next tile's
+// MMAs overlap them; returns whether it was.
+template <uint32_t NT, uint32_t kSums, bool kEarly = false>
+__device__ __forceinline__ bool drain_tile(const MxParams& p, const MxTile& ti, uint32_t taddr,
+                                           uint32_t r0, uint32_t r1, uint32_t sp, uint32_t lane,
+                                           float* stage = nullptr, uint64_t* release = nullptr) {
+  const TileDrain<NT, kSums> d(p, ti, taddr, sp, lane, stage);
   if constexpr (kEarly) {
     if (release != nullptr && r1 - r0 == 32u) {
       float xa[16], xb[16];
-      load(r0, xa);
-      load(r0 + 16u, xb);
+      d.load(r0, xa);
+      d.load(r0 + 16u, xb);
       tc_fence_before();
       mbar_arrive(release);
-      finish(r0, xa);
-      finish(r0 + 16u, xb);
+      d.finish(r0, xa);
+      d.finish(r0 + 16u, xb);
       return true;
     }
   }
 #pragma unroll 1
   for (uint32_t j0 = r0; j0 < r1; j0 += 16) {
     float x[16];
-    load(j0, x);
-    finish(j0, x);
+    d.load(j0, x);
+    d.finish(j0, x);
   }
   return false;
 }
