@@ -807,34 +807,26 @@ __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
 // A unit of work is a pair: tiles 2u and 2u + 1 of the launch's tile array,
 // whose second tile may be absent (w = null, a GEMM with an odd number of
 // column tiles); the tile array of a pair launch is laid out that way
-// (mx_fill_pair_tiles).  Weights and activations stream through rings of
-// their own, so that the weight stream from HBM (whose latency sets how much
-// must be in flight) keeps four K steps ahead while the activation blocks
-// come from L2: warp 0 streams weights (and, with a plan's weights, never
-// waits on the kernel before), warp 2 activation blocks, warp 1 owns TMEM
-// and issues MMAs, warps 3 .. 10 drain.
+// (mx_fill_pair_tiles).  Same warps and rings as k_gemm_mxf4: warp 0
+// streams stages, warp 1 owns TMEM and issues MMAs, warps 2 .. 9 drain.
 struct PairCfg {
   static constexpr uint32_t NT = 64;
   static constexpr uint32_t kABlock = mx_act_block_bytes(NT);          // 26624
-  static constexpr uint32_t kWSlot = 2 * kWChunk;                       // 34816: both weight chunks
-  static constexpr uint32_t kASlots = 3;
+  static constexpr uint32_t kSlot = 2 * kWChunk + kABlock;              // 61440
   static constexpr uint32_t kEpiWarps = 8;
   static constexpr uint32_t kStage = 512u * kEpiWarps;                  // store regrouping
-  static constexpr uint32_t kOffW = kASlots * kABlock;
-  static constexpr uint32_t kWSlots = (kSmemLimit - 1024 - 512 - kStage - kOffW) / kWSlot;
-  static constexpr uint32_t kOffBar = kOffW + kWSlots * kWSlot;
+  static constexpr uint32_t kSlots = (kSmemLimit - 1024 - 512 - kStage) / kSlot;
+  static constexpr uint32_t kOffBar = kSlots * kSlot;
   static constexpr uint32_t kOffStage = kOffBar + 512;
   static constexpr uint32_t kSmem = kOffStage + kStage + 1024;
   static constexpr uint32_t kDCols = 3 * NT;          // three plane sums of 64 tokens
   static constexpr uint32_t kColSfa = 2 * kDCols;     // weight scales: 8 columns a tile
   static constexpr uint32_t kColSfb = kColSfa + 16;   // activation scales: 4 chunks
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kFirstEpi = 3;            // 0 weights, 1 MMA, 2 activations
-  static constexpr uint32_t kThreads = 32u * (kFirstEpi + kEpiWarps);
-  static_assert(kWSlots >= 3, "weight ring");
+  static constexpr uint32_t kThreads = 32u * (2u + kEpiWarps);
+  static_assert(kSlots >= 2, "pair ring");
   static_assert(kColSfb + 16 <= kTmemCols, "TMEM columns");
-  static_assert(kABlock % 1024 == 0 && kWSlot % 1024 == 0 && kSmem <= kSmemLimit,
-                "shared memory");
+  static_assert(kSlot % 1024 == 0 && kSmem <= kSmemLimit, "shared memory");
   static_assert(mx_parts(NT) == 1, "one stacked MMA of 192 rows a K slice");
 };
 
@@ -868,23 +860,16 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1) k_gemm_mxf4_pair(const _
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
-  const Ring aring{bars, bars + Cfg::kASlots, Cfg::kASlots};
-  const Ring wring{bars + 2 * Cfg::kASlots, bars + 2 * Cfg::kASlots + Cfg::kWSlots, Cfg::kWSlots};
-  uint64_t* acc_full = bars + 2 * (Cfg::kASlots + Cfg::kWSlots);  // both accumulators ready
+  const Ring ring{bars, bars + Cfg::kSlots, Cfg::kSlots};
+  uint64_t* acc_full = bars + 2 * Cfg::kSlots;   // both accumulators ready
   uint64_t* acc_empty = acc_full + 1;            // both read out (every epilogue thread)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
-  uint8_t* abase = smem;
-  uint8_t* wbase = smem + Cfg::kOffW;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
 
   if (threadIdx.x == 0) {
-    for (uint32_t s = 0; s < Cfg::kASlots; ++s) {
-      mbar_init(&aring.full[s], 1);
-      mbar_init(&aring.empty[s], 1);
-    }
-    for (uint32_t s = 0; s < Cfg::kWSlots; ++s) {
-      mbar_init(&wring.full[s], 1);
-      mbar_init(&wring.empty[s], 1);
+    for (uint32_t s = 0; s < Cfg::kSlots; ++s) {
+      mbar_init(&ring.full[s], 1);
+      mbar_init(&ring.empty[s], 1);
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 32 * Cfg::kEpiWarps);
@@ -899,18 +884,14 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1) k_gemm_mxf4_pair(const _
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
-  // With ready weights (a plan's) the weight producer reads nothing the
-  // kernel before may write, and does not wait for it.
+  // As in k_gemm_mxf4: with ready weights the producer streams the weight
+  // halves of its first stages before the dependency wait.
   griddep_launch_dependents();
   const bool early_weights = p.weights_ready != 0 && warp == 0;
   if (!early_weights) griddep_wait();
 
-  if (warp == 0 || warp == 2) {
-    // Warp 0 lane 0 streams both weight chunks of each step, warp 2 lane 0
-    // the activation block; each tile pair's fields are loaded a pair ahead.
+  if (warp == 0) {
     if (lane == 0) {
-      const bool weights = warp == 0;
-      const Ring& ring = weights ? wring : aring;
       uint32_t n = 0;  // uses of the ring so far
       MxTile na, nb;
       bool nh;
@@ -920,23 +901,35 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1) k_gemm_mxf4_pair(const _
         const bool hb = nh;
         if (u + gridDim.x < p.total_tiles) pair_info(p, u + gridDim.x, na, nb, nh);
         const uint32_t k_steps = a.flags & 0x0FFFFFFFu;
+        const uint32_t bytes = (hb ? 2u : 1u) * kWChunk + Cfg::kABlock;
+        uint32_t pre = 0;  // stages whose weights went out before the wait
+        if (early_weights && n == 0) {
+          pre = k_steps < ring.slots ? k_steps : ring.slots;
+          for (uint32_t c = 0; c < pre; ++c) {
+            uint8_t* slot = smem + c * Cfg::kSlot;
+            mbar_arrive_expect_tx(&ring.full[c], bytes);
+            bulk_g2s(slot, a.w + static_cast<size_t>(c) * kWChunk, kWChunk, &ring.full[c]);
+            if (hb) {
+              bulk_g2s(slot + kWChunk, b.w + static_cast<size_t>(c) * kWChunk, kWChunk,
+                       &ring.full[c]);
+            }
+          }
+          griddep_wait();
+        }
         for (uint32_t c = 0; c < k_steps && ok; ++c, ++n) {
           const uint32_t sl = n % ring.slots;
-          if (weights) {
-            ok = ring_acquire(ring, n, (hb ? 2u : 1u) * kWChunk, p.err);
+          uint8_t* slot = smem + sl * Cfg::kSlot;
+          if (c >= pre) {
+            ok = ring_acquire(ring, n, bytes, p.err);
             if (!ok) break;
-            uint8_t* slot = wbase + sl * Cfg::kWSlot;
             bulk_g2s(slot, a.w + static_cast<size_t>(c) * kWChunk, kWChunk, &ring.full[sl]);
             if (hb) {
               bulk_g2s(slot + kWChunk, b.w + static_cast<size_t>(c) * kWChunk, kWChunk,
                        &ring.full[sl]);
             }
-          } else {
-            ok = ring_acquire(ring, n, Cfg::kABlock, p.err);
-            if (!ok) break;
-            bulk_g2s(abase + sl * Cfg::kABlock, a.a + static_cast<size_t>(c) * Cfg::kABlock,
-                     Cfg::kABlock, &ring.full[sl]);
           }
+          bulk_g2s(slot + 2 * kWChunk, a.a + static_cast<size_t>(c) * Cfg::kABlock, Cfg::kABlock,
+                   &ring.full[sl]);
         }
       }
       if (ok) ring_drain(ring, n, p.err);
@@ -956,14 +949,13 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1) k_gemm_mxf4_pair(const _
         if (!ok) break;
         tc_fence_after();
         for (uint32_t i = 0; i < k_steps && ok; ++i, ++n) {
-          const uint32_t as = n % aring.slots, ws = n % wring.slots;
-          ok = mbar_wait(&aring.full[as], (n / aring.slots) & 1u, p.err) &&
-               mbar_wait(&wring.full[ws], (n / wring.slots) & 1u, p.err);
+          const uint32_t sl = n % ring.slots;
+          ok = mbar_wait(&ring.full[sl], (n / ring.slots) & 1u, p.err);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t wa = smem_addr(wbase + ws * Cfg::kWSlot);
+          const uint32_t wa = smem_addr(smem + sl * Cfg::kSlot);
           const uint32_t wb = wa + kWChunk;
-          const uint32_t act = smem_addr(abase + as * Cfg::kABlock);
+          const uint32_t act = wa + 2 * kWChunk;
           const uint32_t a_sf = act + 3 * Cfg::NT * kRowB;
           // Scales of this step into TMEM (ordered before the MMAs below).
 #pragma unroll
@@ -993,20 +985,18 @@ __global__ void __launch_bounds__(PairCfg::kThreads, 1) k_gemm_mxf4_pair(const _
                        (tmem + Cfg::kColSfa + 8 + 4 * grp) | (sf_id << 30), sfb, acc);
             }
           }
-          // Release the step's slots once these MMAs have read them.
-          mma_commit(&wring.empty[ws]);
-          mma_commit(&aring.empty[as]);
+          // Release the stage once these MMAs have read it.
+          mma_commit(&ring.empty[sl]);
         }
         mma_commit(acc_full);
       }
     }
-  } else if (warp >= Cfg::kFirstEpi) {
-    // Warps 3 .. 10: lane quarter sp = warp % 4 (TMEM's access rule), token
+  } else {
+    // Warps 2 .. 9: lane quarter sp = warp % 4 (TMEM's access rule), token
     // rows [r0, r0 + 32) of each tile.
     const uint32_t sp = warp & 3u;
-    const uint32_t r0 = ((warp - Cfg::kFirstEpi) / 4u) * 32u;
-    float* stage =
-        reinterpret_cast<float*>(smem + Cfg::kOffStage) + (warp - Cfg::kFirstEpi) * 128u;
+    const uint32_t r0 = ((warp - 2u) / 4u) * 32u;
+    float* stage = reinterpret_cast<float*>(smem + Cfg::kOffStage) + (warp - 2u) * 128u;
     uint32_t t = 0;
     for (uint32_t u = blockIdx.x; u < p.total_tiles; u += gridDim.x, ++t) {
       // Only the accumulators' values live across the release; the pair's
