@@ -74,7 +74,6 @@ struct hrb_plan {
     uint32_t nt, njobs, tiles;
     const void* d_jobs;  // DenseJob (exact) or TcJob (tensor-core) array
     const hrb::MxTile* d_tiles;  // kind 2: the launch's output tiles
-    bool pairs;                  // kind 2: the pair kernel (d_tiles in pair layout)
   };
   std::vector<Group> groups;
   // Per GEMM, in creation order: the device activations and output the
@@ -618,10 +617,8 @@ hrb_status conv_execute(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, 
     }
     if (take()) {
       tj.tile_begin = 0;
-      const bool pairs = hrb::mx_use_pairs(d->wfmt, qj.tile_rows, hrb::mx_pair_tiles(tj) / 2u,
-                                           ctx->sm_count);
       const int n = hrb::launch_mxf4(nullptr, &tj, qj.tile_rows, d->wfmt, tj.m_tiles * tj.n_tiles,
-                                     ctx->sm_count, ctx->d_error, s, peers, false, pairs);
+                                     ctx->sm_count, ctx->d_error, s, peers);
       if (n < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
       *launched += static_cast<uint32_t>(n);
     }
@@ -1035,10 +1032,8 @@ hrb_status hrb_gemm_dense(hrb_ctx* ctx, const hrb_gemm_desc* d, void* stream) {
     tc_translate(d, tj, s);
     hrb::launch_quantize_planes(nullptr, 1, &qj, qj.units, ctx->d_error, ctx->sm_count, s);
     tj.tile_begin = 0;
-    const bool pairs = hrb::mx_use_pairs(tj.wfmt, qj.tile_rows, hrb::mx_pair_tiles(tj) / 2u,
-                                         ctx->sm_count);
     const int n = hrb::launch_mxf4(nullptr, &tj, qj.tile_rows, tj.wfmt, tj.m_tiles * tj.n_tiles,
-                                   ctx->sm_count, ctx->d_error, s, nullptr, false, pairs);
+                                   ctx->sm_count, ctx->d_error, s);
     if (n < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
     ctx->launches += 2u + static_cast<uint64_t>(n);
     HRB_CUDA(ctx, cudaGetLastError());
@@ -1208,7 +1203,6 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
   std::vector<TcKey> tc_keys;
   std::vector<std::vector<hrb::TcJob>> tc_groups;
   std::vector<uint32_t> tc_tiles;
-  std::vector<std::vector<uint32_t>> tc_desc;  // per group: the descriptor of each job
   auto* sbase = static_cast<uint8_t*>(plan->d_scratch);
   size_t soff = 0;
   for (uint32_t i = 0; i < count; ++i) {
@@ -1234,12 +1228,10 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
         tc_keys.push_back({qj.tile_rows, tj.wfmt, kind});
         tc_groups.emplace_back();
         tc_tiles.push_back(0);
-        tc_desc.emplace_back();
       }
       tj.tile_begin = tc_tiles[g];
       tc_tiles[g] += tj.m_tiles * tj.n_tiles;
       tc_groups[g].push_back(tj);
-      tc_desc[g].push_back(i);
       plan->io[i].tile_begin = tj.tile_begin;
       plan->io[i].tiles = tj.m_tiles * tj.n_tiles;
       continue;
@@ -1275,37 +1267,13 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
   size_t bytes = (quant.size() + planes.size() + post.size()) * sizeof(hrb::QuantJob);
   for (auto& g : exact) bytes += g.size() * sizeof(hrb::DenseJob);
   for (auto& g : tc_groups) bytes += g.size() * sizeof(hrb::TcJob);
-  // kind::mxf4 groups also get their output tiles located on the host; a
-  // group of MXFP4 GEMMs with 64 tokens and pairs enough for every SM takes
-  // the pair kernel, its tiles in pair layout (each GEMM an even number of
-  // entries, its odd last column tile followed by an absent one).
-  std::vector<bool> tc_pairs(tc_groups.size(), false);
-  for (size_t g = 0; g < tc_groups.size(); ++g) {
-    if (tc_keys[g].kind != 2) continue;
-    uint64_t units = 0;
-    for (const hrb::TcJob& tj : tc_groups[g]) units += hrb::mx_pair_tiles(tj) / 2u;
-    tc_pairs[g] = hrb::mx_use_pairs(tc_keys[g].wfmt, tc_keys[g].nt, units, ctx->sm_count);
-    if (!tc_pairs[g]) continue;
-    uint32_t at = 0;
-    for (size_t j = 0; j < tc_groups[g].size(); ++j) {
-      hrb::TcJob& tj = tc_groups[g][j];
-      tj.tile_begin = at;
-      plan->io[tc_desc[g][j]].tile_begin = at;
-      plan->io[tc_desc[g][j]].tiles = hrb::mx_pair_tiles(tj);
-      at += hrb::mx_pair_tiles(tj);
-    }
-    tc_tiles[g] = at;
-  }
+  // kind::mxf4 groups also get their output tiles located on the host.
   std::vector<std::vector<hrb::MxTile>> mx_tiles(tc_groups.size());
   for (size_t g = 0; g < tc_groups.size(); ++g) {
     if (tc_keys[g].kind != 2) continue;
     mx_tiles[g].resize(tc_tiles[g]);
     for (const hrb::TcJob& tj : tc_groups[g]) {
-      if (tc_pairs[g]) {
-        hrb::mx_fill_pair_tiles(tj, tc_keys[g].nt, mx_tiles[g].data() + tj.tile_begin);
-      } else {
-        hrb::mx_fill_tiles(tj, tc_keys[g].nt, mx_tiles[g].data() + tj.tile_begin);
-      }
+      hrb::mx_fill_tiles(tj, tc_keys[g].nt, mx_tiles[g].data() + tj.tile_begin);
     }
     bytes += 16 + mx_tiles[g].size() * sizeof(hrb::MxTile);  // 16: alignment slack
   }
@@ -1353,7 +1321,7 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
                              cudaMemcpyHostToDevice));
     plan->groups.push_back({tc_keys[g].wfmt, tc_keys[g].kind, tc_keys[g].nt,
                             static_cast<uint32_t>(tc_groups[g].size()), tc_tiles[g], dst,
-                            nullptr, static_cast<bool>(tc_pairs[g])});
+                            nullptr});
     dst += tc_groups[g].size() * sizeof(hrb::TcJob);
     if (!mx_tiles[g].empty()) {
       auto* base = static_cast<uint8_t*>(plan->d_jobs);
@@ -1407,7 +1375,7 @@ hrb_status plan_launch(hrb_plan* plan, cudaStream_t s, int64_t only, uint32_t* l
           static_cast<const hrb::DenseJob*>(g.d_jobs), g.njobs, nullptr, g.tiles, g.wfmt, s));
     } else {
       const int k = hrb::launch_mxf4(g.d_tiles, nullptr, g.nt, g.wfmt, g.tiles, ctx->sm_count,
-                                     ctx->d_error, s, &plan->peers, true, g.pairs);
+                                     ctx->d_error, s, &plan->peers, true);
       if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
       n += static_cast<uint32_t>(k);
     }
@@ -1541,7 +1509,7 @@ hrb_status hrb_plan_run_host(hrb_plan* plan, void* stream, const void* const* a_
     const uint32_t t0 = plan->io[g0].tile_begin;
     const uint32_t t1 = plan->io[g1 - 1].tile_begin + plan->io[g1 - 1].tiles;
     const int k = hrb::launch_mxf4(g.d_tiles + t0, nullptr, g.nt, g.wfmt, t1 - t0,
-                                   ctx->sm_count, ctx->d_error, s, &plan->peers, true, g.pairs);
+                                   ctx->sm_count, ctx->d_error, s, &plan->peers, true);
     if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
     ctx->launches += 1u + static_cast<uint64_t>(k);
     HRB_CUDA(ctx, cudaEventRecord(ev[kChunks + c], s));

@@ -348,24 +348,6 @@ __device__ __forceinline__ void requant_rows(const MxTile& ti, const float (&x)[
 // copies 16-byte aligned, is regrouped through shared memory, four rows at a
 // time, into 16-byte stores (local, then each peer): lane l writes row l / 8,
 // columns 4 (l % 8) .. + 3.
-// The plane sums of rows j0 .. j0 + 15 of an accumulator at TMEM address
-// taddr (kSums partial sums per output at taddr, taddr + NT, taddr + 2 NT),
-// added smallest scale first.
-template <uint32_t NT, uint32_t kSums>
-__device__ __forceinline__ void tile_sums(uint32_t taddr, uint32_t j0, float (&x)[16]) {
-  uint32_t v0[16], v1[16], v2[16];
-  tmem_ld16(taddr + j0, v0);
-  if constexpr (kSums > 1) tmem_ld16(taddr + NT + j0, v1);
-  if constexpr (kSums > 2) tmem_ld16(taddr + 2 * NT + j0, v2);
-  tmem_wait_ld();
-#pragma unroll
-  for (uint32_t j = 0; j < 16; ++j) {
-    x[j] = __uint_as_float(v0[j]);
-    if constexpr (kSums > 1) x[j] = x[j] + __uint_as_float(v1[j]);
-    if constexpr (kSums > 2) x[j] += __uint_as_float(v2[j]);
-  }
-}
-
 template <uint32_t NT, uint32_t kSums>
 struct TileDrain {
   const MxParams& p;
@@ -414,7 +396,17 @@ struct TileDrain {
 
   // The plane sums of rows j0 .. j0 + 15 out of TMEM.
   __device__ __forceinline__ void load(uint32_t j0, float (&x)[16]) const {
-    tile_sums<NT, kSums>(taddr, j0, x);
+    uint32_t v0[16], v1[16], v2[16];
+    tmem_ld16(taddr + j0, v0);
+    if constexpr (kSums > 1) tmem_ld16(taddr + NT + j0, v1);
+    if constexpr (kSums > 2) tmem_ld16(taddr + 2 * NT + j0, v2);
+    tmem_wait_ld();
+#pragma unroll
+    for (uint32_t j = 0; j < 16; ++j) {
+      x[j] = __uint_as_float(v0[j]);
+      if constexpr (kSums > 1) x[j] = x[j] + __uint_as_float(v1[j]);
+      if constexpr (kSums > 2) x[j] += __uint_as_float(v2[j]);
+    }
   }
 
   // Accumulate, scale, bias, RELU and the stores of rows j0 .. j0 + 15.
@@ -794,256 +786,6 @@ __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Pair tiles: MXFP4 weights with at most 64 tokens, launches of many tiles.
-//
-// These GEMMs (C2's shape) are bound by what each SM takes in from L2 per K
-// step, not by HBM: a 128-column tile reads a 17 KB weight chunk and the
-// 26 KB block of three E2M1 activation planes, and the same activation block
-// is read again by every other column tile of the GEMM.  Here one CTA runs
-// two adjacent column tiles of the same token tile against one activation
-// block: a stage holds both weight chunks and the block (60 KB for twice the
-// work), the MMAs of each K slice go to two accumulators (192 TMEM columns
-// each), and the epilogue reads both out of TMEM before it releases them.
-// A unit of work is a pair: tiles 2u and 2u + 1 of the launch's tile array,
-// whose second tile may be absent (w = null, a GEMM with an odd number of
-// column tiles); the tile array of a pair launch is laid out that way
-// (mx_fill_pair_tiles).  Same warps and rings as k_gemm_mxf4: warp 0
-// streams stages, warp 1 owns TMEM and issues MMAs, warps 2 .. 9 drain.
-struct PairCfg {
-  static constexpr uint32_t NT = 64;
-  static constexpr uint32_t kABlock = mx_act_block_bytes(NT);          // 26624
-  static constexpr uint32_t kSlot = 2 * kWChunk + kABlock;              // 61440
-  static constexpr uint32_t kEpiWarps = 8;
-  static constexpr uint32_t kStage = 512u * kEpiWarps;                  // store regrouping
-  static constexpr uint32_t kSlots = (kSmemLimit - 1024 - 512 - kStage) / kSlot;
-  static constexpr uint32_t kOffBar = kSlots * kSlot;
-  static constexpr uint32_t kOffStage = kOffBar + 512;
-  static constexpr uint32_t kSmem = kOffStage + kStage + 1024;
-  static constexpr uint32_t kDCols = 3 * NT;          // three plane sums of 64 tokens
-  static constexpr uint32_t kColSfa = 2 * kDCols;     // weight scales: 8 columns a tile
-  static constexpr uint32_t kColSfb = kColSfa + 16;   // activation scales: 4 chunks
-  static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kThreads = 32u * (2u + kEpiWarps);
-  static_assert(kSlots >= 2, "pair ring");
-  static_assert(kColSfb + 16 <= kTmemCols, "TMEM columns");
-  static_assert(kSlot % 1024 == 0 && kSmem <= kSmemLimit, "shared memory");
-  static_assert(mx_parts(NT) == 1, "one stacked MMA of 192 rows a K slice");
-};
-
-// Tile `which` (0 or 1) of pair u (the second may be absent: w == null).
-__device__ __forceinline__ MxTile pair_tile(const MxParams& p, uint32_t u, uint32_t which) {
-  if (p.tiles != nullptr) return tile_info<PairCfg::NT>(p, 2u * u + which);
-  const TcJob& job = p.inline_job;
-  const uint32_t per_row = (job.n_tiles + 1u) / 2u, mt = u / per_row, j = u % per_row;
-  return make_tile(job, PairCfg::NT, mt * job.n_tiles + 2u * j + which);
-}
-
-// The two tiles of pair u; has_b is false when the second is absent.
-__device__ __forceinline__ void pair_info(const MxParams& p, uint32_t u, MxTile& a, MxTile& b,
-                                          bool& has_b) {
-  if (p.tiles != nullptr) {
-    a = tile_info<PairCfg::NT>(p, 2u * u);
-    b = tile_info<PairCfg::NT>(p, 2u * u + 1u);
-    has_b = b.w != nullptr;
-    return;
-  }
-  const TcJob& job = p.inline_job;
-  const uint32_t per_row = (job.n_tiles + 1u) / 2u, mt = u / per_row, j = u % per_row;
-  a = make_tile(job, PairCfg::NT, mt * job.n_tiles + 2u * j);
-  has_b = 2u * j + 1u < job.n_tiles;
-  b = has_b ? make_tile(job, PairCfg::NT, mt * job.n_tiles + 2u * j + 1u) : a;
-}
-
-__global__ void __launch_bounds__(PairCfg::kThreads, 1) k_gemm_mxf4_pair(const __grid_constant__ MxParams p) {
-  using Cfg = PairCfg;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
-  const Ring ring{bars, bars + Cfg::kSlots, Cfg::kSlots};
-  uint64_t* acc_full = bars + 2 * Cfg::kSlots;   // both accumulators ready
-  uint64_t* acc_empty = acc_full + 1;            // both read out (every epilogue thread)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-
-  if (threadIdx.x == 0) {
-    for (uint32_t s = 0; s < Cfg::kSlots; ++s) {
-      mbar_init(&ring.full[s], 1);
-      mbar_init(&ring.empty[s], 1);
-    }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 32 * Cfg::kEpiWarps);
-    fence_barrier_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  bool ok = true;
-  // As in k_gemm_mxf4: with ready weights the producer streams the weight
-  // halves of its first stages before the dependency wait.
-  griddep_launch_dependents();
-  const bool early_weights = p.weights_ready != 0 && warp == 0;
-  if (!early_weights) griddep_wait();
-
-  if (warp == 0) {
-    if (lane == 0) {
-      uint32_t n = 0;  // uses of the ring so far
-      MxTile na, nb;
-      bool nh;
-      pair_info(p, blockIdx.x, na, nb, nh);
-      for (uint32_t u = blockIdx.x; u < p.total_tiles && ok; u += gridDim.x) {
-        const MxTile a = na, b = nb;
-        const bool hb = nh;
-        if (u + gridDim.x < p.total_tiles) pair_info(p, u + gridDim.x, na, nb, nh);
-        const uint32_t k_steps = a.flags & 0x0FFFFFFFu;
-        const uint32_t bytes = (hb ? 2u : 1u) * kWChunk + Cfg::kABlock;
-        uint32_t pre = 0;  // stages whose weights went out before the wait
-        if (early_weights && n == 0) {
-          pre = k_steps < ring.slots ? k_steps : ring.slots;
-          for (uint32_t c = 0; c < pre; ++c) {
-            uint8_t* slot = smem + c * Cfg::kSlot;
-            mbar_arrive_expect_tx(&ring.full[c], bytes);
-            bulk_g2s(slot, a.w + static_cast<size_t>(c) * kWChunk, kWChunk, &ring.full[c]);
-            if (hb) {
-              bulk_g2s(slot + kWChunk, b.w + static_cast<size_t>(c) * kWChunk, kWChunk,
-                       &ring.full[c]);
-            }
-          }
-          griddep_wait();
-        }
-        for (uint32_t c = 0; c < k_steps && ok; ++c, ++n) {
-          const uint32_t sl = n % ring.slots;
-          uint8_t* slot = smem + sl * Cfg::kSlot;
-          if (c >= pre) {
-            ok = ring_acquire(ring, n, bytes, p.err);
-            if (!ok) break;
-            bulk_g2s(slot, a.w + static_cast<size_t>(c) * kWChunk, kWChunk, &ring.full[sl]);
-            if (hb) {
-              bulk_g2s(slot + kWChunk, b.w + static_cast<size_t>(c) * kWChunk, kWChunk,
-                       &ring.full[sl]);
-            }
-          }
-          bulk_g2s(slot + 2 * kWChunk, a.a + static_cast<size_t>(c) * Cfg::kABlock, Cfg::kABlock,
-                   &ring.full[sl]);
-        }
-      }
-      if (ok) ring_drain(ring, n, p.err);
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      uint32_t n = 0, t = 0;
-      MxTile na, nb;
-      bool nh;
-      pair_info(p, blockIdx.x, na, nb, nh);
-      for (uint32_t u = blockIdx.x; u < p.total_tiles && ok; u += gridDim.x, ++t) {
-        const uint32_t k_steps = na.flags & 0x0FFFFFFFu;
-        const bool hb = nh;
-        if (u + gridDim.x < p.total_tiles) pair_info(p, u + gridDim.x, na, nb, nh);
-        // One pair of accumulators: the last pair's must have been read.
-        if (t >= 1) ok = mbar_wait(acc_empty, (t - 1) & 1u, p.err);
-        if (!ok) break;
-        tc_fence_after();
-        for (uint32_t i = 0; i < k_steps && ok; ++i, ++n) {
-          const uint32_t sl = n % ring.slots;
-          ok = mbar_wait(&ring.full[sl], (n / ring.slots) & 1u, p.err);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t wa = smem_addr(smem + sl * Cfg::kSlot);
-          const uint32_t wb = wa + kWChunk;
-          const uint32_t act = wa + 2 * kWChunk;
-          const uint32_t a_sf = act + 3 * Cfg::NT * kRowB;
-          // Scales of this step into TMEM (ordered before the MMAs below).
-#pragma unroll
-          for (uint32_t c = 0; c < 2; ++c) {
-            sf_copy(tmem + Cfg::kColSfa + 4 * c, desc_sf_chunk(wa + kTileW * kRowB + c * kSfChunk));
-            if (hb) {
-              sf_copy(tmem + Cfg::kColSfa + 8 + 4 * c,
-                      desc_sf_chunk(wb + kTileW * kRowB + c * kSfChunk));
-            }
-          }
-#pragma unroll
-          for (uint32_t c = 0; c < 4; ++c) {
-            sf_copy(tmem + Cfg::kColSfb + 4 * c, desc_sf_chunk(a_sf + c * kSfChunk));
-          }
-#pragma unroll
-          for (uint32_t k = 0; k < 4; ++k) {
-            // MMA k covers blocks 2k, 2k+1: group k / 2, bytes 2 (k % 2).
-            const uint32_t grp = k / 2, sf_id = (k % 2) * 2;
-            const uint32_t idesc = idesc_mxf4(kTileW, 3 * Cfg::NT, sf_id);
-            const uint32_t sfb = (tmem + Cfg::kColSfb + 8 * grp) | (sf_id << 30);
-            const uint64_t ad = desc_sw128(act + 32 * k);
-            const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-            mma_mxf4(tmem, desc_sw128(wa + 32 * k), ad, idesc,
-                     (tmem + Cfg::kColSfa + 4 * grp) | (sf_id << 30), sfb, acc);
-            if (hb) {
-              mma_mxf4(tmem + Cfg::kDCols, desc_sw128(wb + 32 * k), ad, idesc,
-                       (tmem + Cfg::kColSfa + 8 + 4 * grp) | (sf_id << 30), sfb, acc);
-            }
-          }
-          // Release the stage once these MMAs have read it.
-          mma_commit(&ring.empty[sl]);
-        }
-        mma_commit(acc_full);
-      }
-    }
-  } else {
-    // Warps 2 .. 9: lane quarter sp = warp % 4 (TMEM's access rule), token
-    // rows [r0, r0 + 32) of each tile.
-    const uint32_t sp = warp & 3u;
-    const uint32_t r0 = ((warp - 2u) / 4u) * 32u;
-    float* stage = reinterpret_cast<float*>(smem + Cfg::kOffStage) + (warp - 2u) * 128u;
-    uint32_t t = 0;
-    for (uint32_t u = blockIdx.x; u < p.total_tiles; u += gridDim.x, ++t) {
-      // Only the accumulators' values live across the release; the pair's
-      // fields are loaded after it (these warps hold 64 values a thread).
-      const bool hb = p.tiles != nullptr
-                          ? __ldg(reinterpret_cast<const unsigned long long*>(p.tiles + 2u * u + 1u)) != 0
-                          : 2u * (u % ((p.inline_job.n_tiles + 1u) / 2u)) + 1u < p.inline_job.n_tiles;
-      if (ok) ok = mbar_wait(acc_full, t & 1u, p.err);
-      ok = __all_sync(0xFFFFFFFFu, ok);
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t taddr = tmem + ((sp * 32u) << 16);
-      float xa[16], xb[16], ya[16], yb[16];
-      tile_sums<Cfg::NT, 3>(taddr, r0, xa);
-      tile_sums<Cfg::NT, 3>(taddr, r0 + 16u, xb);
-      if (hb) {
-        tile_sums<Cfg::NT, 3>(taddr + Cfg::kDCols, r0, ya);
-        tile_sums<Cfg::NT, 3>(taddr + Cfg::kDCols, r0 + 16u, yb);
-      }
-      // Both accumulators are in registers: the next pair's MMAs may start.
-      tc_fence_before();
-      mbar_arrive(acc_empty);
-      {
-        const MxTile a = pair_tile(p, u, 0);
-        const TileDrain<Cfg::NT, 3> da(p, a, taddr, sp, lane, stage);
-        da.finish(r0, xa);
-        da.finish(r0 + 16u, xb);
-      }
-      if (hb) {
-        const MxTile b = pair_tile(p, u, 1);
-        const TileDrain<Cfg::NT, 3> db(p, b, taddr + Cfg::kDCols, sp, lane, stage);
-        db.finish(r0, ya);
-        db.finish(r0 + 16u, yb);
-      }
-    }
-    // Peer stores performed before the kernel is seen to finish.
-    if (p.peers.count != 0) __threadfence_system();
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, Cfg::kTmemCols);
-  }
-}
-
-// ---------------------------------------------------------------------------
 // W8 with at most 64 tokens (path format kTcW8Bf16): kind::f16 on BF16.
 //
 // These GEMMs are bound by the weight stream, so the weights travel as the
@@ -1370,21 +1112,6 @@ int launch_pdl(const void* fn, uint32_t grid, uint32_t threads, uint32_t smem, c
   return cudaLaunchKernelExC(&cfg, fn, args) == cudaSuccess ? 1 : -1;
 }
 
-int launch_pair(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t units, int sm_count,
-                uint32_t* err, cudaStream_t s, const MxPeers* peers, bool weights_ready) {
-  MxParams p{};
-  p.tiles = tiles_dev;
-  p.total_tiles = units;
-  p.err = err;
-  p.weights_ready = weights_ready ? 1u : 0u;
-  if (peers != nullptr) p.peers = *peers;
-  if (inline_job != nullptr) p.inline_job = *inline_job;
-  const uint32_t grid = std::min<uint32_t>(units, static_cast<uint32_t>(sm_count));
-  const void* fn = reinterpret_cast<const void*>(k_gemm_mxf4_pair);
-  if (!set_smem_limit_once(fn, PairCfg::kSmem)) return -1;
-  return launch_pdl(fn, grid, PairCfg::kThreads, PairCfg::kSmem, s, p);
-}
-
 int launch_w8bf(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, int sm_count,
                 uint32_t* err, cudaStream_t s, const MxPeers* peers) {
   MxParams p{};
@@ -1594,27 +1321,6 @@ void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out) {
   for (uint32_t i = 0; i < job.m_tiles * job.n_tiles; ++i) out[i] = make_tile(job, nt, i);
 }
 
-uint32_t mx_pair_tiles(const TcJob& job) { return job.m_tiles * 2u * ((job.n_tiles + 1u) / 2u); }
-
-void mx_fill_pair_tiles(const TcJob& job, uint32_t nt, MxTile* out) {
-  const uint32_t per_row = (job.n_tiles + 1u) / 2u;
-  for (uint32_t mt = 0; mt < job.m_tiles; ++mt) {
-    for (uint32_t j = 0; j < per_row; ++j) {
-      MxTile* pair = out + 2u * (mt * per_row + j);
-      pair[0] = make_tile(job, nt, mt * job.n_tiles + 2u * j);
-      pair[1] = 2u * j + 1u < job.n_tiles ? make_tile(job, nt, mt * job.n_tiles + 2u * j + 1u)
-                                          : MxTile{};  // absent: w == null
-    }
-  }
-}
-
-bool mx_use_pairs(uint32_t wfmt, uint32_t nt, uint64_t pair_units, int sm_count) {
-  // Two tiles a CTA pay when every SM still gets a pair; a launch of fewer
-  // pairs than SMs finishes sooner spread one tile a CTA.
-  return wfmt == HRB_WFMT_MXFP4 && nt == PairCfg::NT &&
-         pair_units >= static_cast<uint64_t>(sm_count);
-}
-
 int launch_mxf4_gather(const TcJob& inline_job, uint32_t nt, uint32_t tiles, int sm_count,
                        uint32_t* err, cudaStream_t s, const MxGather& gather,
                        const MxPeers* peers) {
@@ -1628,17 +1334,10 @@ int launch_mxf4_gather(const TcJob& inline_job, uint32_t nt, uint32_t tiles, int
 
 int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t wfmt,
                 uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t s,
-                const MxPeers* peers, bool weights_ready, bool pairs) {
+                const MxPeers* peers, bool weights_ready) {
   if (tiles == 0) return 0;
   if (tiles_dev == nullptr && inline_job == nullptr) return -1;
   if (peers != nullptr && peers->count > kMaxPeers) return -1;
-  if (pairs) {
-    if (wfmt != HRB_WFMT_MXFP4 || nt != PairCfg::NT) return -1;
-    const uint32_t units = tiles_dev != nullptr
-                               ? (tiles + 1u) / 2u
-                               : inline_job->m_tiles * ((inline_job->n_tiles + 1u) / 2u);
-    return launch_pair(tiles_dev, inline_job, units, sm_count, err, s, peers, weights_ready);
-  }
   const auto go = [&](auto cfg) {
     using C = decltype(cfg);
     return launch_mx<C::kNt, C::kWp, C::kKb>(tiles_dev, inline_job, tiles, sm_count, err, s,

@@ -124,14 +124,6 @@ struct MxTile {
 static_assert(sizeof(MxTile) == 64, "MxTile is read as four 16-byte loads");
 // The m_tiles * n_tiles tiles of one job (tile index mt * n_tiles + nt).
 void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out);
-// Pair launches (MXFP4, 64 tokens): one CTA runs two adjacent column tiles
-// of a token tile against one activation block.  Their tile array holds the
-// pairs in order, a GEMM's odd last column tile followed by an absent tile
-// (w == null): mx_pair_tiles entries a job.  mx_use_pairs: whether a launch
-// of pair_units pairs takes the pair kernel.
-uint32_t mx_pair_tiles(const TcJob& job);
-void mx_fill_pair_tiles(const TcJob& job, uint32_t nt, MxTile* out);
-bool mx_use_pairs(uint32_t wfmt, uint32_t nt, uint64_t pair_units, int sm_count);
 // Peers that receive a copy of every output (the fused all-gather of a
 // column- or row-sharded layer): an output byte at address x (C or the
 // MXINT8 copy) is also stored at x + delta[i].
@@ -160,11 +152,9 @@ int launch_mxf4_gather(const TcJob& inline_job, uint32_t nt, uint32_t tiles, int
 // it is null, the tiles of the single *inline_job.  `peers` may be null.
 // weights_ready: the weight chunks were written and the stream synchronised
 // before (a plan's), so the kernel may read them before its dependency wait.
-// pairs: the pair kernel (tiles_dev laid out by mx_fill_pair_tiles, `tiles`
-// its entries; or the inline job's pairs).
 int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t wfmt,
                 uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t stream,
-                const MxPeers* peers = nullptr, bool weights_ready = false, bool pairs = false);
+                const MxPeers* peers = nullptr, bool weights_ready = false);
 
 // Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current
 // device, once per (kernel, device).
