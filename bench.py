@@ -340,7 +340,8 @@ def place_w8(wf: np.ndarray):
 # ---------------------------------------------------------------------------
 # The reference's CPU implementation (test infrastructure, timed only)
 
-def cpu_reference(wl: Workload, min_seconds: float = 2.0, max_reps: int = 50) -> dict:
+def cpu_reference(wl: Workload, min_seconds: float = 2.0, max_reps: int = 50,
+                  columns: bool = False) -> dict:
     """hotarubi's ExecuteGemm, compiled from the reference sources
     (oracle/_ref), tiled into legal GEMM instructions over all host threads,
     on GEMMs of the workload until ~min_seconds of wall time; rows of large-M
@@ -399,10 +400,64 @@ def cpu_reference(wl: Workload, min_seconds: float = 2.0, max_reps: int = 50) ->
                                   prow)
         reps += 1
     dt = time.perf_counter() - t0
-    return {"value": reps * sample_flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
-            "kind": "reference",
-            "sample": f"{reps} x {label} through ExecuteGemm tiles on {threads} threads",
-            "seconds": dt}
+    out = {"value": reps * sample_flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
+           "kind": "reference",
+           "sample": f"{reps} x {label} through ExecuteGemm tiles on {threads} threads",
+           "seconds": dt}
+    if columns:
+        out["columns"] = cpu_columns(ref, nplanes, prow, wl, a_words, planes, c, sample_flops,
+                                     min_seconds / 2)
+    return out
+
+
+def cpu_columns(ref, nplanes, rows, wl, a_words, planes, c, flops, min_seconds):
+    """The other CPU columns of the metric ("vs gemm_ref CPU"): the same
+    sample through ExecuteGemm on one thread, and through tb/gemm_ref's
+    ReferenceGemm (tb/gemm_ref.cpp:47-68, the model the RTL is checked
+    against) on one thread and on all host threads."""
+    import ctypes
+
+    f = ref.hrbref_dense_gemm_tb
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_uint32] * 4 + [np.ctypeslib.ndpointer(np.uint8),
+                                          np.ctypeslib.ndpointer(np.uint8),
+                                          np.ctypeslib.ndpointer(np.uint32), ctypes.c_uint32]
+    threads = os.cpu_count() or 1
+
+    def timed(run):
+        run()
+        t0 = time.perf_counter()
+        reps = 0
+        while reps < 1 or time.perf_counter() - t0 < min_seconds:
+            run()
+            reps += 1
+        return reps * flops / (time.perf_counter() - t0) / 1e12
+
+    return {
+        "execute_gemm_1_thread": timed(lambda: ref.hrbref_dense_gemm_iss(
+            nplanes, rows, wl.N, wl.kb, a_words, planes, c, 1, 0, rows)),
+        "gemm_ref_1_thread": timed(lambda: f(nplanes, rows, wl.N, wl.kb, a_words, planes, c, 1)),
+        f"gemm_ref_{threads}_threads": timed(lambda: f(nplanes, rows, wl.N, wl.kb, a_words,
+                                                         planes, c, threads)),
+        "unit": "TFLOP/s",
+    }
+
+
+def trial_stats(ms: list[float]) -> dict:
+    """Per-step device times of the timed region (each step a trial)."""
+    v = sorted(ms)
+    return {"n": len(v), "median_ms": statistics.median(v), "min_ms": v[0], "max_ms": v[-1],
+            "spread": (v[-1] - v[0]) / statistics.median(v) if v else 0.0}
+
+
+def tensor_fracs(tflops: float, pk: dict, wfmt: int) -> dict:
+    """A tensor-bound rate against (i) the dense peak of the MMA kind the
+    kernel issues (kind::mxf4 4x, kind::mxf8f6f4 2x the measured dense BF16
+    rate: NVIDIA's dense ratios) and (ii) the 8-bit dense peak (2x BF16)."""
+    kind, mult = ("kind::mxf8f6f4", 2.0) if wfmt == 2 else ("kind::mxf4", 4.0)
+    return {"mma_kind": kind,
+            "frac_of_kind_dense_peak": tflops / (mult * pk["bf16_tflops"]),
+            "frac_of_8bit_dense_peak": tflops / (2.0 * pk["bf16_tflops"])}
 
 
 def run_reference(args, wl: Workload, rank: int, world: int) -> None:
@@ -591,19 +646,20 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
-        start.record(stream)
+        # One event after every step as well: each step is a timing trial.
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        marks[0].record(stream)
         launches = 0
-        for _ in range(args.steps):
+        for i in range(args.steps):
             launches += plan_full.run(stream.cuda_stream)
-        end.record(stream)
-        end.synchronize()
+            marks[i + 1].record(stream)
+        marks[-1].synchronize()
         torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
     lib.sync()
-    ms = start.elapsed_time(end) / args.steps
+    ms = marks[0].elapsed_time(marks[-1]) / args.steps
+    trials = trial_stats([marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)])
     if dist is not None:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -654,10 +710,13 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
                 peak = pk["bf16_tflops"] * 4.0 / (3.0 if wl.wfmt == 0 else 9.0)
                 how = (" (cuBLAS BF16 x 4/3: FP4 MMA rate over three digit planes)"
                        if wl.wfmt == 0 else " (cuBLAS BF16 x 4/9: FP4 MMA rate over 3 x 3 planes)")
-            roof = {"bound": "tensor", "kernel": kname, "achieved": tflops, "peak": peak,
-                    "unit": "TFLOP/s", "frac": tflops / peak,
-                    "peak_source": pk["source"] + how,
-                    "frac_of_bf16_peak": tflops / pk["bf16_tflops"],
+            roof = {"bound": "tensor", "kernel": kname, "achieved": tflops,
+                    "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                    "frac": tflops / pk["bf16_tflops"],
+                    "peak_source": pk["source"] + " (cuBLAS BF16 dense)",
+                    **tensor_fracs(tflops, pk, wl.wfmt),
+                    "useful_ceiling": {"peak": peak, "frac": tflops / peak,
+                                       "how": pk["source"] + how},
                     "alg_flops_per_launch": batch * wl.flops}
         roof.update({"traffic": (None if per_gemm_traffic is None
                                  else per_gemm_traffic * batch),
@@ -680,6 +739,8 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
                                 else ""),
                        "parallelism": f"replicas x{world} (independent GEMMs)"},
             "step_hbm_gbs": step_gbs,
+            "step_hbm_frac": step_gbs / pk["hbm_gbs"],
+            "trials": trials,
             "roofline": roof,
             "encoder": {"kernel": qname, "launch_ms": quant_ms, "achieved_gbs": quant_gbs,
                         "frac": quant_gbs / pk["hbm_gbs"],
@@ -701,7 +762,8 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
                                       "model": "CostModel::Gemm over the GEMM instructions "
                                                "of a tiled run, 250 MHz"}
         if not args.no_cpu_baseline:
-            line["cpu_baseline"] = {k: v for k, v in cpu_reference(wl).items() if k != "seconds"}
+            line["cpu_baseline"] = {k: v for k, v in cpu_reference(wl, columns=True).items()
+                                    if k != "seconds"}
         print(json.dumps(line), flush=True)
     plan_full.close()
     lib.close()
@@ -875,10 +937,13 @@ def run_conv(args, rank: int, world: int, local_rank: int) -> None:
                              " MB > 2 x 126 MB L2",
                        "parallelism": f"replicas x{world}"},
             "roofline": {"bound": "tensor", "kernel": "k_gemm_mxf4" if mode == capi.MODE_FAST
-                         else "k_dense_exact", "achieved": tflops, "peak": peak,
-                         "unit": "TFLOP/s", "frac": tflops / peak,
-                         "peak_source": pk["source"] + " (cuBLAS BF16 x 4/3: FP4 MMA rate over "
-                                                       "three digit planes)",
+                         else "k_dense_exact", "achieved": tflops, "peak": pk["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": tflops / pk["bf16_tflops"],
+                         "peak_source": pk["source"] + " (cuBLAS BF16 dense)",
+                         **tensor_fracs(tflops, pk, cw.wfmt),
+                         "useful_ceiling": {"peak": peak, "frac": tflops / peak,
+                                            "how": "cuBLAS BF16 x 4/3: FP4 MMA rate over three "
+                                                   "digit planes"},
                          "alg_flops_per_launch": cw.flops, "traffic": None,
                          "launch_ms": gemm_ms},
             "encoder": {"kernels": "k_quantize_planes (map) + k_conv_gather_tiles"
@@ -1356,8 +1421,8 @@ def run_shard(args, wl: Workload, rank: int, world: int, local_rank: int) -> Non
                                       "epilogue (NVLink peer stores)"},
             "nvlink": {"bytes_per_rank_per_step": nvlink,
                        "gbs_per_rank": nvlink / (ms / 1e3) / 1e9},
-            "tensor_peak_frac": batch * wl.flops / world / (ms / 1e3) / 1e12
-                                / (pk["bf16_tflops"] * 4.0 / 3.0),
+            **{"per_gpu_" + k: v for k, v in tensor_fracs(
+                batch * wl.flops / world / (ms / 1e3) / 1e12, pk, wl.wfmt).items()},
             "gpu_launches": 2 * args.steps if plan is not None else 0,
             "e2e": None, "clocks": clocks.summary(),
         }
