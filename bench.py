@@ -43,6 +43,7 @@ import argparse
 import dataclasses
 import json
 import os
+import re
 import statistics
 import sys
 import threading
@@ -106,18 +107,20 @@ WORKLOADS = {
                    False, 4, "tensor"),
     # C4's largest GEMM (the action expert's MLP 720 -> 2048, MXFP8) for one
     # GPU's share of the 256 requests at 8 GPUs: 32 requests x 50 tokens,
-    # one GEMM per layer of a flow step (16).
-    "c4": Workload("c4", "c4_mxfp8_1600x720x2048", "C4 1600x720x2048", 2, 1600, 2048, 720,
-                   False, 16, "tensor"),
+    # one GEMM per layer of a flow step (16).  The whole C4 job is --config c4.
+    "c4gemm": Workload("c4gemm", "c4_mxfp8_1600x720x2048", "C4 1600x720x2048", 2, 1600, 2048,
+                       720, False, 16, "tensor"),
 }
 
 
 @dataclasses.dataclass(frozen=True)
 class ConvWorkload:
-    """The C5 conv (3x3, 256 -> 256 channels, 16 x 44 maps,
-    6 cameras x batch 8), MXFP4 weights, bias, FP32 NHWC input."""
+    """The C5 conv (ResNet-50 stage-3 3x3, 256 -> 256 channels,
+    16 x 44 maps, 6 cameras x batch 8), bias, FP32 NHWC input; W8 weights as
+    the config names them (per-channel int8 placed as MXINT8 blocks), or
+    MXFP4."""
     key: str = "c5conv"
-    name: str = "c5_conv3x3_48x16x44x256_mxfp4"
+    name: str = "c5_conv3x3_48x16x44x256_w8"
     images: int = 48
     H: int = 16
     W: int = 44
@@ -125,7 +128,7 @@ class ConvWorkload:
     cout: int = 256
     kh: int = 3
     stride: int = 1
-    wfmt: int = 0
+    wfmt: int = 1
     instances: int = 3   # rotated per step: 3 x ~190 MB > 2 x L2
 
     @property
@@ -142,14 +145,21 @@ class ConvWorkload:
 
     @property
     def metric(self) -> str:
-        return "MXFP4 implicit-GEMM conv TFLOP/s (C5 conv 3x3 256->256, 48 x 16x44)"
+        return (f"{FMT_NAMES[self.wfmt].upper()} implicit-GEMM conv TFLOP/s "
+                "(C5 conv 3x3 256->256, 48 x 16x44)")
+
+    def w_bytes(self) -> int:
+        return self.cout * self.K // 2 if self.wfmt == 0 else self.cout * self.K
 
     def bytes_step(self) -> int:
-        return (self.images * self.H * self.W * self.cin * 4 + self.cout * self.K // 2
+        return (self.images * self.H * self.W * self.cin * 4 + self.w_bytes()
                 + self.cout * self.K // 32 + self.cout * 4 + self.M * self.cout * 4)
 
 
 CONV = ConvWorkload()
+CONV_MXFP4 = dataclasses.replace(CONV, key="c5conv_mxfp4", name="c5_conv3x3_48x16x44x256_mxfp4",
+                                 wfmt=0)
+CONVS = {c.key: c for c in (CONV, CONV_MXFP4)}
 
 
 @dataclasses.dataclass(frozen=True)
@@ -227,6 +237,75 @@ class PrefixWorkload:
 
 
 PREFIX = PrefixWorkload()
+
+
+@dataclasses.dataclass(frozen=True)
+class ExpertWorkload:
+    """C4: the SmolVLA-shaped action expert over a batch of 256 independent
+    requests (tools/compiler/smolvla_expert.cpp: 16 layers of width 720,
+    MLP 2048, odd layers cross-attending to the 141-token prefix,
+    :75,182-203,608-651; 15 query / 5 KV heads of 64, smolvla_parts.hpp:
+    29-30), every GEMM MXFP8 as the config sets it.  One bench step is the
+    whole job: the cross-attention K/V projections of the prefix (960 ->
+    320, once per request), then 10 flow steps, each the suffix heads
+    (action in 32 -> 720, the time MLP 720 -> 720 twice and 720 -> 720,
+    action out 720 -> 32) around the 16 layers.  The requests' rows are
+    batched into each GEMM (50 tokens a request); N GPUs take 256 / N
+    requests each (strong scaling).  Attention, norms and SiLU between the
+    GEMMs are outside the GEMM path, so each dependency group reads a seeded
+    synthetic FP32 input of its shape (rows of RMS 1)."""
+    key: str = "c4"
+    name: str = "c4_smolvla_expert_256req_10steps"
+    requests: int = 256
+    tokens: int = 50
+    prefix: int = 141
+    steps: int = 10
+    layers: int = 16
+    wfmt: int = 2
+    # (group, [(name, K, N)]) per layer kind; the input of a group is shared.
+    self_layer: tuple = (("qkv", (("q", 720, 960), ("k", 720, 320), ("v", 720, 320))),
+                         ("o", (("o", 960, 720),)),
+                         ("gate_up", (("gate", 720, 2048), ("up", 720, 2048))),
+                         ("down", (("down", 2048, 720),)))
+    cross_layer: tuple = (("q", (("q", 720, 960),)),
+                          ("o", (("o", 960, 720),)),
+                          ("gate_up", (("gate", 720, 2048), ("up", 720, 2048))),
+                          ("down", (("down", 2048, 720),)))
+    heads_in: tuple = (("action_in", (("in", 32, 720),)),
+                       ("time_mlp_in", (("mlp_in_action", 720, 720),
+                                        ("mlp_in_time", 720, 720))),
+                       ("time_mlp_out", (("mlp_out", 720, 720),)))
+    heads_out: tuple = (("action_out", (("out", 720, 32),)),)
+    cross_kv: tuple = (("k", 960, 320), ("v", 960, 320))
+
+    def rows(self, world: int) -> tuple[int, int]:
+        """(suffix rows, prefix rows) of one GPU's GEMMs."""
+        r = self.requests // world
+        return r * self.tokens, r * self.prefix
+
+    def step_groups(self) -> list:
+        """One flow step's dependency groups in launch order: (label, gemms)."""
+        out = [(f"head.{g}", gm) for g, gm in self.heads_in]
+        for layer in range(self.layers):
+            kind = self.cross_layer if layer % 2 else self.self_layer
+            out += [(f"L{layer}.{g}", gm) for g, gm in kind]
+        out += [(f"head.{g}", gm) for g, gm in self.heads_out]
+        return out
+
+    def flops(self, world: int = 1) -> int:
+        """All GPUs' FLOPs of one job."""
+        m, mp = self.rows(world)
+        step = sum(2 * m * k * n for _, gm in self.step_groups() for _, k, n in gm)
+        kv = (self.layers // 2) * sum(2 * mp * k * n for _, k, n in self.cross_kv)
+        return world * (self.steps * step + kv)
+
+    @property
+    def metric(self) -> str:
+        return ("MXFP8 GEMM TFLOP/s (C4 SmolVLA action expert, 256 requests x 10 flow steps "
+                "x 16 layers)")
+
+
+EXPERT = ExpertWorkload()
 
 
 def peaks() -> dict:
@@ -532,15 +611,20 @@ def dequant_weights(wfmt: int, w: np.ndarray, ws: np.ndarray, n: int, kp: int) -
     return np.where(w & 0x80, -v, v) * sc
 
 
-def fast_parity(torch, lib, wl: Workload, x, w, ws, bias, c_dev, rows: int = 64) -> dict:
-    """GEMM 0's fast-mode output on its first rows against the float64 dot
-    product of its dequantized operands (activation codes from the library's
-    own MXINT8 encoder): the max relative error, the stated bound
-    (K/16 + 4) 2^-23 sum|a w| per output, and the ulp histogram against
-    that product rounded to FP32."""
+def fast_parity(torch, lib, wl: Workload, x, w, ws, bias, c_dev, rows: int = 64,
+                tail: bool = False) -> dict:
+    """GEMM 0's fast-mode output on its first rows (with `tail`, half of them
+    the last rows: the last token tile) against the float64 dot product of
+    its dequantized operands (activation codes from the library's own MXINT8
+    encoder): the max relative error, the stated bound (K/16 + 4) 2^-23
+    sum|a w| per output, and the ulp histogram against that product rounded
+    to FP32."""
     m = min(rows, wl.M)
+    sel = np.arange(m)
+    if tail and wl.M > m:
+        sel = np.concatenate([np.arange(m // 2), np.arange(wl.M - (m - m // 2), wl.M)])
     kb, kp = wl.kb, wl.kb * 32
-    xd = torch.from_numpy(np.ascontiguousarray(x[:m])).cuda()
+    xd = torch.from_numpy(np.ascontiguousarray(x[sel])).cuda()
     q = torch.zeros((m, kp), dtype=torch.int8, device="cuda")
     s = torch.zeros((m, kb), dtype=torch.uint8, device="cuda")
     lib.quantize(xd, m, wl.K, q, s)
@@ -553,7 +637,7 @@ def fast_parity(torch, lib, wl: Workload, x, w, ws, bias, c_dev, rows: int = 64)
     if bias is not None:
         ref += bias.astype(np.float64)
         absref += np.abs(bias.astype(np.float64))
-    got = c_dev[:m].cpu().numpy()
+    got = c_dev[torch.from_numpy(sel).to(c_dev.device)].cpu().numpy()
     err = np.abs(got.astype(np.float64) - ref)
     bound = (kp / 16 + 4) * 2.0**-23 * absref + 1e-30
     rel = err / (absref + 1e-30)
@@ -563,7 +647,8 @@ def fast_parity(torch, lib, wl: Workload, x, w, ws, bias, c_dev, rows: int = 64)
         return np.where(i < 0, -(i & 0x7FFFFFFF), i)
     d = np.abs(ordered(got.astype(np.float32)) - ordered(ref.astype(np.float32)))
     return {"reference": "float64 dot of the dequantized operands (library MXINT8 encoder)",
-            "rows": m, "outputs": int(err.size), "max_rel_err": float(rel.max()),
+            "rows": m if not tail or wl.M <= m else f"first {m // 2} and last {m - m // 2}",
+            "outputs": int(err.size), "max_rel_err": float(rel.max()),
             "bound": "(K/16 + 4) * 2^-23 * sum|a w| per output",
             "within_bound": bool((err <= bound).all()),
             "ulp_hist_vs_fp32_rounded": {"0": int((d == 0).sum()), "1": int((d == 1).sum()),
@@ -772,10 +857,17 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
         dist.destroy_process_group()
 
 
-def conv_operands(cw: ConvWorkload, i: int):
+def conv_operands(cw: ConvWorkload, i: int, place=None):
+    """FP32 NHWC map, weights [cout][9 x cin] (tap-major) in the dense format,
+    bias.  W8: per-channel int8 placed as MXINT8 blocks (`place`, default
+    this library's device encoder)."""
     from hotarubi_b200 import workloads
     x = workloads.activations(500 + i, cw.images * cw.H * cw.W, cw.cin)
-    w, ws = workloads.mxfp4_weights(600 + i, cw.cout, cw.K)
+    if cw.wfmt == 1:
+        q, sc = workloads.w8_per_channel(600 + i, cw.cout, cw.K)
+        w, ws = (place or place_w8)(workloads.dequantize_per_channel(q, sc))
+    else:
+        w, ws = workloads.mxfp4_weights(600 + i, cw.cout, cw.K)
     b = workloads.bias(700 + i, cw.cout)
     return x, w, ws, b
 
@@ -786,14 +878,22 @@ def conv_cpu_reference(cw: ConvWorkload, min_seconds: float = 2.0) -> dict:
     on one image of the batch."""
     from oracle import cpu
     ref = cpu.ref()
-    x, w, ws, b = conv_operands(cw, 0)
+
+    def place_cpu(wf):  # W8 placement on the host (EncodeMxint8)
+        q, s = cpu.encode_mxint8(wf.view(np.uint32))
+        return q.view(np.uint8), s
+
+    x, w, ws, b = conv_operands(cw, 0, place_cpu)
     hw = cw.H * cw.W
     # One image, x-major as the compiler's maps are (the conv is the same).
     img = x[:hw].reshape(cw.H, cw.W, cw.cin).transpose(1, 0, 2).reshape(hw, cw.cin)
     q, s = cpu.encode_mxint8(np.ascontiguousarray(img).view(np.uint32))
-    codes = np.zeros((cw.cout, cw.K), np.uint8)
-    codes[:, 0::2] = w & 0xF
-    codes[:, 1::2] = w >> 4
+    if cw.wfmt == 0:
+        codes = np.zeros((cw.cout, cw.K), np.uint8)
+        codes[:, 0::2] = w & 0xF
+        codes[:, 1::2] = w >> 4
+    else:
+        hi, lo = cpu.split_w8(w.view(np.int8))
     e = ws.astype(np.int32) - 127
     flops = 2 * hw // (cw.stride * cw.stride) * cw.cout * cw.K
     c = np.zeros((hw // (cw.stride * cw.stride), cw.cout), np.uint32)
@@ -807,8 +907,14 @@ def conv_cpu_reference(cw: ConvWorkload, min_seconds: float = 2.0) -> dict:
     t0 = time.perf_counter()
     reps = 0
     while reps < 1 or time.perf_counter() - t0 < min_seconds:
-        ref.hrbref_conv_iss(cw.H, cw.W, cw.cin, cw.cout, cw.kh, cw.stride, q.ravel(), s.ravel(),
-                            codes.ravel(), e.ravel(), b.view(np.uint32), None, 0, c.ravel())
+        if cw.wfmt == 0:
+            ref.hrbref_conv_iss(cw.H, cw.W, cw.cin, cw.cout, cw.kh, cw.stride, q.ravel(),
+                                s.ravel(), codes.ravel(), e.ravel(), b.view(np.uint32), None, 0,
+                                c.ravel())
+        else:
+            ref.hrbref_conv_iss_w8(cw.H, cw.W, cw.cin, cw.cout, cw.kh, cw.stride, q.ravel(),
+                                   s.ravel(), hi.ravel(), lo.ravel(), e.ravel(),
+                                   b.view(np.uint32), None, 0, c.ravel())
         reps += 1
     dt = time.perf_counter() - t0
     return {"value": reps * flops / dt / 1e12, "unit": "TFLOP/s", "cores": 1,
@@ -826,7 +932,7 @@ def run_conv(args, rank: int, world: int, local_rank: int) -> None:
     import torch
 
     from hotarubi_b200 import capi
-    cw = CONV
+    cw = CONVS[args.config]
     if args.impl == "reference":
         if rank != 0:
             return
@@ -921,7 +1027,7 @@ def run_conv(args, rank: int, world: int, local_rank: int) -> None:
     if rank == 0:
         pk = peaks()
         tflops = cw.flops / (gemm_ms / 1e3) / 1e12
-        peak = pk["bf16_tflops"] * 4.0 / 3.0
+        peak = pk["bf16_tflops"] * 4.0 / (3.0 if cw.wfmt == 0 else 9.0)
         line = {
             "metric": cw.metric, "value": world * cw.flops / (ms / 1e3) / 1e12,
             "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -929,7 +1035,7 @@ def run_conv(args, rank: int, world: int, local_rank: int) -> None:
             "dtype": "int8 block dot + fp32 accumulate", "data": "synthetic",
             "config": {"workload": cw.name, "M": cw.M, "N": cw.cout, "K": cw.K,
                        "images": cw.images, "map": f"{cw.H}x{cw.W}x{cw.cin}",
-                       "kernel": f"{cw.kh}x{cw.kh}", "format": "mxfp4", "bias": True,
+                       "kernel": f"{cw.kh}x{cw.kh}", "format": FMT_NAMES[cw.wfmt], "bias": True,
                        "mode": args.mode, "activations": "fp32 NHWC map, encoded and gathered "
                                                          "on device each step",
                        "l2": f"{cw.instances} instances rotated, ~"
@@ -943,10 +1049,14 @@ def run_conv(args, rank: int, world: int, local_rank: int) -> None:
                          **tensor_fracs(tflops, pk, cw.wfmt),
                          "useful_ceiling": {"peak": peak, "frac": tflops / peak,
                                             "how": "cuBLAS BF16 x 4/3: FP4 MMA rate over three "
+                                                   "digit planes" if cw.wfmt == 0 else
+                                                   "cuBLAS BF16 x 4/9: FP4 MMA rate over 3 x 3 "
                                                    "digit planes"},
                          "alg_flops_per_launch": cw.flops, "traffic": None,
                          "launch_ms": gemm_ms},
-            "encoder": {"kernels": "k_quantize_planes (map) + k_conv_gather_tiles"
+            "encoder": {"kernels": ("k_quantize_planes (map; the GEMM gathers its blocks)"
+                                    if cw.wfmt == 0 else
+                                    "k_quantize_planes (map) + k_conv_gather_tiles")
                                    if mode == capi.MODE_FAST else "encoder + im2col",
                         "launch_ms": prep_ms, "per_kernel_ms": kernel_ms},
             "e2e": e2e, "gpu_launches": launches, "clocks": clocks.summary(),
@@ -1451,7 +1561,7 @@ def run_conv_shard(args, rank: int, world: int, local_rank: int) -> None:
     import torch.distributed as dist
 
     from hotarubi_b200 import capi, shard
-    cw = CONV
+    cw = CONVS[args.config]
     torch.cuda.set_device(local_rank)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", local_rank))
@@ -1507,7 +1617,8 @@ def run_conv_shard(args, rank: int, world: int, local_rank: int) -> None:
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int8 block dot + fp32 accumulate", "data": "synthetic",
             "config": {"workload": cw.name, "M": cw.M, "N": cw.cout, "K": cw.K,
-                       "images": cw.images, "format": "mxfp4", "bias": True, "mode": "fast",
+                       "images": cw.images, "format": FMT_NAMES[cw.wfmt], "bias": True,
+                       "mode": "fast",
                        "parallelism": f"M-sharded (images) x{world}, all-gather along M fused "
                                       "into the GEMM epilogue (NVLink peer stores)"},
             "nvlink": {"bytes_per_rank_per_step": nvlink,
@@ -1524,13 +1635,451 @@ def run_conv_shard(args, rank: int, world: int, local_rank: int) -> None:
     dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# C4: the action expert's whole job
+
+def expert_cpu_reference(ew: ExpertWorkload, min_seconds: float = 0.5) -> dict:
+    """The reference has no MXFP8 path, so the oracle's C restatement (one
+    thread) stands in: one request's self-attention layer (7 GEMMs at 50
+    rows) and one cross-attention K/V pair (141 rows), each timed; the job's
+    rate is its FLOPs over the time those shapes predict."""
+    secs = {}
+    parts = []
+    for label, gm in list(ew.self_layer) + [("kv", ew.cross_kv)]:
+        for name, k, n in gm:
+            m = ew.prefix if label == "kv" else ew.tokens
+            wl = Workload(f"c4{name}", f"c4_{name}", f"C4 {name} {m}x{k}x{n}", ew.wfmt, m, n, k,
+                          False, 1, "tensor")
+            r = cpu_reference(wl, min_seconds=min_seconds, max_reps=5)
+            secs[(m, k, n)] = 2 * m * k * n / (r["value"] * 1e12)
+            parts.append(r)
+
+    def t(m, k, n):  # seconds for m rows of (k, n), scaled from the timed rows
+        base = ew.prefix if (k, n) in [(kk, nn) for _, kk, nn in ew.cross_kv] else ew.tokens
+        key = next((x for x in secs if x[0] == base and x[1:] == (k, n)), None)
+        if key is None:  # the heads: the closest timed shape by MACs
+            key = min(secs, key=lambda x: abs(x[1] * x[2] - k * n))
+            return secs[key] * (m * k * n) / (key[0] * key[1] * key[2])
+        return secs[key] * m / key[0]
+
+    m, mp = ew.rows(1)
+    total = ew.steps * sum(t(m, k, n) for _, gm in ew.step_groups() for _, k, n in gm)
+    total += (ew.layers // 2) * sum(t(mp, k, n) for _, k, n in ew.cross_kv)
+    return {"value": ew.flops() / total / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+            "sample": "one request's self-attention layer (7 GEMMs, 50 rows) and one "
+                      "cross K/V pair (141 rows) through the oracle's MXFP8 chain on 1 thread "
+                      "(the reference has no MXFP8), scaled to the job's shapes",
+            "seconds": total}
+
+
+def run_expert(args, rank: int, world: int, local_rank: int) -> None:
+    """--config c4: the action expert's job (ExpertWorkload) as one CUDA graph
+    of plan runs: the cross K/V plan, then per flow step the 68 dependency
+    groups in order.  The requests split over the ranks (strong scaling,
+    no collective: requests are independent)."""
+    import torch
+
+    from hotarubi_b200 import capi, workloads
+    ew = EXPERT
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        warm, timed = min(args.warmup, 1), max(1, min(args.steps, 5))
+        runs = [expert_cpu_reference(ew, 0.2) for _ in range(warm + timed)][warm:]
+        value = statistics.median(r["value"] for r in runs)
+        base = runs[-1]
+        print(json.dumps({
+            "impl": "reference", "metric": ew.metric, "value": value, "unit": "TFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ew.flops() / (value * 1e12) * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "e4m3 x int8 block dot + fp32 accumulate", "data": "synthetic",
+            "config": {"workload": ew.name, "sample": base["sample"]},
+            "cpu_baseline": {k: v for k, v in base.items() if k != "seconds"} | {"value": value},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    lib = capi.Library(local_rank)
+    mode = capi.MODE_FAST if args.mode == "fast" else capi.MODE_EXACT
+    stream = torch.cuda.Stream()
+    lib.set_stream(stream.cuda_stream)
+    m, mp = ew.rows(world)
+    gen = torch.Generator(device="cuda")
+
+    def synthetic(seed, rows, k):
+        gen.manual_seed(seed)
+        x = torch.randn((rows, k), generator=gen, device="cuda", dtype=torch.float32)
+        return x / x.pow(2).mean(dim=1, keepdim=True).sqrt()
+
+    keep = []
+
+    def group_plan(seed, rows, gemms, separate_inputs=False):
+        """One plan over a dependency group's GEMMs (one shared input)."""
+        x = None
+        descs = []
+        for j, (name, k, n) in enumerate(gemms):
+            if x is None or separate_inputs:
+                x = synthetic(seed + 97 * j, rows, k)
+            kp = (k + 31) // 32 * 32
+            w, ws = workloads.mxfp8_weights(seed + j, n, kp)
+            w[:, k:] = 0
+            t = {"x": x, "w": torch.from_numpy(w).cuda(), "ws": torch.from_numpy(ws).cuda(),
+                 "c": torch.empty((rows, n), dtype=torch.float32, device="cuda")}
+            keep.append(t)
+            descs.append(capi.Library.desc(ew.wfmt, rows, n, k, a=t["x"], w=t["w"],
+                                           wscale=t["ws"], c=t["c"], mode=mode))
+        return lib.plan(descs)
+
+    # Cross K/V of the prefix: the 8 cross layers' K and V projections in one
+    # plan (independent GEMMs), each layer's prefix states its own input.
+    kv_descs = []
+    for layer in range(1, ew.layers, 2):
+        for j, (name, k, n) in enumerate(ew.cross_kv):
+            if j == 0:
+                x = synthetic(50_000 + layer, mp, k)
+            w, ws = workloads.mxfp8_weights(60_000 + 10 * layer + j, n, k)
+            t = {"x": x, "w": torch.from_numpy(w).cuda(), "ws": torch.from_numpy(ws).cuda(),
+                 "c": torch.empty((mp, n), dtype=torch.float32, device="cuda")}
+            keep.append(t)
+            kv_descs.append(capi.Library.desc(ew.wfmt, mp, n, k, a=t["x"], w=t["w"],
+                                              wscale=t["ws"], c=t["c"], mode=mode))
+    kv_plan = lib.plan(kv_descs)
+    kv_inputs = [t["x"] for t in keep[::2]]
+    plans = []
+    labels = []
+    for gi, (label, gemms) in enumerate(ew.step_groups()):
+        plans.append(group_plan(1000 * (gi + 1), m, gemms,
+                                separate_inputs=label == "head.time_mlp_in"))
+        labels.append(label)
+    x_noise = keep[len(kv_descs)]["x"]          # action_in's input (the noise x_t)
+    v_out = keep[-1]["c"]                      # action_out's output (the velocity)
+    torch.cuda.synchronize()
+
+    def job(s):
+        n = kv_plan.run(s)
+        for _ in range(ew.steps):
+            for pl in plans:
+                n += pl.run(s)
+        return n
+
+    launches_per_job = job(stream.cuda_stream)   # warm (kernel attributes set)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        job(stream.cuda_stream)
+    torch.cuda.synchronize()
+    # The heaviest group: a layer's gate + up, profiled alone.
+    gu = labels.index("L0.gate_up")
+    per_plan = plans[gu].profile(reps=20, stream=stream.cuda_stream)
+    gemm_ms = per_plan[-1] if mode == capi.MODE_FAST else max(per_plan)
+    if dist is not None:
+        dist.barrier()
+    with ClockSampler(local_rank) as clocks:
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                graph.replay()
+        stream.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        with torch.cuda.stream(stream):
+            marks[0].record(stream)
+            for i in range(args.steps):
+                graph.replay()
+                marks[i + 1].record(stream)
+        marks[-1].synchronize()
+        if dist is not None:
+            dist.barrier()
+    lib.sync()
+    ms = marks[0].elapsed_time(marks[-1]) / args.steps
+    trials = trial_stats([marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)])
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # End to end: the job's inputs from pinned host memory (the noise and the
+    # 8 cross layers' prefix states), the graph, the velocity back.
+    e2e = None
+    if not args.no_e2e:
+        hx = x_noise.cpu().pin_memory()
+        hkv = [x.cpu().pin_memory() for x in kv_inputs]
+        hv = torch.empty(tuple(v_out.shape), dtype=torch.float32).pin_memory()
+        n_e2e = max(1, min(args.steps, 5))
+        for k in range(1 + n_e2e):
+            if k == 1:
+                stream.synchronize()
+                w0 = time.perf_counter()
+            with torch.cuda.stream(stream):
+                x_noise.copy_(hx, non_blocking=True)
+                for d, h in zip(kv_inputs, hkv):
+                    d.copy_(h, non_blocking=True)
+                graph.replay()
+                hv.copy_(v_out, non_blocking=True)
+            stream.synchronize()
+        dt = (time.perf_counter() - w0) / n_e2e
+        if dist is not None:
+            t = torch.tensor([dt], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt = float(t.item())
+        h2d = hx.numel() * 4 + sum(h.numel() * 4 for h in hkv)
+        e2e = {"value": ew.flops(world) / dt / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": world * h2d, "d2h_bytes_per_step": world * hv.numel() * 4,
+               "ms_per_step": dt * 1e3,
+               "entry_point": "pinned copies + the job's hrb_plan_run calls in a CUDA graph "
+                              "(weights resident)"}
+    if rank == 0:
+        pk = peaks()
+        gu_flops = sum(2 * m * k * n for _, k, n in ew.step_groups()[gu][1])
+        tflops = gu_flops / (gemm_ms / 1e3) / 1e12
+        w_bytes = sum(n * ((k + 31) // 32) * 33 for _, gm in ew.step_groups() for _, k, n in gm)
+        line = {
+            "metric": ew.metric, "value": ew.flops(world) / (ms / 1e3) / 1e12,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "e4m3 x int8 block dot + fp32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": ew.name, "requests": ew.requests,
+                       "requests_per_gpu": ew.requests // world, "rows_per_gemm": m,
+                       "prefix_rows_per_gemm": mp, "flow_steps": ew.steps,
+                       "layers": ew.layers, "format": "mxfp8", "bias": False,
+                       "mode": args.mode,
+                       "activations": "fp32 per dependency group (synthetic, RMS 1 rows), "
+                                      "encoded on device by each plan run",
+                       "l2": f"activations {m} rows per GEMM, {w_bytes * ew.layers / 1e6:.0f}"
+                             " MB of weights per flow step; no flush (the job's own data "
+                             "exceeds L2 many times)",
+                       "parallelism": f"requests split x{world} (data parallel, no collective)",
+                       "launch": f"{1 + ew.steps * len(plans)} plan runs in one CUDA graph"},
+            "trials": trials,
+            "roofline": {"bound": "tensor",
+                         "kernel": "k_gemm_mxf4 (kind::mxf8f6f4; a layer's gate + up, one "
+                                   "launch)" if mode == capi.MODE_FAST else "k_dense_exact",
+                         "achieved": tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": tflops / pk["bf16_tflops"],
+                         "peak_source": pk["source"] + " (cuBLAS BF16 dense)",
+                         **tensor_fracs(tflops, pk, ew.wfmt),
+                         "alg_flops_per_launch": gu_flops, "traffic": None,
+                         "launch_ms": gemm_ms},
+            "e2e": e2e, "gpu_launches": launches_per_job * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = {k: v for k, v in expert_cpu_reference(ew).items()
+                                    if k != "seconds"}
+        print(json.dumps(line), flush=True)
+    del graph
+    kv_plan.close()
+    for pl in plans:
+        pl.close()
+    lib.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# The C5 sweep: 27 GEMMs and the conv, one command
+
+SWEEP_M = (256, 4096, 65536)
+SWEEP_KN = ((960, 2560), (2560, 960), (4096, 4096))
+SWEEP_FMTS = (1, 0, 2)   # W8, MXFP4, MXFP8
+
+
+def sweep_workloads() -> list[Workload]:
+    """M x (K, N) x format, each with its config's distributions
+    (W8 as C1 with bias, MXFP4 as C2, MXFP8 as C4, no bias)."""
+    out = []
+    for k, n in SWEEP_KN:
+        for m in SWEEP_M:
+            for wfmt in SWEEP_FMTS:
+                f = FMT_NAMES[wfmt]
+                out.append(Workload(f"s_{f}_{m}_{k}_{n}", f"c5sweep_{f}_{m}x{k}x{n}",
+                                    f"C5 sweep {m}x{k}x{n}", wfmt, m, n, k, wfmt == 1, 1,
+                                    "tensor"))
+    return out
+
+
+def run_sweep(args, rank: int, world: int, local_rank: int) -> None:
+    """--config c5sweep (one GPU): every GEMM of the sweep through a plan of B
+    instances (B so that a step's operands exceed 2 x L2), W untimed steps,
+    then K steps each bracketed by events (the median is the figure); the
+    GEMM kernel alone timed over repeated launches (plan profile) for its
+    tensor fractions; parity on the first and last rows; then both conv
+    formats through run_conv.  Prints one JSON line holding every record and
+    writes a markdown table with --summary-md."""
+    import contextlib
+    import io
+
+    import torch
+
+    from hotarubi_b200 import capi
+    if world != 1 or args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": args.impl, "config": "c5sweep",
+                              "unavailable": "the sweep runs on one GPU through this library"}))
+        return
+    torch.cuda.set_device(local_rank)
+    lib = capi.Library(local_rank)
+    stream = torch.cuda.Stream()
+    lib.set_stream(stream.cuda_stream)
+    pk = peaks()
+    records = []
+    cpu_rates = {}
+    x_cache = {}
+    for wl0 in sweep_workloads():
+        if args.sweep_filter and not re.search(args.sweep_filter, wl0.key):
+            continue
+        batch = max(1, -(-320_000_000 // wl0.bytes_step()))
+        wl = dataclasses.replace(wl0, batch=batch)
+        distinct = min(2, batch)
+        sets = []
+        for i in range(distinct):
+            # The three formats of one shape share their activations.
+            key = (wl.M, wl.K, i)
+            if key not in x_cache:
+                from hotarubi_b200 import workloads
+                x_cache = {k2: v for k2, v in x_cache.items() if k2[:2] == key[:2]}
+                x_cache[key] = workloads.activations(100 + i, wl.M, wl.K)
+            _, w, ws, b = host_operands(dataclasses.replace(wl, M=1), i)
+            sets.append((x_cache[key], w, ws, b))
+        a_all = torch.empty((batch, wl.M, wl.K), dtype=torch.float32, device="cuda")
+        c_all = torch.zeros((batch, wl.M, wl.N), dtype=torch.float32, device="cuda")
+        keep = []
+        descs = []
+        for j in range(batch):
+            x, w, ws, b = sets[j % distinct]
+            a_all[j].copy_(torch.from_numpy(x))
+            t = {"w": torch.from_numpy(w).cuda(), "ws": torch.from_numpy(ws).cuda(),
+                 "b": None if b is None else torch.from_numpy(b).cuda()}
+            keep.append(t)
+            descs.append(capi.Library.desc(wl.wfmt, wl.M, wl.N, wl.K, a=a_all[j], w=t["w"],
+                                           wscale=t["ws"], bias=t["b"], c=c_all[j],
+                                           mode=capi.MODE_FAST))
+        plan = lib.plan(descs)
+        torch.cuda.synchronize()
+        kernel_ms = plan.profile(reps=max(3, min(20, int(2e13 / (batch * wl.flops)))),
+                                 stream=stream.cuda_stream)
+        gemm_ms = sum(kernel_ms[1:])
+        with ClockSampler(local_rank) as clocks:
+            for _ in range(args.warmup):
+                plan.run(stream.cuda_stream)
+            marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+            marks[0].record(stream)
+            for i in range(args.steps):
+                plan.run(stream.cuda_stream)
+                marks[i + 1].record(stream)
+            marks[-1].synchronize()
+        trials = trial_stats([marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)])
+        x0, w0, ws0, b0 = sets[0]
+        par = fast_parity(torch, lib, wl, x0, w0, ws0, b0, c_all[0], rows=64, tail=True)
+        step_tf = batch * wl.flops / (trials["median_ms"] / 1e3) / 1e12
+        gemm_tf = batch * wl.flops / (gemm_ms / 1e3) / 1e12
+        rec = {"workload": wl.name, "format": FMT_NAMES[wl.wfmt], "M": wl.M, "K": wl.K,
+               "N": wl.N, "batch": batch, "bias": wl.bias,
+               "step_tflops": step_tf, "trials": trials,
+               "gemm": {"kernel": "k_gemm_mxf4", "launch_ms": gemm_ms, "tflops": gemm_tf,
+                        **tensor_fracs(gemm_tf, pk, wl.wfmt)},
+               "encoder_ms": kernel_ms[0],
+               "hbm_gbs_gemm": batch * wl.bytes_gemm() / (gemm_ms / 1e3) / 1e9,
+               "parity": {k: par[k] for k in ("rows", "outputs", "max_rel_err",
+                                              "within_bound")},
+               "clocks": clocks.summary()}
+        if not args.no_cpu_baseline:
+            ck = (wl.wfmt, wl.K, wl.N)
+            if ck not in cpu_rates:
+                r = cpu_reference(dataclasses.replace(wl, M=256), min_seconds=0.5, max_reps=5)
+                cpu_rates[ck] = {k: v for k, v in r.items() if k != "seconds"}
+            rec["cpu_baseline"] = cpu_rates[ck]
+            rec["vs_cpu"] = step_tf / cpu_rates[ck]["value"]
+        records.append(rec)
+        print(f"# {wl.name}: step {step_tf:.1f} TFLOP/s, GEMM {gemm_tf:.1f} TFLOP/s "
+              f"({rec['gemm']['frac_of_8bit_dense_peak']:.3f} of 8-bit dense), "
+              f"parity {par['within_bound']}", file=sys.stderr, flush=True)
+        plan.close()
+        del a_all, c_all, keep, descs, sets
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    lib.close()
+    conv = []
+    for key in sorted(CONVS):
+        if args.sweep_filter and not re.search(args.sweep_filter, key):
+            continue
+        sub = argparse.Namespace(**vars(args))
+        sub.config = key
+        sub.no_e2e = True
+        buf = io.StringIO()
+        with contextlib.redirect_stdout(buf):
+            run_conv(sub, rank, world, local_rank)
+        for line in buf.getvalue().splitlines():
+            if line.startswith("{"):
+                conv.append(json.loads(line))
+    line = {"metric": "W8/MXFP4/MXFP8 GEMM TFLOP/s (C5 large-M sweep, 27 GEMMs + conv)",
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "data": "synthetic",
+            "peaks": {"bf16_tflops": pk["bf16_tflops"], "hbm_gbs": pk["hbm_gbs"],
+                      "source": pk["source"]},
+            "gemms": records, "conv": conv}
+    print(json.dumps(line), flush=True)
+    if args.summary_md:
+        write_sweep_md(args, line)
+
+
+def write_sweep_md(args, line: dict) -> None:
+    pk = line["peaks"]
+    out = [f"# C5 sweep on one B200: {len(line['gemms'])} GEMMs + conv", "",
+           "Command: `python bench.py --config c5sweep --steps {} --warmup {} "
+           "--summary-md <file>`".format(args.steps, args.warmup), "",
+           f"Peaks ({pk['source']}): dense BF16 {pk['bf16_tflops']:.1f} TFLOP/s (8-bit dense = 2x, "
+           "kind::mxf4 = 4x, kind::mxf8f6f4 = 2x), HBM "
+           f"{pk['hbm_gbs']:.0f} GB/s.", "",
+           "Step = the plan's launches (FP32 activations encoded, then the GEMM) over a batch "
+           "of B instances whose operands exceed 2 x L2; median of the per-step event "
+           "times.  GEMM = the tensor-core kernel alone over repeated launches.  "
+           "Parity: first 32 and last 32 rows against the float64 product, bound "
+           "(K/16 + 4) 2^-23 sum|a w|.", "",
+           "| format | M | K | N | B | step TFLOP/s | spread | GEMM TFLOP/s | of MMA kind's "
+           "dense | of 8-bit dense | GEMM HBM GB/s | max rel err | in bound | vs CPU |",
+           "|---|---|---|---|---|---|---|---|---|---|---|---|---|---|"]
+    for r in line["gemms"]:
+        g = r["gemm"]
+        out.append(f"| {r['format']} | {r['M']} | {r['K']} | {r['N']} | {r['batch']} | "
+                   f"{r['step_tflops']:.1f} | {r['trials']['spread']:.3f} | {g['tflops']:.1f} | "
+                   f"{g['frac_of_kind_dense_peak']:.3f} | {g['frac_of_8bit_dense_peak']:.3f} | "
+                   f"{r['hbm_gbs_gemm']:.0f} | {r['parity']['max_rel_err']:.2e} | "
+                   f"{r['parity']['within_bound']} | "
+                   + (f"{r['vs_cpu']:.0f}x |" if "vs_cpu" in r else "- |"))
+    if line["conv"]:
+        out += ["", "| conv | ms/step | TFLOP/s | GEMM TFLOP/s | of MMA kind's dense | "
+                "of 8-bit dense | CPU (reference, 1 thread) TFLOP/s |", "|---|---|---|---|---|---|---|"]
+        for c in line["conv"]:
+            ro = c["roofline"]
+            cb = c.get("cpu_baseline", {}).get("value")
+            out.append(f"| {c['config']['workload']} | {c['ms_per_step']:.3f} | {c['value']:.1f} | "
+                       f"{ro['achieved']:.1f} | {ro['frac_of_kind_dense_peak']:.3f} | "
+                       f"{ro['frac_of_8bit_dense_peak']:.3f} | "
+                       + (f"{cb:.5f} |" if cb else "- |"))
+    with open(args.summary_md, "w") as f:
+        f.write("\n".join(out) + "\n")
+
+
 def main() -> None:
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", choices=sorted(WORKLOADS) + [PREFIX.key, CONV.key, GACC.key],
+    p.add_argument("--config", choices=sorted(WORKLOADS) + [PREFIX.key, GACC.key, EXPERT.key,
+                                                            "c5sweep"]
+                   + sorted(CONVS),
                    default="c2")
     p.add_argument("--mode", choices=["exact", "fast"], default="fast")
     p.add_argument("--w8-kernel", choices=["planes", "bf16"], default="planes",
@@ -1544,11 +2093,20 @@ def main() -> None:
     p.add_argument("--shard", action="store_true", help="split each GEMM along N (c5conv: the "
                    "images along M) over the ranks, with the all-gather fused into the kernel "
                    "(strong scaling)")
+    p.add_argument("--sweep-filter", default="", help="c5sweep: only the GEMMs (and convs) "
+                   "whose key matches this regex")
+    p.add_argument("--summary-md", default="", help="c5sweep: write a markdown table here")
     args = p.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.config == CONV.key:
+    if args.config == "c5sweep":
+        run_sweep(args, rank, world, local_rank)
+        return
+    if args.config == EXPERT.key:
+        run_expert(args, rank, world, local_rank)
+        return
+    if args.config in CONVS:
         if args.shard and args.impl != "reference":
             run_conv_shard(args, rank, world, local_rank)
         else:

@@ -95,6 +95,38 @@ class GaccDesc(ctypes.Structure):
     ]
 
 
+class Rows(ctypes.Structure):
+    """hrb_rows: activations in the DMA row format (ROW, or ROW_INDEXED with
+    `index`)."""
+    _fields_ = [
+        ("window", ctypes.c_void_p), ("ddr_base", ctypes.c_uint64),
+        ("window_bytes", ctypes.c_uint64), ("tok", ctypes.c_uint32), ("planes", ctypes.c_uint32),
+        ("plane_stride", ctypes.c_uint64), ("ddr_addr", ctypes.c_uint32),
+        ("row_tokens", ctypes.c_uint32), ("row_stride", ctypes.c_uint64),
+        ("index", ctypes.c_void_p),
+    ]
+
+
+NULL_ENTRY = 0xFFFFFFFF
+
+
+def row_unit_bytes(tok: int) -> int:
+    """Bytes of one MXINT8 row-format unit (tok x 32 codes, tok scale bytes
+    padded to 16, or to 32 when tok > 16)."""
+    return tok * 32 + (32 if tok > 16 else 16)
+
+
+def rows(window, ddr_base: int, window_bytes: int, tok: int, planes: int, plane_stride: int,
+         *, ddr_addr: int = 0, row_tokens: int = 0, row_stride: int = 0, index=None) -> Rows:
+    r = Rows()
+    r.window = _ptr(window)
+    r.ddr_base, r.window_bytes = ddr_base, window_bytes
+    r.tok, r.planes, r.plane_stride = tok, planes, plane_stride
+    r.ddr_addr, r.row_tokens, r.row_stride = ddr_addr, row_tokens, row_stride
+    r.index = _ptr(index)
+    return r
+
+
 def header_functions() -> list[str]:
     """Every function include/hrb_gemm.h declares."""
     text = open(HEADER).read()
@@ -130,6 +162,8 @@ def load() -> ctypes.CDLL:
             "hrb_gemm_accesses": (ctypes.c_int, [ctypes.POINTER(GemmCmd), P, P, P, P]),
             "hrb_gemm_dense": (ctypes.c_int, [P, ctypes.POINTER(GemmDesc), P]),
             "hrb_gemm_dense_host": (ctypes.c_int, [P, ctypes.POINTER(GemmDesc)]),
+            "hrb_gemm_rows": (ctypes.c_int, [P, ctypes.POINTER(GemmDesc), ctypes.POINTER(Rows),
+                                             P]),
             "hrb_gemm_dense_noalloc": (ctypes.c_int, [ctypes.POINTER(GemmDesc), P]),
             "hrb_quantize_mxint8": (ctypes.c_int, [P, P, u32, u32, u32, u32, P, P, P]),
             "hrb_plan_create": (ctypes.c_int, [P, ctypes.POINTER(GemmDesc), u32,
@@ -423,6 +457,11 @@ class Library:
 
     def dense(self, d: GemmDesc, stream: int = 0) -> None:
         self._check(self.lib.hrb_gemm_dense(self.ctx, ctypes.byref(d), stream or None))
+
+    def gemm_rows(self, d: GemmDesc, r: Rows, stream: int = 0) -> None:
+        """hrb_gemm_rows: d's activations from the row-format source r."""
+        self._check(self.lib.hrb_gemm_rows(self.ctx, ctypes.byref(d), ctypes.byref(r),
+                                           stream or None))
 
     def dense_host(self, d: GemmDesc) -> None:
         self._check(self.lib.hrb_gemm_dense_host(self.ctx, ctypes.byref(d)))

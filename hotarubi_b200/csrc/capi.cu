@@ -802,6 +802,13 @@ hrb_status hrb_sync(hrb_ctx* ctx) {
     HRB_CUDA(ctx, cudaMemset(ctx->d_error, 0, sizeof(uint32_t)));
     if (flag & 2u) return fail(ctx, HRB_ECUDA, "a tensor-core GEMM timed out waiting");
     if (flag & 4u) return fail(ctx, HRB_EDATA, "a GACC entry names a row outside the feature rows");
+    if (flag & hrb::kErrRowOutside) {
+      return fail(ctx, HRB_EDATA, "a ROW_INDEXED entry names a unit outside the DDR window");
+    }
+    if (flag & hrb::kErrScaleRange) {
+      return fail(ctx, HRB_EDATA, "an activation scale byte of 255 has no tensor-core encoding "
+                                  "(use HRB_MODE_EXACT)");
+    }
     return fail(ctx, HRB_EDATA, "MXINT8 input is infinite or NaN");
   }
   return HRB_OK;
@@ -1056,6 +1063,132 @@ hrb_status hrb_gemm_dense(hrb_ctx* ctx, const hrb_gemm_desc* d, void* stream) {
   st = run_dense(ctx, make_dense_job(d, aq, ascale, pieces, npieces), s);
   if (st != HRB_OK || d->cq == nullptr) return st;
   const hrb::QuantJob pq = post_quant_job(d);
+  hrb::launch_quantize(nullptr, 1, &pq, pq.units, ctx->d_error, ctx->sm_count, s);
+  ctx->launches += 1;
+  HRB_CUDA(ctx, cudaGetLastError());
+  return HRB_OK;
+}
+
+namespace {
+
+// The row-format source of hrb_gemm_rows, checked against M and K.
+hrb_status make_rows_src(hrb_ctx* ctx, const hrb_gemm_desc* d, const hrb_rows* r,
+                         hrb::RowsSrc* out) {
+  if (r->window == nullptr || !aligned(r->window, 16)) {
+    return fail(ctx, HRB_EINVAL, "the DDR window is null or not 16-byte aligned");
+  }
+  if (r->ddr_base % 16u != 0) return fail(ctx, HRB_EINVAL, "ddr_base is not a multiple of 16");
+  if (r->tok == 0 || r->tok > 32) return fail(ctx, HRB_EINVAL, "row format with tok = %u", r->tok);
+  if (r->plane_stride % 16u != 0) {
+    return fail(ctx, HRB_EINVAL, "plane_stride is not a multiple of 16");
+  }
+  const uint32_t kb = blocks_of(d->K);
+  if (r->planes == 0 || (kb + r->tok - 1) / r->tok != r->planes) {
+    return fail(ctx, HRB_EINVAL, "%u planes of %u blocks do not hold K = %u", r->planes, r->tok,
+                d->K);
+  }
+  hrb::RowsSrc& s = *out;
+  s = hrb::RowsSrc{};
+  s.window = static_cast<const uint8_t*>(r->window);
+  s.ddr_base = r->ddr_base;
+  s.window_bytes = r->window_bytes;
+  s.index = r->index;
+  s.plane_stride = r->plane_stride;
+  s.row_stride = r->row_stride;
+  s.tok = r->tok;
+  s.planes = r->planes;
+  s.row_tokens = r->row_tokens;
+  s.unit_bytes = r->tok * 32u + (r->tok > 16 ? 32u : 16u);
+  s.kb = kb;
+  s.kp = kb * 32u;
+  if (r->index != nullptr) {
+    if (!aligned(r->index, 4)) return fail(ctx, HRB_EINVAL, "the index list is not 4-byte aligned");
+    return HRB_OK;
+  }
+  if (r->row_tokens == 0 || r->row_tokens % 4u != 0) {
+    return fail(ctx, HRB_EINVAL, "row format with %u tokens a row, not a multiple of 4",
+                r->row_tokens);
+  }
+  if (r->row_stride % 16u != 0) return fail(ctx, HRB_EINVAL, "row_stride is not a multiple of 16");
+  const uint64_t first = uint64_t{r->ddr_addr} * 16u;
+  if (first < r->ddr_base) return fail(ctx, HRB_EINVAL, "ddr_addr lies before the window");
+  s.first = first - r->ddr_base;
+  // The farthest unit: the last row's last token, or the full row before it.
+  const uint64_t rt = r->row_tokens, q = (d->M - 1u) / rt;
+  uint64_t far = q * r->row_stride + ((d->M - 1u) % rt) * s.unit_bytes;
+  if (q > 0) far = std::max<uint64_t>(far, (q - 1) * r->row_stride + (rt - 1) * s.unit_bytes);
+  far += s.first + uint64_t{r->planes - 1u} * r->plane_stride + s.unit_bytes;
+  if (far > r->window_bytes) {
+    return fail(ctx, HRB_EINVAL, "row-format units reach byte %llu of a %llu-byte window",
+                static_cast<unsigned long long>(far),
+                static_cast<unsigned long long>(r->window_bytes));
+  }
+  return HRB_OK;
+}
+
+}  // namespace
+
+hrb_status hrb_gemm_rows(hrb_ctx* ctx, const hrb_gemm_desc* desc, const hrb_rows* rows,
+                         void* stream) {
+  if (ctx == nullptr) return HRB_EINVAL;
+  if (desc == nullptr || rows == nullptr) return fail(ctx, HRB_EINVAL, "null descriptor");
+  if (desc->a != nullptr || desc->aq != nullptr || desc->ascale != nullptr) {
+    return fail(ctx, HRB_EINVAL, "row-format activations replace a, aq and ascale");
+  }
+  if (desc->c == nullptr) return fail(ctx, HRB_EINVAL, "row-format activations need the output c");
+  if (desc->M == 0 || desc->K == 0) return fail(ctx, HRB_EINVAL, "empty GEMM");
+  hrb::RowsSrc src;
+  hrb_status st = make_rows_src(ctx, desc, rows, &src);
+  if (st != HRB_OK) return st;
+  // The descriptor's own checks, with the window standing in for the codes.
+  hrb_gemm_desc d = *desc;
+  d.aq = static_cast<const int8_t*>(rows->window);
+  d.ascale = static_cast<const uint8_t*>(rows->window);
+  uint32_t plane_pieces[hrb::kMaxPieces];
+  if (d.pieces == nullptr || d.npieces == 0) {
+    if (rows->planes > hrb::kMaxPieces) {
+      return fail(ctx, HRB_EINVAL, "%u planes (at most %u K pieces)", rows->planes,
+                  hrb::kMaxPieces);
+    }
+    for (uint32_t p = 0; p < rows->planes; ++p) {
+      plane_pieces[p] = std::min(rows->tok, src.kb - p * rows->tok);
+    }
+    d.pieces = plane_pieces;
+    d.npieces = rows->planes;
+  }
+  uint32_t pieces[hrb::kMaxPieces];
+  uint32_t npieces = 0;
+  st = check_desc(ctx, &d, pieces, &npieces);
+  if (st != HRB_OK) return st;
+  HRB_CUDA(ctx, cudaSetDevice(ctx->device));
+  cudaStream_t s = pick(ctx, stream);
+  if (d.mode == HRB_MODE_FAST) {
+    const uint32_t pf = tc_fmt(&d);
+    st = grow(ctx, &ctx->scratch, &ctx->scratch_bytes, tc_scratch_bytes(&d, pf));
+    if (st != HRB_OK) return st;
+    hrb::QuantJob qj;
+    hrb::TcJob tj;
+    tc_jobs(&d, pf, static_cast<uint8_t*>(ctx->scratch), &qj, &tj);
+    HRB_CUDA(ctx, cudaMemsetAsync(ctx->scratch, 0, align_up(tc_act_bytes(&d, pf), 1024), s));
+    tc_translate(&d, tj, s);
+    hrb::launch_rows_planes(src, qj, ctx->d_error, ctx->sm_count, s);
+    tj.tile_begin = 0;
+    const int n = hrb::launch_mxf4(nullptr, &tj, qj.tile_rows, tj.wfmt, tj.m_tiles * tj.n_tiles,
+                                   ctx->sm_count, ctx->d_error, s);
+    if (n < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
+    ctx->launches += 2u + static_cast<uint64_t>(n);
+    HRB_CUDA(ctx, cudaGetLastError());
+    return HRB_OK;
+  }
+  st = grow(ctx, &ctx->scratch, &ctx->scratch_bytes, act_scratch_bytes(d.M, d.K));
+  if (st != HRB_OK) return st;
+  auto* q = static_cast<int8_t*>(ctx->scratch);
+  auto* sc = reinterpret_cast<uint8_t*>(ctx->scratch) + align_up(size_t{d.M} * src.kb * 32u, 256);
+  hrb::launch_rows_dense(src, d.M, q, sc, ctx->d_error, ctx->sm_count, s);
+  ctx->launches += 1;
+  st = run_dense(ctx, make_dense_job(&d, q, sc, pieces, npieces), s);
+  if (st != HRB_OK || d.cq == nullptr) return st;
+  const hrb::QuantJob pq = post_quant_job(&d);
   hrb::launch_quantize(nullptr, 1, &pq, pq.units, ctx->d_error, ctx->sm_count, s);
   ctx->launches += 1;
   HRB_CUDA(ctx, cudaGetLastError());

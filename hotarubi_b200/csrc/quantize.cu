@@ -317,6 +317,10 @@ __device__ __forceinline__ float max_nan_abs(uint32_t a, uint32_t b) {
   return r;
 }
 
+__device__ __forceinline__ void write_planes(const PlaneJob& j, const PlaneOut& o, uint32_t step,
+                                             const float (&t)[8], uint32_t scale, uint32_t lane,
+                                             const uint32_t* lut);
+
 template <bool kVec>
 __device__ __forceinline__ void encode_planes(const PlaneJob& j, const PlaneOut& o, uint32_t step,
                                               uint32_t v[8], uint32_t lane, uint32_t& bad,
@@ -375,6 +379,16 @@ __device__ __forceinline__ void encode_planes(const PlaneJob& j, const PlaneOut&
                                                : quantize_host_rule(v[i], e));
     }
   }
+  write_planes(j, o, step, t, scale, lane, lut);
+}
+
+// The lane's eight codes of one unit, t[i] = q + 1.5 * 2^23 (q in the low
+// byte of the bits), with their block's scale byte, into the operand blocks:
+// BF16 values, two E4M3 digit planes or three E2M1 digit planes.
+__device__ __forceinline__ void write_planes(const PlaneJob& j, const PlaneOut& o, uint32_t step,
+                                             const float (&t)[8], uint32_t scale, uint32_t lane,
+                                             const uint32_t* lut) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
   if (j.bf16) {
     // q * 2^(scale - 133) in FP32, exact (a power-of-two multiple of an
     // integer below 2^8, at least 2^-133: a subnormal at worst, with the
@@ -977,6 +991,178 @@ void launch_quantize_planes(const QuantJob* jobs_dev, uint32_t njobs, const Quan
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaLaunchKernelEx(&cfg, kFns[variant], jobs_dev, njobs, one, error_flag);
+}
+
+// ---------------------------------------------------------------------------
+// MXINT8 activations (row format or dense) to the tensor-core operands.
+
+namespace {
+
+// The unit of token m, plane p: its window offset, or ~0 for a null entry;
+// sets `outside` when the unit leaves the window.
+__device__ __forceinline__ uint64_t rows_unit(const RowsSrc& s, uint32_t m, uint32_t p,
+                                              bool& outside) {
+  uint64_t off;
+  if (s.index != nullptr) {
+    const uint32_t e = s.index[m];
+    if (e == 0xFFFFFFFFu) return ~uint64_t{0};
+    const uint64_t addr = uint64_t{e} * 16u;
+    if (addr < s.ddr_base) {
+      outside = true;
+      return ~uint64_t{0};
+    }
+    off = addr - s.ddr_base;
+  } else {
+    off = s.first + uint64_t{m / s.row_tokens} * s.row_stride +
+          uint64_t{m % s.row_tokens} * s.unit_bytes;
+  }
+  off += uint64_t{p} * s.plane_stride;
+  if (off + s.unit_bytes > s.window_bytes) {
+    outside = true;
+    return ~uint64_t{0};
+  }
+  return off;
+}
+
+// Eight codes (bytes 8 c .. 8 c + 7 of block b) of token m and the block's
+// scale byte; a null entry or a block past kb reads as zero codes with
+// scale 127 (the null unit of LoadRows, dma_engine.cpp:250-255).
+__device__ __forceinline__ void rows_load8(const RowsSrc& s, uint32_t m, uint32_t b, uint32_t c,
+                                           uint2& codes, uint32_t& scale, bool& outside) {
+  codes = make_uint2(0u, 0u);
+  scale = 127u;
+  if (b >= s.kb) return;
+  if (s.window == nullptr) {
+    codes = *reinterpret_cast<const uint2*>(s.aq + size_t{m} * s.kp + b * 32u + c * 8u);
+    scale = s.ascale[size_t{m} * s.kb + b];
+    return;
+  }
+  const uint32_t p = b / s.tok, t = b % s.tok;
+  const uint64_t off = rows_unit(s, m, p, outside);
+  if (off == ~uint64_t{0}) return;
+  const uint8_t* unit = s.window + off;
+  codes = *reinterpret_cast<const uint2*>(unit + t * 32u + c * 8u);
+  scale = unit[s.tok * 32u + t];
+}
+
+__global__ void __launch_bounds__(256)
+k_rows_planes(const __grid_constant__ RowsSrc src, const __grid_constant__ QuantJob qj,
+              uint32_t* error_flag) {
+  __shared__ uint32_t lut[256];  // q -> its three E2M1 digit codes, as k_quantize_planes's
+  {
+    constexpr float kMagic = 12582912.0f;
+    const float q = static_cast<float>(static_cast<int8_t>(threadIdx.x & 0xFFu));
+    const float d2 = __fadd_rn(__fmaf_rn(q, 0.015625f, kMagic), -kMagic);
+    const float r = __fmaf_rn(d2, -64.0f, q);
+    const float d1 = __fadd_rn(__fmaf_rn(r, 0.125f, kMagic), -kMagic);
+    const float d0 = __fmaf_rn(d1, -8.0f, r);
+    const float d[8] = {d0, d1, d2, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    const uint32_t packed = pack_e2m1x8(d);
+    lut[threadIdx.x] = (packed & 0xFu) | ((packed >> 4) & 0xFu) << 8 | ((packed >> 8) & 0xFu) << 16;
+  }
+  __syncthreads();
+  sm100::griddep_launch_dependents();
+  sm100::griddep_wait();
+  constexpr float kMagic = 12582912.0f;
+  const PlaneJob j = plane_job(qj);
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint64_t warp = (uint64_t{blockIdx.x} * blockDim.x + threadIdx.x) >> 5;
+  const uint64_t nwarps = (uint64_t{gridDim.x} * blockDim.x) >> 5;
+  uint32_t bad = 0;
+  bool outside = false;
+  const bool e2m1 = !j.f8 && !j.bf16;
+  for (uint64_t u = warp; u < j.units; u += nwarps) {
+    // Unit (row m, 256-element group g): lane l holds elements 8 l .. 8 l + 7,
+    // block 8 g + l / 4.
+    const uint32_t m = static_cast<uint32_t>(u / j.k_steps);
+    const uint32_t g = static_cast<uint32_t>(u % j.k_steps);
+    uint2 codes;
+    uint32_t scale;
+    rows_load8(src, m, g * 8u + lane / 4u, lane & 3u, codes, scale, outside);
+    float t[8];
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) {
+      const uint32_t word = i < 4 ? codes.x : codes.y;
+      t[i] = kMagic + static_cast<float>(static_cast<int8_t>((word >> (8u * (i & 3u))) & 0xFFu));
+    }
+    // As the FP32 encoders: E2M1 and E4M3 planes of a block with scale < 6
+    // start below E8M0's range and the block is zero; E2M1's top plane
+    // needs scale + 0 <= 254.
+    if (!j.bf16 && scale < 6u) {
+#pragma unroll
+      for (uint32_t i = 0; i < 8; ++i) t[i] = kMagic;
+    }
+    if (e2m1 && scale == 255u) bad |= kErrScaleRange;
+    write_planes(j, plane_out(j, m, lane), g, t, scale, lane, lut);
+  }
+  if (outside) bad |= kErrRowOutside;
+  bad = __reduce_or_sync(0xFFFFFFFFu, bad);
+  if (bad != 0 && lane == 0) atomicOr(error_flag, bad);
+}
+
+// Dense codes and scales: one warp per (token, group of 8 blocks); lane l
+// copies 8 bytes of block 8 g + l / 4, lanes l % 4 == 0 the scale byte.
+__global__ void __launch_bounds__(256)
+k_rows_dense(const __grid_constant__ RowsSrc src, uint32_t M, int8_t* aq, uint8_t* ascale,
+             uint32_t* error_flag) {
+  sm100::griddep_launch_dependents();
+  sm100::griddep_wait();
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint64_t warp = (uint64_t{blockIdx.x} * blockDim.x + threadIdx.x) >> 5;
+  const uint64_t nwarps = (uint64_t{gridDim.x} * blockDim.x) >> 5;
+  const uint32_t groups = (src.kb + 7u) / 8u;
+  bool outside = false;
+  for (uint64_t u = warp; u < uint64_t{M} * groups; u += nwarps) {
+    const uint32_t m = static_cast<uint32_t>(u / groups);
+    const uint32_t b = static_cast<uint32_t>(u % groups) * 8u + lane / 4u;
+    if (b >= src.kb) continue;
+    uint2 codes;
+    uint32_t scale;
+    rows_load8(src, m, b, lane & 3u, codes, scale, outside);
+    *reinterpret_cast<uint2*>(aq + size_t{m} * src.kb * 32u + b * 32u + (lane & 3u) * 8u) = codes;
+    if ((lane & 3u) == 0) ascale[size_t{m} * src.kb + b] = static_cast<uint8_t>(scale);
+  }
+  if (__any_sync(0xFFFFFFFFu, outside) && lane == 0) atomicOr(error_flag, kErrRowOutside);
+}
+
+void launch_pdl(const void* fn, uint64_t work_warps, int sm_count, cudaStream_t stream,
+                void** args) {
+  uint64_t blocks = (work_warps + 7u) / 8u;
+  const uint64_t cap = static_cast<uint64_t>(sm_count) * 8u;
+  blocks = blocks > cap ? cap : (blocks == 0 ? 1 : blocks);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace
+
+void launch_rows_planes(const RowsSrc& src, const QuantJob& job, uint32_t* error_flag,
+                        int sm_count, cudaStream_t stream) {
+  RowsSrc s = src;
+  QuantJob j = job;
+  uint32_t* e = error_flag;
+  void* args[] = {&s, &j, &e};
+  launch_pdl(reinterpret_cast<const void*>(k_rows_planes), job.units, sm_count, stream, args);
+}
+
+void launch_rows_dense(const RowsSrc& src, uint32_t M, int8_t* aq, uint8_t* ascale,
+                       uint32_t* error_flag, int sm_count, cudaStream_t stream) {
+  RowsSrc s = src;
+  uint32_t m = M;
+  int8_t* q = aq;
+  uint8_t* sc = ascale;
+  uint32_t* e = error_flag;
+  void* args[] = {&s, &m, &q, &sc, &e};
+  launch_pdl(reinterpret_cast<const void*>(k_rows_dense),
+             uint64_t{M} * ((src.kb + 7u) / 8u), sm_count, stream, args);
 }
 
 }  // namespace hrb

@@ -35,3 +35,35 @@ def test_reference_leg_pads_rows_to_the_iss_token_multiple():
     r = bench.cpu_reference(wl, min_seconds=0.01, max_reps=1)
     assert r["kind"] == "reference" and "padded to 64 rows" in r["sample"]
     assert np.isfinite(r["value"]) and r["value"] > 0
+
+
+def test_c4_expert_job_shapes():
+    ew = bench.EXPERT
+    groups = ew.step_groups()
+    # 3 head groups in, 16 layers x 4 groups, 1 head group out.
+    assert len(groups) == 68
+    self_gemms = [g for _, gm in ew.self_layer for g in gm]
+    assert [(k, n) for _, k, n in self_gemms] == [(720, 960), (720, 320), (720, 320),
+                                                 (960, 720), (720, 2048), (720, 2048),
+                                                 (2048, 720)]
+    cross_gemms = [g for _, gm in ew.cross_layer for g in gm]
+    assert [name for name, _, _ in cross_gemms] == ["q", "o", "gate", "up", "down"]
+    assert ew.rows(1) == (12800, 36096) and ew.rows(8) == (1600, 4512)
+    # Strong scaling: the job's FLOPs do not depend on the GPU count.
+    assert ew.flops(1) == ew.flops(2) == ew.flops(8)
+    per_token_step = (8 * sum(2 * k * n for _, k, n in self_gemms)
+                      + 8 * sum(2 * k * n for _, k, n in cross_gemms)
+                      + 2 * (32 * 720 + 3 * 720 * 720 + 720 * 32))
+    kv = 8 * 2 * 2 * 141 * 960 * 320 * 256
+    assert ew.flops() == 10 * 12800 * per_token_step + kv
+
+
+def test_c5_sweep_covers_27_gemms_and_both_convs():
+    wls = bench.sweep_workloads()
+    assert len(wls) == 27 and len({w.key for w in wls}) == 27
+    assert {(w.M, w.K, w.N, w.wfmt) for w in wls} == {
+        (m, k, n, f) for m in (256, 4096, 65536) for k, n in ((960, 2560), (2560, 960),
+                                                              (4096, 4096)) for f in (0, 1, 2)}
+    assert all(w.bias == (w.wfmt == 1) for w in wls)
+    assert bench.CONV.wfmt == 1 and bench.CONV_MXFP4.wfmt == 0
+    assert bench.CONV.M == 48 * 16 * 44 and bench.CONV.K == 9 * 256

@@ -66,6 +66,31 @@ def test_conv_chain_vs_reference(ref_lib, H, W, cin, cout, kh, stride, res, relu
     assert (got == want).all()
 
 
+@pytest.mark.parametrize("H,W,cin,cout,kh,stride,seed", [
+    (4, 3, 64, 8, 3, 1, 5),
+    (8, 6, 256, 24, 3, 2, 6),
+    (4, 5, 512, 16, 1, 1, 7),
+])
+def test_w8_conv_chain_vs_reference(ref_lib, H, W, cin, cout, kh, stride, seed):
+    """W8 weights: each (plane, tap) job chained HI then LO on both sides."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((H * W, cin)).astype(np.float32)
+    aq, asc = cpu.encode_mxint8(x.view(np.uint32))
+    wf = (rng.standard_normal((cout, kh * kh * cin)) * 0.05).astype(np.float32)
+    wq, ws = cpu.encode_mxint8(wf.view(np.uint32))
+    hi, lo = cpu.split_w8(wq)
+    bias = (rng.standard_normal(cout) * 0.1).astype(np.float32).view(np.uint32)
+    ho, wo = H // stride, W // stride
+    want = np.zeros((ho * wo, cout), np.uint32)
+    e = ws.astype(np.int32) - 127
+    assert ref_lib.hrbref_conv_iss_w8(H, W, cin, cout, kh, stride, aq.ravel(), asc.ravel(),
+                                      hi.ravel(), lo.ravel(), e.ravel(), bias, None, 0,
+                                      want.ravel()) == 0
+    got = cpu.conv_dense(cpu.WFMT_W8, aq, asc, 1, H, W, cin, cout, kh, stride,
+                         wq.view(np.uint8), ws, bias_bits=bias)
+    assert (got == want).all()
+
+
 def test_im2col_null_entries_and_chain_order():
     H, W, cin = 4, 4, 64
     aq = np.arange(H * W * cin, dtype=np.int64).astype(np.int8).reshape(H * W, cin)
