@@ -74,6 +74,7 @@ struct hrb_plan {
     uint32_t nt, njobs, tiles;
     const void* d_jobs;  // DenseJob (exact) or TcJob (tensor-core) array
     const hrb::MxTile* d_tiles;  // kind 2: the launch's output tiles
+    bool pairs = false;          // kind 2: d_tiles in pair order (CTA pairs)
   };
   std::vector<Group> groups;
   // Per GEMM, in creation order: the device activations and output the
@@ -1332,7 +1333,7 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
   std::vector<hrb::QuantJob> quant, planes, post;
   std::vector<std::vector<hrb::DenseJob>> exact(3);
   uint32_t exact_tiles[3] = {0, 0, 0};
-  struct TcKey { uint32_t nt, wfmt, kind; };
+  struct TcKey { uint32_t nt, wfmt, kind; bool pairs; };
   std::vector<TcKey> tc_keys;
   std::vector<std::vector<hrb::TcJob>> tc_groups;
   std::vector<uint32_t> tc_tiles;
@@ -1353,20 +1354,22 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
       planes.push_back(qj);
       size_t g = 0;
       const uint32_t kind = 2u;
+      const bool pairs = hrb::mx_pairs(tj.wfmt, tj.n_tiles);
       while (g < tc_keys.size() && !(tc_keys[g].nt == qj.tile_rows && tc_keys[g].wfmt == tj.wfmt &&
-                                     tc_keys[g].kind == kind)) {
+                                     tc_keys[g].kind == kind && tc_keys[g].pairs == pairs)) {
         ++g;
       }
       if (g == tc_keys.size()) {
-        tc_keys.push_back({qj.tile_rows, tj.wfmt, kind});
+        tc_keys.push_back({qj.tile_rows, tj.wfmt, kind, pairs});
         tc_groups.emplace_back();
         tc_tiles.push_back(0);
       }
+      const uint32_t job_tiles = hrb::mx_job_tiles(tj, pairs);
       tj.tile_begin = tc_tiles[g];
-      tc_tiles[g] += tj.m_tiles * tj.n_tiles;
+      tc_tiles[g] += job_tiles;
       tc_groups[g].push_back(tj);
       plan->io[i].tile_begin = tj.tile_begin;
-      plan->io[i].tiles = tj.m_tiles * tj.n_tiles;
+      plan->io[i].tiles = job_tiles;
       continue;
     }
     const int8_t* aq = d.aq;
@@ -1406,7 +1409,7 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
     if (tc_keys[g].kind != 2) continue;
     mx_tiles[g].resize(tc_tiles[g]);
     for (const hrb::TcJob& tj : tc_groups[g]) {
-      hrb::mx_fill_tiles(tj, tc_keys[g].nt, mx_tiles[g].data() + tj.tile_begin);
+      hrb::mx_fill_tiles(tj, tc_keys[g].nt, mx_tiles[g].data() + tj.tile_begin, tc_keys[g].pairs);
     }
     bytes += 16 + mx_tiles[g].size() * sizeof(hrb::MxTile);  // 16: alignment slack
   }
@@ -1454,7 +1457,7 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
                              cudaMemcpyHostToDevice));
     plan->groups.push_back({tc_keys[g].wfmt, tc_keys[g].kind, tc_keys[g].nt,
                             static_cast<uint32_t>(tc_groups[g].size()), tc_tiles[g], dst,
-                            nullptr});
+                            nullptr, tc_keys[g].pairs});
     dst += tc_groups[g].size() * sizeof(hrb::TcJob);
     if (!mx_tiles[g].empty()) {
       auto* base = static_cast<uint8_t*>(plan->d_jobs);
@@ -1508,7 +1511,7 @@ hrb_status plan_launch(hrb_plan* plan, cudaStream_t s, int64_t only, uint32_t* l
           static_cast<const hrb::DenseJob*>(g.d_jobs), g.njobs, nullptr, g.tiles, g.wfmt, s));
     } else {
       const int k = hrb::launch_mxf4(g.d_tiles, nullptr, g.nt, g.wfmt, g.tiles, ctx->sm_count,
-                                     ctx->d_error, s, &plan->peers, true);
+                                     ctx->d_error, s, &plan->peers, true, g.pairs ? 1 : 0);
       if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
       n += static_cast<uint32_t>(k);
     }
@@ -1642,7 +1645,8 @@ hrb_status hrb_plan_run_host(hrb_plan* plan, void* stream, const void* const* a_
     const uint32_t t0 = plan->io[g0].tile_begin;
     const uint32_t t1 = plan->io[g1 - 1].tile_begin + plan->io[g1 - 1].tiles;
     const int k = hrb::launch_mxf4(g.d_tiles + t0, nullptr, g.nt, g.wfmt, t1 - t0,
-                                   ctx->sm_count, ctx->d_error, s, &plan->peers, true);
+                                   ctx->sm_count, ctx->d_error, s, &plan->peers, true,
+                                   g.pairs ? 1 : 0);
     if (k < 0) return fail(ctx, HRB_ECUDA, "tensor-core launch failed");
     ctx->launches += 1u + static_cast<uint64_t>(k);
     HRB_CUDA(ctx, cudaEventRecord(ev[kChunks + c], s));

@@ -37,6 +37,7 @@
 // (for NT = 64 two TMEM accumulator buffers, so one tile's epilogue overlaps
 // the next tile's MMAs).  Every wait is bounded.
 #include <algorithm>
+#include <cstdlib>
 #include <cstdint>
 #include <mutex>
 #include <tuple>
@@ -235,6 +236,26 @@ __device__ __forceinline__ uint64_t desc_sf_chunk(uint32_t smem_byte_addr) {
 __device__ __forceinline__ void sf_copy(uint32_t taddr, uint64_t desc) {
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc)
                : "memory");
+}
+
+// The same for a CTA pair, issued by rank 0: each CTA's chunk at the
+// descriptor's offset of its own shared memory into its own TMEM.
+__device__ __forceinline__ void sf_copy_pair(uint32_t taddr, uint64_t desc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc)
+               : "memory");
+}
+
+// kind::mxf4 MMA of a CTA pair (M = 256: rank 0's 128 rows of A, then rank
+// 1's; B's rows half from each CTA), issued by rank 0.
+__device__ __forceinline__ void mma_mxf4_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%4], [%5], p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
+      : "memory");
 }
 
 // Global -> shared copies of 16 and 4 bytes that complete asynchronously;
@@ -786,6 +807,273 @@ __global__ void __launch_bounds__(MxWarps<NT, WP, KB, kGather>::kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// MXFP4 on CTA pairs (tcgen05 .cta_group::2).
+//
+// The kernel above reads each activation block once per 128-column weight
+// tile, so for the GEMMs of this path the operand traffic from L2 is
+// dominated by activation re-reads (about 1.5 times the weight bytes at
+// 64 tokens, 3 times at 4096), and that L2-to-SM stream, not HBM or the
+// tensor pipe, sets the pace.  Here the two CTAs of a cluster take two
+// adjacent column tiles of the same token tile and run them as one MMA of
+// M = 256: each streams its own weight chunk but only half of the
+// activation block's stacked plane rows (rows [96 r, 96 r + 96) of each
+// 192-row part for rank r; the MMA takes B's rows half from each CTA), plus
+// all the scale chunks (each CTA's TMEM needs the scales of every B row).
+// Activation bytes from L2 halve; the epilogue is the same per CTA (its
+// 128 weight columns x NT tokens in its own TMEM).
+//
+// Roles: warp 0 lane 0 of each CTA streams its stages into its own ring;
+// warp 1 owns the pair's TMEM (allocated by both CTAs together); on rank 0
+// lane 0 of warp 1 issues the scale copies and MMAs for both CTAs once both
+// halves of a stage have landed (rank 1's warp 1 relays its stage
+// completions to rank 0), and its commits free the stage in both CTAs and
+// publish finished accumulators to both epilogues, which hand the
+// accumulator back to rank 0.  Tiles go in pairs: p.tiles in pair order
+// (tile 2u + rank of pair u; a dummy tile with no columns fills an odd
+// column count), or the inline job's. Every wait is bounded; both CTAs meet
+// at a cluster barrier before TMEM is freed.
+template <uint32_t NT>
+struct PairCfg {
+  using Base = MxCfg<NT, 1, 4>;
+  static constexpr uint32_t kParts = Base::kParts;              // 192-row MMA parts
+  static constexpr uint32_t kHalf = Base::kPartRows / 2u;       // stacked rows a CTA a part
+  static constexpr uint32_t kHalfBytes = kHalf * kRowB;         // 12 KB
+  static constexpr uint32_t kSfBytes = kParts * 2048u;          // the block's scale chunks
+  static constexpr uint32_t kABlock = mx_act_block_bytes(NT);   // the block in global memory
+  static constexpr uint32_t kOffA = kWChunk;                    // in a slot: weights, halves, scales
+  static constexpr uint32_t kOffSf = kOffA + kParts * kHalfBytes;
+  static constexpr uint32_t kSlot = kOffSf + kSfBytes;
+  static constexpr uint32_t kSlots = NT == 64 ? 7u : 4u;
+  static constexpr uint32_t kOffBar = kSlots * kSlot;
+  static constexpr uint32_t kStage = Base::kStage;
+  static constexpr uint32_t kOffStage = kOffBar + 512;
+  static constexpr uint32_t kSmem = kOffStage + kStage + 1024;
+  static constexpr uint32_t kEpiWarps = Base::kEpiWarps;
+  static constexpr uint32_t kFirstEpi = 3;
+  static constexpr uint32_t kThreads = 32u * (kFirstEpi + kEpiWarps);
+  static_assert(kSlot % 1024 == 0 && kOffA % 1024 == 0 && kHalfBytes % 1024 == 0, "alignment");
+  static_assert(kSmem <= kSmemLimit, "shared memory");
+};
+
+__host__ __device__ inline MxTile dummy_tile(MxTile t) {
+  t.c = nullptr;
+  t.cq = nullptr;
+  t.cscale = nullptr;
+  t.cols_kbq &= ~0xFFu;
+  t.flags &= ~0x80000000u;
+  return t;
+}
+
+template <uint32_t NT>
+__device__ __forceinline__ MxTile pair_tile(const MxParams& p, uint32_t u, uint32_t rank) {
+  if (p.tiles != nullptr) return tile_info<NT>(p, 2u * u + rank);
+  const TcJob& job = p.inline_job;
+  const uint32_t np = (job.n_tiles + 1u) / 2u;
+  const uint32_t mt = u / np, n = 2u * (u % np) + rank;
+  return n < job.n_tiles ? make_tile(job, NT, mt * job.n_tiles + n)
+                         : dummy_tile(make_tile(job, NT, mt * job.n_tiles + n - 1u));
+}
+
+template <uint32_t NT, bool kEarly>
+__global__ void __launch_bounds__(PairCfg<NT>::kThreads, 1)
+    k_gemm_mxf4_pair(const __grid_constant__ MxParams p) {
+  using Cfg = PairCfg<NT>;
+  using Base = typename Cfg::Base;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  const Ring ring{bars, bars + Cfg::kSlots, Cfg::kSlots};
+  uint64_t* peer_full = bars + 2 * Cfg::kSlots;        // rank 0: rank 1's stage landed
+  uint64_t* acc_full = bars + 3 * Cfg::kSlots;         // [kDBufs]
+  uint64_t* acc_empty = acc_full + Base::kDBufs;       // [kDBufs] rank 0: both epilogues done
+  uint64_t* drained = acc_empty + Base::kDBufs;        // rank 0: every MMA complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const uint32_t rank = cluster_rank();
+  const uint32_t first = blockIdx.x >> 1, stride = gridDim.x >> 1;
+  const uint32_t pairs = p.total_tiles >> 1;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < Cfg::kSlots; ++s) {
+      mbar_init(&ring.full[s], 1);
+      mbar_init(&ring.empty[s], 1);
+      mbar_init(&peer_full[s], 1);
+    }
+    for (uint32_t b = 0; b < Base::kDBufs; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2u * Cfg::kEpiWarps);
+    }
+    mbar_init(drained, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Base::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, the pair's TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+  griddep_launch_dependents();
+  const bool early_weights = p.weights_ready != 0 && warp == 0;
+  if (!early_weights) griddep_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t n = 0;
+      MxTile next = pair_tile<NT>(p, first, rank);
+      for (uint32_t u = first; u < pairs && ok; u += stride) {
+        const MxTile ti = next;
+        if (u + stride < pairs) next = pair_tile<NT>(p, u + stride, rank);
+        const uint32_t k_steps = ti.flags & 0x0FFFFFFFu;
+        uint32_t pre = 0;
+        if (early_weights && n == 0) {
+          pre = k_steps < Cfg::kSlots ? k_steps : Cfg::kSlots;
+          for (uint32_t c = 0; c < pre; ++c) {
+            mbar_arrive_expect_tx(&ring.full[c], Cfg::kSlot);
+            bulk_g2s(smem + c * Cfg::kSlot, ti.w + static_cast<size_t>(c) * kWChunk, kWChunk,
+                     &ring.full[c]);
+          }
+          griddep_wait();
+        }
+        for (uint32_t c = 0; c < k_steps && ok; ++c, ++n) {
+          const uint32_t sl = n % Cfg::kSlots;
+          uint8_t* slot = smem + sl * Cfg::kSlot;
+          if (c >= pre) {
+            ok = ring_acquire(ring, n, Cfg::kSlot, p.err);
+            if (!ok) break;
+            bulk_g2s(slot, ti.w + static_cast<size_t>(c) * kWChunk, kWChunk, &ring.full[sl]);
+          }
+          const uint8_t* blk = ti.a + static_cast<size_t>(c) * Cfg::kABlock;
+#pragma unroll
+          for (uint32_t part = 0; part < Cfg::kParts; ++part) {
+            bulk_g2s(slot + Cfg::kOffA + part * Cfg::kHalfBytes,
+                     blk + (part * Base::kPartRows + rank * Cfg::kHalf) * kRowB, Cfg::kHalfBytes,
+                     &ring.full[sl]);
+          }
+          bulk_g2s(slot + Cfg::kOffSf, blk + 3u * NT * kRowB, Cfg::kSfBytes, &ring.full[sl]);
+        }
+      }
+      if (ok) ring_drain(ring, n, p.err);
+    }
+  } else if (warp == 1 && rank == 1) {
+    // Relay: each landed stage of this CTA, announced to rank 0.
+    if (lane == 0) {
+      uint32_t n = 0;
+      for (uint32_t u = first; u < pairs && ok; u += stride) {
+        const uint32_t k_steps = pair_tile<NT>(p, u, rank).flags & 0x0FFFFFFFu;
+        for (uint32_t c = 0; c < k_steps && ok; ++c, ++n) {
+          const uint32_t sl = n % Cfg::kSlots;
+          ok = mbar_spin(&ring.full[sl], (n / Cfg::kSlots) & 1u, p.err);
+          if (ok) mbar_arrive_cluster(&peer_full[sl], 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      uint32_t n = 0, t = 0;
+      const uint32_t sfa = tmem + Base::kColSfa;
+      for (uint32_t u = first; u < pairs && ok; u += stride, ++t) {
+        const uint32_t k_steps = pair_tile<NT>(p, u, 0).flags & 0x0FFFFFFFu;
+        const uint32_t b = t % Base::kDBufs;
+        if (t >= Base::kDBufs) {
+          ok = mbar_wait_cluster(&acc_empty[b], ((t / Base::kDBufs) - 1) & 1u, p.err);
+        }
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d = tmem + b * Base::kDCols;
+        for (uint32_t i = 0; i < k_steps && ok; ++i, ++n) {
+          const uint32_t sl = n % Cfg::kSlots, par = (n / Cfg::kSlots) & 1u;
+          ok = mbar_wait(&ring.full[sl], par, p.err) && mbar_wait_cluster(&peer_full[sl], par, p.err);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t w_tile = smem_addr(smem + sl * Cfg::kSlot);
+          const uint32_t a_half = w_tile + Cfg::kOffA;
+          const uint32_t a_sf = w_tile + Cfg::kOffSf;
+#pragma unroll
+          for (uint32_t c = 0; c < 2; ++c) {
+            sf_copy_pair(sfa + 4 * c, desc_sf_chunk(w_tile + kTileW * kRowB + c * kSfChunk));
+          }
+#pragma unroll
+          for (uint32_t c = 0; c < Base::kASf; ++c) {
+            sf_copy_pair(tmem + Base::kColSfb + 4 * c, desc_sf_chunk(a_sf + c * kSfChunk));
+          }
+#pragma unroll
+          for (uint32_t k = 0; k < 4; ++k) {
+            const uint32_t grp = k / 2, sf_id = (k % 2) * 2;
+            const uint32_t idesc = idesc_mxf4(2u * kTileW, Base::kPartRows, sf_id);
+#pragma unroll
+            for (uint32_t part = 0; part < Cfg::kParts; ++part) {
+              const uint32_t sfb_k = (tmem + Base::kColSfb + 8 * (part * 2 + grp)) | (sf_id << 30);
+              mma_mxf4_pair(d + Base::kPartRows * part, desc_sw128(w_tile + 32 * k),
+                            desc_sw128(a_half + part * Cfg::kHalfBytes + 32 * k), idesc,
+                            (sfa + 4 * grp) | (sf_id << 30), sfb_k, (i > 0 || k > 0) ? 1u : 0u);
+            }
+          }
+          mma_commit_pair(&ring.empty[sl]);  // the stage is free in both CTAs
+        }
+        if (ok) mma_commit_pair(&acc_full[b]);
+      }
+      // Every MMA issued has completed before the pair's TMEM is freed.
+      asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                   ::"r"(smem_addr(drained))
+                   : "memory");
+      mbar_wait(drained, 0, p.err);
+    }
+  } else if (warp >= Cfg::kFirstEpi) {
+    const uint32_t sp = warp & 3u;
+    constexpr uint32_t kRowsPer = NT / (Cfg::kEpiWarps / 4);
+    const uint32_t r0 = ((warp - Cfg::kFirstEpi) / 4u) * kRowsPer, r1 = r0 + kRowsPer;
+    float* stage = Cfg::kStage != 0
+                       ? reinterpret_cast<float*>(smem + Cfg::kOffStage) + (warp - Cfg::kFirstEpi) * 128u
+                       : nullptr;
+    uint32_t t = 0;
+    for (uint32_t u = first; u < pairs; u += stride, ++t) {
+      const MxTile ti = pair_tile<NT>(p, u, rank);
+      const uint32_t b = t % Base::kDBufs;
+      if (ok) ok = mbar_wait(&acc_full[b], (t / Base::kDBufs) & 1u, p.err);
+      ok = __all_sync(0xFFFFFFFFu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const TileDrain<NT, 3> dr(p, ti, tmem + ((sp * 32u) << 16) + b * Base::kDCols, sp, lane,
+                                stage);
+      const bool early = kEarly && Base::kDBufs == 1 && r1 - r0 == 32u;
+      if (early) {
+        // Both row chunks in registers, then the accumulator goes back.
+        float xa[16], xb[16];
+        dr.load(r0, xa);
+        dr.load(r0 + 16u, xb);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(&acc_empty[b], 0);
+        dr.finish(r0, xa);
+        dr.finish(r0 + 16u, xb);
+      } else {
+#pragma unroll 1
+        for (uint32_t j0 = r0; j0 < r1; j0 += 16) {
+          float x[16];
+          dr.load(j0, x);
+          dr.finish(j0, x);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(&acc_empty[b], 0);
+      }
+    }
+    if (p.peers.count != 0) __threadfence_system();
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // both CTAs done: no more arrivals on rank 0's barriers, no MMA reads
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, Base::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // W8 with at most 64 tokens (path format kTcW8Bf16): kind::f16 on BF16.
 //
 // These GEMMs are bound by the weight stream, so the weights travel as the
@@ -1253,6 +1541,54 @@ int launch_mx(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, 
   return launch_pdl(fn, grid, MxWarps<NT, WP, KB, false>::kThreads, Cfg::kSmem, s, p);
 }
 
+// The CTA-pair kernel: clusters of two, as many as fit at once.
+template <uint32_t NT>
+int launch_pair(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t tiles, int sm_count,
+                uint32_t* err, cudaStream_t s, const MxPeers* peers, bool weights_ready) {
+  using Cfg = PairCfg<NT>;
+  MxParams p{};
+  p.weights_ready = weights_ready ? 1u : 0u;
+  p.tiles = tiles_dev;
+  p.total_tiles = tiles;
+  p.err = err;
+  if (peers != nullptr) p.peers = *peers;
+  if (inline_job != nullptr) p.inline_job = *inline_job;
+  const uint32_t pairs = tiles / 2u;
+  if (pairs == 0) return 0;
+  static int max_clusters[2] = {0, 0};
+  int& mc = max_clusters[NT == 64 ? 0 : 1];
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.blockDim = dim3(Cfg::kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const void* plain = reinterpret_cast<const void*>(k_gemm_mxf4_pair<NT, false>);
+  const void* early = reinterpret_cast<const void*>(k_gemm_mxf4_pair<NT, true>);
+  if (!set_smem_limit_once(plain, Cfg::kSmem) || !set_smem_limit_once(early, Cfg::kSmem)) return -1;
+  if (mc == 0) {
+    cfg.gridDim = dim3(static_cast<unsigned>(sm_count & ~1));
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, plain, &cfg) != cudaSuccess || n < 1) {
+      (void)cudaGetLastError();
+      n = sm_count / 2;
+    }
+    mc = n;
+  }
+  const uint32_t clusters = std::min<uint32_t>(pairs, static_cast<uint32_t>(mc));
+  cfg.gridDim = dim3(2u * clusters);
+  const void* fn = MxCfg<NT, 1, 4>::kDBufs == 1 && pairs >= 3u * clusters ? early : plain;
+  void* args[] = {&p};
+  return cudaLaunchKernelExC(&cfg, fn, args) == cudaSuccess ? 1 : -1;
+}
+
 template <uint32_t NT, uint32_t WP, uint32_t KB>
 struct Pick {
   static constexpr uint32_t kNt = NT, kWp = WP, kKb = KB;
@@ -1317,8 +1653,36 @@ void launch_tile_weights_mxf4(uint32_t wfmt, const uint8_t* w, const uint8_t* ws
       out);
 }
 
-void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out) {
-  for (uint32_t i = 0; i < job.m_tiles * job.n_tiles; ++i) out[i] = make_tile(job, nt, i);
+bool mx_pairs(uint32_t wfmt, uint32_t n_tiles) {
+  // Opt-in (HRB_CTA_PAIRS=1): on the B200 the pair kernel measures slower
+  // than one CTA a tile at every shape of the benchmark (it halves the
+  // activation bytes from L2, but neither kernel is bound by them).
+  static const bool enabled = [] {
+    const char* e = std::getenv("HRB_CTA_PAIRS");
+    return e != nullptr && e[0] == '1';
+  }();
+  return enabled && wfmt == HRB_WFMT_MXFP4 && n_tiles >= 2;
+}
+
+uint32_t mx_job_tiles(const TcJob& job, bool pairs) {
+  return pairs ? job.m_tiles * 2u * ((job.n_tiles + 1u) / 2u) : job.m_tiles * job.n_tiles;
+}
+
+void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out, bool pairs) {
+  if (!pairs) {
+    for (uint32_t i = 0; i < job.m_tiles * job.n_tiles; ++i) out[i] = make_tile(job, nt, i);
+    return;
+  }
+  // Pair order: tiles 2u, 2u + 1 are column tiles 2c, 2c + 1 of one token
+  // tile; an odd last column tile is paired with a dummy (no columns).
+  uint32_t k = 0;
+  for (uint32_t mt = 0; mt < job.m_tiles; ++mt) {
+    for (uint32_t n = 0; n < job.n_tiles; n += 2) {
+      const MxTile a = make_tile(job, nt, mt * job.n_tiles + n);
+      out[k++] = a;
+      out[k++] = n + 1 < job.n_tiles ? make_tile(job, nt, mt * job.n_tiles + n + 1) : dummy_tile(a);
+    }
+  }
 }
 
 int launch_mxf4_gather(const TcJob& inline_job, uint32_t nt, uint32_t tiles, int sm_count,
@@ -1334,10 +1698,18 @@ int launch_mxf4_gather(const TcJob& inline_job, uint32_t nt, uint32_t tiles, int
 
 int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t wfmt,
                 uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t s,
-                const MxPeers* peers, bool weights_ready) {
+                const MxPeers* peers, bool weights_ready, int pairs) {
   if (tiles == 0) return 0;
   if (tiles_dev == nullptr && inline_job == nullptr) return -1;
   if (peers != nullptr && peers->count > kMaxPeers) return -1;
+  if (pairs < 0) pairs = tiles_dev == nullptr && mx_pairs(wfmt, inline_job->n_tiles) ? 1 : 0;
+  if (pairs != 0) {
+    if (wfmt != HRB_WFMT_MXFP4) return -1;
+    if (tiles_dev == nullptr) tiles = mx_job_tiles(*inline_job, true);
+    if (nt == 64) return launch_pair<64>(tiles_dev, inline_job, tiles, sm_count, err, s, peers, weights_ready);
+    if (nt == 128) return launch_pair<128>(tiles_dev, inline_job, tiles, sm_count, err, s, peers, weights_ready);
+    return -1;
+  }
   const auto go = [&](auto cfg) {
     using C = decltype(cfg);
     return launch_mx<C::kNt, C::kWp, C::kKb>(tiles_dev, inline_job, tiles, sm_count, err, s,

@@ -122,8 +122,15 @@ struct MxTile {
                         // | accumulate << 31
 };
 static_assert(sizeof(MxTile) == 64, "MxTile is read as four 16-byte loads");
-// The m_tiles * n_tiles tiles of one job (tile index mt * n_tiles + nt).
-void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out);
+// Whether MXFP4 GEMMs of n_tiles column tiles run on CTA pairs (two
+// adjacent column tiles as one MMA of M = 256; opt-in with the environment
+// variable HRB_CTA_PAIRS=1), the tiles of a job in that order, and the tiles
+// themselves: mt * n_tiles + nt, or in pairs (tiles 2u, 2u + 1 the column
+// tiles 2c, 2c + 1 of one token tile, an odd last one paired with a tile of
+// no columns).
+bool mx_pairs(uint32_t wfmt, uint32_t n_tiles);
+uint32_t mx_job_tiles(const TcJob& job, bool pairs);
+void mx_fill_tiles(const TcJob& job, uint32_t nt, MxTile* out, bool pairs = false);
 // Peers that receive a copy of every output (the fused all-gather of a
 // column- or row-sharded layer): an output byte at address x (C or the
 // MXINT8 copy) is also stored at x + delta[i].
@@ -152,9 +159,12 @@ int launch_mxf4_gather(const TcJob& inline_job, uint32_t nt, uint32_t tiles, int
 // it is null, the tiles of the single *inline_job.  `peers` may be null.
 // weights_ready: the weight chunks were written and the stream synchronised
 // before (a plan's), so the kernel may read them before its dependency wait.
+// pairs: 1 when tiles_dev is in pair order (mx_fill_tiles with pairs; CTA
+// pairs run it), 0 when it is not, -1 (the inline job) to decide by
+// mx_pairs (the tile count then follows).
 int launch_mxf4(const MxTile* tiles_dev, const TcJob* inline_job, uint32_t nt, uint32_t wfmt,
                 uint32_t tiles, int sm_count, uint32_t* err, cudaStream_t stream,
-                const MxPeers* peers = nullptr, bool weights_ready = false);
+                const MxPeers* peers = nullptr, bool weights_ready = false, int pairs = -1);
 
 // Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current
 // device, once per (kernel, device).

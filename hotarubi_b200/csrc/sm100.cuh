@@ -253,4 +253,103 @@ __host__ __device__ constexpr uint32_t idesc_bf16(uint32_t m, uint32_t n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
+// ---------------------------------------------------------------------------
+// Thread-block clusters and CTA pairs (tcgen05 .cta_group::2): the two CTAs
+// of a cluster of two share one MMA of M = 256 (each its 128 rows of A and
+// half of B's rows from its own shared memory, each its 128 accumulator rows
+// in its own TMEM).  The even CTA (rank 0) issues the MMAs, scale copies and
+// commits; barriers the two CTAs share live in rank 0 and are reached by
+// the other through its cluster address.
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of both CTAs (all warps converged).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The cluster address of the same shared-memory variable in CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+  return r;
+}
+
+// Arrival on a barrier of CTA `rank` (release at cluster scope).
+__device__ __forceinline__ void mbar_arrive_cluster(uint64_t* bar, uint32_t rank) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];"
+               ::"r"(cluster_addr(bar, rank))
+               : "memory");
+}
+
+// mbar_wait for barriers the other CTA of the pair arrives on (acquire at
+// cluster scope); the same limit.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                                  uint32_t limit = 50000u) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(20000u)
+        : "memory");
+    if (ok != 0) return true;
+  }
+  atomicOr(err, kErrTimeout);
+  return false;
+}
+
+// mbar_wait by polling (test_wait, no suspension): for a thread whose only
+// job is to react to one barrier at a time, where a wake-up delay would sit
+// on the critical path.  Gives up after `limit` tests.
+__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                          uint32_t limit = 200000000u) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    if (ok != 0) return true;
+  }
+  atomicOr(err, kErrTimeout);
+  return false;
+}
+
+// TMEM of a CTA pair: one warp of each CTA (the same warp), the same
+// destination offset in both.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+               ::"r"(smem_addr(dst_smem)), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// Arrives on the barrier at this offset in both CTAs of the pair once the
+// pair MMAs and copies issued so far by this thread have completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(smem_addr(bar)), "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
 }  // namespace hrb::sm100
