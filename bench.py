@@ -409,6 +409,7 @@ def place_w8(wf: np.ndarray):
     x = torch.from_numpy(np.ascontiguousarray(wf)).cuda()
     q = torch.zeros((n, kb * 32), dtype=torch.int8, device="cuda")
     s = torch.zeros((n, kb), dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()  # the fills (torch's stream) before the encoder (the library's)
     lib.quantize(x, n, k, q, s)
     lib.sync()
     out = q.cpu().numpy().view(np.uint8), s.cpu().numpy()
@@ -627,6 +628,7 @@ def fast_parity(torch, lib, wl: Workload, x, w, ws, bias, c_dev, rows: int = 64,
     xd = torch.from_numpy(np.ascontiguousarray(x[sel])).cuda()
     q = torch.zeros((m, kp), dtype=torch.int8, device="cuda")
     s = torch.zeros((m, kb), dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()  # the fills (torch's stream) before the encoder (the library's)
     lib.quantize(xd, m, wl.K, q, s)
     lib.sync()
     a = q.cpu().numpy().astype(np.float64) * np.repeat(

@@ -43,6 +43,7 @@ def main(out):
         d = capi.Library.desc(0, m, n, k, a=t["x"], w=t["w"], wscale=t["ws"], bias=t["b"],
                               c=t["c"], accumulate=acc, mode=capi.MODE_FAST, cq=t["q"],
                               cscale=t["s"])
+        torch.cuda.synchronize()  # torch's fills before the library's stream
         lib.dense(d)
         lib.sync()
         np.save(os.path.join(out, f"dense{i}_c.npy"), t["c"].cpu().numpy())
@@ -54,6 +55,7 @@ def main(out):
             descs.append(d)
             keep.append(t)
     plan = lib.plan(descs)
+    torch.cuda.synchronize()
     plan.run(0)
     lib.sync()
     for j, t in enumerate(keep):

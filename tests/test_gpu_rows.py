@@ -73,6 +73,7 @@ def run(hrb, capi, wfmt, m, n, k, win, lay, w, ws, mode):
     idx_d = None if lay.get("index") is None else dev(lay["index"].view(np.int32))
     c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
     d = capi.Library.desc(wfmt, m, n, k, w=dev(w), wscale=dev(ws), c=c, mode=mode)
+    torch.cuda.synchronize()  # torch's fills come before the library's stream reads them
     d._keep = (win_d, idx_d)
     hrb.gemm_rows(d, rows_desc(capi, win_d, win.size, lay, idx_d))
     hrb.sync()

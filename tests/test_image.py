@@ -123,6 +123,8 @@ def test_gemm_image_equals_the_dense_gemm(hrb, ref_lib, mode):
             bias = (rng.standard_normal(n) * 0.01).astype(np.float32)
             xd, bd = torch.from_numpy(x).cuda(), torch.from_numpy(bias).cuda()
             want = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+            # The library's stream does not wait for torch's: its fills first.
+            torch.cuda.synchronize()
             hrb.dense(capi.Library.desc(wfmt, m, n, k, a=xd, w=torch.from_numpy(w).cuda(),
                                         wscale=torch.from_numpy(ws).cuda(), bias=bd, c=want,
                                         mode=mode))
@@ -133,6 +135,7 @@ def test_gemm_image_equals_the_dense_gemm(hrb, ref_lib, mode):
                 off, lo = capi.image_region(meta, "w8_hi")[0], capi.image_region(meta, "w8_lo")[0]
             for _ in range(2):  # the second call reuses the cached dense weights
                 got = torch.full((m, n), 3.0, dtype=torch.float32, device="cuda")
+                torch.cuda.synchronize()
                 img.gemm(capi.Library.desc(wfmt, m, n, k, a=xd, bias=bd, c=got, mode=mode),
                          off, lo)
                 hrb.sync()
@@ -144,6 +147,7 @@ def test_gemm_image_equals_the_dense_gemm(hrb, ref_lib, mode):
             # The dense weights themselves.
             wd = torch.zeros(w.shape, dtype=torch.uint8, device="cuda")
             wsd = torch.zeros(ws.shape, dtype=torch.uint8, device="cuda")
+            torch.cuda.synchronize()
             img.weights(wfmt, off, n, k, wd, wsd, offset_lo=lo)
             hrb.sync()
             assert np.array_equal(wd.cpu().numpy(), w) and np.array_equal(wsd.cpu().numpy(), ws)
