@@ -142,7 +142,7 @@ def run_gpu_columns(lib, group) -> None:
     out.close()
 
 
-def run_gpu_rows(lib, group) -> None:
+def run_gpu_rows(lib, group, wfmt: int = 0) -> None:
     from hotarubi_b200 import capi
     rank, ranks = group.rank, group.ranks
     c = CONV
@@ -152,14 +152,20 @@ def run_gpu_rows(lib, group) -> None:
     kpn = (c["cout"] + 31) // 32 * 32
     geo = (c["H"], c["W"], c["cin"], c["cout"], c["kh"], c["stride"])
     xa = torch.from_numpy(workloads.activations(5, c["images"] * hw, c["cin"])).cuda()
-    w, ws = workloads.mxfp4_weights(6, c["cout"], c["kh"] ** 2 * c["cin"])
+    kk = c["kh"] ** 2 * c["cin"]
+    if wfmt == 0:
+        w, ws = workloads.mxfp4_weights(6, c["cout"], kk)
+    else:  # W8: MXINT8 codes with their block scale bytes
+        rng = np.random.default_rng(6)
+        w = rng.integers(-127, 128, (c["cout"], kk)).astype(np.int8).view(np.uint8)
+        ws = rng.integers(116, 124, (c["cout"], kk // 32)).astype(np.uint8)
     bias = (np.random.default_rng(7).standard_normal(c["cout"]) * 0.01).astype(np.float32)
     wd, wsd, bd = (torch.from_numpy(v).cuda() for v in (w, ws, bias))
     # The unsharded convolution on this GPU.
     ref = torch.zeros((m, c["cout"]), dtype=torch.float32, device="cuda")
     ref_q = torch.zeros((m, kpn), dtype=torch.int8, device="cuda")
     ref_s = torch.zeros((m, kpn // 32), dtype=torch.uint8, device="cuda")
-    full = lib.conv_plan(capi.conv_desc(0, c["images"], *geo, order=capi.CONV_YMAJOR, a=xa,
+    full = lib.conv_plan(capi.conv_desc(wfmt, c["images"], *geo, order=capi.CONV_YMAJOR, a=xa,
                                         w=wd, wscale=wsd, bias=bd, c=ref, relu=True,
                                         mode=capi.MODE_FAST, cq=ref_q, cscale=ref_s))
     full.run()
@@ -173,7 +179,7 @@ def run_gpu_rows(lib, group) -> None:
     r0, r1 = i0 * per, i1 * per
     plan = None
     if i1 > i0:
-        plan = lib.conv_plan(capi.conv_desc(0, i1 - i0, *geo, order=capi.CONV_YMAJOR,
+        plan = lib.conv_plan(capi.conv_desc(wfmt, i1 - i0, *geo, order=capi.CONV_YMAJOR,
                                             a=xa[i0 * hw:i1 * hw], w=wd, wscale=wsd, bias=bd,
                                             c=out.tensor[r0:r1], relu=True, mode=capi.MODE_FAST,
                                             cq=out.q[r0:r1], cscale=out.s[r0:r1]))
@@ -185,7 +191,7 @@ def run_gpu_rows(lib, group) -> None:
     group.fence()
     lib.sync()
     assert torch.equal(out.tensor.view(torch.int32), ref.view(torch.int32)), \
-        f"rank {rank}: fused row gather (FP32)"
+        f"rank {rank}: fused row gather (FP32, format {wfmt})"
     assert torch.equal(out.q, ref_q) and torch.equal(out.s, ref_s), \
         f"rank {rank}: fused row gather (MXINT8 copy)"
     # The communicator's in-place all-gather of the row ranges.
@@ -221,7 +227,8 @@ def main() -> None:
         lib = capi.Library(local)
         group = shard.Group(lib)
         run_gpu_columns(lib, group)
-        run_gpu_rows(lib, group)
+        run_gpu_rows(lib, group, 0)
+        run_gpu_rows(lib, group, 1)
         group.barrier()
         group.close()
         lib.close()
