@@ -776,7 +776,7 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
     if rank == 0:
         pk = peaks()
         fast = mode == capi.MODE_FAST
-        kname = ("k_gemm_w8bf" if w8_bf16 else "k_gemm_mxf4") if fast else "k_dense_exact"
+        kname = ("k_gemm_w8bf" if w8_bf16 else "k_gemm_mxf4") if fast else exact_kernel(wl.wfmt)
         qname = "k_quantize_planes" if fast else "k_quantize"
         gemm_gbs = batch * wl.bytes_gemm() / (gemm_ms / 1e3) / 1e9
         quant_gbs = batch * wl.bytes_quant() / (quant_ms / 1e3) / 1e9
@@ -790,7 +790,13 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
                     "alg_bytes_per_launch": batch * wl.bytes_gemm()}
         else:
             tflops = batch * wl.flops / (gemm_ms / 1e3) / 1e12
-            if wl.wfmt == 2:
+            if not fast and exact_kernel(wl.wfmt) == "k_exact_tc":
+                # k_exact_tc: one kind::i8 MMA per block product (2x the dense
+                # BF16 rate), W8 two (its HI and LO nibble planes).
+                peak = pk["bf16_tflops"] * 2.0 / (1.0 if wl.wfmt == 0 else 2.0)
+                how = (" (cuBLAS BF16 x 2: the int8 MMA rate)" if wl.wfmt == 0
+                       else " (cuBLAS BF16 x 2 / 2: the int8 MMA rate over two nibble planes)")
+            elif wl.wfmt == 2:
                 # MXFP8 runs kind::mxf8f6f4 at 2x the dense BF16 rate, with two
                 # E4M3 digit planes per exact product: the BF16 peak.
                 peak, how = pk["bf16_tflops"], " (cuBLAS BF16: FP8 MMA rate over two digit planes)"
@@ -863,6 +869,13 @@ def run_ours(args, wl: Workload, rank: int, world: int, local_rank: int) -> None
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def exact_kernel(wfmt: int) -> str:
+    """The kernel of an exact-mode GEMM: k_exact_tc (int8 tensor-core block
+    dots) for MXFP4 and W8 unless HRB_EXACT_TC=0, else k_dense_exact."""
+    tc = os.environ.get("HRB_EXACT_TC", "1") != "0"
+    return "k_exact_tc" if tc and wfmt in (0, 1) else "k_dense_exact"
 
 
 def conv_operands(cw: ConvWorkload, i: int, place=None):
@@ -1051,7 +1064,7 @@ def run_conv(args, rank: int, world: int, local_rank: int) -> None:
                              " MB > 2 x 126 MB L2",
                        "parallelism": f"replicas x{world}"},
             "roofline": {"bound": "tensor", "kernel": "k_gemm_mxf4" if mode == capi.MODE_FAST
-                         else "k_dense_exact", "achieved": tflops, "peak": pk["bf16_tflops"],
+                         else exact_kernel(cw.wfmt), "achieved": tflops, "peak": pk["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": tflops / pk["bf16_tflops"],
                          "peak_source": pk["source"] + " (cuBLAS BF16 dense)",
                          **tensor_fracs(tflops, pk, cw.wfmt),
@@ -1280,7 +1293,7 @@ def run_prefix(args, rank: int, world: int, local_rank: int) -> None:
                        "parallelism": f"replicas x{world}",
                        "launch": f"{pw.layers * 4} dependent plan runs in a CUDA graph"},
             "roofline": {"bound": "hbm", "kernel": "k_gemm_mxf4 (gate + up, one launch)"
-                         if mode == capi.MODE_FAST else "k_dense_exact",
+                         if mode == capi.MODE_FAST else exact_kernel(0),
                          "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"], "peak_source": pk["source"] +
                          " (HBM copy)", "alg_bytes_per_launch": mlp_bytes, "traffic": None,

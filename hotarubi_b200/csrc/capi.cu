@@ -11,6 +11,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -38,6 +39,9 @@ struct hrb_ctx {
   // Operand staging for hrb_gemm_dense_host.
   void* staging = nullptr;
   size_t staging_bytes = 0;
+  // The int8 weight chunks of the tensor-core exact GEMM (launch_x_translate).
+  void* xscratch = nullptr;
+  size_t xscratch_bytes = 0;
   // Bit 0: the encoder met Inf/NaN; bit 1: a tensor-core kernel gave up
   // waiting (it then leaves its outputs unwritten).
   uint32_t* d_error = nullptr;
@@ -70,9 +74,9 @@ struct hrb_plan {
   const hrb::QuantJob* d_post = nullptr;
   struct Group {
     uint32_t wfmt;
-    uint32_t kind;  // 0 exact kernel, 2 block-scaled tensor-core kernel
+    uint32_t kind;  // 0 exact kernel, 1 exact tensor-core kernel, 2 block-scaled tensor-core kernel
     uint32_t nt, njobs, tiles;
-    const void* d_jobs;  // DenseJob (exact) or TcJob (tensor-core) array
+    const void* d_jobs;  // DenseJob (kind 0), XJob (kind 1) or TcJob (kind 2) array
     const hrb::MxTile* d_tiles;  // kind 2: the launch's output tiles
     bool pairs = false;          // kind 2: d_tiles in pair order (CTA pairs)
   };
@@ -279,7 +283,47 @@ hrb::QuantJob post_quant_job(const hrb_gemm_desc* d) {
 }
 
 // The exact GEMM, once activations are MXINT8 on the device.
+// MXFP4 and W8 run their block dots on the tensor cores (k_exact_tc) unless
+// HRB_EXACT_TC=0; MXFP8 and that switch take k_dense_exact.  Both give the
+// same bits.
+bool exact_tc(uint32_t wfmt) {
+  static const bool on = [] {
+    const char* e = std::getenv("HRB_EXACT_TC");
+    return e == nullptr || std::strcmp(e, "0") != 0;
+  }();
+  return on && hrb::x_supported(wfmt);
+}
+
+// The tensor-core job of a dense exact job whose weights were translated
+// into xw.
+hrb::XJob x_job(const hrb::DenseJob& job, const uint8_t* xw, uint32_t tile_begin) {
+  hrb::XJob x{};
+  x.d = job;
+  x.wt = xw;
+  x.wsc = xw + hrb::x_code_bytes(job.wfmt, job.N, job.kb);
+  x.planes = job.wfmt == 1 ? 2u : 1u;
+  x.steps = (job.kb + 3u) / 4u;
+  x.m_tiles = (job.M + 63u) / 64u;
+  x.n_tiles = (job.N + 127u) / 128u;
+  x.tile_begin = tile_begin;
+  return x;
+}
+
 hrb_status run_dense(hrb_ctx* ctx, const hrb::DenseJob& job, cudaStream_t s) {
+  if (exact_tc(job.wfmt)) {
+    hrb_status st = grow(ctx, &ctx->xscratch, &ctx->xscratch_bytes,
+                         hrb::x_weight_bytes(job.wfmt, job.N, job.kb));
+    if (st != HRB_OK) return st;
+    uint8_t* xw = static_cast<uint8_t*>(ctx->xscratch);
+    hrb::launch_x_translate(job.wfmt, job.w, job.wscale, job.N, job.kb, xw, s);
+    const hrb::XJob x = x_job(job, xw, 0);
+    const int n = hrb::launch_x_exact(nullptr, 1, &x, hrb::x_tiles(job.M, job.N), ctx->sm_count,
+                                      ctx->d_error, s);
+    if (n < 0) return fail(ctx, HRB_ECUDA, "k_exact_tc launch failed");
+    ctx->launches += 1u + static_cast<uint64_t>(n);
+    HRB_CUDA(ctx, cudaGetLastError());
+    return HRB_OK;
+  }
   hrb::DenseJob one = job;
   uint32_t tiles_n = 0;
   const uint32_t tiles = hrb::dense_exact_tiles(job.M, job.N, tiles_n);
@@ -787,6 +831,7 @@ hrb_status hrb_destroy(hrb_ctx* ctx) {
   cudaFree(ctx->d_fbuf);
   cudaFree(ctx->scratch);
   cudaFree(ctx->staging);
+  cudaFree(ctx->xscratch);
   cudaFree(ctx->d_error);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -1294,8 +1339,12 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
     if (st != HRB_OK) return st;
     if (use_tc(&descs[i])) {
       scratch += tc_scratch_bytes(&descs[i]);
-    } else if (descs[i].a != nullptr) {
-      scratch += align_up(act_scratch_bytes(descs[i].M, descs[i].K), 1024);
+    } else {
+      if (descs[i].a != nullptr) scratch += align_up(act_scratch_bytes(descs[i].M, descs[i].K), 1024);
+      if (exact_tc(descs[i].wfmt)) {
+        scratch += align_up(hrb::x_weight_bytes(descs[i].wfmt, descs[i].N, blocks_of(descs[i].K)),
+                            1024);
+      }
     }
   }
   HRB_CUDA(ctx, cudaSetDevice(ctx->device));
@@ -1333,6 +1382,9 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
   std::vector<hrb::QuantJob> quant, planes, post;
   std::vector<std::vector<hrb::DenseJob>> exact(3);
   uint32_t exact_tiles[3] = {0, 0, 0};
+  // Exact GEMMs on the tensor cores (exact_tc), per format, weights translated now.
+  std::vector<std::vector<hrb::XJob>> xexact(2);
+  uint32_t xexact_tiles[2] = {0, 0};
   struct TcKey { uint32_t nt, wfmt, kind; bool pairs; };
   std::vector<TcKey> tc_keys;
   std::vector<std::vector<hrb::TcJob>> tc_groups;
@@ -1393,6 +1445,16 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
       post.push_back(pq);
     }
     hrb::DenseJob j = make_dense_job(&d, aq, as, pieces[i].data(), npieces[i]);
+    if (exact_tc(j.wfmt)) {
+      uint8_t* xw = sbase + soff;
+      soff += align_up(hrb::x_weight_bytes(j.wfmt, j.N, j.kb), 1024);
+      hrb::launch_x_translate(j.wfmt, j.w, j.wscale, j.N, j.kb, xw, ctx->stream);
+      xexact[j.wfmt].push_back(x_job(j, xw, xexact_tiles[j.wfmt]));
+      xexact_tiles[j.wfmt] += hrb::x_tiles(j.M, j.N);
+      plan->io[i].tile_begin = xexact[j.wfmt].back().tile_begin;
+      plan->io[i].tiles = hrb::x_tiles(j.M, j.N);
+      continue;
+    }
     uint32_t tiles_n = 0;
     const uint32_t tiles = hrb::dense_exact_tiles(j.M, j.N, tiles_n);
     j.tiles_n = tiles_n;
@@ -1402,6 +1464,7 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
   }
   size_t bytes = (quant.size() + planes.size() + post.size()) * sizeof(hrb::QuantJob);
   for (auto& g : exact) bytes += g.size() * sizeof(hrb::DenseJob);
+  for (auto& g : xexact) bytes += g.size() * sizeof(hrb::XJob);
   for (auto& g : tc_groups) bytes += g.size() * sizeof(hrb::TcJob);
   // kind::mxf4 groups also get their output tiles located on the host.
   std::vector<std::vector<hrb::MxTile>> mx_tiles(tc_groups.size());
@@ -1451,6 +1514,14 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
     plan->groups.push_back({f, 0u, 0, static_cast<uint32_t>(g.size()), exact_tiles[f], dst,
                             nullptr});
     dst += g.size() * sizeof(hrb::DenseJob);
+  }
+  for (uint32_t f = 0; f < 2; ++f) {
+    auto& g = xexact[f];
+    if (g.empty()) continue;
+    HRB_CUDA(ctx, cudaMemcpy(dst, g.data(), g.size() * sizeof(hrb::XJob), cudaMemcpyHostToDevice));
+    plan->groups.push_back({f, 1u, 0, static_cast<uint32_t>(g.size()), xexact_tiles[f], dst,
+                            nullptr});
+    dst += g.size() * sizeof(hrb::XJob);
   }
   for (size_t g = 0; g < tc_groups.size(); ++g) {
     HRB_CUDA(ctx, cudaMemcpy(dst, tc_groups[g].data(), tc_groups[g].size() * sizeof(hrb::TcJob),
@@ -1509,6 +1580,11 @@ hrb_status plan_launch(hrb_plan* plan, cudaStream_t s, int64_t only, uint32_t* l
     if (g.kind == 0) {
       n += static_cast<uint32_t>(hrb::launch_dense_exact(
           static_cast<const hrb::DenseJob*>(g.d_jobs), g.njobs, nullptr, g.tiles, g.wfmt, s));
+    } else if (g.kind == 1) {
+      const int k = hrb::launch_x_exact(static_cast<const hrb::XJob*>(g.d_jobs), g.njobs, nullptr,
+                                        g.tiles, ctx->sm_count, ctx->d_error, s);
+      if (k < 0) return fail(ctx, HRB_ECUDA, "k_exact_tc launch failed");
+      n += static_cast<uint32_t>(k);
     } else {
       const int k = hrb::launch_mxf4(g.d_tiles, nullptr, g.nt, g.wfmt, g.tiles, ctx->sm_count,
                                      ctx->d_error, s, &plan->peers, true, g.pairs ? 1 : 0);
