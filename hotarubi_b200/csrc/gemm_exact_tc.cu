@@ -20,7 +20,7 @@
 //   * the MMA thread issues one MMA per block, in chain order, into one of
 //     two groups of four TMEM accumulators (64 columns each; a chain segment
 //     is at most the four blocks of a step, and takes a group), with one
-//     commit per segment; the 16 epilogue warps (warp w: TMEM lane quarter
+//     commit per segment; the epilogue warps (warp w: TMEM lane quarter
 //     w % 4, tokens 16 (w / 4) .. + 15) hold the 16 chains of their weight
 //     row in registers and hand the group back once per segment;
 //   * every accumulator starts at 1.5 2^23 (as int32 0x4B400000, written by
@@ -74,11 +74,14 @@ constexpr uint32_t kXSlots = 7;
 constexpr uint32_t kXGroups = 2;                  // TMEM accumulator groups, one per segment
 constexpr uint32_t kXGroupCols = 4u * kXTok;      // a group: one 64-column accumulator per block
 constexpr uint32_t kXMagic = 0x4B400000u;         // FP32 1.5 2^23, the accumulators' start
-constexpr uint32_t kXEpiWarps = 16;
+constexpr uint32_t kXEpiTok = 16;                 // tokens per epilogue thread (x_tmem_ld)
+constexpr uint32_t kXEpiWarps = 4u * kXTok / kXEpiTok;
 constexpr uint32_t kXFirstEpi = 3;                // warps 0 producer, 1 MMA, 2 activation stager
 constexpr uint32_t kXThreads = 32u * (kXFirstEpi + kXEpiWarps);
 constexpr uint32_t kXOffBar = kXSlots * kXSlot;
-constexpr uint32_t kXSmem = kXOffBar + 1024 + 1024;
+constexpr uint32_t kXJobCache = 2048;             // jobs whose first tiles are kept in smem
+constexpr uint32_t kXOffJobs = kXOffBar + 1024;
+constexpr uint32_t kXSmem = kXOffJobs + kXJobCache * 4u + 1024;
 static_assert(kXSmem <= 232448, "shared memory");
 
 static_assert(kXGroups * kXGroupCols == 512, "TMEM columns");
@@ -239,24 +242,45 @@ __device__ __forceinline__ void x_next(const XChain& c, XWalk& w) {
   x_segment(w);
 }
 
-// The job of tile u: the last whose tile_begin is at most u.
-__device__ __forceinline__ uint32_t x_find(const XJob* jobs, uint32_t njobs, uint32_t u) {
+// The job of tile u: the last whose tile_begin is at most u, searched in
+// the shared-memory copy of the first tiles when the launch has at most
+// kXJobCache jobs.
+__device__ __forceinline__ uint32_t x_find(const XJob* jobs, const uint32_t* begins,
+                                           uint32_t njobs, uint32_t u) {
   uint32_t lo = 0, hi = njobs - 1;
   while (lo < hi) {
     const uint32_t mid = (lo + hi + 1) >> 1;
-    if (jobs[mid].tile_begin <= u) lo = mid; else hi = mid - 1;
+    const uint32_t tb = begins != nullptr ? begins[mid] : jobs[mid].tile_begin;
+    if (tb <= u) lo = mid; else hi = mid - 1;
   }
   return lo;
 }
 
 
+// The scale bytes of segment w's blocks for tokens m0 + lane and + 32: 127
+// for tokens past M, blocks outside the segment, and a finished walk.
+__device__ __forceinline__ void x_load_ea(const uint8_t* ascale, uint32_t M, uint32_t kb,
+                                          uint32_t m0, const XWalk& w, uint32_t lane,
+                                          int32_t (&ea)[2][4]) {
+#pragma unroll
+  for (uint32_t h = 0; h < 2; ++h) {
+    const uint32_t m = m0 + lane + 32u * h;
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      const uint32_t b = 4u * w.step + j;
+      ea[h][j] = !w.done && m < M && b >= w.b0 && b < w.b1
+                     ? static_cast<int32_t>(ascale[size_t{m} * kb + b]) : 127;
+    }
+  }
+}
+
 // Shared-memory layout and the tile's job: weights chunk then activation
 // codes per ring slot; barriers; the activation-scale table.
 struct XSmem {
   uint64_t* full;       // [kXSlots] weights (tx bytes), 32 stager cp.async lanes, its table
-  uint64_t* empty;      // [kXSlots] the segment's MMAs done and the 16 epilogue warps past it
+  uint64_t* empty;      // [kXSlots] the segment's MMAs done and the epilogue warps past it
   uint64_t* acc_full;   // [kXGroups] a segment's dots are in TMEM
-  uint64_t* acc_empty;  // [kXGroups] the 16 epilogue warps have read them
+  uint64_t* acc_empty;  // [kXGroups] the epilogue warps have read them
   uint32_t* tmem_slot;
 };
 
@@ -275,10 +299,10 @@ struct XTile {
   uint32_t jx, m0, n0, nt;  // job, first token, first weight row, weight tile
 };
 
-__device__ __forceinline__ XTile x_tile(const XJob* jobs, uint32_t njobs, const XJob& inline_job,
-                                        uint32_t u, const XJob*& job) {
+__device__ __forceinline__ XTile x_tile(const XJob* jobs, const uint32_t* begins, uint32_t njobs,
+                                        const XJob& inline_job, uint32_t u, const XJob*& job) {
   XTile t;
-  t.jx = jobs != nullptr ? x_find(jobs, njobs, u) : 0u;
+  t.jx = jobs != nullptr ? x_find(jobs, begins, njobs, u) : 0u;
   job = jobs != nullptr ? &jobs[t.jx] : &inline_job;
   const uint32_t local = u - job->tile_begin;
   t.nt = local % job->n_tiles;
@@ -288,10 +312,82 @@ __device__ __forceinline__ XTile x_tile(const XJob* jobs, uint32_t njobs, const 
 }
 
 
+// The epilogue thread's kXEpiTok columns of one accumulator (16; 32
+// tokens a thread were measured slower: fewer warps, and spills).
+__device__ __forceinline__ void x_tmem_ld(uint32_t taddr, uint32_t (&r)[16]) { tmem_ld16(taddr, r); }
+// kXEpiTok columns of one accumulator set to v (one register for all).
+__device__ __forceinline__ void x_tmem_fill(uint32_t taddr, uint32_t v) {
+  if (kXEpiTok == 32) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+        "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr), "r"(v)
+        : "memory");
+  } else {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr), "r"(v)
+        : "memory");
+  }
+}
+
 __device__ __forceinline__ float fma_rn_ftz(float a, float b, float c) {
   float r;
   asm("fma.rn.ftz.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
   return r;
+}
+
+// acc plus one token's block value by the integer rule.  Not inlined: the
+// rare path then costs the hot loop no registers.  ea_at: the token's scale
+// byte (null past M).
+__device__ __noinline__ float x_slow(float acc, uint32_t dot_bits, const uint8_t* ea_at,
+                                     int32_t ew) {
+  const int32_t ea = ea_at != nullptr ? static_cast<int32_t>(*ea_at) : 127;
+  const float f = __int2float_rn(static_cast<int32_t>(dot_bits - kXMagic));
+  return add_rn_ftz(acc, __uint_as_float(scale_pow2_bits(f, ea + ew - 254)));
+}
+
+// Block b of the chain for the thread's kXEpiTok tokens (weight row r of
+// the tile), from its accumulator bits 1.5 2^23 + dot and the slot's table.
+// arow: the scale bytes of the thread's first token; mrem: tokens left from
+// it (for the integer rule).
+__device__ __forceinline__ void x_block(float (&acc)[kXEpiTok], const uint32_t (&dot)[kXEpiTok],
+                                        const uint8_t* sp, uint32_t b, uint32_t r, uint32_t tok0,
+                                        int32_t sb, const uint8_t* arow, uint32_t mrem,
+                                        uint32_t kb) {
+  const uint32_t j4 = b & 3u;
+  const int32_t ew = static_cast<int32_t>(sp[kXSlotWs + j4 * kXTileW + r]) + sb;
+  const int2 rg = reinterpret_cast<const int2*>(sp + kXSlotRg)[j4];
+  if (ew >= rg.x && ew <= rg.y) {
+    // The first FMA removes 1.5 2^23 from the exact product: dot
+    // 2^(ea - 127).  The second's product is exact and normal, so it rounds
+    // as the chain's add of the block value.
+    const float tw = __uint_as_float(static_cast<uint32_t>(ew) << 23);
+    const float4* ta = reinterpret_cast<const float4*>(sp + kXSlotTa) + (j4 * kXTok + tok0) / 4u;
+    const float4* nc = reinterpret_cast<const float4*>(sp + kXSlotNc) + (j4 * kXTok + tok0) / 4u;
+    // 16 tokens at a time: the empty asm keeps the compiler from loading
+    // every table value at once (register pressure).
+#pragma unroll
+    for (uint32_t h = 0; h < kXEpiTok / 16u; ++h) {
+#pragma unroll
+      for (uint32_t v = 4u * h; v < 4u * h + 4u; ++v) {
+        const float4 t4 = ta[v], n4 = nc[v];
+        const float tv[4] = {t4.x, t4.y, t4.z, t4.w}, nv[4] = {n4.x, n4.y, n4.z, n4.w};
+#pragma unroll
+        for (uint32_t e = 0; e < 4; ++e) {
+          const uint32_t j = 4u * v + e;
+          acc[j] = fma_rn_ftz(fma_rn_ftz(__uint_as_float(dot[j]), tv[e], nv[e]), tw, acc[j]);
+        }
+      }
+      asm volatile("" ::: "memory");
+    }
+  } else {
+    // The integer rule (BlockValue with its flush and overflow).
+#pragma unroll
+    for (uint32_t j = 0; j < kXEpiTok; ++j) {
+      acc[j] = x_slow(acc[j], dot[j], j < mrem ? arow + size_t{j} * kb + b : nullptr, ew);
+    }
+  }
 }
 
 
@@ -303,6 +399,13 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
                                              ~uintptr_t(1023));
   const XSmem x = x_smem(smem);
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  // The jobs' first tiles (written when the plan was made, not by the
+  // kernel before this one), for the per-tile job search.
+  uint32_t* begins = nullptr;
+  if (jobs != nullptr && njobs <= kXJobCache) {
+    begins = reinterpret_cast<uint32_t*>(smem + kXOffJobs);
+    for (uint32_t i = threadIdx.x; i < njobs; i += blockDim.x) begins[i] = jobs[i].tile_begin;
+  }
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < kXSlots; ++s) {
       mbar_init(&x.full[s], 1u + 32u + 1u);  // weights, the stager's copies, its table
@@ -332,7 +435,7 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
       uint32_t n = 0;
       for (uint32_t u = blockIdx.x; u < total_tiles && ok; u += gridDim.x) {
         const XJob* job;
-        const XTile t = x_tile(jobs, njobs, inline_job, u, job);
+        const XTile t = x_tile(jobs, begins, njobs, inline_job, u, job);
         const XChain c = x_chain(*job);
         const uint8_t* wt = job->wt;
         const uint8_t* wsc = job->wsc;
@@ -358,14 +461,19 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
     uint32_t n = 0;
     for (uint32_t u = blockIdx.x; u < total_tiles && ok; u += gridDim.x) {
       const XJob* job;
-      const XTile t = x_tile(jobs, njobs, inline_job, u, job);
+      const XTile t = x_tile(jobs, begins, njobs, inline_job, u, job);
       const XChain c = x_chain(*job);
       const int8_t* aq = job->d.aq;
       const uint8_t* ascale = job->d.ascale;
       const uint32_t M = job->d.M;
       const size_t kp = size_t{c.kb} * 32u;
+      // Each segment's scale bytes are loaded one segment ahead, so that
+      // their latency overlaps the segment before.
       XWalk w;
-      for (x_begin(c, w); !w.done && ok; x_next(c, w), ++n) {
+      x_begin(c, w);
+      int32_t ea[2][4];
+      x_load_ea(ascale, M, c.kb, t.m0, w, lane, ea);
+      for (; !w.done && ok; ++n) {
         const uint32_t sl = n % kXSlots;
         if (n >= kXSlots) ok = mbar_wait(&x.empty[sl], ((n / kXSlots) - 1u) & 1u, err);
         ok = __all_sync(0xFFFFFFFFu, ok);
@@ -381,17 +489,10 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
           cp_async16(dst0 + r * kXRowB + ((cc ^ (r & 7u)) << 4), src, have ? 16u : 0u);
         }
         cp_async_arrive(&x.full[sl]);
-        int32_t ea[2][4];
-#pragma unroll
-        for (uint32_t h = 0; h < 2; ++h) {
-          const uint32_t m = t.m0 + lane + 32u * h;
-#pragma unroll
-          for (uint32_t j = 0; j < 4; ++j) {
-            const uint32_t b = 4u * w.step + j;
-            ea[h][j] = m < M && b >= w.b0 && b < w.b1
-                           ? static_cast<int32_t>(ascale[size_t{m} * c.kb + b]) : 127;
-          }
-        }
+        XWalk nx = w;
+        x_next(c, nx);
+        int32_t ea_nx[2][4];
+        x_load_ea(ascale, M, c.kb, t.m0, nx, lane, ea_nx);
         uint8_t* sp = smem + sl * kXSlot;
 #pragma unroll
         for (uint32_t j = 0; j < 4; ++j) {
@@ -415,6 +516,12 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&x.full[sl]);
+        w = nx;
+#pragma unroll
+        for (uint32_t h = 0; h < 2; ++h) {
+#pragma unroll
+          for (uint32_t j = 0; j < 4; ++j) ea[h][j] = ea_nx[h][j];
+        }
       }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
@@ -426,7 +533,7 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
       constexpr uint32_t kIdesc = idesc_i8(kXTileW, kXTok);
       for (uint32_t u = blockIdx.x; u < total_tiles && ok; u += gridDim.x) {
         const XJob* job;
-        x_tile(jobs, njobs, inline_job, u, job);
+        x_tile(jobs, begins, njobs, inline_job, u, job);
         const XChain c = x_chain(*job);
         XWalk w;
         for (x_begin(c, w); !w.done && ok; x_next(c, w), ++n) {
@@ -451,16 +558,14 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
     }
   } else {
     // Epilogue warps: TMEM lane quarter qd = warp % 4 (weight row n0 + 32 qd
-    // + lane), tokens m0 + 16 g .. + 15.
+    // + lane), tokens m0 + kXEpiTok g .. + kXEpiTok - 1.
     const uint32_t qd = warp & 3u, g = (warp - kXFirstEpi) / 4u;
     const uint32_t r = 32u * qd + lane;                  // the thread's weight row in the tile
-    const uint32_t tbase = tmem + ((32u * qd) << 16) + 16u * g;
-    uint32_t magic[16];
-#pragma unroll
-    for (uint32_t j = 0; j < 16; ++j) magic[j] = kXMagic;
+    const uint32_t tbase = tmem + ((32u * qd) << 16) + kXEpiTok * g;
+    const uint32_t tok0 = kXEpiTok * g;                  // the thread's first token in the tile
     // Every accumulator starts at 1.5 2^23; the first arrival on each group's
     // acc_empty hands the group to the MMA thread.
-    for (uint32_t a = 0; a < kXGroups * 4u; ++a) tmem_st16(tbase + a * kXTok, magic);
+    for (uint32_t a = 0; a < kXGroups * 4u; ++a) x_tmem_fill(tbase + a * kXTok, kXMagic);
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
@@ -470,21 +575,21 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
     uint32_t n = 0;
     for (uint32_t u = blockIdx.x; u < total_tiles; u += gridDim.x) {
       const XJob* job;
-      const XTile t = x_tile(jobs, njobs, inline_job, u, job);
+      const XTile t = x_tile(jobs, begins, njobs, inline_job, u, job);
       const XChain c = x_chain(*job);
       const DenseJob& d = job->d;
       const uint32_t M = d.M, N = d.N, kb = c.kb;
       const uint8_t* ascale = d.ascale;
       const uint32_t col = t.n0 + r;
       const bool n_ok = col < N;
-      float acc[16];
+      float acc[kXEpiTok];
       {
         const bool accumulate = d.accumulate != 0u;
         const float* cin = d.c;
         const uint32_t ldc = d.ldc;
 #pragma unroll
-        for (uint32_t j = 0; j < 16; ++j) {
-          const uint32_t m = t.m0 + 16u * g + j;
+        for (uint32_t j = 0; j < kXEpiTok; ++j) {
+          const uint32_t m = t.m0 + tok0 + j;
           acc[j] = accumulate && n_ok && m < M ? cin[size_t{m} * ldc + col] : 0.0f;
         }
       }
@@ -500,50 +605,23 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
         got = got && mbar_wait(&x.acc_full[gi], (n / kXGroups) & 1u, err);
         got = __all_sync(0xFFFFFFFFu, got);
         tc_fence_after();
+        // The segment's blocks: each accumulator read, reset to 1.5 2^23, and
+        // its block added to the chains.
+        const uint32_t gcol = tbase + gi * kXGroupCols;
+        const uint8_t* arow = ascale + size_t{t.m0 + tok0} * kb;
+        const uint32_t mrem = M - min(M, t.m0 + tok0);
         for (uint32_t b = w.b0; b < w.b1; ++b) {
-          // The block's 1.5 2^23 + dot, read and reset to 1.5 2^23.
-          const uint32_t ta_col = tbase + gi * kXGroupCols + (b & 3u) * kXTok;
-          uint32_t dot[16];
+          const uint32_t tcol = gcol + (b & 3u) * kXTok;
+          uint32_t dot[kXEpiTok];
           if (got) {
-            tmem_ld16(ta_col, dot);
+            x_tmem_ld(tcol, dot);
             tmem_wait_ld();
-            tmem_st16(ta_col, magic);
+            x_tmem_fill(tcol, kXMagic);
           } else {
 #pragma unroll
-            for (uint32_t j = 0; j < 16; ++j) dot[j] = kXMagic;
+            for (uint32_t i = 0; i < kXEpiTok; ++i) dot[i] = kXMagic;
           }
-          const uint32_t j4 = b & 3u;
-          const int32_t ew = static_cast<int32_t>(sp[kXSlotWs + j4 * kXTileW + r]) + sb;
-          const int2 rg = reinterpret_cast<const int2*>(sp + kXSlotRg)[j4];
-          if (ew >= rg.x && ew <= rg.y) {
-            // The first FMA removes 1.5 2^23 from the exact product: dot
-            // 2^(ea - 127).  The second's product is exact and normal, so it
-            // rounds as the chain's add of the block value.
-            const float tw = __uint_as_float(static_cast<uint32_t>(ew) << 23);
-            const float4* ta =
-                reinterpret_cast<const float4*>(sp + kXSlotTa) + (j4 * kXTok + 16u * g) / 4u;
-            const float4* nc =
-                reinterpret_cast<const float4*>(sp + kXSlotNc) + (j4 * kXTok + 16u * g) / 4u;
-#pragma unroll
-            for (uint32_t v = 0; v < 4; ++v) {
-              const float4 t4 = ta[v], n4 = nc[v];
-              const float tv[4] = {t4.x, t4.y, t4.z, t4.w}, nv[4] = {n4.x, n4.y, n4.z, n4.w};
-#pragma unroll
-              for (uint32_t e = 0; e < 4; ++e) {
-                const uint32_t j = 4u * v + e;
-                acc[j] = fma_rn_ftz(fma_rn_ftz(__uint_as_float(dot[j]), tv[e], nv[e]), tw, acc[j]);
-              }
-            }
-          } else {
-            // The integer rule (BlockValue with its flush and overflow).
-#pragma unroll
-            for (uint32_t j = 0; j < 16; ++j) {
-              const uint32_t m = t.m0 + 16u * g + j;
-              const int32_t ea = m < M ? static_cast<int32_t>(ascale[size_t{m} * kb + b]) : 127;
-              const float f = __int2float_rn(static_cast<int32_t>(dot[j] - kXMagic));
-              acc[j] = add_rn_ftz(acc[j], __uint_as_float(scale_pow2_bits(f, ea + ew - 254)));
-            }
-          }
+          x_block(acc, dot, sp, b, r, tok0, sb, arow, mrem, kb);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -563,8 +641,8 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
         float* cout = d.c;
         const uint32_t ldc = d.ldc;
 #pragma unroll
-        for (uint32_t j = 0; j < 16; ++j) {
-          const uint32_t m = t.m0 + 16u * g + j;
+        for (uint32_t j = 0; j < kXEpiTok; ++j) {
+          const uint32_t m = t.m0 + tok0 + j;
           if (m >= M) continue;
           float v = acc[j];
           const bool special = is_special(__float_as_uint(v));
