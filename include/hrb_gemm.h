@@ -56,7 +56,10 @@ typedef struct hrb_ctx hrb_ctx;
  * ------------------------------------------------------------------- */
 
 /* Creates a context on CUDA device `device` with its own non-blocking
- * stream.  Device buffers the context needs are owned by it. */
+ * stream.  Device buffers the context needs are owned by it, and the calls
+ * of one context share them: issue a context's calls from one host thread
+ * and on one stream (or order the streams), and use one context per
+ * concurrent stream otherwise.  Plans own their own buffers. */
 HRB_API hrb_status hrb_create(int device, hrb_ctx** out);
 HRB_API hrb_status hrb_destroy(hrb_ctx* ctx);
 /* Waits for all work on the context's stream; returns HRB_EDATA when an
