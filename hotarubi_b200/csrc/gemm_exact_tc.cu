@@ -23,10 +23,10 @@
 //     commit per segment; the epilogue warps (warp w: TMEM lane quarter
 //     w % 4, tokens 16 (w / 4) .. + 15) hold the 16 chains of their weight
 //     row in registers and hand the group back once per segment;
-//   * every accumulator starts at 1.5 2^23 (as int32 0x4B400000, written by
-//     the epilogue after each read) and the MMA adds the dot to it, so it
-//     holds the FP32 bits of 1.5 2^23 + dot (|dot| < 2^16): the conversion
-//     costs no instruction;
+//   * the int32 dot plus 0x4B400000 is the FP32 bits of 1.5 2^23 + dot
+//     (|dot| < 2^16): one integer add converts it (measured a little faster
+//     than accumulating the MMA onto that constant and writing it back to
+//     TMEM after each read);
 //   * block value: fma(1.5 2^23 + dot, 2^(ea - 127), -1.5 2^23 2^(ea - 127))
 //     is dot 2^(ea - 127) exactly, and the chain's add of the block value is
 //     fma(that, 2^(ew - 127 + SBIAS), acc): its product is exact, so the FMA
@@ -73,7 +73,7 @@ constexpr uint32_t kXSlot = (kXSlotRg + 4u * 8u + 1023u) / 1024u * 1024u;  // 27
 constexpr uint32_t kXSlots = 7;
 constexpr uint32_t kXGroups = 2;                  // TMEM accumulator groups, one per segment
 constexpr uint32_t kXGroupCols = 4u * kXTok;      // a group: one 64-column accumulator per block
-constexpr uint32_t kXMagic = 0x4B400000u;         // FP32 1.5 2^23, the accumulators' start
+constexpr uint32_t kXMagic = 0x4B400000u;         // FP32 1.5 2^23: 1.5 2^23 + dot as int32 bits
 constexpr uint32_t kXEpiTok = 16;                 // tokens per epilogue thread (x_tmem_ld)
 constexpr uint32_t kXEpiWarps = 4u * kXTok / kXEpiTok;
 constexpr uint32_t kXFirstEpi = 3;                // warps 0 producer, 1 MMA, 2 activation stager
@@ -93,13 +93,12 @@ __host__ __device__ constexpr uint32_t idesc_i8(uint32_t m, uint32_t n) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
-// D += A B: every accumulator starts at kXMagic (written by the epilogue), so
-// D ends as the FP32 bits of 1.5 2^23 + dot.
+// D = A B (no accumulation across blocks).
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                        uint32_t idesc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, 1, 0;\n\t"
+      "setp.ne.b32 p, 0, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc)
       : "memory");
@@ -315,22 +314,6 @@ __device__ __forceinline__ XTile x_tile(const XJob* jobs, const uint32_t* begins
 // The epilogue thread's kXEpiTok columns of one accumulator (16; 32
 // tokens a thread were measured slower: fewer warps, and spills).
 __device__ __forceinline__ void x_tmem_ld(uint32_t taddr, uint32_t (&r)[16]) { tmem_ld16(taddr, r); }
-// kXEpiTok columns of one accumulator set to v (one register for all).
-__device__ __forceinline__ void x_tmem_fill(uint32_t taddr, uint32_t v) {
-  if (kXEpiTok == 32) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-        "{%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-        "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr), "r"(v)
-        : "memory");
-  } else {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-        "{%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr), "r"(v)
-        : "memory");
-  }
-}
-
 __device__ __forceinline__ float fma_rn_ftz(float a, float b, float c) {
   float r;
   asm("fma.rn.ftz.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -348,7 +331,7 @@ __device__ __noinline__ float x_slow(float acc, uint32_t dot_bits, const uint8_t
 }
 
 // Block b of the chain for the thread's kXEpiTok tokens (weight row r of
-// the tile), from its accumulator bits 1.5 2^23 + dot and the slot's table.
+// the tile), from the bits of 1.5 2^23 + dot and the slot's table.
 // arow: the scale bytes of the thread's first token; mrem: tokens left from
 // it (for the integer rule).
 __device__ __forceinline__ void x_block(float (&acc)[kXEpiTok], const uint32_t (&dot)[kXEpiTok],
@@ -563,12 +546,8 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
     const uint32_t r = 32u * qd + lane;                  // the thread's weight row in the tile
     const uint32_t tbase = tmem + ((32u * qd) << 16) + kXEpiTok * g;
     const uint32_t tok0 = kXEpiTok * g;                  // the thread's first token in the tile
-    // Every accumulator starts at 1.5 2^23; the first arrival on each group's
-    // acc_empty hands the group to the MMA thread.
-    for (uint32_t a = 0; a < kXGroups * 4u; ++a) x_tmem_fill(tbase + a * kXTok, kXMagic);
-    tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
+    // The first arrival on each group's acc_empty hands the group to the MMA
+    // thread.
     if (lane == 0) {
       for (uint32_t a = 0; a < kXGroups; ++a) mbar_arrive(&x.acc_empty[a]);
     }
@@ -605,8 +584,8 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
         got = got && mbar_wait(&x.acc_full[gi], (n / kXGroups) & 1u, err);
         got = __all_sync(0xFFFFFFFFu, got);
         tc_fence_after();
-        // The segment's blocks: each accumulator read, reset to 1.5 2^23, and
-        // its block added to the chains.
+        // The segment's blocks: each dot read, 1.5 2^23 added to it as int32
+        // (its FP32 bits), and its block added to the chains.
         const uint32_t gcol = tbase + gi * kXGroupCols;
         const uint8_t* arow = ascale + size_t{t.m0 + tok0} * kb;
         const uint32_t mrem = M - min(M, t.m0 + tok0);
@@ -616,14 +595,14 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
           if (got) {
             x_tmem_ld(tcol, dot);
             tmem_wait_ld();
-            x_tmem_fill(tcol, kXMagic);
+#pragma unroll
+            for (uint32_t i = 0; i < kXEpiTok; ++i) dot[i] += kXMagic;
           } else {
 #pragma unroll
             for (uint32_t i = 0; i < kXEpiTok; ++i) dot[i] = kXMagic;
           }
           x_block(acc, dot, sp, b, r, tok0, sb, arow, mrem, kb);
         }
-        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
