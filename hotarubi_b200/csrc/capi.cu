@@ -453,6 +453,8 @@ struct ConvRun {
   size_t o_aq = 0, o_as = 0;     // exact path: the gathered MXINT8 rows
   size_t o_tc = 0;               // tensor cores: activation tiles, weight chunks
   size_t o_mt = 0;               // tensor cores: the input map's own operand blocks
+  bool xtc = false;              // exact path on k_exact_tc (exact_tc): weights translated once
+  size_t o_xw = 0;               // its int8 weight chunks and scales
   size_t bytes = 0;
 };
 
@@ -584,6 +586,8 @@ hrb_status check_conv(hrb_ctx* ctx, const hrb_conv_desc* d, ConvRun* r) {
     }
     x.o_aq = take(size_t{x.M} * kb * 32u);
     x.o_as = take(size_t{x.M} * kb);
+    x.xtc = exact_tc(d->wfmt);
+    if (x.xtc) x.o_xw = take(hrb::x_weight_bytes(d->wfmt, x.N, static_cast<uint32_t>(kb)));
   }
   x.bytes = off;
   return HRB_OK;
@@ -609,6 +613,11 @@ hrb_status conv_prepare(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, 
       HRB_CUDA(ctx, cudaMemsetAsync(base + r.o_tc, 0, align_up(tc_act_bytes(&g, g.wfmt), 1024), s));
     }
     tc_translate(&g, tj, s);
+    *launched += 1;
+  }
+  if (r.xtc) {
+    const hrb_gemm_desc g = conv_gemm(d, r, base);
+    hrb::launch_x_translate(g.wfmt, g.w, g.wscale, g.N, blocks_of(g.K), base + r.o_xw, s);
     *launched += 1;
   }
   HRB_CUDA(ctx, cudaGetLastError());
@@ -690,12 +699,21 @@ hrb_status conv_execute(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, 
     *launched += 1;
   }
   if (take()) {
-    const uint64_t before = ctx->launches;
-    const hrb_status st =
-        run_dense(ctx, make_dense_job(&g, g.aq, g.ascale, r.pieces, r.npieces), s);
-    *launched += static_cast<uint32_t>(ctx->launches - before);
-    ctx->launches = before;
-    if (st != HRB_OK) return st;
+    const hrb::DenseJob job = make_dense_job(&g, g.aq, g.ascale, r.pieces, r.npieces);
+    if (r.xtc) {
+      // The weights were translated by conv_prepare.
+      const hrb::XJob xj = x_job(job, base + r.o_xw, 0);
+      const int n = hrb::launch_x_exact(nullptr, 1, &xj, hrb::x_tiles(job.M, job.N),
+                                        ctx->sm_count, ctx->d_error, s);
+      if (n < 0) return fail(ctx, HRB_ECUDA, "k_exact_tc launch failed");
+      *launched += static_cast<uint32_t>(n);
+    } else {
+      const uint64_t before = ctx->launches;
+      const hrb_status st = run_dense(ctx, job, s);
+      *launched += static_cast<uint32_t>(ctx->launches - before);
+      ctx->launches = before;
+      if (st != HRB_OK) return st;
+    }
   }
   if (d->relu && take()) {
     hrb::launch_relu_exact(d->c, r.M, r.N, r.N, s);
