@@ -295,15 +295,16 @@ bool exact_tc(uint32_t wfmt) {
 }
 
 // The tensor-core job of a dense exact job whose weights were translated
-// into xw.
+// into xw, in tiles of hrb::x_tok(job.M) tokens.
 hrb::XJob x_job(const hrb::DenseJob& job, const uint8_t* xw, uint32_t tile_begin) {
+  const uint32_t tok = hrb::x_tok(job.M);
   hrb::XJob x{};
   x.d = job;
   x.wt = xw;
   x.wsc = xw + hrb::x_code_bytes(job.wfmt, job.N, job.kb);
   x.planes = job.wfmt == 1 ? 2u : 1u;
   x.steps = (job.kb + 3u) / 4u;
-  x.m_tiles = (job.M + 63u) / 64u;
+  x.m_tiles = (job.M + tok - 1u) / tok;
   x.n_tiles = (job.N + 127u) / 128u;
   x.tile_begin = tile_begin;
   return x;
@@ -317,8 +318,9 @@ hrb_status run_dense(hrb_ctx* ctx, const hrb::DenseJob& job, cudaStream_t s) {
     uint8_t* xw = static_cast<uint8_t*>(ctx->xscratch);
     hrb::launch_x_translate(job.wfmt, job.w, job.wscale, job.N, job.kb, xw, s);
     const hrb::XJob x = x_job(job, xw, 0);
-    const int n = hrb::launch_x_exact(nullptr, 1, &x, hrb::x_tiles(job.M, job.N), ctx->sm_count,
-                                      ctx->d_error, s);
+    const uint32_t tok = hrb::x_tok(job.M);
+    const int n = hrb::launch_x_exact(nullptr, 1, &x, hrb::x_tiles(job.M, job.N, tok), tok,
+                                      ctx->sm_count, ctx->d_error, s);
     if (n < 0) return fail(ctx, HRB_ECUDA, "k_exact_tc launch failed");
     ctx->launches += 1u + static_cast<uint64_t>(n);
     HRB_CUDA(ctx, cudaGetLastError());
@@ -703,7 +705,8 @@ hrb_status conv_execute(hrb_ctx* ctx, const hrb_conv_desc* d, const ConvRun& r, 
     if (r.xtc) {
       // The weights were translated by conv_prepare.
       const hrb::XJob xj = x_job(job, base + r.o_xw, 0);
-      const int n = hrb::launch_x_exact(nullptr, 1, &xj, hrb::x_tiles(job.M, job.N),
+      const uint32_t tok = hrb::x_tok(job.M);
+      const int n = hrb::launch_x_exact(nullptr, 1, &xj, hrb::x_tiles(job.M, job.N, tok), tok,
                                         ctx->sm_count, ctx->d_error, s);
       if (n < 0) return fail(ctx, HRB_ECUDA, "k_exact_tc launch failed");
       *launched += static_cast<uint32_t>(n);
@@ -1401,8 +1404,9 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
   std::vector<std::vector<hrb::DenseJob>> exact(3);
   uint32_t exact_tiles[3] = {0, 0, 0};
   // Exact GEMMs on the tensor cores (exact_tc), per format, weights translated now.
-  std::vector<std::vector<hrb::XJob>> xexact(2);
-  uint32_t xexact_tiles[2] = {0, 0};
+  // Groups: format (MXFP4, W8) x token tile (64, 16): index 2 wfmt + (tok == 16).
+  std::vector<std::vector<hrb::XJob>> xexact(4);
+  uint32_t xexact_tiles[4] = {0, 0, 0, 0};
   struct TcKey { uint32_t nt, wfmt, kind; bool pairs; };
   std::vector<TcKey> tc_keys;
   std::vector<std::vector<hrb::TcJob>> tc_groups;
@@ -1467,10 +1471,11 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
       uint8_t* xw = sbase + soff;
       soff += align_up(hrb::x_weight_bytes(j.wfmt, j.N, j.kb), 1024);
       hrb::launch_x_translate(j.wfmt, j.w, j.wscale, j.N, j.kb, xw, ctx->stream);
-      xexact[j.wfmt].push_back(x_job(j, xw, xexact_tiles[j.wfmt]));
-      xexact_tiles[j.wfmt] += hrb::x_tiles(j.M, j.N);
-      plan->io[i].tile_begin = xexact[j.wfmt].back().tile_begin;
-      plan->io[i].tiles = hrb::x_tiles(j.M, j.N);
+      const uint32_t tok = hrb::x_tok(j.M), xg = 2u * j.wfmt + (tok == 16u ? 1u : 0u);
+      xexact[xg].push_back(x_job(j, xw, xexact_tiles[xg]));
+      xexact_tiles[xg] += hrb::x_tiles(j.M, j.N, tok);
+      plan->io[i].tile_begin = xexact[xg].back().tile_begin;
+      plan->io[i].tiles = hrb::x_tiles(j.M, j.N, tok);
       continue;
     }
     uint32_t tiles_n = 0;
@@ -1533,12 +1538,13 @@ hrb_status hrb_plan_create(hrb_ctx* ctx, const hrb_gemm_desc* descs, uint32_t co
                             nullptr});
     dst += g.size() * sizeof(hrb::DenseJob);
   }
-  for (uint32_t f = 0; f < 2; ++f) {
-    auto& g = xexact[f];
+  for (uint32_t xg = 0; xg < 4; ++xg) {
+    auto& g = xexact[xg];
     if (g.empty()) continue;
     HRB_CUDA(ctx, cudaMemcpy(dst, g.data(), g.size() * sizeof(hrb::XJob), cudaMemcpyHostToDevice));
-    plan->groups.push_back({f, 1u, 0, static_cast<uint32_t>(g.size()), xexact_tiles[f], dst,
-                            nullptr});
+    // nt: the group's token tile.
+    plan->groups.push_back({xg / 2u, 1u, xg % 2u != 0 ? 16u : 64u,
+                            static_cast<uint32_t>(g.size()), xexact_tiles[xg], dst, nullptr});
     dst += g.size() * sizeof(hrb::XJob);
   }
   for (size_t g = 0; g < tc_groups.size(); ++g) {
@@ -1600,7 +1606,7 @@ hrb_status plan_launch(hrb_plan* plan, cudaStream_t s, int64_t only, uint32_t* l
           static_cast<const hrb::DenseJob*>(g.d_jobs), g.njobs, nullptr, g.tiles, g.wfmt, s));
     } else if (g.kind == 1) {
       const int k = hrb::launch_x_exact(static_cast<const hrb::XJob*>(g.d_jobs), g.njobs, nullptr,
-                                        g.tiles, ctx->sm_count, ctx->d_error, s);
+                                        g.tiles, g.nt, ctx->sm_count, ctx->d_error, s);
       if (k < 0) return fail(ctx, HRB_ECUDA, "k_exact_tc launch failed");
       n += static_cast<uint32_t>(k);
     } else {

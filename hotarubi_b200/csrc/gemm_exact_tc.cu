@@ -55,36 +55,42 @@ namespace {
 using namespace sm100;
 
 constexpr uint32_t kXTileW = 128;                 // weight rows per tile (MMA M)
-constexpr uint32_t kXTok = 64;                    // tokens per tile (MMA N)
 constexpr uint32_t kXRowB = 128;                  // bytes per operand row per step
 constexpr uint32_t kXWChunk = kXTileW * kXRowB;   // one plane's weights of a step
-constexpr uint32_t kXABlock = kXTok * kXRowB;     // the step's activation codes
 constexpr uint32_t kXWScales = 4u * kXTileW;     // a step's weight scale bytes [4][128]
-// A ring slot holds one chain segment: the weight chunk, the activation
+constexpr uint32_t kXGroups = 2;                  // TMEM accumulator groups, one per segment
+constexpr uint32_t kXMagic = 0x4B400000u;         // FP32 1.5 2^23: 1.5 2^23 + dot as int32 bits
+constexpr uint32_t kXEpiTok = 16;                 // tokens per epilogue thread (x_tmem_ld)
+constexpr uint32_t kXFirstEpi = 3;                // warps 0 producer, 1 MMA, 2 activation stager
+constexpr uint32_t kXJobCache = 2048;             // jobs whose first tiles are kept in smem
+
+// A launch's layout for TOK tokens a tile (the MMA's N): 64, or 16 for
+// GEMMs of at most 16 tokens (four epilogue warps, two CTAs an SM).
+//   A ring slot holds one chain segment: the weight chunk, the activation
 // codes, the step's weight scale bytes, and the stager's activation-scale
 // table: per block and token 2^(ea - 127) and -1.5 2^23 times it, per block
 // the weight exponents the fast rule holds for.
-constexpr uint32_t kXSlotA = kXWChunk;
-constexpr uint32_t kXSlotWs = kXSlotA + kXABlock;
-constexpr uint32_t kXSlotTa = kXSlotWs + kXWScales;
-constexpr uint32_t kXSlotNc = kXSlotTa + 4u * kXTok * 4u;
-constexpr uint32_t kXSlotRg = kXSlotNc + 4u * kXTok * 4u;
-constexpr uint32_t kXSlot = (kXSlotRg + 4u * 8u + 1023u) / 1024u * 1024u;  // 27 KB
-constexpr uint32_t kXSlots = 7;
-constexpr uint32_t kXGroups = 2;                  // TMEM accumulator groups, one per segment
-constexpr uint32_t kXGroupCols = 4u * kXTok;      // a group: one 64-column accumulator per block
-constexpr uint32_t kXMagic = 0x4B400000u;         // FP32 1.5 2^23: 1.5 2^23 + dot as int32 bits
-constexpr uint32_t kXEpiTok = 16;                 // tokens per epilogue thread (x_tmem_ld)
-constexpr uint32_t kXEpiWarps = 4u * kXTok / kXEpiTok;
-constexpr uint32_t kXFirstEpi = 3;                // warps 0 producer, 1 MMA, 2 activation stager
-constexpr uint32_t kXThreads = 32u * (kXFirstEpi + kXEpiWarps);
-constexpr uint32_t kXOffBar = kXSlots * kXSlot;
-constexpr uint32_t kXJobCache = 2048;             // jobs whose first tiles are kept in smem
-constexpr uint32_t kXOffJobs = kXOffBar + 1024;
-constexpr uint32_t kXSmem = kXOffJobs + kXJobCache * 4u + 1024;
-static_assert(kXSmem <= 232448, "shared memory");
-
-static_assert(kXGroups * kXGroupCols == 512, "TMEM columns");
+template <uint32_t TOK>
+struct XCfg {
+  static constexpr uint32_t kTok = TOK;
+  static constexpr uint32_t kABlock = TOK * kXRowB;          // the step's activation codes
+  static constexpr uint32_t kSlotWs = kXWChunk + kABlock;
+  static constexpr uint32_t kSlotTa = kSlotWs + kXWScales;
+  static constexpr uint32_t kSlotNc = kSlotTa + 4u * TOK * 4u;
+  static constexpr uint32_t kSlotRg = kSlotNc + 4u * TOK * 4u;
+  static constexpr uint32_t kSlot = (kSlotRg + 4u * 8u + 1023u) / 1024u * 1024u;
+  static constexpr uint32_t kSlots = TOK == 64 ? 7u : 5u;
+  static constexpr uint32_t kCtas = TOK == 64 ? 1u : 2u;     // CTAs an SM
+  static constexpr uint32_t kGroupCols = 4u * TOK;           // one TOK-column accumulator a block
+  static constexpr uint32_t kTmemCols = kXGroups * kGroupCols;
+  static constexpr uint32_t kEpiWarps = 4u * TOK / kXEpiTok;
+  static constexpr uint32_t kThreads = 32u * (kXFirstEpi + kEpiWarps);
+  static constexpr uint32_t kOffBar = kSlots * kSlot;
+  static constexpr uint32_t kOffJobs = kOffBar + 1024;
+  static constexpr uint32_t kSmem = kOffJobs + kXJobCache * 4u + 1024;
+  static_assert(kSmem * kCtas <= 232448, "shared memory");
+  static_assert(kTmemCols * kCtas <= 512 && (kTmemCols & (kTmemCols - 1)) == 0, "TMEM columns");
+};
 
 // tcgen05 instruction descriptor of kind::i8: D S32 (2 at [4,6)), A and B
 // signed 8-bit (1 at [7,10) and [10,13)), both K-major, N >> 3 at [17,23),
@@ -257,13 +263,16 @@ __device__ __forceinline__ uint32_t x_find(const XJob* jobs, const uint32_t* beg
 
 
 // The scale bytes of segment w's blocks for tokens m0 + lane and + 32: 127
-// for tokens past M, blocks outside the segment, and a finished walk.
+// for tokens past M or past the tile's TOK, blocks outside the segment, and
+// a finished walk.
+template <uint32_t TOK>
 __device__ __forceinline__ void x_load_ea(const uint8_t* ascale, uint32_t M, uint32_t kb,
                                           uint32_t m0, const XWalk& w, uint32_t lane,
                                           int32_t (&ea)[2][4]) {
 #pragma unroll
   for (uint32_t h = 0; h < 2; ++h) {
-    const uint32_t m = m0 + lane + 32u * h;
+    const uint32_t tk = lane + 32u * h;  // the tile's token (TOK of them)
+    const uint32_t m = tk < TOK ? m0 + tk : M;
 #pragma unroll
     for (uint32_t j = 0; j < 4; ++j) {
       const uint32_t b = 4u * w.step + j;
@@ -276,21 +285,23 @@ __device__ __forceinline__ void x_load_ea(const uint8_t* ascale, uint32_t M, uin
 // Shared-memory layout and the tile's job: weights chunk then activation
 // codes per ring slot; barriers; the activation-scale table.
 struct XSmem {
-  uint64_t* full;       // [kXSlots] weights (tx bytes), 32 stager cp.async lanes, its table
-  uint64_t* empty;      // [kXSlots] the segment's MMAs done and the epilogue warps past it
+  uint64_t* full;       // [kSlots] weights (tx bytes), 32 stager cp.async lanes, its table
+  uint64_t* empty;      // [kSlots] the segment's MMAs done and the epilogue warps past it
   uint64_t* acc_full;   // [kXGroups] a segment's dots are in TMEM
   uint64_t* acc_empty;  // [kXGroups] the epilogue warps have read them
   uint32_t* tmem_slot;
 };
 
+template <uint32_t TOK>
 __device__ __forceinline__ XSmem x_smem(uint8_t* smem) {
+  using XC = XCfg<TOK>;
   XSmem x;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kXOffBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + XC::kOffBar);
   x.full = bars;
-  x.empty = bars + kXSlots;
-  x.acc_full = bars + 2 * kXSlots;
-  x.acc_empty = bars + 2 * kXSlots + kXGroups;
-  x.tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kXSlots + 2 * kXGroups);
+  x.empty = bars + XC::kSlots;
+  x.acc_full = bars + 2 * XC::kSlots;
+  x.acc_empty = bars + 2 * XC::kSlots + kXGroups;
+  x.tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * XC::kSlots + 2 * kXGroups);
   return x;
 }
 
@@ -298,6 +309,7 @@ struct XTile {
   uint32_t jx, m0, n0, nt;  // job, first token, first weight row, weight tile
 };
 
+template <uint32_t TOK>
 __device__ __forceinline__ XTile x_tile(const XJob* jobs, const uint32_t* begins, uint32_t njobs,
                                         const XJob& inline_job, uint32_t u, const XJob*& job) {
   XTile t;
@@ -305,7 +317,7 @@ __device__ __forceinline__ XTile x_tile(const XJob* jobs, const uint32_t* begins
   job = jobs != nullptr ? &jobs[t.jx] : &inline_job;
   const uint32_t local = u - job->tile_begin;
   t.nt = local % job->n_tiles;
-  t.m0 = (local / job->n_tiles) * kXTok;
+  t.m0 = (local / job->n_tiles) * TOK;
   t.n0 = t.nt * kXTileW;
   return t;
 }
@@ -334,20 +346,23 @@ __device__ __noinline__ float x_slow(float acc, uint32_t dot_bits, const uint8_t
 // the tile), from the bits of 1.5 2^23 + dot and the slot's table.
 // arow: the scale bytes of the thread's first token; mrem: tokens left from
 // it (for the integer rule).
+template <uint32_t TOK>
 __device__ __forceinline__ void x_block(float (&acc)[kXEpiTok], const uint32_t (&dot)[kXEpiTok],
                                         const uint8_t* sp, uint32_t b, uint32_t r, uint32_t tok0,
                                         int32_t sb, const uint8_t* arow, uint32_t mrem,
                                         uint32_t kb) {
+  using XC = XCfg<TOK>;
   const uint32_t j4 = b & 3u;
-  const int32_t ew = static_cast<int32_t>(sp[kXSlotWs + j4 * kXTileW + r]) + sb;
-  const int2 rg = reinterpret_cast<const int2*>(sp + kXSlotRg)[j4];
+  const int32_t ew = static_cast<int32_t>(sp[XC::kSlotWs + j4 * kXTileW + r]) + sb;
+  const int2 rg = reinterpret_cast<const int2*>(sp + XC::kSlotRg)[j4];
   if (ew >= rg.x && ew <= rg.y) {
     // The first FMA removes 1.5 2^23 from the exact product: dot
     // 2^(ea - 127).  The second's product is exact and normal, so it rounds
     // as the chain's add of the block value.
     const float tw = __uint_as_float(static_cast<uint32_t>(ew) << 23);
-    const float4* ta = reinterpret_cast<const float4*>(sp + kXSlotTa) + (j4 * kXTok + tok0) / 4u;
-    const float4* nc = reinterpret_cast<const float4*>(sp + kXSlotNc) + (j4 * kXTok + tok0) / 4u;
+    const uint32_t first = (j4 * XC::kTok + tok0) / 4u;  // the thread's first token, in float4s
+    const float4* ta = reinterpret_cast<const float4*>(sp + XC::kSlotTa) + first;
+    const float4* nc = reinterpret_cast<const float4*>(sp + XC::kSlotNc) + first;
     // 16 tokens at a time: the empty asm keeps the compiler from loading
     // every table value at once (register pressure).
 #pragma unroll
@@ -374,34 +389,36 @@ __device__ __forceinline__ void x_block(float (&acc)[kXEpiTok], const uint32_t (
 }
 
 
-__global__ void __launch_bounds__(kXThreads, 1)
+template <uint32_t TOK>
+__global__ void __launch_bounds__(XCfg<TOK>::kThreads, XCfg<TOK>::kCtas)
 k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline_job,
            uint32_t total_tiles, uint32_t* err) {
+  using XC = XCfg<TOK>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  const XSmem x = x_smem(smem);
+  const XSmem x = x_smem<TOK>(smem);
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   // The jobs' first tiles (written when the plan was made, not by the
   // kernel before this one), for the per-tile job search.
   uint32_t* begins = nullptr;
   if (jobs != nullptr && njobs <= kXJobCache) {
-    begins = reinterpret_cast<uint32_t*>(smem + kXOffJobs);
+    begins = reinterpret_cast<uint32_t*>(smem + XC::kOffJobs);
     for (uint32_t i = threadIdx.x; i < njobs; i += blockDim.x) begins[i] = jobs[i].tile_begin;
   }
   if (threadIdx.x == 0) {
-    for (uint32_t s = 0; s < kXSlots; ++s) {
+    for (uint32_t s = 0; s < XC::kSlots; ++s) {
       mbar_init(&x.full[s], 1u + 32u + 1u);  // weights, the stager's copies, its table
-      mbar_init(&x.empty[s], 1u + kXEpiWarps);
+      mbar_init(&x.empty[s], 1u + XC::kEpiWarps);
     }
     for (uint32_t a = 0; a < kXGroups; ++a) {
       mbar_init(&x.acc_full[a], 1u);
-      mbar_init(&x.acc_empty[a], kXEpiWarps);
+      mbar_init(&x.acc_empty[a], XC::kEpiWarps);
     }
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(x.tmem_slot, kXGroups * kXGroupCols);
+    tmem_alloc(x.tmem_slot, kXGroups * XC::kGroupCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -418,21 +435,21 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
       uint32_t n = 0;
       for (uint32_t u = blockIdx.x; u < total_tiles && ok; u += gridDim.x) {
         const XJob* job;
-        const XTile t = x_tile(jobs, begins, njobs, inline_job, u, job);
+        const XTile t = x_tile<TOK>(jobs, begins, njobs, inline_job, u, job);
         const XChain c = x_chain(*job);
         const uint8_t* wt = job->wt;
         const uint8_t* wsc = job->wsc;
         const uint32_t steps = job->steps;
         XWalk w;
         for (x_begin(c, w); !w.done && ok; x_next(c, w), ++n) {
-          const uint32_t sl = n % kXSlots;
-          if (n >= kXSlots) ok = mbar_wait(&x.empty[sl], ((n / kXSlots) - 1u) & 1u, err);
+          const uint32_t sl = n % XC::kSlots;
+          if (n >= XC::kSlots) ok = mbar_wait(&x.empty[sl], ((n / XC::kSlots) - 1u) & 1u, err);
           if (!ok) break;
           mbar_arrive_expect_tx(&x.full[sl], kXWChunk + kXWScales);
           const size_t ts = size_t{t.nt} * steps + w.step;
-          bulk_g2s(smem + sl * kXSlot, wt + (ts * c.planes + w.plane) * kXWChunk, kXWChunk,
+          bulk_g2s(smem + sl * XC::kSlot, wt + (ts * c.planes + w.plane) * kXWChunk, kXWChunk,
                    &x.full[sl]);
-          bulk_g2s(smem + sl * kXSlot + kXSlotWs, wsc + ts * kXWScales, kXWScales, &x.full[sl]);
+          bulk_g2s(smem + sl * XC::kSlot + XC::kSlotWs, wsc + ts * kXWScales, kXWScales, &x.full[sl]);
         }
       }
     }
@@ -444,7 +461,7 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
     uint32_t n = 0;
     for (uint32_t u = blockIdx.x; u < total_tiles && ok; u += gridDim.x) {
       const XJob* job;
-      const XTile t = x_tile(jobs, begins, njobs, inline_job, u, job);
+      const XTile t = x_tile<TOK>(jobs, begins, njobs, inline_job, u, job);
       const XChain c = x_chain(*job);
       const int8_t* aq = job->d.aq;
       const uint8_t* ascale = job->d.ascale;
@@ -455,15 +472,15 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
       XWalk w;
       x_begin(c, w);
       int32_t ea[2][4];
-      x_load_ea(ascale, M, c.kb, t.m0, w, lane, ea);
+      x_load_ea<TOK>(ascale, M, c.kb, t.m0, w, lane, ea);
       for (; !w.done && ok; ++n) {
-        const uint32_t sl = n % kXSlots;
-        if (n >= kXSlots) ok = mbar_wait(&x.empty[sl], ((n / kXSlots) - 1u) & 1u, err);
+        const uint32_t sl = n % XC::kSlots;
+        if (n >= XC::kSlots) ok = mbar_wait(&x.empty[sl], ((n / XC::kSlots) - 1u) & 1u, err);
         ok = __all_sync(0xFFFFFFFFu, ok);
         if (!ok) break;
-        const uint32_t dst0 = smem_addr(smem + sl * kXSlot + kXWChunk);
+        const uint32_t dst0 = smem_addr(smem + sl * XC::kSlot + kXWChunk);
 #pragma unroll 4
-        for (uint32_t i = 0; i < kXTok * 8u / 32u; ++i) {
+        for (uint32_t i = 0; i < XC::kTok * 8u / 32u; ++i) {
           const uint32_t chunk = lane + 32u * i, r = chunk / 8u, cc = chunk % 8u;
           const uint32_t row = t.m0 + r;
           const size_t col = size_t{w.step} * 128u + cc * 16u;
@@ -475,16 +492,18 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
         XWalk nx = w;
         x_next(c, nx);
         int32_t ea_nx[2][4];
-        x_load_ea(ascale, M, c.kb, t.m0, nx, lane, ea_nx);
-        uint8_t* sp = smem + sl * kXSlot;
+        x_load_ea<TOK>(ascale, M, c.kb, t.m0, nx, lane, ea_nx);
+        uint8_t* sp = smem + sl * XC::kSlot;
 #pragma unroll
         for (uint32_t j = 0; j < 4; ++j) {
 #pragma unroll
           for (uint32_t h = 0; h < 2; ++h) {
             const float ta = __uint_as_float(static_cast<uint32_t>(ea[h][j]) << 23);
-            const uint32_t e = j * kXTok + lane + 32u * h;
-            reinterpret_cast<float*>(sp + kXSlotTa)[e] = ta;
-            reinterpret_cast<float*>(sp + kXSlotNc)[e] = -12582912.0f * ta;
+            const uint32_t tk = lane + 32u * h;
+            if (tk < TOK) {
+              reinterpret_cast<float*>(sp + XC::kSlotTa)[j * TOK + tk] = ta;
+              reinterpret_cast<float*>(sp + XC::kSlotNc)[j * TOK + tk] = -12582912.0f * ta;
+            }
           }
           const int32_t lo = __reduce_min_sync(0xFFFFFFFFu, min(ea[0][j], ea[1][j]));
           const int32_t hi = __reduce_max_sync(0xFFFFFFFFu, max(ea[0][j], ea[1][j]));
@@ -492,7 +511,7 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
             // |dot| < 2^16: dot 2^(ea + e - 254) stays in [2^-126, 2^128)
             // for e in [128 - min ea, 365 - max ea]; 2^(ea - 127) and its
             // 1.5 2^23 multiple are normal for ea in [1, 230].
-            reinterpret_cast<int2*>(sp + kXSlotRg)[j] =
+            reinterpret_cast<int2*>(sp + XC::kSlotRg)[j] =
                 lo >= 1 && hi <= 230 ? make_int2(max(1, 128 - lo), min(254, 365 - hi))
                                      : make_int2(1000, -1000);
           }
@@ -513,25 +532,25 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
     // the accumulators of group n % 2, one commit per segment.
     if (lane == 0) {
       uint32_t n = 0;
-      constexpr uint32_t kIdesc = idesc_i8(kXTileW, kXTok);
+      constexpr uint32_t kIdesc = idesc_i8(kXTileW, XC::kTok);
       for (uint32_t u = blockIdx.x; u < total_tiles && ok; u += gridDim.x) {
         const XJob* job;
-        x_tile(jobs, begins, njobs, inline_job, u, job);
+        x_tile<TOK>(jobs, begins, njobs, inline_job, u, job);
         const XChain c = x_chain(*job);
         XWalk w;
         for (x_begin(c, w); !w.done && ok; x_next(c, w), ++n) {
-          const uint32_t sl = n % kXSlots, gi = n % kXGroups;
-          ok = mbar_wait(&x.full[sl], (n / kXSlots) & 1u, err);
+          const uint32_t sl = n % XC::kSlots, gi = n % kXGroups;
+          ok = mbar_wait(&x.full[sl], (n / XC::kSlots) & 1u, err);
           // Phase k of acc_empty: the epilogue has read segment n - 2 (k = 0:
           // the accumulators hold their start value).
           if (ok) ok = mbar_wait(&x.acc_empty[gi], (n / kXGroups) & 1u, err);
           if (!ok) break;
           tc_fence_after();
           fence_proxy_async_smem();  // the stager's cp.async writes
-          const uint32_t wa = smem_addr(smem + sl * kXSlot), aa = wa + kXWChunk;
+          const uint32_t wa = smem_addr(smem + sl * XC::kSlot), aa = wa + kXWChunk;
           for (uint32_t b = w.b0; b < w.b1; ++b) {
             const uint32_t k = (b & 3u) * 32u;
-            mma_i8(tmem + gi * kXGroupCols + (b & 3u) * kXTok, desc_sw128(wa + k),
+            mma_i8(tmem + gi * XC::kGroupCols + (b & 3u) * XC::kTok, desc_sw128(wa + k),
                    desc_sw128(aa + k), kIdesc);
           }
           mma_commit(&x.acc_full[gi]);
@@ -554,7 +573,7 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
     uint32_t n = 0;
     for (uint32_t u = blockIdx.x; u < total_tiles; u += gridDim.x) {
       const XJob* job;
-      const XTile t = x_tile(jobs, begins, njobs, inline_job, u, job);
+      const XTile t = x_tile<TOK>(jobs, begins, njobs, inline_job, u, job);
       const XChain c = x_chain(*job);
       const DenseJob& d = job->d;
       const uint32_t M = d.M, N = d.N, kb = c.kb;
@@ -577,20 +596,20 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
         const uint32_t mode = c.planes == 1 ? kModeFp4 : (w.plane == 0 ? kModeW8Hi : kModeW8Lo);
         const int32_t sb = scale_bias(mode);
         const uint32_t gi = n % kXGroups;
-        const uint8_t* sp = smem + (n % kXSlots) * kXSlot;
+        const uint8_t* sp = smem + (n % XC::kSlots) * XC::kSlot;
         // The slot's table (the stager's stores, acquired here directly) and
         // the segment's dots.
-        bool got = mbar_wait(&x.full[n % kXSlots], (n / kXSlots) & 1u, err);
+        bool got = mbar_wait(&x.full[n % XC::kSlots], (n / XC::kSlots) & 1u, err);
         got = got && mbar_wait(&x.acc_full[gi], (n / kXGroups) & 1u, err);
         got = __all_sync(0xFFFFFFFFu, got);
         tc_fence_after();
         // The segment's blocks: each dot read, 1.5 2^23 added to it as int32
         // (its FP32 bits), and its block added to the chains.
-        const uint32_t gcol = tbase + gi * kXGroupCols;
+        const uint32_t gcol = tbase + gi * XC::kGroupCols;
         const uint8_t* arow = ascale + size_t{t.m0 + tok0} * kb;
         const uint32_t mrem = M - min(M, t.m0 + tok0);
         for (uint32_t b = w.b0; b < w.b1; ++b) {
-          const uint32_t tcol = gcol + (b & 3u) * kXTok;
+          const uint32_t tcol = gcol + (b & 3u) * XC::kTok;
           uint32_t dot[kXEpiTok];
           if (got) {
             x_tmem_ld(tcol, dot);
@@ -601,13 +620,13 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
 #pragma unroll
             for (uint32_t i = 0; i < kXEpiTok; ++i) dot[i] = kXMagic;
           }
-          x_block(acc, dot, sp, b, r, tok0, sb, arow, mrem, kb);
+          x_block<TOK>(acc, dot, sp, b, r, tok0, sb, arow, mrem, kb);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&x.acc_empty[gi]);
-          mbar_arrive(&x.empty[n % kXSlots]);
+          mbar_arrive(&x.empty[n % XC::kSlots]);
         }
       }
       // The tile's outputs: column scale, bias, +0 for zeros; a chain that met
@@ -642,7 +661,7 @@ k_exact_tc(const XJob* jobs, uint32_t njobs, const __grid_constant__ XJob inline
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kXGroups * kXGroupCols);
+    tmem_dealloc(tmem, kXGroups * XC::kGroupCols);
   }
 }
 
@@ -660,8 +679,10 @@ size_t x_weight_bytes(uint32_t wfmt, uint32_t N, uint32_t kb) {
   return x_code_bytes(wfmt, N, kb) + n_tiles * steps * kXWScales;
 }
 
-uint32_t x_tiles(uint32_t M, uint32_t N) {
-  return ((M + kXTok - 1) / kXTok) * ((N + kXTileW - 1) / kXTileW);
+uint32_t x_tok(uint32_t M) { return M <= 16u ? 16u : 64u; }
+
+uint32_t x_tiles(uint32_t M, uint32_t N, uint32_t tok) {
+  return ((M + tok - 1) / tok) * ((N + kXTileW - 1) / kXTileW);
 }
 
 void launch_x_translate(uint32_t wfmt, const uint8_t* w, const uint8_t* wscale, uint32_t N,
@@ -673,11 +694,14 @@ void launch_x_translate(uint32_t wfmt, const uint8_t* w, const uint8_t* wscale, 
                                                                  wfmt == 1 ? 2u : 1u, wfmt, out);
 }
 
-int launch_x_exact(const XJob* jobs_dev, uint32_t njobs, const XJob* inline_job, uint32_t tiles,
-                   int sm_count, uint32_t* err, cudaStream_t stream) {
-  if (tiles == 0) return 0;
-  const void* fn = reinterpret_cast<const void*>(k_exact_tc);
-  if (!set_smem_limit_once(fn, kXSmem)) return -1;
+namespace {
+
+template <uint32_t TOK>
+int launch_x(const XJob* jobs_dev, uint32_t njobs, const XJob* inline_job, uint32_t tiles,
+             int sm_count, uint32_t* err, cudaStream_t stream) {
+  using XC = XCfg<TOK>;
+  const void* fn = reinterpret_cast<const void*>(k_exact_tc<TOK>);
+  if (!set_smem_limit_once(fn, XC::kSmem)) return -1;
   XJob one{};
   if (inline_job != nullptr) one = *inline_job;
   const XJob* jd = jobs_dev;
@@ -685,9 +709,9 @@ int launch_x_exact(const XJob* jobs_dev, uint32_t njobs, const XJob* inline_job,
   uint32_t* e = err;
   void* args[] = {&jd, &nj, &one, &total, &e};
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(std::min<uint32_t>(tiles, static_cast<uint32_t>(sm_count)));
-  cfg.blockDim = dim3(kXThreads);
-  cfg.dynamicSmemBytes = kXSmem;
+  cfg.gridDim = dim3(std::min<uint32_t>(tiles, XC::kCtas * static_cast<uint32_t>(sm_count)));
+  cfg.blockDim = dim3(XC::kThreads);
+  cfg.dynamicSmemBytes = XC::kSmem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -695,6 +719,16 @@ int launch_x_exact(const XJob* jobs_dev, uint32_t njobs, const XJob* inline_job,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelExC(&cfg, fn, args) == cudaSuccess ? 1 : -1;
+}
+
+}  // namespace
+
+int launch_x_exact(const XJob* jobs_dev, uint32_t njobs, const XJob* inline_job, uint32_t tiles,
+                   uint32_t tok, int sm_count, uint32_t* err, cudaStream_t stream) {
+  if (tiles == 0) return 0;
+  if (tok == 64) return launch_x<64>(jobs_dev, njobs, inline_job, tiles, sm_count, err, stream);
+  if (tok == 16) return launch_x<16>(jobs_dev, njobs, inline_job, tiles, sm_count, err, stream);
+  return -1;
 }
 
 }  // namespace hrb

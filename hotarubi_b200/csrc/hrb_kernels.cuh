@@ -157,13 +157,14 @@ struct DenseJob {
 // The exact chain with its block dots on the tensor cores
 // (gemm_exact_tc.cu): a DenseJob whose weights were translated into int8
 // chunks by launch_x_translate, in output tiles of 128 weight rows x 64
-// tokens.  MXFP4 and W8 only (x_supported).
+// tokens (16 for GEMMs of at most 16 tokens).  MXFP4 and W8 only
+// (x_supported).
 struct XJob {
   DenseJob d;
   const uint8_t* wt;          // [n_tiles][steps][planes] chunks of 128 x 128 int8
   const uint8_t* wsc;         // [n_tiles][steps] 4 blocks x 128 rows of scale bytes
   uint32_t planes, steps;     // 1 (MXFP4) or 2 (W8: HI, LO); ceil(kb / 4)
-  uint32_t m_tiles, n_tiles;
+  uint32_t m_tiles, n_tiles;  // of the launch's token tile
   uint32_t tile_begin;        // prefix over the launch's jobs
 };
 
@@ -171,12 +172,16 @@ bool x_supported(uint32_t wfmt);
 // Bytes of the translated weights: the chunks (x_code_bytes), then the scales.
 size_t x_code_bytes(uint32_t wfmt, uint32_t N, uint32_t kb);
 size_t x_weight_bytes(uint32_t wfmt, uint32_t N, uint32_t kb);
-uint32_t x_tiles(uint32_t M, uint32_t N);
+// The token tile of a job of M tokens (16 for M <= 16, else 64) and its
+// output tiles.
+uint32_t x_tok(uint32_t M);
+uint32_t x_tiles(uint32_t M, uint32_t N, uint32_t tok);
 void launch_x_translate(uint32_t wfmt, const uint8_t* w, const uint8_t* wscale, uint32_t N,
                         uint32_t kb, uint8_t* out, cudaStream_t stream);
-// One launch over `tiles` output tiles of jobs_dev (or of *inline_job).
+// One launch over `tiles` output tiles of jobs_dev (or of *inline_job),
+// every job with token tile `tok` (x_tok).
 int launch_x_exact(const XJob* jobs_dev, uint32_t njobs, const XJob* inline_job, uint32_t tiles,
-                   int sm_count, uint32_t* err, cudaStream_t stream);
+                   uint32_t tok, int sm_count, uint32_t* err, cudaStream_t stream);
 
 // Host-side launchers (async on `stream`).  Either jobs_dev points to njobs
 // device-resident jobs, or it is null and the single *inline_job travels as

@@ -223,6 +223,22 @@ def test_larger_gemm(hrb, wfmt):
     _check(hrb, wfmt, q, s, w, ws, 1024)
 
 
+@pytest.mark.parametrize("wfmt", [0, 1])
+def test_decode_token_tile(hrb, wfmt):
+    """GEMMs of at most 16 tokens run 16-token tiles (four epilogue warps, two
+    CTAs an SM); 17 tokens the 64-token tile: both sides of the switch, W8
+    pieces, bias and accumulate."""
+    rng = np.random.default_rng(80 + wfmt)
+    for m, n, kb in ((1, 1000, 80), (16, 300, 40), (17, 300, 40), (9, 129, 130)):
+        q, s = _mxint8(rng, m, kb)
+        w, ws = _weights(rng, wfmt, n, kb)
+        _check(hrb, wfmt, q, s, w, ws, n)
+        bias = (rng.standard_normal(n).astype(np.float32)).view(np.uint32)
+        c0 = rng.standard_normal((m, n)).astype(np.float32).view(np.uint32)
+        pieces = [kb // 3, kb - kb // 3] if wfmt == 1 else None
+        _check(hrb, wfmt, q, s, w, ws, n, bias=bias, c_init=c0, pieces=pieces)
+
+
 @pytest.mark.skipif(not TC, reason="the rerun itself")
 def test_dense_exact_kernel_passes_the_same_cases():
     """k_dense_exact (HRB_EXACT_TC=0) on every case above: both kernels give
