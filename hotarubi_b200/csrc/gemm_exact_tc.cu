@@ -6,23 +6,27 @@
 // tools/iss/fp32.hpp:46-75); W8 runs all HI blocks of a K piece, then all
 // LO blocks (tools/compiler/kernels.cpp:35-37).  The block dots are exact
 // integers, so they can come from anywhere: here each is one
-// tcgen05.mma kind::i8 (M = 128 weight rows, N = 64 tokens, K = 32 = one
+// tcgen05.mma kind::i8 (M = 128 weight rows, N = TOK tokens, K = 32 = one
 // block, int32 accumulator in TMEM, no accumulation across blocks), and the
 // CUDA cores turn the dots into block values and run the chain in the
-// reference's order.
+// reference's order.  TOK is 64, or 16 for GEMMs of at most 16 tokens (XCfg).
 //
 //   * weights: int8 values per (128-row tile, plane, 4-block step), 128 rows
-//     x 128 bytes in the 128-byte swizzle (translated once per plan or call):
-//     MXFP4 as 2 x E2M1 (-12 .. 12), W8 as its HI nibble (-8 .. 7) and LO
-//     nibble (0 .. 15) planes; their scale bytes stay in the dense [N][kb];
+//     x 128 bytes in the 128-byte swizzle, then per (tile, step) the scale
+//     bytes [4 blocks][128 rows] (translated once per plan or call): MXFP4
+//     as 2 x E2M1 (-12 .. 12), W8 as its HI nibble (-8 .. 7) and LO nibble
+//     (0 .. 15) planes;
 //   * activations: the dense MXINT8 codes [M][kp] and scales [M][kb], the
-//     codes staged by one warp with cp.async into the same swizzle;
+//     codes staged by one warp with cp.async into the same swizzle, which
+//     also writes each segment's scale table into the ring slot (the scale
+//     bytes loaded a segment ahead);
 //   * the MMA thread issues one MMA per block, in chain order, into one of
-//     two groups of four TMEM accumulators (64 columns each; a chain segment
-//     is at most the four blocks of a step, and takes a group), with one
-//     commit per segment; the epilogue warps (warp w: TMEM lane quarter
+//     two groups of four TMEM accumulators (TOK columns each; a chain
+//     segment is at most the four blocks of a step, and takes a group), with
+//     one commit per segment; the epilogue warps (warp w: TMEM lane quarter
 //     w % 4, tokens 16 (w / 4) .. + 15) hold the 16 chains of their weight
-//     row in registers and hand the group back once per segment;
+//     row in registers and hand the group, and the ring slot, back once per
+//     segment;
 //   * the int32 dot plus 0x4B400000 is the FP32 bits of 1.5 2^23 + dot
 //     (|dot| < 2^16): one integer add converts it (measured a little faster
 //     than accumulating the MMA onto that constant and writing it back to
@@ -34,10 +38,11 @@
 //     block is normal and finite and the table values are normal (ea in
 //     [1, 230], ea + ew + SBIAS in [128, 365], per block over its tokens);
 //     other blocks take the integer rule (scale_pow2_bits);
-//   * chain: FTZ round-to-nearest FP32 adds, equal to the reference adder while results stay
-//     below exponent 255 (hrb_device.cuh); a chain that reaches exponent 255
-//     is recomputed from the dense operands with the integer adder, and zero
-//     results are made +0 at the end, as in k_dense_exact.
+//   * chain: FTZ round-to-nearest FP32 adds, equal to the reference adder
+//     while results stay below exponent 255 (hrb_device.cuh); a chain that
+//     reaches exponent 255 is recomputed from the dense operands with the
+//     integer adder, and zero results are made +0 at the end, as in
+//     k_dense_exact.
 //
 // Every wait is bounded.
 #include <algorithm>
