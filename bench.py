@@ -1494,7 +1494,13 @@ def run_shard(args, wl: Workload, rank: int, world: int, local_rank: int) -> Non
     group = shard.Group(lib)   # the library's communicator (NCCL through the C ABI)
     batch = args.batch or wl.batch
     n0, n1 = shard.columns(wl.N)
-    out = shard.PeerOutput(lib, group, (batch, wl.M, wl.N))
+    mx = args.gather == "mxint8"
+    kpn = (wl.N + 31) // 32 * 32
+    # --gather mxint8: each GEMM keeps only its MXINT8 copy (1 + 1/32 bytes an
+    # output, the next layer's activation format), written in the full
+    # matrix's layout (ldcq) into every rank's buffer.
+    out = (shard.PeerOutput(lib, group, (1,), mx_shape=(batch * wl.M, kpn)) if mx
+           else shard.PeerOutput(lib, group, (batch, wl.M, wl.N)))
     sets = [host_operands(wl, i) for i in range(min(4, batch))]
     keep, descs = [], []
     a_all = torch.empty((batch, wl.M, wl.K), dtype=torch.float32, device="cuda")
@@ -1504,7 +1510,14 @@ def run_shard(args, wl: Workload, rank: int, world: int, local_rank: int) -> Non
         t = [torch.from_numpy(w[n0:n1].copy()).cuda(), torch.from_numpy(ws[n0:n1].copy()).cuda(),
              None if bias is None else torch.from_numpy(bias[n0:n1].copy()).cuda()]
         keep += t
-        if n1 > n0:
+        if n1 > n0 and mx:
+            rows = slice(b * wl.M, (b + 1) * wl.M)
+            descs.append(capi.Library.desc(wl.wfmt, wl.M, n1 - n0, wl.K, a=a_all[b], w=t[0],
+                                           wscale=t[1], bias=t[2], c=None,
+                                           cq=out.q[rows].data_ptr() + n0,
+                                           cscale=out.s[rows].data_ptr() + n0 // 32,
+                                           ldcq=kpn, mode=capi.MODE_FAST))
+        elif n1 > n0:
             descs.append(capi.Library.desc(wl.wfmt, wl.M, n1 - n0, wl.K, a=a_all[b], w=t[0],
                                            wscale=t[1], bias=t[2],
                                            c=out.tensor[b].data_ptr() + 4 * n0, ldc=wl.N,
@@ -1539,7 +1552,8 @@ def run_shard(args, wl: Workload, rank: int, world: int, local_rank: int) -> Non
     ms = float(t.item())
     if rank == 0:
         pk = peaks()
-        nvlink = (world - 1) * batch * wl.M * wl.N * 4 / world   # bytes each rank stores to peers
+        per_out = (1 + 1 / 32) if mx else 4                       # bytes an output crosses
+        nvlink = (world - 1) * batch * wl.M * wl.N * per_out / world  # each rank to its peers
         line = {
             "metric": wl.metric, "value": batch * wl.flops / (ms / 1e3) / 1e12,
             "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -1548,6 +1562,8 @@ def run_shard(args, wl: Workload, rank: int, world: int, local_rank: int) -> Non
             "data": "synthetic",
             "config": {"workload": wl.name, "batch": batch, "M": wl.M, "N": wl.N, "K": wl.K,
                        "format": FMT_NAMES[wl.wfmt], "mode": "fast",
+                       "gather": ("MXINT8 copy (1 + 1/32 B an output, the FP32 output "
+                                  "not kept)" if mx else "FP32 output"),
                        "parallelism": f"N-sharded x{world}, all-gather fused into the GEMM "
                                       "epilogue (NVLink peer stores)"},
             "nvlink": {"bytes_per_rank_per_step": nvlink,
@@ -2124,6 +2140,9 @@ def main() -> None:
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the host entry-point leg "
                    "(profiling runs)")
+    p.add_argument("--gather", choices=["fp32", "mxint8"], default="fp32",
+                   help="--shard on a GEMM config: what the fused all-gather moves (mxint8: the "
+                        "output's MXINT8 copy only)")
     p.add_argument("--shard", action="store_true", help="split each GEMM along N (c5conv: the "
                    "images along M) over the ranks, with the all-gather fused into the kernel "
                    "(strong scaling)")

@@ -62,6 +62,7 @@ class GemmDesc(ctypes.Structure):
         ("pieces", ctypes.c_void_p), ("npieces", ctypes.c_uint32),
         ("cq", ctypes.c_void_p), ("cscale", ctypes.c_void_p), ("cquant", ctypes.c_uint32),
         ("wcol_scale", ctypes.c_void_p), ("w8_kernel", ctypes.c_uint32),
+        ("ldcq", ctypes.c_uint32),
     ]
 
 
@@ -433,7 +434,7 @@ class Library:
     def desc(wfmt, M, N, K, *, a=None, lda=None, quant=QUANT_HOST, aq=None, ascale=None,
              w=None, wscale=None, bias=None, c=None, ldc=None, accumulate=False,
              pieces=None, mode=MODE_EXACT, cq=None, cscale=None, cquant=QUANT_VEC,
-             wcol_scale=None, w8_kernel=0):
+             wcol_scale=None, w8_kernel=0, ldcq=0):
         d = GemmDesc()
         d.wfmt, d.mode, d.M, d.N, d.K = wfmt, mode, M, N, K
         d.a = _ptr(a)
@@ -448,6 +449,7 @@ class Library:
         d.cq, d.cscale, d.cquant = _ptr(cq), _ptr(cscale), cquant
         d.wcol_scale = _ptr(wcol_scale)
         d.w8_kernel = w8_kernel
+        d.ldcq = ldcq
         if pieces is not None:
             arr = np.ascontiguousarray(pieces, dtype=np.uint32)
             d._pieces_keep = arr  # keep alive

@@ -189,6 +189,11 @@ hrb_status check_desc(hrb_ctx* ctx, const hrb_gemm_desc* d, uint32_t* pieces,
   if (d->cq != nullptr && d->cquant > HRB_QUANT_VEC) {
     return fail(ctx, HRB_EINVAL, "unknown output quantizer %u", d->cquant);
   }
+  if (d->ldcq != 0 &&
+      (d->cq == nullptr || d->ldcq % 32u != 0 || d->ldcq < blocks_of(d->N) * 32u)) {
+    return fail(ctx, HRB_EINVAL, "ldcq %u: needs cq, a multiple of 32 and at least N rounded up "
+                                 "to 32 (%u)", d->ldcq, blocks_of(d->N) * 32u);
+  }
   if (d->c == nullptr) {
     // Only the fused re-quantisation may stand in for the FP32 output.
     if (d->cq == nullptr || d->mode != HRB_MODE_FAST || d->a == nullptr || d->accumulate) {
@@ -279,7 +284,9 @@ size_t act_scratch_bytes(uint32_t M, uint32_t K) {
 // The MXINT8 copy of C for GEMMs that do not take the tensor-core path (its
 // epilogue makes the copy itself): the encoder over C, after the GEMM.
 hrb::QuantJob post_quant_job(const hrb_gemm_desc* d) {
-  return make_quant_job(d->c, d->M, d->N, d->ldc, d->cquant, d->cq, d->cscale);
+  hrb::QuantJob j = make_quant_job(d->c, d->M, d->N, d->ldc, d->cquant, d->cq, d->cscale);
+  j.ldq = d->ldcq / 32u;
+  return j;
 }
 
 // The exact GEMM, once activations are MXINT8 on the device.
@@ -418,6 +425,7 @@ void tc_jobs(const hrb_gemm_desc* d, uint32_t pf, uint8_t* base, hrb::QuantJob* 
   tj->cq = d->cq;
   tj->cscale = d->cscale;
   tj->cquant = d->cquant;
+  tj->ldcq = d->ldcq;
 }
 
 // Translates the weights of one tensor-core GEMM into the chunk layout.
@@ -1280,7 +1288,7 @@ hrb_status hrb_gemm_dense_host(hrb_ctx* ctx, const hrb_gemm_desc* d) {
   const size_t b_bytes = d->bias ? size_t{d->N} * 4u : 0;
   const size_t cs_bytes = d->wcol_scale ? size_t{d->N} * 4u : 0;
   const size_t c_bytes = d->c ? size_t{d->M} * d->N * 4u : 0;
-  const uint32_t kbq = blocks_of(d->N);
+  const uint32_t kbq = d->ldcq != 0 ? d->ldcq / 32u : blocks_of(d->N);  // row blocks of the copy
   const size_t q_bytes = d->cq ? size_t{d->M} * kbq * 32u : 0;
   const size_t qs_bytes = d->cq ? size_t{d->M} * kbq : 0;
   size_t off = 0;
@@ -1338,8 +1346,18 @@ hrb_status hrb_gemm_dense_host(hrb_ctx* ctx, const hrb_gemm_desc* d) {
                                     size_t{d->N} * 4u, d->M, cudaMemcpyDeviceToHost, s));
   }
   if (d->cq) {
-    HRB_CUDA(ctx, cudaMemcpyAsync(d->cq, dd.cq, q_bytes, cudaMemcpyDeviceToHost, s));
-    HRB_CUDA(ctx, cudaMemcpyAsync(d->cscale, dd.cscale, qs_bytes, cudaMemcpyDeviceToHost, s));
+    if (d->ldcq == 0) {
+      HRB_CUDA(ctx, cudaMemcpyAsync(d->cq, dd.cq, q_bytes, cudaMemcpyDeviceToHost, s));
+      HRB_CUDA(ctx, cudaMemcpyAsync(d->cscale, dd.cscale, qs_bytes, cudaMemcpyDeviceToHost, s));
+    } else {
+      // Only this GEMM's columns of each row: the rest of the wider rows is
+      // the caller's.
+      const size_t kpn = size_t{blocks_of(d->N)} * 32u;
+      HRB_CUDA(ctx, cudaMemcpy2DAsync(d->cq, d->ldcq, dd.cq, d->ldcq, kpn, d->M,
+                                      cudaMemcpyDeviceToHost, s));
+      HRB_CUDA(ctx, cudaMemcpy2DAsync(d->cscale, d->ldcq / 32u, dd.cscale, d->ldcq / 32u,
+                                      kpn / 32u, d->M, cudaMemcpyDeviceToHost, s));
+    }
   }
   return hrb_sync(ctx);
 }

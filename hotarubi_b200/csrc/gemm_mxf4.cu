@@ -151,7 +151,8 @@ __host__ __device__ inline MxTile make_tile(const TcJob& job, uint32_t nt, uint3
   t.a = job.a_tiles + static_cast<size_t>(mt) * job.k_steps * act_block_bytes(job.wfmt, nt);
   t.c = job.c != nullptr ? job.c + static_cast<size_t>(row0) * job.ldc + col0 : nullptr;
   t.bias = job.epv != nullptr ? job.epv + 2u * col0 : (job.bias != nullptr ? job.bias + col0 : nullptr);
-  const uint32_t kbq = (job.N + 31u) / 32u;  // blocks per row of the MXINT8 copy
+  // Blocks per row of the MXINT8 copy.
+  const uint32_t kbq = job.ldcq != 0 ? job.ldcq / 32u : (job.N + 31u) / 32u;
   t.cq = job.cq != nullptr ? job.cq + static_cast<size_t>(row0) * kbq * 32u + col0 : nullptr;
   t.cscale = job.cq != nullptr ? job.cscale + static_cast<size_t>(row0) * kbq + col0 / 32u
                                : nullptr;

@@ -110,8 +110,9 @@ __host__ __device__ inline int64_t conv_source_block(const ConvGeom& g, uint32_t
 // `unit_begin` is the prefix sum over the jobs of a launch.
 struct QuantJob {
   const float* x;
-  int8_t* q;          // [rows][kb * 32], or null
-  uint8_t* scale;     // [rows][kb], or null
+  int8_t* q;          // [rows][ldq * 32], or null
+  uint8_t* scale;     // [rows][ldq], or null
+  uint32_t ldq;       // row stride of q and scale in blocks; 0: kb
   // The tensor-core operands (launch_quantize_planes): the activations as
   // digit planes with their E8M0 scales in the activation blocks of
   // hrb_tc.cuh, [row tiles of tile_rows][k_steps][block].  tiles_kind 2:

@@ -35,9 +35,10 @@ struct TcJob {
   uint32_t accumulate;
   uint32_t m_tiles, n_tiles, k_steps;
   uint32_t tile_begin;     // prefix over the jobs of one launch
-  int8_t* cq;              // MXINT8 copy of C [M][kpN] or null
-  uint8_t* cscale;         // [M][kpN / 32]
+  int8_t* cq;              // MXINT8 copy of C [M][ldcq] or null
+  uint8_t* cscale;         // [M][ldcq / 32]
   uint32_t cquant;         // hrb_quant of the copy
+  uint32_t ldcq;           // row stride of the copy in codes; 0: kpN
   uint32_t relu;           // RELU after the bias (before the copy)
 };
 

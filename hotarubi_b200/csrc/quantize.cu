@@ -109,9 +109,9 @@ __device__ __forceinline__ void finish_unit(const Unit& t, const uint32_t v[4], 
                             ((static_cast<uint32_t>(q[1]) & 0xFFu) << 8) |
                             ((static_cast<uint32_t>(q[2]) & 0xFFu) << 16) |
                             ((static_cast<uint32_t>(q[3]) & 0xFFu) << 24);
-    const size_t kp = static_cast<size_t>(job.kb) * 32u;
-    *reinterpret_cast<uint32_t*>(job.q + static_cast<size_t>(t.row) * kp + t.col0) = packed;
-    if ((lane & 7u) == 0) job.scale[static_cast<size_t>(t.row) * job.kb + block] = static_cast<uint8_t>(scale);
+    const size_t ldq = job.ldq != 0 ? job.ldq : job.kb;
+    *reinterpret_cast<uint32_t*>(job.q + static_cast<size_t>(t.row) * ldq * 32u + t.col0) = packed;
+    if ((lane & 7u) == 0) job.scale[static_cast<size_t>(t.row) * ldq + block] = static_cast<uint8_t>(scale);
   }
 
 }

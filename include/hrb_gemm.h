@@ -229,6 +229,13 @@ typedef struct hrb_gemm_desc {
    * them to BF16 in tensor memory, kind::f16.  Both are exact in their
    * products; on the B200 the digit planes are the faster of the two. */
   uint32_t w8_kernel;
+  /* Row stride of the MXINT8 copy in codes (a multiple of 32, at least kpN;
+   * the scales' row stride is ldcq / 32): cq[m * ldcq + n], cscale[m *
+   * ldcq / 32 + n / 32].  0: kpN, the packed layout above.  A GEMM over a
+   * column slice of a wider matrix (a rank's N shard) writes its copy into
+   * the full matrix's layout with cq and cscale pointing at the slice's
+   * first column (a multiple of 32). */
+  uint32_t ldcq;
 } hrb_gemm_desc;
 
 enum { HRB_W8_DIGIT_PLANES = 0, HRB_W8_BF16 = 1 };

@@ -142,6 +142,61 @@ def run_gpu_columns(lib, group) -> None:
     out.close()
 
 
+def run_gpu_columns_mxint8(lib, group) -> None:
+    """Column shards that gather only the MXINT8 copy (hrb_gemm_desc.ldcq):
+    each rank's GEMM over its columns writes the copy, and no FP32 output,
+    into the full matrix's layout in every rank's buffer; bit-equal to the
+    unsharded GEMM's copy."""
+    from hotarubi_b200 import capi
+    rank = group.rank
+    batch, m, n, k = 2, 80, 1000, 512
+    kpn = (n + 31) // 32 * 32
+    out = shard.PeerOutput(lib, group, (1,), mx_shape=(batch * m, kpn))
+    out.q.zero_()
+    out.s.zero_()
+    n0, n1 = shard.columns(n)
+    keep, local_descs, full_descs = [], [], []
+    ref_c = torch.zeros((batch, m, n), dtype=torch.float32, device="cuda")
+    ref_q = torch.zeros((batch * m, kpn), dtype=torch.int8, device="cuda")
+    ref_s = torch.zeros((batch * m, kpn // 32), dtype=torch.uint8, device="cuda")
+    for b in range(batch):
+        x = torch.from_numpy(workloads.activations(40 + b, m, k)).cuda()
+        w, ws = workloads.mxfp4_weights(50 + b, n, k)
+        wd, wsd = torch.from_numpy(w).cuda(), torch.from_numpy(ws).cuda()
+        keep += [x, wd, wsd]
+        rows = slice(b * m, (b + 1) * m)
+        full_descs.append(capi.Library.desc(0, m, n, k, a=x, w=wd, wscale=wsd, c=ref_c[b],
+                                            mode=capi.MODE_FAST, cq=ref_q[rows],
+                                            cscale=ref_s[rows]))
+        if n1 > n0:
+            local_descs.append(capi.Library.desc(
+                0, m, n1 - n0, k, a=x, w=wd[n0:n1], wscale=wsd[n0:n1], c=None,
+                mode=capi.MODE_FAST, cq=out.q[rows].data_ptr() + n0,
+                cscale=out.s[rows].data_ptr() + n0 // 32, ldcq=kpn))
+    torch.cuda.synchronize()
+    full = lib.plan(full_descs)
+    full.run()
+    lib.sync()
+    plan = None
+    if local_descs:
+        plan = lib.plan(local_descs)
+        plan.set_peers(out.ptr, out.peer_bases)
+    group.barrier()
+    if plan is not None:
+        plan.run()
+    group.fence()
+    lib.sync()
+    assert torch.equal(out.q, ref_q), f"rank {rank}: gathered MXINT8 codes"
+    assert torch.equal(out.s, ref_s), f"rank {rank}: gathered MXINT8 scales"
+    group.barrier()
+    if plan is not None:
+        plan.close()
+    full.close()
+    torch.cuda.synchronize()
+    group.barrier()
+    out.close()
+
+
 def run_gpu_rows(lib, group, wfmt: int = 0) -> None:
     from hotarubi_b200 import capi
     rank, ranks = group.rank, group.ranks
@@ -227,6 +282,7 @@ def main() -> None:
         lib = capi.Library(local)
         group = shard.Group(lib)
         run_gpu_columns(lib, group)
+        run_gpu_columns_mxint8(lib, group)
         run_gpu_rows(lib, group, 0)
         run_gpu_rows(lib, group, 1)
         group.barrier()

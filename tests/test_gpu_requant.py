@@ -121,3 +121,62 @@ def test_copy_needs_an_output_unless_fused(hrb):
         with pytest.raises(capi.HrbError) as e:
             hrb.dense(d)
         assert e.value.status == capi.HRB_EINVAL
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("wfmt", [0, 1])
+def test_copy_with_a_row_stride(hrb, wfmt, mode):
+    """hrb_gemm_desc.ldcq: the copy of a GEMM over a column slice lands in a
+    wider matrix's layout (cq and cscale pointing at the slice's first
+    column), bit-equal to the packed copy, with the wider rows' other columns
+    untouched; device and host entry points."""
+    from hotarubi_b200 import capi
+    rng = np.random.default_rng(300 + 10 * wfmt + mode)
+    m, n, k = 70, 200, 320
+    wide, n0 = 512, 96                  # the slice's columns [96, 296) of 512
+    x, w, ws, b = operands(rng, wfmt, m, n, k)
+    kbq = (n + 31) // 32
+    keep = [dev(x), dev(w), dev(ws), dev(b)]
+    common = dict(a=keep[0], w=keep[1], wscale=keep[2], bias=keep[3], mode=mode, cquant=1)
+    c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    q0 = torch.zeros((m, kbq * 32), dtype=torch.int8, device="cuda")
+    s0 = torch.zeros((m, kbq), dtype=torch.uint8, device="cuda")
+    qw = torch.full((m, wide), 77, dtype=torch.int8, device="cuda")
+    sw = torch.full((m, wide // 32), 99, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    hrb.dense(capi.Library.desc(wfmt, m, n, k, c=c, cq=q0, cscale=s0, **common))
+    hrb.dense(capi.Library.desc(wfmt, m, n, k, c=c, cq=qw[:, n0:], cscale=sw[:, n0 // 32:],
+                                ldcq=wide, **common))
+    hrb.sync()
+    got_q, got_s = qw.cpu().numpy(), sw.cpu().numpy()
+    assert (got_q[:, n0:n0 + kbq * 32] == q0.cpu().numpy()).all()
+    assert (got_s[:, n0 // 32:n0 // 32 + kbq] == s0.cpu().numpy()).all()
+    assert (got_q[:, :n0] == 77).all() and (got_q[:, n0 + kbq * 32:] == 77).all()
+    assert (got_s[:, :n0 // 32] == 99).all() and (got_s[:, n0 // 32 + kbq:] == 99).all()
+    # The host entry point: a pitched copy of the slice's columns only.
+    hq = np.full((m, wide), 55, np.int8)
+    hs = np.full((m, wide // 32), 44, np.uint8)
+    hc = np.zeros((m, n), np.float32)
+    hrb.dense_host(capi.Library.desc(wfmt, m, n, k, a=x, w=w, wscale=ws, bias=b, c=hc,
+                                     mode=mode, cquant=1, cq=hq[:, n0:], cscale=hs[:, n0 // 32:],
+                                     ldcq=wide))
+    assert (hq[:, n0:n0 + kbq * 32] == q0.cpu().numpy()).all()
+    assert (hs[:, n0 // 32:n0 // 32 + kbq] == s0.cpu().numpy()).all()
+    assert (hq[:, :n0] == 55).all() and (hq[:, n0 + kbq * 32:] == 55).all()
+    assert (hs[:, :n0 // 32] == 44).all() and (hs[:, n0 // 32 + kbq:] == 44).all()
+
+
+def test_row_stride_checks(hrb):
+    from hotarubi_b200 import capi
+    rng = np.random.default_rng(7)
+    m, n, k = 8, 200, 64
+    x, w, ws, b = operands(rng, 0, m, n, k)
+    keep = [dev(x), dev(w), dev(ws)]
+    c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    q = torch.zeros((m, 512), dtype=torch.int8, device="cuda")
+    s = torch.zeros((m, 16), dtype=torch.uint8, device="cuda")
+    for ldcq, cq in ((100, q), (192, q), (256, None)):
+        d = capi.Library.desc(0, m, n, k, a=keep[0], w=keep[1], wscale=keep[2], c=c,
+                              cq=cq, cscale=None if cq is None else s, ldcq=ldcq)
+        with pytest.raises(capi.HrbError):
+            hrb.dense(d)
