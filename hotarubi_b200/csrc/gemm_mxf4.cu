@@ -468,8 +468,9 @@ struct TileDrain {
           if (ti.c != nullptr) cbase[static_cast<size_t>(j0 + j) * ti.ldc] = x[j];
         }
       }
-      if (npeers != 0) {
-        // The same outputs into each peer's C (NVLink stores).
+      if (npeers != 0 && ti.c != nullptr) {
+        // The same outputs into each peer's C (NVLink stores); none when
+        // the FP32 output is not kept (the MXINT8 copy alone is gathered).
         for (uint32_t q = 0; q < npeers; ++q) {
           char* peer = reinterpret_cast<char*>(cbase) + p.peers.delta[q];
 #pragma unroll
